@@ -1,0 +1,224 @@
+/*
+ * vates_b200 — C ABI of the B200 (sm_100a) kernels for the AMOS144/Vates hot
+ * path: fused quantized MoE, pool slot-table gather, IsoQuant K4/V3 KV cache.
+ *
+ * Conventions
+ *  - Every pointer argument is a device pointer unless documented otherwise.
+ *  - bf16 tensors are passed as uint16_t (raw bf16 bits), like the reference
+ *    extension, which keeps scales/biases as uint16 holding bf16 bits
+ *    (mlx_streaming/core/moe/native_moe.py:57-72).
+ *  - `stream` is a cudaStream_t (CUstream) handle; NULL is the legacy stream.
+ *  - Functions return VB_OK (0) or an error code; vb_last_error() gives the
+ *    message of the calling thread's last failing call. No function throws,
+ *    allocates device memory, or synchronises the stream unless stated.
+ *  - Conditions only the device can see (a routed expert whose slot is -1,
+ *    an out-of-range id) are OR-ed as VB_STATUS_* bits into the optional
+ *    device int32 `status` word; the host reads it when it chooses.
+ *  - Scratch memory is supplied by the caller (`workspace`), sized by the
+ *    matching *_workspace_size() query.
+ */
+#ifndef VATES_B200_H
+#define VATES_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void *vb_stream_t;
+
+enum {
+  VB_OK = 0,
+  VB_ERR_INVALID = 1,   /* bad argument or unsupported shape */
+  VB_ERR_CUDA = 2,      /* CUDA runtime error while launching */
+  VB_ERR_WORKSPACE = 3, /* workspace too small */
+};
+
+/* Device status bits (OR-ed into *status by kernels). */
+enum {
+  VB_STATUS_MISS = 1,     /* routed expert not resident (slot -1) */
+  VB_STATUS_BOUNDS = 2,   /* id or slot out of range; access skipped */
+  VB_STATUS_TIMEOUT = 4,  /* a bounded inter-CTA wait gave up */
+};
+
+int vb_version(void);
+const char *vb_last_error(void);
+
+/* Nine-tensor quantized expert pool, MLX affine format (uint32-packed codes,
+ * continuous LSB-first bitstream per row; bf16 scale and bias per group).
+ * Order: gate_w, gate_s, gate_b, up_w, up_s, up_b, down_w, down_s, down_b.
+ * ptr[i] + slot * slot_stride[i] is the start of that slot's tensor, so both
+ * the reference's nine stacked arrays [cap, out, ...] (fused_moe.cpp:635-664)
+ * and one packed blob row per expert (prep/blob_layout.py:14-32) are
+ * described. gate/up are [inter, hidden*bits/32] words, down is
+ * [hidden, inter*bits/32] words; scale/bias rows are [out, in/group]. */
+typedef struct VbQuantPool {
+  const void *ptr[9];
+  int64_t slot_stride[9]; /* bytes */
+  int32_t cap;            /* number of slots */
+  int32_t reserved;
+} VbQuantPool;
+
+/* ---------------------------------------------------------------------------
+ * Pool slot-table gather.
+ * Replaces demand_gpu_remap_only (native/ext/pool/demand.cpp:1954-1970,
+ * Metal kernel demand_gpu_remap 1201-1232) and the mx.take of
+ * ResidentExpertPool.acquire_gpu (mlx_streaming/core/cache/resident_pool.py:
+ * 560-569). local[i] = table[ids[i]] (-1 = not resident). Ids outside
+ * [0, table_size) give -1 and VB_STATUS_BOUNDS. miss_count (nullable) is
+ * incremented once per -1 produced. */
+int vb_slot_remap(const uint32_t *ids, const int32_t *table, int32_t *local,
+                  int64_t n, int32_t table_size, int32_t *miss_count,
+                  int32_t *status, vb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused MoE, float32 native-extension semantics.
+ * vb_fused_moe_slots replaces fused_moe_slots (native/ext/compute/
+ * fused_moe.cpp:635-664, bindings.cpp:300-320): x f32 [tokens, hidden],
+ * local_slots u32 [tokens*k], scores f32 [tokens*k], out f32 [tokens, hidden];
+ * pair p uses token p/k and pool slot local_slots[p]; out[t] =
+ * sum_j y[t*k+j] * scores[t*k+j] (reduce_pairs, fused_moe.cpp:284-298).
+ * local_slots == NULL selects the staged variant, pair p -> slot p
+ * (fused_moe_staged, fused_moe.cpp:605-633, bindings.cpp:31-50).
+ * bits in {2,3,4,5,6,8}; (hidden*bits)%32 == (inter*bits)%32 == 0;
+ * hidden and inter multiples of group. */
+size_t vb_fused_moe_workspace_size(int32_t pairs, int32_t inter);
+int vb_fused_moe_slots(const float *x, const uint32_t *local_slots,
+                       const float *scores, const VbQuantPool *pool,
+                       int32_t tokens, int32_t k, int32_t hidden,
+                       int32_t inter, int32_t group, int32_t bits, float *out,
+                       int32_t *status, void *workspace, size_t workspace_bytes,
+                       vb_stream_t stream);
+
+/* Per-pair fused expert (no combine): replaces _custom_fused_moe_indexed
+ * (mlx_streaming/core/moe/custom_kernel.py:226-383). x f32 [pairs, hidden]
+ * (one row per pair), indices u32 [pairs], active_mask u8 [pairs] nullable
+ * (0 -> zero row), y f32 [pairs, hidden]. */
+int vb_fused_moe_pairs(const float *x, const uint32_t *indices,
+                       const uint8_t *active_mask, const VbQuantPool *pool,
+                       int32_t pairs, int32_t hidden, int32_t inter,
+                       int32_t group, int32_t bits, float *y, int32_t *status,
+                       void *workspace, size_t workspace_bytes,
+                       vb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Whole decode / MTP-verify MoE block, T <= 8 tokens, MLX bf16 dtype chain.
+ * Replaces FileStreamingMoeBlock.__call__ for decode (mlx_streaming/core/moe/
+ * block.py:245-1013): router GEMV (block.py:253) -> precise softmax -> top-k
+ * -> renormalise (321-329) -> slot gather (resident_pool.py:560-569) ->
+ * gate/up -> SwiGLU -> down (compute.py:145-199) -> weighted combine
+ * (block.py:1008) -> + sigmoid(x.w_sg) * shared_expert(x) (1009-1012).
+ * 4-bit weights, group 64 or 128, hidden/inter multiples of 64. */
+typedef struct VbMoeDecodeArgs {
+  int32_t tokens;       /* T, 1..8 */
+  int32_t hidden;       /* H */
+  int32_t inter;        /* I (routed and shared experts) */
+  int32_t group;        /* 64 or 128 */
+  int32_t bits;         /* 4 */
+  int32_t num_experts;  /* E <= 1024 */
+  int32_t top_k;        /* k <= 16 */
+  int32_t norm_topk;    /* renormalise the top-k scores */
+  float norm_eps;       /* > 0: the block input is rmsnorm(x) (unit weight,
+                           float32 math, bf16 result); 0: x as given */
+  int32_t reserved0;
+  const uint16_t *x;            /* bf16 [T, H] */
+  const uint16_t *router_w;     /* bf16 [E, H] */
+  const float *router_bias;     /* nullable f32 [E], added before rounding */
+  const int32_t *slot_table;    /* [E], -1 = not resident */
+  VbQuantPool pool;             /* routed experts */
+  VbQuantPool shared;           /* shared expert in slot 0; ptr[0]==NULL: none */
+  const uint16_t *shared_gate_w; /* bf16 [H] */
+  const uint16_t *residual;     /* nullable bf16 [T, H]: out = residual + moe */
+  uint16_t *out;                /* bf16 [T, H] */
+  int32_t *out_inds;            /* nullable [T, k] expert ids */
+  uint16_t *out_scores;         /* nullable bf16 [T, k] */
+  int32_t *out_local;           /* nullable [T, k] pool slots */
+  int32_t *status;              /* nullable device status word */
+  void *workspace;
+  size_t workspace_bytes;
+  void *const *timing_events;   /* nullable: 4 cudaEvent_t recorded before the
+                                   router, gate/up and down kernels and after
+                                   the down kernel (profiling only) */
+} VbMoeDecodeArgs;
+
+/* The decode workspace must be zero-filled before its first use; every call
+ * leaves it reusable by the next call on the same stream. Calls sharing one
+ * workspace must not overlap on the GPU. */
+size_t vb_moe_decode_workspace_size(int32_t tokens, int32_t hidden,
+                                    int32_t inter, int32_t num_experts,
+                                    int32_t top_k);
+int vb_moe_decode(const VbMoeDecodeArgs *args, vb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Deterministic route reduce: replaces deterministic_route_reduce
+ * (mlx_streaming/core/moe/custom_kernel.py:20-118). previous [tokens, H],
+ * weighted [G, H], assignment_pos int32 [G] (unique flat route positions in
+ * [0, tokens*k)); out [tokens, H] (may alias previous). For each token the
+ * routes present are added in ascending route rank to previous[token], with
+ * a rounding to the output dtype after each add. dtype: 0 = f32, 1 = bf16. */
+size_t vb_route_reduce_workspace_size(int32_t tokens, int32_t k);
+int vb_route_reduce(const void *previous, const void *weighted,
+                    const int32_t *assignment_pos, int32_t groups,
+                    int32_t tokens, int32_t hidden, int32_t k, int32_t dtype,
+                    void *out, int32_t *status, void *workspace,
+                    size_t workspace_bytes, vb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * IsoQuant KV append: rotate (optional) + quantize + pack rows into a cache.
+ * Replaces rotate_last (mlx_streaming/core/cache/quant_kv.py:68-70) on k/v and
+ * mx.quantize + slice-assign of AsymmetricQuantizedKVCache.update_and_fetch
+ * (quant_kv.py:105-137). src bf16 [B, H, n, D] contiguous; so4_blocks f32
+ * [D/4, 4, 4] (rounded to bf16 inside) or NULL for no rotation; codes u32
+ * [B, H, cap, D*bits/32], scales/biases bf16 [B, H, cap, D/group]; rows are
+ * written at sequence positions [offset, offset+n). D in {64,128,256},
+ * group 64, bits in {2,3,4,5,6,8}. */
+int vb_kv_quant_append(const uint16_t *src, const float *so4_blocks,
+                       int32_t batch, int32_t heads, int32_t n, int32_t dim,
+                       int32_t group, int32_t bits, int32_t offset,
+                       int32_t cap, uint32_t *codes, uint16_t *scales,
+                       uint16_t *biases, vb_stream_t stream);
+
+/* Rotation only: dst = src @ R (4x4 SO(4) blocks, R rounded to bf16),
+ * bf16 [rows, D]; transpose != 0 applies R^T (quant_kv.py:68-70 with Rv.T,
+ * kv_quant_patch.py:67-68). */
+int vb_so4_rotate(const uint16_t *src, const float *so4_blocks, int64_t rows,
+                  int32_t dim, int32_t transpose, uint16_t *dst,
+                  vb_stream_t stream);
+
+/* Quantized GQA attention over a packed cache: replaces asym_quantized_sdpa
+ * (quant_kv.py:212-249) plus the inverse V rotation (kv_quant_patch.py:
+ * 67-68) when rv_blocks != NULL. q bf16 [B, Hq, L, D] (already rotated);
+ * K: codes [B, Hkv, cap, D*k_bits/32], scales/biases [B, Hkv, cap, D/group];
+ * V likewise with v_bits. keys = valid sequence length; causal: query i of L
+ * sees keys <= keys-L+i. out bf16 [B, Hq, L, D]. L <= 4, Hq/Hkv <= 8 and
+ * (Hq/Hkv)*L <= 32; D = 256, group 64, k_bits 4, v_bits 3. */
+size_t vb_kv_attn_workspace_size(int32_t batch, int32_t q_heads, int32_t L,
+                                 int32_t dim, int32_t keys);
+int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
+                      const uint16_t *k_scales, const uint16_t *k_biases,
+                      const uint32_t *v_codes, const uint16_t *v_scales,
+                      const uint16_t *v_biases, const float *rv_blocks,
+                      int32_t batch, int32_t q_heads, int32_t kv_heads,
+                      int32_t L, int32_t dim, int32_t keys, int32_t cap,
+                      int32_t group, int32_t k_bits, int32_t v_bits,
+                      float scale, int32_t causal, uint16_t *out,
+                      void *workspace, size_t workspace_bytes,
+                      vb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Seeded synthetic data (bench and tests): fills `words` uint32 with a
+ * counter hash of (seed, index) and bf16 scales uniform in [lo, hi) with
+ * biases = -8*scale (MLX 4-bit affine weights as in the benchmark configs).
+ * Not part of the reference interface. */
+int vb_synth_fill_u32(uint32_t *words, int64_t n, uint64_t seed,
+                      vb_stream_t stream);
+int vb_synth_fill_scales(uint16_t *scales, uint16_t *biases, int64_t n,
+                         uint64_t seed, float lo, float hi, float bias_mul,
+                         vb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VATES_B200_H */

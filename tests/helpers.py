@@ -1,0 +1,63 @@
+"""Shared builders for the GPU parity tests (host numpy -> device tensors)."""
+import numpy as np
+
+from oracle import mlx_ops as M
+
+KEYS = ("gate_w", "gate_s", "gate_b", "up_w", "up_s", "up_b", "down_w", "down_s", "down_b")
+
+
+def random_pool_np(rng, cap, H, I, bits=4, group=64, lo=0.002, hi=0.02, gaussian=False):
+    """Nine-array pool in the oracle format. ``gaussian`` quantizes N(0, 0.1)
+    weights with the MLX rule (like the reference's tests) instead of drawing
+    uniform codes with bias -8*scale."""
+    out = {}
+    for name, (o, i) in (("gate", (I, H)), ("up", (I, H)), ("down", (H, I))):
+        if gaussian:
+            w = M.bf16((rng.standard_normal((cap, o, i)) * 0.1).astype(np.float32))
+            q, s, b = M.mlx_affine_quantize(w, group, bits)
+        else:
+            q = rng.integers(0, 2 ** 32, size=(cap, o, i * bits // 32), dtype=np.uint64).astype(np.uint32)
+            s = M.bf16_bits(rng.uniform(lo, hi, (cap, o, i // group)).astype(np.float32))
+            b = M.bf16_bits(M.bf16_from_bits(s) * np.float32(-8))
+        out[name + "_w"], out[name + "_s"], out[name + "_b"] = q, s, b
+    return out
+
+
+def pool_to_torch(pool_np, device="cuda"):
+    import torch
+    out = {}
+    for k in KEYS:
+        a = np.ascontiguousarray(pool_np[k])
+        if k.endswith("_w"):
+            out[k] = torch.from_numpy(a.view(np.int32)).to(device)
+        else:
+            out[k] = torch.from_numpy(a.view(np.int16)).to(device).view(torch.bfloat16)
+    return out
+
+
+def bf16_tensor(a, device="cuda"):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(M.bf16(a))).to(torch.bfloat16).to(device)
+
+
+def to_np(t):
+    import torch
+    if t.dtype == torch.bfloat16:
+        return t.float().cpu().numpy()
+    return t.cpu().numpy()
+
+
+def routes_agree(gpu_inds, ref_probs, ref_inds, k):
+    """Per token: True when the GPU's expert set equals the oracle's, or
+    differs only inside a tie at the k-th probability (bf16 ties are common
+    with 512 experts)."""
+    ok = []
+    for t in range(gpu_inds.shape[0]):
+        g, r = set(gpu_inds[t].tolist()), set(ref_inds[t].tolist())
+        if g == r:
+            ok.append(True)
+            continue
+        p = ref_probs[t]
+        kth = np.sort(p)[::-1][k - 1]
+        ok.append(all(p[e] >= kth for e in g))
+    return np.array(ok)

@@ -1,0 +1,112 @@
+"""ctypes binding of ``libvates_b200.so`` (the C ABI in ``include/vates_b200.h``).
+
+The library is built in-tree by :mod:`vates_b200.build`. There is no fallback:
+if the library is missing or fails to load, importing this module raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libvates_b200.so")
+
+VB_OK = 0
+VB_STATUS_MISS = 1
+VB_STATUS_BOUNDS = 2
+VB_STATUS_TIMEOUT = 4
+
+
+class VbQuantPool(C.Structure):
+    _fields_ = [("ptr", C.c_void_p * 9), ("slot_stride", C.c_int64 * 9),
+                ("cap", C.c_int32), ("reserved", C.c_int32)]
+
+
+class VbMoeDecodeArgs(C.Structure):
+    _fields_ = [
+        ("tokens", C.c_int32), ("hidden", C.c_int32), ("inter", C.c_int32),
+        ("group", C.c_int32), ("bits", C.c_int32), ("num_experts", C.c_int32),
+        ("top_k", C.c_int32), ("norm_topk", C.c_int32),
+        ("norm_eps", C.c_float), ("reserved0", C.c_int32),
+        ("x", C.c_void_p), ("router_w", C.c_void_p), ("router_bias", C.c_void_p),
+        ("slot_table", C.c_void_p), ("pool", VbQuantPool), ("shared", VbQuantPool),
+        ("shared_gate_w", C.c_void_p), ("residual", C.c_void_p), ("out", C.c_void_p),
+        ("out_inds", C.c_void_p), ("out_scores", C.c_void_p), ("out_local", C.c_void_p),
+        ("status", C.c_void_p), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+        ("timing_events", C.c_void_p),
+    ]
+
+
+class VbMoePrefillArgs(C.Structure):
+    _fields_ = [
+        ("tokens", C.c_int32), ("hidden", C.c_int32), ("inter", C.c_int32),
+        ("group", C.c_int32), ("bits", C.c_int32), ("num_experts", C.c_int32),
+        ("top_k", C.c_int32), ("norm_topk", C.c_int32),
+        ("layer_cap", C.c_int32), ("max_assignments", C.c_int32),
+        ("x", C.c_void_p), ("router_w", C.c_void_p), ("router_bias", C.c_void_p),
+        ("slot_table", C.c_void_p), ("pool", VbQuantPool), ("shared", VbQuantPool),
+        ("shared_gate_w", C.c_void_p), ("out", C.c_void_p),
+        ("out_inds", C.c_void_p), ("out_scores", C.c_void_p),
+        ("status", C.c_void_p), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+    ]
+
+
+_P = C.c_void_p
+_I32 = C.c_int32
+_I64 = C.c_int64
+_SZ = C.c_size_t
+
+_SIGNATURES = {
+    "vb_version": (_I32, []),
+    "vb_last_error": (C.c_char_p, []),
+    "vb_slot_remap": (_I32, [_P, _P, _P, _I64, _I32, _P, _P, _P]),
+    "vb_fused_moe_workspace_size": (_SZ, [_I32, _I32]),
+    "vb_fused_moe_slots": (_I32, [_P, _P, _P, C.POINTER(VbQuantPool), _I32, _I32, _I32,
+                                  _I32, _I32, _I32, _P, _P, _P, _SZ, _P]),
+    "vb_fused_moe_pairs": (_I32, [_P, _P, _P, C.POINTER(VbQuantPool), _I32, _I32, _I32,
+                                  _I32, _I32, _P, _P, _P, _SZ, _P]),
+    "vb_moe_decode_workspace_size": (_SZ, [_I32, _I32, _I32, _I32, _I32]),
+    "vb_moe_decode": (_I32, [C.POINTER(VbMoeDecodeArgs), _P]),
+    "vb_route_reduce_workspace_size": (_SZ, [_I32, _I32]),
+    "vb_route_reduce": (_I32, [_P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P,
+                               _SZ, _P]),
+    "vb_kv_quant_append": (_I32, [_P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _I32,
+                                  _I32, _P, _P, _P, _P]),
+    "vb_so4_rotate": (_I32, [_P, _P, _I64, _I32, _I32, _P, _P]),
+    "vb_kv_attn_workspace_size": (_SZ, [_I32, _I32, _I32, _I32, _I32]),
+    "vb_kv_decode_attn": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32,
+                                 _I32, _I32, _I32, _I32, _I32, _I32, C.c_float, _I32, _P,
+                                 _P, _SZ, _P]),
+    "vb_synth_fill_u32": (_I32, [_P, _I64, C.c_uint64, _P]),
+    "vb_synth_fill_scales": (_I32, [_P, _P, _I64, C.c_uint64, C.c_float, C.c_float,
+                                    C.c_float, _P]),
+}
+
+# Every symbol the header declares (tests check the library exports them).
+EXPORTED = tuple(_SIGNATURES)
+
+
+def _load() -> C.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"vates_b200: {LIB_PATH} is missing; build it with "
+            "`python -m vates_b200.build` (there is no CPU fallback)")
+    lib = C.CDLL(LIB_PATH)
+    for name, (res, args) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+class VbError(RuntimeError):
+    """A vates_b200 C-ABI call returned a non-zero status."""
+
+
+def check(rc: int, what: str) -> None:
+    if rc != VB_OK:
+        msg = lib.vb_last_error().decode(errors="replace")
+        raise VbError(f"{what} failed (status {rc}): {msg}")

@@ -1,0 +1,120 @@
+// Shared device helpers for the vates_b200 sm_100a kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/vates_b200.h"
+
+namespace vb {
+
+// ----------------------------------------------------------------------------
+// Host-side error reporting (abi.cu)
+// ----------------------------------------------------------------------------
+int set_error(int code, const char *fmt, ...);
+int check_launch(const char *what);
+
+#define VB_REQUIRE(cond, ...)                                   \
+  do {                                                          \
+    if (!(cond)) return ::vb::set_error(VB_ERR_INVALID, __VA_ARGS__); \
+  } while (0)
+
+static inline cudaStream_t as_stream(vb_stream_t s) {
+  return reinterpret_cast<cudaStream_t>(s);
+}
+
+static inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// ----------------------------------------------------------------------------
+// bf16 helpers
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ float bf2f(uint16_t b) {
+  return __uint_as_float(static_cast<uint32_t>(b) << 16);
+}
+// Round-to-nearest-even float -> bf16 bits (hardware cvt.rn).
+__device__ __forceinline__ uint16_t f2bf(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+__device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
+
+// Pack two floats into a bf16x2 word (lo in bits 0-15).
+__device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
+  return static_cast<uint32_t>(f2bf(lo)) | (static_cast<uint32_t>(f2bf(hi)) << 16);
+}
+
+// MLX sigmoid: y = 1/(1+exp(-|x|)), x<0 -> 1-y (float32).
+__device__ __forceinline__ float mlx_sigmoid(float x) {
+  float y = 1.0f / (1.0f + expf(-fabsf(x)));
+  return x < 0.0f ? 1.0f - y : y;
+}
+
+// mlx-lm SwiGLU on bf16 values: bf16(bf16(g*bf16(sigmoid(g)))*u).
+__device__ __forceinline__ float swiglu_bf16(float g, float u) {
+  float s = rbf(mlx_sigmoid(g));
+  float a = rbf(__fmul_rn(g, s));
+  return rbf(__fmul_rn(a, u));
+}
+
+// ----------------------------------------------------------------------------
+// Status word
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void flag_status(int32_t *status, int32_t bits) {
+  if (status) atomicOr(status, bits);
+}
+
+// ----------------------------------------------------------------------------
+// Loads
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ uint2 ldg_nc_v2(const void *p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+               : "=r"(r.x), "=r"(r.y) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint4 ldg_v4(const void *p) {
+  return *reinterpret_cast<const uint4 *>(p);
+}
+__device__ __forceinline__ void prefetch_l2(const void *p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+// ----------------------------------------------------------------------------
+// Warp-level MMA: D[16x8] += A[16x16] * B[16x8], bf16 in, f32 accumulate.
+// Fragment layout (PTX ISA, mma.m16n8k16, g = lane/4, c = lane%4):
+//   a[0] = A[g][2c..2c+1]   a[1] = A[g+8][2c..2c+1]
+//   a[2] = A[g][2c+8..+9]   a[3] = A[g+8][2c+8..+9]
+//   b[0] = B[2c..2c+1][g]   b[1] = B[2c+8..+9][g]
+//   d[0..1] = D[g][2c..2c+1]  d[2..3] = D[g+8][2c..2c+1]
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1,
+                                         uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// 4-bit code pairs as exact bf16 values (128 + q): nibble i (low half) and
+// nibble i+4 (high half) of `w`.
+__device__ __forceinline__ uint32_t nib_pair(uint32_t w, int i) {
+  return ((w >> (4 * i)) & 0x000F000Fu) | 0x43004300u;
+}
+
+// Programmatic dependent launch controls.
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;");
+}
+
+}  // namespace vb

@@ -1,0 +1,198 @@
+// IsoQuant KV append: SO(4) block rotation + MLX affine quantize + pack.
+//
+// Reference: rotate_last (mlx_streaming/core/cache/quant_kv.py:68-70) applied
+// to k (R_k) and v (R_v) at kv_quant_patch.py:49-55, then
+// AsymmetricQuantizedKVCache.update_and_fetch (quant_kv.py:105-137), which
+// quantizes with mx.quantize(group 64, K 4-bit / V 3-bit) and slice-assigns
+// the codes/scales/biases at [offset, offset+n).
+//
+// One row (batch, head, position) of D dims is handled by D/8 lanes, 8
+// consecutive dims per lane (two 4x4 rotation blocks). A 64-dim group spans 8
+// lanes, so group min/max are 3 xor-shuffles. The row's codes form one
+// continuous LSB-first bitstream; each lane builds a 64-bit chunk of its 8
+// codes and words are assembled from at most two neighbouring lanes' chunks.
+#include "common.cuh"
+
+namespace vb {
+
+// Rotate 8 consecutive dims (two 4x4 blocks) held by one lane.
+// out[4b+i] = sum_k x[4b+k] * R[b][k][i] (R rounded to bf16), products and
+// sums in float32 in ascending k, then rounded to bf16.
+__device__ __forceinline__ void rotate8(float (&v)[8], const float *__restrict__ blocks,
+                                        int blk0, bool transpose) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float *R = blocks + (size_t)(blk0 + h) * 16;
+    float x[4] = {v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float acc = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float r = rbf(transpose ? __ldg(R + i * 4 + kk) : __ldg(R + kk * 4 + i));
+        acc = __fadd_rn(acc, __fmul_rn(x[kk], r));
+      }
+      v[4 * h + i] = rbf(acc);
+    }
+  }
+}
+
+template <int LPR>  // lanes per row = D/8
+__global__ void __launch_bounds__(256) kv_quant_kernel(
+    const uint16_t *__restrict__ src, const float *__restrict__ blocks,
+    int64_t rows, int n, int heads_total, int bits, int offset, int cap,
+    uint32_t *__restrict__ codes, uint16_t *__restrict__ scales,
+    uint16_t *__restrict__ biases) {
+  constexpr int D = LPR * 8;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % LPR;           // lane within the row
+  const int rsub = lane / LPR;          // row within the warp
+  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32 * (32 / LPR) + rsub;
+  const bool valid = row < rows;
+  const int64_t r = valid ? row : rows - 1;
+
+  float v[8];
+  {
+    const uint4 raw = *reinterpret_cast<const uint4 *>(src + r * D + sub * 8);
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = bf2f(w[i] & 0xFFFF);
+      v[2 * i + 1] = bf2f(w[i] >> 16);
+    }
+  }
+  if (blocks) rotate8(v, blocks, sub * 2, false);
+
+  // MLX affine quantization of this lane's group (8 lanes = 64 dims).
+  float mn = v[0], mx = v[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) { mn = fminf(mn, v[i]); mx = fmaxf(mx, v[i]); }
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+  const float n_bins = (float)((1 << bits) - 1);
+  float scale = fmaxf(__fdiv_rn(__fsub_rn(mx, mn), n_bins), 1e-7f);
+  const bool side = fabsf(mn) > fabsf(mx);
+  scale = side ? scale : -scale;
+  const float edge = side ? mn : mx;
+  const float q0 = rintf(__fdiv_rn(edge, scale));
+  float bias = 0.f;
+  if (q0 != 0.f) {
+    scale = __fdiv_rn(edge, q0);
+    bias = edge;
+  }
+  uint64_t chunk = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float q = rintf(__fdiv_rn(__fsub_rn(v[i], bias), scale));
+    q = fminf(fmaxf(q, 0.f), n_bins);
+    chunk |= (uint64_t)(uint32_t)q << (bits * i);
+  }
+
+  const int64_t bh = r / n, pos = offset + (r % n);
+  const int64_t crow = bh * cap + pos;  // cache row
+  const int words_per_row = D * bits / 32;
+  const int cbits = 8 * bits;           // bits per lane chunk
+  const int base_lane = rsub * LPR;
+  const int iters = (words_per_row + LPR - 1) / LPR;
+  for (int it = 0; it < iters; ++it) {
+    const int w = sub + it * LPR;
+    const int wq = w < words_per_row ? w : words_per_row - 1;
+    const int l0 = (32 * wq) / cbits;
+    const int o = 32 * wq - l0 * cbits;
+    const int l1 = l0 + 1 < LPR ? l0 + 1 : l0;
+    const uint32_t lo0 = __shfl_sync(0xffffffffu, (uint32_t)chunk, base_lane + l0);
+    const uint32_t hi0 = __shfl_sync(0xffffffffu, (uint32_t)(chunk >> 32), base_lane + l0);
+    const uint32_t lo1 = __shfl_sync(0xffffffffu, (uint32_t)chunk, base_lane + l1);
+    const uint32_t hi1 = __shfl_sync(0xffffffffu, (uint32_t)(chunk >> 32), base_lane + l1);
+    const uint64_t c0 = ((uint64_t)hi0 << 32) | lo0;
+    const uint64_t c1 = ((uint64_t)hi1 << 32) | lo1;
+    uint64_t word = c0 >> o;
+    if (cbits - o < 32 && l1 != l0) word |= c1 << (cbits - o);
+    if (valid && w < words_per_row) codes[crow * words_per_row + w] = (uint32_t)word;
+  }
+  if (valid && (sub & 7) == 0) {
+    const int gi = sub >> 3;
+    scales[crow * (D / 64) + gi] = f2bf(scale);
+    biases[crow * (D / 64) + gi] = f2bf(bias);
+  }
+}
+
+__global__ void so4_rotate_kernel(const uint16_t *__restrict__ src,
+                                  const float *__restrict__ blocks, int64_t rows,
+                                  int dim, int transpose, uint16_t *__restrict__ dst) {
+  const int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;  // one per 8 dims
+  const int per_row = dim / 8;
+  if (idx >= rows * per_row) return;
+  const int64_t r = idx / per_row;
+  const int sub = (int)(idx % per_row);
+  float v[8];
+  const uint4 raw = *reinterpret_cast<const uint4 *>(src + r * dim + sub * 8);
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = bf2f(w[i] & 0xFFFF);
+    v[2 * i + 1] = bf2f(w[i] >> 16);
+  }
+  rotate8(v, blocks, sub * 2, transpose != 0);
+  uint4 o;
+  o.x = pack_bf2(v[0], v[1]);
+  o.y = pack_bf2(v[2], v[3]);
+  o.z = pack_bf2(v[4], v[5]);
+  o.w = pack_bf2(v[6], v[7]);
+  *reinterpret_cast<uint4 *>(dst + r * dim + sub * 8) = o;
+}
+
+}  // namespace vb
+
+using namespace vb;
+
+extern "C" {
+
+int vb_kv_quant_append(const uint16_t *src, const float *so4_blocks,
+                       int32_t batch, int32_t heads, int32_t n, int32_t dim,
+                       int32_t group, int32_t bits, int32_t offset,
+                       int32_t cap, uint32_t *codes, uint16_t *scales,
+                       uint16_t *biases, vb_stream_t stream) {
+  VB_REQUIRE(dim == 64 || dim == 128 || dim == 256, "vb_kv_quant_append: dim=%d", dim);
+  VB_REQUIRE(group == 64, "vb_kv_quant_append: group=%d (64 only)", group);
+  VB_REQUIRE(bits == 2 || bits == 3 || bits == 4 || bits == 5 || bits == 6 || bits == 8,
+             "vb_kv_quant_append: bits=%d", bits);
+  VB_REQUIRE(batch > 0 && heads > 0 && n >= 0 && offset >= 0 && offset + n <= cap,
+             "vb_kv_quant_append: batch=%d heads=%d n=%d offset=%d cap=%d", batch,
+             heads, n, offset, cap);
+  if (n == 0) return VB_OK;
+  VB_REQUIRE(src && codes && scales && biases, "vb_kv_quant_append: null pointer");
+  const int64_t rows = (int64_t)batch * heads * n;
+  const int lpr = dim / 8;
+  const int64_t rows_per_block = 8 * (32 / lpr);  // 8 warps
+  const unsigned blocks = (unsigned)((rows + rows_per_block - 1) / rows_per_block);
+  cudaStream_t s = as_stream(stream);
+  if (lpr == 32)
+    kv_quant_kernel<32><<<blocks, 256, 0, s>>>(src, so4_blocks, rows, n, batch * heads,
+                                               bits, offset, cap, codes, scales, biases);
+  else if (lpr == 16)
+    kv_quant_kernel<16><<<blocks, 256, 0, s>>>(src, so4_blocks, rows, n, batch * heads,
+                                               bits, offset, cap, codes, scales, biases);
+  else
+    kv_quant_kernel<8><<<blocks, 256, 0, s>>>(src, so4_blocks, rows, n, batch * heads,
+                                              bits, offset, cap, codes, scales, biases);
+  return check_launch("kv_quant_kernel");
+}
+
+int vb_so4_rotate(const uint16_t *src, const float *so4_blocks, int64_t rows,
+                  int32_t dim, int32_t transpose, uint16_t *dst,
+                  vb_stream_t stream) {
+  VB_REQUIRE(dim % 8 == 0 && dim > 0, "vb_so4_rotate: dim=%d", dim);
+  VB_REQUIRE(rows >= 0, "vb_so4_rotate: rows");
+  if (rows == 0) return VB_OK;
+  VB_REQUIRE(src && so4_blocks && dst, "vb_so4_rotate: null pointer");
+  const int64_t total = rows * (dim / 8);
+  so4_rotate_kernel<<<(unsigned)((total + 255) / 256), 256, 0, as_stream(stream)>>>(
+      src, so4_blocks, rows, dim, transpose, dst);
+  return check_launch("so4_rotate_kernel");
+}
+
+}  // extern "C"
