@@ -249,6 +249,26 @@ def run_decode(args, world, rank, local):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
     barrier(world)
 
+    # ---- warm in-graph kernel spans from the kernels' %globaltimer trace ----
+    trace = torch.empty((L, 16), dtype=torch.int64, device="cuda")
+    init = torch.tensor([-1, 0] * 4 + [0] * 8, dtype=torch.int64, device="cuda")
+    tgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(tgraph, stream=stream):
+        st.step(stream=stream, trace=trace)
+    spans = []
+    for _ in range(3):
+        trace.copy_(init.expand(L, 16))
+        tgraph.replay()
+        torch.cuda.synchronize()
+        tr = trace.cpu().numpy().astype("uint64").astype("float64")
+        spans.append(tr)
+    tr = spans[-1]
+    kspan = [(tr[:, 2 * i + 1] - tr[:, 2 * i]).mean() / 1e3 for i in range(3)]
+    layer_us = (tr[1:, 0] - tr[:-1, 0]).mean() / 1e3
+    gaps = [(tr[:, 2 * (i + 1)] - tr[:, 2 * i + 1]).mean() / 1e3 for i in range(2)]
+    router_marks = [(tr[:, m] - tr[:, 0]).mean() / 1e3 for m in (8, 9, 10)]
+    del tgraph
+
     # ---- dominant kernel (gate/up) timed per launch with CUDA events ----
     evs, arr = st.blocks[0].timing_events()
     phase = [0.0, 0.0, 0.0]
@@ -291,7 +311,11 @@ def run_decode(args, world, rank, local):
                      "frac": achieved / hbm_peak, "traffic": None,
                      "bytes_per_launch": gateup_bytes, "ms_per_launch": gateup_ms,
                      "phase_ms": {"router": phase[0] / n_launch, "gateup": gateup_ms,
-                                  "down": phase[2] / n_launch}},
+                                  "down_combine": phase[2] / n_launch}},
+        "kernel_trace_us": {"router": kspan[0], "gateup": kspan[1],
+                            "down_combine": kspan[2], "layer_period": layer_us,
+                            "start_gaps": gaps,
+                            "router_marks_from_start": router_marks},
         "gpu_launches": 3 * L * args.steps,
         "clocks": clocks,
     }

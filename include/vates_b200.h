@@ -141,6 +141,14 @@ typedef struct VbMoeDecodeArgs {
   void *const *timing_events;   /* nullable: 4 cudaEvent_t recorded before the
                                    router, gate/up and down kernels and after
                                    the down kernel (profiling only) */
+  uint64_t *trace;              /* nullable device [12]: [0..7] per kernel
+                                   (router, gate/up, down, combine) the min
+                                   start and max end %globaltimer (ns) over
+                                   its CTAs, initialised by the caller to
+                                   (UINT64_MAX, 0); [8..10] router markers
+                                   (latest CTA past the PDL wait, latest CTA
+                                   done with its rows, top-k start),
+                                   initialised to 0 (profiling only) */
 } VbMoeDecodeArgs;
 
 /* The decode workspace must be zero-filled before its first use; every call

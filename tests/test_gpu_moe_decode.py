@@ -8,7 +8,7 @@ mean-rel 5e-3 in bf16.
 import numpy as np
 import pytest
 
-from conftest import bf16_close
+from conftest import bf16_close, block_scale
 from helpers import bf16_tensor, pool_to_torch, random_pool_np, routes_agree, to_np
 from oracle import mlx_ops as M
 from oracle import moe as OM
@@ -45,13 +45,14 @@ def _check_block(blk, x, norm_eps=0.0, residual=None, k=10):
                 gs = dict(zip(g_inds[t].tolist(), g_scores[t].tolist()))
                 rs = dict(zip(ref["inds"][t].tolist(), ref["scores"][t].tolist()))
                 assert gs == rs
-            bf16_close(to_np(out), ref["out"], what="block output")
+            bf16_close(to_np(out), ref["out"], scale=block_scale(ref, res), what="block output")
     # Teacher forcing on the GPU's routing isolates the expert path.
     host_table = host["table"]
     assert np.array_equal(g_local >= 0, host_table[g_inds] >= 0)
     ref_tf = OM.moe_block_decode(xr, host, k=k, norm_eps=norm_eps, residual=res,
                                  route=(g_inds, g_scores))
-    return bf16_close(to_np(out), ref_tf["out"], what="teacher-forced block output")
+    return bf16_close(to_np(out), ref_tf["out"], scale=block_scale(ref_tf, res),
+                      what="teacher-forced block output")
 
 
 @pytest.mark.parametrize("T", [1, 4])
@@ -70,7 +71,7 @@ def test_decode_block_small_shapes(cuda, T, group, norm):
     import torch
     from vates_b200.moe_block import MoeBlock
     from vates_b200.pool import QuantPool, make_table
-    H, I, E, k = 512, 128, 64, 6
+    H, I, E, k = (1024 if group == 128 else 512), 128, 64, 6
     rng = np.random.default_rng(T * 10 + group)
     pool_np = random_pool_np(rng, E, H, I, 4, group)
     pool = QuantPool.from_tensors(pool_to_torch(pool_np), H, I, 4, group)
@@ -161,4 +162,5 @@ def test_stack_layers_match_oracle(cuda):
         ref = OM.moe_block_decode(to_np(st.hs[l]), host, k=10, norm_eps=st.norm_eps,
                                   residual=to_np(st.hs[l]),
                                   route=(inds, to_np(dbg["scores"])))
-        bf16_close(to_np(st.hs[l + 1]), ref["out"], what=f"layer {l}")
+        bf16_close(to_np(st.hs[l + 1]), ref["out"], scale=block_scale(ref, to_np(st.hs[l])),
+                   what=f"layer {l}")

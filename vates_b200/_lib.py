@@ -33,7 +33,7 @@ class VbMoeDecodeArgs(C.Structure):
         ("shared_gate_w", C.c_void_p), ("residual", C.c_void_p), ("out", C.c_void_p),
         ("out_inds", C.c_void_p), ("out_scores", C.c_void_p), ("out_local", C.c_void_p),
         ("status", C.c_void_p), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
-        ("timing_events", C.c_void_p),
+        ("timing_events", C.c_void_p), ("trace", C.c_void_p),
     ]
 
 

@@ -5,6 +5,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/vates_b200.h"
 
 namespace vb {
@@ -109,7 +111,8 @@ __device__ __forceinline__ uint32_t nib_pair(uint32_t w, int i) {
   return ((w >> (4 * i)) & 0x000F000Fu) | 0x43004300u;
 }
 
-// Programmatic dependent launch controls.
+// Programmatic dependent launch controls (no-ops without the launch
+// attribute).
 __device__ __forceinline__ void pdl_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
@@ -117,4 +120,34 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;");
 }
 
+// Ampere-style asynchronous 16-byte global -> shared copies.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 }  // namespace vb
+
+// Kernel launch with an optional programmatic-dependent-launch attribute.
+template <typename... KArgs, typename... Args>
+static inline cudaError_t vb_launch(void (*kern)(KArgs...), dim3 grid, dim3 block,
+                                    size_t smem, cudaStream_t s, bool pdl, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}

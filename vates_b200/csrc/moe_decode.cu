@@ -4,23 +4,30 @@
 // :245-1013) with PersistentSubGLU.forward (compute.py:145-199) and the
 // shared expert (block.py:102-109, 1009-1012).
 //
-// Three kernels per block:
-//  K1 router: logits = bf16(x.Wr^T [+bias]) with one warp per expert row.
-//     The last CTA to finish (atomic ticket) runs the precise softmax, top-k
-//     with lower-id tie break, renormalisation, slot gather, and builds the
-//     list of unique expert "entries" (+ the shared expert). CTA 0 also
-//     writes x in MMA-fragment order (xperm) and per-64 column sums (xsum).
-//  K2 gate/up: one CTA per (entry, 16 intermediate rows). Weights are the A
-//     operand of mma.m16n8k16 (16 rows x 16 columns), tokens are the 8 B
-//     columns. 4-bit codes become exact bf16 values 128+q with one LOP3 per
-//     pair, so the tensor core sums (128+q)*x per 64-column group; the
-//     epilogue applies y += s*D + (b - 128*s)*sum(x) per group. 8 warps
-//     split the hidden dimension; partial sums are added in warp order.
-//     SwiGLU (bf16 per op) follows, h is written in fragment order (hperm).
-//  K3 down + combine: one CTA per 16 output rows loops over all entries,
-//     rounds y to bf16, multiplies by the route score (bf16), and adds the
-//     routes of each token in rank order (exact double sum of bf16 values,
-//     rounded to float32 then bf16), then the sigmoid-gated shared expert.
+// Four kernels per block, chained with programmatic dependent launch (PDL):
+//  K1 router: optional unit RMSNorm of x, logits = bf16(x.Wr^T [+bias]) with
+//     one warp per expert row (row loaded before the PDL wait). The last CTA
+//     (atomic ticket) runs the precise softmax, top-k (lower id wins ties),
+//     renormalisation and slot gather, and writes the list of "entries":
+//     the shared expert first, then every distinct routed slot. All CTAs
+//     share writing x in MMA-fragment order (xperm), per-64-column sums
+//     (xsum) and the shared-expert gate sigmoid(x.w_sg).
+//  K2 gate/up: persistent CTAs walk items (entry, 16 intermediate rows). All
+//     512 threads stream an item's packed rows and scales into a multi-stage
+//     cp.async ring (per-thread copy offsets are fixed at kernel start; H is a
+//     template constant). Weights are the A operand of mma.m16n8k16 (16 rows
+//     x 16 columns), tokens the 8 B columns: 4-bit codes become the exact
+//     bf16 values 128+q with one LOP3 per pair, so per 64-column group the
+//     epilogue applies y += s*D + (b - 128*s)*sum(x). 16 warps split the
+//     hidden dimension and their partials are added in warp order; SwiGLU
+//     (bf16 per op) follows and h is stored in fragment order (hperm).
+//     The shared expert's weights are requested before the PDL wait.
+//  K3 down: persistent CTAs walk items (entry, 128 output rows), weights
+//     requested before the PDL wait; per route the result is rounded to
+//     bf16, multiplied by the route score and rounded again (MLX chain).
+//  K4 combine: per token and column, the k routes are added in rank order
+//     (exact double sum of bf16 values, rounded to float32 then bf16), then
+//     the gated shared expert and the optional residual.
 #include "common.cuh"
 
 namespace vb {
@@ -29,18 +36,19 @@ constexpr int DEC_MAX_T = 8;
 constexpr int DEC_MAX_K = 16;
 constexpr int DEC_MAX_E = 1024;
 constexpr int DEC_ROUTER_WARPS = 4;
+constexpr int DEC_SMEM_BUDGET = 200 * 1024;
 
 struct DecEntry {
   int32_t slot;
   int32_t flags;  // bit0 = shared expert
   int32_t pad[2];
-  int32_t rank[DEC_MAX_T];   // route rank of token n, -1 = not routed here
-  float score[DEC_MAX_T];    // bf16 route score
+  int32_t rank[DEC_MAX_T];  // route rank of token n, -1 = not routed here
+  float score[DEC_MAX_T];   // bf16 route score
 };
 
 struct DecodeLayout {
-  size_t counter, n_entries, sgate, logits, entries, xperm, xsum, hperm, hsum,
-      total;
+  size_t counter, n_entries, sgate, rb_count, logits, entries, route_ok, xperm, xsum, hperm,
+      hsum, wparts, sparts, total;
   int max_entries;
 };
 
@@ -52,10 +60,14 @@ static DecodeLayout decode_layout(int T, int H, int I, int E, int k) {
   L.n_entries = off; off += 4;
   off = align_up(off, 16);
   L.sgate = off; off += sizeof(float) * DEC_MAX_T;
+  off = align_up(off, 16);
+  L.rb_count = off; off += sizeof(unsigned) * (H / 128);
   off = align_up(off, 256);
   L.logits = off; off += sizeof(float) * (size_t)T * E;
   off = align_up(off, 256);
   L.entries = off; off += sizeof(DecEntry) * (size_t)L.max_entries;
+  off = align_up(off, 256);
+  L.route_ok = off; off += sizeof(int32_t) * (size_t)T * k;
   off = align_up(off, 256);
   L.xperm = off; off += sizeof(uint32_t) * (size_t)T * (H / 2);
   off = align_up(off, 256);
@@ -64,6 +76,10 @@ static DecodeLayout decode_layout(int T, int H, int I, int E, int k) {
   L.hperm = off; off += sizeof(uint32_t) * (size_t)L.max_entries * DEC_MAX_T * (I / 2);
   off = align_up(off, 256);
   L.hsum = off; off += sizeof(float) * (size_t)L.max_entries * DEC_MAX_T * (I / 16);
+  off = align_up(off, 256);
+  L.wparts = off; off += sizeof(uint16_t) * (size_t)T * k * H;
+  off = align_up(off, 256);
+  L.sparts = off; off += sizeof(uint16_t) * (size_t)T * H;
   L.total = align_up(off, 256);
   return L;
 }
@@ -71,6 +87,7 @@ static DecodeLayout decode_layout(int T, int H, int I, int E, int k) {
 struct DecodeParams {
   int T, H, I, E, k, norm_topk, gshift, has_shared;
   float norm_eps;
+  int stages2, stages3;
   const uint16_t *x, *router_w, *shared_gate_w, *residual;
   const float *router_bias;
   const int32_t *table;
@@ -78,44 +95,108 @@ struct DecodeParams {
   uint16_t *out, *out_scores;
   int32_t *out_inds, *out_local, *status;
   uint8_t *ws;
+  uint64_t *trace;
   DecodeLayout L;
 };
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Optional span trace: thread 0 of every CTA folds its start/end into the
+// kernel's [min start, max end] pair.
+struct SpanTrace {
+  uint64_t *slot;
+  uint64_t t0;
+  __device__ __forceinline__ SpanTrace(uint64_t *trace, int kernel) {
+    slot = (trace && threadIdx.x == 0) ? trace + 2 * kernel : nullptr;
+    t0 = slot ? globaltimer() : 0;
+  }
+  __device__ __forceinline__ void end() {
+    if (slot) {
+      atomicMin(reinterpret_cast<unsigned long long *>(slot), (unsigned long long)t0);
+      atomicMax(reinterpret_cast<unsigned long long *>(slot + 1),
+                (unsigned long long)globaltimer());
+    }
+  }
+};
+
+// Optional marker: latest %globaltimer over the CTAs that pass this point.
+__device__ __forceinline__ void trace_mark(uint64_t *trace, int idx) {
+  if (trace && threadIdx.x == 0)
+    atomicMax(reinterpret_cast<unsigned long long *>(trace + idx),
+              (unsigned long long)globaltimer());
+}
 
 template <typename T>
 __device__ __forceinline__ T *wsp(const DecodeParams &p, size_t off) {
   return reinterpret_cast<T *>(p.ws + off);
 }
 
-// Position of value `o` (0..63) of a 64-group inside the fragment-ordered
-// layout: returns (quarter c, word w, high half?).
-__device__ __forceinline__ void frag_pos(int o, int &c, int &w, int &hi) {
-  c = o >> 4;
-  int o16 = o & 15;
-  int j = o16 >> 3;
-  int rem = o16 & 7;
-  int i0 = (rem & 2);         // {0,1,4,5} -> 0, {2,3,6,7} -> 2
-  int d = rem - i0;           // 0,1,4,5
-  int m = 2 * j + (i0 >> 1);
-  w = 2 * m + (d & 1);
-  hi = d >> 2;
+__device__ __forceinline__ const uint8_t *pool_ptr(const VbQuantPool &pool, int t, int slot) {
+  return (const uint8_t *)pool.ptr[t] + (size_t)slot * pool.slot_stride[t];
+}
+
+__device__ __forceinline__ uint2 lds64(const uint8_t *p) {
+  return *reinterpret_cast<const uint2 *>(p);
 }
 
 // ----------------------------------------------------------------------------
-// K1: router GEMV (+ xperm/xsum/shared gate in CTA 0) + last-CTA top-k
+// K1: router GEMV + last-CTA softmax/top-k/entries. H is a template constant
+// so that every index is a shift.
 // ----------------------------------------------------------------------------
+template <int H, int PER>  // PER = ceil(E / 32) logits per lane
 __global__ void __launch_bounds__(DEC_ROUTER_WARPS * 32)
 moe_router_kernel(DecodeParams p) {
+  constexpr int NVL = H / 256;  // uint4 of a row per lane
+  constexpr int NG = H / 64;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint16_t *xs = reinterpret_cast<uint16_t *>(smem_raw);  // [T][H] bf16
-  const int T = p.T, H = p.H, E = p.E;
+  const int T = p.T, E = p.E;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  SpanTrace span(p.trace, 0);
 
-  // Stage x in shared memory (16-byte vectors).
+  // Router row of this warp and (CTAs t < T, warp 0) the shared-expert gate
+  // row: both independent of the previous kernel.
+  const int e = blockIdx.x * DEC_ROUTER_WARPS + warp;
+  uint4 wv[NVL];
+  if (e < E) {
+    const uint4 *wrow = reinterpret_cast<const uint4 *>(p.router_w + (size_t)e * H);
+#pragma unroll
+    for (int u = 0; u < NVL; ++u) wv[u] = ldg_nc_v4(wrow + u * 32 + lane);
+  }
+  const bool gate_cta = p.has_shared && (int)blockIdx.x < T && warp == 0;
+  uint4 gv[NVL];
+  if (gate_cta) {
+    const uint4 *grow = reinterpret_cast<const uint4 *>(p.shared_gate_w);
+#pragma unroll
+    for (int u = 0; u < NVL; ++u) gv[u] = ldg_nc_v4(grow + u * 32 + lane);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  trace_mark(p.trace, 8);
+
   {
+    // Stage x: independent 16-byte loads issued before the stores.
     const uint4 *src = reinterpret_cast<const uint4 *>(p.x);
     uint4 *dst = reinterpret_cast<uint4 *>(xs);
-    int nvec = T * H / 8;
-    for (int i = tid; i < nvec; i += blockDim.x) dst[i] = src[i];
+    const int nvec = T * (H / 8);
+    constexpr int STEP = DEC_ROUTER_WARPS * 32;
+    for (int base = 0; base < nvec; base += 8 * STEP) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = base + u * STEP + tid;
+        if (i < nvec) v[u] = __ldcg(src + i);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = base + u * STEP + tid;
+        if (i < nvec) dst[i] = v[u];
+      }
+    }
   }
   __syncthreads();
   if (p.norm_eps > 0.f) {
@@ -125,9 +206,16 @@ moe_router_kernel(DecodeParams p) {
     __shared__ float s_inv[DEC_MAX_T];
     for (int t = warp; t < T; t += DEC_ROUTER_WARPS) {
       double ss = 0.0;
-      for (int q = lane; q < H; q += 32) {
-        const float v = bf2f(xs[(size_t)t * H + q]);
-        ss += (double)v * (double)v;
+#pragma unroll
+      for (int u = 0; u < NVL; ++u) {
+        const uint4 v = reinterpret_cast<const uint4 *>(xs + (size_t)t * H)[u * 32 + lane];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const double a = bf2f(w[q] & 0xFFFF), b = bf2f(w[q] >> 16);
+          ss = fma(a, a, ss);
+          ss = fma(b, b, ss);
+        }
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -137,34 +225,30 @@ moe_router_kernel(DecodeParams p) {
       }
     }
     __syncthreads();
-    for (int i = tid; i < T * H; i += blockDim.x) {
-      const int t = i / H;
-      xs[i] = f2bf(__fmul_rn(bf2f(xs[i]), s_inv[t]));
+    for (int i = tid; i < T * (H / 8); i += blockDim.x) {
+      const int t = i / (H / 8);
+      uint4 v = reinterpret_cast<const uint4 *>(xs)[i];
+      uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      const float inv = s_inv[t];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        w[q] = pack_bf2(__fmul_rn(bf2f(w[q] & 0xFFFF), inv), __fmul_rn(bf2f(w[q] >> 16), inv));
+      reinterpret_cast<uint4 *>(xs)[i] = make_uint4(w[0], w[1], w[2], w[3]);
     }
     __syncthreads();
   }
 
-  // Router rows: one warp per expert.
-  const int e = blockIdx.x * DEC_ROUTER_WARPS + warp;
   if (e < E) {
     float acc[DEC_MAX_T];
 #pragma unroll
     for (int t = 0; t < DEC_MAX_T; ++t) acc[t] = 0.f;
-    const uint4 *wrow = reinterpret_cast<const uint4 *>(p.router_w + (size_t)e * H);
-    const int nv = H / 8;  // uint4 per row
-    for (int v0 = 0; v0 < nv; v0 += 32 * 8) {
-      uint4 wv[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        int v = v0 + u * 32 + lane;
-        wv[u] = v < nv ? ldg_nc_v4(wrow + v) : make_uint4(0, 0, 0, 0);
-      }
+    for (int u = 0; u < NVL; ++u) {
+      const int v = u * 32 + lane;
+      const uint32_t wr[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        int v = v0 + u * 32 + lane;
-        if (v >= nv) break;
-        const uint32_t wr[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
-        for (int t = 0; t < T; ++t) {
+      for (int t = 0; t < DEC_MAX_T; ++t) {
+        if (t < T) {
           const uint4 xv = reinterpret_cast<const uint4 *>(xs + (size_t)t * H)[v];
           const uint32_t xr[4] = {xv.x, xv.y, xv.z, xv.w};
           float a = acc[t];
@@ -177,71 +261,92 @@ moe_router_kernel(DecodeParams p) {
         }
       }
     }
-    for (int t = 0; t < T; ++t) {
-      float a = acc[t];
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-      if (lane == 0) {
-        if (p.router_bias) a = a + p.router_bias[e];
-        wsp<float>(p, p.L.logits)[(size_t)t * E + e] = rbf(a);
+    for (int t = 0; t < DEC_MAX_T; ++t) {
+      if (t < T) {
+        float a = acc[t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (lane == 0) {
+          if (p.router_bias) a = a + p.router_bias[e];
+          wsp<float>(p, p.L.logits)[(size_t)t * E + e] = rbf(a);
+        }
       }
     }
   }
 
-  if (blockIdx.x == 0) {
-    // x in MMA fragment order + per-64-column sums (float32).
+  {
+    // x in MMA fragment order (xperm) and per-64-column sums (xsum), spread
+    // over all CTAs (each holds the whole normalised x in shared memory).
     uint32_t *xperm = wsp<uint32_t>(p, p.L.xperm);
-    float *xsum = wsp<float>(p, p.L.xsum);
-    const int NG = H / 64;
-    for (int i = tid; i < T * H / 2; i += blockDim.x) {
-      int n = i / (H / 2);
-      int r = i - n * (H / 2);
-      int G = r / 32, cw = r % 32, c = cw >> 3, w = cw & 7;
-      int m = w >> 1, pp = w & 1, j = m >> 1, i0 = 2 * (m & 1);
-      int base = 64 * G + 16 * c + 8 * j + i0 + pp;
-      uint32_t lo = xs[(size_t)n * H + base], hi = xs[(size_t)n * H + base + 4];
+    const int gtid = blockIdx.x * blockDim.x + tid, gstride = gridDim.x * blockDim.x;
+    for (int i = gtid; i < T * (H / 2); i += gstride) {
+      const int n = i / (H / 2);
+      const int r = i % (H / 2);
+      const int G = r >> 5, c = (r >> 3) & 3, w = r & 7;
+      const int m = w >> 1, pp = w & 1, j = m >> 1, i0 = 2 * (m & 1);
+      const int base = 64 * G + 16 * c + 8 * j + i0 + pp;
+      const uint32_t lo = xs[(size_t)n * H + base], hi = xs[(size_t)n * H + base + 4];
       xperm[i] = lo | (hi << 16);
     }
-    for (int i = tid; i < T * NG; i += blockDim.x) {
-      int n = i / NG, G = i % NG;
-      float s = 0.f;
-      for (int q = 0; q < 64; ++q) s += bf2f(xs[(size_t)n * H + 64 * G + q]);
-      xsum[i] = s;
-    }
-    if (p.has_shared) {
-      for (int t = warp; t < T; t += DEC_ROUTER_WARPS) {
-        float a = 0.f;
-        for (int q = lane; q < H; q += 32)
-          a = fmaf(bf2f(p.shared_gate_w[q]), bf2f(xs[(size_t)t * H + q]), a);
+    float *xsum = wsp<float>(p, p.L.xsum);
+    const int gwarp = blockIdx.x * DEC_ROUTER_WARPS + warp;
+    const int nwarps = gridDim.x * DEC_ROUTER_WARPS;
+    for (int it = gwarp; it < T * NG; it += nwarps) {
+      const int n = it / NG, G = it % NG;
+      const uint32_t v = reinterpret_cast<const uint32_t *>(xs + (size_t)n * H + 64 * G)[lane];
+      float s = bf2f(v & 0xFFFF) + bf2f(v >> 16);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (lane == 0) wsp<float>(p, p.L.sgate)[t] = rbf(mlx_sigmoid(rbf(a)));
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      if (lane == 0) xsum[it] = s;
+    }
+    for (int t = blockIdx.x; gate_cta && t < T; t += gridDim.x) {
+      float a = 0.f;
+#pragma unroll
+      for (int u = 0; u < NVL; ++u) {
+        const uint32_t gr[4] = {gv[u].x, gv[u].y, gv[u].z, gv[u].w};
+        const uint4 xv = reinterpret_cast<const uint4 *>(xs + (size_t)t * H)[u * 32 + lane];
+        const uint32_t xr[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          a = fmaf(bf2f(gr[q] & 0xFFFF), bf2f(xr[q] & 0xFFFF), a);
+          a = fmaf(bf2f(gr[q] >> 16), bf2f(xr[q] >> 16), a);
+        }
       }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0) wsp<float>(p, p.L.sgate)[t] = rbf(mlx_sigmoid(rbf(a)));
     }
   }
 
   // Last-CTA ticket.
   __shared__ unsigned s_ticket;
+  trace_mark(p.trace, 9);
   __threadfence();
   __syncthreads();
   if (tid == 0) s_ticket = atomicAdd(wsp<unsigned>(p, p.L.counter), 1u);
   __syncthreads();
-  if (s_ticket != gridDim.x - 1) return;
+  if (s_ticket != gridDim.x - 1) {
+    span.end();
+    return;
+  }
   __threadfence();
+  trace_mark(p.trace, 10);
 
   // ---- softmax + top-k per token (one warp per token) ----
-  __shared__ int s_exp[DEC_MAX_T * DEC_MAX_K];
   __shared__ int s_slot[DEC_MAX_T * DEC_MAX_K];
   __shared__ float s_score[DEC_MAX_T * DEC_MAX_K];
+  __shared__ int s_first[DEC_MAX_T * DEC_MAX_K];  // 1 = first route of its slot
+  __shared__ int s_ent[DEC_MAX_T * DEC_MAX_K];
+  __shared__ __align__(16) DecEntry s_entries[DEC_MAX_T * DEC_MAX_K + 1];
   const int k = p.k;
   const float *logits = wsp<float>(p, p.L.logits);
-  constexpr int PER = DEC_MAX_E / 32;
   for (int t = warp; t < T; t += DEC_ROUTER_WARPS) {
     float v[PER];
     float m = -INFINITY;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
-      int idx = lane + 32 * i;
+      const int idx = lane + 32 * i;
       v[i] = idx < E ? __ldcg(logits + (size_t)t * E + idx) : -INFINITY;
       m = fmaxf(m, v[i]);
     }
@@ -250,406 +355,507 @@ moe_router_kernel(DecodeParams p) {
     double s = 0.0;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
-      int idx = lane + 32 * i;
-      float ex = idx < E ? expf(__fsub_rn(v[i], m)) : 0.f;
+      const int idx = lane + 32 * i;
+      const float ex = idx < E ? expf(__fsub_rn(v[i], m)) : 0.f;
       v[i] = ex;
       s += (double)ex;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     const float inv = __frcp_rn((float)s);
+    // Probabilities (bf16) and this lane's running maximum; ties resolve to
+    // the lower expert id.
+    float lb = -INFINITY;
+    int li = 0x7fffffff;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
-      int idx = lane + 32 * i;
+      const int idx = lane + 32 * i;
       v[i] = idx < E ? rbf(__fmul_rn(v[i], inv)) : -INFINITY;
+      if (v[i] > lb) { lb = v[i]; li = idx; }
     }
     double ssum = 0.0;
     float sel_p = 0.f;
+    int sel_e = 0;
     for (int r = 0; r < k; ++r) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        if (v[i] > bv) { bv = v[i]; bi = lane + 32 * i; }
-      }
+      float bv = lb;
+      int bi = li;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
         if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
       }
-      if ((bi & 31) == lane) {
+      if ((bi & 31) == lane) {  // winner: drop the value, rescan this lane
+        lb = -INFINITY;
+        li = 0x7fffffff;
 #pragma unroll
-        for (int i = 0; i < PER; ++i)
-          if (lane + 32 * i == bi) v[i] = -INFINITY;
+        for (int i = 0; i < PER; ++i) {
+          const int idx = lane + 32 * i;
+          if (idx == bi) v[i] = -INFINITY;
+          if (v[i] > lb) { lb = v[i]; li = idx; }
+        }
       }
-      if (lane == r) sel_p = bv;
+      if (lane == r) { sel_p = bv; sel_e = bi; }
       ssum += (double)bv;
-      if (lane == 0) s_exp[t * k + r] = bi;
     }
-    __syncwarp();
     float score = sel_p;
     if (p.norm_topk) {
-      float denom = rbf((float)ssum);
+      const float denom = rbf((float)ssum);
       score = rbf(__fdiv_rn(sel_p, denom));
     }
     if (lane < k) {
-      int ex = s_exp[t * k + lane];
+      const int ex = sel_e;
       int slot = -1;
-      if (ex >= 0 && ex < E) slot = p.table[ex];
-      else flag_status(p.status, VB_STATUS_BOUNDS);
-      if (slot < 0 || slot >= p.pool.cap) {
-        if (slot >= p.pool.cap) flag_status(p.status, VB_STATUS_BOUNDS);
-        else flag_status(p.status, VB_STATUS_MISS);
-        slot = -1;
+      if (ex >= 0 && ex < E) {
+        slot = __ldg(p.table + ex);
+        if (slot >= p.pool.cap) {
+          flag_status(p.status, VB_STATUS_BOUNDS);
+          slot = -1;
+        } else if (slot < 0) {
+          flag_status(p.status, VB_STATUS_MISS);
+          slot = -1;
+        }
+      } else {
+        flag_status(p.status, VB_STATUS_BOUNDS);
       }
       s_slot[t * k + lane] = slot;
       s_score[t * k + lane] = score;
+      wsp<int32_t>(p, p.L.route_ok)[t * k + lane] = slot >= 0 ? 1 : 0;
       if (p.out_inds) p.out_inds[t * k + lane] = ex;
       if (p.out_scores) p.out_scores[t * k + lane] = f2bf(score);
       if (p.out_local) p.out_local[t * k + lane] = slot;
     }
   }
+  // Entry table in shared memory: slot -1 / rank -1 defaults.
+  for (int i = tid; i < (DEC_MAX_T * DEC_MAX_K + 1) * (int)(sizeof(DecEntry) / 4);
+       i += blockDim.x) {
+    const int f = i % (int)(sizeof(DecEntry) / 4);  // field word
+    reinterpret_cast<int32_t *>(s_entries)[i] = (f >= 4 && f < 12) ? -1 : 0;
+  }
   __syncthreads();
 
-  // ---- unique entries in route order (t, j) ----
-  if (warp == 0) {
-    const int R = T * k;
-    DecEntry *entries = wsp<DecEntry>(p, p.L.entries);
-    int n_unique = 0;
-    for (int base = 0; base < R; base += 32) {
-      int r = base + lane;
-      int slot = r < R ? s_slot[r] : -1;
-      bool first = slot >= 0;
-      if (first) {
-        for (int q = 0; q < r; ++q)
-          if (s_slot[q] == slot) { first = false; break; }
-      }
-      unsigned mask = __ballot_sync(0xffffffffu, first);
-      if (first) {
-        int idx = n_unique + __popc(mask & ((1u << lane) - 1u));
-        DecEntry en;
-        en.slot = slot;
-        en.flags = 0;
-        en.pad[0] = en.pad[1] = 0;
-#pragma unroll
-        for (int n = 0; n < DEC_MAX_T; ++n) { en.rank[n] = -1; en.score[n] = 0.f; }
-        for (int q = r; q < R; ++q) {
-          if (s_slot[q] == slot) {
-            int tt = q / k, jj = q % k;
-            en.rank[tt] = jj;
-            en.score[tt] = s_score[q];
-          }
-        }
-        entries[idx] = en;
-      }
-      n_unique += __popc(mask);
-    }
-    if (lane == 0) {
-      int n = n_unique;
-      if (p.has_shared) {
-        DecEntry en;
-        en.slot = 0;
-        en.flags = 1;
-        en.pad[0] = en.pad[1] = 0;
-        for (int q = 0; q < DEC_MAX_T; ++q) { en.rank[q] = q < T ? 0 : -1; en.score[q] = 1.f; }
-        entries[n++] = en;
-      }
-      *wsp<int32_t>(p, p.L.n_entries) = n;
-      *wsp<unsigned>(p, p.L.counter) = 0u;  // ready for the next launch
-    }
+  // ---- entries: shared expert first, then the distinct routed slots in
+  // route order (t-major, rank-minor). One thread per route: it finds the
+  // first route with its slot, first routes are numbered by counting the
+  // earlier first routes, and every route fills its (entry, token) cell.
+  const int R = T * k;
+  const int shared_n = p.has_shared ? 1 : 0;
+  const int r = tid;
+  const int slot = r < R ? s_slot[r] : -1;
+  int first = r;
+#pragma unroll 8
+  for (int q = 0; q < R; ++q) {
+    const int sq = s_slot[q];
+    first = (q < first && sq == slot) ? q : first;
   }
+  const bool is_first = slot >= 0 && first == r;
+  if (r < R) s_first[r] = is_first ? 1 : 0;
+  const int n_routed = __syncthreads_count(is_first);
+  if (is_first) {
+    int idx = shared_n;
+#pragma unroll 8
+    for (int q = 0; q < r; ++q) idx += s_first[q];
+    s_ent[r] = idx;
+  }
+  __syncthreads();
+  if (r < R && slot >= 0) {
+    const int ei = s_ent[first];
+    const int tt = r / k, jj = r - tt * k;
+    s_entries[ei].slot = slot;
+    s_entries[ei].rank[tt] = jj;
+    s_entries[ei].score[tt] = s_score[r];
+  }
+  if (tid == 0 && p.has_shared) {
+    s_entries[0].slot = 0;
+    s_entries[0].flags = 1;
+    for (int q = 0; q < T; ++q) { s_entries[0].rank[q] = 0; s_entries[0].score[q] = 1.f; }
+  }
+  __syncthreads();
+  const int n = shared_n + n_routed;
+  const int words = n * (int)(sizeof(DecEntry) / 4);
+  int32_t *dst = wsp<int32_t>(p, p.L.entries);
+  for (int i = tid; i < words; i += blockDim.x)
+    dst[i] = reinterpret_cast<const int32_t *>(s_entries)[i];
+  if (tid == 0) {
+    *wsp<int32_t>(p, p.L.n_entries) = n;
+    *wsp<unsigned>(p, p.L.counter) = 0u;  // ready for the next launch
+  }
+  span.end();
 }
 
 // ----------------------------------------------------------------------------
-// K2: gate/up + SwiGLU for one (entry, 16-row block)
+// K2: gate/up + SwiGLU. One CTA per item (entry, 16 intermediate rows). The 8
+// warps split the hidden dimension (GPW groups of 64 columns each) and load
+// their packed rows, scales and x fragments straight into registers; many
+// small independent CTAs per SM hide each other's memory latency.
 // ----------------------------------------------------------------------------
-template <int GPW>
-__global__ void __launch_bounds__(256, 2) moe_gateup_kernel(DecodeParams p) {
-  const int e = blockIdx.x;
-  const int n_entries = *wsp<const int32_t>(p, p.L.n_entries);
-  if (e >= n_entries) return;
-  const DecEntry ent = wsp<const DecEntry>(p, p.L.entries)[e];
-  const int rb = blockIdx.y;
+constexpr int K2_THREADS = 256;
+constexpr int K2_WARPS = K2_THREADS / 32;
+
+// Load 2*count bytes of bf16 scales (count in {1,2,4,8}) into a uint4.
+__device__ __forceinline__ uint4 ld_scales(const uint16_t *ptr, int count) {
+  uint4 r = make_uint4(0, 0, 0, 0);
+  if (count >= 8) {
+    r = __ldg(reinterpret_cast<const uint4 *>(ptr));
+  } else if (count == 4) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2 *>(ptr));
+    r.x = v.x;
+    r.y = v.y;
+  } else if (count == 2) {
+    r.x = __ldg(reinterpret_cast<const unsigned *>(ptr));
+  } else {
+    r.x = __ldg(ptr);
+  }
+  return r;
+}
+__device__ __forceinline__ float bf_at(const uint4 &v, int i) {
+  const uint32_t w = i < 2 ? v.x : (i < 4 ? v.y : (i < 6 ? v.z : v.w));
+  return bf2f((i & 1) ? (w >> 16) : (w & 0xFFFF));
+}
+
+template <int H>
+__global__ void __launch_bounds__(K2_THREADS, 2) moe_gateup_kernel(DecodeParams p) {
+  constexpr int NG = H / 64;
+  constexpr int GPW = NG / K2_WARPS;
+  __shared__ float red[K2_WARPS][256];
+  __shared__ float hval[128];
+  __shared__ int s_slot, s_n;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int H = p.H, T = p.T;
-  const int NG = H / 64;
-  const bool is_shared = ent.flags & 1;
-  const VbQuantPool &pool = is_shared ? p.shared : p.pool;
-  const int slot = is_shared ? 0 : ent.slot;
-
-  __shared__ float red[8][2][16][8];
-  __shared__ float fin[2][16][8];
-  __shared__ float hval[16][8];
-
-  float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
+  const int T = p.T;
+  SpanTrace span(p.trace, 1);
+  const int e = blockIdx.x, rb = blockIdx.y;
   const int G0 = warp * GPW;
-  if (G0 < NG && slot >= 0) {
-    const int row0 = 16 * rb + g, row1 = row0 + 8;
-    const size_t wrow = (size_t)H / 2;  // bytes per packed row (4-bit)
-    const uint8_t *gw = (const uint8_t *)pool.ptr[0] + (size_t)slot * pool.slot_stride[0];
-    const uint8_t *uw = (const uint8_t *)pool.ptr[3] + (size_t)slot * pool.slot_stride[3];
-    uint2 ag0[GPW], ag1[GPW], au0[GPW], au1[GPW];
+  const int row0 = 16 * rb + g, row1 = row0 + 8;
+  const int NS = H >> (6 + p.gshift);
+  const int sc_count = GPW >> p.gshift ? GPW >> p.gshift : 1;  // scales per row slice
+
+  uint2 ag0[GPW], ag1[GPW], au0[GPW], au1[GPW];
+  uint4 sv[8];  // gate_s r0, r1, gate_b r0, r1, up_s r0, r1, up_b r0, r1
+  auto load_w = [&](const VbQuantPool &pool, int slot) {
+    const uint8_t *gw = pool_ptr(pool, 0, slot), *uw = pool_ptr(pool, 3, slot);
 #pragma unroll
     for (int i = 0; i < GPW; ++i) {
       const size_t col = (size_t)(G0 + i) * 32 + 8 * c;
-      if (G0 + i < NG) {
-        ag0[i] = ldg_nc_v2(gw + row0 * wrow + col);
-        ag1[i] = ldg_nc_v2(gw + row1 * wrow + col);
-        au0[i] = ldg_nc_v2(uw + row0 * wrow + col);
-        au1[i] = ldg_nc_v2(uw + row1 * wrow + col);
-      }
+      ag0[i] = ldg_nc_v2(gw + (size_t)row0 * (H / 2) + col);
+      ag1[i] = ldg_nc_v2(gw + (size_t)row1 * (H / 2) + col);
+      au0[i] = ldg_nc_v2(uw + (size_t)row0 * (H / 2) + col);
+      au1[i] = ldg_nc_v2(uw + (size_t)row1 * (H / 2) + col);
     }
-    // Scales / biases (bf16) for rows row0/row1, groups G0..G0+GPW-1.
-    const int NS = H >> (6 + p.gshift);  // scales per row
-    const uint16_t *gs = (const uint16_t *)((const uint8_t *)pool.ptr[1] + (size_t)slot * pool.slot_stride[1]);
-    const uint16_t *gb = (const uint16_t *)((const uint8_t *)pool.ptr[2] + (size_t)slot * pool.slot_stride[2]);
-    const uint16_t *us = (const uint16_t *)((const uint8_t *)pool.ptr[4] + (size_t)slot * pool.slot_stride[4]);
-    const uint16_t *ub = (const uint16_t *)((const uint8_t *)pool.ptr[5] + (size_t)slot * pool.slot_stride[5]);
-    float sg0[GPW], sg1[GPW], bg0[GPW], bg1[GPW], su0[GPW], su1[GPW], bu0[GPW], bu1[GPW];
+    const int s0 = G0 >> p.gshift;
 #pragma unroll
-    for (int i = 0; i < GPW; ++i) {
-      int si = (G0 + i) >> p.gshift;
-      if (G0 + i < NG) {
-        sg0[i] = bf2f(__ldg(gs + (size_t)row0 * NS + si));
-        sg1[i] = bf2f(__ldg(gs + (size_t)row1 * NS + si));
-        bg0[i] = bf2f(__ldg(gb + (size_t)row0 * NS + si));
-        bg1[i] = bf2f(__ldg(gb + (size_t)row1 * NS + si));
-        su0[i] = bf2f(__ldg(us + (size_t)row0 * NS + si));
-        su1[i] = bf2f(__ldg(us + (size_t)row1 * NS + si));
-        bu0[i] = bf2f(__ldg(ub + (size_t)row0 * NS + si));
-        bu1[i] = bf2f(__ldg(ub + (size_t)row1 * NS + si));
-      }
+    for (int a = 0; a < 8; ++a) {
+      const int t = (a < 4 ? 1 : 4) + ((a >> 1) & 1);  // gate_s, gate_b, up_s, up_b
+      const int row = (a & 1) ? row1 : row0;
+      const uint16_t *sp = reinterpret_cast<const uint16_t *>(pool_ptr(pool, t, slot)) + (size_t)row * NS + s0;
+      sv[a] = ld_scales(sp, sc_count);
     }
-    // B operand: x column n = g in fragment order; inactive columns are 0.
-    const bool col_active = g < T && (is_shared || ent.rank[g] >= 0);
+  };
+
+  // The shared expert (entry 0) needs no routing: load before the PDL wait.
+  const bool pre = p.has_shared && e == 0;
+  if (pre) load_w(p.shared, 0);
+  pdl_wait();
+  pdl_launch_dependents();
+  if (!pre) {
+    if (tid == 0) {
+      s_n = *wsp<const int32_t>(p, p.L.n_entries);
+      s_slot = wsp<const DecEntry>(p, p.L.entries)[e].slot;
+    }
+    __syncthreads();
+    if (e >= s_n) {
+      span.end();
+      return;
+    }
+    load_w(p.pool, s_slot);
+  }
+
+  // x fragments and column sums of this warp's groups (written by the router).
+  uint4 xb[GPW][2];
+  float xs0[GPW], xs1[GPW];
+  {
     const uint32_t *xperm = wsp<const uint32_t>(p, p.L.xperm);
     const float *xsum = wsp<const float>(p, p.L.xsum);
-    uint4 xb[GPW][2];
-    float xs0[GPW], xs1[GPW];
 #pragma unroll
     for (int i = 0; i < GPW; ++i) {
-      if (col_active && G0 + i < NG) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(
-            xperm + (((size_t)g * NG + G0 + i) * 4 + c) * 8);
-        xb[i][0] = src[0];
-        xb[i][1] = src[1];
+      const int G = G0 + i;
+      if (g < T) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(xperm + (((size_t)g * NG + G) * 4 + c) * 8);
+        xb[i][0] = __ldcg(src);
+        xb[i][1] = __ldcg(src + 1);
       } else {
         xb[i][0] = xb[i][1] = make_uint4(0, 0, 0, 0);
       }
-      const int n0 = 2 * c, n1 = 2 * c + 1;
-      const bool a0 = n0 < T && (is_shared || ent.rank[n0] >= 0);
-      const bool a1 = n1 < T && (is_shared || ent.rank[n1] >= 0);
-      xs0[i] = (a0 && G0 + i < NG) ? xsum[n0 * NG + G0 + i] : 0.f;
-      xs1[i] = (a1 && G0 + i < NG) ? xsum[n1 * NG + G0 + i] : 0.f;
-    }
-#pragma unroll
-    for (int i = 0; i < GPW; ++i) {
-      if (G0 + i >= NG) break;
-      float dg[4] = {0.f, 0.f, 0.f, 0.f}, du[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint32_t xw[8] = {xb[i][0].x, xb[i][0].y, xb[i][0].z, xb[i][0].w,
-                              xb[i][1].x, xb[i][1].y, xb[i][1].z, xb[i][1].w};
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const int i0 = 2 * (m & 1);
-        const uint32_t wa = (m >> 1) ? ag0[i].y : ag0[i].x;
-        const uint32_t wb = (m >> 1) ? ag1[i].y : ag1[i].x;
-        mma_bf16(dg, nib_pair(wa, i0), nib_pair(wb, i0), nib_pair(wa, i0 + 1),
-                 nib_pair(wb, i0 + 1), xw[2 * m], xw[2 * m + 1]);
-        const uint32_t va = (m >> 1) ? au0[i].y : au0[i].x;
-        const uint32_t vb2 = (m >> 1) ? au1[i].y : au1[i].x;
-        mma_bf16(du, nib_pair(va, i0), nib_pair(vb2, i0), nib_pair(va, i0 + 1),
-                 nib_pair(vb2, i0 + 1), xw[2 * m], xw[2 * m + 1]);
-      }
-      const float bpg0 = fmaf(-128.f, sg0[i], bg0[i]), bpg1 = fmaf(-128.f, sg1[i], bg1[i]);
-      const float bpu0 = fmaf(-128.f, su0[i], bu0[i]), bpu1 = fmaf(-128.f, su1[i], bu1[i]);
-      accg[0] += fmaf(sg0[i], dg[0], bpg0 * xs0[i]);
-      accg[1] += fmaf(sg0[i], dg[1], bpg0 * xs1[i]);
-      accg[2] += fmaf(sg1[i], dg[2], bpg1 * xs0[i]);
-      accg[3] += fmaf(sg1[i], dg[3], bpg1 * xs1[i]);
-      accu[0] += fmaf(su0[i], du[0], bpu0 * xs0[i]);
-      accu[1] += fmaf(su0[i], du[1], bpu0 * xs1[i]);
-      accu[2] += fmaf(su1[i], du[2], bpu1 * xs0[i]);
-      accu[3] += fmaf(su1[i], du[3], bpu1 * xs1[i]);
+      xs0[i] = 2 * c < T ? __ldcg(xsum + (2 * c) * NG + G) : 0.f;
+      xs1[i] = 2 * c + 1 < T ? __ldcg(xsum + (2 * c + 1) * NG + G) : 0.f;
     }
   }
-  red[warp][0][g][2 * c] = accg[0];
-  red[warp][0][g][2 * c + 1] = accg[1];
-  red[warp][0][g + 8][2 * c] = accg[2];
-  red[warp][0][g + 8][2 * c + 1] = accg[3];
-  red[warp][1][g][2 * c] = accu[0];
-  red[warp][1][g][2 * c + 1] = accu[1];
-  red[warp][1][g + 8][2 * c] = accu[2];
-  red[warp][1][g + 8][2 * c + 1] = accu[3];
-  __syncthreads();
-  {
-    const int P = tid >> 7, row = (tid >> 3) & 15, col = tid & 7;
-    float s = 0.f;
+
+  float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += red[w][P][row][col];
-    fin[P][row][col] = s;
+  for (int i = 0; i < GPW; ++i) {
+    const int si = i >> p.gshift;
+    const float sg0 = bf_at(sv[0], si), sg1 = bf_at(sv[1], si);
+    const float bg0 = bf_at(sv[2], si), bg1 = bf_at(sv[3], si);
+    const float su0 = bf_at(sv[4], si), su1 = bf_at(sv[5], si);
+    const float bu0 = bf_at(sv[6], si), bu1 = bf_at(sv[7], si);
+    float dg[4] = {0.f, 0.f, 0.f, 0.f}, du[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t xw[8] = {xb[i][0].x, xb[i][0].y, xb[i][0].z, xb[i][0].w,
+                            xb[i][1].x, xb[i][1].y, xb[i][1].z, xb[i][1].w};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int i0 = 2 * (m & 1);
+      const uint32_t wa = (m >> 1) ? ag0[i].y : ag0[i].x;
+      const uint32_t wb = (m >> 1) ? ag1[i].y : ag1[i].x;
+      mma_bf16(dg, nib_pair(wa, i0), nib_pair(wb, i0), nib_pair(wa, i0 + 1),
+               nib_pair(wb, i0 + 1), xw[2 * m], xw[2 * m + 1]);
+      const uint32_t va = (m >> 1) ? au0[i].y : au0[i].x;
+      const uint32_t vb2 = (m >> 1) ? au1[i].y : au1[i].x;
+      mma_bf16(du, nib_pair(va, i0), nib_pair(vb2, i0), nib_pair(va, i0 + 1),
+               nib_pair(vb2, i0 + 1), xw[2 * m], xw[2 * m + 1]);
+    }
+    const float bpg0 = fmaf(-128.f, sg0, bg0), bpg1 = fmaf(-128.f, sg1, bg1);
+    const float bpu0 = fmaf(-128.f, su0, bu0), bpu1 = fmaf(-128.f, su1, bu1);
+    accg[0] += fmaf(sg0, dg[0], bpg0 * xs0[i]);
+    accg[1] += fmaf(sg0, dg[1], bpg0 * xs1[i]);
+    accg[2] += fmaf(sg1, dg[2], bpg1 * xs0[i]);
+    accg[3] += fmaf(sg1, dg[3], bpg1 * xs1[i]);
+    accu[0] += fmaf(su0, du[0], bpu0 * xs0[i]);
+    accu[1] += fmaf(su0, du[1], bpu0 * xs1[i]);
+    accu[2] += fmaf(su1, du[2], bpu1 * xs0[i]);
+    accu[3] += fmaf(su1, du[3], bpu1 * xs1[i]);
   }
+  float *rw = red[warp];
+  *reinterpret_cast<float2 *>(rw + g * 8 + 2 * c) = make_float2(accg[0], accg[1]);
+  *reinterpret_cast<float2 *>(rw + (g + 8) * 8 + 2 * c) = make_float2(accg[2], accg[3]);
+  *reinterpret_cast<float2 *>(rw + 128 + g * 8 + 2 * c) = make_float2(accu[0], accu[1]);
+  *reinterpret_cast<float2 *>(rw + 128 + (g + 8) * 8 + 2 * c) = make_float2(accu[2], accu[3]);
   __syncthreads();
   if (tid < 128) {
-    const int row = tid >> 3, col = tid & 7;
-    const bool active = col < T && (is_shared || ent.rank[col] >= 0) && slot >= 0;
-    float h = 0.f;
-    if (active) h = swiglu_bf16(rbf(fin[0][row][col]), rbf(fin[1][row][col]));
-    hval[row][col] = h;
+    // Add the warp partials in warp order, then SwiGLU (bf16 per op).
+    float sg = 0.f, su = 0.f;
+#pragma unroll
+    for (int w = 0; w < K2_WARPS; ++w) {
+      sg += red[w][tid];
+      su += red[w][128 + tid];
+    }
+    hval[tid] = (tid & 7) < T ? swiglu_bf16(rbf(sg), rbf(su)) : 0.f;
   }
   __syncthreads();
+  const int NI = p.I / 64;
   if (tid < 64) {
-    // 16 rows of h are quarter c' = rb%4 of intermediate group G' = rb/4.
+    // The 16 rows of h form quarter c' = rb%4 of intermediate group rb/4.
     const int n = tid >> 3, w = tid & 7;
     const int m = w >> 1, pp = w & 1, j = m >> 1, i0 = 2 * (m & 1);
     const int olo = 8 * j + i0 + pp, ohi = olo + 4;
-    const uint32_t word = pack_bf2(hval[olo][n], hval[ohi][n]);
-    const int NGI = p.I / 64;
+    const uint32_t word = pack_bf2(hval[olo * 8 + n], hval[ohi * 8 + n]);
     uint32_t *hperm = wsp<uint32_t>(p, p.L.hperm);
-    const size_t idx = ((((size_t)e * DEC_MAX_T + n) * NGI + (rb >> 2)) * 4 + (rb & 3)) * 8 + w;
-    hperm[idx] = word;
+    hperm[((((size_t)e * DEC_MAX_T + n) * NI + (rb >> 2)) * 4 + (rb & 3)) * 8 + w] = word;
   } else if (tid < 72) {
     const int n = tid - 64;
-    float s = 0.f;
+    float sh = 0.f;
 #pragma unroll
-    for (int o = 0; o < 16; ++o) s += hval[o][n];
-    wsp<float>(p, p.L.hsum)[((size_t)e * DEC_MAX_T + n) * (p.I / 16) + rb] = s;
+    for (int o = 0; o < 16; ++o) sh += hval[o * 8 + n];
+    wsp<float>(p, p.L.hsum)[((size_t)e * DEC_MAX_T + n) * (p.I / 16) + rb] = sh;
   }
+  span.end();
 }
 
 // ----------------------------------------------------------------------------
-// K3: down projection + weighted combine + shared expert, 16 output rows/CTA
+// K3: down projection + fused combine. One CTA per (entry, 128 output rows),
+// warp w owns rows [16w, 16w+16). Weights are requested before the PDL wait;
+// h is staged in shared memory after it. The last CTA of a 128-row block
+// (atomic ticket per block) adds the routes of every token in rank order
+// (exact double sum of bf16 values, rounded to float32 then bf16), then the
+// gated shared expert and the optional residual.
 // ----------------------------------------------------------------------------
-template <int NGI>
-__global__ void __launch_bounds__(256, 1) moe_down_kernel(DecodeParams p) {
-  const int rb = blockIdx.x;
+constexpr int K3_THREADS = 256;
+
+template <int I>
+__global__ void __launch_bounds__(K3_THREADS, 2) moe_down_kernel(DecodeParams p) {
+  constexpr int NGI = I / 64;
+  constexpr int HW = I / 2 + 4;  // words per staged h column (+16 B pad)
+  __shared__ __align__(16) uint32_t hsm[DEC_MAX_T][HW];
+  __shared__ __align__(16) float hs_sm[DEC_MAX_T][I / 16];
+  __shared__ int s_slot, s_n, s_flags;
+  __shared__ int s_rank[DEC_MAX_T];
+  __shared__ float s_score[DEC_MAX_T];
+  __shared__ unsigned s_ticket;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int T = p.T, k = p.k, I = p.I;
-  __shared__ float contrib[DEC_MAX_T][DEC_MAX_K][16];
-  __shared__ float shy[DEC_MAX_T][16];
-  for (int i = tid; i < DEC_MAX_T * DEC_MAX_K * 16; i += blockDim.x)
-    (&contrib[0][0][0])[i] = 0.f;
-  for (int i = tid; i < DEC_MAX_T * 16; i += blockDim.x) (&shy[0][0])[i] = 0.f;
-  __syncthreads();
+  const int T = p.T, H = p.H;
+  SpanTrace span(p.trace, 2);
+  const int e = blockIdx.x, rb = blockIdx.y;
 
-  const int n_entries = *wsp<const int32_t>(p, p.L.n_entries);
-  const DecEntry *entries = wsp<const DecEntry>(p, p.L.entries);
-  const uint32_t *hperm = wsp<const uint32_t>(p, p.L.hperm);
-  const float *hsum = wsp<const float>(p, p.L.hsum);
-  const int row0 = 16 * rb + g, row1 = row0 + 8;
-  const size_t wrow = (size_t)I / 2;
-  const int NS = I >> (6 + p.gshift);
-
-  for (int e = warp; e < n_entries; e += 8) {
-    const DecEntry ent = entries[e];
-    const bool is_shared = ent.flags & 1;
-    const VbQuantPool &pool = is_shared ? p.shared : p.pool;
-    const int slot = is_shared ? 0 : ent.slot;
-    if (slot < 0) continue;
-    // Prefetch the next entry's rows into L2 while this one computes.
-    if (e + 8 < n_entries) {
-      const DecEntry nx = entries[e + 8];
-      const bool ns = nx.flags & 1;
-      const VbQuantPool &np = ns ? p.shared : p.pool;
-      const int nslot = ns ? 0 : nx.slot;
-      if (nslot >= 0 && lane < 16) {
-        const uint8_t *nd = (const uint8_t *)np.ptr[6] + (size_t)nslot * np.slot_stride[6];
-        const uint8_t *rowp = nd + (size_t)(16 * rb + lane) * wrow;
-        for (size_t off = 0; off < wrow; off += 128) prefetch_l2(rowp + off);
-      }
-    }
-    const uint8_t *dw = (const uint8_t *)pool.ptr[6] + (size_t)slot * pool.slot_stride[6];
-    const uint16_t *ds = (const uint16_t *)((const uint8_t *)pool.ptr[7] + (size_t)slot * pool.slot_stride[7]);
-    const uint16_t *db = (const uint16_t *)((const uint8_t *)pool.ptr[8] + (size_t)slot * pool.slot_stride[8]);
-    uint2 a0[NGI], a1[NGI];
-#pragma unroll
-    for (int G = 0; G < NGI; ++G) {
-      a0[G] = ldg_nc_v2(dw + row0 * wrow + G * 32 + 8 * c);
-      a1[G] = ldg_nc_v2(dw + row1 * wrow + G * 32 + 8 * c);
-    }
-    float s0[NGI], s1[NGI], b0[NGI], b1[NGI];
-#pragma unroll
-    for (int G = 0; G < NGI; ++G) {
-      const int si = G >> p.gshift;
-      s0[G] = bf2f(__ldg(ds + (size_t)row0 * NS + si));
-      s1[G] = bf2f(__ldg(ds + (size_t)row1 * NS + si));
-      b0[G] = bf2f(__ldg(db + (size_t)row0 * NS + si));
-      b1[G] = bf2f(__ldg(db + (size_t)row1 * NS + si));
-    }
-    const bool col_active = g < T && (is_shared || ent.rank[g] >= 0);
-    uint4 hb[NGI][2];
-#pragma unroll
-    for (int G = 0; G < NGI; ++G) {
-      if (col_active) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(
-            hperm + ((((size_t)e * DEC_MAX_T + g) * NGI + G) * 4 + c) * 8);
-        hb[G][0] = __ldcg(src);
-        hb[G][1] = __ldcg(src + 1);
-      } else {
-        hb[G][0] = hb[G][1] = make_uint4(0, 0, 0, 0);
-      }
-    }
-    const int n0 = 2 * c, n1 = 2 * c + 1;
-    const bool act0 = n0 < T && (is_shared || ent.rank[n0] >= 0);
-    const bool act1 = n1 < T && (is_shared || ent.rank[n1] >= 0);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int G = 0; G < NGI; ++G) {
-      float d[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint32_t hw[8] = {hb[G][0].x, hb[G][0].y, hb[G][0].z, hb[G][0].w,
-                              hb[G][1].x, hb[G][1].y, hb[G][1].z, hb[G][1].w};
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const int i0 = 2 * (m & 1);
-        const uint32_t wa = (m >> 1) ? a0[G].y : a0[G].x;
-        const uint32_t wb = (m >> 1) ? a1[G].y : a1[G].x;
-        mma_bf16(d, nib_pair(wa, i0), nib_pair(wb, i0), nib_pair(wa, i0 + 1),
-                 nib_pair(wb, i0 + 1), hw[2 * m], hw[2 * m + 1]);
-      }
-      float hs0 = 0.f, hs1 = 0.f;
-      if (act0) {
-        const float *h = hsum + ((size_t)e * DEC_MAX_T + n0) * (I / 16) + 4 * G;
-        hs0 = ((__ldcg(h) + __ldcg(h + 1)) + __ldcg(h + 2)) + __ldcg(h + 3);
-      }
-      if (act1) {
-        const float *h = hsum + ((size_t)e * DEC_MAX_T + n1) * (I / 16) + 4 * G;
-        hs1 = ((__ldcg(h) + __ldcg(h + 1)) + __ldcg(h + 2)) + __ldcg(h + 3);
-      }
-      const float bp0 = fmaf(-128.f, s0[G], b0[G]), bp1 = fmaf(-128.f, s1[G], b1[G]);
-      acc[0] += fmaf(s0[G], d[0], bp0 * hs0);
-      acc[1] += fmaf(s0[G], d[1], bp0 * hs1);
-      acc[2] += fmaf(s1[G], d[2], bp1 * hs0);
-      acc[3] += fmaf(s1[G], d[3], bp1 * hs1);
-    }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int n = 2 * c + (q & 1);
-      const int r = g + 8 * (q >> 1);
-      if (n >= T) continue;
-      const float yb = rbf(acc[q]);
-      if (is_shared) {
-        shy[n][r] = yb;
-      } else if (ent.rank[n] >= 0) {
-        contrib[n][ent.rank[n]][r] = rbf(__fmul_rn(yb, ent.score[n]));
-      }
+  // Entry list (written by the router two launches back) and weights do not
+  // depend on the gate/up kernel: read them before the PDL wait.
+  if (tid == 0) s_n = *wsp<const int32_t>(p, p.L.n_entries);
+  if (tid < 2 + 2 * DEC_MAX_T) {
+    const int32_t *ent = reinterpret_cast<const int32_t *>(wsp<const DecEntry>(p, p.L.entries) + e);
+    // words: 0 slot, 1 flags, 4..11 rank, 12..19 score
+    const int wi = tid < 2 ? tid : (tid < 2 + DEC_MAX_T ? 4 + (tid - 2) : 12 + (tid - 2 - DEC_MAX_T));
+    if (e < p.L.max_entries) {
+      const int v = ent[wi];
+      if (tid == 0) s_slot = v;
+      else if (tid == 1) s_flags = v;
+      else if (tid < 2 + DEC_MAX_T) s_rank[tid - 2] = v;
+      else s_score[tid - 2 - DEC_MAX_T] = __int_as_float(v);
     }
   }
   __syncthreads();
-  if (tid < T * 16) {
-    const int t = tid >> 4, r = tid & 15;
-    double s = 0.0;
-    for (int j = 0; j < k; ++j) s += (double)contrib[t][j][r];
-    float y = rbf((float)s);
-    if (p.has_shared) {
-      const float gate = wsp<const float>(p, p.L.sgate)[t];
-      y = rbf(__fadd_rn(y, rbf(__fmul_rn(gate, shy[t][r]))));
-    }
-    const size_t oi = (size_t)t * p.H + 16 * rb + r;
-    if (p.residual) y = rbf(__fadd_rn(bf2f(p.residual[oi]), y));
-    p.out[oi] = f2bf(y);
+  const int n_entries = s_n;
+  if (e >= n_entries) {
+    span.end();
+    return;
   }
+  const bool is_shared = s_flags & 1;
+  const VbQuantPool &pool = is_shared ? p.shared : p.pool;
+  const int slot = is_shared ? 0 : s_slot;
+  const int r0 = 128 * rb + 16 * warp + g, r1 = r0 + 8;
+  const int NSI = I >> (6 + p.gshift);
+  uint2 a0[NGI], a1[NGI];
+  {
+    const uint8_t *dw = pool_ptr(pool, 6, slot);
+#pragma unroll
+    for (int G = 0; G < NGI; ++G) {
+      a0[G] = ldg_nc_v2(dw + (size_t)r0 * (I / 2) + G * 32 + 8 * c);
+      a1[G] = ldg_nc_v2(dw + (size_t)r1 * (I / 2) + G * 32 + 8 * c);
+    }
+  }
+  uint4 sv[4];  // down_s r0, r1, down_b r0, r1
+  {
+    const uint16_t *ds = reinterpret_cast<const uint16_t *>(pool_ptr(pool, 7, slot));
+    const uint16_t *db = reinterpret_cast<const uint16_t *>(pool_ptr(pool, 8, slot));
+    sv[0] = ld_scales(ds + (size_t)r0 * NSI, NSI);
+    sv[1] = ld_scales(ds + (size_t)r1 * NSI, NSI);
+    sv[2] = ld_scales(db + (size_t)r0 * NSI, NSI);
+    sv[3] = ld_scales(db + (size_t)r1 * NSI, NSI);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  {
+    // Stage h (fragment order) and its 16-row chunk sums for the T columns.
+    const uint4 *hp = reinterpret_cast<const uint4 *>(wsp<const uint32_t>(p, p.L.hperm) +
+                                                      (size_t)e * DEC_MAX_T * (I / 2));
+    for (int q = tid; q < T * (I / 8); q += K3_THREADS) {
+      const int n = q / (I / 8), j = q % (I / 8);
+      *reinterpret_cast<uint4 *>(&hsm[n][4 * j]) = __ldcg(hp + q);
+    }
+    const float *hs = wsp<const float>(p, p.L.hsum) + (size_t)e * DEC_MAX_T * (I / 16);
+    for (int q = tid; q < T * (I / 16); q += K3_THREADS) (&hs_sm[0][0])[q] = __ldcg(hs + q);
+  }
+  __syncthreads();
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int G = 0; G < NGI; ++G) {
+    uint4 hb0 = make_uint4(0, 0, 0, 0), hb1 = make_uint4(0, 0, 0, 0);
+    if (g < T) {
+      const uint4 *hp = reinterpret_cast<const uint4 *>(&hsm[g][(G * 4 + c) * 8]);
+      hb0 = hp[0];
+      hb1 = hp[1];
+    }
+    const uint32_t hw[8] = {hb0.x, hb0.y, hb0.z, hb0.w, hb1.x, hb1.y, hb1.z, hb1.w};
+    float dd[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int i0 = 2 * (m & 1);
+      const uint32_t wa = (m >> 1) ? a0[G].y : a0[G].x;
+      const uint32_t wb = (m >> 1) ? a1[G].y : a1[G].x;
+      mma_bf16(dd, nib_pair(wa, i0), nib_pair(wb, i0), nib_pair(wa, i0 + 1),
+               nib_pair(wb, i0 + 1), hw[2 * m], hw[2 * m + 1]);
+    }
+    const int si = G >> p.gshift;
+    const float s0 = bf_at(sv[0], si), s1 = bf_at(sv[1], si);
+    const float b0 = bf_at(sv[2], si), b1 = bf_at(sv[3], si);
+    float h0 = 0.f, h1 = 0.f;
+    if (2 * c < T) {
+      const float4 v = *reinterpret_cast<const float4 *>(&hs_sm[2 * c][4 * G]);
+      h0 = ((v.x + v.y) + v.z) + v.w;
+    }
+    if (2 * c + 1 < T) {
+      const float4 v = *reinterpret_cast<const float4 *>(&hs_sm[2 * c + 1][4 * G]);
+      h1 = ((v.x + v.y) + v.z) + v.w;
+    }
+    const float bp0 = fmaf(-128.f, s0, b0), bp1 = fmaf(-128.f, s1, b1);
+    acc[0] += fmaf(s0, dd[0], bp0 * h0);
+    acc[1] += fmaf(s0, dd[1], bp0 * h1);
+    acc[2] += fmaf(s1, dd[2], bp1 * h0);
+    acc[3] += fmaf(s1, dd[3], bp1 * h1);
+  }
+  uint16_t *wparts = wsp<uint16_t>(p, p.L.wparts);
+  uint16_t *sparts = wsp<uint16_t>(p, p.L.sparts);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int n = 2 * c + (q & 1);
+    if (n >= T) continue;
+    const int row = (q >> 1) ? r1 : r0;
+    const float yb = rbf(acc[q]);
+    if (is_shared) {
+      sparts[(size_t)n * H + row] = f2bf(yb);
+    } else if (s_rank[n] >= 0) {
+      wparts[((size_t)n * p.k + s_rank[n]) * H + row] = f2bf(__fmul_rn(yb, s_score[n]));
+    }
+  }
+
+  // ---- fused combine: the last entry CTA of this row block adds the routes.
+  __threadfence();
+  __syncthreads();
+  unsigned *cnt = wsp<unsigned>(p, p.L.rb_count) + rb;
+  if (tid == 0) s_ticket = atomicAdd(cnt, 1u);
+  __syncthreads();
+  if (s_ticket == (unsigned)n_entries - 1) {
+    __threadfence();
+    const int k = p.k;
+    const uint32_t *wp = wsp<const uint32_t>(p, p.L.wparts);
+    const int32_t *ok = wsp<const int32_t>(p, p.L.route_ok);
+    for (int q = tid; q < T * 64; q += K3_THREADS) {  // (token, column pair)
+      const int t = q >> 6, c2 = 64 * rb + (q & 63);
+      uint32_t wv[DEC_MAX_K];
+      int okv[DEC_MAX_K];
+#pragma unroll
+      for (int j = 0; j < DEC_MAX_K; ++j) {
+        if (j < k) {
+          okv[j] = __ldcg(ok + t * k + j);
+          wv[j] = __ldcg(wp + ((size_t)t * k + j) * (H / 2) + c2);
+        }
+      }
+      double s0 = 0.0, s1 = 0.0;
+#pragma unroll
+      for (int j = 0; j < DEC_MAX_K; ++j) {
+        if (j < k && okv[j]) {
+          s0 += (double)bf2f(wv[j] & 0xFFFF);
+          s1 += (double)bf2f(wv[j] >> 16);
+        }
+      }
+      float y0 = rbf((float)s0), y1 = rbf((float)s1);
+      if (p.has_shared) {
+        const float gate = __ldcg(wsp<const float>(p, p.L.sgate) + t);
+        const uint32_t sw = __ldcg(wsp<const uint32_t>(p, p.L.sparts) + (size_t)t * (H / 2) + c2);
+        y0 = rbf(__fadd_rn(y0, rbf(__fmul_rn(gate, bf2f(sw & 0xFFFF)))));
+        y1 = rbf(__fadd_rn(y1, rbf(__fmul_rn(gate, bf2f(sw >> 16)))));
+      }
+      const size_t oi = (size_t)t * (H / 2) + c2;
+      if (p.residual) {
+        const uint32_t rr = reinterpret_cast<const uint32_t *>(p.residual)[oi];
+        y0 = rbf(__fadd_rn(bf2f(rr & 0xFFFF), y0));
+        y1 = rbf(__fadd_rn(bf2f(rr >> 16), y1));
+      }
+      reinterpret_cast<uint32_t *>(p.out)[oi] = pack_bf2(y0, y1);
+    }
+    if (tid == 0) *cnt = 0u;  // ready for the next launch
+  }
+  span.end();
+}
+
+static int sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
 }
 
 }  // namespace vb
@@ -673,10 +879,11 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   VB_REQUIRE(T >= 1 && T <= DEC_MAX_T, "vb_moe_decode: tokens=%d not in [1,8]", T);
   VB_REQUIRE(a->bits == 4, "vb_moe_decode: bits=%d (only 4-bit)", a->bits);
   VB_REQUIRE(a->group == 64 || a->group == 128, "vb_moe_decode: group=%d", a->group);
-  VB_REQUIRE(H % 512 == 0 && H >= 512 && H <= 8192, "vb_moe_decode: hidden=%d", H);
+  VB_REQUIRE(H == 512 || H == 1024 || H == 2048 || H == 4096, "vb_moe_decode: hidden=%d", H);
   VB_REQUIRE(I == 128 || I == 256 || I == 512, "vb_moe_decode: inter=%d", I);
+  VB_REQUIRE(H / a->group >= 8 && I >= a->group, "vb_moe_decode: group too large");
   VB_REQUIRE(E >= k && E <= DEC_MAX_E, "vb_moe_decode: num_experts=%d", E);
-  VB_REQUIRE(k >= 1 && k <= DEC_MAX_K && k <= 32, "vb_moe_decode: top_k=%d", k);
+  VB_REQUIRE(k >= 1 && k <= DEC_MAX_K, "vb_moe_decode: top_k=%d", k);
   VB_REQUIRE(a->x && a->router_w && a->slot_table && a->out, "vb_moe_decode: null tensor");
   VB_REQUIRE(a->pool.ptr[0] && a->pool.cap > 0, "vb_moe_decode: empty pool");
   const bool has_shared = a->shared.ptr[0] != nullptr;
@@ -684,6 +891,11 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   DecodeLayout L = decode_layout(T, H, I, E, k);
   VB_REQUIRE(a->workspace && a->workspace_bytes >= L.total,
              "vb_moe_decode: workspace %zu < %zu", a->workspace_bytes, L.total);
+  VB_REQUIRE(((uintptr_t)a->workspace % 256) == 0, "vb_moe_decode: workspace must be 256-byte aligned");
+  for (int i = 0; i < 9; ++i)
+    VB_REQUIRE(((uintptr_t)a->pool.ptr[i] % 16) == 0 && (a->pool.slot_stride[i] % 16) == 0 &&
+                   (!has_shared || (((uintptr_t)a->shared.ptr[i] % 16) == 0)),
+               "vb_moe_decode: pool tensors and slot strides must be 16-byte aligned");
 
   DecodeParams p;
   p.T = T; p.H = H; p.I = I; p.E = E; p.k = k; p.norm_topk = a->norm_topk;
@@ -696,41 +908,48 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   p.out = a->out; p.out_scores = a->out_scores; p.out_inds = a->out_inds;
   p.out_local = a->out_local; p.status = a->status;
   p.ws = static_cast<uint8_t *>(a->workspace);
+  p.trace = a->trace;
   p.L = L;
-  cudaStream_t s = as_stream(stream);
 
-  // The router's last-CTA ticket counter lives in the first workspace word:
-  // callers zero-fill the workspace once; every call leaves it at zero.
+  void (*k1)(DecodeParams) = nullptr;
+  void (*k2)(DecodeParams) = nullptr;
+  const int per = E <= 256 ? 8 : (E <= 512 ? 16 : 32);
+#define VB_K1(HH) (per == 8 ? moe_router_kernel<HH, 8> : per == 16 ? moe_router_kernel<HH, 16> \
+                                                      : moe_router_kernel<HH, 32>)
+  switch (H) {
+    case 512: k1 = VB_K1(512); k2 = moe_gateup_kernel<512>; break;
+    case 1024: k1 = VB_K1(1024); k2 = moe_gateup_kernel<1024>; break;
+    case 2048: k1 = VB_K1(2048); k2 = moe_gateup_kernel<2048>; break;
+    default: k1 = VB_K1(4096); k2 = moe_gateup_kernel<4096>; break;
+  }
+#undef VB_K1
+  void (*k3)(DecodeParams) = nullptr;
+  switch (I) {
+    case 128: k3 = moe_down_kernel<128>; break;
+    case 256: k3 = moe_down_kernel<256>; break;
+    default: k3 = moe_down_kernel<512>; break;
+  }
+
+  cudaStream_t s = as_stream(stream);
   cudaEvent_t *ev = a->timing_events ? (cudaEvent_t *)a->timing_events : nullptr;
+  const bool pdl = ev == nullptr;  // event records would break the PDL chain
+  // K1 is a PDL secondary of whatever ran before it on the stream (the
+  // previous block's down kernel): it only reads weights before the wait.
   if (ev) cudaEventRecord(ev[0], s);
   const size_t smem1 = (size_t)T * H * 2;
-  if (smem1 > 48 * 1024) {
-    cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem1);
-  }
+  if (smem1 > 48 * 1024)
+    cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
   const int grid1 = (E + DEC_ROUTER_WARPS - 1) / DEC_ROUTER_WARPS;
-  moe_router_kernel<<<grid1, DEC_ROUTER_WARPS * 32, smem1, s>>>(p);
-  int rc = check_launch("moe_router_kernel");
-  if (rc) return rc;
+  cudaError_t err = vb_launch(k1, dim3(grid1), dim3(DEC_ROUTER_WARPS * 32), smem1, s, pdl, p);
+  if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_router_kernel: %s", cudaGetErrorString(err));
   if (ev) cudaEventRecord(ev[1], s);
 
-  dim3 grid2(L.max_entries, I / 16);
-  const int NG = H / 64;
-  if (NG <= 8) moe_gateup_kernel<1><<<grid2, 256, 0, s>>>(p);
-  else if (NG <= 16) moe_gateup_kernel<2><<<grid2, 256, 0, s>>>(p);
-  else if (NG <= 32) moe_gateup_kernel<4><<<grid2, 256, 0, s>>>(p);
-  else if (NG <= 64) moe_gateup_kernel<8><<<grid2, 256, 0, s>>>(p);
-  else moe_gateup_kernel<16><<<grid2, 256, 0, s>>>(p);
-  rc = check_launch("moe_gateup_kernel");
-  if (rc) return rc;
+  err = vb_launch(k2, dim3(L.max_entries, I / 16), dim3(K2_THREADS), 0, s, pdl, p);
+  if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_gateup_kernel: %s", cudaGetErrorString(err));
   if (ev) cudaEventRecord(ev[2], s);
 
-  const int grid3 = H / 16;
-  if (I == 128) moe_down_kernel<2><<<grid3, 256, 0, s>>>(p);
-  else if (I == 256) moe_down_kernel<4><<<grid3, 256, 0, s>>>(p);
-  else moe_down_kernel<8><<<grid3, 256, 0, s>>>(p);
-  rc = check_launch("moe_down_kernel");
-  if (rc) return rc;
+  err = vb_launch(k3, dim3(L.max_entries, H / 128), dim3(K3_THREADS), 0, s, pdl, p);
+  if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_down_kernel: %s", cudaGetErrorString(err));
   if (ev) cudaEventRecord(ev[3], s);
   return VB_OK;
 }

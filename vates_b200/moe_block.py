@@ -64,7 +64,7 @@ class MoeBlock:
         self._shared_c = self.shared.c_struct() if self.shared is not None else None
 
     def decode_args(self, x, out, residual=None, debug=None, status=None,
-                    norm_eps: float = 0.0, timing=None) -> VbMoeDecodeArgs:
+                    norm_eps: float = 0.0, timing=None, trace=None) -> VbMoeDecodeArgs:
         T = int(x.shape[0])
         need = lib.vb_moe_decode_workspace_size(T, self.hidden, self.inter,
                                                 self.num_experts, self.top_k)
@@ -91,11 +91,12 @@ class MoeBlock:
         a.workspace_bytes = ws.numel()
         if timing is not None:
             a.timing_events = C.cast(timing, C.c_void_p)
+        a.trace = ptr(trace)
         return a
 
     def decode(self, x: torch.Tensor, out: torch.Tensor | None = None, residual=None,
                debug: dict | None = None, status=None, stream=None,
-               norm_eps: float = 0.0, timing=None) -> torch.Tensor:
+               norm_eps: float = 0.0, timing=None, trace=None) -> torch.Tensor:
         """``FileStreamingMoeBlock.__call__`` for ``T <= 8`` tokens.
 
         ``x`` bf16 ``[T, H]`` (or ``[B, S, H]`` with ``B*S <= 8``).
@@ -106,7 +107,7 @@ class MoeBlock:
         if out is None:
             out = torch.empty_like(x2)
         a = self.decode_args(x2, out, residual=residual, debug=debug, status=status,
-                             norm_eps=norm_eps, timing=timing)
+                             norm_eps=norm_eps, timing=timing, trace=trace)
         check(lib.vb_moe_decode(C.byref(a), stream_handle(stream)), "vb_moe_decode")
         return out.reshape(shape)
 

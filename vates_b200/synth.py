@@ -118,11 +118,13 @@ class DecodeStack:
         torch.cuda.synchronize()
         return swaps
 
-    def step(self, stream=None):
-        """One whole-stack step: 48 chained MoE blocks over the T tokens."""
+    def step(self, stream=None, trace=None):
+        """One whole-stack step: 48 chained MoE blocks over the T tokens.
+        ``trace`` (int64 [L, 8] device tensor) records per-layer kernel spans."""
         for l, blk in enumerate(self.blocks):
             blk.decode(self.hs[l], out=self.hs[l + 1], residual=self.hs[l],
-                       norm_eps=self.norm_eps, stream=stream)
+                       norm_eps=self.norm_eps, stream=stream,
+                       trace=None if trace is None else trace[l])
         return self.hs[-1]
 
     def unique_experts(self) -> list[int]:
