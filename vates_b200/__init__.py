@@ -4,10 +4,17 @@
 - pool slot-table gather,
 - IsoQuant K4/V3 KV cache quantize + quantized GQA attention.
 
-Importing the package loads ``libvates_b200.so`` (built in-tree with
-``python -m vates_b200.build``); without it the import fails: there is no CPU
-fallback.
+Every compute module imports ``vates_b200._lib``, which loads
+``libvates_b200.so`` (built in-tree with ``python -m vates_b200.build``) and
+raises if it is missing: there is no CPU fallback. The package itself loads
+the library on first use of ``lib``/``VbError``/``EXPORTED`` so that the
+build step can run before the library exists.
 """
-from ._lib import lib, VbError, EXPORTED  # noqa: F401  (loads the library)
-
 __version__ = "0.1.0"
+
+
+def __getattr__(name):
+    if name in ("lib", "VbError", "EXPORTED", "check"):
+        from . import _lib
+        return getattr(_lib, name)
+    raise AttributeError(name)
