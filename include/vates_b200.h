@@ -141,11 +141,12 @@ typedef struct VbMoeDecodeArgs {
   void *const *timing_events;   /* nullable: 4 cudaEvent_t recorded before the
                                    router, gate/up and down kernels and after
                                    the down kernel (profiling only) */
-  uint64_t *trace;              /* nullable device [12]: [0..7] per kernel
-                                   (router, gate/up, down, combine) the min
+  uint64_t *trace;              /* nullable device [12]: [0..5] per kernel
+                                   (router, gate/up, down+combine) the min
                                    start and max end %globaltimer (ns) over
                                    its CTAs, initialised by the caller to
-                                   (UINT64_MAX, 0); [8..10] router markers
+                                   (UINT64_MAX, 0); [6..7] unused; [8..10]
+                                   router markers
                                    (latest CTA past the PDL wait, latest CTA
                                    done with its rows, top-k start),
                                    initialised to 0 (profiling only) */
@@ -158,6 +159,29 @@ size_t vb_moe_decode_workspace_size(int32_t tokens, int32_t hidden,
                                     int32_t inter, int32_t num_experts,
                                     int32_t top_k);
 int vb_moe_decode(const VbMoeDecodeArgs *args, vb_stream_t stream);
+
+/* Decode block without a caller workspace. No counterpart in the reference:
+ * this is for callers that cannot allocate device memory for scratch, such
+ * as a host framework that owns every device buffer through its own pool
+ * and hands a plugin only the tensors of the op, or a latency-critical
+ * decode loop that must not call cudaMalloc (which can synchronise the
+ * device). The scratch is one fixed device array inside this library of
+ * VB_MOE_DECODE_NOALLOC_SCRATCH_BYTES; shapes whose
+ * vb_moe_decode_workspace_size exceeds it are rejected with
+ * VB_ERR_WORKSPACE and a message naming both sizes.
+ * args->workspace and args->workspace_bytes are ignored. Apart from that it
+ * computes exactly what vb_moe_decode computes.
+ * - The first call on a device (current device at the call) looks up the
+ *   array's device address once; make that first call before any stream
+ *   capture on that device. The address belongs to the device's primary
+ *   context: do not call this entry point again after cudaDeviceReset.
+ * - Every call clears the array's counters on `stream` before its kernels
+ *   and allocates nothing (no cudaMalloc, cudaFree or allocating library).
+ * - All calls on a device share the one array, which keeps the last call's
+ *   contents: calls that can overlap on the GPU (other streams, other
+ *   threads) race on it; serialise them on one stream. */
+#define VB_MOE_DECODE_NOALLOC_SCRATCH_BYTES (2u << 20)
+int vb_moe_decode_noalloc(const VbMoeDecodeArgs *args, vb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Deterministic route reduce: replaces deterministic_route_reduce

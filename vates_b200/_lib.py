@@ -67,6 +67,7 @@ _SIGNATURES = {
                                   _I32, _I32, _P, _P, _P, _SZ, _P]),
     "vb_moe_decode_workspace_size": (_SZ, [_I32, _I32, _I32, _I32, _I32]),
     "vb_moe_decode": (_I32, [C.POINTER(VbMoeDecodeArgs), _P]),
+    "vb_moe_decode_noalloc": (_I32, [C.POINTER(VbMoeDecodeArgs), _P]),
     "vb_route_reduce_workspace_size": (_SZ, [_I32, _I32]),
     "vb_route_reduce": (_I32, [_P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P,
                                _SZ, _P]),

@@ -28,6 +28,8 @@
 //  K4 combine: per token and column, the k routes are added in rank order
 //     (exact double sum of bf16 values, rounded to float32 then bf16), then
 //     the gated shared expert and the optional residual.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace vb {
@@ -862,6 +864,36 @@ static int sm_count() {
 
 using namespace vb;
 
+// Scratch of vb_moe_decode_noalloc: one fixed array per device, shared by
+// every call of that entry point on the device. Its device address is looked
+// up once per device (with that device current) and cached here.
+static __device__ __align__(256) uint8_t g_decode_noalloc_scratch[VB_MOE_DECODE_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kNoallocMaxDevices];
+
+int noalloc_scratch(void **out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return set_error(VB_ERR_CUDA, "vb_moe_decode_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  VB_REQUIRE(dev >= 0 && dev < kNoallocMaxDevices, "vb_moe_decode_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_decode_noalloc_scratch);
+    if (e != cudaSuccess || !ptr)
+      return set_error(VB_ERR_CUDA, "vb_moe_decode_noalloc: cudaGetSymbolAddress: %s",
+                       cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = ptr;
+  }
+  *out = g_noalloc_ptr[dev];
+  return VB_OK;
+}
+}  // namespace
+
 extern "C" {
 
 size_t vb_moe_decode_workspace_size(int32_t tokens, int32_t hidden,
@@ -952,6 +984,33 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_down_kernel: %s", cudaGetErrorString(err));
   if (ev) cudaEventRecord(ev[3], s);
   return VB_OK;
+}
+
+int vb_moe_decode_noalloc(const VbMoeDecodeArgs *a, vb_stream_t stream) {
+  VB_REQUIRE(a, "vb_moe_decode_noalloc: null args");
+  const size_t need = vb_moe_decode_workspace_size(a->tokens, a->hidden, a->inter,
+                                                   a->num_experts, a->top_k);
+  VB_REQUIRE(need > 0, "vb_moe_decode_noalloc: invalid shape");
+  if (need > VB_MOE_DECODE_NOALLOC_SCRATCH_BYTES)
+    return set_error(VB_ERR_WORKSPACE,
+                     "vb_moe_decode_noalloc: this shape needs %zu bytes of scratch, more than "
+                     "the fixed %zu-byte array; use vb_moe_decode with a workspace",
+                     need, (size_t)VB_MOE_DECODE_NOALLOC_SCRATCH_BYTES);
+  void *scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc != VB_OK) return rc;
+  // The array keeps the previous call's contents: zero the words the kernels
+  // expect at zero (route ticket, entry count, shared gates, row-block
+  // tickets) before this call's kernels, in stream order.
+  const DecodeLayout L = decode_layout(a->tokens, a->hidden, a->inter, a->num_experts, a->top_k);
+  const size_t clear = L.rb_count + sizeof(unsigned) * (size_t)(a->hidden / 128);
+  const cudaError_t e = cudaMemsetAsync(scratch, 0, clear, as_stream(stream));
+  if (e != cudaSuccess)
+    return set_error(VB_ERR_CUDA, "vb_moe_decode_noalloc: clearing scratch: %s", cudaGetErrorString(e));
+  VbMoeDecodeArgs b = *a;
+  b.workspace = scratch;
+  b.workspace_bytes = VB_MOE_DECODE_NOALLOC_SCRATCH_BYTES;
+  return vb_moe_decode(&b, stream);
 }
 
 }  // extern "C"
