@@ -251,7 +251,7 @@ def run_decode(args, world, rank, local):
 
     # ---- warm in-graph kernel spans from the kernels' %globaltimer trace ----
     trace = torch.empty((L, 16), dtype=torch.int64, device="cuda")
-    init = torch.tensor([-1, 0] * 4 + [0] * 8, dtype=torch.int64, device="cuda")
+    init = torch.tensor([-1, 0] * 3 + [0] * 10, dtype=torch.int64, device="cuda")
     tgraph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(tgraph, stream=stream):
         st.step(stream=stream, trace=trace)
@@ -266,7 +266,7 @@ def run_decode(args, world, rank, local):
     kspan = [(tr[:, 2 * i + 1] - tr[:, 2 * i]).mean() / 1e3 for i in range(3)]
     layer_us = (tr[1:, 0] - tr[:-1, 0]).mean() / 1e3
     gaps = [(tr[:, 2 * (i + 1)] - tr[:, 2 * i + 1]).mean() / 1e3 for i in range(2)]
-    router_marks = [(tr[:, m] - tr[:, 0]).mean() / 1e3 for m in (8, 9, 10)]
+    router_marks = [(tr[:, m] - tr[:, 0]).mean() / 1e3 for m in (8, 11, 12, 13, 9, 10, 14, 15, 6, 7)]
     del tgraph
 
     # ---- dominant kernel (gate/up) timed per launch with CUDA events ----

@@ -141,11 +141,11 @@ typedef struct VbMoeDecodeArgs {
   void *const *timing_events;   /* nullable: 4 cudaEvent_t recorded before the
                                    router, gate/up and down kernels and after
                                    the down kernel (profiling only) */
-  uint64_t *trace;              /* nullable device [12]: [0..5] per kernel
+  uint64_t *trace;              /* nullable device [16]: [0..5] per kernel
                                    (router, gate/up, down+combine) the min
                                    start and max end %globaltimer (ns) over
                                    its CTAs, initialised by the caller to
-                                   (UINT64_MAX, 0); [6..7] unused; [8..10]
+                                   (UINT64_MAX, 0); [6..7] unused; [8..15]
                                    router markers
                                    (latest CTA past the PDL wait, latest CTA
                                    done with its rows, top-k start),

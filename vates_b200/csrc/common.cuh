@@ -83,6 +83,11 @@ __device__ __forceinline__ uint4 ldg_nc_v4(const void *p) {
 __device__ __forceinline__ uint4 ldg_v4(const void *p) {
   return *reinterpret_cast<const uint4 *>(p);
 }
+// Asynchronous bulk prefetch of [p, p + bytes) into L2 (TMA unit; p and
+// bytes multiples of 16). A hint: it neither blocks nor completes anything.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void prefetch_l2(const void *p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }

@@ -28,7 +28,9 @@
 //  K4 combine: per token and column, the k routes are added in rank order
 //     (exact double sum of bf16 values, rounded to float32 then bf16), then
 //     the gated shared expert and the optional residual.
+#include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 
@@ -89,7 +91,6 @@ static DecodeLayout decode_layout(int T, int H, int I, int E, int k) {
 struct DecodeParams {
   int T, H, I, E, k, norm_topk, gshift, has_shared;
   float norm_eps;
-  int stages2, stages3;
   const uint16_t *x, *router_w, *shared_gate_w, *residual;
   const float *router_bias;
   const int32_t *table;
@@ -141,6 +142,37 @@ __device__ __forceinline__ const uint8_t *pool_ptr(const VbQuantPool &pool, int 
   return (const uint8_t *)pool.ptr[t] + (size_t)slot * pool.slot_stride[t];
 }
 
+// Bytes of tensor t (gate w,s,b, up w,s,b, down w,s,b) of one 4-bit expert.
+__device__ __forceinline__ uint32_t expert_tensor_bytes(const DecodeParams &p, int t) {
+  const int f = t % 3;
+  const uint32_t rows = t < 6 ? (uint32_t)p.I : (uint32_t)p.H;
+  const uint32_t cols = t < 6 ? (uint32_t)p.H : (uint32_t)p.I;
+  return f == 0 ? rows * (cols / 2) : rows * (cols >> (6 + p.gshift)) * 2u;
+}
+
+constexpr uint32_t PF_PIECE = 16u << 10;
+
+// L2 bulk prefetch of tensors [t0, t1) of one expert, pieces [first, ...) of
+// the expert's piece sequence with stride `step` (pieces are 16 KB).
+__device__ __forceinline__ int expert_pieces(const DecodeParams &p, int t0, int t1) {
+  int n = 0;
+  for (int t = t0; t < t1; ++t) n += (expert_tensor_bytes(p, t) + PF_PIECE - 1) / PF_PIECE;
+  return n;
+}
+__device__ __forceinline__ void prefetch_expert_piece(const DecodeParams &p, const VbQuantPool &pool,
+                                                      int slot, int t0, int piece) {
+  for (int t = t0; t < 9; ++t) {
+    const uint32_t tb = expert_tensor_bytes(p, t);
+    const int c = (tb + PF_PIECE - 1) / PF_PIECE;
+    if (piece < c) {
+      const uint32_t off = (uint32_t)piece * PF_PIECE;
+      prefetch_l2_bulk(pool_ptr(pool, t, slot) + off, min(PF_PIECE, tb - off));
+      return;
+    }
+    piece -= c;
+  }
+}
+
 __device__ __forceinline__ uint2 lds64(const uint8_t *p) {
   return *reinterpret_cast<const uint2 *>(p);
 }
@@ -176,6 +208,11 @@ moe_router_kernel(DecodeParams p) {
 #pragma unroll
     for (int u = 0; u < NVL; ++u) gv[u] = ldg_nc_v4(grow + u * 32 + lane);
   }
+  if (p.has_shared && tid == 0) {
+    // The shared expert is fixed per layer: stream it into L2 right away.
+    const int np = expert_pieces(p, 0, 9);
+    for (int i = blockIdx.x; i < np; i += gridDim.x) prefetch_expert_piece(p, p.shared, 0, 0, i);
+  }
   pdl_wait();
   pdl_launch_dependents();
   trace_mark(p.trace, 8);
@@ -201,6 +238,7 @@ moe_router_kernel(DecodeParams p) {
     }
   }
   __syncthreads();
+  trace_mark(p.trace, 11);
   if (p.norm_eps > 0.f) {
     // Unit-weight RMSNorm of the block input (decoder post-attention norm):
     // y = bf16(x * (1/sqrt(mean(x^2) + eps))), float32 math with an exact
@@ -240,6 +278,7 @@ moe_router_kernel(DecodeParams p) {
     __syncthreads();
   }
 
+  trace_mark(p.trace, 12);
   if (e < E) {
     float acc[DEC_MAX_T];
 #pragma unroll
@@ -277,6 +316,7 @@ moe_router_kernel(DecodeParams p) {
     }
   }
 
+  trace_mark(p.trace, 13);
   {
     // x in MMA fragment order (xperm) and per-64-column sums (xsum), spread
     // over all CTAs (each holds the whole normalised x in shared memory).
@@ -428,6 +468,7 @@ moe_router_kernel(DecodeParams p) {
       if (p.out_local) p.out_local[t * k + lane] = slot;
     }
   }
+  trace_mark(p.trace, 14);
   // Entry table in shared memory: slot -1 / rank -1 defaults.
   for (int i = tid; i < (DEC_MAX_T * DEC_MAX_K + 1) * (int)(sizeof(DecEntry) / 4);
        i += blockDim.x) {
@@ -474,6 +515,7 @@ moe_router_kernel(DecodeParams p) {
   }
   __syncthreads();
   const int n = shared_n + n_routed;
+  trace_mark(p.trace, 15);
   const int words = n * (int)(sizeof(DecEntry) / 4);
   int32_t *dst = wsp<int32_t>(p, p.L.entries);
   for (int i = tid; i < words; i += blockDim.x)
@@ -486,13 +528,39 @@ moe_router_kernel(DecodeParams p) {
 }
 
 // ----------------------------------------------------------------------------
-// K2: gate/up + SwiGLU. One CTA per item (entry, 16 intermediate rows). The 8
-// warps split the hidden dimension (GPW groups of 64 columns each) and load
-// their packed rows, scales and x fragments straight into registers; many
-// small independent CTAs per SM hide each other's memory latency.
+// K2: gate/up + SwiGLU, persistent. One CTA per SM walks the items (entry,
+// 16 intermediate rows) b, b + grid, ... An item's 16 gate rows, 16 up rows
+// and their scales/biases (each contiguous in the pool) are copied by all
+// threads with 16-byte cp.async into an S-stage shared-memory ring, S-1
+// items ahead of the math. Rows are padded by 32 bytes so that the MMA
+// fragment reads (row g, 8 bytes at column 8c) fall in distinct banks. The
+// shared expert's item is requested before the PDL wait. The 8 warps split
+// the hidden dimension (GPW groups of 64 columns each); their partials are
+// added in warp order, then SwiGLU (bf16 per op) and h in fragment order.
 // ----------------------------------------------------------------------------
-constexpr int K2_THREADS = 256;
-constexpr int K2_WARPS = K2_THREADS / 32;
+constexpr int K2_SMEM_MAX = 200 * 1024;
+
+template <int H, int GS>  // GS: log2(group / 64)
+struct GateUpTile {
+  static constexpr int NG = H / 64;
+  static constexpr int WARPS = NG < 16 ? NG : 16;
+  static constexpr int THREADS = 32 * WARPS;
+  static constexpr int GPW = NG / WARPS;
+  static constexpr int NS = H >> (6 + GS);          // scales per row
+  static constexpr int SC = GPW >> GS ? GPW >> GS : 1;  // scales per warp row slice
+  static constexpr int ROWB = H / 2;                // packed bytes per row
+  static constexpr int PITCH = ROWB + 32;           // padded smem row pitch
+  static constexpr int WBYTES = 16 * PITCH;         // 16 rows of one matrix
+  static constexpr int SBYTES = 16 * NS * 2;        // 16 rows of one scale tensor
+  static constexpr int SCH = SBYTES / 16;           // its 16-byte chunks
+  static constexpr int STAGE = 2 * WBYTES + 4 * SBYTES;
+  static constexpr int S = (K2_SMEM_MAX / STAGE) < 6 ? (K2_SMEM_MAX / STAGE) : 6;
+  static constexpr int CPR = ROWB / 16;             // 16-byte chunks per row
+  static constexpr int RSTEP = THREADS / CPR;       // rows per copy pass
+  static constexpr int PASSES = 16 / RSTEP;
+  static constexpr int SMEM = S * STAGE;
+  static_assert(S >= 2 && RSTEP >= 1 && PASSES * RSTEP == 16, "gate/up tile");
+};
 
 // Load 2*count bytes of bf16 scales (count in {1,2,4,8}) into a uint4.
 __device__ __forceinline__ uint4 ld_scales(const uint16_t *ptr, int count) {
@@ -510,66 +578,113 @@ __device__ __forceinline__ uint4 ld_scales(const uint16_t *ptr, int count) {
   }
   return r;
 }
+
+// bf16 scales (count in {1,2,4,8}) from shared memory into a uint4.
+__device__ __forceinline__ uint4 lds_scales(const uint8_t *ptr, int count) {
+  uint4 r = make_uint4(0, 0, 0, 0);
+  if (count >= 8) {
+    r = *reinterpret_cast<const uint4 *>(ptr);
+  } else if (count == 4) {
+    const uint2 v = *reinterpret_cast<const uint2 *>(ptr);
+    r.x = v.x;
+    r.y = v.y;
+  } else if (count == 2) {
+    r.x = *reinterpret_cast<const unsigned *>(ptr);
+  } else {
+    r.x = *reinterpret_cast<const uint16_t *>(ptr);
+  }
+  return r;
+}
 __device__ __forceinline__ float bf_at(const uint4 &v, int i) {
   const uint32_t w = i < 2 ? v.x : (i < 4 ? v.y : (i < 6 ? v.z : v.w));
   return bf2f((i & 1) ? (w >> 16) : (w & 0xFFFF));
 }
 
-template <int H>
-__global__ void __launch_bounds__(K2_THREADS, 2) moe_gateup_kernel(DecodeParams p) {
-  constexpr int NG = H / 64;
-  constexpr int GPW = NG / K2_WARPS;
-  __shared__ float red[K2_WARPS][256];
+// Copy item (expert tensors `base`, row block rb) into one ring stage.
+// base: gate w, gate s, gate b, up w, up s, up b of the expert's slot.
+template <int H, int GS>
+__device__ __forceinline__ void gateup_issue(uint8_t *stage, const uint8_t *const (&base)[6],
+                                             int rb, int tid) {
+  using Tl = GateUpTile<H, GS>;
+  const int r0 = tid / Tl::CPR, c16 = (tid % Tl::CPR) * 16;
+  const uint8_t *gw = base[0] + (size_t)(16 * rb) * Tl::ROWB;
+  const uint8_t *uw = base[3] + (size_t)(16 * rb) * Tl::ROWB;
+#pragma unroll
+  for (int j = 0; j < Tl::PASSES; ++j) {
+    const int r = r0 + j * Tl::RSTEP;
+    cp_async16(stage + r * Tl::PITCH + c16, gw + r * Tl::ROWB + c16);
+    cp_async16(stage + Tl::WBYTES + r * Tl::PITCH + c16, uw + r * Tl::ROWB + c16);
+  }
+  // Scale tensors (16 rows x NS bf16 each), compact in shared memory.
+#pragma unroll
+  for (int q0 = 0; q0 < 4 * Tl::SCH; q0 += Tl::THREADS) {
+    const int q = q0 + tid;
+    if (q < 4 * Tl::SCH) {
+      const int a = q / Tl::SCH, c = q % Tl::SCH;
+      const uint8_t *t = a == 0 ? base[1] : a == 1 ? base[2] : a == 2 ? base[4] : base[5];
+      cp_async16(stage + 2 * Tl::WBYTES + a * Tl::SBYTES + c * 16,
+                 t + (size_t)rb * Tl::SBYTES + c * 16);
+    }
+  }
+}
+
+template <int H, int GS>
+__global__ void __launch_bounds__(GateUpTile<H, GS>::THREADS, 1) moe_gateup_kernel(DecodeParams p) {
+  using Tl = GateUpTile<H, GS>;
+  constexpr int NG = Tl::NG;
+  constexpr int GPW = Tl::GPW;
+  constexpr int S = Tl::S;
+  constexpr int WARPS = Tl::WARPS;
+  extern __shared__ __align__(16) uint8_t ring[];
+  __shared__ float red[WARPS][256];
   __shared__ float hval[128];
-  __shared__ int s_slot, s_n;
+  __shared__ int s_slot[DEC_MAX_T * DEC_MAX_K + 1];
+  __shared__ int s_n;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
   const int T = p.T;
   SpanTrace span(p.trace, 1);
-  const int e = blockIdx.x, rb = blockIdx.y;
   const int G0 = warp * GPW;
-  const int row0 = 16 * rb + g, row1 = row0 + 8;
-  const int NS = H >> (6 + p.gshift);
-  const int sc_count = GPW >> p.gshift ? GPW >> p.gshift : 1;  // scales per row slice
+  const int rb_shift = 31 - __clz(p.I / 16);  // items per entry = I/16
+  const int RB = 1 << rb_shift;
+  const int b = blockIdx.x, grid = gridDim.x;
 
-  uint2 ag0[GPW], ag1[GPW], au0[GPW], au1[GPW];
-  uint4 sv[8];  // gate_s r0, r1, gate_b r0, r1, up_s r0, r1, up_b r0, r1
-  auto load_w = [&](const VbQuantPool &pool, int slot) {
-    const uint8_t *gw = pool_ptr(pool, 0, slot), *uw = pool_ptr(pool, 3, slot);
+  auto bases = [&](const VbQuantPool &pool, int slot, const uint8_t *(&base)[6]) {
 #pragma unroll
-    for (int i = 0; i < GPW; ++i) {
-      const size_t col = (size_t)(G0 + i) * 32 + 8 * c;
-      ag0[i] = ldg_nc_v2(gw + (size_t)row0 * (H / 2) + col);
-      ag1[i] = ldg_nc_v2(gw + (size_t)row1 * (H / 2) + col);
-      au0[i] = ldg_nc_v2(uw + (size_t)row0 * (H / 2) + col);
-      au1[i] = ldg_nc_v2(uw + (size_t)row1 * (H / 2) + col);
-    }
-    const int s0 = G0 >> p.gshift;
-#pragma unroll
-    for (int a = 0; a < 8; ++a) {
-      const int t = (a < 4 ? 1 : 4) + ((a >> 1) & 1);  // gate_s, gate_b, up_s, up_b
-      const int row = (a & 1) ? row1 : row0;
-      const uint16_t *sp = reinterpret_cast<const uint16_t *>(pool_ptr(pool, t, slot)) + (size_t)row * NS + s0;
-      sv[a] = ld_scales(sp, sc_count);
-    }
+    for (int t = 0; t < 6; ++t) base[t] = pool_ptr(pool, t, slot);
   };
-
-  // The shared expert (entry 0) needs no routing: load before the PDL wait.
-  const bool pre = p.has_shared && e == 0;
-  if (pre) load_w(p.shared, 0);
+  // The shared expert (entry 0) needs no routing: its item goes first.
+  const bool pre = p.has_shared && b < RB;
+  if (pre) {
+    const uint8_t *base[6];
+    bases(p.shared, 0, base);
+    gateup_issue<H, GS>(ring, base, b, tid);
+  }
+  cp_async_commit();
   pdl_wait();
   pdl_launch_dependents();
-  if (!pre) {
-    if (tid == 0) {
-      s_n = *wsp<const int32_t>(p, p.L.n_entries);
-      s_slot = wsp<const DecEntry>(p, p.L.entries)[e].slot;
+  const int max_e = p.L.max_entries;
+  if (tid == 0) s_n = *wsp<const int32_t>(p, p.L.n_entries);
+  if (tid < max_e) s_slot[tid] = wsp<const DecEntry>(p, p.L.entries)[tid].slot;
+  __syncthreads();
+  trace_mark(p.trace, 6);
+  const int n_items = s_n << rb_shift;
+  auto issue = [&](int k) {
+    const int i = b + k * grid;
+    if (i < n_items) {
+      const int e = i >> rb_shift;
+      const uint8_t *base[6];
+      if (p.has_shared && e == 0) bases(p.shared, 0, base);
+      else bases(p.pool, s_slot[e], base);
+      gateup_issue<H, GS>(ring + (k % S) * Tl::STAGE, base, i & (RB - 1), tid);
     }
-    __syncthreads();
-    if (e >= s_n) {
-      span.end();
-      return;
-    }
-    load_w(p.pool, s_slot);
+  };
+  if (!pre) issue(0);
+  cp_async_commit();
+#pragma unroll 1
+  for (int k = 1; k < S - 1; ++k) {
+    issue(k);
+    cp_async_commit();
   }
 
   // x fragments and column sums of this warp's groups (written by the router).
@@ -593,73 +708,101 @@ __global__ void __launch_bounds__(K2_THREADS, 2) moe_gateup_kernel(DecodeParams 
     }
   }
 
-  float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int i = 0; i < GPW; ++i) {
-    const int si = i >> p.gshift;
-    const float sg0 = bf_at(sv[0], si), sg1 = bf_at(sv[1], si);
-    const float bg0 = bf_at(sv[2], si), bg1 = bf_at(sv[3], si);
-    const float su0 = bf_at(sv[4], si), su1 = bf_at(sv[5], si);
-    const float bu0 = bf_at(sv[6], si), bu1 = bf_at(sv[7], si);
-    float dg[4] = {0.f, 0.f, 0.f, 0.f}, du[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint32_t xw[8] = {xb[i][0].x, xb[i][0].y, xb[i][0].z, xb[i][0].w,
-                            xb[i][1].x, xb[i][1].y, xb[i][1].z, xb[i][1].w};
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const int i0 = 2 * (m & 1);
-      const uint32_t wa = (m >> 1) ? ag0[i].y : ag0[i].x;
-      const uint32_t wb = (m >> 1) ? ag1[i].y : ag1[i].x;
-      mma_bf16(dg, nib_pair(wa, i0), nib_pair(wb, i0), nib_pair(wa, i0 + 1),
-               nib_pair(wb, i0 + 1), xw[2 * m], xw[2 * m + 1]);
-      const uint32_t va = (m >> 1) ? au0[i].y : au0[i].x;
-      const uint32_t vb2 = (m >> 1) ? au1[i].y : au1[i].x;
-      mma_bf16(du, nib_pair(va, i0), nib_pair(vb2, i0), nib_pair(va, i0 + 1),
-               nib_pair(vb2, i0 + 1), xw[2 * m], xw[2 * m + 1]);
-    }
-    const float bpg0 = fmaf(-128.f, sg0, bg0), bpg1 = fmaf(-128.f, sg1, bg1);
-    const float bpu0 = fmaf(-128.f, su0, bu0), bpu1 = fmaf(-128.f, su1, bu1);
-    accg[0] += fmaf(sg0, dg[0], bpg0 * xs0[i]);
-    accg[1] += fmaf(sg0, dg[1], bpg0 * xs1[i]);
-    accg[2] += fmaf(sg1, dg[2], bpg1 * xs0[i]);
-    accg[3] += fmaf(sg1, dg[3], bpg1 * xs1[i]);
-    accu[0] += fmaf(su0, du[0], bpu0 * xs0[i]);
-    accu[1] += fmaf(su0, du[1], bpu0 * xs1[i]);
-    accu[2] += fmaf(su1, du[2], bpu1 * xs0[i]);
-    accu[3] += fmaf(su1, du[3], bpu1 * xs1[i]);
-  }
-  float *rw = red[warp];
-  *reinterpret_cast<float2 *>(rw + g * 8 + 2 * c) = make_float2(accg[0], accg[1]);
-  *reinterpret_cast<float2 *>(rw + (g + 8) * 8 + 2 * c) = make_float2(accg[2], accg[3]);
-  *reinterpret_cast<float2 *>(rw + 128 + g * 8 + 2 * c) = make_float2(accu[0], accu[1]);
-  *reinterpret_cast<float2 *>(rw + 128 + (g + 8) * 8 + 2 * c) = make_float2(accu[2], accu[3]);
-  __syncthreads();
-  if (tid < 128) {
-    // Add the warp partials in warp order, then SwiGLU (bf16 per op).
-    float sg = 0.f, su = 0.f;
-#pragma unroll
-    for (int w = 0; w < K2_WARPS; ++w) {
-      sg += red[w][tid];
-      su += red[w][128 + tid];
-    }
-    hval[tid] = (tid & 7) < T ? swiglu_bf16(rbf(sg), rbf(su)) : 0.f;
-  }
-  __syncthreads();
   const int NI = p.I / 64;
-  if (tid < 64) {
-    // The 16 rows of h form quarter c' = rb%4 of intermediate group rb/4.
-    const int n = tid >> 3, w = tid & 7;
-    const int m = w >> 1, pp = w & 1, j = m >> 1, i0 = 2 * (m & 1);
-    const int olo = 8 * j + i0 + pp, ohi = olo + 4;
-    const uint32_t word = pack_bf2(hval[olo * 8 + n], hval[ohi * 8 + n]);
-    uint32_t *hperm = wsp<uint32_t>(p, p.L.hperm);
-    hperm[((((size_t)e * DEC_MAX_T + n) * NI + (rb >> 2)) * 4 + (rb & 3)) * 8 + w] = word;
-  } else if (tid < 72) {
-    const int n = tid - 64;
-    float sh = 0.f;
+#pragma unroll 1
+  for (int k = 0; b + k * grid < n_items; ++k) {
+    cp_async_wait<S - 2>();
+    __syncthreads();
+    issue(k + S - 1);
+    cp_async_commit();
+    const int item = b + k * grid;
+    const int e = item >> rb_shift, rb = item & (RB - 1);
+    const uint8_t *st = ring + (k % S) * Tl::STAGE;
+
+    uint4 sv[8];  // gate_s r0, r1, gate_b r0, r1, up_s r0, r1, up_b r0, r1
+    {
+      const int s0 = G0 >> GS;
 #pragma unroll
-    for (int o = 0; o < 16; ++o) sh += hval[o * 8 + n];
-    wsp<float>(p, p.L.hsum)[((size_t)e * DEC_MAX_T + n) * (p.I / 16) + rb] = sh;
+      for (int a = 0; a < 8; ++a) {
+        const int row = (a & 1) ? g + 8 : g;
+        sv[a] = lds_scales(st + 2 * Tl::WBYTES + (a >> 1) * Tl::SBYTES + (row * Tl::NS + s0) * 2,
+                           Tl::SC);
+      }
+    }
+    float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < GPW; ++i) {
+      const int col = (G0 + i) * 32 + 8 * c;
+      const uint2 ag0 = lds64(st + g * Tl::PITCH + col);
+      const uint2 ag1 = lds64(st + (g + 8) * Tl::PITCH + col);
+      const uint2 au0 = lds64(st + Tl::WBYTES + g * Tl::PITCH + col);
+      const uint2 au1 = lds64(st + Tl::WBYTES + (g + 8) * Tl::PITCH + col);
+      const int si = i >> GS;
+      const float sg0 = bf_at(sv[0], si), sg1 = bf_at(sv[1], si);
+      const float bg0 = bf_at(sv[2], si), bg1 = bf_at(sv[3], si);
+      const float su0 = bf_at(sv[4], si), su1 = bf_at(sv[5], si);
+      const float bu0 = bf_at(sv[6], si), bu1 = bf_at(sv[7], si);
+      float dg[4] = {0.f, 0.f, 0.f, 0.f}, du[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint32_t xw[8] = {xb[i][0].x, xb[i][0].y, xb[i][0].z, xb[i][0].w,
+                              xb[i][1].x, xb[i][1].y, xb[i][1].z, xb[i][1].w};
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int i0 = 2 * (m & 1);
+        const uint32_t wa = (m >> 1) ? ag0.y : ag0.x;
+        const uint32_t wb = (m >> 1) ? ag1.y : ag1.x;
+        mma_bf16(dg, nib_pair(wa, i0), nib_pair(wb, i0), nib_pair(wa, i0 + 1),
+                 nib_pair(wb, i0 + 1), xw[2 * m], xw[2 * m + 1]);
+        const uint32_t va = (m >> 1) ? au0.y : au0.x;
+        const uint32_t vb2 = (m >> 1) ? au1.y : au1.x;
+        mma_bf16(du, nib_pair(va, i0), nib_pair(vb2, i0), nib_pair(va, i0 + 1),
+                 nib_pair(vb2, i0 + 1), xw[2 * m], xw[2 * m + 1]);
+      }
+      const float bpg0 = fmaf(-128.f, sg0, bg0), bpg1 = fmaf(-128.f, sg1, bg1);
+      const float bpu0 = fmaf(-128.f, su0, bu0), bpu1 = fmaf(-128.f, su1, bu1);
+      accg[0] += fmaf(sg0, dg[0], bpg0 * xs0[i]);
+      accg[1] += fmaf(sg0, dg[1], bpg0 * xs1[i]);
+      accg[2] += fmaf(sg1, dg[2], bpg1 * xs0[i]);
+      accg[3] += fmaf(sg1, dg[3], bpg1 * xs1[i]);
+      accu[0] += fmaf(su0, du[0], bpu0 * xs0[i]);
+      accu[1] += fmaf(su0, du[1], bpu0 * xs1[i]);
+      accu[2] += fmaf(su1, du[2], bpu1 * xs0[i]);
+      accu[3] += fmaf(su1, du[3], bpu1 * xs1[i]);
+    }
+    float *rw = red[warp];
+    *reinterpret_cast<float2 *>(rw + g * 8 + 2 * c) = make_float2(accg[0], accg[1]);
+    *reinterpret_cast<float2 *>(rw + (g + 8) * 8 + 2 * c) = make_float2(accg[2], accg[3]);
+    *reinterpret_cast<float2 *>(rw + 128 + g * 8 + 2 * c) = make_float2(accu[0], accu[1]);
+    *reinterpret_cast<float2 *>(rw + 128 + (g + 8) * 8 + 2 * c) = make_float2(accu[2], accu[3]);
+    __syncthreads();
+    if (tid < 128) {
+      // Add the warp partials in warp order, then SwiGLU (bf16 per op).
+      float sg = 0.f, su = 0.f;
+#pragma unroll
+      for (int w = 0; w < WARPS; ++w) {
+        sg += red[w][tid];
+        su += red[w][128 + tid];
+      }
+      hval[tid] = (tid & 7) < T ? swiglu_bf16(rbf(sg), rbf(su)) : 0.f;
+    }
+    __syncthreads();
+    if (tid < 64) {
+      // The 16 rows of h form quarter c' = rb%4 of intermediate group rb/4.
+      const int n = tid >> 3, w = tid & 7;
+      const int m = w >> 1, pp = w & 1, j = m >> 1, i0 = 2 * (m & 1);
+      const int olo = 8 * j + i0 + pp, ohi = olo + 4;
+      const uint32_t word = pack_bf2(hval[olo * 8 + n], hval[ohi * 8 + n]);
+      uint32_t *hperm = wsp<uint32_t>(p, p.L.hperm);
+      hperm[((((size_t)e * DEC_MAX_T + n) * NI + (rb >> 2)) * 4 + (rb & 3)) * 8 + w] = word;
+    } else if (tid < 72) {
+      const int n = tid - 64;
+      float sh = 0.f;
+#pragma unroll
+      for (int o = 0; o < 16; ++o) sh += hval[o * 8 + n];
+      wsp<float>(p, p.L.hsum)[((size_t)e * DEC_MAX_T + n) * (p.I / 16) + rb] = sh;
+    }
+    if (k == 0) trace_mark(p.trace, 7);
   }
+  cp_async_wait<0>();
   span.end();
 }
 
@@ -849,6 +992,23 @@ __global__ void __launch_bounds__(K3_THREADS, 2) moe_down_kernel(DecodeParams p)
   span.end();
 }
 
+// One-time per-kernel attributes: the dynamic shared memory it needs and the
+// largest shared-memory carveout, so that consecutive decode kernels never
+// make an SM switch its L1/shared split.
+static cudaError_t decode_kernel_attrs(const void *fn, size_t smem) {
+  static std::mutex mu;
+  static std::vector<std::pair<const void *, size_t>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  for (auto &d : done)
+    if (d.first == fn && d.second >= smem) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                       (int)cudaSharedmemCarveoutMaxShared);
+  if (e == cudaSuccess && smem > 48 * 1024)
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess) done.emplace_back(fn, smem);
+  return e;
+}
+
 static int sm_count() {
   static int n = 0;
   if (!n) {
@@ -948,12 +1108,28 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   const int per = E <= 256 ? 8 : (E <= 512 ? 16 : 32);
 #define VB_K1(HH) (per == 8 ? moe_router_kernel<HH, 8> : per == 16 ? moe_router_kernel<HH, 16> \
                                                       : moe_router_kernel<HH, 32>)
+  size_t k2_smem = 0;
+  int k2_threads = 0;
+#define VB_K2(HH)                                                             \
+  do {                                                                        \
+    k1 = VB_K1(HH);                                                           \
+    if (p.gshift) {                                                           \
+      k2 = moe_gateup_kernel<HH, 1>;                                          \
+      k2_smem = GateUpTile<HH, 1>::SMEM;                                      \
+      k2_threads = GateUpTile<HH, 1>::THREADS;                                \
+    } else {                                                                  \
+      k2 = moe_gateup_kernel<HH, 0>;                                          \
+      k2_smem = GateUpTile<HH, 0>::SMEM;                                      \
+      k2_threads = GateUpTile<HH, 0>::THREADS;                                \
+    }                                                                         \
+  } while (0)
   switch (H) {
-    case 512: k1 = VB_K1(512); k2 = moe_gateup_kernel<512>; break;
-    case 1024: k1 = VB_K1(1024); k2 = moe_gateup_kernel<1024>; break;
-    case 2048: k1 = VB_K1(2048); k2 = moe_gateup_kernel<2048>; break;
-    default: k1 = VB_K1(4096); k2 = moe_gateup_kernel<4096>; break;
+    case 512: VB_K2(512); break;
+    case 1024: VB_K2(1024); break;
+    case 2048: VB_K2(2048); break;
+    default: VB_K2(4096); break;
   }
+#undef VB_K2
 #undef VB_K1
   void (*k3)(DecodeParams) = nullptr;
   switch (I) {
@@ -969,14 +1145,19 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   // previous block's down kernel): it only reads weights before the wait.
   if (ev) cudaEventRecord(ev[0], s);
   const size_t smem1 = (size_t)T * H * 2;
-  if (smem1 > 48 * 1024)
-    cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
+  cudaError_t err = decode_kernel_attrs((const void *)k1, smem1);
+  if (err == cudaSuccess) err = decode_kernel_attrs((const void *)k2, k2_smem);
+  if (err == cudaSuccess) err = decode_kernel_attrs((const void *)k3, 0);
+  if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "decode kernel attributes: %s", cudaGetErrorString(err));
   const int grid1 = (E + DEC_ROUTER_WARPS - 1) / DEC_ROUTER_WARPS;
-  cudaError_t err = vb_launch(k1, dim3(grid1), dim3(DEC_ROUTER_WARPS * 32), smem1, s, pdl, p);
+  err = vb_launch(k1, dim3(grid1), dim3(DEC_ROUTER_WARPS * 32), smem1, s, pdl, p);
   if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_router_kernel: %s", cudaGetErrorString(err));
   if (ev) cudaEventRecord(ev[1], s);
 
-  err = vb_launch(k2, dim3(L.max_entries, I / 16), dim3(K2_THREADS), 0, s, pdl, p);
+  {
+    const int grid2 = std::min(sm_count(), L.max_entries * (I / 16));
+    err = vb_launch(k2, dim3(grid2), dim3(k2_threads), k2_smem, s, pdl, p);
+  }
   if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_gateup_kernel: %s", cudaGetErrorString(err));
   if (ev) cudaEventRecord(ev[2], s);
 
