@@ -103,7 +103,7 @@ __device__ __forceinline__ void prefetch_l2(const void *p) {
 __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1,
                                          uint32_t a2, uint32_t a3, uint32_t b0,
                                          uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -114,6 +114,22 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
 // nibble i+4 (high half) of `w`.
 __device__ __forceinline__ uint32_t nib_pair(uint32_t w, int i) {
   return ((w >> (4 * i)) & 0x000F000Fu) | 0x43004300u;
+}
+
+// (a & m) | o in one LOP3.
+__device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t o) {
+  uint32_t r;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(m), "r"(o));
+  return r;
+}
+// The four code pairs of a 32-bit word of 4-bit codes as exact bf16 pairs
+// (128 + q): p[i] holds nibble i (low half) and nibble i+4 (high half).
+__device__ __forceinline__ void nib_pairs4(uint32_t w, uint32_t (&p)[4]) {
+  constexpr uint32_t M = 0x000F000Fu, O = 0x43004300u;
+  p[0] = lop_and_or(w, M, O);
+  p[1] = lop_and_or(w >> 4, M, O);
+  p[2] = lop_and_or(w >> 8, M, O);
+  p[3] = lop_and_or(w >> 12, M, O);
 }
 
 // Programmatic dependent launch controls (no-ops without the launch
@@ -129,6 +145,14 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
   const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async8(void *smem, const void *gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem) {
+  const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(s), "l"(gmem) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() {
   asm volatile("cp.async.commit_group;" ::: "memory");

@@ -4,28 +4,25 @@
 // :245-1013) with PersistentSubGLU.forward (compute.py:145-199) and the
 // shared expert (block.py:102-109, 1009-1012).
 //
-// Four kernels per block, chained with programmatic dependent launch (PDL):
-//  K1 router: optional unit RMSNorm of x, logits = bf16(x.Wr^T [+bias]) with
-//     one warp per expert row (row loaded before the PDL wait). The last CTA
-//     (atomic ticket) runs the precise softmax, top-k (lower id wins ties),
-//     renormalisation and slot gather, and writes the list of "entries":
-//     the shared expert first, then every distinct routed slot. All CTAs
-//     share writing x in MMA-fragment order (xperm), per-64-column sums
-//     (xsum) and the shared-expert gate sigmoid(x.w_sg).
-//  K2 gate/up: persistent CTAs walk items (entry, 16 intermediate rows). All
-//     512 threads stream an item's packed rows and scales into a multi-stage
-//     cp.async ring (per-thread copy offsets are fixed at kernel start; H is a
-//     template constant). Weights are the A operand of mma.m16n8k16 (16 rows
-//     x 16 columns), tokens the 8 B columns: 4-bit codes become the exact
-//     bf16 values 128+q with one LOP3 per pair, so per 64-column group the
-//     epilogue applies y += s*D + (b - 128*s)*sum(x). 16 warps split the
-//     hidden dimension and their partials are added in warp order; SwiGLU
-//     (bf16 per op) follows and h is stored in fragment order (hperm).
-//     The shared expert's weights are requested before the PDL wait.
-//  K3 down: persistent CTAs walk items (entry, 128 output rows), weights
-//     requested before the PDL wait; per route the result is rounded to
-//     bf16, multiplied by the route score and rounded again (MLX chain).
-//  K4 combine: per token and column, the k routes are added in rank order
+// Three kernels per block, chained with programmatic dependent launch (PDL):
+//  K1 router: optional unit RMSNorm of x, logits = bf16(x.Wr^T [+bias]) and
+//     the shared-expert gate sigmoid(x.w_sg) as one more row; every row is
+//     split over 2-4 warps and loaded before the PDL wait. All CTAs share
+//     writing x in MMA-fragment order (xperm) and per-64-column sums (xsum).
+//     The last CTA (atomic ticket) runs the precise softmax, top-k (one warp
+//     reduction per pick on (bf16 probability, expert id) keys, lower id wins
+//     ties), renormalisation and slot gather, and writes the list of
+//     "entries": the shared expert first, then every distinct routed expert.
+//  K2 gate/up: persistent CTAs; the two warps of a pair split an item (entry,
+//     16 intermediate rows) over the hidden dimension and stream it through
+//     per-warp cp.async rings; 4-bit codes become exact bf16 values 128+q for
+//     mma.m16n8k16 and the per-group epilogue applies y += s*D + (b-128*s)*
+//     sum(x). SwiGLU (bf16 per op); h in fragment order (hperm). Item blocks
+//     and the matching down-projection rows are bulk-prefetched into L2.
+//  K3 down + combine: one CTA per (entry, 128 output rows), weights requested
+//     before the PDL wait; per route the result is rounded to bf16, times the
+//     route score, rounded again (MLX chain). The last CTA of each 128-row
+//     block (atomic ticket) adds the k routes of every token in rank order
 //     (exact double sum of bf16 values, rounded to float32 then bf16), then
 //     the gated shared expert and the optional residual.
 #include <algorithm>
@@ -39,7 +36,6 @@ namespace vb {
 constexpr int DEC_MAX_T = 8;
 constexpr int DEC_MAX_K = 16;
 constexpr int DEC_MAX_E = 1024;
-constexpr int DEC_ROUTER_WARPS = 4;
 constexpr int DEC_SMEM_BUDGET = 200 * 1024;
 
 struct DecEntry {
@@ -179,40 +175,57 @@ __device__ __forceinline__ uint2 lds64(const uint8_t *p) {
 
 // ----------------------------------------------------------------------------
 // K1: router GEMV + last-CTA softmax/top-k/entries. H is a template constant
-// so that every index is a shift.
+// so that every index is a shift. Rows 0..E-1 are the experts' router rows,
+// row E (when there is a shared expert) the shared-expert gate row; each row
+// is split over Q warps (RPC = 8/Q rows per CTA) whose partial dots are added
+// in part order. Rows are loaded before the PDL wait.
 // ----------------------------------------------------------------------------
+constexpr int K1_THREADS = 256;
+constexpr int K1_WARPS = K1_THREADS / 32;
+
+template <int H>
+struct RouterTile {
+  static constexpr int Q = H >= 1024 ? 4 : 2;  // warps per row
+  static constexpr int RPC = K1_WARPS / Q;      // rows per CTA
+  static constexpr int NVQ = H / (256 * Q);     // uint4 of a row part per lane
+  static_assert(NVQ >= 1, "router tile");
+};
+
+// Orderable key of a float (for unsigned max).
+__device__ __forceinline__ uint32_t f2key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float key2f(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 template <int H, int PER>  // PER = ceil(E / 32) logits per lane
-__global__ void __launch_bounds__(DEC_ROUTER_WARPS * 32)
-moe_router_kernel(DecodeParams p) {
-  constexpr int NVL = H / 256;  // uint4 of a row per lane
+__global__ void __launch_bounds__(K1_THREADS, 2) moe_router_kernel(DecodeParams p) {
+  using Tl = RouterTile<H>;
+  constexpr int Q = Tl::Q, RPC = Tl::RPC, NVQ = Tl::NVQ;
   constexpr int NG = H / 64;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint16_t *xs = reinterpret_cast<uint16_t *>(smem_raw);  // [T][H] bf16
+  __shared__ double s_ss[K1_WARPS][DEC_MAX_T];
+  __shared__ float s_inv[DEC_MAX_T];
+  __shared__ float s_part[RPC][Q][DEC_MAX_T];
   const int T = p.T, E = p.E;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   SpanTrace span(p.trace, 0);
 
-  // Router row of this warp and (CTAs t < T, warp 0) the shared-expert gate
-  // row: both independent of the previous kernel.
-  const int e = blockIdx.x * DEC_ROUTER_WARPS + warp;
-  uint4 wv[NVL];
-  if (e < E) {
-    const uint4 *wrow = reinterpret_cast<const uint4 *>(p.router_w + (size_t)e * H);
+  // This warp's row part; row E is the shared-expert gate.
+  const int rloc = warp / Q, part = warp % Q;
+  const int row = blockIdx.x * RPC + rloc;
+  const int nrows = E + (p.has_shared ? 1 : 0);
+  uint4 wv[NVQ];
+  if (row < nrows) {
+    const uint16_t *src = row < E ? p.router_w + (size_t)row * H : p.shared_gate_w;
+    const uint4 *w4 = reinterpret_cast<const uint4 *>(src + part * (H / Q));
 #pragma unroll
-    for (int u = 0; u < NVL; ++u) wv[u] = ldg_nc_v4(wrow + u * 32 + lane);
+    for (int u = 0; u < NVQ; ++u) wv[u] = ldg_nc_v4(w4 + u * 32 + lane);
   }
-  const bool gate_cta = p.has_shared && (int)blockIdx.x < T && warp == 0;
-  uint4 gv[NVL];
-  if (gate_cta) {
-    const uint4 *grow = reinterpret_cast<const uint4 *>(p.shared_gate_w);
-#pragma unroll
-    for (int u = 0; u < NVL; ++u) gv[u] = ldg_nc_v4(grow + u * 32 + lane);
-  }
-  if (p.has_shared && tid == 0) {
-    // The shared expert is fixed per layer: stream it into L2 right away.
-    const int np = expert_pieces(p, 0, 9);
-    for (int i = blockIdx.x; i < np; i += gridDim.x) prefetch_expert_piece(p, p.shared, 0, 0, i);
-  }
+  if (blockIdx.x == 0 && tid * 32 < E) prefetch_l2(p.table + tid * 32);  // slot table lines
   pdl_wait();
   pdl_launch_dependents();
   trace_mark(p.trace, 8);
@@ -221,20 +234,18 @@ moe_router_kernel(DecodeParams p) {
     // Stage x: independent 16-byte loads issued before the stores.
     const uint4 *src = reinterpret_cast<const uint4 *>(p.x);
     uint4 *dst = reinterpret_cast<uint4 *>(xs);
+    constexpr int PT = (DEC_MAX_T * H / 8 + K1_THREADS - 1) / K1_THREADS;
     const int nvec = T * (H / 8);
-    constexpr int STEP = DEC_ROUTER_WARPS * 32;
-    for (int base = 0; base < nvec; base += 8 * STEP) {
-      uint4 v[8];
+    uint4 v[PT];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = base + u * STEP + tid;
-        if (i < nvec) v[u] = __ldcg(src + i);
-      }
+    for (int u = 0; u < PT; ++u) {
+      const int i = u * K1_THREADS + tid;
+      if (i < nvec) v[u] = __ldcg(src + i);
+    }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = base + u * STEP + tid;
-        if (i < nvec) dst[i] = v[u];
-      }
+    for (int u = 0; u < PT; ++u) {
+      const int i = u * K1_THREADS + tid;
+      if (i < nvec) dst[i] = v[u];
     }
   }
   __syncthreads();
@@ -242,30 +253,41 @@ moe_router_kernel(DecodeParams p) {
   if (p.norm_eps > 0.f) {
     // Unit-weight RMSNorm of the block input (decoder post-attention norm):
     // y = bf16(x * (1/sqrt(mean(x^2) + eps))), float32 math with an exact
-    // (double) sum of squares. Every CTA computes it identically.
-    __shared__ float s_inv[DEC_MAX_T];
-    for (int t = warp; t < T; t += DEC_ROUTER_WARPS) {
-      double ss = 0.0;
+    // (double) sum of squares: squares of bf16 values have 16 significant
+    // bits, so their double sum does not depend on the order. Every CTA
+    // computes it identically.
+    constexpr int VPT = H / 8;  // uint4 per token
+    double ss[DEC_MAX_T];
 #pragma unroll
-      for (int u = 0; u < NVL; ++u) {
-        const uint4 v = reinterpret_cast<const uint4 *>(xs + (size_t)t * H)[u * 32 + lane];
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    for (int t = 0; t < DEC_MAX_T; ++t) ss[t] = 0.0;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const double a = bf2f(w[q] & 0xFFFF), b = bf2f(w[q] >> 16);
-          ss = fma(a, a, ss);
-          ss = fma(b, b, ss);
+    for (int t = 0; t < DEC_MAX_T; ++t) {
+      if (t < T) {
+        for (int v = tid; v < VPT; v += K1_THREADS) {
+          const uint4 q = reinterpret_cast<const uint4 *>(xs + (size_t)t * H)[v];
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const double a = bf2f(w[j] & 0xFFFF), b = bf2f(w[j] >> 16);
+            ss[t] = fma(a, a, ss[t]);
+            ss[t] = fma(b, b, ss[t]);
+          }
         }
-      }
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      if (lane == 0) {
-        const float ms = __fdiv_rn((float)ss, (float)H);
-        s_inv[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.norm_eps)));
+        for (int o = 16; o > 0; o >>= 1) ss[t] += __shfl_xor_sync(0xffffffffu, ss[t], o);
+        if (lane == 0) s_ss[warp][t] = ss[t];
       }
     }
     __syncthreads();
-    for (int i = tid; i < T * (H / 8); i += blockDim.x) {
+    if (tid < T) {
+      double tot = 0.0;
+#pragma unroll
+      for (int w = 0; w < K1_WARPS; ++w) tot += s_ss[w][tid];
+      const float ms = __fdiv_rn((float)tot, (float)H);
+      s_inv[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.norm_eps)));
+    }
+    __syncthreads();
+    for (int i = tid; i < T * (H / 8); i += K1_THREADS) {
       const int t = i / (H / 8);
       uint4 v = reinterpret_cast<const uint4 *>(xs)[i];
       uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -277,15 +299,15 @@ moe_router_kernel(DecodeParams p) {
     }
     __syncthreads();
   }
-
   trace_mark(p.trace, 12);
-  if (e < E) {
+
+  if (row < nrows) {
     float acc[DEC_MAX_T];
 #pragma unroll
     for (int t = 0; t < DEC_MAX_T; ++t) acc[t] = 0.f;
 #pragma unroll
-    for (int u = 0; u < NVL; ++u) {
-      const int v = u * 32 + lane;
+    for (int u = 0; u < NVQ; ++u) {
+      const int v = part * (H / Q / 8) + u * 32 + lane;
       const uint32_t wr[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
 #pragma unroll
       for (int t = 0; t < DEC_MAX_T; ++t) {
@@ -308,15 +330,28 @@ moe_router_kernel(DecodeParams p) {
         float a = acc[t];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (lane == 0) {
-          if (p.router_bias) a = a + p.router_bias[e];
-          wsp<float>(p, p.L.logits)[(size_t)t * E + e] = rbf(a);
-        }
+        if (lane == 0) s_part[rloc][part][t] = a;
       }
     }
   }
-
+  __syncthreads();
+  if (tid < RPC * DEC_MAX_T) {
+    const int rl = tid / DEC_MAX_T, t = tid % DEC_MAX_T;
+    const int r = blockIdx.x * RPC + rl;
+    if (r < nrows && t < T) {
+      float a = 0.f;
+#pragma unroll
+      for (int q = 0; q < Q; ++q) a += s_part[rl][q][t];
+      if (r < E) {
+        if (p.router_bias) a = a + p.router_bias[r];
+        wsp<float>(p, p.L.logits)[(size_t)t * E + r] = rbf(a);
+      } else {
+        wsp<float>(p, p.L.sgate)[t] = rbf(mlx_sigmoid(rbf(a)));
+      }
+    }
+  }
   trace_mark(p.trace, 13);
+
   {
     // x in MMA fragment order (xperm) and per-64-column sums (xsum), spread
     // over all CTAs (each holds the whole normalised x in shared memory).
@@ -332,8 +367,8 @@ moe_router_kernel(DecodeParams p) {
       xperm[i] = lo | (hi << 16);
     }
     float *xsum = wsp<float>(p, p.L.xsum);
-    const int gwarp = blockIdx.x * DEC_ROUTER_WARPS + warp;
-    const int nwarps = gridDim.x * DEC_ROUTER_WARPS;
+    const int gwarp = blockIdx.x * K1_WARPS + warp;
+    const int nwarps = gridDim.x * K1_WARPS;
     for (int it = gwarp; it < T * NG; it += nwarps) {
       const int n = it / NG, G = it % NG;
       const uint32_t v = reinterpret_cast<const uint32_t *>(xs + (size_t)n * H + 64 * G)[lane];
@@ -341,23 +376,6 @@ moe_router_kernel(DecodeParams p) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
       if (lane == 0) xsum[it] = s;
-    }
-    for (int t = blockIdx.x; gate_cta && t < T; t += gridDim.x) {
-      float a = 0.f;
-#pragma unroll
-      for (int u = 0; u < NVL; ++u) {
-        const uint32_t gr[4] = {gv[u].x, gv[u].y, gv[u].z, gv[u].w};
-        const uint4 xv = reinterpret_cast<const uint4 *>(xs + (size_t)t * H)[u * 32 + lane];
-        const uint32_t xr[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          a = fmaf(bf2f(gr[q] & 0xFFFF), bf2f(xr[q] & 0xFFFF), a);
-          a = fmaf(bf2f(gr[q] >> 16), bf2f(xr[q] >> 16), a);
-        }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-      if (lane == 0) wsp<float>(p, p.L.sgate)[t] = rbf(mlx_sigmoid(rbf(a)));
     }
   }
 
@@ -376,80 +394,100 @@ moe_router_kernel(DecodeParams p) {
   trace_mark(p.trace, 10);
 
   // ---- softmax + top-k per token (one warp per token) ----
+  __shared__ int s_ex[DEC_MAX_T * DEC_MAX_K];
   __shared__ int s_slot[DEC_MAX_T * DEC_MAX_K];
   __shared__ float s_score[DEC_MAX_T * DEC_MAX_K];
-  __shared__ int s_first[DEC_MAX_T * DEC_MAX_K];  // 1 = first route of its slot
+  __shared__ int s_first[DEC_MAX_E];  // first route of each expert
   __shared__ int s_ent[DEC_MAX_T * DEC_MAX_K];
+  __shared__ int s_wcnt[K1_WARPS];
   __shared__ __align__(16) DecEntry s_entries[DEC_MAX_T * DEC_MAX_K + 1];
+  __shared__ int s_table[DEC_MAX_E];
   const int k = p.k;
   const float *logits = wsp<float>(p, p.L.logits);
-  for (int t = warp; t < T; t += DEC_ROUTER_WARPS) {
-    float v[PER];
-    float m = -INFINITY;
+  // Slot table and logits are loaded together (one memory round trip).
+  float v[PER];
+  {
+    const int t = warp;
+    int tb[(DEC_MAX_E + K1_THREADS - 1) / K1_THREADS];
+#pragma unroll
+    for (int j = 0; j < (DEC_MAX_E + K1_THREADS - 1) / K1_THREADS; ++j) {
+      const int i = tid + j * K1_THREADS;
+      tb[j] = i < E ? __ldg(p.table + i) : -1;
+    }
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       const int idx = lane + 32 * i;
-      v[i] = idx < E ? __ldcg(logits + (size_t)t * E + idx) : -INFINITY;
-      m = fmaxf(m, v[i]);
+      v[i] = (t < T && idx < E) ? __ldcg(logits + (size_t)t * E + idx) : -INFINITY;
     }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    double s = 0.0;
+    for (int j = 0; j < (DEC_MAX_E + K1_THREADS - 1) / K1_THREADS; ++j) {
+      const int i = tid + j * K1_THREADS;
+      if (i < E) {
+        s_table[i] = tb[j];
+        s_first[i] = 0x7fffffff;
+      }
+    }
+  }
+  __syncthreads();
+  for (int t = warp; t < T; t += K1_WARPS) {
+    uint32_t mk = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) mk = max(mk, f2key(v[i]));
+    const float m = key2f(__reduce_max_sync(0xffffffffu, mk));
+    double sd[PER];
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       const int idx = lane + 32 * i;
       const float ex = idx < E ? expf(__fsub_rn(v[i], m)) : 0.f;
       v[i] = ex;
-      s += (double)ex;
+      sd[i] = (double)ex;
     }
+    // Pairwise sum (float sums of a few hundred exponentials are exact in
+    // double, so the order does not matter).
+#pragma unroll
+    for (int w = 1; w < PER; w *= 2)
+#pragma unroll
+      for (int i = 0; i + w < PER; i += 2 * w) sd[i] += sd[i + w];
+    double s = sd[0];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     const float inv = __frcp_rn((float)s);
-    // Probabilities (bf16) and this lane's running maximum; ties resolve to
-    // the lower expert id.
-    float lb = -INFINITY;
-    int li = 0x7fffffff;
+    // Keys: bf16 probability bits above (0xFFFF - expert id), so the unsigned
+    // maximum is the largest probability with ties to the lower id.
+    uint32_t key[PER];
+    uint32_t lb = 0;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       const int idx = lane + 32 * i;
-      v[i] = idx < E ? rbf(__fmul_rn(v[i], inv)) : -INFINITY;
-      if (v[i] > lb) { lb = v[i]; li = idx; }
+      key[i] = idx < E ? ((uint32_t)f2bf(__fmul_rn(v[i], inv)) << 16) | (0xFFFFu - idx) : 0u;
+      lb = max(lb, key[i]);
     }
     double ssum = 0.0;
-    float sel_p = 0.f;
-    int sel_e = 0;
+    uint32_t sel = 0;
     for (int r = 0; r < k; ++r) {
-      float bv = lb;
-      int bi = li;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-      }
-      if ((bi & 31) == lane) {  // winner: drop the value, rescan this lane
-        lb = -INFINITY;
-        li = 0x7fffffff;
+      const uint32_t best = __reduce_max_sync(0xffffffffu, lb);
+      if (lb == best) {  // the one lane holding it drops it and rescans
+        lb = 0;
 #pragma unroll
         for (int i = 0; i < PER; ++i) {
-          const int idx = lane + 32 * i;
-          if (idx == bi) v[i] = -INFINITY;
-          if (v[i] > lb) { lb = v[i]; li = idx; }
+          if (key[i] == best) key[i] = 0u;
+          lb = max(lb, key[i]);
         }
       }
-      if (lane == r) { sel_p = bv; sel_e = bi; }
-      ssum += (double)bv;
+      if (lane == r) sel = best;
+      ssum += (double)bf2f(best >> 16);
     }
+    const float sel_p = bf2f(sel >> 16);
     float score = sel_p;
     if (p.norm_topk) {
       const float denom = rbf((float)ssum);
       score = rbf(__fdiv_rn(sel_p, denom));
     }
     if (lane < k) {
-      const int ex = sel_e;
+      const int ex = 0xFFFF - (int)(sel & 0xFFFFu);
       int slot = -1;
       if (ex >= 0 && ex < E) {
-        slot = __ldg(p.table + ex);
+        slot = s_table[ex];
         if (slot >= p.pool.cap) {
           flag_status(p.status, VB_STATUS_BOUNDS);
           slot = -1;
@@ -460,6 +498,7 @@ moe_router_kernel(DecodeParams p) {
       } else {
         flag_status(p.status, VB_STATUS_BOUNDS);
       }
+      s_ex[t * k + lane] = ex;
       s_slot[t * k + lane] = slot;
       s_score[t * k + lane] = score;
       wsp<int32_t>(p, p.L.route_ok)[t * k + lane] = slot >= 0 ? 1 : 0;
@@ -468,43 +507,41 @@ moe_router_kernel(DecodeParams p) {
       if (p.out_local) p.out_local[t * k + lane] = slot;
     }
   }
+  __syncthreads();
   trace_mark(p.trace, 14);
-  // Entry table in shared memory: slot -1 / rank -1 defaults.
-  for (int i = tid; i < (DEC_MAX_T * DEC_MAX_K + 1) * (int)(sizeof(DecEntry) / 4);
-       i += blockDim.x) {
+
+  // ---- entries: shared expert first, then one entry per distinct routed
+  // expert in route order (t-major, rank-minor): the first route of each
+  // expert is found with an atomic minimum, first routes are numbered with
+  // ballots, and every route fills its (entry, token) cell.
+  const int R = T * k;
+  const int shared_n = p.has_shared ? 1 : 0;
+  const int r = tid;
+  const bool valid = r < R && s_slot[r] >= 0;
+  if (valid) atomicMin(&s_first[s_ex[r]], r);
+  // Entry table defaults: slot -1 / rank -1.
+  for (int i = tid; i < (R + 1) * (int)(sizeof(DecEntry) / 4); i += K1_THREADS) {
     const int f = i % (int)(sizeof(DecEntry) / 4);  // field word
     reinterpret_cast<int32_t *>(s_entries)[i] = (f >= 4 && f < 12) ? -1 : 0;
   }
   __syncthreads();
-
-  // ---- entries: shared expert first, then the distinct routed slots in
-  // route order (t-major, rank-minor). One thread per route: it finds the
-  // first route with its slot, first routes are numbered by counting the
-  // earlier first routes, and every route fills its (entry, token) cell.
-  const int R = T * k;
-  const int shared_n = p.has_shared ? 1 : 0;
-  const int r = tid;
-  const int slot = r < R ? s_slot[r] : -1;
-  int first = r;
-#pragma unroll 8
-  for (int q = 0; q < R; ++q) {
-    const int sq = s_slot[q];
-    first = (q < first && sq == slot) ? q : first;
-  }
-  const bool is_first = slot >= 0 && first == r;
-  if (r < R) s_first[r] = is_first ? 1 : 0;
-  const int n_routed = __syncthreads_count(is_first);
+  const bool is_first = valid && s_first[s_ex[r]] == r;
+  const unsigned bal = __ballot_sync(0xffffffffu, is_first);
+  if (lane == 0) s_wcnt[warp] = __popc(bal);
+  __syncthreads();
   if (is_first) {
-    int idx = shared_n;
-#pragma unroll 8
-    for (int q = 0; q < r; ++q) idx += s_first[q];
+    int idx = shared_n + __popc(bal & ((1u << lane) - 1u));
+    for (int w = 0; w < warp; ++w) idx += s_wcnt[w];
     s_ent[r] = idx;
   }
+  int n_routed = 0;
+#pragma unroll
+  for (int w = 0; w < K1_WARPS; ++w) n_routed += s_wcnt[w];
   __syncthreads();
-  if (r < R && slot >= 0) {
-    const int ei = s_ent[first];
+  if (valid) {
+    const int ei = s_ent[s_first[s_ex[r]]];
     const int tt = r / k, jj = r - tt * k;
-    s_entries[ei].slot = slot;
+    s_entries[ei].slot = s_slot[r];
     s_entries[ei].rank[tt] = jj;
     s_entries[ei].score[tt] = s_score[r];
   }
@@ -518,7 +555,7 @@ moe_router_kernel(DecodeParams p) {
   trace_mark(p.trace, 15);
   const int words = n * (int)(sizeof(DecEntry) / 4);
   int32_t *dst = wsp<int32_t>(p, p.L.entries);
-  for (int i = tid; i < words; i += blockDim.x)
+  for (int i = tid; i < words; i += K1_THREADS)
     dst[i] = reinterpret_cast<const int32_t *>(s_entries)[i];
   if (tid == 0) {
     *wsp<int32_t>(p, p.L.n_entries) = n;
@@ -528,38 +565,46 @@ moe_router_kernel(DecodeParams p) {
 }
 
 // ----------------------------------------------------------------------------
-// K2: gate/up + SwiGLU, persistent. One CTA per SM walks the items (entry,
-// 16 intermediate rows) b, b + grid, ... An item's 16 gate rows, 16 up rows
-// and their scales/biases (each contiguous in the pool) are copied by all
-// threads with 16-byte cp.async into an S-stage shared-memory ring, S-1
-// items ahead of the math. Rows are padded by 32 bytes so that the MMA
-// fragment reads (row g, 8 bytes at column 8c) fall in distinct banks. The
-// shared expert's item is requested before the PDL wait. The 8 warps split
-// the hidden dimension (GPW groups of 64 columns each); their partials are
-// added in warp order, then SwiGLU (bf16 per op) and h in fragment order.
+// K2: gate/up + SwiGLU. Persistent CTAs of W warps; an item (entry, 16
+// intermediate rows) is split over the hidden dimension between the two
+// warps of a pair, and each warp streams its half through its own cp.async
+// ring of chunks (16 rows x 4 groups of 64 columns of gate and up plus their
+// scales and biases; rows padded so that the MMA fragment reads hit distinct
+// banks), RS-1 chunks ahead of the math. Item i runs on CTA i % grid, so
+// every SM gets the same share. The odd warp hands its partial sums to the
+// even one through shared memory (one named barrier per pair and item), which
+// adds them in half order and applies SwiGLU (bf16 per op); h goes out in MMA
+// fragment order for the down projection. Weights are the A operand of
+// mma.m16n8k16 (4-bit codes as exact bf16 128+q, one LOP3 per pair), tokens
+// the 8 B columns; per 64-column group y += s*D + (b - 128*s)*sum(x). x in
+// fragment order and its group sums sit in shared memory for all warps. The
+// shared expert's first chunks are requested before the PDL wait.
 // ----------------------------------------------------------------------------
-constexpr int K2_SMEM_MAX = 200 * 1024;
+constexpr int K2_SMEM_MAX = 225 * 1024;
 
 template <int H, int GS>  // GS: log2(group / 64)
 struct GateUpTile {
-  static constexpr int NG = H / 64;
-  static constexpr int WARPS = NG < 16 ? NG : 16;
+  static constexpr int NG = H / 64;           // 64-column groups per row
+  static constexpr int CG = 4;                // groups per chunk
+  static constexpr int NCH = NG / CG;         // chunks per row block
+  static constexpr int CPH = NCH / 2;         // chunks per half
+  static constexpr int ROWB = H / 2;          // packed bytes per row
+  static constexpr int CROW = CG * 32;        // chunk bytes per row (128)
+  static constexpr int PITCH = CROW + 32;     // padded chunk row pitch
+  static constexpr int NS = H >> (6 + GS);    // scales per row
+  static constexpr int SCB = (CG >> GS) * 2;  // scale bytes per row per chunk
+  static constexpr int WB = 2 * 16 * PITCH;   // gate + up codes of a chunk
+  static constexpr int CHUNK = WB + 4 * 16 * SCB;
+  static constexpr int RS = 3;                // ring stages per warp
+  static constexpr int XB = NG * DEC_MAX_T * 4 * 8 * 4 + NG * DEC_MAX_T * 4;  // x frags, sums
+  // Per warp pair: two rings, the odd warp's partials (2 slots x 32 lanes x
+  // 8 floats) and the h tile (16 rows x 8 tokens).
+  static constexpr int PER_PAIR = 2 * RS * CHUNK + 2048 + 512;
+  static constexpr int P_FIT = (K2_SMEM_MAX - XB) / PER_PAIR;
+  static constexpr int WARPS = 2 * (P_FIT < 6 ? P_FIT : 6);
   static constexpr int THREADS = 32 * WARPS;
-  static constexpr int GPW = NG / WARPS;
-  static constexpr int NS = H >> (6 + GS);          // scales per row
-  static constexpr int SC = GPW >> GS ? GPW >> GS : 1;  // scales per warp row slice
-  static constexpr int ROWB = H / 2;                // packed bytes per row
-  static constexpr int PITCH = ROWB + 32;           // padded smem row pitch
-  static constexpr int WBYTES = 16 * PITCH;         // 16 rows of one matrix
-  static constexpr int SBYTES = 16 * NS * 2;        // 16 rows of one scale tensor
-  static constexpr int SCH = SBYTES / 16;           // its 16-byte chunks
-  static constexpr int STAGE = 2 * WBYTES + 4 * SBYTES;
-  static constexpr int S = (K2_SMEM_MAX / STAGE) < 6 ? (K2_SMEM_MAX / STAGE) : 6;
-  static constexpr int CPR = ROWB / 16;             // 16-byte chunks per row
-  static constexpr int RSTEP = THREADS / CPR;       // rows per copy pass
-  static constexpr int PASSES = 16 / RSTEP;
-  static constexpr int SMEM = S * STAGE;
-  static_assert(S >= 2 && RSTEP >= 1 && PASSES * RSTEP == 16, "gate/up tile");
+  static constexpr int SMEM = XB + (WARPS / 2) * PER_PAIR;
+  static_assert(CPH >= 1 && WARPS >= 2 && (WARPS & 1) == 0, "gate/up tile");
 };
 
 // Load 2*count bytes of bf16 scales (count in {1,2,4,8}) into a uint4.
@@ -578,229 +623,284 @@ __device__ __forceinline__ uint4 ld_scales(const uint16_t *ptr, int count) {
   }
   return r;
 }
-
-// bf16 scales (count in {1,2,4,8}) from shared memory into a uint4.
-__device__ __forceinline__ uint4 lds_scales(const uint8_t *ptr, int count) {
-  uint4 r = make_uint4(0, 0, 0, 0);
-  if (count >= 8) {
-    r = *reinterpret_cast<const uint4 *>(ptr);
-  } else if (count == 4) {
-    const uint2 v = *reinterpret_cast<const uint2 *>(ptr);
-    r.x = v.x;
-    r.y = v.y;
-  } else if (count == 2) {
-    r.x = *reinterpret_cast<const unsigned *>(ptr);
-  } else {
-    r.x = *reinterpret_cast<const uint16_t *>(ptr);
-  }
-  return r;
-}
 __device__ __forceinline__ float bf_at(const uint4 &v, int i) {
   const uint32_t w = i < 2 ? v.x : (i < 4 ? v.y : (i < 6 ? v.z : v.w));
   return bf2f((i & 1) ? (w >> 16) : (w & 0xFFFF));
 }
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+// bf16 at index i (0..3) of a 2-word vector.
+__device__ __forceinline__ float bf_at2(const uint2 &v, int i) {
+  const uint32_t w = i < 2 ? v.x : v.y;
+  return (i & 1) ? bf_hi(w) : bf_lo(w);
+}
 
-// Copy item (expert tensors `base`, row block rb) into one ring stage.
-// base: gate w, gate s, gate b, up w, up s, up b of the expert's slot.
+struct GateUpItem {
+  const uint8_t *gw, *uw;  // row block start of the gate and up codes
+  const uint8_t *sc[4];    // row block start of gate s, gate b, up s, up b
+};
+
 template <int H, int GS>
-__device__ __forceinline__ void gateup_issue(uint8_t *stage, const uint8_t *const (&base)[6],
-                                             int rb, int tid) {
+__device__ __forceinline__ void gateup_item(const VbQuantPool &pool, int slot, int rb,
+                                            GateUpItem &it) {
   using Tl = GateUpTile<H, GS>;
-  const int r0 = tid / Tl::CPR, c16 = (tid % Tl::CPR) * 16;
-  const uint8_t *gw = base[0] + (size_t)(16 * rb) * Tl::ROWB;
-  const uint8_t *uw = base[3] + (size_t)(16 * rb) * Tl::ROWB;
+  it.gw = pool_ptr(pool, 0, slot) + (size_t)rb * 16 * Tl::ROWB;
+  it.uw = pool_ptr(pool, 3, slot) + (size_t)rb * 16 * Tl::ROWB;
+  it.sc[0] = pool_ptr(pool, 1, slot) + (size_t)rb * 16 * Tl::NS * 2;
+  it.sc[1] = pool_ptr(pool, 2, slot) + (size_t)rb * 16 * Tl::NS * 2;
+  it.sc[2] = pool_ptr(pool, 4, slot) + (size_t)rb * 16 * Tl::NS * 2;
+  it.sc[3] = pool_ptr(pool, 5, slot) + (size_t)rb * 16 * Tl::NS * 2;
+}
+
+// Chunk ch (codes and scales) of an item into a ring stage.
+template <int H, int GS>
+__device__ __forceinline__ void gateup_chunk(uint8_t *stage, const GateUpItem &it, int ch,
+                                             int lane) {
+  using Tl = GateUpTile<H, GS>;
+  // 2 matrices x 16 rows x 8 pieces of 16 bytes; lane -> piece lane%8 of
+  // rows lane/8 + 4j.
+  const int r0 = lane >> 3, p16 = (lane & 7) * 16;
+  const uint8_t *g = it.gw + r0 * Tl::ROWB + ch * Tl::CROW + p16;
+  const uint8_t *u = it.uw + r0 * Tl::ROWB + ch * Tl::CROW + p16;
+  uint8_t *dg = stage + r0 * Tl::PITCH + p16;
 #pragma unroll
-  for (int j = 0; j < Tl::PASSES; ++j) {
-    const int r = r0 + j * Tl::RSTEP;
-    cp_async16(stage + r * Tl::PITCH + c16, gw + r * Tl::ROWB + c16);
-    cp_async16(stage + Tl::WBYTES + r * Tl::PITCH + c16, uw + r * Tl::ROWB + c16);
+  for (int j = 0; j < 4; ++j) {
+    cp_async16(dg + 4 * j * Tl::PITCH, g + 4 * j * Tl::ROWB);
+    cp_async16(dg + 16 * Tl::PITCH + 4 * j * Tl::PITCH, u + 4 * j * Tl::ROWB);
   }
-  // Scale tensors (16 rows x NS bf16 each), compact in shared memory.
+  // Scales: 4 tensors x 16 rows x SCB bytes -> [tensor][row][SCB].
 #pragma unroll
-  for (int q0 = 0; q0 < 4 * Tl::SCH; q0 += Tl::THREADS) {
-    const int q = q0 + tid;
-    if (q < 4 * Tl::SCH) {
-      const int a = q / Tl::SCH, c = q % Tl::SCH;
-      const uint8_t *t = a == 0 ? base[1] : a == 1 ? base[2] : a == 2 ? base[4] : base[5];
-      cp_async16(stage + 2 * Tl::WBYTES + a * Tl::SBYTES + c * 16,
-                 t + (size_t)rb * Tl::SBYTES + c * 16);
-    }
+  for (int k = 0; k < 2; ++k) {
+    const int piece = lane + 32 * k, a = piece >> 4, r = piece & 15;
+    const uint8_t *src = it.sc[a] + r * Tl::NS * 2 + ch * Tl::SCB;
+    uint8_t *dst = stage + Tl::WB + piece * Tl::SCB;
+    if (Tl::SCB == 8) cp_async8(dst, src);
+    else cp_async4(dst, src);
   }
+}
+
+__device__ __forceinline__ void named_bar(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 template <int H, int GS>
 __global__ void __launch_bounds__(GateUpTile<H, GS>::THREADS, 1) moe_gateup_kernel(DecodeParams p) {
   using Tl = GateUpTile<H, GS>;
-  constexpr int NG = Tl::NG;
-  constexpr int GPW = Tl::GPW;
-  constexpr int S = Tl::S;
-  constexpr int WARPS = Tl::WARPS;
-  extern __shared__ __align__(16) uint8_t ring[];
-  __shared__ float red[WARPS][256];
-  __shared__ float hval[128];
+  constexpr int NG = Tl::NG, CG = Tl::CG, CPH = Tl::CPH, RS = Tl::RS, W = Tl::WARPS;
+  constexpr int PAIRS = W / 2;
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint32_t *xf = reinterpret_cast<uint32_t *>(smem);                         // [NG][8][4][8] words
+  float *xsm = reinterpret_cast<float *>(smem + NG * DEC_MAX_T * 4 * 8 * 4);  // [NG][8]
   __shared__ int s_slot[DEC_MAX_T * DEC_MAX_K + 1];
   __shared__ int s_n;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
   const int T = p.T;
   SpanTrace span(p.trace, 1);
-  const int G0 = warp * GPW;
-  const int rb_shift = 31 - __clz(p.I / 16);  // items per entry = I/16
+  const int pair = warp >> 1, half = warp & 1;
+  uint8_t *pbase = smem + Tl::XB + pair * Tl::PER_PAIR;
+  uint8_t *ring = pbase + half * RS * Tl::CHUNK;
+  float *red = reinterpret_cast<float *>(pbase + 2 * RS * Tl::CHUNK);  // [2][32][8]
+  float *hbuf = red + 2 * 32 * 8;                                        // [16][8]
+  const int rb_shift = 31 - __clz(p.I / 16);  // row blocks per entry = I/16
   const int RB = 1 << rb_shift;
-  const int b = blockIdx.x, grid = gridDim.x;
+  const int grid = gridDim.x;
+  // This pair's items: blockIdx.x + grid * (pair + PAIRS * r), r = 0, 1, ...
+  const int first = blockIdx.x + grid * pair, step = grid * PAIRS;
 
-  auto bases = [&](const VbQuantPool &pool, int slot, const uint8_t *(&base)[6]) {
-#pragma unroll
-    for (int t = 0; t < 6; ++t) base[t] = pool_ptr(pool, t, slot);
+  GateUpItem cur;
+  int issue_q = 0;
+  auto issue_next = [&](int n_items) {
+    const int r = issue_q / CPH, ch = half * CPH + issue_q % CPH;
+    const int i = first + r * step;
+    if (i < n_items) {
+      if (issue_q % CPH == 0) {
+        const int e = i >> rb_shift;
+        if (p.has_shared && e == 0) gateup_item<H, GS>(p.shared, 0, i & (RB - 1), cur);
+        else gateup_item<H, GS>(p.pool, s_slot[e], i & (RB - 1), cur);
+      }
+      gateup_chunk<H, GS>(ring + (issue_q % RS) * Tl::CHUNK, cur, ch, lane);
+    }
+    cp_async_commit();
+    ++issue_q;
   };
-  // The shared expert (entry 0) needs no routing: its item goes first.
-  const bool pre = p.has_shared && b < RB;
+
+  // The shared expert (entry 0) needs no routing: its chunks go first.
+  const bool pre = p.has_shared && first < RB;
   if (pre) {
-    const uint8_t *base[6];
-    bases(p.shared, 0, base);
-    gateup_issue<H, GS>(ring, base, b, tid);
+#pragma unroll 1
+    for (int k = 0; k < RS - 1; ++k) issue_next(first + 1);
   }
-  cp_async_commit();
   pdl_wait();
   pdl_launch_dependents();
   const int max_e = p.L.max_entries;
   if (tid == 0) s_n = *wsp<const int32_t>(p, p.L.n_entries);
-  if (tid < max_e) s_slot[tid] = wsp<const DecEntry>(p, p.L.entries)[tid].slot;
+  for (int i = tid; i < max_e; i += blockDim.x) s_slot[i] = wsp<const DecEntry>(p, p.L.entries)[i].slot;
+  {
+    // x fragments [token][group][c][8 words] -> [group][token][c][8 words],
+    // group sums [token][group] -> [group][8] (zero beyond T).
+    const uint4 *src = reinterpret_cast<const uint4 *>(wsp<const uint32_t>(p, p.L.xperm));
+    uint4 *dst = reinterpret_cast<uint4 *>(xf);
+    for (int u = tid; u < T * NG * 8; u += blockDim.x) {
+      const int n = u / (NG * 8), rest = u % (NG * 8), G = rest >> 3, k = rest & 7;
+      dst[(G * DEC_MAX_T + n) * 8 + k] = __ldcg(src + u);
+    }
+    const float *xs = wsp<const float>(p, p.L.xsum);
+    for (int i = tid; i < NG * DEC_MAX_T; i += blockDim.x) {
+      const int G = i >> 3, n = i & 7;
+      xsm[i] = n < T ? __ldcg(xs + n * NG + G) : 0.f;
+    }
+  }
   __syncthreads();
   trace_mark(p.trace, 6);
   const int n_items = s_n << rb_shift;
-  auto issue = [&](int k) {
-    const int i = b + k * grid;
-    if (i < n_items) {
-      const int e = i >> rb_shift;
-      const uint8_t *base[6];
-      if (p.has_shared && e == 0) bases(p.shared, 0, base);
-      else bases(p.pool, s_slot[e], base);
-      gateup_issue<H, GS>(ring + (k % S) * Tl::STAGE, base, i & (RB - 1), tid);
-    }
-  };
-  if (!pre) issue(0);
-  cp_async_commit();
+  if (!pre) {
 #pragma unroll 1
-  for (int k = 1; k < S - 1; ++k) {
-    issue(k);
-    cp_async_commit();
+    for (int k = 0; k < RS - 1; ++k) issue_next(n_items);
   }
-
-  // x fragments and column sums of this warp's groups (written by the router).
-  uint4 xb[GPW][2];
-  float xs0[GPW], xs1[GPW];
-  {
-    const uint32_t *xperm = wsp<const uint32_t>(p, p.L.xperm);
-    const float *xsum = wsp<const float>(p, p.L.xsum);
-#pragma unroll
-    for (int i = 0; i < GPW; ++i) {
-      const int G = G0 + i;
-      if (g < T) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(xperm + (((size_t)g * NG + G) * 4 + c) * 8);
-        xb[i][0] = __ldcg(src);
-        xb[i][1] = __ldcg(src + 1);
+  if (!half && lane < 9) {
+    // Whole row blocks of this pair's items into L2 in one go (contiguous
+    // 16-row blocks of gate and up codes and of their four scale tensors):
+    // DRAM then streams each block at once and the chunk copies hit L2.
+    // Lanes 6..8 do the same for the slice of the entry's down projection
+    // (rows [rb, rb + 1) * H / RB) that the next kernel reads.
+    for (int i = first; i < n_items; i += step) {
+      const int e = i >> rb_shift, rb = i & (RB - 1);
+      const VbQuantPool &pool = (p.has_shared && e == 0) ? p.shared : p.pool;
+      const int slot = (p.has_shared && e == 0) ? 0 : s_slot[e];
+      if (lane < 6) {
+        GateUpItem it;
+        gateup_item<H, GS>(pool, slot, rb, it);
+        if (lane < 2) prefetch_l2_bulk(lane ? it.uw : it.gw, 16 * Tl::ROWB);
+        else prefetch_l2_bulk(it.sc[lane - 2], 16 * Tl::NS * 2);
       } else {
-        xb[i][0] = xb[i][1] = make_uint4(0, 0, 0, 0);
+        const int rows = H / RB, ngi = p.I >> (6 + GS);
+        const uint32_t rbytes = lane == 6 ? (uint32_t)p.I / 2 : (uint32_t)ngi * 2;
+        prefetch_l2_bulk(pool_ptr(pool, lane, slot) + (size_t)rb * rows * rbytes, rows * rbytes);
       }
-      xs0[i] = 2 * c < T ? __ldcg(xsum + (2 * c) * NG + G) : 0.f;
-      xs1[i] = 2 * c + 1 < T ? __ldcg(xsum + (2 * c + 1) * NG + G) : 0.f;
     }
   }
 
   const int NI = p.I / 64;
+  float accg[4], accu[4];
 #pragma unroll 1
-  for (int k = 0; b + k * grid < n_items; ++k) {
-    cp_async_wait<S - 2>();
-    __syncthreads();
-    issue(k + S - 1);
-    cp_async_commit();
-    const int item = b + k * grid;
-    const int e = item >> rb_shift, rb = item & (RB - 1);
-    const uint8_t *st = ring + (k % S) * Tl::STAGE;
-
-    uint4 sv[8];  // gate_s r0, r1, gate_b r0, r1, up_s r0, r1, up_b r0, r1
-    {
-      const int s0 = G0 >> GS;
+  for (int q = 0;; ++q) {
+    const int r = q / CPH, cq = q % CPH, ch = half * CPH + cq;
+    const int item = first + r * step;
+    if (item >= n_items) break;
+    cp_async_wait<RS - 2>();
+    __syncwarp();
+    issue_next(n_items);  // into the stage consumed one chunk ago
+    if (cq == 0) {
 #pragma unroll
-      for (int a = 0; a < 8; ++a) {
-        const int row = (a & 1) ? g + 8 : g;
-        sv[a] = lds_scales(st + 2 * Tl::WBYTES + (a >> 1) * Tl::SBYTES + (row * Tl::NS + s0) * 2,
-                           Tl::SC);
-      }
+      for (int j = 0; j < 4; ++j) accg[j] = accu[j] = 0.f;
     }
-    float accg[4] = {0.f, 0.f, 0.f, 0.f}, accu[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint8_t *st = ring + (q % RS) * Tl::CHUNK;
+    // Scales of this chunk's groups for rows g and g+8: gate s, gate b,
+    // up s, up b.
+    uint2 sv[8];
 #pragma unroll
-    for (int i = 0; i < GPW; ++i) {
-      const int col = (G0 + i) * 32 + 8 * c;
-      const uint2 ag0 = lds64(st + g * Tl::PITCH + col);
-      const uint2 ag1 = lds64(st + (g + 8) * Tl::PITCH + col);
-      const uint2 au0 = lds64(st + Tl::WBYTES + g * Tl::PITCH + col);
-      const uint2 au1 = lds64(st + Tl::WBYTES + (g + 8) * Tl::PITCH + col);
-      const int si = i >> GS;
-      const float sg0 = bf_at(sv[0], si), sg1 = bf_at(sv[1], si);
-      const float bg0 = bf_at(sv[2], si), bg1 = bf_at(sv[3], si);
-      const float su0 = bf_at(sv[4], si), su1 = bf_at(sv[5], si);
-      const float bu0 = bf_at(sv[6], si), bu1 = bf_at(sv[7], si);
+    for (int a = 0; a < 8; ++a) {
+      const uint8_t *sp = st + Tl::WB + ((a >> 1) * 16 + ((a & 1) ? g + 8 : g)) * Tl::SCB;
+      if (Tl::SCB == 8) sv[a] = *reinterpret_cast<const uint2 *>(sp);
+      else sv[a] = make_uint2(*reinterpret_cast<const uint32_t *>(sp), 0u);
+    }
+#pragma unroll
+    for (int gl = 0; gl < CG; ++gl) {
+      const int G = ch * CG + gl;
+      uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0;
+      if (g < T) {
+        const uint4 *xp = reinterpret_cast<const uint4 *>(xf + ((G * DEC_MAX_T + g) * 4 + c) * 8);
+        x0 = xp[0];
+        x1 = xp[1];
+      }
+      const float2 xs = *reinterpret_cast<const float2 *>(xsm + G * DEC_MAX_T + 2 * c);
+      const uint2 ag0 = lds64(st + g * Tl::PITCH + gl * 32 + 8 * c);
+      const uint2 ag1 = lds64(st + (g + 8) * Tl::PITCH + gl * 32 + 8 * c);
+      const uint2 au0 = lds64(st + (16 + g) * Tl::PITCH + gl * 32 + 8 * c);
+      const uint2 au1 = lds64(st + (24 + g) * Tl::PITCH + gl * 32 + 8 * c);
+      uint32_t pg0[2][4], pg1[2][4], pu0[2][4], pu1[2][4];
+      nib_pairs4(ag0.x, pg0[0]);
+      nib_pairs4(ag0.y, pg0[1]);
+      nib_pairs4(ag1.x, pg1[0]);
+      nib_pairs4(ag1.y, pg1[1]);
+      nib_pairs4(au0.x, pu0[0]);
+      nib_pairs4(au0.y, pu0[1]);
+      nib_pairs4(au1.x, pu1[0]);
+      nib_pairs4(au1.y, pu1[1]);
+      const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
       float dg[4] = {0.f, 0.f, 0.f, 0.f}, du[4] = {0.f, 0.f, 0.f, 0.f};
-      const uint32_t xw[8] = {xb[i][0].x, xb[i][0].y, xb[i][0].z, xb[i][0].w,
-                              xb[i][1].x, xb[i][1].y, xb[i][1].z, xb[i][1].w};
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
-        const int i0 = 2 * (m & 1);
-        const uint32_t wa = (m >> 1) ? ag0.y : ag0.x;
-        const uint32_t wb = (m >> 1) ? ag1.y : ag1.x;
-        mma_bf16(dg, nib_pair(wa, i0), nib_pair(wb, i0), nib_pair(wa, i0 + 1),
-                 nib_pair(wb, i0 + 1), xw[2 * m], xw[2 * m + 1]);
-        const uint32_t va = (m >> 1) ? au0.y : au0.x;
-        const uint32_t vb2 = (m >> 1) ? au1.y : au1.x;
-        mma_bf16(du, nib_pair(va, i0), nib_pair(vb2, i0), nib_pair(va, i0 + 1),
-                 nib_pair(vb2, i0 + 1), xw[2 * m], xw[2 * m + 1]);
+        const int i0 = 2 * (m & 1), h = m >> 1;
+        mma_bf16(dg, pg0[h][i0], pg1[h][i0], pg0[h][i0 + 1], pg1[h][i0 + 1], xw[2 * m],
+                 xw[2 * m + 1]);
+        mma_bf16(du, pu0[h][i0], pu1[h][i0], pu0[h][i0 + 1], pu1[h][i0 + 1], xw[2 * m],
+                 xw[2 * m + 1]);
       }
+      const int si = gl >> GS;
+      const float sg0 = bf_at2(sv[0], si), sg1 = bf_at2(sv[1], si);
+      const float bg0 = bf_at2(sv[2], si), bg1 = bf_at2(sv[3], si);
+      const float su0 = bf_at2(sv[4], si), su1 = bf_at2(sv[5], si);
+      const float bu0 = bf_at2(sv[6], si), bu1 = bf_at2(sv[7], si);
       const float bpg0 = fmaf(-128.f, sg0, bg0), bpg1 = fmaf(-128.f, sg1, bg1);
       const float bpu0 = fmaf(-128.f, su0, bu0), bpu1 = fmaf(-128.f, su1, bu1);
-      accg[0] += fmaf(sg0, dg[0], bpg0 * xs0[i]);
-      accg[1] += fmaf(sg0, dg[1], bpg0 * xs1[i]);
-      accg[2] += fmaf(sg1, dg[2], bpg1 * xs0[i]);
-      accg[3] += fmaf(sg1, dg[3], bpg1 * xs1[i]);
-      accu[0] += fmaf(su0, du[0], bpu0 * xs0[i]);
-      accu[1] += fmaf(su0, du[1], bpu0 * xs1[i]);
-      accu[2] += fmaf(su1, du[2], bpu1 * xs0[i]);
-      accu[3] += fmaf(su1, du[3], bpu1 * xs1[i]);
+      accg[0] += fmaf(sg0, dg[0], bpg0 * xs.x);
+      accg[1] += fmaf(sg0, dg[1], bpg0 * xs.y);
+      accg[2] += fmaf(sg1, dg[2], bpg1 * xs.x);
+      accg[3] += fmaf(sg1, dg[3], bpg1 * xs.y);
+      accu[0] += fmaf(su0, du[0], bpu0 * xs.x);
+      accu[1] += fmaf(su0, du[1], bpu0 * xs.y);
+      accu[2] += fmaf(su1, du[2], bpu1 * xs.x);
+      accu[3] += fmaf(su1, du[3], bpu1 * xs.y);
     }
-    float *rw = red[warp];
-    *reinterpret_cast<float2 *>(rw + g * 8 + 2 * c) = make_float2(accg[0], accg[1]);
-    *reinterpret_cast<float2 *>(rw + (g + 8) * 8 + 2 * c) = make_float2(accg[2], accg[3]);
-    *reinterpret_cast<float2 *>(rw + 128 + g * 8 + 2 * c) = make_float2(accu[0], accu[1]);
-    *reinterpret_cast<float2 *>(rw + 128 + (g + 8) * 8 + 2 * c) = make_float2(accu[2], accu[3]);
-    __syncthreads();
-    if (tid < 128) {
-      // Add the warp partials in warp order, then SwiGLU (bf16 per op).
-      float sg = 0.f, su = 0.f;
+    if (cq == CPH - 1) {
+      // Pair hand-off: the odd warp's partials to the even warp.
+      float *slot = red + ((r & 1) * 32 + lane) * 8;
+      if (half) {
 #pragma unroll
-      for (int w = 0; w < WARPS; ++w) {
-        sg += red[w][tid];
-        su += red[w][128 + tid];
+        for (int j = 0; j < 4; ++j) {
+          slot[j] = accg[j];
+          slot[4 + j] = accu[j];
+        }
       }
-      hval[tid] = (tid & 7) < T ? swiglu_bf16(rbf(sg), rbf(su)) : 0.f;
-    }
-    __syncthreads();
-    if (tid < 64) {
-      // The 16 rows of h form quarter c' = rb%4 of intermediate group rb/4.
-      const int n = tid >> 3, w = tid & 7;
-      const int m = w >> 1, pp = w & 1, j = m >> 1, i0 = 2 * (m & 1);
-      const int olo = 8 * j + i0 + pp, ohi = olo + 4;
-      const uint32_t word = pack_bf2(hval[olo * 8 + n], hval[ohi * 8 + n]);
-      uint32_t *hperm = wsp<uint32_t>(p, p.L.hperm);
-      hperm[((((size_t)e * DEC_MAX_T + n) * NI + (rb >> 2)) * 4 + (rb & 3)) * 8 + w] = word;
-    } else if (tid < 72) {
-      const int n = tid - 64;
-      float sh = 0.f;
+      named_bar(1 + pair, 64);
+      if (!half) {
 #pragma unroll
-      for (int o = 0; o < 16; ++o) sh += hval[o * 8 + n];
-      wsp<float>(p, p.L.hsum)[((size_t)e * DEC_MAX_T + n) * (p.I / 16) + rb] = sh;
+        for (int j = 0; j < 4; ++j) {
+          accg[j] += slot[j];
+          accu[j] += slot[4 + j];
+        }
+        // SwiGLU (bf16 per op) of rows g, g+8 x tokens 2c, 2c+1, then h of
+        // the 16 rows in fragment order and its per-token sums.
+        const int e = item >> rb_shift, rb = item & (RB - 1);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int row = (j >> 1) ? g + 8 : g, n = 2 * c + (j & 1);
+          hbuf[row * 8 + n] = n < T ? swiglu_bf16(rbf(accg[j]), rbf(accu[j])) : 0.f;
+        }
+        __syncwarp();
+        uint32_t *hperm = wsp<uint32_t>(p, p.L.hperm);
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int idx = lane + 32 * h2;  // (token n, word w)
+          const int n = idx >> 3, w = idx & 7;
+          const int m = w >> 1, pp = w & 1, j = m >> 1, i0 = 2 * (m & 1);
+          const int olo = 8 * j + i0 + pp, ohi = olo + 4;
+          if (n < T)
+            hperm[((((size_t)e * DEC_MAX_T + n) * NI + (rb >> 2)) * 4 + (rb & 3)) * 8 + w] =
+                pack_bf2(hbuf[olo * 8 + n], hbuf[ohi * 8 + n]);
+        }
+        if (lane < T) {
+          float sh = 0.f;
+#pragma unroll
+          for (int o = 0; o < 16; ++o) sh += hbuf[o * 8 + lane];
+          wsp<float>(p, p.L.hsum)[((size_t)e * DEC_MAX_T + lane) * (p.I / 16) + rb] = sh;
+        }
+        __syncwarp();
+        if (r == 0) trace_mark(p.trace, 7);
+      }
     }
-    if (k == 0) trace_mark(p.trace, 7);
   }
   cp_async_wait<0>();
   span.end();
@@ -1149,8 +1249,9 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   if (err == cudaSuccess) err = decode_kernel_attrs((const void *)k2, k2_smem);
   if (err == cudaSuccess) err = decode_kernel_attrs((const void *)k3, 0);
   if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "decode kernel attributes: %s", cudaGetErrorString(err));
-  const int grid1 = (E + DEC_ROUTER_WARPS - 1) / DEC_ROUTER_WARPS;
-  err = vb_launch(k1, dim3(grid1), dim3(DEC_ROUTER_WARPS * 32), smem1, s, pdl, p);
+  const int rpc = K1_WARPS / (H >= 1024 ? 4 : 2);
+  const int grid1 = (E + (has_shared ? 1 : 0) + rpc - 1) / rpc;
+  err = vb_launch(k1, dim3(grid1), dim3(K1_THREADS), smem1, s, pdl, p);
   if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_router_kernel: %s", cudaGetErrorString(err));
   if (ev) cudaEventRecord(ev[1], s);
 
