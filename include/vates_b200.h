@@ -184,6 +184,53 @@ int vb_moe_decode(const VbMoeDecodeArgs *args, vb_stream_t stream);
 int vb_moe_decode_noalloc(const VbMoeDecodeArgs *args, vb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Expert-major prefill of one sparse-MoE block (T tokens, any T >= 1).
+ * Replaces the prefill branch of FileStreamingMoeBlock.__call__
+ * (mlx_streaming/core/moe/block.py:318-347) and _expert_major_forward
+ * (block.py:111-243): router -> precise softmax -> top-k -> renormalise ->
+ * per-expert grouped gate/up -> SwiGLU -> down (gather_qmm matrix path,
+ * compute.py:156-199; dequantized weights rounded once to bf16) -> y * score
+ * -> reduce in the reference's order (expert group of block.py:154-172, then
+ * route rank; bf16 rounding after every add, custom_kernel.py:63-77) ->
+ * + bf16(sigmoid(x.w_sg) * shared_expert(x)) (block.py:345-346).
+ * 4-bit weights, group 64 or 128; hidden % 256 == 0, inter % 128 == 0.
+ * Routed experts whose slot is -1 are skipped (VB_STATUS_MISS). The
+ * workspace (vb_moe_prefill_workspace_size) is 1024-byte aligned; its
+ * contents need no initialisation. */
+typedef struct VbMoePrefillArgs {
+  int32_t tokens;
+  int32_t hidden;
+  int32_t inter;
+  int32_t group;
+  int32_t bits;
+  int32_t num_experts;
+  int32_t top_k;
+  int32_t norm_topk;
+  int32_t layer_cap;        /* experts per reduce group: min(layer_cap, 128);
+                               <= 0: num_experts (block.py:154) */
+  int32_t max_assignments;  /* routes per reduce group; <= 0: 32768 (155) */
+  const uint16_t *x;            /* bf16 [T, H] */
+  const uint16_t *router_w;     /* bf16 [E, H] */
+  const float *router_bias;     /* nullable f32 [E], added before rounding */
+  const int32_t *slot_table;    /* [E], -1 = not resident */
+  VbQuantPool pool;
+  VbQuantPool shared;           /* ptr[0] == NULL: no shared expert */
+  const uint16_t *shared_gate_w; /* bf16 [H] */
+  uint16_t *out;                /* bf16 [T, H] */
+  int32_t *out_inds;            /* nullable [T, k] */
+  uint16_t *out_scores;         /* nullable bf16 [T, k] */
+  uint16_t *out_logits;         /* nullable bf16 [T, E] router logits */
+  int32_t *status;              /* nullable device status word */
+  void *workspace;
+  size_t workspace_bytes;
+} VbMoePrefillArgs;
+
+size_t vb_moe_prefill_workspace_size(int32_t tokens, int32_t hidden,
+                                     int32_t inter, int32_t num_experts,
+                                     int32_t top_k);
+int vb_moe_prefill(const VbMoePrefillArgs *args, vb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Deterministic route reduce: replaces deterministic_route_reduce
  * (mlx_streaming/core/moe/custom_kernel.py:20-118). previous [tokens, H],
  * weighted [G, H], assignment_pos int32 [G] (unique flat route positions in

@@ -56,13 +56,20 @@ def router(x, wr, k: int, norm_topk: bool = True, logit_bias=None):
     if logit_bias is not None:
         acc = (acc + np.asarray(logit_bias, np.float32)).astype(np.float32)
     logits = M.bf16(acc)
-    probs = M.bf16(M.softmax_precise(logits))
+    probs, inds, scores = route_from_logits(logits, k, norm_topk)
+    return logits, probs, inds, scores
+
+
+def route_from_logits(logits, k: int, norm_topk: bool = True):
+    """The router after the gate Linear (block.py:321-329): bf16 logits ->
+    (probs, inds, scores)."""
+    probs = M.bf16(M.softmax_precise(np.asarray(logits, np.float32)))
     inds = M.topk_desc(probs, k)
     scores = np.take_along_axis(probs, inds, axis=-1)
     if norm_topk:
         denom = M.bf16(scores.astype(np.float64).sum(-1, keepdims=True).astype(np.float32))
         scores = M.bf16(scores / denom)
-    return logits, probs, inds, scores
+    return probs, inds, scores
 
 
 def slot_remap(ids, table):
@@ -256,13 +263,16 @@ def expert_mlp_prefill(x_rows, wg_b, wu_b, wd_b):
 
 
 def expert_major_forward(x, inds, scores, pool_of_expert, hidden, inter, group,
-                         bits, layer_cap: int = 512, max_assignments: int = 32768):
+                         bits, layer_cap: int = 512, max_assignments: int = 32768,
+                         abs_sum: bool = False):
     """``FileStreamingMoeBlock._expert_major_forward`` (block.py:111-243).
 
     ``pool_of_expert(e)`` returns ``(pool, slot)`` holding expert ``e``.
     Routed contributions are accumulated group by group with
     :func:`route_reduce` into a bf16 zero buffer; the order of additions
     follows the group sequence and, within a group, the route rank.
+    With ``abs_sum`` also returns the per-element sum of |weighted route|,
+    the bound on every partial sum of the reduce chain (its rounding scale).
     """
     x = M.bf16(np.asarray(x, np.float32))
     T, k = inds.shape
@@ -271,6 +281,7 @@ def expert_major_forward(x, inds, scores, pool_of_expert, hidden, inter, group,
     counts = np.bincount(route_ids, minlength=512)
     order = np.argsort(route_ids, kind="stable")
     output = np.zeros((T, hidden), np.float32)
+    absacc = np.zeros((T, hidden), np.float32)
     prefix = 0
     for experts, count in expert_groups(counts, layer_cap, max_assignments):
         pos = order[prefix:prefix + count]
@@ -283,8 +294,10 @@ def expert_major_forward(x, inds, scores, pool_of_expert, hidden, inter, group,
             ys[sel] = expert_mlp_prefill(x[pos[sel] // k], wg, wu, wd)
         weighted = M.bf16(ys * route_scores[pos][:, None])
         output = route_reduce(output, weighted, pos, k, out_bf16=True)
+        if abs_sum:
+            np.add.at(absacc, pos // k, np.abs(weighted))
         prefix += count
-    return output
+    return (output, absacc) if abs_sum else output
 
 
 def shared_prefill(x, shared, wsg, hidden, inter, group, bits):

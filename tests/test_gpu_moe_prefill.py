@@ -1,0 +1,116 @@
+"""Expert-major prefill (tcgen05 grouped GEMM) on the GPU vs the CPU oracle.
+
+Parity bar: router logits within one bf16 ulp of the oracle's (the router
+GEMM accumulates in the tensor core's fp32 order, so a logit next to a
+rounding midpoint can round the other way); from the GPU's logits the
+oracle's softmax/top-k gives the same expert ids (up to bf16 ties at the
+k-th probability) and bit-exact scores; top-k ids agree with the oracle's
+own routing up to ties; with the
+GPU's routes fed to the oracle (teacher forcing) the block output is within
+max-abs 2e-2 or 3 bf16 ulps of the reduce chain's scale (sum of |route|),
+at most 0.5% of elements beyond one such ulp, and mean-rel 5e-3. The prefill
+reduce rounds to bf16 after each of the k adds (custom_kernel.py:63-77), one
+more ulp of headroom than the decode path, which sums the k routes exactly.
+"""
+import numpy as np
+import pytest
+
+from conftest import bf16_close
+from helpers import bf16_tensor, pool_to_torch, random_pool_np, routes_agree, to_np
+from oracle import mlx_ops as M
+from oracle import moe as OM
+
+pytestmark = pytest.mark.gpu
+
+
+def _case(T, H, I, E, k, group=64, seed=0, shared=True, bias=False, layer_cap=0,
+          max_assignments=0, missing=()):
+    import torch
+    from vates_b200.moe_block import MoeBlock
+    from vates_b200.pool import QuantPool, make_table
+    from vates_b200.prefill import moe_prefill
+
+    rng = np.random.default_rng(seed)
+    pool_np = random_pool_np(rng, E, H, I, 4, group)
+    pool = QuantPool.from_tensors(pool_to_torch(pool_np), H, I, 4, group)
+    sh_np = random_pool_np(rng, 1, H, I, 4, group) if shared else None
+    sh = QuantPool.from_tensors(pool_to_torch(sh_np), H, I, 4, group) if shared else None
+    wsg_np = M.bf16(rng.standard_normal(H).astype(np.float32) * 0.02)
+    wr_np = M.bf16(rng.standard_normal((E, H)).astype(np.float32) * 0.02)
+    perm = rng.permutation(E)
+    slot_of = {int(e): int(s) for s, e in enumerate(perm)}
+    for e in missing:
+        slot_of.pop(int(e))
+    table = make_table(E, slot_of)
+    lb = (np.log(1.0 / np.arange(1, E + 1) ** 1.1)[rng.permutation(E)].astype(np.float32)
+          if bias else None)
+    blk = MoeBlock(bf16_tensor(wr_np), table, pool, sh, bf16_tensor(wsg_np) if shared else None,
+                   top_k=k, router_bias=None if lb is None else torch.from_numpy(lb).cuda())
+    x = bf16_tensor(rng.standard_normal((T, H)).astype(np.float32))
+    dbg = {"inds": torch.empty((T, k), dtype=torch.int32, device="cuda"),
+           "scores": torch.empty((T, k), dtype=torch.bfloat16, device="cuda"),
+           "logits": torch.empty((T, E), dtype=torch.bfloat16, device="cuda")}
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = moe_prefill(blk, x, debug=dbg, status=status, layer_cap=layer_cap,
+                      max_assignments=max_assignments)
+    torch.cuda.synchronize()
+    xr = to_np(x)
+    g_inds, g_scores = to_np(dbg["inds"]), to_np(dbg["scores"])
+    r_logits, probs, r_inds, _ = OM.router(xr, wr_np, k, True, logit_bias=lb)
+    assert routes_agree(g_inds, probs, r_inds, k).all(), "top-k differs beyond bf16 ties"
+    g_logits = to_np(dbg["logits"])
+    assert (np.abs(g_logits - r_logits) <= M.bf16_ulp(np.abs(r_logits))).all(), "router logits"
+    f_probs, f_inds, f_scores = OM.route_from_logits(g_logits, k, True)
+    assert routes_agree(g_inds, f_probs, f_inds, k).all(), "top-k on the GPU logits"
+    for t in range(T):
+        if set(g_inds[t].tolist()) == set(f_inds[t].tolist()):
+            assert dict(zip(g_inds[t].tolist(), g_scores[t].tolist())) == \
+                dict(zip(f_inds[t].tolist(), f_scores[t].tolist())), t
+    # Teacher forcing on the GPU's routes; experts without a slot add nothing.
+    keep = np.isin(g_inds, list(slot_of.keys()))
+    # (a route with a zero score adds exact zeros, like a skipped route)
+    routed, absacc = OM.expert_major_forward(
+        xr, g_inds, np.where(keep, g_scores, 0).astype(np.float32),
+        lambda e: (pool_np, slot_of.get(int(e), 0)), H, I, group, 4,
+        layer_cap=layer_cap if layer_cap > 0 else E,
+        max_assignments=max_assignments if max_assignments > 0 else 32768, abs_sum=True)
+    # Rounding scale: every partial sum of the bf16 reduce chain is bounded
+    # by the sum of |route| values, and a flipped intermediate rounding is
+    # worth one ulp of that partial sum.
+    ref, scale = routed, absacc
+    if shared:
+        sh_term = OM.shared_prefill(xr, sh_np, wsg_np, H, I, group, 4)
+        ref = M.bf16(routed + sh_term)
+        scale = np.maximum(absacc, np.abs(sh_term))
+    st = int(status.item())
+    return to_np(out), ref, scale, st
+
+
+@pytest.mark.parametrize("T,H,I,E,k,group", [(256, 1024, 256, 16, 4, 64),
+                                             (300, 2048, 512, 32, 10, 64),
+                                             (130, 1024, 256, 8, 2, 128)])
+def test_prefill_block(cuda, T, H, I, E, k, group):
+    got, ref, scale, st = _case(T, H, I, E, k, group, seed=T + E)
+    assert st == 0
+    bf16_close(got, ref, scale=scale, max_ulps=3, what="prefill block output")
+
+
+def test_prefill_groups_order_and_zipf_bias(cuda):
+    """Small reduce groups (several per layer) and a Zipf router bias: the
+    add order of every token's routes follows the groups."""
+    got, ref, scale, st = _case(384, 1024, 256, 32, 8, 64, seed=7, bias=True, layer_cap=3,
+                                max_assignments=200)
+    assert st == 0
+    bf16_close(got, ref, scale=scale, max_ulps=3, what="grouped prefill output")
+
+
+def test_prefill_without_shared_expert(cuda):
+    got, ref, scale, st = _case(200, 1024, 256, 16, 4, seed=3, shared=False)
+    assert st == 0
+    bf16_close(got, ref, scale=scale, max_ulps=3, what="prefill output (no shared expert)")
+
+
+def test_prefill_missing_expert_flags_status(cuda):
+    got, ref, scale, st = _case(128, 1024, 256, 16, 4, seed=5, missing=(0, 1, 2, 3, 4, 5, 6, 7))
+    assert st & 1  # VB_STATUS_MISS
+    bf16_close(got, ref, scale=scale, max_ulps=3, what="prefill output with skipped routes")

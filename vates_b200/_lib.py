@@ -46,7 +46,7 @@ class VbMoePrefillArgs(C.Structure):
         ("x", C.c_void_p), ("router_w", C.c_void_p), ("router_bias", C.c_void_p),
         ("slot_table", C.c_void_p), ("pool", VbQuantPool), ("shared", VbQuantPool),
         ("shared_gate_w", C.c_void_p), ("out", C.c_void_p),
-        ("out_inds", C.c_void_p), ("out_scores", C.c_void_p),
+        ("out_inds", C.c_void_p), ("out_scores", C.c_void_p), ("out_logits", C.c_void_p),
         ("status", C.c_void_p), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
     ]
 
@@ -68,6 +68,8 @@ _SIGNATURES = {
     "vb_moe_decode_workspace_size": (_SZ, [_I32, _I32, _I32, _I32, _I32]),
     "vb_moe_decode": (_I32, [C.POINTER(VbMoeDecodeArgs), _P]),
     "vb_moe_decode_noalloc": (_I32, [C.POINTER(VbMoeDecodeArgs), _P]),
+    "vb_moe_prefill_workspace_size": (_SZ, [_I32, _I32, _I32, _I32, _I32]),
+    "vb_moe_prefill": (_I32, [C.POINTER(VbMoePrefillArgs), _P]),
     "vb_route_reduce_workspace_size": (_SZ, [_I32, _I32]),
     "vb_route_reduce": (_I32, [_P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P,
                                _SZ, _P]),

@@ -116,6 +116,11 @@ __device__ __forceinline__ uint32_t nib_pair(uint32_t w, int i) {
   return ((w >> (4 * i)) & 0x000F000Fu) | 0x43004300u;
 }
 
+// Start of tensor t (gate w,s,b, up w,s,b, down w,s,b) of a pool slot.
+__device__ __forceinline__ const uint8_t *pool_ptr(const VbQuantPool &pool, int t, int slot) {
+  return (const uint8_t *)pool.ptr[t] + (size_t)slot * pool.slot_stride[t];
+}
+
 // (a & m) | o in one LOP3.
 __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t m, uint32_t o) {
   uint32_t r;

@@ -134,9 +134,6 @@ __device__ __forceinline__ T *wsp(const DecodeParams &p, size_t off) {
   return reinterpret_cast<T *>(p.ws + off);
 }
 
-__device__ __forceinline__ const uint8_t *pool_ptr(const VbQuantPool &pool, int t, int slot) {
-  return (const uint8_t *)pool.ptr[t] + (size_t)slot * pool.slot_stride[t];
-}
 
 // Bytes of tensor t (gate w,s,b, up w,s,b, down w,s,b) of one 4-bit expert.
 __device__ __forceinline__ uint32_t expert_tensor_bytes(const DecodeParams &p, int t) {

@@ -1,0 +1,935 @@
+// Expert-major prefill of one sparse-MoE block on the 5th-generation tensor
+// cores (tcgen05), MLX bf16 dtype chain.
+//
+// Reference: FileStreamingMoeBlock.__call__ prefill branch (mlx_streaming/
+// core/moe/block.py:318-347) -> _expert_major_forward (block.py:111-243):
+// histogram of routes, expert-ordered assignment list, groups of <= 128
+// experts and <= 32768 assignments, per group gather -> gate/up -> SwiGLU ->
+// down (gather_qmm, compute.py:156-199) -> y * score -> canonical route-rank
+// reduce (deterministic_route_reduce, custom_kernel.py:20-118); then
+// + sigmoid(x.w_sg) * shared_expert(x) (block.py:102-109, 345-346).
+//
+// B200 design (one call, all on the device, no host round trip):
+//  P1 router GEMM (tcgen05, bf16 operands by TMA): logits of the E router
+//     rows plus the shared-expert gate row, + bias, rounded to bf16.
+//  P2 softmax (precise) + top-k + renormalisation per token (one warp per
+//     token), route histogram, shared gate sigmoid.
+//  P3 plan (one CTA): expert offsets, the reference's group of every expert
+//     (the add order of the final reduce), and the list of 128-row tiles.
+//     The shared expert is expert E and takes every token.
+//  P4 gather: x rows into expert-sorted order (with the 8-column code
+//     permutation described below), route <-> row maps.
+//  P5 grouped GEMM gate/up: dequantized 4-bit tiles (bf16, exact q*s+b
+//     rounded once) x gathered rows, fp32 accumulation in TMEM; epilogue
+//     bf16(gate), bf16(up), SwiGLU (bf16 per op) -> h rows.
+//  P6 grouped GEMM down: h rows x dequantized down tiles; epilogue
+//     bf16(bf16(y) * score).
+//  P7 combine: per token, the routed rows are added starting from zero in
+//     the reference's order (group of the expert, then route rank) with a
+//     bf16 rounding after every add, then + bf16(bf16(sigmoid) * shared).
+//
+// Code permutation: a packed 32-bit word holds codes 8w..8w+7 (LSB first).
+// One LOP3 turns nibbles (i, i+4) into the bf16 pair (128+q_i, 128+q_{i+4}),
+// so the dequantized B tiles hold, inside every 8-column block, the columns
+// in the order (0,4,1,5,2,6,3,7). The A operands (gathered x rows and h
+// rows) are written in the same order, which leaves every dot product
+// unchanged.
+//
+// GEMM kernel (one persistent CTA per SM, 16 warps): warp 0 issues TMA loads
+// (A tile 128x64 bf16 with the 128-byte swizzle, packed B 256 rows x 32 B),
+// warp 1 issues tcgen05.mma (M=128, N=256, K=16 steps) into one of two TMEM
+// accumulators, warps 4-11 dequantize B into the swizzled bf16 layout, and
+// warps 12-15 drain TMEM through the epilogue. Every mbarrier wait is
+// bounded; on a timeout the kernel raises VB_STATUS_TIMEOUT, winds down and
+// frees its TMEM.
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+#include "tc100.cuh"
+
+namespace vb {
+
+constexpr int PF_BM = 128;
+constexpr int PF_BN = 256;
+constexpr int PF_BK = 64;
+constexpr int PF_STAGES = 3;
+constexpr int PF_THREADS = 512;
+constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;        // 16 KB
+constexpr int PF_B_BYTES = PF_BN * PF_BK * 2;        // 32 KB
+constexpr int PF_P_BYTES = PF_BN * PF_BK / 2;        // 8 KB packed codes
+constexpr int PF_STAGE_BYTES = PF_A_BYTES + PF_B_BYTES + PF_P_BYTES;
+constexpr int PF_SMEM = PF_STAGES * PF_STAGE_BYTES + 1024;  // + alignment slack
+constexpr uint64_t PF_WAIT_NS = 2000000000ull;       // 2 s per wait
+
+enum PfMode : int { PF_GATEUP = 0, PF_DOWN = 1, PF_ROUTER = 2 };
+
+struct PfGemmParams {
+  int mode;
+  int K;            // reduction length
+  int nt;           // N tiles
+  int gshift;       // log2(group / 64)
+  int shared_e;     // expert index of the shared expert (-1: none)
+  int n_valid;      // router: valid output columns
+  const int32_t *mtiles;   // [n] (expert, row0, rows)
+  const int32_t *n_mtiles;
+  const int32_t *slot_of;  // expert -> pool slot
+  VbQuantPool pool, shared;
+  uint16_t *out;    // output rows (bf16)
+  int out_ld;
+  const float *row_score;  // down: per sorted row
+  const float *bias;       // router: per column (nullable)
+  int32_t *status;
+};
+
+// Swizzled byte offset of 16-byte chunk `c` of row `r` in a K-major
+// 128-byte-swizzled tile.
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ uint32_t bf16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(PF_THREADS, 1)
+pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+               const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmS0,
+               const __grid_constant__ CUtensorMap tmS1, PfGemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t bar_tma[PF_STAGES], bar_deq[PF_STAGES], bar_empty[PF_STAGES];
+  __shared__ __align__(8) uint64_t bar_acc_full[2], bar_acc_empty[2], bar_final;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_abort;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_mt = *p.n_mtiles;
+  const int n_tiles = n_mt * p.nt;
+  const int ksteps = p.K / PF_BK;
+  constexpr bool DEQ = MODE != PF_ROUTER;
+
+  if (tid == 0) {
+    for (int s = 0; s < PF_STAGES; ++s) {
+      tc::mbar_init(&bar_tma[s], 1);
+      tc::mbar_init(&bar_deq[s], 8);
+      tc::mbar_init(&bar_empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      tc::mbar_init(&bar_acc_full[a], 1);
+      tc::mbar_init(&bar_acc_empty[a], 4);
+    }
+    tc::mbar_init(&bar_final, 1);
+    s_abort = 0;
+    tc::fence_mbar_init();
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&s_tmem, 512);
+    tc::tmem_relinquish();
+  }
+  if (warp == 0 && lane == 0) {
+    tc::prefetch_tmap(&tmA);
+    tc::prefetch_tmap(&tmB0);
+    if (MODE == PF_GATEUP) tc::prefetch_tmap(&tmB1);
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = s_tmem;
+  volatile int32_t *abort = &s_abort;
+  auto fail = [&]() {
+    s_abort = 1;
+    flag_status(p.status, VB_STATUS_TIMEOUT);
+  };
+  auto stage_a = [&](int s) { return smem + s * PF_STAGE_BYTES; };
+  auto stage_b = [&](int s) { return smem + s * PF_STAGE_BYTES + PF_A_BYTES; };
+  auto stage_p = [&](int s) { return smem + s * PF_STAGE_BYTES + PF_A_BYTES + PF_B_BYTES; };
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int it = 0;
+      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
+        const int mt = t / p.nt, nt = t % p.nt;
+        const int e = p.mtiles[3 * mt], row0 = p.mtiles[3 * mt + 1];
+        const bool sh = e == p.shared_e;
+        const int slot = sh ? 0 : (MODE == PF_ROUTER ? 0 : p.slot_of[e]);
+        for (int ks = 0; ks < ksteps; ++ks, ++it) {
+          const int s = it % PF_STAGES;
+          const uint32_t ph = (it / PF_STAGES) & 1;
+          if (!tc::mbar_wait(&bar_empty[s], ph ^ 1, abort, PF_WAIT_NS)) { fail(); break; }
+          if (MODE == PF_ROUTER) {
+            tc::mbar_arrive_expect_tx(&bar_tma[s], PF_A_BYTES + PF_B_BYTES);
+            tc::tma_load_2d(stage_a(s), &tmA, &bar_tma[s], ks * PF_BK, row0);
+            tc::tma_load_2d(stage_b(s), &tmB0, &bar_tma[s], ks * PF_BK, nt * PF_BN);
+          } else if (MODE == PF_GATEUP) {
+            tc::mbar_arrive_expect_tx(&bar_tma[s], PF_A_BYTES + PF_P_BYTES);
+            tc::tma_load_2d(stage_a(s), &tmA, &bar_tma[s], ks * PF_BK, row0);
+            const CUtensorMap *g = sh ? &tmS0 : &tmB0;
+            const CUtensorMap *u = sh ? &tmS1 : &tmB1;
+            tc::tma_load_3d(stage_p(s), g, &bar_tma[s], ks * (PF_BK / 2), nt * 128, slot);
+            tc::tma_load_3d(stage_p(s) + PF_P_BYTES / 2, u, &bar_tma[s], ks * (PF_BK / 2),
+                            nt * 128, slot);
+          } else {
+            tc::mbar_arrive_expect_tx(&bar_tma[s], PF_A_BYTES + PF_P_BYTES);
+            tc::tma_load_2d(stage_a(s), &tmA, &bar_tma[s], ks * PF_BK, row0);
+            const CUtensorMap *d = sh ? &tmS0 : &tmB0;
+            tc::tma_load_3d(stage_p(s), d, &bar_tma[s], ks * (PF_BK / 2), nt * PF_BN, slot);
+          }
+        }
+      }
+      // Wind down: let the copies already issued land before the CTA ends.
+      for (int k = 0; k < PF_STAGES && it - 1 - k >= 0; ++k) {
+        const int j = it - 1 - k;
+        tc::mbar_wait(&bar_tma[j % PF_STAGES], (j / PF_STAGES) & 1, nullptr, PF_WAIT_NS);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = tc::idesc_bf16_f32(PF_BM, PF_BN);
+      int it = 0, tcount = 0;
+      bool issued = false;
+      for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++tcount) {
+        const int acc = tcount & 1;
+        if (!tc::mbar_wait(&bar_acc_empty[acc], ((tcount >> 1) & 1) ^ 1, abort, PF_WAIT_NS)) {
+          fail();
+          break;
+        }
+        tc::tc_fence_after();
+        const uint32_t d = tmem + acc * PF_BN;
+        bool ok = true;
+        for (int ks = 0; ks < ksteps; ++ks, ++it) {
+          const int s = it % PF_STAGES;
+          const uint32_t ph = (it / PF_STAGES) & 1;
+          uint64_t *ready = DEQ ? &bar_deq[s] : &bar_tma[s];
+          if (!tc::mbar_wait(ready, ph, abort, PF_WAIT_NS)) { fail(); ok = false; break; }
+          tc::tc_fence_after();
+          const uint32_t a0 = tc::smem_u32(stage_a(s)), b0 = tc::smem_u32(stage_b(s));
+#pragma unroll
+          for (int k = 0; k < PF_BK / 16; ++k)
+            tc::mma_bf16_ss(d, tc::smem_desc_sw128(a0 + 32 * k), tc::smem_desc_sw128(b0 + 32 * k),
+                            idesc, (ks | k) != 0);
+          tc::mma_commit(&bar_empty[s]);
+          issued = true;
+        }
+        if (!ok) break;
+        tc::mma_commit(&bar_acc_full[acc]);
+      }
+      // All issued MMAs complete before TMEM is released.
+      if (issued) {
+        tc::mma_commit(&bar_final);
+        tc::mbar_wait(&bar_final, 0, nullptr, PF_WAIT_NS);
+      }
+    }
+  } else if (DEQ && warp >= 4 && warp < 12) {
+    // ---------------- dequantize B ----------------
+    // Thread r owns B row r: gate rows 0..127 and up rows 128..255 of the
+    // N tile (gate/up), or down rows (down).
+    const int r = tid - 128;
+    int it = 0;
+    for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
+      const int mt = t / p.nt, nt = t % p.nt;
+      const int e = p.mtiles[3 * mt];
+      const bool sh = e == p.shared_e;
+      const VbQuantPool &pool = sh ? p.shared : p.pool;
+      const int slot = sh ? 0 : p.slot_of[e];
+      int tsc, row;
+      if (MODE == PF_GATEUP) {
+        tsc = r < 128 ? 1 : 4;
+        row = nt * 128 + (r & 127);
+      } else {
+        tsc = 7;
+        row = nt * PF_BN + r;
+      }
+      const int ng = (p.K >> 6) >> p.gshift;  // scale groups per row
+      const uint16_t *sp =
+          reinterpret_cast<const uint16_t *>(pool_ptr(pool, tsc, slot)) + (size_t)row * ng;
+      const uint16_t *bp =
+          reinterpret_cast<const uint16_t *>(pool_ptr(pool, tsc + 1, slot)) + (size_t)row * ng;
+      bool ok = true;
+      for (int ks = 0; ks < ksteps; ++ks, ++it) {
+        const int s = it % PF_STAGES;
+        const uint32_t ph = (it / PF_STAGES) & 1;
+        const int gi = ks >> p.gshift;
+        const uint32_t sc = __ldg(sp + gi), bi = __ldg(bp + gi);
+        if (!tc::mbar_wait(&bar_tma[s], ph, abort, PF_WAIT_NS)) { fail(); ok = false; break; }
+        const uint4 *src = reinterpret_cast<const uint4 *>(stage_p(s) + r * 32);
+        const uint4 w0 = src[0], w1 = src[1];
+        const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const uint32_t s2 = sc | (sc << 16), b2 = bi | (bi << 16);
+        uint8_t *dst = stage_b(s);
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          uint32_t pr[4];
+          nib_pairs4(words[w], pr);
+          uint32_t o[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            // (128 + q) - 128 is exact; q*s + b is rounded once.
+            uint32_t q;
+            asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(pr[i]), "r"(0x43004300u));
+            o[i] = bf16x2_fma(q, s2, b2);
+          }
+          *reinterpret_cast<uint4 *>(dst + sw128(r, w)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&bar_deq[s]);
+      }
+      if (!ok) break;
+    }
+  } else if (warp >= 12) {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;
+    const int m = q * 32 + lane;  // tile row = TMEM lane
+    int tcount = 0;
+    for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++tcount) {
+      const int mt = t / p.nt, nt = t % p.nt;
+      const int row0 = p.mtiles[3 * mt + 1], rows = p.mtiles[3 * mt + 2];
+      const int acc = tcount & 1;
+      if (!tc::mbar_wait(&bar_acc_full[acc], (tcount >> 1) & 1, abort, PF_WAIT_NS)) {
+        fail();
+        break;
+      }
+      tc::tc_fence_after();
+      const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + acc * PF_BN;
+      const bool valid = m < rows;
+      const size_t orow = (size_t)(row0 + m);
+      if (MODE == PF_GATEUP) {
+        // Columns [0,128) gate, [128,256) up of intermediate rows nt*128 + c.
+#pragma unroll 1
+        for (int c0 = 0; c0 < 128; c0 += 16) {
+          uint32_t g[16], u[16];
+          tc::tmem_ld16(tb + c0, g);
+          tc::tmem_ld16(tb + 128 + c0, u);
+          tc::tmem_ld_wait();
+          float h[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            h[j] = swiglu_bf16(rbf(__uint_as_float(g[j])), rbf(__uint_as_float(u[j])));
+          // Two 8-column blocks in the (0,4,1,5,2,6,3,7) code order.
+          uint32_t o[8];
+#pragma unroll
+          for (int b = 0; b < 2; ++b)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[4 * b + i] = pack_bf2(h[8 * b + i], h[8 * b + i + 4]);
+          if (valid) {
+            uint4 *dst = reinterpret_cast<uint4 *>(p.out + orow * p.out_ld + nt * 128 + c0);
+            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        }
+      } else {
+        const float sc = (MODE == PF_DOWN && valid) ? p.row_score[orow] : 1.f;
+#pragma unroll 1
+        for (int c0 = 0; c0 < PF_BN; c0 += 16) {
+          uint32_t v[16];
+          tc::tmem_ld16(tb + c0, v);
+          tc::tmem_ld_wait();
+          float y[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float a = __uint_as_float(v[j]);
+            if (MODE == PF_DOWN) {
+              y[j] = rbf(__fmul_rn(rbf(a), sc));
+            } else {
+              const int col = nt * PF_BN + c0 + j;
+              const float b = (p.bias && col < p.n_valid) ? p.bias[col] : 0.f;
+              y[j] = rbf(a + b);
+            }
+          }
+          uint32_t o[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = pack_bf2(y[2 * j], y[2 * j + 1]);
+          if (valid) {
+            uint4 *dst = reinterpret_cast<uint4 *>(p.out + orow * p.out_ld + nt * PF_BN + c0);
+            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+        }
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&bar_acc_empty[acc]);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (warp == 1) tc::tmem_dealloc(tmem, 512);
+}
+
+// ----------------------------------------------------------------------------
+// P0: router rows (E experts + the shared gate) into a zero-padded bf16
+// matrix of NRP rows.
+// ----------------------------------------------------------------------------
+__global__ void pf_router_rows_kernel(const uint16_t *__restrict__ wr,
+                                      const uint16_t *__restrict__ wsg, int E, int H, int NRP,
+                                      uint16_t *__restrict__ dst) {
+  const size_t n = (size_t)NRP * H / 8;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t row = i / (H / 8), c = i % (H / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < (size_t)E) v = reinterpret_cast<const uint4 *>(wr + row * H)[c];
+    else if (row == (size_t)E && wsg) v = reinterpret_cast<const uint4 *>(wsg)[c];
+    reinterpret_cast<uint4 *>(dst)[i] = v;
+  }
+}
+
+// Tile list (0, row0, rows) covering T rows.
+__global__ void pf_row_tiles_kernel(int T, int32_t *__restrict__ mtiles,
+                                    int32_t *__restrict__ n_mtiles) {
+  const int nm = (T + PF_BM - 1) / PF_BM;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < nm) {
+    mtiles[3 * i] = 0;
+    mtiles[3 * i + 1] = i * PF_BM;
+    mtiles[3 * i + 2] = min(PF_BM, T - i * PF_BM);
+  }
+  if (i == 0) *n_mtiles = nm;
+}
+
+// ----------------------------------------------------------------------------
+// P2: per token softmax + top-k + renormalisation (one warp per token).
+// ----------------------------------------------------------------------------
+template <int PER>
+__global__ void pf_topk_kernel(const uint16_t *__restrict__ logits, int ld, int T, int E, int k,
+                               int norm_topk, int has_shared, const int32_t *__restrict__ table,
+                               int cap, int32_t *__restrict__ inds, float *__restrict__ scores,
+                               int32_t *__restrict__ counts, float *__restrict__ sgate,
+                               int32_t *__restrict__ out_inds, uint16_t *__restrict__ out_scores,
+                               uint16_t *__restrict__ out_logits, int32_t *__restrict__ status) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  const uint16_t *lr = logits + (size_t)t * ld;
+  float v[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int idx = lane + 32 * i;
+    v[i] = idx < E ? bf2f(lr[idx]) : -INFINITY;
+    if (out_logits && idx < E) out_logits[(size_t)t * E + idx] = lr[idx];
+  }
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) m = fmaxf(m, v[i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  double sd[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int idx = lane + 32 * i;
+    const float ex = idx < E ? expf(__fsub_rn(v[i], m)) : 0.f;
+    v[i] = ex;
+    sd[i] = (double)ex;
+  }
+#pragma unroll
+  for (int w = 1; w < PER; w *= 2)
+#pragma unroll
+    for (int i = 0; i + w < PER; i += 2 * w) sd[i] += sd[i + w];
+  double s = sd[0];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float inv = __frcp_rn((float)s);
+  uint32_t key[PER];
+  uint32_t lb = 0;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int idx = lane + 32 * i;
+    key[i] = idx < E ? ((uint32_t)f2bf(__fmul_rn(v[i], inv)) << 16) | (0xFFFFu - idx) : 0u;
+    lb = max(lb, key[i]);
+  }
+  double ssum = 0.0;
+  uint32_t sel = 0;
+  for (int r = 0; r < k; ++r) {
+    const uint32_t best = __reduce_max_sync(0xffffffffu, lb);
+    if (lb == best) {
+      lb = 0;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        if (key[i] == best) key[i] = 0u;
+        lb = max(lb, key[i]);
+      }
+    }
+    if (lane == r) sel = best;
+    ssum += (double)bf2f(best >> 16);
+  }
+  const float sel_p = bf2f(sel >> 16);
+  float score = sel_p;
+  if (norm_topk) score = rbf(__fdiv_rn(sel_p, rbf((float)ssum)));
+  if (lane < k) {
+    const int ex = 0xFFFF - (int)(sel & 0xFFFFu);
+    const int slot = table[ex];
+    if (slot < 0 || slot >= cap) flag_status(status, slot < 0 ? VB_STATUS_MISS : VB_STATUS_BOUNDS);
+    inds[t * k + lane] = ex;
+    scores[t * k + lane] = score;
+    atomicAdd(counts + ex, 1);
+    if (out_inds) out_inds[t * k + lane] = ex;
+    if (out_scores) out_scores[t * k + lane] = f2bf(score);
+  }
+  if (lane == 0 && has_shared) sgate[t] = rbf(mlx_sigmoid(bf2f(lr[E])));
+}
+
+// ----------------------------------------------------------------------------
+// P3: plan (one CTA of 32 threads; sequential scans over <= 1025 experts).
+// Routed experts whose slot is not resident get no rows.
+// ----------------------------------------------------------------------------
+__global__ void pf_plan_kernel(int32_t *__restrict__ counts, const int32_t *__restrict__ table,
+                               int E, int cap, int T, int has_shared, int layer_cap,
+                               int max_assign, int32_t *__restrict__ offsets,
+                               int32_t *__restrict__ group_of, int32_t *__restrict__ slot_of,
+                               int32_t *__restrict__ cursor, int32_t *__restrict__ mtiles,
+                               int32_t *__restrict__ n_mtiles) {
+  if (threadIdx.x != 0) return;
+  // The reference's groups: experts in id order, skipping empty ones; a
+  // group closes at min(layer_cap, 128) experts or before exceeding
+  // max_assign routes (block.py:154-172).
+  const int gcap = min(layer_cap, 128);
+  int gid = 0, in_group = 0, sum = 0;
+  for (int e = 0; e < E; ++e) {
+    const int c = counts[e];
+    group_of[e] = -1;
+    if (c == 0) continue;
+    if (in_group && (in_group >= gcap || sum + c > max_assign)) {
+      ++gid;
+      in_group = 0;
+      sum = 0;
+    }
+    group_of[e] = gid;
+    ++in_group;
+    sum += c;
+  }
+  int off = 0, nm = 0;
+  const int ne = E + (has_shared ? 1 : 0);
+  for (int e = 0; e < ne; ++e) {
+    int c;
+    if (e < E) {
+      const int slot = table[e];
+      const bool ok = slot >= 0 && slot < cap;
+      slot_of[e] = ok ? slot : -1;
+      c = ok ? counts[e] : 0;
+      counts[e] = c;
+    } else {
+      c = T;
+      slot_of[e] = 0;
+    }
+    offsets[e] = off;
+    cursor[e] = 0;
+    for (int m0 = 0; m0 < c; m0 += PF_BM) {
+      mtiles[3 * nm] = e;
+      mtiles[3 * nm + 1] = off + m0;
+      mtiles[3 * nm + 2] = min(PF_BM, c - m0);
+      ++nm;
+    }
+    off += c;
+  }
+  offsets[ne] = off;
+  *n_mtiles = nm;
+}
+
+// ----------------------------------------------------------------------------
+// P4: gather rows of x into expert order, in the 8-column code order
+// (0,4,1,5,2,6,3,7). One warp per route (t, j), then one per shared row.
+// ----------------------------------------------------------------------------
+__global__ void pf_gather_kernel(const uint16_t *__restrict__ x, int T, int H, int k, int E,
+                                 int has_shared, const int32_t *__restrict__ inds,
+                                 const float *__restrict__ scores,
+                                 const int32_t *__restrict__ slot_of,
+                                 const int32_t *__restrict__ offsets,
+                                 int32_t *__restrict__ cursor, uint16_t *__restrict__ xs,
+                                 float *__restrict__ row_score, int32_t *__restrict__ pos_of) {
+  const int lane = threadIdx.x & 31;
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int R = T * k;
+  if (w >= R + (has_shared ? T : 0)) return;
+  int t, pos = -1;
+  float sc = 1.f;
+  if (w < R) {
+    t = w / k;
+    const int e = inds[w];
+    if (slot_of[e] >= 0) {
+      if (lane == 0) pos = offsets[e] + atomicAdd(cursor + e, 1);
+      pos = __shfl_sync(0xffffffffu, pos, 0);
+    }
+    if (lane == 0) pos_of[w] = pos;
+    sc = scores[w];
+  } else {
+    t = w - R;
+    pos = offsets[E] + t;
+  }
+  if (pos < 0) return;
+  if (lane == 0) row_score[pos] = sc;
+  const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)t * H);
+  uint4 *dst = reinterpret_cast<uint4 *>(xs + (size_t)pos * H);
+  for (int c = lane; c < H / 8; c += 32) {
+    const uint4 v = __ldg(src + c);
+    // bf16 lanes 0..7 -> (0,4,1,5,2,6,3,7)
+    uint4 o;
+    o.x = __byte_perm(v.x, v.z, 0x5410);
+    o.y = __byte_perm(v.x, v.z, 0x7632);
+    o.z = __byte_perm(v.y, v.w, 0x5410);
+    o.w = __byte_perm(v.y, v.w, 0x7632);
+    dst[c] = o;
+  }
+}
+
+// ----------------------------------------------------------------------------
+// P7: combine. One warp per token; routes are ordered by (group of the
+// expert, route rank); lanes own 8 columns at a time.
+// ----------------------------------------------------------------------------
+__global__ void pf_combine_kernel(const uint16_t *__restrict__ ys, int T, int H, int k, int E,
+                                  int has_shared, const int32_t *__restrict__ inds,
+                                  const int32_t *__restrict__ group_of,
+                                  const int32_t *__restrict__ pos_of,
+                                  const int32_t *__restrict__ offsets,
+                                  const float *__restrict__ sgate, uint16_t *__restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  // Order of this token's routes: key = group * 32 + rank (lanes < k).
+  int key = 0x7fffffff, pos = -1;
+  if (lane < k) {
+    pos = pos_of[t * k + lane];
+    const int g = group_of[inds[t * k + lane]];
+    key = pos >= 0 ? g * 32 + lane : 0x7fffffff;
+  }
+  int order[16];
+  int n = 0;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (j >= k) break;
+    // j-th smallest key
+    int kmin = key;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) kmin = min(kmin, __shfl_xor_sync(0xffffffffu, kmin, o));
+    if (kmin == 0x7fffffff) break;
+    const int src = __ffs(__ballot_sync(0xffffffffu, key == kmin)) - 1;
+    order[j] = __shfl_sync(0xffffffffu, pos, src);
+    if (lane == src) key = 0x7fffffff;
+    n = j + 1;
+  }
+  const float g = has_shared ? sgate[t] : 0.f;
+  const uint16_t *shr = has_shared ? ys + (size_t)(offsets[E] + t) * H : nullptr;
+  for (int c = lane * 8; c < H; c += 256) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int j = 0; j < n; ++j) {
+      const uint4 v = *reinterpret_cast<const uint4 *>(ys + (size_t)order[j] * H + c);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[2 * i] = rbf(acc[2 * i] + bf2f(w[i] & 0xFFFF));
+        acc[2 * i + 1] = rbf(acc[2 * i + 1] + bf2f(w[i] >> 16));
+      }
+    }
+    if (has_shared) {
+      const uint4 v = *reinterpret_cast<const uint4 *>(shr + c);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[2 * i] = rbf(acc[2 * i] + rbf(__fmul_rn(g, bf2f(w[i] & 0xFFFF))));
+        acc[2 * i + 1] = rbf(acc[2 * i + 1] + rbf(__fmul_rn(g, bf2f(w[i] >> 16))));
+      }
+    }
+    uint4 o;
+    o.x = pack_bf2(acc[0], acc[1]);
+    o.y = pack_bf2(acc[2], acc[3]);
+    o.z = pack_bf2(acc[4], acc[5]);
+    o.w = pack_bf2(acc[6], acc[7]);
+    *reinterpret_cast<uint4 *>(out + (size_t)t * H + c) = o;
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Host side
+// ----------------------------------------------------------------------------
+struct PrefillLayout {
+  size_t wr, logits, inds, scores, sgate, counts, offsets, group_of, slot_of, cursor, mtiles,
+      n_mtiles, pos_of, row_score, xs, hs, ys, total;
+  int NRP, rows, max_mtiles;
+};
+
+static PrefillLayout prefill_layout(int T, int H, int I, int E, int k) {
+  PrefillLayout L;
+  L.NRP = ((E + 1) + PF_BN - 1) / PF_BN * PF_BN;
+  L.rows = T * k + T;
+  L.max_mtiles = L.rows / PF_BM + E + 2;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 1024);
+    return o;
+  };
+  L.wr = take((size_t)L.NRP * H * 2);
+  L.logits = take((size_t)T * L.NRP * 2);
+  L.inds = take((size_t)T * k * 4);
+  L.scores = take((size_t)T * k * 4);
+  L.sgate = take((size_t)T * 4);
+  L.counts = take((size_t)(E + 2) * 4);
+  L.offsets = take((size_t)(E + 2) * 4);
+  L.group_of = take((size_t)(E + 1) * 4);
+  L.slot_of = take((size_t)(E + 1) * 4);
+  L.cursor = take((size_t)(E + 1) * 4);
+  L.mtiles = take((size_t)L.max_mtiles * 3 * 4);
+  L.n_mtiles = take(4);
+  L.pos_of = take((size_t)T * k * 4);
+  L.row_score = take((size_t)L.rows * 4);
+  L.xs = take((size_t)(L.rows + PF_BM) * H * 2);
+  L.hs = take((size_t)(L.rows + PF_BM) * I * 2);
+  L.ys = take((size_t)(L.rows + PF_BM) * H * 2);
+  L.total = off;
+  return L;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// bf16 [rows, cols] row-major, box {64 cols, box_rows}, 128-byte swizzle.
+static int make_map_bf16(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols,
+                         uint32_t box_rows) {
+  EncodeTiledFn f = encode_fn();
+  if (!f) return set_error(VB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides,
+                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(VB_ERR_INVALID, "tensor map (bf16) failed: %d", (int)r);
+  return VB_OK;
+}
+
+// Packed 4-bit codes of one pool tensor: bytes [slots][rows][cols/2], box
+// {32 bytes, box_rows, 1}.
+static int make_map_codes(CUtensorMap *m, const void *base, uint64_t slots, uint64_t slot_stride,
+                          uint64_t rows, uint64_t cols, uint32_t box_rows) {
+  EncodeTiledFn f = encode_fn();
+  if (!f) return set_error(VB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {cols / 2, rows, slots};
+  const cuuint64_t strides[2] = {cols / 2, slot_stride};
+  const cuuint32_t box[3] = {32, box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = f(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void *>(base), dims, strides,
+                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(VB_ERR_INVALID, "tensor map (codes) failed: %d", (int)r);
+  return VB_OK;
+}
+
+static int pf_sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int MODE>
+static int launch_gemm(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
+                       const CUtensorMap &s0, const CUtensorMap &s1, const PfGemmParams &p,
+                       int max_tiles, cudaStream_t s) {
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(pf_gemm_kernel<MODE>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
+  });
+  if (attr_err != cudaSuccess)
+    return set_error(VB_ERR_CUDA, "pf_gemm_kernel attributes: %s", cudaGetErrorString(attr_err));
+  const int grid = std::max(1, std::min(pf_sm_count(), max_tiles));
+  pf_gemm_kernel<MODE><<<grid, PF_THREADS, PF_SMEM, s>>>(a, b0, b1, s0, s1, p);
+  return check_launch("pf_gemm_kernel");
+}
+
+}  // namespace vb
+
+using namespace vb;
+
+extern "C" {
+
+size_t vb_moe_prefill_workspace_size(int32_t tokens, int32_t hidden, int32_t inter,
+                                     int32_t num_experts, int32_t top_k) {
+  if (tokens <= 0 || hidden <= 0 || inter <= 0 || num_experts <= 0 || top_k <= 0) return 0;
+  return prefill_layout(tokens, hidden, inter, num_experts, top_k).total;
+}
+
+int vb_moe_prefill(const VbMoePrefillArgs *a, vb_stream_t stream) {
+  VB_REQUIRE(a, "vb_moe_prefill: null args");
+  const int T = a->tokens, H = a->hidden, I = a->inter, E = a->num_experts, k = a->top_k;
+  VB_REQUIRE(T >= 1, "vb_moe_prefill: tokens=%d", T);
+  VB_REQUIRE(a->bits == 4, "vb_moe_prefill: bits=%d (only 4-bit)", a->bits);
+  VB_REQUIRE(a->group == 64 || a->group == 128, "vb_moe_prefill: group=%d", a->group);
+  VB_REQUIRE(H % 256 == 0 && H >= 256 && H <= 8192, "vb_moe_prefill: hidden=%d", H);
+  VB_REQUIRE(I % 128 == 0 && I >= 128 && I <= 4096, "vb_moe_prefill: inter=%d", I);
+  VB_REQUIRE(E >= k && E <= 1024 && k >= 1 && k <= 16, "vb_moe_prefill: experts/top_k");
+  VB_REQUIRE(a->x && a->router_w && a->slot_table && a->out, "vb_moe_prefill: null tensor");
+  VB_REQUIRE(a->pool.ptr[0] && a->pool.cap > 0, "vb_moe_prefill: empty pool");
+  const bool has_shared = a->shared.ptr[0] != nullptr;
+  VB_REQUIRE(!has_shared || a->shared_gate_w, "vb_moe_prefill: shared expert without gate");
+  const PrefillLayout L = prefill_layout(T, H, I, E, k);
+  VB_REQUIRE(a->workspace && a->workspace_bytes >= L.total, "vb_moe_prefill: workspace %zu < %zu",
+             a->workspace_bytes, L.total);
+  VB_REQUIRE(((uintptr_t)a->workspace % 1024) == 0, "vb_moe_prefill: workspace alignment");
+  VB_REQUIRE(((uintptr_t)a->x % 16) == 0 && ((uintptr_t)a->out % 16) == 0,
+             "vb_moe_prefill: x/out must be 16-byte aligned");
+  for (int i = 0; i < 9; ++i)
+    VB_REQUIRE(((uintptr_t)a->pool.ptr[i] % 16) == 0 && (a->pool.slot_stride[i] % 16) == 0 &&
+                   (!has_shared || ((uintptr_t)a->shared.ptr[i] % 16) == 0),
+               "vb_moe_prefill: pool tensors must be 16-byte aligned");
+  uint8_t *ws = static_cast<uint8_t *>(a->workspace);
+  auto W = [&](size_t off) { return ws + off; };
+  cudaStream_t s = as_stream(stream);
+  const int gshift = a->group == 128 ? 1 : 0;
+  int rc;
+
+  // P0 + P1: router rows and router GEMM over x (natural column order).
+  pf_router_rows_kernel<<<256, 256, 0, s>>>(a->router_w, has_shared ? a->shared_gate_w : nullptr,
+                                            E, H, L.NRP, (uint16_t *)W(L.wr));
+  if ((rc = check_launch("pf_router_rows_kernel")) != VB_OK) return rc;
+  cudaMemsetAsync(W(L.counts), 0, (size_t)(E + 2) * 4, s);
+  // Router tiles: all tokens as one "expert" (id 0).
+  {
+    const int nm = (T + PF_BM - 1) / PF_BM;
+    VB_REQUIRE(nm <= L.max_mtiles, "vb_moe_prefill: router tiles");
+    pf_row_tiles_kernel<<<(nm + 255) / 256, 256, 0, s>>>(T, (int32_t *)W(L.mtiles),
+                                                         (int32_t *)W(L.n_mtiles));
+    if ((rc = check_launch("pf_row_tiles_kernel")) != VB_OK) return rc;
+    CUtensorMap ta, tb;
+    if ((rc = make_map_bf16(&ta, a->x, T, H, PF_BM)) != VB_OK) return rc;
+    if ((rc = make_map_bf16(&tb, W(L.wr), L.NRP, H, PF_BN)) != VB_OK) return rc;
+    PfGemmParams p{};
+    p.mode = PF_ROUTER;
+    p.K = H;
+    p.nt = L.NRP / PF_BN;
+    p.shared_e = -1;
+    p.n_valid = E;
+    p.mtiles = (const int32_t *)W(L.mtiles);
+    p.n_mtiles = (const int32_t *)W(L.n_mtiles);
+    p.out = (uint16_t *)W(L.logits);
+    p.out_ld = L.NRP;
+    p.bias = a->router_bias;
+    p.status = a->status;
+    if ((rc = launch_gemm<PF_ROUTER>(ta, tb, tb, tb, tb, p, nm * p.nt, s)) != VB_OK) return rc;
+  }
+  // P2
+  {
+    const int per = E <= 256 ? 8 : (E <= 512 ? 16 : 32);
+    auto kfn = per == 8 ? pf_topk_kernel<8> : per == 16 ? pf_topk_kernel<16> : pf_topk_kernel<32>;
+    kfn<<<(T + 7) / 8, 256, 0, s>>>((const uint16_t *)W(L.logits), L.NRP, T, E, k, a->norm_topk,
+                                    has_shared ? 1 : 0, a->slot_table, a->pool.cap,
+                                    (int32_t *)W(L.inds), (float *)W(L.scores),
+                                    (int32_t *)W(L.counts), (float *)W(L.sgate), a->out_inds,
+                                    a->out_scores, a->out_logits, a->status);
+    if ((rc = check_launch("pf_topk_kernel")) != VB_OK) return rc;
+  }
+  // P3
+  pf_plan_kernel<<<1, 32, 0, s>>>((int32_t *)W(L.counts), a->slot_table, E, a->pool.cap, T,
+                                  has_shared ? 1 : 0, a->layer_cap > 0 ? a->layer_cap : E,
+                                  a->max_assignments > 0 ? a->max_assignments : 32768,
+                                  (int32_t *)W(L.offsets), (int32_t *)W(L.group_of),
+                                  (int32_t *)W(L.slot_of), (int32_t *)W(L.cursor),
+                                  (int32_t *)W(L.mtiles), (int32_t *)W(L.n_mtiles));
+  if ((rc = check_launch("pf_plan_kernel")) != VB_OK) return rc;
+  // P4
+  {
+    const int warps = T * k + (has_shared ? T : 0);
+    pf_gather_kernel<<<(warps + 7) / 8, 256, 0, s>>>(
+        a->x, T, H, k, E, has_shared ? 1 : 0, (const int32_t *)W(L.inds),
+        (const float *)W(L.scores), (const int32_t *)W(L.slot_of), (const int32_t *)W(L.offsets),
+        (int32_t *)W(L.cursor), (uint16_t *)W(L.xs), (float *)W(L.row_score),
+        (int32_t *)W(L.pos_of));
+    if ((rc = check_launch("pf_gather_kernel")) != VB_OK) return rc;
+  }
+  const int rows_alloc = L.rows + PF_BM;
+  // P5 gate/up
+  {
+    CUtensorMap ta, g, u, sg, su;
+    if ((rc = make_map_bf16(&ta, W(L.xs), rows_alloc, H, PF_BM)) != VB_OK) return rc;
+    if ((rc = make_map_codes(&g, a->pool.ptr[0], a->pool.cap, a->pool.slot_stride[0], I, H, 128)) != VB_OK) return rc;
+    if ((rc = make_map_codes(&u, a->pool.ptr[3], a->pool.cap, a->pool.slot_stride[3], I, H, 128)) != VB_OK) return rc;
+    if (has_shared) {
+      if ((rc = make_map_codes(&sg, a->shared.ptr[0], 1, (uint64_t)I * H / 2, I, H, 128)) != VB_OK) return rc;
+      if ((rc = make_map_codes(&su, a->shared.ptr[3], 1, (uint64_t)I * H / 2, I, H, 128)) != VB_OK) return rc;
+    } else {
+      sg = g;
+      su = u;
+    }
+    PfGemmParams p{};
+    p.mode = PF_GATEUP;
+    p.K = H;
+    p.nt = I / 128;
+    p.gshift = gshift;
+    p.shared_e = has_shared ? E : -1;
+    p.mtiles = (const int32_t *)W(L.mtiles);
+    p.n_mtiles = (const int32_t *)W(L.n_mtiles);
+    p.slot_of = (const int32_t *)W(L.slot_of);
+    p.pool = a->pool;
+    p.shared = a->shared;
+    p.out = (uint16_t *)W(L.hs);
+    p.out_ld = I;
+    p.status = a->status;
+    if ((rc = launch_gemm<PF_GATEUP>(ta, g, u, sg, su, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
+  }
+  // P6 down
+  {
+    CUtensorMap ta, d, sd;
+    if ((rc = make_map_bf16(&ta, W(L.hs), rows_alloc, I, PF_BM)) != VB_OK) return rc;
+    if ((rc = make_map_codes(&d, a->pool.ptr[6], a->pool.cap, a->pool.slot_stride[6], H, I, PF_BN)) != VB_OK) return rc;
+    if (has_shared) {
+      if ((rc = make_map_codes(&sd, a->shared.ptr[6], 1, (uint64_t)H * I / 2, H, I, PF_BN)) != VB_OK) return rc;
+    } else {
+      sd = d;
+    }
+    PfGemmParams p{};
+    p.mode = PF_DOWN;
+    p.K = I;
+    p.nt = H / PF_BN;
+    p.gshift = gshift;
+    p.shared_e = has_shared ? E : -1;
+    p.mtiles = (const int32_t *)W(L.mtiles);
+    p.n_mtiles = (const int32_t *)W(L.n_mtiles);
+    p.slot_of = (const int32_t *)W(L.slot_of);
+    p.pool = a->pool;
+    p.shared = a->shared;
+    p.out = (uint16_t *)W(L.ys);
+    p.out_ld = H;
+    p.row_score = (const float *)W(L.row_score);
+    p.status = a->status;
+    if ((rc = launch_gemm<PF_DOWN>(ta, d, d, sd, sd, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
+  }
+  // P7
+  pf_combine_kernel<<<(T + 7) / 8, 256, 0, s>>>(
+      (const uint16_t *)W(L.ys), T, H, k, E, has_shared ? 1 : 0, (const int32_t *)W(L.inds),
+      (const int32_t *)W(L.group_of), (const int32_t *)W(L.pos_of), (const int32_t *)W(L.offsets),
+      (const float *)W(L.sgate), a->out);
+  return check_launch("pf_combine_kernel");
+}
+
+}  // extern "C"
