@@ -75,6 +75,7 @@ struct PfGemmParams {
   const int32_t *mtiles;   // [n] (expert, row0, rows)
   const int32_t *n_mtiles;
   const int32_t *slot_of;  // expert -> pool slot
+  const int32_t *heavy_of; // expert -> index of its pre-dequantized bf16 copy, or -1
   VbQuantPool pool, shared;
   uint16_t *out;    // output rows (bf16)
   int out_ld;
@@ -99,7 +100,8 @@ template <int MODE>
 __global__ void __launch_bounds__(PF_THREADS, 1)
 pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmS0,
-               const __grid_constant__ CUtensorMap tmS1, PfGemmParams p) {
+               const __grid_constant__ CUtensorMap tmS1, const __grid_constant__ CUtensorMap tmHv,
+               PfGemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
@@ -158,11 +160,17 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int e = p.mtiles[3 * mt], row0 = p.mtiles[3 * mt + 1];
         const bool sh = e == p.shared_e;
         const int slot = sh ? 0 : (MODE == PF_ROUTER ? 0 : p.slot_of[e]);
+        const int hv = MODE == PF_ROUTER ? -1 : p.heavy_of[e];
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
           const int s = it % PF_STAGES;
           const uint32_t ph = (it / PF_STAGES) & 1;
           if (!tc::mbar_wait(&bar_empty[s], ph ^ 1, abort, PF_WAIT_NS)) { fail(); break; }
-          if (MODE == PF_ROUTER) {
+          if (hv >= 0) {
+            // pre-dequantized bf16 weights: straight into the B tile
+            tc::mbar_arrive_expect_tx(&bar_tma[s], PF_A_BYTES + PF_B_BYTES);
+            tc::tma_load_2d(stage_a(s), &tmA, &bar_tma[s], ks * PF_BK, row0);
+            tc::tma_load_3d(stage_b(s), &tmHv, &bar_tma[s], ks * PF_BK, nt * PF_BN, hv);
+          } else if (MODE == PF_ROUTER) {
             tc::mbar_arrive_expect_tx(&bar_tma[s], PF_A_BYTES + PF_B_BYTES);
             tc::tma_load_2d(stage_a(s), &tmA, &bar_tma[s], ks * PF_BK, row0);
             tc::tma_load_2d(stage_b(s), &tmB0, &bar_tma[s], ks * PF_BK, nt * PF_BN);
@@ -193,9 +201,11 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     if (lane == 0) {
       const uint32_t idesc = tc::idesc_bf16_f32(PF_BM, PF_BN);
       int it = 0, tcount = 0;
+      uint32_t deq_par = 0;  // per stage: parity of the next dequant phase
       bool issued = false;
       for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++tcount) {
         const int acc = tcount & 1;
+        const bool deq = DEQ && p.heavy_of[p.mtiles[3 * (t / p.nt)]] < 0;
         if (!tc::mbar_wait(&bar_acc_empty[acc], ((tcount >> 1) & 1) ^ 1, abort, PF_WAIT_NS)) {
           fail();
           break;
@@ -206,8 +216,12 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
           const int s = it % PF_STAGES;
           const uint32_t ph = (it / PF_STAGES) & 1;
-          uint64_t *ready = DEQ ? &bar_deq[s] : &bar_tma[s];
-          if (!tc::mbar_wait(ready, ph, abort, PF_WAIT_NS)) { fail(); ok = false; break; }
+          // The dequant barrier of a stage only advances on dequantized
+          // steps, so its parity is tracked separately.
+          uint64_t *ready = deq ? &bar_deq[s] : &bar_tma[s];
+          const uint32_t rph = deq ? ((deq_par >> s) & 1u) : ph;
+          if (deq) deq_par ^= 1u << s;
+          if (!tc::mbar_wait(ready, rph, abort, PF_WAIT_NS)) { fail(); ok = false; break; }
           tc::tc_fence_after();
           const uint32_t a0 = tc::smem_u32(stage_a(s)), b0 = tc::smem_u32(stage_b(s));
 #pragma unroll
@@ -235,6 +249,20 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
       const int mt = t / p.nt, nt = t % p.nt;
       const int e = p.mtiles[3 * mt];
+      if (p.heavy_of[e] >= 0) {
+        // Pre-dequantized: B arrives by TMA. Still follow every phase of the
+        // TMA barriers so that no later parity wait can match a stale phase.
+        bool ok = true;
+        for (int ks = 0; ks < ksteps; ++ks, ++it) {
+          if (!tc::mbar_wait(&bar_tma[it % PF_STAGES], (it / PF_STAGES) & 1, abort, PF_WAIT_NS)) {
+            fail();
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
+        continue;
+      }
       const bool sh = e == p.shared_e;
       const VbQuantPool &pool = sh ? p.shared : p.pool;
       const int slot = sh ? 0 : p.slot_of[e];
@@ -477,60 +505,163 @@ __global__ void pf_topk_kernel(const uint16_t *__restrict__ logits, int ld, int 
 }
 
 // ----------------------------------------------------------------------------
-// P3: plan (one CTA of 32 threads; sequential scans over <= 1025 experts).
-// Routed experts whose slot is not resident get no rows.
+// P3: plan (one CTA of 1024 threads). Routed experts whose slot is not
+// resident get no rows. Experts (and the shared expert) with at least
+// PF_HEAVY_ROWS rows get a pre-dequantized bf16 copy (up to PF_HEAVY_MAX).
 // ----------------------------------------------------------------------------
-__global__ void pf_plan_kernel(int32_t *__restrict__ counts, const int32_t *__restrict__ table,
-                               int E, int cap, int T, int has_shared, int layer_cap,
-                               int max_assign, int32_t *__restrict__ offsets,
-                               int32_t *__restrict__ group_of, int32_t *__restrict__ slot_of,
-                               int32_t *__restrict__ cursor, int32_t *__restrict__ mtiles,
-                               int32_t *__restrict__ n_mtiles) {
-  if (threadIdx.x != 0) return;
-  // The reference's groups: experts in id order, skipping empty ones; a
-  // group closes at min(layer_cap, 128) experts or before exceeding
-  // max_assign routes (block.py:154-172).
-  const int gcap = min(layer_cap, 128);
-  int gid = 0, in_group = 0, sum = 0;
-  for (int e = 0; e < E; ++e) {
-    const int c = counts[e];
-    group_of[e] = -1;
-    if (c == 0) continue;
-    if (in_group && (in_group >= gcap || sum + c > max_assign)) {
-      ++gid;
-      in_group = 0;
-      sum = 0;
-    }
-    group_of[e] = gid;
-    ++in_group;
-    sum += c;
+constexpr int PF_PLAN_THREADS = 1024;
+constexpr int PF_HEAVY_ROWS = 3 * PF_BM;
+constexpr int PF_HEAVY_MAX = 48;
+
+__device__ __forceinline__ int block_excl_scan(int v, int *tmp) {
+  // inclusive scan over the CTA via shared memory (Hillis-Steele), returns exclusive
+  const int tid = threadIdx.x;
+  tmp[tid] = v;
+  __syncthreads();
+  for (int o = 1; o < PF_PLAN_THREADS; o <<= 1) {
+    const int add = tid >= o ? tmp[tid - o] : 0;
+    __syncthreads();
+    tmp[tid] += add;
+    __syncthreads();
   }
-  int off = 0, nm = 0;
+  const int incl = tmp[tid];
+  __syncthreads();
+  return incl - v;
+}
+
+__global__ void __launch_bounds__(PF_PLAN_THREADS)
+pf_plan_kernel(int32_t *__restrict__ counts, const int32_t *__restrict__ table, int E, int cap,
+               int T, int has_shared, int layer_cap, int max_assign,
+               int32_t *__restrict__ offsets, int32_t *__restrict__ group_of,
+               int32_t *__restrict__ slot_of, int32_t *__restrict__ heavy_of,
+               int32_t *__restrict__ heavy_e, int32_t *__restrict__ n_heavy,
+               int32_t *__restrict__ cursor, int32_t *__restrict__ mtiles,
+               int32_t *__restrict__ n_mtiles) {
+  __shared__ int s_cnt[PF_PLAN_THREADS];
+  __shared__ int s_tmp[PF_PLAN_THREADS];
+  const int tid = threadIdx.x;
   const int ne = E + (has_shared ? 1 : 0);
-  for (int e = 0; e < ne; ++e) {
-    int c;
-    if (e < E) {
-      const int slot = table[e];
-      const bool ok = slot >= 0 && slot < cap;
-      slot_of[e] = ok ? slot : -1;
-      c = ok ? counts[e] : 0;
-      counts[e] = c;
-    } else {
-      c = T;
-      slot_of[e] = 0;
+  int c = 0;
+  if (tid < E) c = counts[tid];
+  else if (tid == E && has_shared) c = T;
+  s_cnt[tid] = c;
+  __syncthreads();
+  if (tid == 0) {
+    // The reference's groups: experts in id order, skipping empty ones; a
+    // group closes at min(layer_cap, 128) experts or before exceeding
+    // max_assign routes (block.py:154-172).
+    const int gcap = min(layer_cap, 128);
+    int gid = 0, in_group = 0, sum = 0;
+    for (int e = 0; e < E; ++e) {
+      const int ce = s_cnt[e];
+      if (ce == 0) {
+        group_of[e] = -1;
+        continue;
+      }
+      if (in_group && (in_group >= gcap || sum + ce > max_assign)) {
+        ++gid;
+        in_group = 0;
+        sum = 0;
+      }
+      group_of[e] = gid;
+      ++in_group;
+      sum += ce;
     }
-    offsets[e] = off;
-    cursor[e] = 0;
-    for (int m0 = 0; m0 < c; m0 += PF_BM) {
-      mtiles[3 * nm] = e;
-      mtiles[3 * nm + 1] = off + m0;
-      mtiles[3 * nm + 2] = min(PF_BM, c - m0);
-      ++nm;
-    }
-    off += c;
   }
-  offsets[ne] = off;
-  *n_mtiles = nm;
+  // Rows only for resident experts.
+  int slot = -1;
+  if (tid < E) {
+    const int sl = table[tid];
+    slot = (sl >= 0 && sl < cap) ? sl : -1;
+    if (slot < 0) c = 0;
+    counts[tid] = c;
+  } else if (tid == E && has_shared) {
+    slot = 0;
+  }
+  if (tid < ne) {
+    slot_of[tid] = slot;
+    cursor[tid] = 0;
+  }
+  const int off = block_excl_scan(c, s_tmp);
+  const int nt = (c + PF_BM - 1) / PF_BM;
+  const int toff = block_excl_scan(nt, s_tmp);
+  const int hflag = (tid < ne && c >= PF_HEAVY_ROWS) ? 1 : 0;
+  const int hidx = block_excl_scan(hflag, s_tmp);
+  if (tid < ne) {
+    offsets[tid] = off;
+    const int h = (hflag && hidx < PF_HEAVY_MAX) ? hidx : -1;
+    heavy_of[tid] = h;
+    if (h >= 0) heavy_e[h] = tid;
+    for (int m = 0; m < nt; ++m) {
+      mtiles[3 * (toff + m)] = tid;
+      mtiles[3 * (toff + m) + 1] = off + m * PF_BM;
+      mtiles[3 * (toff + m) + 2] = min(PF_BM, c - m * PF_BM);
+    }
+  }
+  if (tid == ne - 1) {
+    offsets[ne] = off + c;
+    *n_mtiles = toff + nt;
+    *n_heavy = min(hidx + hflag, PF_HEAVY_MAX);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Pre-dequantization of the heavy experts into bf16 (the same values and
+// 8-column code order as the GEMM's own dequantization). Gate/up rows are
+// stored in 256-row blocks [gate rows 128j..128j+127 | up rows 128j..],
+// down rows as they are. One thread per packed word.
+// ----------------------------------------------------------------------------
+__global__ void pf_predequant_kernel(VbQuantPool pool, VbQuantPool shared, int shared_e,
+                                     const int32_t *__restrict__ heavy_e,
+                                     const int32_t *__restrict__ n_heavy,
+                                     const int32_t *__restrict__ slot_of, int H, int I,
+                                     int gshift, uint16_t *__restrict__ wgu,
+                                     uint16_t *__restrict__ wd) {
+  const int h = blockIdx.y;
+  if (h >= *n_heavy) return;
+  const int e = heavy_e[h];
+  const bool sh = e == shared_e;
+  const VbQuantPool &pl = sh ? shared : pool;
+  const int slot = sh ? 0 : slot_of[e];
+  const size_t wgu_words = (size_t)2 * I * (H / 8), wd_words = (size_t)H * (I / 8);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < wgu_words + wd_words;
+       i += (size_t)gridDim.x * blockDim.x) {
+    int row, wcol, K, tw, tsc;
+    uint16_t *dst;
+    if (i < wgu_words) {
+      K = H;
+      const int r = (int)(i / (H / 8));  // destination row
+      wcol = (int)(i % (H / 8));
+      const int blk = r >> 8, within = r & 255;
+      const bool up = within >= 128;
+      row = blk * 128 + (within & 127);
+      tw = up ? 3 : 0;
+      tsc = up ? 4 : 1;
+      dst = wgu + ((size_t)h * 2 * I + r) * H + wcol * 8;
+    } else {
+      K = I;
+      const size_t j = i - wgu_words;
+      row = (int)(j / (I / 8));
+      wcol = (int)(j % (I / 8));
+      tw = 6;
+      tsc = 7;
+      dst = wd + ((size_t)h * H + row) * I + wcol * 8;
+    }
+    const uint32_t w = reinterpret_cast<const uint32_t *>(pool_ptr(pl, tw, slot))[(size_t)row * (K / 8) + wcol];
+    const int ng = (K >> 6) >> gshift, gi = (wcol * 8 / 64) >> gshift;
+    const uint32_t sc = reinterpret_cast<const uint16_t *>(pool_ptr(pl, tsc, slot))[(size_t)row * ng + gi];
+    const uint32_t bi = reinterpret_cast<const uint16_t *>(pool_ptr(pl, tsc + 1, slot))[(size_t)row * ng + gi];
+    const uint32_t s2 = sc | (sc << 16), b2 = bi | (bi << 16);
+    uint32_t pr[4], o[4];
+    nib_pairs4(w, pr);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t q;
+      asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(pr[k]), "r"(0x43004300u));
+      o[k] = bf16x2_fma(q, s2, b2);
+    }
+    *reinterpret_cast<uint4 *>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
 }
 
 // ----------------------------------------------------------------------------
@@ -651,8 +782,8 @@ __global__ void pf_combine_kernel(const uint16_t *__restrict__ ys, int T, int H,
 // Host side
 // ----------------------------------------------------------------------------
 struct PrefillLayout {
-  size_t wr, logits, inds, scores, sgate, counts, offsets, group_of, slot_of, cursor, mtiles,
-      n_mtiles, pos_of, row_score, xs, hs, ys, total;
+  size_t wr, logits, inds, scores, sgate, counts, offsets, group_of, slot_of, heavy_of, heavy_e,
+      n_heavy, cursor, mtiles, n_mtiles, pos_of, row_score, xs, hs, ys, wgu, wd, total;
   int NRP, rows, max_mtiles;
 };
 
@@ -661,6 +792,7 @@ static PrefillLayout prefill_layout(int T, int H, int I, int E, int k) {
   L.NRP = ((E + 1) + PF_BN - 1) / PF_BN * PF_BN;
   L.rows = T * k + T;
   L.max_mtiles = L.rows / PF_BM + E + 2;
+  if (E + 1 > PF_PLAN_THREADS) L.max_mtiles = -1;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -676,6 +808,9 @@ static PrefillLayout prefill_layout(int T, int H, int I, int E, int k) {
   L.offsets = take((size_t)(E + 2) * 4);
   L.group_of = take((size_t)(E + 1) * 4);
   L.slot_of = take((size_t)(E + 1) * 4);
+  L.heavy_of = take((size_t)(E + 1) * 4);
+  L.heavy_e = take((size_t)PF_HEAVY_MAX * 4);
+  L.n_heavy = take(4);
   L.cursor = take((size_t)(E + 1) * 4);
   L.mtiles = take((size_t)L.max_mtiles * 3 * 4);
   L.n_mtiles = take(4);
@@ -684,6 +819,8 @@ static PrefillLayout prefill_layout(int T, int H, int I, int E, int k) {
   L.xs = take((size_t)(L.rows + PF_BM) * H * 2);
   L.hs = take((size_t)(L.rows + PF_BM) * I * 2);
   L.ys = take((size_t)(L.rows + PF_BM) * H * 2);
+  L.wgu = take((size_t)PF_HEAVY_MAX * 2 * I * H * 2);
+  L.wd = take((size_t)PF_HEAVY_MAX * H * I * 2);
   L.total = off;
   return L;
 }
@@ -723,6 +860,22 @@ static int make_map_bf16(CUtensorMap *m, const void *base, uint64_t rows, uint64
   return VB_OK;
 }
 
+// bf16 [n][rows][cols] (row-major), box {64 cols, box_rows, 1}, 128-byte swizzle.
+static int make_map_bf16_3d(CUtensorMap *m, const void *base, uint64_t n, uint64_t rows,
+                            uint64_t cols, uint32_t box_rows) {
+  EncodeTiledFn f = encode_fn();
+  if (!f) return set_error(VB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[3] = {cols, rows, n};
+  const cuuint64_t strides[2] = {cols * 2, rows * cols * 2};
+  const cuuint32_t box[3] = {64, box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides,
+                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(VB_ERR_INVALID, "tensor map (bf16 3d) failed: %d", (int)r);
+  return VB_OK;
+}
+
 // Packed 4-bit codes of one pool tensor: bytes [slots][rows][cols/2], box
 // {32 bytes, box_rows, 1}.
 static int make_map_codes(CUtensorMap *m, const void *base, uint64_t slots, uint64_t slot_stride,
@@ -753,8 +906,8 @@ static int pf_sm_count() {
 
 template <int MODE>
 static int launch_gemm(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
-                       const CUtensorMap &s0, const CUtensorMap &s1, const PfGemmParams &p,
-                       int max_tiles, cudaStream_t s) {
+                       const CUtensorMap &s0, const CUtensorMap &s1, const CUtensorMap &hv,
+                       const PfGemmParams &p, int max_tiles, cudaStream_t s) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
@@ -764,7 +917,7 @@ static int launch_gemm(const CUtensorMap &a, const CUtensorMap &b0, const CUtens
   if (attr_err != cudaSuccess)
     return set_error(VB_ERR_CUDA, "pf_gemm_kernel attributes: %s", cudaGetErrorString(attr_err));
   const int grid = std::max(1, std::min(pf_sm_count(), max_tiles));
-  pf_gemm_kernel<MODE><<<grid, PF_THREADS, PF_SMEM, s>>>(a, b0, b1, s0, s1, p);
+  pf_gemm_kernel<MODE><<<grid, PF_THREADS, PF_SMEM, s>>>(a, b0, b1, s0, s1, hv, p);
   return check_launch("pf_gemm_kernel");
 }
 
@@ -788,7 +941,7 @@ int vb_moe_prefill(const VbMoePrefillArgs *a, vb_stream_t stream) {
   VB_REQUIRE(a->group == 64 || a->group == 128, "vb_moe_prefill: group=%d", a->group);
   VB_REQUIRE(H % 256 == 0 && H >= 256 && H <= 8192, "vb_moe_prefill: hidden=%d", H);
   VB_REQUIRE(I % 128 == 0 && I >= 128 && I <= 4096, "vb_moe_prefill: inter=%d", I);
-  VB_REQUIRE(E >= k && E <= 1024 && k >= 1 && k <= 16, "vb_moe_prefill: experts/top_k");
+  VB_REQUIRE(E >= k && E < PF_PLAN_THREADS && k >= 1 && k <= 16, "vb_moe_prefill: experts/top_k");
   VB_REQUIRE(a->x && a->router_w && a->slot_table && a->out, "vb_moe_prefill: null tensor");
   VB_REQUIRE(a->pool.ptr[0] && a->pool.cap > 0, "vb_moe_prefill: empty pool");
   const bool has_shared = a->shared.ptr[0] != nullptr;
@@ -836,7 +989,7 @@ int vb_moe_prefill(const VbMoePrefillArgs *a, vb_stream_t stream) {
     p.out_ld = L.NRP;
     p.bias = a->router_bias;
     p.status = a->status;
-    if ((rc = launch_gemm<PF_ROUTER>(ta, tb, tb, tb, tb, p, nm * p.nt, s)) != VB_OK) return rc;
+    if ((rc = launch_gemm<PF_ROUTER>(ta, tb, tb, tb, tb, tb, p, nm * p.nt, s)) != VB_OK) return rc;
   }
   // P2
   {
@@ -850,13 +1003,18 @@ int vb_moe_prefill(const VbMoePrefillArgs *a, vb_stream_t stream) {
     if ((rc = check_launch("pf_topk_kernel")) != VB_OK) return rc;
   }
   // P3
-  pf_plan_kernel<<<1, 32, 0, s>>>((int32_t *)W(L.counts), a->slot_table, E, a->pool.cap, T,
-                                  has_shared ? 1 : 0, a->layer_cap > 0 ? a->layer_cap : E,
-                                  a->max_assignments > 0 ? a->max_assignments : 32768,
-                                  (int32_t *)W(L.offsets), (int32_t *)W(L.group_of),
-                                  (int32_t *)W(L.slot_of), (int32_t *)W(L.cursor),
-                                  (int32_t *)W(L.mtiles), (int32_t *)W(L.n_mtiles));
+  pf_plan_kernel<<<1, PF_PLAN_THREADS, 0, s>>>(
+      (int32_t *)W(L.counts), a->slot_table, E, a->pool.cap, T, has_shared ? 1 : 0,
+      a->layer_cap > 0 ? a->layer_cap : E, a->max_assignments > 0 ? a->max_assignments : 32768,
+      (int32_t *)W(L.offsets), (int32_t *)W(L.group_of), (int32_t *)W(L.slot_of),
+      (int32_t *)W(L.heavy_of), (int32_t *)W(L.heavy_e), (int32_t *)W(L.n_heavy),
+      (int32_t *)W(L.cursor), (int32_t *)W(L.mtiles), (int32_t *)W(L.n_mtiles));
   if ((rc = check_launch("pf_plan_kernel")) != VB_OK) return rc;
+  pf_predequant_kernel<<<dim3(64, PF_HEAVY_MAX), 256, 0, s>>>(
+      a->pool, a->shared, has_shared ? E : -1, (const int32_t *)W(L.heavy_e),
+      (const int32_t *)W(L.n_heavy), (const int32_t *)W(L.slot_of), H, I, gshift,
+      (uint16_t *)W(L.wgu), (uint16_t *)W(L.wd));
+  if ((rc = check_launch("pf_predequant_kernel")) != VB_OK) return rc;
   // P4
   {
     const int warps = T * k + (has_shared ? T : 0);
@@ -881,8 +1039,11 @@ int vb_moe_prefill(const VbMoePrefillArgs *a, vb_stream_t stream) {
       sg = g;
       su = u;
     }
+    CUtensorMap hv;
+    if ((rc = make_map_bf16_3d(&hv, W(L.wgu), PF_HEAVY_MAX, 2 * (uint64_t)I, H, PF_BN)) != VB_OK) return rc;
     PfGemmParams p{};
     p.mode = PF_GATEUP;
+    p.heavy_of = (const int32_t *)W(L.heavy_of);
     p.K = H;
     p.nt = I / 128;
     p.gshift = gshift;
@@ -895,7 +1056,7 @@ int vb_moe_prefill(const VbMoePrefillArgs *a, vb_stream_t stream) {
     p.out = (uint16_t *)W(L.hs);
     p.out_ld = I;
     p.status = a->status;
-    if ((rc = launch_gemm<PF_GATEUP>(ta, g, u, sg, su, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
+    if ((rc = launch_gemm<PF_GATEUP>(ta, g, u, sg, su, hv, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
   }
   // P6 down
   {
@@ -907,8 +1068,11 @@ int vb_moe_prefill(const VbMoePrefillArgs *a, vb_stream_t stream) {
     } else {
       sd = d;
     }
+    CUtensorMap hv;
+    if ((rc = make_map_bf16_3d(&hv, W(L.wd), PF_HEAVY_MAX, H, I, PF_BN)) != VB_OK) return rc;
     PfGemmParams p{};
     p.mode = PF_DOWN;
+    p.heavy_of = (const int32_t *)W(L.heavy_of);
     p.K = I;
     p.nt = H / PF_BN;
     p.gshift = gshift;
@@ -922,7 +1086,7 @@ int vb_moe_prefill(const VbMoePrefillArgs *a, vb_stream_t stream) {
     p.out_ld = H;
     p.row_score = (const float *)W(L.row_score);
     p.status = a->status;
-    if ((rc = launch_gemm<PF_DOWN>(ta, d, d, sd, sd, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
+    if ((rc = launch_gemm<PF_DOWN>(ta, d, d, sd, sd, hv, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
   }
   // P7
   pf_combine_kernel<<<(T + 7) / 8, 256, 0, s>>>(

@@ -58,6 +58,28 @@ def config0(seed: int = 0, device="cuda", hidden=H, inter=I, num_experts=E, top_
     return blk, x
 
 
+def zipf_bias(seed: int, num_experts: int = E, s: float = 1.1) -> np.ndarray:
+    """Router logit bias ``b_e = ln Zipf_pmf(rank(e); s)`` with the rank of
+    each expert from a seeded permutation (config 2's skewed routing)."""
+    rng = np.random.Generator(np.random.PCG64([seed, 424242]))
+    ranks = rng.permutation(num_experts) + 1
+    pmf = ranks.astype(np.float64) ** -s
+    pmf /= (np.arange(1, num_experts + 1, dtype=np.float64) ** -s).sum()
+    return np.log(pmf).astype(np.float32)
+
+
+def config2(seed: int = 2, T: int = 32768, device="cuda", hidden=H, inter=I, num_experts=E,
+            top_k=K):
+    """Config 2: one sparse-MoE layer for expert-major prefill of T tokens;
+    all experts resident (identity table), Zipf(1.1) router bias."""
+    pool = QuantPool.empty_blob(num_experts, hidden, inter, 4, 64, device)
+    bias = torch.from_numpy(zipf_bias(seed, num_experts)).to(device)
+    blk = make_layer(seed, 0, pool, range(num_experts), device, hidden, inter, num_experts,
+                     top_k, router_bias=bias)
+    x = input_tokens(seed, T, hidden, device)
+    return blk, x
+
+
 class DecodeStack:
     """Config 1: ``L`` stacked MoE blocks, T tokens (MTP K=3 verify uses 4).
 
