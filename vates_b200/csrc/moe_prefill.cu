@@ -39,7 +39,7 @@
 // (A tile 128x64 bf16 with the 128-byte swizzle, packed B 256 rows x 32 B),
 // warp 1 issues tcgen05.mma (M=128, N=256, K=16 steps) into one of two TMEM
 // accumulators, warps 4-11 dequantize B into the swizzled bf16 layout, and
-// warps 12-15 drain TMEM through the epilogue. Every mbarrier wait is
+// warps 12-19 drain TMEM through the epilogue. Every mbarrier wait is
 // bounded; on a timeout the kernel raises VB_STATUS_TIMEOUT, winds down and
 // frees its TMEM.
 #include <algorithm>
@@ -55,7 +55,7 @@ constexpr int PF_BM = 128;
 constexpr int PF_BN = 256;
 constexpr int PF_BK = 64;
 constexpr int PF_STAGES = 3;
-constexpr int PF_THREADS = 512;
+constexpr int PF_THREADS = 640;  // 20 warps
 constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;        // 16 KB
 constexpr int PF_B_BYTES = PF_BN * PF_BK * 2;        // 32 KB
 constexpr int PF_P_BYTES = PF_BN * PF_BK / 2;        // 8 KB packed codes
@@ -123,7 +123,7 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     for (int a = 0; a < 2; ++a) {
       tc::mbar_init(&bar_acc_full[a], 1);
-      tc::mbar_init(&bar_acc_empty[a], 4);
+      tc::mbar_init(&bar_acc_empty[a], 8);
     }
     tc::mbar_init(&bar_final, 1);
     s_abort = 0;
@@ -254,7 +254,8 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // TMA barriers so that no later parity wait can match a stale phase.
         bool ok = true;
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
-          if (!tc::mbar_wait(&bar_tma[it % PF_STAGES], (it / PF_STAGES) & 1, abort, PF_WAIT_NS)) {
+          if (!tc::mbar_wait_sleep(&bar_tma[it % PF_STAGES], (it / PF_STAGES) & 1, abort,
+                                   PF_WAIT_NS)) {
             fail();
             ok = false;
             break;
@@ -313,14 +314,16 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
   } else if (warp >= 12) {
     // ---------------- epilogue ----------------
-    const int q = warp & 3;
+    // 8 warps: lane quarter q = warp % 4 (TMEM lanes 32q..32q+31), column
+    // half hf = (warp - 12) / 4.
+    const int q = warp & 3, hf = (warp - 12) >> 2;
     const int m = q * 32 + lane;  // tile row = TMEM lane
     int tcount = 0;
     for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++tcount) {
       const int mt = t / p.nt, nt = t % p.nt;
       const int row0 = p.mtiles[3 * mt + 1], rows = p.mtiles[3 * mt + 2];
       const int acc = tcount & 1;
-      if (!tc::mbar_wait(&bar_acc_full[acc], (tcount >> 1) & 1, abort, PF_WAIT_NS)) {
+      if (!tc::mbar_wait_sleep(&bar_acc_full[acc], (tcount >> 1) & 1, abort, PF_WAIT_NS)) {
         fail();
         break;
       }
@@ -329,55 +332,61 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const bool valid = m < rows;
       const size_t orow = (size_t)(row0 + m);
       if (MODE == PF_GATEUP) {
-        // Columns [0,128) gate, [128,256) up of intermediate rows nt*128 + c.
+        // Columns [0,128) gate, [128,256) up of intermediate rows nt*128 + c;
+        // this warp takes c in [64 hf, 64 hf + 64).
 #pragma unroll 1
-        for (int c0 = 0; c0 < 128; c0 += 16) {
-          uint32_t g[16], u[16];
-          tc::tmem_ld16(tb + c0, g);
-          tc::tmem_ld16(tb + 128 + c0, u);
+        for (int c0 = 64 * hf; c0 < 64 * hf + 64; c0 += 32) {
+          uint32_t g[32], u[32];
+          tc::tmem_ld32(tb + c0, g);
+          tc::tmem_ld32(tb + 128 + c0, u);
           tc::tmem_ld_wait();
-          float h[16];
+          uint32_t o[16];
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            h[j] = swiglu_bf16(rbf(__uint_as_float(g[j])), rbf(__uint_as_float(u[j])));
-          // Two 8-column blocks in the (0,4,1,5,2,6,3,7) code order.
-          uint32_t o[8];
+          for (int b = 0; b < 4; ++b) {
+            float h[8];
 #pragma unroll
-          for (int b = 0; b < 2; ++b)
+            for (int j = 0; j < 8; ++j)
+              h[j] = swiglu_bf16(rbf(__uint_as_float(g[8 * b + j])),
+                                 rbf(__uint_as_float(u[8 * b + j])));
+            // 8-column block in the (0,4,1,5,2,6,3,7) code order
 #pragma unroll
-            for (int i = 0; i < 4; ++i) o[4 * b + i] = pack_bf2(h[8 * b + i], h[8 * b + i + 4]);
+            for (int i = 0; i < 4; ++i) o[4 * b + i] = pack_bf2(h[i], h[i + 4]);
+          }
           if (valid) {
             uint4 *dst = reinterpret_cast<uint4 *>(p.out + orow * p.out_ld + nt * 128 + c0);
-            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
           }
         }
       } else {
         const float sc = (MODE == PF_DOWN && valid) ? p.row_score[orow] : 1.f;
 #pragma unroll 1
-        for (int c0 = 0; c0 < PF_BN; c0 += 16) {
-          uint32_t v[16];
-          tc::tmem_ld16(tb + c0, v);
+        for (int c0 = 128 * hf; c0 < 128 * hf + 128; c0 += 32) {
+          uint32_t v[32];
+          tc::tmem_ld32(tb + c0, v);
           tc::tmem_ld_wait();
-          float y[16];
+          uint32_t o[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const float a = __uint_as_float(v[j]);
+            float y0 = __uint_as_float(v[2 * j]), y1 = __uint_as_float(v[2 * j + 1]);
             if (MODE == PF_DOWN) {
-              y[j] = rbf(__fmul_rn(rbf(a), sc));
+              y0 = rbf(__fmul_rn(rbf(y0), sc));
+              y1 = rbf(__fmul_rn(rbf(y1), sc));
             } else {
-              const int col = nt * PF_BN + c0 + j;
-              const float b = (p.bias && col < p.n_valid) ? p.bias[col] : 0.f;
-              y[j] = rbf(a + b);
+              const int col = nt * PF_BN + c0 + 2 * j;
+              const float b0 = (p.bias && col < p.n_valid) ? p.bias[col] : 0.f;
+              const float b1 = (p.bias && col + 1 < p.n_valid) ? p.bias[col + 1] : 0.f;
+              y0 = rbf(y0 + b0);
+              y1 = rbf(y1 + b1);
             }
+            o[j] = pack_bf2(y0, y1);
           }
-          uint32_t o[8];
-#pragma unroll
-          for (int j = 0; j < 8; ++j) o[j] = pack_bf2(y[2 * j], y[2 * j + 1]);
           if (valid) {
             uint4 *dst = reinterpret_cast<uint4 *>(p.out + orow * p.out_ld + nt * PF_BN + c0);
-            dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-            dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+#pragma unroll
+            for (int w = 0; w < 4; ++w)
+              dst[w] = make_uint4(o[4 * w], o[4 * w + 1], o[4 * w + 2], o[4 * w + 3]);
           }
         }
       }
@@ -1010,7 +1019,7 @@ int vb_moe_prefill(const VbMoePrefillArgs *a, vb_stream_t stream) {
       (int32_t *)W(L.heavy_of), (int32_t *)W(L.heavy_e), (int32_t *)W(L.n_heavy),
       (int32_t *)W(L.cursor), (int32_t *)W(L.mtiles), (int32_t *)W(L.n_mtiles));
   if ((rc = check_launch("pf_plan_kernel")) != VB_OK) return rc;
-  pf_predequant_kernel<<<dim3(64, PF_HEAVY_MAX), 256, 0, s>>>(
+  pf_predequant_kernel<<<dim3(384, PF_HEAVY_MAX), 256, 0, s>>>(
       a->pool, a->shared, has_shared ? E : -1, (const int32_t *)W(L.heavy_e),
       (const int32_t *)W(L.n_heavy), (const int32_t *)W(L.slot_of), H, I, gshift,
       (uint16_t *)W(L.wgu), (uint16_t *)W(L.wd));
