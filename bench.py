@@ -185,6 +185,89 @@ def run_reference(args, world, rank):
 
 # ------------------------------------------------------------------ GPU arm
 
+PREFILL_FLOPS_32K = 2.3365e12   # routed + shared + router FLOPs of one 32768-token layer
+
+
+def run_prefill_leg(steps: int = 10, warmup: int = 3, T: int = 32768):
+    """Config 2: expert-major prefill of T tokens through one layer (device
+    time per call of vb_moe_prefill, inputs resident in HBM)."""
+    import torch
+    from vates_b200.prefill import moe_prefill
+    from vates_b200.synth import config2
+    _, bf16_peak, peak_kind = peaks()
+    blk, x = config2(T=T)
+    out = torch.empty_like(x)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    for _ in range(max(warmup, 3)):
+        moe_prefill(blk, x, out=out, status=status)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        moe_prefill(blk, x, out=out)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    flops = PREFILL_FLOPS_32K * T / 32768
+    tf = flops / (ms / 1e3) / 1e12
+    res = {"workload": "prefill_32k_1layer", "tokens": T, "ms_per_step": ms,
+           "tok_per_s": T / (ms / 1e3), "tflops_algorithmic": tf,
+           "frac_of_bf16_peak": tf / bf16_peak, "peak_tflops": bf16_peak, "peak_kind": peak_kind,
+           "status": int(status.item()), "routing": "Zipf(1.1) router bias, top-10 of 512",
+           "flops_per_step": flops}
+    del blk, x, out
+    torch.cuda.empty_cache()
+    return res
+
+
+def run_isoquant_leg(steps: int = 20, warmup: int = 3, S: int = 131072, layers: int = 12):
+    """Config 3: quantized GQA decode attention over 12 IsoQuant K4/V3 caches
+    of S tokens (Hq=16, Hkv=2, D=256), one query (T=1) and an MTP verify
+    block (T=4, causal). Algorithmic bytes: the packed cache read once."""
+    import torch
+    from vates_b200.quant_kv import AsymmetricQuantizedKVCache, asym_quantized_sdpa, build_block_so4, so4_blocks
+    hbm_peak, _, peak_kind = peaks()
+    g = torch.Generator(device="cuda").manual_seed(3)
+    rk = so4_blocks(build_block_so4(256, seed=0))
+    rv = so4_blocks(build_block_so4(256, seed=1))
+    caches = []
+    for _ in range(layers):
+        c = AsymmetricQuantizedKVCache(64, 4, 3)
+        k = torch.randn((1, 2, S, 256), generator=g, device="cuda").to(torch.bfloat16)
+        v = torch.randn((1, 2, S, 256), generator=g, device="cuda").to(torch.bfloat16)
+        kq, vq = c.update_and_fetch(k, v, rk=rk, rv=rv)
+        caches.append((kq, vq))
+        del k, v
+    torch.cuda.synchronize()
+    res = {"workload": "isoquant_128k_12layers", "context": S, "layers": layers}
+    bytes_step = layers * 2 * S * (128 + 96 + 32)
+    for T in (1, 4):
+        q = torch.randn((1, 16, T, 256), generator=g, device="cuda").to(torch.bfloat16)
+        ws = torch.empty(1 << 26, dtype=torch.uint8, device="cuda")
+        mask = "causal" if T > 1 else None
+
+        def step():
+            for kq, vq in caches:
+                asym_quantized_sdpa(q, kq, vq, 256 ** -0.5, mask, 64, 4, 3, rv=rv, workspace=ws)
+        for _ in range(max(warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / steps * 1e3
+        gbs = bytes_step / (us / 1e6) / 1e9
+        res[f"T{T}"] = {"us_per_step": us, "hbm_gbs_algorithmic": gbs,
+                        "frac_of_hbm_peak": gbs / hbm_peak, "bytes_per_step": bytes_step}
+    res["peak_gbs"], res["peak_kind"] = hbm_peak, peak_kind
+    del caches
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_decode(args, world, rank, local):
     import torch
     from vates_b200.synth import DecodeStack
@@ -319,6 +402,9 @@ def run_decode(args, world, rank, local):
         "gpu_launches": 3 * L * args.steps,
         "clocks": clocks,
     }
+    if world == 1 and not args.no_extra:
+        out["prefill"] = run_prefill_leg()
+        out["isoquant"] = run_isoquant_leg()
     if rank == 0 and not args.no_cpu:
         dt, det = cpu_decode_sample(args.cpu_layers)
         cpu_tok_s = T / (dt * L / args.cpu_layers)
@@ -342,6 +428,8 @@ def main():
     ap.add_argument("--cpu-layers", type=int, default=2)
     ap.add_argument("--ref-layers", type=int, default=1)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the prefill (config 2) and IsoQuant (config 3) legs")
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
     try:
