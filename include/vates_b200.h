@@ -231,6 +231,132 @@ size_t vb_moe_prefill_workspace_size(int32_t tokens, int32_t hidden,
 int vb_moe_prefill(const VbMoePrefillArgs *args, vb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Phases of the expert-major prefill, for callers that place experts
+ * themselves (the expert-parallel prefill: every rank owns a subset of the
+ * experts). vb_moe_prefill = route + experts + combine on one device.
+ *
+ * vb_moe_route: router GEMM, precise softmax, top-k, renormalisation for T
+ * tokens (block.py:253, 321-329) and the route histogram (block.py:142-144;
+ * out_counts[E] overwritten, [E] entries). out_scores are bf16 values stored
+ * as f32; out_sgate (when shared_gate_w is given) = bf16(sigmoid(x.w_sg)). */
+typedef struct VbMoeRouteArgs {
+  int32_t tokens;
+  int32_t hidden;
+  int32_t num_experts;
+  int32_t top_k;
+  int32_t norm_topk;
+  int32_t reserved0;
+  const uint16_t *x;            /* bf16 [T, H] */
+  const uint16_t *router_w;     /* bf16 [E, H] */
+  const float *router_bias;     /* nullable f32 [E] */
+  const uint16_t *shared_gate_w; /* nullable bf16 [H] */
+  int32_t *out_inds;            /* [T, k] */
+  float *out_scores;            /* [T, k] */
+  float *out_sgate;             /* [T] when shared_gate_w */
+  int32_t *out_counts;          /* [E + 1] (entry E left 0) */
+  uint16_t *out_logits;         /* nullable bf16 [T, E] */
+  int32_t *status;
+  void *workspace;              /* vb_moe_route_workspace_size, 1024-aligned */
+  size_t workspace_bytes;
+} VbMoeRouteArgs;
+size_t vb_moe_route_workspace_size(int32_t tokens, int32_t hidden,
+                                   int32_t num_experts);
+int vb_moe_route(const VbMoeRouteArgs *args, vb_stream_t stream);
+
+/* vb_moe_experts: the per-group expert work of _expert_major_forward
+ * (block.py:206-216: gather rows, gather_qmm gate/up -> SwiGLU -> down,
+ * y * score) for an arbitrary route list. Route i reads row route_row[i] of
+ * x, runs expert route_expert[i] (num_experts = the shared expert, < 0 =
+ * skipped) and writes bf16(bf16(y) * route_score[i]) to row i of out (zeros
+ * for skipped routes or experts without a slot). */
+typedef struct VbMoeExpertsArgs {
+  int32_t rows;                 /* rows of x */
+  int32_t routes;
+  int32_t hidden;
+  int32_t inter;
+  int32_t group;
+  int32_t bits;                 /* 4 */
+  int32_t num_experts;
+  int32_t reserved0;
+  const uint16_t *x;            /* bf16 [rows, H] */
+  const int32_t *route_row;     /* [routes] */
+  const int32_t *route_expert;  /* [routes] */
+  const float *route_score;     /* [routes] */
+  const int32_t *slot_table;    /* [E], -1 = not resident on this device */
+  VbQuantPool pool;
+  VbQuantPool shared;           /* ptr[0] == NULL: no shared expert */
+  uint16_t *out;                /* bf16 [routes, H] */
+  int32_t *status;
+  void *workspace;              /* vb_moe_experts_workspace_size, 1024-aligned */
+  size_t workspace_bytes;
+} VbMoeExpertsArgs;
+size_t vb_moe_experts_workspace_size(int32_t routes, int32_t hidden,
+                                     int32_t inter, int32_t num_experts);
+int vb_moe_experts(const VbMoeExpertsArgs *args, vb_stream_t stream);
+
+/* vb_moe_combine: the reduce of _expert_major_forward (block.py:220 with
+ * deterministic_route_reduce, custom_kernel.py:63-77) and the shared expert
+ * add (block.py:345-346). Per token the k routed rows y_routes[route_row[t*k
+ * + j]] (route_row -1 = skipped) are added from zero in the order (reference
+ * group of the expert, route rank j), rounding to bf16 after every add; the
+ * groups come from `counts`, the route histogram of the WHOLE prefill batch
+ * (all ranks), with layer_cap / max_assignments as in VbMoePrefillArgs. Then
+ * + bf16(sgate[t] * y_shared[shared_row ? shared_row[t] : t]). */
+typedef struct VbMoeCombineArgs {
+  int32_t tokens;
+  int32_t hidden;
+  int32_t num_experts;
+  int32_t top_k;
+  int32_t layer_cap;
+  int32_t max_assignments;
+  const int32_t *inds;          /* [T, k] */
+  const int32_t *counts;        /* [E] */
+  const uint16_t *y_routes;     /* bf16 rows */
+  const int32_t *route_row;     /* [T, k] */
+  const uint16_t *y_shared;     /* nullable bf16 rows */
+  const int32_t *shared_row;    /* nullable [T] */
+  const float *sgate;           /* [T] when y_shared */
+  uint16_t *out;                /* bf16 [T, H] */
+  int32_t *group_of_ws;         /* device scratch [E] */
+} VbMoeCombineArgs;
+int vb_moe_combine(const VbMoeCombineArgs *args, vb_stream_t stream);
+
+/* Expert-parallel dispatch (no counterpart in the reference, which runs on
+ * one device). vb_ep_pack: for T local tokens and owner[e] = rank holding
+ * expert e, packs the rows to send (each token row once per destination
+ * rank; destination-major, tokens ascending) and the route metadata
+ * (row in the destination's chunk, expert, score bits; routes (t, j)
+ * ascending), and returns per-destination row / route counts and, per local
+ * route, its index in the send order. Buffers are sized for the worst case:
+ * send_x [T * min(k, world), H], send_meta [T * k, 3]. */
+typedef struct VbEpPackArgs {
+  int32_t tokens;
+  int32_t top_k;
+  int32_t hidden;
+  int32_t world;                /* <= 8 */
+  const uint16_t *x;            /* bf16 [T, H] */
+  const int32_t *inds;          /* [T, k] */
+  const float *scores;          /* [T, k] */
+  const int32_t *owner;         /* [E] */
+  uint16_t *send_x;
+  int32_t *send_meta;
+  int32_t *route_send_idx;      /* [T, k] */
+  int32_t *dest_rows;           /* [world] */
+  int32_t *dest_routes;         /* [world] */
+  void *workspace;              /* vb_ep_pack_workspace_size */
+  size_t workspace_bytes;
+} VbEpPackArgs;
+size_t vb_ep_pack_workspace_size(int32_t tokens, int32_t world);
+int vb_ep_pack(const VbEpPackArgs *args, vb_stream_t stream);
+/* Received routes -> (row of the received rows, expert, score): source s
+ * sent routes [src_route_off[s], src_route_off[s+1]) whose rows start at
+ * src_row_off[s] in the received rows. */
+int vb_ep_unpack(const int32_t *recv_meta, int32_t routes,
+                 const int32_t *src_route_off, const int32_t *src_row_off,
+                 int32_t world, int32_t *route_row, int32_t *route_expert,
+                 float *route_score, vb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Deterministic route reduce: replaces deterministic_route_reduce
  * (mlx_streaming/core/moe/custom_kernel.py:20-118). previous [tokens, H],
  * weighted [G, H], assignment_pos int32 [G] (unique flat route positions in

@@ -51,6 +51,50 @@ class VbMoePrefillArgs(C.Structure):
     ]
 
 
+class VbMoeRouteArgs(C.Structure):
+    _fields_ = [
+        ("tokens", C.c_int32), ("hidden", C.c_int32), ("num_experts", C.c_int32),
+        ("top_k", C.c_int32), ("norm_topk", C.c_int32), ("reserved0", C.c_int32),
+        ("x", C.c_void_p), ("router_w", C.c_void_p), ("router_bias", C.c_void_p),
+        ("shared_gate_w", C.c_void_p), ("out_inds", C.c_void_p), ("out_scores", C.c_void_p),
+        ("out_sgate", C.c_void_p), ("out_counts", C.c_void_p), ("out_logits", C.c_void_p),
+        ("status", C.c_void_p), ("workspace", C.c_void_p), ("workspace_bytes", C.c_size_t),
+    ]
+
+
+class VbMoeExpertsArgs(C.Structure):
+    _fields_ = [
+        ("rows", C.c_int32), ("routes", C.c_int32), ("hidden", C.c_int32), ("inter", C.c_int32),
+        ("group", C.c_int32), ("bits", C.c_int32), ("num_experts", C.c_int32),
+        ("reserved0", C.c_int32),
+        ("x", C.c_void_p), ("route_row", C.c_void_p), ("route_expert", C.c_void_p),
+        ("route_score", C.c_void_p), ("slot_table", C.c_void_p),
+        ("pool", VbQuantPool), ("shared", VbQuantPool),
+        ("out", C.c_void_p), ("status", C.c_void_p), ("workspace", C.c_void_p),
+        ("workspace_bytes", C.c_size_t),
+    ]
+
+
+class VbMoeCombineArgs(C.Structure):
+    _fields_ = [
+        ("tokens", C.c_int32), ("hidden", C.c_int32), ("num_experts", C.c_int32),
+        ("top_k", C.c_int32), ("layer_cap", C.c_int32), ("max_assignments", C.c_int32),
+        ("inds", C.c_void_p), ("counts", C.c_void_p), ("y_routes", C.c_void_p),
+        ("route_row", C.c_void_p), ("y_shared", C.c_void_p), ("shared_row", C.c_void_p),
+        ("sgate", C.c_void_p), ("out", C.c_void_p), ("group_of_ws", C.c_void_p),
+    ]
+
+
+class VbEpPackArgs(C.Structure):
+    _fields_ = [
+        ("tokens", C.c_int32), ("top_k", C.c_int32), ("hidden", C.c_int32), ("world", C.c_int32),
+        ("x", C.c_void_p), ("inds", C.c_void_p), ("scores", C.c_void_p), ("owner", C.c_void_p),
+        ("send_x", C.c_void_p), ("send_meta", C.c_void_p), ("route_send_idx", C.c_void_p),
+        ("dest_rows", C.c_void_p), ("dest_routes", C.c_void_p), ("workspace", C.c_void_p),
+        ("workspace_bytes", C.c_size_t),
+    ]
+
+
 _P = C.c_void_p
 _I32 = C.c_int32
 _I64 = C.c_int64
@@ -70,6 +114,14 @@ _SIGNATURES = {
     "vb_moe_decode_noalloc": (_I32, [C.POINTER(VbMoeDecodeArgs), _P]),
     "vb_moe_prefill_workspace_size": (_SZ, [_I32, _I32, _I32, _I32, _I32]),
     "vb_moe_prefill": (_I32, [C.POINTER(VbMoePrefillArgs), _P]),
+    "vb_moe_route_workspace_size": (_SZ, [_I32, _I32, _I32]),
+    "vb_moe_route": (_I32, [C.POINTER(VbMoeRouteArgs), _P]),
+    "vb_moe_experts_workspace_size": (_SZ, [_I32, _I32, _I32, _I32]),
+    "vb_moe_experts": (_I32, [C.POINTER(VbMoeExpertsArgs), _P]),
+    "vb_moe_combine": (_I32, [C.POINTER(VbMoeCombineArgs), _P]),
+    "vb_ep_pack_workspace_size": (_SZ, [_I32, _I32]),
+    "vb_ep_pack": (_I32, [C.POINTER(VbEpPackArgs), _P]),
+    "vb_ep_unpack": (_I32, [_P, _I32, _P, _P, _I32, _P, _P, _P, _P]),
     "vb_route_reduce_workspace_size": (_SZ, [_I32, _I32]),
     "vb_route_reduce": (_I32, [_P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _P, _P,
                                _SZ, _P]),

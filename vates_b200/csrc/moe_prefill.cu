@@ -502,8 +502,10 @@ __global__ void pf_topk_kernel(const uint16_t *__restrict__ logits, int ld, int 
   if (norm_topk) score = rbf(__fdiv_rn(sel_p, rbf((float)ssum)));
   if (lane < k) {
     const int ex = 0xFFFF - (int)(sel & 0xFFFFu);
-    const int slot = table[ex];
-    if (slot < 0 || slot >= cap) flag_status(status, slot < 0 ? VB_STATUS_MISS : VB_STATUS_BOUNDS);
+    if (table) {
+      const int slot = table[ex];
+      if (slot < 0 || slot >= cap) flag_status(status, slot < 0 ? VB_STATUS_MISS : VB_STATUS_BOUNDS);
+    }
     inds[t * k + lane] = ex;
     scores[t * k + lane] = score;
     atomicAdd(counts + ex, 1);
@@ -540,54 +542,25 @@ __device__ __forceinline__ int block_excl_scan(int v, int *tmp) {
 
 __global__ void __launch_bounds__(PF_PLAN_THREADS)
 pf_plan_kernel(int32_t *__restrict__ counts, const int32_t *__restrict__ table, int E, int cap,
-               int T, int has_shared, int layer_cap, int max_assign,
-               int32_t *__restrict__ offsets, int32_t *__restrict__ group_of,
-               int32_t *__restrict__ slot_of, int32_t *__restrict__ heavy_of,
-               int32_t *__restrict__ heavy_e, int32_t *__restrict__ n_heavy,
-               int32_t *__restrict__ cursor, int32_t *__restrict__ mtiles,
-               int32_t *__restrict__ n_mtiles) {
-  __shared__ int s_cnt[PF_PLAN_THREADS];
+               int has_shared, int32_t *__restrict__ offsets, int32_t *__restrict__ slot_of,
+               int32_t *__restrict__ heavy_of, int32_t *__restrict__ heavy_e,
+               int32_t *__restrict__ n_heavy, int32_t *__restrict__ cursor,
+               int32_t *__restrict__ mtiles, int32_t *__restrict__ n_mtiles) {
   __shared__ int s_tmp[PF_PLAN_THREADS];
   const int tid = threadIdx.x;
-  const int ne = E + (has_shared ? 1 : 0);
-  int c = 0;
-  if (tid < E) c = counts[tid];
-  else if (tid == E && has_shared) c = T;
-  s_cnt[tid] = c;
-  __syncthreads();
-  if (tid == 0) {
-    // The reference's groups: experts in id order, skipping empty ones; a
-    // group closes at min(layer_cap, 128) experts or before exceeding
-    // max_assign routes (block.py:154-172).
-    const int gcap = min(layer_cap, 128);
-    int gid = 0, in_group = 0, sum = 0;
-    for (int e = 0; e < E; ++e) {
-      const int ce = s_cnt[e];
-      if (ce == 0) {
-        group_of[e] = -1;
-        continue;
-      }
-      if (in_group && (in_group >= gcap || sum + ce > max_assign)) {
-        ++gid;
-        in_group = 0;
-        sum = 0;
-      }
-      group_of[e] = gid;
-      ++in_group;
-      sum += ce;
-    }
-  }
+  const int ne = E + 1;  // expert E = the shared expert
+  int c = tid < ne ? counts[tid] : 0;
   // Rows only for resident experts.
   int slot = -1;
   if (tid < E) {
     const int sl = table[tid];
     slot = (sl >= 0 && sl < cap) ? sl : -1;
-    if (slot < 0) c = 0;
-    counts[tid] = c;
   } else if (tid == E && has_shared) {
     slot = 0;
   }
+  if (slot < 0) c = 0;
   if (tid < ne) {
+    counts[tid] = c;
     slot_of[tid] = slot;
     cursor[tid] = 0;
   }
@@ -611,6 +584,70 @@ pf_plan_kernel(int32_t *__restrict__ counts, const int32_t *__restrict__ table, 
     offsets[ne] = off + c;
     *n_mtiles = toff + nt;
     *n_heavy = min(hidx + hflag, PF_HEAVY_MAX);
+  }
+}
+
+// The reference's reduce groups (block.py:154-172): experts in id order,
+// skipping empty ones; a group closes at min(layer_cap, 128) experts or
+// before exceeding max_assign routes. `counts` covers every routed expert of
+// the whole prefill batch (all ranks).
+__global__ void __launch_bounds__(PF_PLAN_THREADS)
+pf_groups_kernel(const int32_t *__restrict__ counts, int E, int layer_cap, int max_assign,
+                 int32_t *__restrict__ group_of) {
+  __shared__ int s_cnt[PF_PLAN_THREADS];
+  const int tid = threadIdx.x;
+  if (tid < E) s_cnt[tid] = counts[tid];
+  __syncthreads();
+  if (tid == 0) {
+    const int gcap = min(layer_cap, 128);
+    int gid = 0, in_group = 0, sum = 0;
+    for (int e = 0; e < E; ++e) {
+      const int ce = s_cnt[e];
+      if (ce == 0) {
+        s_cnt[e] = -1;
+        continue;
+      }
+      if (in_group && (in_group >= gcap || sum + ce > max_assign)) {
+        ++gid;
+        in_group = 0;
+        sum = 0;
+      }
+      s_cnt[e] = gid;
+      ++in_group;
+      sum += ce;
+    }
+  }
+  __syncthreads();
+  if (tid < E) group_of[tid] = s_cnt[tid];
+}
+
+// Route list of a single-GPU prefill: routes t*k+j, then one shared-expert
+// route per token (expert E, score 1).
+__global__ void pf_routes_kernel(int T, int k, int E, int has_shared,
+                                 const int32_t *__restrict__ inds,
+                                 const float *__restrict__ scores, int32_t *__restrict__ r_row,
+                                 int32_t *__restrict__ r_exp, float *__restrict__ r_score) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int R = T * k;
+  if (i < R) {
+    r_row[i] = i / k;
+    r_exp[i] = inds[i];
+    r_score[i] = scores[i];
+  } else if (i < R + T && has_shared) {
+    r_row[i] = i - R;
+    r_exp[i] = E;
+    r_score[i] = 1.f;
+  }
+}
+
+__global__ void pf_set_kernel(int32_t *p, int32_t v) { *p = v; }
+
+// Route histogram over experts 0..E (E = shared); negative ids are skipped.
+__global__ void pf_hist_kernel(const int32_t *__restrict__ r_exp, int n, int E,
+                               int32_t *__restrict__ counts) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int e = r_exp[i];
+    if (e >= 0 && e <= E) atomicAdd(counts + e, 1);
   }
 }
 
@@ -677,35 +714,27 @@ __global__ void pf_predequant_kernel(VbQuantPool pool, VbQuantPool shared, int s
 // P4: gather rows of x into expert order, in the 8-column code order
 // (0,4,1,5,2,6,3,7). One warp per route (t, j), then one per shared row.
 // ----------------------------------------------------------------------------
-__global__ void pf_gather_kernel(const uint16_t *__restrict__ x, int T, int H, int k, int E,
-                                 int has_shared, const int32_t *__restrict__ inds,
-                                 const float *__restrict__ scores,
+__global__ void pf_gather_kernel(const uint16_t *__restrict__ x, int H, int n,
+                                 const int32_t *__restrict__ r_row,
+                                 const int32_t *__restrict__ r_exp,
+                                 const float *__restrict__ r_score,
                                  const int32_t *__restrict__ slot_of,
                                  const int32_t *__restrict__ offsets,
                                  int32_t *__restrict__ cursor, uint16_t *__restrict__ xs,
                                  float *__restrict__ row_score, int32_t *__restrict__ pos_of) {
   const int lane = threadIdx.x & 31;
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int R = T * k;
-  if (w >= R + (has_shared ? T : 0)) return;
-  int t, pos = -1;
-  float sc = 1.f;
-  if (w < R) {
-    t = w / k;
-    const int e = inds[w];
-    if (slot_of[e] >= 0) {
-      if (lane == 0) pos = offsets[e] + atomicAdd(cursor + e, 1);
-      pos = __shfl_sync(0xffffffffu, pos, 0);
-    }
-    if (lane == 0) pos_of[w] = pos;
-    sc = scores[w];
-  } else {
-    t = w - R;
-    pos = offsets[E] + t;
+  if (w >= n) return;
+  const int e = r_exp[w];
+  int pos = -1;
+  if (e >= 0 && slot_of[e] >= 0) {
+    if (lane == 0) pos = offsets[e] + atomicAdd(cursor + e, 1);
+    pos = __shfl_sync(0xffffffffu, pos, 0);
   }
+  if (lane == 0) pos_of[w] = pos;
   if (pos < 0) return;
-  if (lane == 0) row_score[pos] = sc;
-  const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)t * H);
+  if (lane == 0) row_score[pos] = r_score[w];
+  const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)r_row[w] * H);
   uint4 *dst = reinterpret_cast<uint4 *>(xs + (size_t)pos * H);
   for (int c = lane; c < H / 8; c += 32) {
     const uint4 v = __ldg(src + c);
@@ -719,15 +748,29 @@ __global__ void pf_gather_kernel(const uint16_t *__restrict__ x, int T, int H, i
   }
 }
 
+// Rows of the expert-sorted output back into route order (skipped routes
+// become zero rows).
+__global__ void pf_unsort_kernel(const uint16_t *__restrict__ ys, int H, int n,
+                                 const int32_t *__restrict__ pos_of, uint16_t *__restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (w >= n) return;
+  const int pos = pos_of[w];
+  uint4 *dst = reinterpret_cast<uint4 *>(out + (size_t)w * H);
+  const uint4 *src = reinterpret_cast<const uint4 *>(ys + (size_t)(pos < 0 ? 0 : pos) * H);
+  for (int c = lane; c < H / 8; c += 32) dst[c] = pos < 0 ? make_uint4(0, 0, 0, 0) : src[c];
+}
+
 // ----------------------------------------------------------------------------
 // P7: combine. One warp per token; routes are ordered by (group of the
 // expert, route rank); lanes own 8 columns at a time.
 // ----------------------------------------------------------------------------
-__global__ void pf_combine_kernel(const uint16_t *__restrict__ ys, int T, int H, int k, int E,
-                                  int has_shared, const int32_t *__restrict__ inds,
+__global__ void pf_combine_kernel(const uint16_t *__restrict__ y, int T, int H, int k,
+                                  const int32_t *__restrict__ inds,
                                   const int32_t *__restrict__ group_of,
-                                  const int32_t *__restrict__ pos_of,
-                                  const int32_t *__restrict__ offsets,
+                                  const int32_t *__restrict__ route_row,
+                                  const uint16_t *__restrict__ y_shared,
+                                  const int32_t *__restrict__ shared_row,
                                   const float *__restrict__ sgate, uint16_t *__restrict__ out) {
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -735,7 +778,7 @@ __global__ void pf_combine_kernel(const uint16_t *__restrict__ ys, int T, int H,
   // Order of this token's routes: key = group * 32 + rank (lanes < k).
   int key = 0x7fffffff, pos = -1;
   if (lane < k) {
-    pos = pos_of[t * k + lane];
+    pos = route_row[t * k + lane];
     const int g = group_of[inds[t * k + lane]];
     key = pos >= 0 ? g * 32 + lane : 0x7fffffff;
   }
@@ -754,14 +797,16 @@ __global__ void pf_combine_kernel(const uint16_t *__restrict__ ys, int T, int H,
     if (lane == src) key = 0x7fffffff;
     n = j + 1;
   }
+  const bool has_shared = y_shared != nullptr;
   const float g = has_shared ? sgate[t] : 0.f;
-  const uint16_t *shr = has_shared ? ys + (size_t)(offsets[E] + t) * H : nullptr;
+  const uint16_t *shr =
+      has_shared ? y_shared + (size_t)(shared_row ? shared_row[t] : t) * H : nullptr;
   for (int c = lane * 8; c < H; c += 256) {
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
     for (int j = 0; j < n; ++j) {
-      const uint4 v = *reinterpret_cast<const uint4 *>(ys + (size_t)order[j] * H + c);
+      const uint4 v = *reinterpret_cast<const uint4 *>(y + (size_t)order[j] * H + c);
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -788,20 +833,149 @@ __global__ void pf_combine_kernel(const uint16_t *__restrict__ ys, int T, int H,
 }
 
 // ----------------------------------------------------------------------------
+// Expert-parallel dispatch: pack the rows and routes a rank sends to every
+// destination rank (token rows deduplicated per destination; destination-
+// major, tokens ascending, routes (t, j) ascending), and unpack the routes a
+// rank received.
+// ----------------------------------------------------------------------------
+constexpr int EP_MAX_WORLD = 8;
+
+__global__ void ep_count_kernel(const int32_t *__restrict__ inds, const int32_t *__restrict__ owner,
+                                int T, int k, int world, int32_t *__restrict__ tok_cnt) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  int cnt[EP_MAX_WORLD];
+#pragma unroll
+  for (int d = 0; d < EP_MAX_WORLD; ++d) cnt[d] = 0;
+  for (int j = 0; j < k; ++j) {
+    const int d = owner[inds[t * k + j]];
+#pragma unroll
+    for (int q = 0; q < EP_MAX_WORLD; ++q) cnt[q] += (q == d) ? 1 : 0;
+  }
+  for (int d = 0; d < world; ++d) tok_cnt[(size_t)t * world + d] = cnt[d];
+}
+
+// One CTA per destination: exclusive scans over tokens of (token goes to d)
+// and (routes of the token to d).
+__global__ void __launch_bounds__(1024)
+ep_scan_kernel(const int32_t *__restrict__ tok_cnt, int T, int world, int32_t *__restrict__ row_idx,
+               int32_t *__restrict__ route_base, int32_t *__restrict__ dest_rows,
+               int32_t *__restrict__ dest_routes) {
+  __shared__ int s_tmp[1024];
+  const int d = blockIdx.x, tid = threadIdx.x;
+  const int per = (T + 1023) / 1024;
+  const int t0 = tid * per, t1 = min(T, t0 + per);
+  int rows = 0, routes = 0;
+  for (int t = t0; t < t1; ++t) {
+    const int c = tok_cnt[(size_t)t * world + d];
+    rows += c > 0 ? 1 : 0;
+    routes += c;
+  }
+  // two block scans
+  s_tmp[tid] = rows;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {
+    const int add = tid >= o ? s_tmp[tid - o] : 0;
+    __syncthreads();
+    s_tmp[tid] += add;
+    __syncthreads();
+  }
+  int rbase = s_tmp[tid] - rows;
+  const int rtot = s_tmp[1023];
+  __syncthreads();
+  s_tmp[tid] = routes;
+  __syncthreads();
+  for (int o = 1; o < 1024; o <<= 1) {
+    const int add = tid >= o ? s_tmp[tid - o] : 0;
+    __syncthreads();
+    s_tmp[tid] += add;
+    __syncthreads();
+  }
+  int qbase = s_tmp[tid] - routes;
+  const int qtot = s_tmp[1023];
+  for (int t = t0; t < t1; ++t) {
+    const int c = tok_cnt[(size_t)t * world + d];
+    row_idx[(size_t)t * world + d] = c > 0 ? rbase : -1;
+    route_base[(size_t)t * world + d] = qbase;
+    rbase += c > 0 ? 1 : 0;
+    qbase += c;
+  }
+  if (tid == 0) {
+    dest_rows[d] = rtot;
+    dest_routes[d] = qtot;
+  }
+}
+
+// One warp per token: copy the token row once per destination, write the
+// route metadata (row in the destination chunk, expert, score bits) and the
+// route's index in the send order.
+__global__ void ep_pack_kernel(const uint16_t *__restrict__ x, const int32_t *__restrict__ inds,
+                               const float *__restrict__ scores, const int32_t *__restrict__ owner,
+                               int T, int k, int H, int world,
+                               const int32_t *__restrict__ tok_cnt,
+                               const int32_t *__restrict__ row_idx,
+                               const int32_t *__restrict__ route_base,
+                               const int32_t *__restrict__ dest_rows,
+                               const int32_t *__restrict__ dest_routes,
+                               uint16_t *__restrict__ send_x, int32_t *__restrict__ send_meta,
+                               int32_t *__restrict__ route_send_idx) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= T) return;
+  int row_off[EP_MAX_WORLD], route_off[EP_MAX_WORLD];
+  int ro = 0, qo = 0;
+  for (int d = 0; d < world; ++d) {
+    row_off[d] = ro;
+    route_off[d] = qo;
+    ro += dest_rows[d];
+    qo += dest_routes[d];
+  }
+  if (lane < k) {
+    const int e = inds[t * k + lane];
+    const int d = owner[e];
+    int rank = 0;
+    for (int j = 0; j < lane; ++j) rank += owner[inds[t * k + j]] == d ? 1 : 0;
+    const int idx = route_off[d] + route_base[(size_t)t * world + d] + rank;
+    send_meta[3 * (size_t)idx] = row_idx[(size_t)t * world + d];
+    send_meta[3 * (size_t)idx + 1] = e;
+    send_meta[3 * (size_t)idx + 2] = __float_as_int(scores[t * k + lane]);
+    route_send_idx[t * k + lane] = idx;
+  }
+  const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)t * H);
+  for (int d = 0; d < world; ++d) {
+    if (tok_cnt[(size_t)t * world + d] == 0) continue;
+    uint4 *dst = reinterpret_cast<uint4 *>(send_x + (size_t)(row_off[d] + row_idx[(size_t)t * world + d]) * H);
+    for (int c = lane; c < H / 8; c += 32) dst[c] = __ldg(src + c);
+  }
+}
+
+// Received routes: source s's routes [route_off[s], route_off[s+1]) refer to
+// rows relative to s's chunk, which starts at row_off[s].
+__global__ void ep_unpack_kernel(const int32_t *__restrict__ meta, int n,
+                                 const int32_t *__restrict__ route_off,
+                                 const int32_t *__restrict__ row_off, int world,
+                                 int32_t *__restrict__ r_row, int32_t *__restrict__ r_exp,
+                                 float *__restrict__ r_score) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  int s = 0;
+  while (s + 1 < world && i >= route_off[s + 1]) ++s;
+  r_row[i] = row_off[s] + meta[3 * (size_t)i];
+  r_exp[i] = meta[3 * (size_t)i + 1];
+  r_score[i] = __int_as_float(meta[3 * (size_t)i + 2]);
+}
+
+// ----------------------------------------------------------------------------
 // Host side
 // ----------------------------------------------------------------------------
-struct PrefillLayout {
-  size_t wr, logits, inds, scores, sgate, counts, offsets, group_of, slot_of, heavy_of, heavy_e,
-      n_heavy, cursor, mtiles, n_mtiles, pos_of, row_score, xs, hs, ys, wgu, wd, total;
-  int NRP, rows, max_mtiles;
+// Workspace of the route phase (router GEMM + top-k).
+struct RouteLayout {
+  size_t wr, logits, mtiles, n_mtiles, total;
+  int NRP;
 };
-
-static PrefillLayout prefill_layout(int T, int H, int I, int E, int k) {
-  PrefillLayout L;
+static RouteLayout route_layout(int T, int H, int E) {
+  RouteLayout L;
   L.NRP = ((E + 1) + PF_BN - 1) / PF_BN * PF_BN;
-  L.rows = T * k + T;
-  L.max_mtiles = L.rows / PF_BM + E + 2;
-  if (E + 1 > PF_PLAN_THREADS) L.max_mtiles = -1;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -810,26 +984,75 @@ static PrefillLayout prefill_layout(int T, int H, int I, int E, int k) {
   };
   L.wr = take((size_t)L.NRP * H * 2);
   L.logits = take((size_t)T * L.NRP * 2);
-  L.inds = take((size_t)T * k * 4);
-  L.scores = take((size_t)T * k * 4);
-  L.sgate = take((size_t)T * 4);
+  L.mtiles = take((size_t)((T + PF_BM - 1) / PF_BM) * 12);
+  L.n_mtiles = take(4);
+  L.total = off;
+  return L;
+}
+
+// Workspace of the expert phase for n routes (experts 0..E, E = shared).
+struct ExpertsLayout {
+  size_t counts, offsets, slot_of, heavy_of, heavy_e, n_heavy, cursor, mtiles, n_mtiles, pos_of,
+      row_score, xs, hs, ys, wgu, wd, total;
+  int max_mtiles, rows_alloc;
+};
+static ExpertsLayout experts_layout(int n, int H, int I, int E) {
+  ExpertsLayout L;
+  L.max_mtiles = n / PF_BM + E + 2;
+  L.rows_alloc = n + PF_BM;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 1024);
+    return o;
+  };
   L.counts = take((size_t)(E + 2) * 4);
   L.offsets = take((size_t)(E + 2) * 4);
-  L.group_of = take((size_t)(E + 1) * 4);
   L.slot_of = take((size_t)(E + 1) * 4);
   L.heavy_of = take((size_t)(E + 1) * 4);
   L.heavy_e = take((size_t)PF_HEAVY_MAX * 4);
   L.n_heavy = take(4);
   L.cursor = take((size_t)(E + 1) * 4);
-  L.mtiles = take((size_t)L.max_mtiles * 3 * 4);
+  L.mtiles = take((size_t)L.max_mtiles * 12);
   L.n_mtiles = take(4);
-  L.pos_of = take((size_t)T * k * 4);
-  L.row_score = take((size_t)L.rows * 4);
-  L.xs = take((size_t)(L.rows + PF_BM) * H * 2);
-  L.hs = take((size_t)(L.rows + PF_BM) * I * 2);
-  L.ys = take((size_t)(L.rows + PF_BM) * H * 2);
+  L.pos_of = take((size_t)n * 4 + 4);
+  L.row_score = take((size_t)n * 4 + 4);
+  L.xs = take((size_t)L.rows_alloc * H * 2);
+  L.hs = take((size_t)L.rows_alloc * I * 2);
+  L.ys = take((size_t)L.rows_alloc * H * 2);
   L.wgu = take((size_t)PF_HEAVY_MAX * 2 * I * H * 2);
   L.wd = take((size_t)PF_HEAVY_MAX * H * I * 2);
+  L.total = off;
+  return L;
+}
+
+// Single-call prefill: route + route list + experts + combine.
+struct PrefillLayout {
+  RouteLayout R;
+  ExpertsLayout X;
+  size_t route, inds, scores, sgate, counts, r_row, r_exp, r_score, group_of, experts, total;
+};
+static PrefillLayout prefill_layout(int T, int H, int I, int E, int k) {
+  PrefillLayout L;
+  L.R = route_layout(T, H, E);
+  const int n = T * k + T;
+  L.X = experts_layout(n, H, I, E);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, 1024);
+    return o;
+  };
+  L.route = take(L.R.total);
+  L.inds = take((size_t)T * k * 4);
+  L.scores = take((size_t)T * k * 4);
+  L.sgate = take((size_t)T * 4);
+  L.counts = take((size_t)(E + 2) * 4);
+  L.r_row = take((size_t)n * 4);
+  L.r_exp = take((size_t)n * 4);
+  L.r_score = take((size_t)n * 4);
+  L.group_of = take((size_t)(E + 1) * 4);
+  L.experts = take(L.X.total);
   L.total = off;
   return L;
 }
@@ -930,6 +1153,157 @@ static int launch_gemm(const CUtensorMap &a, const CUtensorMap &b0, const CUtens
   return check_launch("pf_gemm_kernel");
 }
 
+// ---- phase implementations ----
+
+static int run_route(const uint16_t *x, int T, int H, int E, int k, int norm_topk,
+                     const uint16_t *router_w, const float *bias, const uint16_t *wsg,
+                     const int32_t *table, int cap, int32_t *inds, float *scores, float *sgate,
+                     int32_t *counts, int32_t *out_inds, uint16_t *out_scores,
+                     uint16_t *out_logits, int32_t *status, uint8_t *ws, cudaStream_t s) {
+  const RouteLayout L = route_layout(T, H, E);
+  auto W = [&](size_t off) { return ws + off; };
+  int rc;
+  pf_router_rows_kernel<<<256, 256, 0, s>>>(router_w, wsg, E, H, L.NRP, (uint16_t *)W(L.wr));
+  if ((rc = check_launch("pf_router_rows_kernel")) != VB_OK) return rc;
+  if (cudaMemsetAsync(counts, 0, (size_t)(E + 1) * 4, s) != cudaSuccess)
+    return set_error(VB_ERR_CUDA, "route: memset");
+  const int nm = (T + PF_BM - 1) / PF_BM;
+  pf_row_tiles_kernel<<<(nm + 255) / 256, 256, 0, s>>>(T, (int32_t *)W(L.mtiles),
+                                                       (int32_t *)W(L.n_mtiles));
+  if ((rc = check_launch("pf_row_tiles_kernel")) != VB_OK) return rc;
+  CUtensorMap ta, tb;
+  if ((rc = make_map_bf16(&ta, x, T, H, PF_BM)) != VB_OK) return rc;
+  if ((rc = make_map_bf16(&tb, W(L.wr), L.NRP, H, PF_BN)) != VB_OK) return rc;
+  PfGemmParams p{};
+  p.mode = PF_ROUTER;
+  p.K = H;
+  p.nt = L.NRP / PF_BN;
+  p.shared_e = -1;
+  p.n_valid = E;
+  p.mtiles = (const int32_t *)W(L.mtiles);
+  p.n_mtiles = (const int32_t *)W(L.n_mtiles);
+  p.out = (uint16_t *)W(L.logits);
+  p.out_ld = L.NRP;
+  p.bias = bias;
+  p.status = status;
+  if ((rc = launch_gemm<PF_ROUTER>(ta, tb, tb, tb, tb, tb, p, nm * p.nt, s)) != VB_OK) return rc;
+  const int per = E <= 256 ? 8 : (E <= 512 ? 16 : 32);
+  auto kfn = per == 8 ? pf_topk_kernel<8> : per == 16 ? pf_topk_kernel<16> : pf_topk_kernel<32>;
+  kfn<<<(T + 7) / 8, 256, 0, s>>>((const uint16_t *)W(L.logits), L.NRP, T, E, k, norm_topk,
+                                  wsg ? 1 : 0, table, cap, inds, scores, counts, sgate, out_inds,
+                                  out_scores, out_logits, status);
+  return check_launch("pf_topk_kernel");
+}
+
+// Expert phase: rows x [R, H], n routes (row, expert 0..E with E = shared,
+// score). Output: expert-sorted weighted rows in L.ys and pos_of (route ->
+// row of L.ys, -1 = skipped).
+static int run_experts(const uint16_t *x, int R, const int32_t *r_row, const int32_t *r_exp,
+                       const float *r_score, int n, int H, int I, int E, int gshift,
+                       const int32_t *table, const VbQuantPool &pool, const VbQuantPool &shared,
+                       bool has_shared, int32_t *status, uint8_t *ws, const ExpertsLayout &L,
+                       cudaStream_t s, bool counts_ready) {
+  (void)R;
+  auto W = [&](size_t off) { return ws + off; };
+  int rc;
+  if (!counts_ready) {
+    if (cudaMemsetAsync(W(L.counts), 0, (size_t)(E + 2) * 4, s) != cudaSuccess)
+      return set_error(VB_ERR_CUDA, "experts: memset");
+    pf_hist_kernel<<<std::max(1, std::min(1024, (n + 255) / 256)), 256, 0, s>>>(
+        r_exp, n, E, (int32_t *)W(L.counts));
+    if ((rc = check_launch("pf_hist_kernel")) != VB_OK) return rc;
+  }
+  pf_plan_kernel<<<1, PF_PLAN_THREADS, 0, s>>>(
+      (int32_t *)W(L.counts), table, E, pool.cap, has_shared ? 1 : 0, (int32_t *)W(L.offsets),
+      (int32_t *)W(L.slot_of), (int32_t *)W(L.heavy_of), (int32_t *)W(L.heavy_e),
+      (int32_t *)W(L.n_heavy), (int32_t *)W(L.cursor), (int32_t *)W(L.mtiles),
+      (int32_t *)W(L.n_mtiles));
+  if ((rc = check_launch("pf_plan_kernel")) != VB_OK) return rc;
+  pf_predequant_kernel<<<dim3(384, PF_HEAVY_MAX), 256, 0, s>>>(
+      pool, shared, has_shared ? E : -1, (const int32_t *)W(L.heavy_e),
+      (const int32_t *)W(L.n_heavy), (const int32_t *)W(L.slot_of), H, I, gshift,
+      (uint16_t *)W(L.wgu), (uint16_t *)W(L.wd));
+  if ((rc = check_launch("pf_predequant_kernel")) != VB_OK) return rc;
+  if (n > 0) {
+    pf_gather_kernel<<<(n + 7) / 8, 256, 0, s>>>(
+        x, H, n, r_row, r_exp, r_score, (const int32_t *)W(L.slot_of),
+        (const int32_t *)W(L.offsets), (int32_t *)W(L.cursor), (uint16_t *)W(L.xs),
+        (float *)W(L.row_score), (int32_t *)W(L.pos_of));
+    if ((rc = check_launch("pf_gather_kernel")) != VB_OK) return rc;
+  }
+  // gate/up
+  {
+    CUtensorMap ta, g, u, sg, su, hv;
+    if ((rc = make_map_bf16(&ta, W(L.xs), L.rows_alloc, H, PF_BM)) != VB_OK) return rc;
+    if ((rc = make_map_codes(&g, pool.ptr[0], pool.cap, pool.slot_stride[0], I, H, 128)) != VB_OK) return rc;
+    if ((rc = make_map_codes(&u, pool.ptr[3], pool.cap, pool.slot_stride[3], I, H, 128)) != VB_OK) return rc;
+    if (has_shared) {
+      if ((rc = make_map_codes(&sg, shared.ptr[0], 1, (uint64_t)I * H / 2, I, H, 128)) != VB_OK) return rc;
+      if ((rc = make_map_codes(&su, shared.ptr[3], 1, (uint64_t)I * H / 2, I, H, 128)) != VB_OK) return rc;
+    } else {
+      sg = g;
+      su = u;
+    }
+    if ((rc = make_map_bf16_3d(&hv, W(L.wgu), PF_HEAVY_MAX, 2 * (uint64_t)I, H, PF_BN)) != VB_OK) return rc;
+    PfGemmParams p{};
+    p.mode = PF_GATEUP;
+    p.heavy_of = (const int32_t *)W(L.heavy_of);
+    p.K = H;
+    p.nt = I / 128;
+    p.gshift = gshift;
+    p.shared_e = has_shared ? E : -1;
+    p.mtiles = (const int32_t *)W(L.mtiles);
+    p.n_mtiles = (const int32_t *)W(L.n_mtiles);
+    p.slot_of = (const int32_t *)W(L.slot_of);
+    p.pool = pool;
+    p.shared = shared;
+    p.out = (uint16_t *)W(L.hs);
+    p.out_ld = I;
+    p.status = status;
+    if ((rc = launch_gemm<PF_GATEUP>(ta, g, u, sg, su, hv, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
+  }
+  // down
+  {
+    CUtensorMap ta, d, sd, hv;
+    if ((rc = make_map_bf16(&ta, W(L.hs), L.rows_alloc, I, PF_BM)) != VB_OK) return rc;
+    if ((rc = make_map_codes(&d, pool.ptr[6], pool.cap, pool.slot_stride[6], H, I, PF_BN)) != VB_OK) return rc;
+    if (has_shared) {
+      if ((rc = make_map_codes(&sd, shared.ptr[6], 1, (uint64_t)H * I / 2, H, I, PF_BN)) != VB_OK) return rc;
+    } else {
+      sd = d;
+    }
+    if ((rc = make_map_bf16_3d(&hv, W(L.wd), PF_HEAVY_MAX, H, I, PF_BN)) != VB_OK) return rc;
+    PfGemmParams p{};
+    p.mode = PF_DOWN;
+    p.heavy_of = (const int32_t *)W(L.heavy_of);
+    p.K = I;
+    p.nt = H / PF_BN;
+    p.gshift = gshift;
+    p.shared_e = has_shared ? E : -1;
+    p.mtiles = (const int32_t *)W(L.mtiles);
+    p.n_mtiles = (const int32_t *)W(L.n_mtiles);
+    p.slot_of = (const int32_t *)W(L.slot_of);
+    p.pool = pool;
+    p.shared = shared;
+    p.out = (uint16_t *)W(L.ys);
+    p.out_ld = H;
+    p.row_score = (const float *)W(L.row_score);
+    p.status = status;
+    if ((rc = launch_gemm<PF_DOWN>(ta, d, d, sd, sd, hv, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
+  }
+  return VB_OK;
+}
+
+static int check_pool(const VbQuantPool &pool, const VbQuantPool &shared, bool has_shared,
+                      const char *what) {
+  VB_REQUIRE(pool.ptr[0] && pool.cap > 0, "%s: empty pool", what);
+  for (int i = 0; i < 9; ++i)
+    VB_REQUIRE(((uintptr_t)pool.ptr[i] % 16) == 0 && (pool.slot_stride[i] % 16) == 0 &&
+                   (!has_shared || ((uintptr_t)shared.ptr[i] % 16) == 0),
+               "%s: pool tensors must be 16-byte aligned", what);
+  return VB_OK;
+}
+
 }  // namespace vb
 
 using namespace vb;
@@ -952,157 +1326,177 @@ int vb_moe_prefill(const VbMoePrefillArgs *a, vb_stream_t stream) {
   VB_REQUIRE(I % 128 == 0 && I >= 128 && I <= 4096, "vb_moe_prefill: inter=%d", I);
   VB_REQUIRE(E >= k && E < PF_PLAN_THREADS && k >= 1 && k <= 16, "vb_moe_prefill: experts/top_k");
   VB_REQUIRE(a->x && a->router_w && a->slot_table && a->out, "vb_moe_prefill: null tensor");
-  VB_REQUIRE(a->pool.ptr[0] && a->pool.cap > 0, "vb_moe_prefill: empty pool");
   const bool has_shared = a->shared.ptr[0] != nullptr;
   VB_REQUIRE(!has_shared || a->shared_gate_w, "vb_moe_prefill: shared expert without gate");
+  int rc;
+  if ((rc = check_pool(a->pool, a->shared, has_shared, "vb_moe_prefill")) != VB_OK) return rc;
   const PrefillLayout L = prefill_layout(T, H, I, E, k);
   VB_REQUIRE(a->workspace && a->workspace_bytes >= L.total, "vb_moe_prefill: workspace %zu < %zu",
              a->workspace_bytes, L.total);
   VB_REQUIRE(((uintptr_t)a->workspace % 1024) == 0, "vb_moe_prefill: workspace alignment");
   VB_REQUIRE(((uintptr_t)a->x % 16) == 0 && ((uintptr_t)a->out % 16) == 0,
              "vb_moe_prefill: x/out must be 16-byte aligned");
-  for (int i = 0; i < 9; ++i)
-    VB_REQUIRE(((uintptr_t)a->pool.ptr[i] % 16) == 0 && (a->pool.slot_stride[i] % 16) == 0 &&
-                   (!has_shared || ((uintptr_t)a->shared.ptr[i] % 16) == 0),
-               "vb_moe_prefill: pool tensors must be 16-byte aligned");
   uint8_t *ws = static_cast<uint8_t *>(a->workspace);
   auto W = [&](size_t off) { return ws + off; };
   cudaStream_t s = as_stream(stream);
   const int gshift = a->group == 128 ? 1 : 0;
-  int rc;
-
-  // P0 + P1: router rows and router GEMM over x (natural column order).
-  pf_router_rows_kernel<<<256, 256, 0, s>>>(a->router_w, has_shared ? a->shared_gate_w : nullptr,
-                                            E, H, L.NRP, (uint16_t *)W(L.wr));
-  if ((rc = check_launch("pf_router_rows_kernel")) != VB_OK) return rc;
-  cudaMemsetAsync(W(L.counts), 0, (size_t)(E + 2) * 4, s);
-  // Router tiles: all tokens as one "expert" (id 0).
-  {
-    const int nm = (T + PF_BM - 1) / PF_BM;
-    VB_REQUIRE(nm <= L.max_mtiles, "vb_moe_prefill: router tiles");
-    pf_row_tiles_kernel<<<(nm + 255) / 256, 256, 0, s>>>(T, (int32_t *)W(L.mtiles),
-                                                         (int32_t *)W(L.n_mtiles));
-    if ((rc = check_launch("pf_row_tiles_kernel")) != VB_OK) return rc;
-    CUtensorMap ta, tb;
-    if ((rc = make_map_bf16(&ta, a->x, T, H, PF_BM)) != VB_OK) return rc;
-    if ((rc = make_map_bf16(&tb, W(L.wr), L.NRP, H, PF_BN)) != VB_OK) return rc;
-    PfGemmParams p{};
-    p.mode = PF_ROUTER;
-    p.K = H;
-    p.nt = L.NRP / PF_BN;
-    p.shared_e = -1;
-    p.n_valid = E;
-    p.mtiles = (const int32_t *)W(L.mtiles);
-    p.n_mtiles = (const int32_t *)W(L.n_mtiles);
-    p.out = (uint16_t *)W(L.logits);
-    p.out_ld = L.NRP;
-    p.bias = a->router_bias;
-    p.status = a->status;
-    if ((rc = launch_gemm<PF_ROUTER>(ta, tb, tb, tb, tb, tb, p, nm * p.nt, s)) != VB_OK) return rc;
-  }
-  // P2
-  {
-    const int per = E <= 256 ? 8 : (E <= 512 ? 16 : 32);
-    auto kfn = per == 8 ? pf_topk_kernel<8> : per == 16 ? pf_topk_kernel<16> : pf_topk_kernel<32>;
-    kfn<<<(T + 7) / 8, 256, 0, s>>>((const uint16_t *)W(L.logits), L.NRP, T, E, k, a->norm_topk,
-                                    has_shared ? 1 : 0, a->slot_table, a->pool.cap,
-                                    (int32_t *)W(L.inds), (float *)W(L.scores),
-                                    (int32_t *)W(L.counts), (float *)W(L.sgate), a->out_inds,
-                                    a->out_scores, a->out_logits, a->status);
-    if ((rc = check_launch("pf_topk_kernel")) != VB_OK) return rc;
-  }
-  // P3
-  pf_plan_kernel<<<1, PF_PLAN_THREADS, 0, s>>>(
-      (int32_t *)W(L.counts), a->slot_table, E, a->pool.cap, T, has_shared ? 1 : 0,
-      a->layer_cap > 0 ? a->layer_cap : E, a->max_assignments > 0 ? a->max_assignments : 32768,
-      (int32_t *)W(L.offsets), (int32_t *)W(L.group_of), (int32_t *)W(L.slot_of),
-      (int32_t *)W(L.heavy_of), (int32_t *)W(L.heavy_e), (int32_t *)W(L.n_heavy),
-      (int32_t *)W(L.cursor), (int32_t *)W(L.mtiles), (int32_t *)W(L.n_mtiles));
-  if ((rc = check_launch("pf_plan_kernel")) != VB_OK) return rc;
-  pf_predequant_kernel<<<dim3(384, PF_HEAVY_MAX), 256, 0, s>>>(
-      a->pool, a->shared, has_shared ? E : -1, (const int32_t *)W(L.heavy_e),
-      (const int32_t *)W(L.n_heavy), (const int32_t *)W(L.slot_of), H, I, gshift,
-      (uint16_t *)W(L.wgu), (uint16_t *)W(L.wd));
-  if ((rc = check_launch("pf_predequant_kernel")) != VB_OK) return rc;
-  // P4
-  {
-    const int warps = T * k + (has_shared ? T : 0);
-    pf_gather_kernel<<<(warps + 7) / 8, 256, 0, s>>>(
-        a->x, T, H, k, E, has_shared ? 1 : 0, (const int32_t *)W(L.inds),
-        (const float *)W(L.scores), (const int32_t *)W(L.slot_of), (const int32_t *)W(L.offsets),
-        (int32_t *)W(L.cursor), (uint16_t *)W(L.xs), (float *)W(L.row_score),
-        (int32_t *)W(L.pos_of));
-    if ((rc = check_launch("pf_gather_kernel")) != VB_OK) return rc;
-  }
-  const int rows_alloc = L.rows + PF_BM;
-  // P5 gate/up
-  {
-    CUtensorMap ta, g, u, sg, su;
-    if ((rc = make_map_bf16(&ta, W(L.xs), rows_alloc, H, PF_BM)) != VB_OK) return rc;
-    if ((rc = make_map_codes(&g, a->pool.ptr[0], a->pool.cap, a->pool.slot_stride[0], I, H, 128)) != VB_OK) return rc;
-    if ((rc = make_map_codes(&u, a->pool.ptr[3], a->pool.cap, a->pool.slot_stride[3], I, H, 128)) != VB_OK) return rc;
-    if (has_shared) {
-      if ((rc = make_map_codes(&sg, a->shared.ptr[0], 1, (uint64_t)I * H / 2, I, H, 128)) != VB_OK) return rc;
-      if ((rc = make_map_codes(&su, a->shared.ptr[3], 1, (uint64_t)I * H / 2, I, H, 128)) != VB_OK) return rc;
-    } else {
-      sg = g;
-      su = u;
-    }
-    CUtensorMap hv;
-    if ((rc = make_map_bf16_3d(&hv, W(L.wgu), PF_HEAVY_MAX, 2 * (uint64_t)I, H, PF_BN)) != VB_OK) return rc;
-    PfGemmParams p{};
-    p.mode = PF_GATEUP;
-    p.heavy_of = (const int32_t *)W(L.heavy_of);
-    p.K = H;
-    p.nt = I / 128;
-    p.gshift = gshift;
-    p.shared_e = has_shared ? E : -1;
-    p.mtiles = (const int32_t *)W(L.mtiles);
-    p.n_mtiles = (const int32_t *)W(L.n_mtiles);
-    p.slot_of = (const int32_t *)W(L.slot_of);
-    p.pool = a->pool;
-    p.shared = a->shared;
-    p.out = (uint16_t *)W(L.hs);
-    p.out_ld = I;
-    p.status = a->status;
-    if ((rc = launch_gemm<PF_GATEUP>(ta, g, u, sg, su, hv, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
-  }
-  // P6 down
-  {
-    CUtensorMap ta, d, sd;
-    if ((rc = make_map_bf16(&ta, W(L.hs), rows_alloc, I, PF_BM)) != VB_OK) return rc;
-    if ((rc = make_map_codes(&d, a->pool.ptr[6], a->pool.cap, a->pool.slot_stride[6], H, I, PF_BN)) != VB_OK) return rc;
-    if (has_shared) {
-      if ((rc = make_map_codes(&sd, a->shared.ptr[6], 1, (uint64_t)H * I / 2, H, I, PF_BN)) != VB_OK) return rc;
-    } else {
-      sd = d;
-    }
-    CUtensorMap hv;
-    if ((rc = make_map_bf16_3d(&hv, W(L.wd), PF_HEAVY_MAX, H, I, PF_BN)) != VB_OK) return rc;
-    PfGemmParams p{};
-    p.mode = PF_DOWN;
-    p.heavy_of = (const int32_t *)W(L.heavy_of);
-    p.K = I;
-    p.nt = H / PF_BN;
-    p.gshift = gshift;
-    p.shared_e = has_shared ? E : -1;
-    p.mtiles = (const int32_t *)W(L.mtiles);
-    p.n_mtiles = (const int32_t *)W(L.n_mtiles);
-    p.slot_of = (const int32_t *)W(L.slot_of);
-    p.pool = a->pool;
-    p.shared = a->shared;
-    p.out = (uint16_t *)W(L.ys);
-    p.out_ld = H;
-    p.row_score = (const float *)W(L.row_score);
-    p.status = a->status;
-    if ((rc = launch_gemm<PF_DOWN>(ta, d, d, sd, sd, hv, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
-  }
-  // P7
-  pf_combine_kernel<<<(T + 7) / 8, 256, 0, s>>>(
-      (const uint16_t *)W(L.ys), T, H, k, E, has_shared ? 1 : 0, (const int32_t *)W(L.inds),
-      (const int32_t *)W(L.group_of), (const int32_t *)W(L.pos_of), (const int32_t *)W(L.offsets),
-      (const float *)W(L.sgate), a->out);
+  int32_t *inds = (int32_t *)W(L.inds), *counts = (int32_t *)W(L.counts);
+  float *scores = (float *)W(L.scores), *sgate = (float *)W(L.sgate);
+  if ((rc = run_route(a->x, T, H, E, k, a->norm_topk, a->router_w, a->router_bias,
+                      has_shared ? a->shared_gate_w : nullptr, a->slot_table, a->pool.cap, inds,
+                      scores, sgate, counts, a->out_inds, a->out_scores, a->out_logits, a->status,
+                      W(L.route), s)) != VB_OK)
+    return rc;
+  // The reference's reduce groups from the routed counts (all experts).
+  pf_groups_kernel<<<1, PF_PLAN_THREADS, 0, s>>>(
+      counts, E, a->layer_cap > 0 ? a->layer_cap : E,
+      a->max_assignments > 0 ? a->max_assignments : 32768, (int32_t *)W(L.group_of));
+  if ((rc = check_launch("pf_groups_kernel")) != VB_OK) return rc;
+  const int n = T * k + (has_shared ? T : 0);
+  int32_t *r_row = (int32_t *)W(L.r_row), *r_exp = (int32_t *)W(L.r_exp);
+  float *r_score = (float *)W(L.r_score);
+  pf_routes_kernel<<<(n + 255) / 256, 256, 0, s>>>(T, k, E, has_shared ? 1 : 0, inds, scores, r_row,
+                                                   r_exp, r_score);
+  if ((rc = check_launch("pf_routes_kernel")) != VB_OK) return rc;
+  const ExpertsLayout &X = L.X;
+  uint8_t *xw = W(L.experts);
+  // expert counts: routed from the top-k histogram, shared = T
+  if (cudaMemcpyAsync(xw + X.counts, counts, (size_t)E * 4, cudaMemcpyDeviceToDevice, s) !=
+      cudaSuccess)
+    return set_error(VB_ERR_CUDA, "prefill: counts copy");
+  pf_set_kernel<<<1, 1, 0, s>>>((int32_t *)(xw + X.counts) + E, has_shared ? T : 0);
+  if ((rc = check_launch("pf_set_kernel")) != VB_OK) return rc;
+  if ((rc = run_experts(a->x, T, r_row, r_exp, r_score, n, H, I, E, gshift, a->slot_table,
+                        a->pool, a->shared, has_shared, a->status, xw, X, s, true)) != VB_OK)
+    return rc;
+  const int32_t *pos_of = (const int32_t *)(xw + X.pos_of);
+  const uint16_t *ys = (const uint16_t *)(xw + X.ys);
+  pf_combine_kernel<<<(T + 7) / 8, 256, 0, s>>>(ys, T, H, k, inds, (const int32_t *)W(L.group_of),
+                                                pos_of, has_shared ? ys : nullptr,
+                                                has_shared ? pos_of + (size_t)T * k : nullptr, sgate,
+                                                a->out);
   return check_launch("pf_combine_kernel");
+}
+
+size_t vb_moe_route_workspace_size(int32_t tokens, int32_t hidden, int32_t num_experts) {
+  if (tokens <= 0 || hidden <= 0 || num_experts <= 0) return 0;
+  return route_layout(tokens, hidden, num_experts).total;
+}
+
+int vb_moe_route(const VbMoeRouteArgs *a, vb_stream_t stream) {
+  VB_REQUIRE(a, "vb_moe_route: null args");
+  const int T = a->tokens, H = a->hidden, E = a->num_experts, k = a->top_k;
+  VB_REQUIRE(T >= 1 && H % 256 == 0 && H >= 256 && H <= 8192, "vb_moe_route: shape");
+  VB_REQUIRE(E >= k && E < PF_PLAN_THREADS && k >= 1 && k <= 16, "vb_moe_route: experts/top_k");
+  VB_REQUIRE(a->x && a->router_w && a->out_inds && a->out_scores && a->out_counts,
+             "vb_moe_route: null tensor");
+  VB_REQUIRE(!a->shared_gate_w || a->out_sgate, "vb_moe_route: shared gate without output");
+  const size_t need = route_layout(T, H, E).total;
+  VB_REQUIRE(a->workspace && a->workspace_bytes >= need && ((uintptr_t)a->workspace % 1024) == 0,
+             "vb_moe_route: workspace %zu < %zu (1024-byte aligned)", a->workspace_bytes, need);
+  return run_route(a->x, T, H, E, k, a->norm_topk, a->router_w, a->router_bias, a->shared_gate_w,
+                   nullptr, 0, a->out_inds, a->out_scores, a->out_sgate, a->out_counts, nullptr,
+                   nullptr, a->out_logits, a->status, static_cast<uint8_t *>(a->workspace),
+                   as_stream(stream));
+}
+
+size_t vb_moe_experts_workspace_size(int32_t routes, int32_t hidden, int32_t inter,
+                                     int32_t num_experts) {
+  if (routes < 0 || hidden <= 0 || inter <= 0 || num_experts <= 0) return 0;
+  return experts_layout(routes, hidden, inter, num_experts).total;
+}
+
+int vb_moe_experts(const VbMoeExpertsArgs *a, vb_stream_t stream) {
+  VB_REQUIRE(a, "vb_moe_experts: null args");
+  const int n = a->routes, H = a->hidden, I = a->inter, E = a->num_experts;
+  VB_REQUIRE(n >= 0 && a->rows >= 0, "vb_moe_experts: sizes");
+  VB_REQUIRE(a->bits == 4 && (a->group == 64 || a->group == 128), "vb_moe_experts: format");
+  VB_REQUIRE(H % 256 == 0 && H >= 256 && H <= 8192 && I % 128 == 0 && I >= 128 && I <= 4096,
+             "vb_moe_experts: hidden/inter");
+  VB_REQUIRE(E >= 1 && E < PF_PLAN_THREADS, "vb_moe_experts: num_experts");
+  VB_REQUIRE(n == 0 || (a->x && a->route_row && a->route_expert && a->route_score && a->out),
+             "vb_moe_experts: null tensor");
+  VB_REQUIRE(a->slot_table, "vb_moe_experts: null slot table");
+  const bool has_shared = a->shared.ptr[0] != nullptr;
+  int rc;
+  if ((rc = check_pool(a->pool, a->shared, has_shared, "vb_moe_experts")) != VB_OK) return rc;
+  const ExpertsLayout L = experts_layout(n, H, I, E);
+  VB_REQUIRE(a->workspace && a->workspace_bytes >= L.total && ((uintptr_t)a->workspace % 1024) == 0,
+             "vb_moe_experts: workspace %zu < %zu (1024-byte aligned)", a->workspace_bytes, L.total);
+  if (n == 0) return VB_OK;
+  cudaStream_t s = as_stream(stream);
+  uint8_t *ws = static_cast<uint8_t *>(a->workspace);
+  if ((rc = run_experts(a->x, a->rows, a->route_row, a->route_expert, a->route_score, n, H, I, E,
+                        a->group == 128 ? 1 : 0, a->slot_table, a->pool, a->shared, has_shared,
+                        a->status, ws, L, s, false)) != VB_OK)
+    return rc;
+  pf_unsort_kernel<<<(n + 7) / 8, 256, 0, s>>>((const uint16_t *)(ws + L.ys), H, n,
+                                               (const int32_t *)(ws + L.pos_of), a->out);
+  return check_launch("pf_unsort_kernel");
+}
+
+int vb_moe_combine(const VbMoeCombineArgs *a, vb_stream_t stream) {
+  VB_REQUIRE(a, "vb_moe_combine: null args");
+  const int T = a->tokens, H = a->hidden, E = a->num_experts, k = a->top_k;
+  VB_REQUIRE(T >= 1 && H % 256 == 0 && E >= k && E < PF_PLAN_THREADS && k >= 1 && k <= 16,
+             "vb_moe_combine: shape");
+  VB_REQUIRE(a->inds && a->counts && a->y_routes && a->route_row && a->out && a->group_of_ws,
+             "vb_moe_combine: null tensor");
+  VB_REQUIRE(!a->y_shared || a->sgate, "vb_moe_combine: shared rows without gate");
+  cudaStream_t s = as_stream(stream);
+  pf_groups_kernel<<<1, PF_PLAN_THREADS, 0, s>>>(a->counts, E, a->layer_cap > 0 ? a->layer_cap : E,
+                                                 a->max_assignments > 0 ? a->max_assignments : 32768,
+                                                 a->group_of_ws);
+  int rc;
+  if ((rc = check_launch("pf_groups_kernel")) != VB_OK) return rc;
+  pf_combine_kernel<<<(T + 7) / 8, 256, 0, s>>>(a->y_routes, T, H, k, a->inds, a->group_of_ws,
+                                                a->route_row, a->y_shared, a->shared_row, a->sgate,
+                                                a->out);
+  return check_launch("pf_combine_kernel");
+}
+
+size_t vb_ep_pack_workspace_size(int32_t tokens, int32_t world) {
+  if (tokens <= 0 || world <= 0) return 0;
+  return align_up((size_t)tokens * world * 4, 256) * 3;
+}
+
+int vb_ep_pack(const VbEpPackArgs *a, vb_stream_t stream) {
+  VB_REQUIRE(a, "vb_ep_pack: null args");
+  const int T = a->tokens, k = a->top_k, H = a->hidden, N = a->world;
+  VB_REQUIRE(T >= 1 && k >= 1 && k <= 32 && H % 8 == 0 && N >= 1 && N <= EP_MAX_WORLD,
+             "vb_ep_pack: shape");
+  VB_REQUIRE(a->x && a->inds && a->scores && a->owner && a->send_x && a->send_meta &&
+                 a->route_send_idx && a->dest_rows && a->dest_routes,
+             "vb_ep_pack: null tensor");
+  const size_t seg = align_up((size_t)T * N * 4, 256);
+  VB_REQUIRE(a->workspace && a->workspace_bytes >= 3 * seg, "vb_ep_pack: workspace");
+  uint8_t *ws = static_cast<uint8_t *>(a->workspace);
+  int32_t *tok_cnt = (int32_t *)ws, *row_idx = (int32_t *)(ws + seg),
+          *route_base = (int32_t *)(ws + 2 * seg);
+  cudaStream_t s = as_stream(stream);
+  int rc;
+  ep_count_kernel<<<(T + 255) / 256, 256, 0, s>>>(a->inds, a->owner, T, k, N, tok_cnt);
+  if ((rc = check_launch("ep_count_kernel")) != VB_OK) return rc;
+  ep_scan_kernel<<<N, 1024, 0, s>>>(tok_cnt, T, N, row_idx, route_base, a->dest_rows,
+                                    a->dest_routes);
+  if ((rc = check_launch("ep_scan_kernel")) != VB_OK) return rc;
+  ep_pack_kernel<<<(T + 7) / 8, 256, 0, s>>>(a->x, a->inds, a->scores, a->owner, T, k, H, N,
+                                             tok_cnt, row_idx, route_base, a->dest_rows,
+                                             a->dest_routes, a->send_x, a->send_meta,
+                                             a->route_send_idx);
+  return check_launch("ep_pack_kernel");
+}
+
+int vb_ep_unpack(const int32_t *recv_meta, int32_t routes, const int32_t *src_route_off,
+                 const int32_t *src_row_off, int32_t world, int32_t *route_row,
+                 int32_t *route_expert, float *route_score, vb_stream_t stream) {
+  VB_REQUIRE(routes >= 0 && world >= 1 && world <= EP_MAX_WORLD, "vb_ep_unpack: shape");
+  if (routes == 0) return VB_OK;
+  VB_REQUIRE(recv_meta && src_route_off && src_row_off && route_row && route_expert && route_score,
+             "vb_ep_unpack: null tensor");
+  ep_unpack_kernel<<<(routes + 255) / 256, 256, 0, as_stream(stream)>>>(
+      recv_meta, routes, src_route_off, src_row_off, world, route_row, route_expert, route_score);
+  return check_launch("ep_unpack_kernel");
 }
 
 }  // extern "C"
