@@ -220,6 +220,48 @@ def run_prefill_leg(steps: int = 10, warmup: int = 3, T: int = 32768):
     return res
 
 
+def run_prefill_ep_leg(world: int, rank: int, steps: int = 10, warmup: int = 3, T: int = 32768):
+    """Config 2 expert-parallel over the ranks (one per GPU): rank r owns
+    the experts that a greedy LPT placement over the expected Zipf load
+    gives it and starts with tokens [r*T/N, (r+1)*T/N); dispatch and combine
+    are NCCL all-to-all. Time = max over ranks (strong scaling, T fixed)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from vates_b200.ep import CudaEpBackend, ep_prefill, lpt_placement
+    from vates_b200.pool import QuantPool
+    from vates_b200.synth import E as NE, H as HH, I as II, input_tokens, make_layer, zipf_bias
+    _, bf16_peak, peak_kind = peaks()
+    seed = 2
+    bias = zipf_bias(seed, NE)
+    owner = lpt_placement(np.exp(bias.astype(np.float64)), world)
+    owned = [e for e in range(NE) if owner[e] == rank]
+    pool = QuantPool.empty_blob(len(owned), HH, II, 4, 64, "cuda")
+    blk = make_layer(seed, 0, pool, owned, "cuda", router_bias=torch.from_numpy(bias).cuda())
+    per = T // world
+    x = input_tokens(seed, T)[rank * per:(rank + 1) * per].contiguous()
+    be = CudaEpBackend(blk, torch.from_numpy(owner))
+    for _ in range(max(warmup, 3)):
+        ep_prefill(be, x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        ep_prefill(be, x)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    dist.barrier()
+    flops = PREFILL_FLOPS_32K * T / 32768
+    tf = flops / (ms / 1e3) / 1e12
+    return {"workload": "prefill_32k_1layer_ep", "tokens": T, "n_gpus": world,
+            "ms_per_step": ms, "tok_per_s": T / (ms / 1e3), "tflops_algorithmic": tf,
+            "tflops_per_gpu": tf / world, "frac_of_bf16_peak_per_gpu": tf / world / bf16_peak,
+            "peak_kind": peak_kind, "experts_per_gpu": len(owned),
+            "placement": "LPT over the Zipf(1.1) expected load", "scaling": "strong"}
+
+
 def run_isoquant_leg(steps: int = 20, warmup: int = 3, S: int = 131072, layers: int = 12):
     """Config 3: quantized GQA decode attention over 12 IsoQuant K4/V3 caches
     of S tokens (Hq=16, Hkv=2, D=256), one query (T=1) and an MTP verify
@@ -402,10 +444,13 @@ def run_decode(args, world, rank, local):
         "gpu_launches": 3 * L * args.steps,
         "clocks": clocks,
     }
-    if world == 1 and not args.no_extra:
-        out["prefill"] = run_prefill_leg()
-        out["isoquant"] = run_isoquant_leg()
-    if rank == 0 and not args.no_cpu:
+    if not args.no_extra:
+        if world == 1:
+            out["prefill"] = run_prefill_leg()
+            out["isoquant"] = run_isoquant_leg()
+        else:
+            out["prefill"] = run_prefill_ep_leg(world, rank)
+    if rank == 0 and world == 1 and not args.no_cpu:
         dt, det = cpu_decode_sample(args.cpu_layers)
         cpu_tok_s = T / (dt * L / args.cpu_layers)
         out["cpu_baseline"] = {"value": cpu_tok_s, "unit": "tokens/s", "cores": os.cpu_count(),
