@@ -294,13 +294,22 @@ def run_isoquant_leg(steps: int = 20, warmup: int = 3, S: int = 131072, layers: 
         for _ in range(max(warmup, 3)):
             step()
         torch.cuda.synchronize()
+        # the 12-layer step replayed as one CUDA graph (device time)
+        side = torch.cuda.Stream()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            step()
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(steps):
-            step()
+            graph.replay()
         e1.record()
         torch.cuda.synchronize()
         us = e0.elapsed_time(e1) / steps * 1e3
+        del graph
         gbs = bytes_step / (us / 1e6) / 1e9
         res[f"T{T}"] = {"us_per_step": us, "hbm_gbs_algorithmic": gbs,
                         "frac_of_hbm_peak": gbs / hbm_peak, "bytes_per_step": bytes_step}

@@ -46,6 +46,11 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t &r0, uint32_t &r1, uint32
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
 }
 
+__device__ __forceinline__ float bf_at2(const uint2 &v, int i) {
+  const uint32_t w = i < 2 ? v.x : v.y;
+  return (i & 1) ? __uint_as_float(w & 0xFFFF0000u) : __uint_as_float(w << 16);
+}
+
 __device__ __forceinline__ uint32_t v3_pair(uint32_t u, int s0) {
   // codes at bit s0 and s0+3 of u -> exact bf16 pair (c0, c1)
   const uint32_t lo = u >> s0;
@@ -307,42 +312,405 @@ __global__ void __launch_bounds__(ATT_WARPS * 32, 2) kv_attn_partial_kernel(Attn
   }
 }
 
-// One CTA (256 threads = dims) per query row: merge splits, round to bf16,
-// optional inverse V rotation (4x4 blocks of R_v^T, R rounded to bf16).
+// Merge of the split partials: grid (query row, 8 chunks of 32 dims), 256
+// threads = 32 dims x 8 split lanes. Each CTA finds the row max over the
+// splits, keeps exp(m_s - M) of every split in shared memory, sums its
+// split lanes' shares per dim and adds the 8 lanes in lane order; the result
+// is rounded to bf16, with the optional inverse V rotation (4x4 blocks of
+// R_v^T, R rounded to bf16; a 32-dim chunk holds 8 whole blocks).
+constexpr int ATT_MAX_SPLITS = 1024;
+
 __global__ void __launch_bounds__(256) kv_attn_combine_kernel(AttnParams p) {
+  __shared__ float s_red[256];
+  __shared__ float s_e[ATT_MAX_SPLITS];
+  __shared__ float s_num[8][32];
+  __shared__ float ov[32];
   const int row_id = blockIdx.x;  // ((b*Hq + hq)*L + l)
+  const int chunk = blockIdx.y;   // dims [32 chunk, 32 chunk + 32)
   const int l = row_id % p.L;
   const int bhq = row_id / p.L;
   const int b = bhq / p.Hq, hq = bhq % p.Hq;
   const int hkv = hq / p.rep, rep_i = hq % p.rep;
   const int r = rep_i * p.L + l;
   const size_t bh = (size_t)b * p.Hkv + hkv;
-  const int d = threadIdx.x;
-  float M = -INFINITY;
-  for (int s = 0; s < p.nsplit; ++s) M = fmaxf(M, p.mpart[(bh * p.nsplit + s) * 32 + r]);
-  float num = 0.f, den = 0.f;
-  for (int s = 0; s < p.nsplit; ++s) {
-    const size_t cta = bh * p.nsplit + s;
-    const float ms = p.mpart[cta * 32 + r];
-    if (ms == -INFINITY) continue;
-    const float e = expf(ms - M);
-    den = fmaf(p.lpart[cta * 32 + r], e, den);
-    num = fmaf(p.opart[(cta * 32 + r) * 256 + d], e, num);
-  }
-  float o = rbf(den > 0.f ? num / den : 0.f);
-  if (p.rv) {
-    __shared__ float ov[256];
-    ov[d] = o;
+  const int tid = threadIdx.x;
+  const int ns = p.nsplit;
+  float m = -INFINITY;
+  for (int s = tid; s < ns; s += 256) m = fmaxf(m, p.mpart[(bh * ns + s) * 32 + r]);
+  s_red[tid] = m;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (tid < o) s_red[tid] = fmaxf(s_red[tid], s_red[tid + o]);
     __syncthreads();
-    const int blk = d >> 2, i = d & 3;
-    const float *R = p.rv + (size_t)blk * 16;
-    float acc = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk)
-      acc = __fadd_rn(acc, __fmul_rn(ov[4 * blk + kk], rbf(__ldg(R + i * 4 + kk))));
-    o = rbf(acc);
   }
-  p.out[(size_t)row_id * 256 + d] = f2bf(o);
+  const float M = s_red[0];
+  __syncthreads();
+  float dn = 0.f;
+  for (int s = tid; s < ns; s += 256) {
+    const size_t cta = bh * ns + s;
+    const float ms = p.mpart[cta * 32 + r];
+    const float e = ms == -INFINITY ? 0.f : expf(ms - M);
+    s_e[s] = e;
+    dn = fmaf(p.lpart[cta * 32 + r], e, dn);
+  }
+  s_red[tid] = dn;
+  __syncthreads();
+  for (int o = 128; o > 0; o >>= 1) {
+    if (tid < o) s_red[tid] += s_red[tid + o];
+    __syncthreads();
+  }
+  const float den = s_red[0];
+  const int dl = tid & 31, sl = tid >> 5;
+  const int d = 32 * chunk + dl;
+  float num = 0.f;
+#pragma unroll 4
+  for (int s = sl; s < ns; s += 8)
+    num = fmaf(p.opart[((bh * ns + s) * 32 + r) * 256 + d], s_e[s], num);
+  s_num[sl][dl] = num;
+  __syncthreads();
+  if (tid < 32) {
+    float nm = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) nm += s_num[i][tid];
+    float o = rbf(den > 0.f ? nm / den : 0.f);
+    ov[tid] = o;
+    __syncwarp();
+    if (p.rv) {
+      const int blk = d >> 2, i = d & 3;
+      const float *R = p.rv + (size_t)blk * 16;
+      float acc = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        acc = __fadd_rn(acc, __fmul_rn(ov[(tid & ~3) + kk], rbf(__ldg(R + i * 4 + kk))));
+      o = rbf(acc);
+    }
+    p.out[(size_t)row_id * 256 + d] = f2bf(o);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Single-query-position path (rep * L <= 8 query rows per kv head, i.e. GQA
+// decode at T=1): every warp owns whole 16-key tiles. Scores are computed
+// transposed, S^T[key][row] = K * Q^T, with the 4-bit K codes as the A
+// operand (exact bf16 128+q by one LOP3 per pair) and the 8 query rows as
+// the N=8 columns; per 64-dim group the epilogue applies s*D + (b-128s)*sum(q)
+// and the group partials are added in group order, then rounded to bf16.
+// The output is accumulated transposed too, O^T[dim][row] += V^T * P^T, with
+// V unpacked to exact bf16 in shared memory (read as A by ldmatrix.trans)
+// and P (bf16, times the key's V scale of the dim group) moved from the S^T
+// accumulator layout to the B layout with movmatrix.trans. Raw K/V codes and
+// scales of the next tile are prefetched with cp.async. The 4 warps' partial
+// softmax states are merged in shared memory into the CTA's split partial.
+// ----------------------------------------------------------------------------
+constexpr int A1_WARPS = 4;
+constexpr int A1_VPITCH = 256 + 8;                       // bf16 per unpacked V row
+constexpr int A1_VBYTES = 16 * A1_VPITCH * 2;            // 8448
+constexpr int A1_RAW = 16 * 128 + 16 * 96 + 4 * 16 * 8;  // K codes, V codes, 4 scale tensors
+constexpr int A1_WARP_SMEM = A1_VBYTES + 2 * A1_RAW;     // 16640
+constexpr int A1_SMEM = A1_WARPS * A1_WARP_SMEM;
+
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ uint2 lds_u2(const uint8_t *p) {
+  return *reinterpret_cast<const uint2 *>(p);
+}
+
+// Raw tile (16 keys from key0; keys past S-1 read key S-1 and are masked
+// later) -> staging buffer: K codes [16][128 B], V codes [16][96 B], then
+// the K scale, K bias, V scale, V bias of each key [4][16][8 B].
+__device__ __forceinline__ void a1_fetch(const AttnParams &p, size_t head_row0, int key0,
+                                         uint8_t *raw, int lane) {
+#pragma unroll
+  for (int i = 0; i < 7; ++i) {
+    const int q = lane + 32 * i;  // 16-byte chunk
+    const uint8_t *src;
+    if (q < 128) {  // K codes: 8 chunks per key
+      const int key = min(key0 + (q >> 3), p.S - 1);
+      src = reinterpret_cast<const uint8_t *>(p.kc + (head_row0 + key) * 32) + (q & 7) * 16;
+    } else {  // V codes: 6 chunks per key
+      const int qq = q - 128;
+      const int key = min(key0 + qq / 6, p.S - 1);
+      src = reinterpret_cast<const uint8_t *>(p.vc + (head_row0 + key) * 24) + (qq % 6) * 16;
+    }
+    cp_async16(raw + q * 16, src);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int q = lane + 32 * i;  // (tensor, key) 8-byte piece
+    const int t = q >> 4, kk = q & 15;
+    const uint16_t *base = t == 0 ? p.ks : t == 1 ? p.kb : t == 2 ? p.vs : p.vb;
+    const int key = min(key0 + kk, p.S - 1);
+    cp_async8(raw + 3584 + q * 8, base + (head_row0 + key) * 4);
+  }
+}
+
+__global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int bh = blockIdx.x, split = blockIdx.y;
+  const int b = bh / p.Hkv, hkv = bh % p.Hkv;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int k_begin = split * p.kps;
+  const int k_end = min(p.S, k_begin + p.kps);
+  uint8_t *wsm = smem_raw + warp * A1_WARP_SMEM;
+  uint16_t *Vt = reinterpret_cast<uint16_t *>(wsm);
+  uint8_t *raw0 = wsm + A1_VBYTES;
+
+  // Q^T as B fragments (row g; zero for rows >= QR) and the per-group q sums
+  // of rows 2c, 2c+1.
+  uint32_t qb[4][4][2];
+  float qs[4][2];
+  {
+    float vals[64];
+    const int r = g;
+    float part[4] = {0.f, 0.f, 0.f, 0.f};
+    if (r < p.QR) {
+      const int rep_i = r / p.L, l = r % p.L;
+      const int hq = hkv * p.rep + rep_i;
+      const uint16_t *qp = p.q + (((size_t)b * p.Hq + hq) * p.L + l) * 256;
+#pragma unroll
+      for (int G = 0; G < 4; ++G)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float v = rbf(__fmul_rn(bf2f(qp[64 * G + 16 * c + i]), p.scale));
+          vals[16 * G + i] = v;
+          part[G] += v;
+        }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 64; ++i) vals[i] = 0.f;
+    }
+#pragma unroll
+    for (int G = 0; G < 4; ++G) {
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int d0 = 16 * G + 8 * (m >> 1) + 2 * (m & 1);
+        qb[G][m][0] = pack_bf2(vals[d0], vals[d0 + 4]);
+        qb[G][m][1] = pack_bf2(vals[d0 + 1], vals[d0 + 5]);
+      }
+      float t = part[G];
+      t += __shfl_xor_sync(0xffffffffu, t, 1);
+      t += __shfl_xor_sync(0xffffffffu, t, 2);
+      // row g's sum -> lanes needing rows 2c, 2c+1
+      qs[G][0] = __shfl_sync(0xffffffffu, t, (2 * c) * 4);
+      qs[G][1] = __shfl_sync(0xffffffffu, t, (2 * c + 1) * 4);
+    }
+  }
+
+  float O[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) O[i][0] = O[i][1] = O[i][2] = O[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  float bsum[4][2];
+#pragma unroll
+  for (int G = 0; G < 4; ++G) bsum[G][0] = bsum[G][1] = 0.f;
+
+  const size_t head_row0 = (size_t)bh * p.cap;
+  const int n_tiles = (k_end - k_begin + 15) / 16;
+  int it = 0;
+  int t_cur = warp;
+  if (t_cur < n_tiles) a1_fetch(p, head_row0, k_begin + 16 * t_cur, raw0, lane);
+  cp_async_commit();
+  for (; t_cur < n_tiles; t_cur += A1_WARPS, ++it) {
+    const int t_next = t_cur + A1_WARPS;
+    if (t_next < n_tiles)
+      a1_fetch(p, head_row0, k_begin + 16 * t_next, raw0 + ((it + 1) & 1) * A1_RAW, lane);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();
+    const uint8_t *rw = raw0 + (it & 1) * A1_RAW;
+    const uint8_t *Kr = rw, *Vr = rw + 2048, *Sk = rw + 3584, *Bk = Sk + 128, *Sv = Sk + 256,
+                  *Bv = Sk + 384;
+    const int key0 = k_begin + 16 * t_cur;
+
+    // ---- scores S^T for keys g, g+8 and rows 2c, 2c+1 ----
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint2 ksg = lds_u2(Sk + g * 8), ks8 = lds_u2(Sk + (g + 8) * 8);
+    const uint2 kbg = lds_u2(Bk + g * 8), kb8 = lds_u2(Bk + (g + 8) * 8);
+#pragma unroll
+    for (int G = 0; G < 4; ++G) {
+      const uint2 wa = lds_u2(Kr + g * 128 + G * 32 + 8 * c);
+      const uint2 wb = lds_u2(Kr + (g + 8) * 128 + G * 32 + 8 * c);
+      uint32_t pa[2][4], pb[2][4];
+      nib_pairs4(wa.x, pa[0]);
+      nib_pairs4(wa.y, pa[1]);
+      nib_pairs4(wb.x, pb[0]);
+      nib_pairs4(wb.y, pb[1]);
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int i0 = 2 * (m & 1), h = m >> 1;
+        mma_bf16(d, pa[h][i0], pb[h][i0], pa[h][i0 + 1], pb[h][i0 + 1], qb[G][m][0], qb[G][m][1]);
+      }
+      const float s_g = bf_at2(ksg, G), s_8 = bf_at2(ks8, G);
+      const float bp_g = fmaf(-128.f, s_g, bf_at2(kbg, G));
+      const float bp_8 = fmaf(-128.f, s_8, bf_at2(kb8, G));
+      sc[0] += fmaf(s_g, d[0], bp_g * qs[G][0]);
+      sc[1] += fmaf(s_g, d[1], bp_g * qs[G][1]);
+      sc[2] += fmaf(s_8, d[2], bp_8 * qs[G][0]);
+      sc[3] += fmaf(s_8, d[3], bp_8 * qs[G][1]);
+    }
+    // bf16 scores; mask keys outside [k_begin, k_end), rows >= QR and the
+    // causal bound key <= S - L + l.
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int key = key0 + g + 8 * (j >> 1);
+      const int row = 2 * c + (j & 1);
+      bool ok = row < p.QR && key < k_end;
+      if (p.causal && ok) ok = key <= p.S - p.L + (row % p.L);
+      sc[j] = ok ? rbf(sc[j]) : -INFINITY;
+    }
+    // ---- online softmax (rows 2c, 2c+1) ----
+    float mx[2] = {fmaxf(sc[0], sc[2]), fmaxf(sc[1], sc[3])};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 4));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 8));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 16));
+    }
+    float mnew[2], alpha[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mnew[h] = fmaxf(m_run[h], mx[h]);
+      alpha[h] = (m_run[h] == -INFINITY) ? 0.f : expf(m_run[h] - mnew[h]);
+      if (mnew[h] == -INFINITY) alpha[h] = 1.f;
+      m_run[h] = mnew[h];
+    }
+    if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        l_run[h] *= alpha[h];
+#pragma unroll
+        for (int G = 0; G < 4; ++G) bsum[G][h] *= alpha[h];
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        O[i][0] *= alpha[0];
+        O[i][1] *= alpha[1];
+        O[i][2] *= alpha[0];
+        O[i][3] *= alpha[1];
+      }
+    }
+    float e[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int h = j & 1;
+      e[j] = sc[j] == -INFINITY ? 0.f : expf(sc[j] - mnew[h]);
+      l_run[h] += e[j];
+    }
+    // P^T fragments per V group: p = bf16(e * vs); V bias term on the side.
+    const uint2 vsg = lds_u2(Sv + g * 8), vs8 = lds_u2(Sv + (g + 8) * 8);
+    const uint2 vbg = lds_u2(Bv + g * 8), vb8 = lds_u2(Bv + (g + 8) * 8);
+    uint32_t pB[4][2];
+#pragma unroll
+    for (int G = 0; G < 4; ++G) {
+      const float sg = bf_at2(vsg, G), s8 = bf_at2(vs8, G);
+      const float bg = bf_at2(vbg, G), b8 = bf_at2(vb8, G);
+      bsum[G][0] = fmaf(e[0], bg, fmaf(e[2], b8, bsum[G][0]));
+      bsum[G][1] = fmaf(e[1], bg, fmaf(e[3], b8, bsum[G][1]));
+      const uint32_t x0 = pack_bf2(e[0] * sg, e[1] * sg);  // key g: rows 2c, 2c+1
+      const uint32_t x1 = pack_bf2(e[2] * s8, e[3] * s8);  // key g+8
+      pB[G][0] = movmatrix_trans(x0);  // keys 2c, 2c+1 of row g
+      pB[G][1] = movmatrix_trans(x1);  // keys 8+2c, 8+2c+1
+    }
+    // ---- V codes -> exact bf16 rows of Vt ----
+    {
+      const int kk = lane >> 1, hh = lane & 1;
+      const uint32_t *vw = reinterpret_cast<const uint32_t *>(Vr + kk * 96 + hh * 48);
+      uint32_t w[13];
+#pragma unroll
+      for (int i = 0; i < 12; ++i) w[i] = vw[i];
+      w[12] = 0;
+      uint16_t *dst = Vt + kk * A1_VPITCH + 128 * hh;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int bit = 24 * j, wi = bit >> 5, sh = bit & 31;
+        const uint32_t u = __funnelshift_r(w[wi], w[wi + 1], sh) & 0xFFFFFFu;
+        uint4 o;
+        o.x = v3_pair(u, 0);
+        o.y = v3_pair(u, 6);
+        o.z = v3_pair(u, 12);
+        o.w = v3_pair(u, 18);
+        *reinterpret_cast<uint4 *>(dst + 8 * j) = o;
+      }
+    }
+    __syncwarp();
+    // ---- O^T += V^T P^T ----
+    {
+      const int q = lane >> 3, r = lane & 7;
+      const int key = (q >> 1) * 8 + r, dq = (q & 1) * 8;
+#pragma unroll
+      for (int G = 0; G < 4; ++G) {
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_trans(a0, a1, a2, a3, Vt + key * A1_VPITCH + 64 * G + 16 * mt + dq);
+          mma_bf16(O[4 * G + mt], a0, a1, a2, a3, pB[G][0], pB[G][1]);
+        }
+      }
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+
+  // ---- reduce the lane partials of l and the V bias sums (over g) ----
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], o);
+#pragma unroll
+      for (int G = 0; G < 4; ++G) bsum[G][h] += __shfl_xor_sync(0xffffffffu, bsum[G][h], o);
+    }
+  }
+  // ---- merge the 4 warps in shared memory: [warp][row 8][dim 256] + m, l ----
+  __syncthreads();
+  float *Om = reinterpret_cast<float *>(smem_raw);            // 4 x 8 x 256 floats (32 KB)
+  float *Mm = Om + A1_WARPS * 8 * 256, *Lm = Mm + A1_WARPS * 8;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int G = i >> 2, mt = i & 3;
+    const int d0 = 64 * G + 16 * mt + g;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = 2 * c + h;
+      Om[(warp * 8 + row) * 256 + d0] = O[i][h] + bsum[G][h];
+      Om[(warp * 8 + row) * 256 + d0 + 8] = O[i][2 + h] + bsum[G][h];
+    }
+  }
+  if (g == 0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      Mm[warp * 8 + 2 * c + h] = m_run[h];
+      Lm[warp * 8 + 2 * c + h] = l_run[h];
+    }
+  }
+  __syncthreads();
+  const size_t cta = (size_t)bh * p.nsplit + split;
+  for (int i = threadIdx.x; i < 8 * 256; i += blockDim.x) {
+    const int row = i >> 8, d = i & 255;
+    if (row >= p.QR) continue;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < A1_WARPS; ++w) M = fmaxf(M, Mm[w * 8 + row]);
+    float num = 0.f, den = 0.f;
+#pragma unroll
+    for (int w = 0; w < A1_WARPS; ++w) {
+      const float mw = Mm[w * 8 + row];
+      if (mw == -INFINITY) continue;
+      const float sw = expf(mw - M);
+      num = fmaf(Om[(w * 8 + row) * 256 + d], sw, num);
+      den = fmaf(Lm[w * 8 + row], sw, den);
+    }
+    p.opart[(cta * 32 + row) * 256 + d] = num;
+    if (d == 0) {
+      p.mpart[cta * 32 + row] = M;
+      p.lpart[cta * 32 + row] = den;
+    }
+  }
 }
 
 static void attn_split(int bhk, int S, int &nsplit, int &kps) {
@@ -366,7 +734,7 @@ size_t vb_kv_attn_workspace_size(int32_t batch, int32_t q_heads, int32_t L,
   if (batch <= 0 || keys <= 0) return 0;
   // Upper bound over kv_heads >= 1: splits <= 296 per (batch, kv head) and
   // at most 296 CTAs overall plus one per (batch, kv head).
-  const size_t ctas = 2 * 148 + (size_t)batch * 64;
+  const size_t ctas = 3 * 148 + (size_t)batch * 64;
   return align_up(ctas * 32 * 256 * sizeof(float), 256) + 2 * align_up(ctas * 32 * sizeof(float), 256);
 }
 
@@ -396,6 +764,7 @@ int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
   p.B = batch; p.Hq = q_heads; p.Hkv = kv_heads; p.L = L; p.S = keys; p.cap = cap;
   p.rep = rep; p.QR = rep * L; p.causal = causal; p.scale = scale;
   attn_split(batch * kv_heads, keys, p.nsplit, p.kps);
+  VB_REQUIRE(p.nsplit <= ATT_MAX_SPLITS, "vb_kv_decode_attn: %d splits", p.nsplit);
   const size_t ctas = (size_t)batch * kv_heads * p.nsplit;
   const size_t obytes = align_up(ctas * 32 * 256 * sizeof(float), 256);
   const size_t mbytes = align_up(ctas * 32 * sizeof(float), 256);
@@ -407,6 +776,33 @@ int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
   p.lpart = reinterpret_cast<float *>(ws + obytes + mbytes);
   p.out = out;
   cudaStream_t s = as_stream(stream);
+  if (p.QR <= 8) {
+    // split for the single-position kernel: 3 CTAs per SM, 64-key multiples
+    int target = (3 * 148 + batch * kv_heads - 1) / (batch * kv_heads);
+    if (target < 1) target = 1;
+    int kps = (keys + target - 1) / target;
+    kps = (kps + 63) / 64 * 64;
+    p.kps = kps;
+    p.nsplit = (keys + kps - 1) / kps;
+    VB_REQUIRE(p.nsplit <= ATT_MAX_SPLITS, "vb_kv_decode_attn: %d splits", p.nsplit);
+    const size_t ctas1 = (size_t)batch * kv_heads * p.nsplit;
+    const size_t ob1 = align_up(ctas1 * 32 * 256 * sizeof(float), 256);
+    const size_t mb1 = align_up(ctas1 * 32 * sizeof(float), 256);
+    VB_REQUIRE(workspace_bytes >= ob1 + 2 * mb1, "vb_kv_decode_attn: workspace %zu < %zu",
+               workspace_bytes, ob1 + 2 * mb1);
+    p.mpart = reinterpret_cast<float *>(ws + ob1);
+    p.lpart = reinterpret_cast<float *>(ws + ob1 + mb1);
+    static bool attr_done = false;
+    if (!attr_done) {
+      cudaFuncSetAttribute(kv_attn1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, A1_SMEM);
+      attr_done = true;
+    }
+    kv_attn1_kernel<<<dim3(batch * kv_heads, p.nsplit), A1_WARPS * 32, A1_SMEM, s>>>(p);
+    int rc1 = check_launch("kv_attn1_kernel");
+    if (rc1) return rc1;
+    kv_attn_combine_kernel<<<dim3(batch * q_heads * L, 8), 256, 0, s>>>(p);
+    return check_launch("kv_attn_combine_kernel");
+  }
   const int MT = p.QR > 16 ? 2 : 1;
   const size_t smem = (size_t)2 * ATT_WARPS * 16 * MT * ATT_SX_STRIDE * sizeof(float) +
                       (size_t)ATT_WARPS * ATT_ROUND * ATT_VS_STRIDE * sizeof(uint16_t) +
@@ -421,7 +817,7 @@ int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
   }
   int rc = check_launch("kv_attn_partial_kernel");
   if (rc) return rc;
-  kv_attn_combine_kernel<<<batch * q_heads * L, 256, 0, s>>>(p);
+  kv_attn_combine_kernel<<<dim3(batch * q_heads * L, 8), 256, 0, s>>>(p);
   return check_launch("kv_attn_combine_kernel");
 }
 
