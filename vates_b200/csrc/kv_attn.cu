@@ -409,6 +409,12 @@ constexpr int A1_RAW = 16 * 128 + 16 * 96 + 4 * 16 * 8;  // K codes, V codes, 4 
 constexpr int A1_WARP_SMEM = A1_VBYTES + 2 * A1_RAW;     // 16640
 constexpr int A1_SMEM = A1_WARPS * A1_WARP_SMEM;
 
+// Codes at bits s0 and s0+3 of u (3-bit) -> bf16 pair (128 + c0, 128 + c1).
+__device__ __forceinline__ uint32_t v3_pair128(uint32_t u, int s0) {
+  const uint32_t a = u >> s0;
+  return lop_and_or(a << 13, 0x00070000u, lop_and_or(a, 0x7u, 0x43004300u));
+}
+
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   uint32_t y;
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
@@ -420,30 +426,30 @@ __device__ __forceinline__ uint2 lds_u2(const uint8_t *p) {
 
 // Raw tile (16 keys from key0; keys past S-1 read key S-1 and are masked
 // later) -> staging buffer: K codes [16][128 B], V codes [16][96 B], then
-// the K scale, K bias, V scale, V bias of each key [4][16][8 B].
-__device__ __forceinline__ void a1_fetch(const AttnParams &p, size_t head_row0, int key0,
+// the K scale, K bias, V scale, V bias of each key [4][16][8 B]. A lane's
+// chunks are fixed: keys key0 + kq[i] at byte offsets that do not change
+// from tile to tile.
+__device__ __forceinline__ void a1_fetch(const uint8_t *kbase, const uint8_t *vbase,
+                                         const uint8_t *s0, const uint8_t *s1, int S, int key0,
                                          uint8_t *raw, int lane) {
+  // K codes: piece lane + 32 i, i < 4 -> key (lane >> 3) + 4 i, offset (lane & 7) * 16
 #pragma unroll
-  for (int i = 0; i < 7; ++i) {
-    const int q = lane + 32 * i;  // 16-byte chunk
-    const uint8_t *src;
-    if (q < 128) {  // K codes: 8 chunks per key
-      const int key = min(key0 + (q >> 3), p.S - 1);
-      src = reinterpret_cast<const uint8_t *>(p.kc + (head_row0 + key) * 32) + (q & 7) * 16;
-    } else {  // V codes: 6 chunks per key
-      const int qq = q - 128;
-      const int key = min(key0 + qq / 6, p.S - 1);
-      src = reinterpret_cast<const uint8_t *>(p.vc + (head_row0 + key) * 24) + (qq % 6) * 16;
-    }
-    cp_async16(raw + q * 16, src);
+  for (int i = 0; i < 4; ++i) {
+    const int key = min(key0 + (lane >> 3) + 4 * i, S - 1);
+    cp_async16(raw + (lane + 32 * i) * 16, kbase + (size_t)key * 128 + (lane & 7) * 16);
   }
+  // V codes: pieces 128 + lane + 32 i -> key qq / 6, offset (qq % 6) * 16
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const int qq = lane + 32 * i;
+    const int key = min(key0 + qq / 6, S - 1);
+    cp_async16(raw + 2048 + qq * 16, vbase + (size_t)key * 96 + (qq % 6) * 16);
+  }
+  // scales: piece lane + 32 i -> tensor (lane >> 4) + 2 i, key lane & 15
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
-    const int q = lane + 32 * i;  // (tensor, key) 8-byte piece
-    const int t = q >> 4, kk = q & 15;
-    const uint16_t *base = t == 0 ? p.ks : t == 1 ? p.kb : t == 2 ? p.vs : p.vb;
-    const int key = min(key0 + kk, p.S - 1);
-    cp_async8(raw + 3584 + q * 8, base + (head_row0 + key) * 4);
+    const int key = min(key0 + (lane & 15), S - 1);
+    cp_async8(raw + 3584 + (lane + 32 * i) * 8, (i ? s1 : s0) + (size_t)key * 8);
   }
 }
 
@@ -504,20 +510,27 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
 #pragma unroll
   for (int i = 0; i < 16; ++i) O[i][0] = O[i][1] = O[i][2] = O[i][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-  float bsum[4][2];
+  float bsum[4][2], psum[4][2];
 #pragma unroll
-  for (int G = 0; G < 4; ++G) bsum[G][0] = bsum[G][1] = 0.f;
+  for (int G = 0; G < 4; ++G) bsum[G][0] = bsum[G][1] = psum[G][0] = psum[G][1] = 0.f;
 
   const size_t head_row0 = (size_t)bh * p.cap;
   const int n_tiles = (k_end - k_begin + 15) / 16;
+  const uint8_t *kbase = reinterpret_cast<const uint8_t *>(p.kc + head_row0 * 32);
+  const uint8_t *vbase = reinterpret_cast<const uint8_t *>(p.vc + head_row0 * 24);
+  // scale tensors of this lane's two pieces: (lane >> 4) and (lane >> 4) + 2
+  const uint16_t *sc_t[4] = {p.ks, p.kb, p.vs, p.vb};
+  const uint8_t *sb0 = reinterpret_cast<const uint8_t *>(((lane >> 4) ? sc_t[1] : sc_t[0]) + head_row0 * 4);
+  const uint8_t *sb1 = reinterpret_cast<const uint8_t *>(((lane >> 4) ? sc_t[3] : sc_t[2]) + head_row0 * 4);
   int it = 0;
   int t_cur = warp;
-  if (t_cur < n_tiles) a1_fetch(p, head_row0, k_begin + 16 * t_cur, raw0, lane);
+  if (t_cur < n_tiles) a1_fetch(kbase, vbase, sb0, sb1, p.S, k_begin + 16 * t_cur, raw0, lane);
   cp_async_commit();
   for (; t_cur < n_tiles; t_cur += A1_WARPS, ++it) {
     const int t_next = t_cur + A1_WARPS;
     if (t_next < n_tiles)
-      a1_fetch(p, head_row0, k_begin + 16 * t_next, raw0 + ((it + 1) & 1) * A1_RAW, lane);
+      a1_fetch(kbase, vbase, sb0, sb1, p.S, k_begin + 16 * t_next,
+               raw0 + ((it + 1) & 1) * A1_RAW, lane);
     cp_async_commit();
     cp_async_wait<1>();
     __syncwarp();
@@ -584,7 +597,10 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
       for (int h = 0; h < 2; ++h) {
         l_run[h] *= alpha[h];
 #pragma unroll
-        for (int G = 0; G < 4; ++G) bsum[G][h] *= alpha[h];
+        for (int G = 0; G < 4; ++G) {
+          bsum[G][h] *= alpha[h];
+          psum[G][h] *= alpha[h];
+        }
       }
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -613,6 +629,8 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
       bsum[G][1] = fmaf(e[1], bg, fmaf(e[3], b8, bsum[G][1]));
       const uint32_t x0 = pack_bf2(e[0] * sg, e[1] * sg);  // key g: rows 2c, 2c+1
       const uint32_t x1 = pack_bf2(e[2] * s8, e[3] * s8);  // key g+8
+      psum[G][0] += __uint_as_float(x0 << 16) + __uint_as_float(x1 << 16);
+      psum[G][1] += __uint_as_float(x0 & 0xFFFF0000u) + __uint_as_float(x1 & 0xFFFF0000u);
       pB[G][0] = movmatrix_trans(x0);  // keys 2c, 2c+1 of row g
       pB[G][1] = movmatrix_trans(x1);  // keys 8+2c, 8+2c+1
     }
@@ -630,15 +648,15 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
         const int bit = 24 * j, wi = bit >> 5, sh = bit & 31;
         const uint32_t u = __funnelshift_r(w[wi], w[wi + 1], sh) & 0xFFFFFFu;
         uint4 o;
-        o.x = v3_pair(u, 0);
-        o.y = v3_pair(u, 6);
-        o.z = v3_pair(u, 12);
-        o.w = v3_pair(u, 18);
+        o.x = v3_pair128(u, 0);
+        o.y = v3_pair128(u, 6);
+        o.z = v3_pair128(u, 12);
+        o.w = v3_pair128(u, 18);
         *reinterpret_cast<uint4 *>(dst + 8 * j) = o;
       }
     }
     __syncwarp();
-    // ---- O^T += V^T P^T ----
+    // ---- O^T += V^T P^T (V as 128 + c; 128 * sum(p) removed at the end) ----
     {
       const int q = lane >> 3, r = lane & 7;
       const int key = (q >> 1) * 8 + r, dq = (q & 1) * 8;
@@ -663,7 +681,10 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
     for (int o = 4; o < 32; o <<= 1) {
       l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], o);
 #pragma unroll
-      for (int G = 0; G < 4; ++G) bsum[G][h] += __shfl_xor_sync(0xffffffffu, bsum[G][h], o);
+      for (int G = 0; G < 4; ++G) {
+        bsum[G][h] += __shfl_xor_sync(0xffffffffu, bsum[G][h], o);
+        psum[G][h] += __shfl_xor_sync(0xffffffffu, psum[G][h], o);
+      }
     }
   }
   // ---- merge the 4 warps in shared memory: [warp][row 8][dim 256] + m, l ----
@@ -677,8 +698,9 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int row = 2 * c + h;
-      Om[(warp * 8 + row) * 256 + d0] = O[i][h] + bsum[G][h];
-      Om[(warp * 8 + row) * 256 + d0 + 8] = O[i][2 + h] + bsum[G][h];
+      const float off = fmaf(-128.f, psum[G][h], bsum[G][h]);
+      Om[(warp * 8 + row) * 256 + d0] = O[i][h] + off;
+      Om[(warp * 8 + row) * 256 + d0 + 8] = O[i][2 + h] + off;
     }
   }
   if (g == 0) {
