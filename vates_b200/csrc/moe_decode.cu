@@ -47,8 +47,8 @@ struct DecEntry {
 };
 
 struct DecodeLayout {
-  size_t counter, n_entries, sgate, rb_count, logits, entries, route_ok, xperm, xsum, hperm,
-      hsum, wparts, sparts, total;
+  size_t counter, n_entries, sgate, rb_count, zero_end, logits, entries, route_ok, xperm, xsum,
+      hperm, hsum, wparts, sparts, total;
   int max_entries;
 };
 
@@ -61,7 +61,8 @@ static DecodeLayout decode_layout(int T, int H, int I, int E, int k) {
   off = align_up(off, 16);
   L.sgate = off; off += sizeof(float) * DEC_MAX_T;
   off = align_up(off, 16);
-  L.rb_count = off; off += sizeof(unsigned) * (H / 128);
+  L.rb_count = off; off += sizeof(unsigned) * (H / 16);
+  L.zero_end = off;  // [0, zero_end) must be zero before a call (tickets)
   off = align_up(off, 256);
   L.logits = off; off += sizeof(float) * (size_t)T * E;
   off = align_up(off, 256);
@@ -904,187 +905,258 @@ __global__ void __launch_bounds__(GateUpTile<H, GS>::THREADS, 1) moe_gateup_kern
 }
 
 // ----------------------------------------------------------------------------
-// K3: down projection + fused combine. One CTA per (entry, 128 output rows),
-// warp w owns rows [16w, 16w+16). Weights are requested before the PDL wait;
-// h is staged in shared memory after it. The last CTA of a 128-row block
-// (atomic ticket per block) adds the routes of every token in rank order
-// (exact double sum of bf16 values, rounded to float32 then bf16), then the
-// gated shared expert and the optional residual.
+// K3: down projection + fused combine. Persistent CTAs of 8 warps; the items
+// (entry, 16 output rows) are split into contiguous entry-major ranges, one
+// per warp (warps of consecutive global index sit on different SMs), so a
+// warp keeps one entry's h fragments in registers across its row blocks.
+// Each item's 16 weight rows and scales are copied by the warp with
+// cp.async into a per-warp ring (the first ones before the PDL wait: the
+// entry list is final by then); h and its group sums are read after it.
+// Per route the result is rounded to bf16, times the route score, rounded
+// again (MLX chain). The last warp to finish a 16-row block (atomic ticket
+// per block) adds the routes of every token in rank order (exact double sum
+// of bf16 values, rounded to float32 then bf16), then the gated shared
+// expert and the optional residual.
 // ----------------------------------------------------------------------------
 constexpr int K3_THREADS = 256;
+constexpr int K3_WARPS = K3_THREADS / 32;
 
-template <int I>
-__global__ void __launch_bounds__(K3_THREADS, 2) moe_down_kernel(DecodeParams p) {
-  constexpr int NGI = I / 64;
-  constexpr int HW = I / 2 + 4;  // words per staged h column (+16 B pad)
-  __shared__ __align__(16) uint32_t hsm[DEC_MAX_T][HW];
-  __shared__ __align__(16) float hs_sm[DEC_MAX_T][I / 16];
-  __shared__ int s_slot, s_n, s_flags;
-  __shared__ int s_rank[DEC_MAX_T];
-  __shared__ float s_score[DEC_MAX_T];
-  __shared__ unsigned s_ticket;
+template <int I, int GS>
+struct DownTile {
+  static constexpr int NGI = I / 64;
+  static constexpr int ROWB = I / 2;        // packed bytes per row
+  static constexpr int PITCH = ROWB + 32;   // padded smem pitch (conflict-free fragments)
+  static constexpr int NSI = I >> (6 + GS); // scales per row
+  static constexpr int WB = 16 * PITCH;
+  static constexpr int SB = 16 * NSI * 2;   // 16 rows of one scale tensor
+  static constexpr int SLOT = WB + 2 * SB;
+  static constexpr int RS = 5;
+  static constexpr int SMEM = K3_WARPS * RS * SLOT;
+};
+
+template <int I, int GS>
+__device__ __forceinline__ void down_issue(uint8_t *slot, const VbQuantPool &pool, int pslot,
+                                           int rb, int lane) {
+  using Tl = DownTile<I, GS>;
+  const uint8_t *dw = pool_ptr(pool, 6, pslot) + (size_t)rb * 16 * Tl::ROWB;
+  constexpr int CPR = Tl::ROWB / 16;  // chunks per row
+#pragma unroll
+  for (int j = 0; j < 16 * CPR / 32; ++j) {
+    const int q = lane + 32 * j, r = q / CPR, c16 = (q % CPR) * 16;
+    cp_async16(slot + r * Tl::PITCH + c16, dw + r * Tl::ROWB + c16);
+  }
+  constexpr int SCH = Tl::SB / 16;  // chunks per scale tensor
+  for (int q = lane; q < 2 * SCH; q += 32) {
+    const int t = q / SCH, c = q % SCH;
+    cp_async16(slot + Tl::WB + t * Tl::SB + c * 16,
+               pool_ptr(pool, 7 + t, pslot) + (size_t)rb * Tl::SB + c * 16);
+  }
+}
+
+// Rank-order combine of one 16-row block for all tokens (one warp; lane =
+// token t = lane / 8 (+4 per pass), row pair 2 * (lane % 8)). Every load of a
+// pass is issued before the first add.
+__device__ __forceinline__ void down_combine_block(const DecodeParams &p, int rb, int lane) {
+  const int T = p.T, H = p.H, k = p.k;
+  const uint32_t *wp = wsp<const uint32_t>(p, p.L.wparts);
+  const int32_t *okr = wsp<const int32_t>(p, p.L.route_ok);
+  const int rp = 16 * rb + 2 * (lane & 7);
+#pragma unroll 1
+  for (int t = lane >> 3; t < T; t += 4) {
+    uint32_t v[DEC_MAX_K];
+    int ok[DEC_MAX_K];
+#pragma unroll
+    for (int j = 0; j < DEC_MAX_K; ++j) {
+      if (j < k) {
+        ok[j] = __ldcg(okr + t * k + j);
+        v[j] = __ldcg(wp + (((size_t)t * k + j) * H + rp) / 2);
+      }
+    }
+    float gate = 0.f;
+    uint32_t sw = 0, rr = 0;
+    const size_t oi = (size_t)t * H + rp;
+    if (p.has_shared) {
+      gate = __ldcg(wsp<const float>(p, p.L.sgate) + t);
+      sw = __ldcg(wsp<const uint32_t>(p, p.L.sparts) + oi / 2);
+    }
+    if (p.residual) rr = __ldg(reinterpret_cast<const uint32_t *>(p.residual) + oi / 2);
+    double s0 = 0.0, s1 = 0.0;
+#pragma unroll
+    for (int j = 0; j < DEC_MAX_K; ++j) {
+      if (j < k && ok[j]) {
+        s0 += (double)bf2f(v[j] & 0xFFFFu);
+        s1 += (double)bf2f(v[j] >> 16);
+      }
+    }
+    float y0 = rbf((float)s0), y1 = rbf((float)s1);
+    if (p.has_shared) {
+      y0 = rbf(__fadd_rn(y0, rbf(__fmul_rn(gate, bf2f(sw & 0xFFFFu)))));
+      y1 = rbf(__fadd_rn(y1, rbf(__fmul_rn(gate, bf2f(sw >> 16)))));
+    }
+    if (p.residual) {
+      y0 = rbf(__fadd_rn(bf2f(rr & 0xFFFFu), y0));
+      y1 = rbf(__fadd_rn(bf2f(rr >> 16), y1));
+    }
+    reinterpret_cast<uint32_t *>(p.out)[oi / 2] = (uint32_t)f2bf(y0) | ((uint32_t)f2bf(y1) << 16);
+  }
+}
+
+template <int I, int GS>
+__global__ void __launch_bounds__(K3_THREADS, 1) moe_down_kernel(DecodeParams p) {
+  using Tl = DownTile<I, GS>;
+  constexpr int NGI = Tl::NGI, RS = Tl::RS;
+  extern __shared__ __align__(16) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
   const int T = p.T, H = p.H;
   SpanTrace span(p.trace, 2);
-  const int e = blockIdx.x, rb = blockIdx.y;
+  uint8_t *ring = smem + warp * RS * Tl::SLOT;
+  const int RBN = H / 16;
+  const int n_entries = __ldcg(wsp<const int32_t>(p, p.L.n_entries));
+  const DecEntry *ents = wsp<const DecEntry>(p, p.L.entries);
+  // This warp's contiguous item range (entry-major).
+  const int nw = gridDim.x * K3_WARPS;
+  const int wg = blockIdx.x + gridDim.x * warp;
+  const int n_items = n_entries * RBN;
+  const int i0 = (int)(((long long)n_items * wg) / nw);
+  const int i1 = (int)(((long long)n_items * (wg + 1)) / nw);
 
-  // Entry list (written by the router two launches back) and weights do not
-  // depend on the gate/up kernel: read them before the PDL wait.
-  if (tid == 0) s_n = *wsp<const int32_t>(p, p.L.n_entries);
-  if (tid < 2 + 2 * DEC_MAX_T) {
-    const int32_t *ent = reinterpret_cast<const int32_t *>(wsp<const DecEntry>(p, p.L.entries) + e);
-    // words: 0 slot, 1 flags, 4..11 rank, 12..19 score
-    const int wi = tid < 2 ? tid : (tid < 2 + DEC_MAX_T ? 4 + (tid - 2) : 12 + (tid - 2 - DEC_MAX_T));
-    if (e < p.L.max_entries) {
-      const int v = ent[wi];
-      if (tid == 0) s_slot = v;
-      else if (tid == 1) s_flags = v;
-      else if (tid < 2 + DEC_MAX_T) s_rank[tid - 2] = v;
-      else s_score[tid - 2 - DEC_MAX_T] = __int_as_float(v);
+  // The entry list is final before this kernel starts (the router ran two
+  // launches back): weights are copied before the PDL wait.
+  int issue_i = i0;
+  auto issue_next = [&]() {
+    if (issue_i < i1) {
+      const int e = issue_i / RBN, rb = issue_i % RBN;
+      const int2 sf = __ldcg(reinterpret_cast<const int2 *>(&ents[e]));  // slot, flags
+      const bool sh = sf.y & 1;
+      down_issue<I, GS>(ring + ((issue_i - i0) % RS) * Tl::SLOT, sh ? p.shared : p.pool,
+                        sh ? 0 : sf.x, rb, lane);
     }
-  }
-  __syncthreads();
-  const int n_entries = s_n;
-  if (e >= n_entries) {
-    span.end();
-    return;
-  }
-  const bool is_shared = s_flags & 1;
-  const VbQuantPool &pool = is_shared ? p.shared : p.pool;
-  const int slot = is_shared ? 0 : s_slot;
-  const int r0 = 128 * rb + 16 * warp + g, r1 = r0 + 8;
-  const int NSI = I >> (6 + p.gshift);
-  uint2 a0[NGI], a1[NGI];
-  {
-    const uint8_t *dw = pool_ptr(pool, 6, slot);
-#pragma unroll
-    for (int G = 0; G < NGI; ++G) {
-      a0[G] = ldg_nc_v2(dw + (size_t)r0 * (I / 2) + G * 32 + 8 * c);
-      a1[G] = ldg_nc_v2(dw + (size_t)r1 * (I / 2) + G * 32 + 8 * c);
-    }
-  }
-  uint4 sv[4];  // down_s r0, r1, down_b r0, r1
-  {
-    const uint16_t *ds = reinterpret_cast<const uint16_t *>(pool_ptr(pool, 7, slot));
-    const uint16_t *db = reinterpret_cast<const uint16_t *>(pool_ptr(pool, 8, slot));
-    sv[0] = ld_scales(ds + (size_t)r0 * NSI, NSI);
-    sv[1] = ld_scales(ds + (size_t)r1 * NSI, NSI);
-    sv[2] = ld_scales(db + (size_t)r0 * NSI, NSI);
-    sv[3] = ld_scales(db + (size_t)r1 * NSI, NSI);
-  }
+    cp_async_commit();
+    ++issue_i;
+  };
+#pragma unroll 1
+  for (int k = 0; k < RS - 1; ++k) issue_next();
   pdl_wait();
   pdl_launch_dependents();
-  {
-    // Stage h (fragment order) and its 16-row chunk sums for the T columns.
-    const uint4 *hp = reinterpret_cast<const uint4 *>(wsp<const uint32_t>(p, p.L.hperm) +
-                                                      (size_t)e * DEC_MAX_T * (I / 2));
-    for (int q = tid; q < T * (I / 8); q += K3_THREADS) {
-      const int n = q / (I / 8), j = q % (I / 8);
-      *reinterpret_cast<uint4 *>(&hsm[n][4 * j]) = __ldcg(hp + q);
-    }
-    const float *hs = wsp<const float>(p, p.L.hsum) + (size_t)e * DEC_MAX_T * (I / 16);
-    for (int q = tid; q < T * (I / 16); q += K3_THREADS) (&hs_sm[0][0])[q] = __ldcg(hs + q);
-  }
-  __syncthreads();
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int G = 0; G < NGI; ++G) {
-    uint4 hb0 = make_uint4(0, 0, 0, 0), hb1 = make_uint4(0, 0, 0, 0);
-    if (g < T) {
-      const uint4 *hp = reinterpret_cast<const uint4 *>(&hsm[g][(G * 4 + c) * 8]);
-      hb0 = hp[0];
-      hb1 = hp[1];
-    }
-    const uint32_t hw[8] = {hb0.x, hb0.y, hb0.z, hb0.w, hb1.x, hb1.y, hb1.z, hb1.w};
-    float dd[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const int i0 = 2 * (m & 1);
-      const uint32_t wa = (m >> 1) ? a0[G].y : a0[G].x;
-      const uint32_t wb = (m >> 1) ? a1[G].y : a1[G].x;
-      mma_bf16(dd, nib_pair(wa, i0), nib_pair(wb, i0), nib_pair(wa, i0 + 1),
-               nib_pair(wb, i0 + 1), hw[2 * m], hw[2 * m + 1]);
-    }
-    const int si = G >> p.gshift;
-    const float s0 = bf_at(sv[0], si), s1 = bf_at(sv[1], si);
-    const float b0 = bf_at(sv[2], si), b1 = bf_at(sv[3], si);
-    float h0 = 0.f, h1 = 0.f;
-    if (2 * c < T) {
-      const float4 v = *reinterpret_cast<const float4 *>(&hs_sm[2 * c][4 * G]);
-      h0 = ((v.x + v.y) + v.z) + v.w;
-    }
-    if (2 * c + 1 < T) {
-      const float4 v = *reinterpret_cast<const float4 *>(&hs_sm[2 * c + 1][4 * G]);
-      h1 = ((v.x + v.y) + v.z) + v.w;
-    }
-    const float bp0 = fmaf(-128.f, s0, b0), bp1 = fmaf(-128.f, s1, b1);
-    acc[0] += fmaf(s0, dd[0], bp0 * h0);
-    acc[1] += fmaf(s0, dd[1], bp0 * h1);
-    acc[2] += fmaf(s1, dd[2], bp1 * h0);
-    acc[3] += fmaf(s1, dd[3], bp1 * h1);
-  }
+
   uint16_t *wparts = wsp<uint16_t>(p, p.L.wparts);
   uint16_t *sparts = wsp<uint16_t>(p, p.L.sparts);
+  int cur_e = -1;
+  uint32_t hb[NGI][8];
+  float hs0[NGI], hs1[NGI];
+  int rank0 = -1, rank1 = -1;
+  float score0 = 0.f, score1 = 0.f;
+  bool is_sh = false;
+#pragma unroll 1
+  for (int i = i0; i < i1; ++i) {
+    const int e = i / RBN, rb = i % RBN;
+    if (e != cur_e) {
+      // h fragments and group sums of the entry (tokens g and 2c, 2c+1),
+      // requested while the weight copy is still in flight.
+      cur_e = e;
+      const uint32_t *hp = wsp<const uint32_t>(p, p.L.hperm) + (size_t)e * DEC_MAX_T * (I / 2);
+      const float *hsum = wsp<const float>(p, p.L.hsum) + (size_t)e * DEC_MAX_T * (I / 16);
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int n = 2 * c + (q & 1);
-    if (n >= T) continue;
-    const int row = (q >> 1) ? r1 : r0;
-    const float yb = rbf(acc[q]);
-    if (is_shared) {
-      sparts[(size_t)n * H + row] = f2bf(yb);
-    } else if (s_rank[n] >= 0) {
-      wparts[((size_t)n * p.k + s_rank[n]) * H + row] = f2bf(__fmul_rn(yb, s_score[n]));
+      for (int G = 0; G < NGI; ++G) {
+        uint4 a = make_uint4(0, 0, 0, 0), b = a;
+        if (g < T) {
+          const uint4 *src = reinterpret_cast<const uint4 *>(hp + ((size_t)g * NGI + G) * 32 + c * 8);
+          a = __ldcg(src);
+          b = __ldcg(src + 1);
+        }
+        hb[G][0] = a.x; hb[G][1] = a.y; hb[G][2] = a.z; hb[G][3] = a.w;
+        hb[G][4] = b.x; hb[G][5] = b.y; hb[G][6] = b.z; hb[G][7] = b.w;
+        float v0 = 0.f, v1 = 0.f;
+        if (2 * c < T) {
+          const float4 v = __ldcg(reinterpret_cast<const float4 *>(hsum + (size_t)(2 * c) * (I / 16) + 4 * G));
+          v0 = ((v.x + v.y) + v.z) + v.w;
+        }
+        if (2 * c + 1 < T) {
+          const float4 v = __ldcg(reinterpret_cast<const float4 *>(hsum + (size_t)(2 * c + 1) * (I / 16) + 4 * G));
+          v1 = ((v.x + v.y) + v.z) + v.w;
+        }
+        hs0[G] = v0;
+        hs1[G] = v1;
+      }
+      is_sh = __ldcg(&ents[e].flags) & 1;
+      rank0 = 2 * c < T ? __ldcg(&ents[e].rank[2 * c]) : -1;
+      rank1 = 2 * c + 1 < T ? __ldcg(&ents[e].rank[2 * c + 1]) : -1;
+      score0 = 2 * c < T ? __ldcg(&ents[e].score[2 * c]) : 0.f;
+      score1 = 2 * c + 1 < T ? __ldcg(&ents[e].score[2 * c + 1]) : 0.f;
+    }
+    cp_async_wait<RS - 2>();
+    __syncwarp();
+    issue_next();
+    const uint8_t *st = ring + ((i - i0) % RS) * Tl::SLOT;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int G = 0; G < NGI; ++G) {
+      const uint2 a0 = lds64(st + g * Tl::PITCH + G * 32 + 8 * c);
+      const uint2 a1 = lds64(st + (g + 8) * Tl::PITCH + G * 32 + 8 * c);
+      uint32_t p0[2][4], p1[2][4];
+      nib_pairs4(a0.x, p0[0]);
+      nib_pairs4(a0.y, p0[1]);
+      nib_pairs4(a1.x, p1[0]);
+      nib_pairs4(a1.y, p1[1]);
+      float dd[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int i0m = 2 * (m & 1), h = m >> 1;
+        mma_bf16(dd, p0[h][i0m], p1[h][i0m], p0[h][i0m + 1], p1[h][i0m + 1], hb[G][2 * m],
+                 hb[G][2 * m + 1]);
+      }
+      const int si = G >> GS;
+      const uint16_t *ss = reinterpret_cast<const uint16_t *>(st + Tl::WB);
+      const float s0 = bf2f(ss[g * Tl::NSI + si]), s1 = bf2f(ss[(g + 8) * Tl::NSI + si]);
+      const float b0 = bf2f(ss[Tl::SB / 2 + g * Tl::NSI + si]);
+      const float b1 = bf2f(ss[Tl::SB / 2 + (g + 8) * Tl::NSI + si]);
+      const float bp0 = fmaf(-128.f, s0, b0), bp1 = fmaf(-128.f, s1, b1);
+      acc[0] += fmaf(s0, dd[0], bp0 * hs0[G]);
+      acc[1] += fmaf(s0, dd[1], bp0 * hs1[G]);
+      acc[2] += fmaf(s1, dd[2], bp1 * hs0[G]);
+      acc[3] += fmaf(s1, dd[3], bp1 * hs1[G]);
+    }
+    const int r0 = 16 * rb + g, r1 = r0 + 8;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int n = 2 * c + (q & 1);
+      if (n >= T) continue;
+      const int row = (q >> 1) ? r1 : r0;
+      const float yb = rbf(acc[q]);
+      if (is_sh) {
+        sparts[(size_t)n * H + row] = f2bf(yb);
+      } else {
+        const int rk = (q & 1) ? rank1 : rank0;
+        const float sc = (q & 1) ? score1 : score0;
+        if (rk >= 0) wparts[((size_t)n * p.k + rk) * H + row] = f2bf(__fmul_rn(yb, sc));
+      }
     }
   }
-
-  // ---- fused combine: the last entry CTA of this row block adds the routes.
+  cp_async_wait<0>();
+  // ---- tickets: one fence for all of this warp's items, one atomic per item
+  // (lanes in parallel); the warp that completes a 16-row block combines it.
   __threadfence();
-  __syncthreads();
-  unsigned *cnt = wsp<unsigned>(p, p.L.rb_count) + rb;
-  if (tid == 0) s_ticket = atomicAdd(cnt, 1u);
-  __syncthreads();
-  if (s_ticket == (unsigned)n_entries - 1) {
-    __threadfence();
-    const int k = p.k;
-    const uint32_t *wp = wsp<const uint32_t>(p, p.L.wparts);
-    const int32_t *ok = wsp<const int32_t>(p, p.L.route_ok);
-    for (int q = tid; q < T * 64; q += K3_THREADS) {  // (token, column pair)
-      const int t = q >> 6, c2 = 64 * rb + (q & 63);
-      uint32_t wv[DEC_MAX_K];
-      int okv[DEC_MAX_K];
-#pragma unroll
-      for (int j = 0; j < DEC_MAX_K; ++j) {
-        if (j < k) {
-          okv[j] = __ldcg(ok + t * k + j);
-          wv[j] = __ldcg(wp + ((size_t)t * k + j) * (H / 2) + c2);
-        }
-      }
-      double s0 = 0.0, s1 = 0.0;
-#pragma unroll
-      for (int j = 0; j < DEC_MAX_K; ++j) {
-        if (j < k && okv[j]) {
-          s0 += (double)bf2f(wv[j] & 0xFFFF);
-          s1 += (double)bf2f(wv[j] >> 16);
-        }
-      }
-      float y0 = rbf((float)s0), y1 = rbf((float)s1);
-      if (p.has_shared) {
-        const float gate = __ldcg(wsp<const float>(p, p.L.sgate) + t);
-        const uint32_t sw = __ldcg(wsp<const uint32_t>(p, p.L.sparts) + (size_t)t * (H / 2) + c2);
-        y0 = rbf(__fadd_rn(y0, rbf(__fmul_rn(gate, bf2f(sw & 0xFFFF)))));
-        y1 = rbf(__fadd_rn(y1, rbf(__fmul_rn(gate, bf2f(sw >> 16)))));
-      }
-      const size_t oi = (size_t)t * (H / 2) + c2;
-      if (p.residual) {
-        const uint32_t rr = reinterpret_cast<const uint32_t *>(p.residual)[oi];
-        y0 = rbf(__fadd_rn(bf2f(rr & 0xFFFF), y0));
-        y1 = rbf(__fadd_rn(bf2f(rr >> 16), y1));
-      }
-      reinterpret_cast<uint32_t *>(p.out)[oi] = pack_bf2(y0, y1);
+  __syncwarp();
+  unsigned *cnt = wsp<unsigned>(p, p.L.rb_count);
+#pragma unroll 1
+  for (int base = i0; base < i1; base += 32) {
+    const int i = base + lane;
+    int rb = 0;
+    bool win = false;
+    if (i < i1) {
+      rb = i % RBN;
+      win = atomicAdd(cnt + rb, 1u) == (unsigned)n_entries - 1;
     }
-    if (tid == 0) *cnt = 0u;  // ready for the next launch
+    unsigned m = __ballot_sync(0xffffffffu, win);
+    if (m) __threadfence();
+    while (m) {
+      const int src = __ffs(m) - 1;
+      m &= m - 1;
+      const int rbw = __shfl_sync(0xffffffffu, rb, src);
+      down_combine_block(p, rbw, lane);
+      if (lane == 0) cnt[rbw] = 0u;  // ready for the next launch
+    }
   }
   span.end();
 }
@@ -1229,11 +1301,23 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
 #undef VB_K2
 #undef VB_K1
   void (*k3)(DecodeParams) = nullptr;
+  size_t k3_smem = 0;
+#define VB_K3(II)                                                 \
+  do {                                                            \
+    if (p.gshift) {                                               \
+      k3 = moe_down_kernel<II, 1>;                                \
+      k3_smem = DownTile<II, 1>::SMEM;                            \
+    } else {                                                      \
+      k3 = moe_down_kernel<II, 0>;                                \
+      k3_smem = DownTile<II, 0>::SMEM;                            \
+    }                                                             \
+  } while (0)
   switch (I) {
-    case 128: k3 = moe_down_kernel<128>; break;
-    case 256: k3 = moe_down_kernel<256>; break;
-    default: k3 = moe_down_kernel<512>; break;
+    case 128: VB_K3(128); break;
+    case 256: VB_K3(256); break;
+    default: VB_K3(512); break;
   }
+#undef VB_K3
 
   cudaStream_t s = as_stream(stream);
   cudaEvent_t *ev = a->timing_events ? (cudaEvent_t *)a->timing_events : nullptr;
@@ -1244,7 +1328,7 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   const size_t smem1 = (size_t)T * H * 2;
   cudaError_t err = decode_kernel_attrs((const void *)k1, smem1);
   if (err == cudaSuccess) err = decode_kernel_attrs((const void *)k2, k2_smem);
-  if (err == cudaSuccess) err = decode_kernel_attrs((const void *)k3, 0);
+  if (err == cudaSuccess) err = decode_kernel_attrs((const void *)k3, k3_smem);
   if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "decode kernel attributes: %s", cudaGetErrorString(err));
   const int rpc = K1_WARPS / (H >= 1024 ? 4 : 2);
   const int grid1 = (E + (has_shared ? 1 : 0) + rpc - 1) / rpc;
@@ -1259,7 +1343,8 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_gateup_kernel: %s", cudaGetErrorString(err));
   if (ev) cudaEventRecord(ev[2], s);
 
-  err = vb_launch(k3, dim3(L.max_entries, H / 128), dim3(K3_THREADS), 0, s, pdl, p);
+  err = vb_launch(k3, dim3(std::min(sm_count(), L.max_entries * (H / 16))), dim3(K3_THREADS),
+                  k3_smem, s, pdl, p);
   if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_down_kernel: %s", cudaGetErrorString(err));
   if (ev) cudaEventRecord(ev[3], s);
   return VB_OK;
@@ -1282,7 +1367,7 @@ int vb_moe_decode_noalloc(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   // expect at zero (route ticket, entry count, shared gates, row-block
   // tickets) before this call's kernels, in stream order.
   const DecodeLayout L = decode_layout(a->tokens, a->hidden, a->inter, a->num_experts, a->top_k);
-  const size_t clear = L.rb_count + sizeof(unsigned) * (size_t)(a->hidden / 128);
+  const size_t clear = L.zero_end;
   const cudaError_t e = cudaMemsetAsync(scratch, 0, clear, as_stream(stream));
   if (e != cudaSuccess)
     return set_error(VB_ERR_CUDA, "vb_moe_decode_noalloc: clearing scratch: %s", cudaGetErrorString(e));
