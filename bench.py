@@ -32,7 +32,6 @@ METRIC = "MoE tokens/s and HBM GB/s (decode T≤4); prefill tok/s at 1/2/4/8 B20
 EXPERT_BYTES = 1_769_472          # blob_layout stride at H=2048, I=512, 4-bit g64
 ROUTER_BYTES = 512 * 2048 * 2
 SHARED_GATE_BYTES = 2048 * 2
-GATEUP_BYTES = 2 * 589_824        # gate + up of one expert
 
 
 def peaks():
@@ -383,45 +382,42 @@ def run_decode(args, world, rank, local):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
     barrier(world)
 
-    # ---- warm in-graph kernel spans from the kernels' %globaltimer trace ----
+    # ---- warm in-graph kernel spans from the kernel's %globaltimer trace ----
     trace = torch.empty((L, 16), dtype=torch.int64, device="cuda")
-    init = torch.tensor([-1, 0] * 3 + [0] * 10, dtype=torch.int64, device="cuda")
+    init = torch.tensor([-1, 0] + [0] * 14, dtype=torch.int64, device="cuda")
     tgraph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(tgraph, stream=stream):
         st.step(stream=stream, trace=trace)
-    spans = []
     for _ in range(3):
         trace.copy_(init.expand(L, 16))
         tgraph.replay()
         torch.cuda.synchronize()
-        tr = trace.cpu().numpy().astype("uint64").astype("float64")
-        spans.append(tr)
-    tr = spans[-1]
-    kspan = [(tr[:, 2 * i + 1] - tr[:, 2 * i]).mean() / 1e3 for i in range(3)]
-    layer_us = (tr[1:, 0] - tr[:-1, 0]).mean() / 1e3
-    gaps = [(tr[:, 2 * (i + 1)] - tr[:, 2 * i + 1]).mean() / 1e3 for i in range(2)]
-    router_marks = [(tr[:, m] - tr[:, 0]).mean() / 1e3 for m in (8, 11, 12, 13, 9, 10, 14, 15, 6, 7)]
+    tr = trace.cpu().numpy().astype("uint64").astype("float64")
     del tgraph
+    kspan = (tr[:, 1] - tr[:, 0]).mean() / 1e3
+    layer_us = (tr[1:, 0] - tr[:-1, 0]).mean() / 1e3
+    marks = {name: (tr[:, m] - tr[:, 0]).mean() / 1e3 for m, name in (
+        (2, "pdl_wait"), (3, "router_rows"), (4, "grid_barrier"), (5, "routing"),
+        (6, "gateup"), (7, "down"), (8, "combine"))}
 
-    # ---- dominant kernel (gate/up) timed per launch with CUDA events ----
+    # ---- the layer kernel timed per launch with CUDA events (outside the
+    # PDL chain, so each launch starts cold) ----
     evs, arr = st.blocks[0].timing_events()
-    phase = [0.0, 0.0, 0.0]
+    launch_ms = 0.0
     reps = 3
     for _ in range(reps):
         for l, blk in enumerate(st.blocks):
             blk.decode(st.hs[l], out=st.hs[l + 1], residual=st.hs[l], norm_eps=st.norm_eps,
                        timing=arr)
-            evs[3].synchronize()
-            for i in range(3):
-                phase[i] += evs[i].elapsed_time(evs[i + 1])
-    n_launch = reps * L
-    gateup_ms = phase[1] / n_launch
-    gateup_bytes = sum((u + 1) * GATEUP_BYTES for u in U) / L  # per launch, algorithmic
-    achieved = gateup_bytes / (gateup_ms / 1e3) / 1e9
+            evs[1].synchronize()
+            launch_ms += evs[0].elapsed_time(evs[1])
+    launch_ms /= reps * L
 
     step_bytes = sum(u * EXPERT_BYTES + EXPERT_BYTES + ROUTER_BYTES + SHARED_GATE_BYTES
                      + 3 * T * 2048 * 2 for u in U)
     hbm_gbs = step_bytes / (ms / 1e3) / 1e9
+    layer_bytes = step_bytes / L  # per launch, algorithmic
+    achieved = layer_bytes / (launch_ms / 1e3) / 1e9
 
     out = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -440,17 +436,14 @@ def run_decode(args, world, rank, local):
         "unique_experts_per_layer_mean": sum(U) / len(U),
         "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s",
                 "h2d_bytes_per_step": T * 2048 * 2, "d2h_bytes_per_step": T * 2048 * 2},
-        "roofline": {"kernel": "moe_gateup_kernel", "bound": "hbm", "achieved": achieved,
+        "roofline": {"kernel": "moe_layer_kernel", "bound": "hbm", "achieved": achieved,
                      "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "traffic": None,
-                     "bytes_per_launch": gateup_bytes, "ms_per_launch": gateup_ms,
-                     "phase_ms": {"router": phase[0] / n_launch, "gateup": gateup_ms,
-                                  "down_combine": phase[2] / n_launch}},
-        "kernel_trace_us": {"router": kspan[0], "gateup": kspan[1],
-                            "down_combine": kspan[2], "layer_period": layer_us,
-                            "start_gaps": gaps,
-                            "router_marks_from_start": router_marks},
-        "gpu_launches": 3 * L * args.steps,
+                     "bytes_per_launch": layer_bytes, "ms_per_launch": launch_ms,
+                     "in_graph_gbs": layer_bytes / (layer_us / 1e6) / 1e9},
+        "kernel_trace_us": {"span": kspan, "layer_period": layer_us,
+                            "marks_from_start": marks},
+        "gpu_launches": L * args.steps,
         "clocks": clocks,
     }
     if not args.no_extra:

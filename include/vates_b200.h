@@ -110,7 +110,10 @@ int vb_fused_moe_pairs(const float *x, const uint32_t *indices,
  * -> renormalise (321-329) -> slot gather (resident_pool.py:560-569) ->
  * gate/up -> SwiGLU -> down (compute.py:145-199) -> weighted combine
  * (block.py:1008) -> + sigmoid(x.w_sg) * shared_expert(x) (1009-1012).
- * 4-bit weights, group 64 or 128, hidden/inter multiples of 64. */
+ * 4-bit weights, group 64 or 128, hidden in {512, 1024, 2048, 4096}, inter
+ * in {128, 256, 512}. One persistent kernel with one CTA per SM; its CTAs
+ * synchronise through the workspace with bounded waits (2 s, then
+ * VB_STATUS_TIMEOUT), so it needs every SM's share of the GPU. */
 typedef struct VbMoeDecodeArgs {
   int32_t tokens;       /* T, 1..8 */
   int32_t hidden;       /* H */
@@ -123,7 +126,8 @@ typedef struct VbMoeDecodeArgs {
   float norm_eps;       /* > 0: the block input is rmsnorm(x) (unit weight,
                            float32 math, bf16 result); 0: x as given */
   int32_t reserved0;
-  const uint16_t *x;            /* bf16 [T, H] */
+  const uint16_t *x;            /* bf16 [T, H]; x, residual and out are
+                                   16-byte aligned */
   const uint16_t *router_w;     /* bf16 [E, H] */
   const float *router_bias;     /* nullable f32 [E], added before rounding */
   const int32_t *slot_table;    /* [E], -1 = not resident */
@@ -138,23 +142,25 @@ typedef struct VbMoeDecodeArgs {
   int32_t *status;              /* nullable device status word */
   void *workspace;
   size_t workspace_bytes;
-  void *const *timing_events;   /* nullable: 4 cudaEvent_t recorded before the
-                                   router, gate/up and down kernels and after
-                                   the down kernel (profiling only) */
-  uint64_t *trace;              /* nullable device [16]: [0..5] per kernel
-                                   (router, gate/up, down+combine) the min
-                                   start and max end %globaltimer (ns) over
-                                   its CTAs, initialised by the caller to
-                                   (UINT64_MAX, 0); [6..7] unused; [8..15]
-                                   router markers
-                                   (latest CTA past the PDL wait, latest CTA
-                                   done with its rows, top-k start),
-                                   initialised to 0 (profiling only) */
+  void *const *timing_events;   /* nullable: 2 cudaEvent_t recorded before
+                                   and after the layer kernel; the launch
+                                   then leaves the PDL chain (profiling only) */
+  uint64_t *trace;              /* nullable device [16] %globaltimer (ns)
+                                   markers of the layer kernel (profiling
+                                   only): [0] min CTA start, [1] max CTA end,
+                                   initialised by the caller to
+                                   (UINT64_MAX, 0); latest CTA past the PDL
+                                   wait [2], done with its router rows [3],
+                                   past the grid barrier [4], done routing
+                                   [5]; latest warp done with gate/up [6],
+                                   with its down items [7], with its
+                                   combines [8]; [2..15] initialised to 0 */
 } VbMoeDecodeArgs;
 
 /* The decode workspace must be zero-filled before its first use; every call
- * leaves it reusable by the next call on the same stream. Calls sharing one
- * workspace must not overlap on the GPU. */
+ * leaves it reusable by the next call on the same stream (after a call that
+ * reported VB_STATUS_TIMEOUT it must be zero-filled again). Calls sharing
+ * one workspace must not overlap on the GPU. */
 size_t vb_moe_decode_workspace_size(int32_t tokens, int32_t hidden,
                                     int32_t inter, int32_t num_experts,
                                     int32_t top_k);

@@ -4,27 +4,38 @@
 // :245-1013) with PersistentSubGLU.forward (compute.py:145-199) and the
 // shared expert (block.py:102-109, 1009-1012).
 //
-// Three kernels per block, chained with programmatic dependent launch (PDL):
-//  K1 router: optional unit RMSNorm of x, logits = bf16(x.Wr^T [+bias]) and
-//     the shared-expert gate sigmoid(x.w_sg) as one more row; every row is
-//     split over 2-4 warps and loaded before the PDL wait. All CTAs share
-//     writing x in MMA-fragment order (xperm) and per-64-column sums (xsum).
-//     The last CTA (atomic ticket) runs the precise softmax, top-k (one warp
-//     reduction per pick on (bf16 probability, expert id) keys, lower id wins
-//     ties), renormalisation and slot gather, and writes the list of
-//     "entries": the shared expert first, then every distinct routed expert.
-//  K2 gate/up: persistent CTAs; the two warps of a pair split an item (entry,
-//     16 intermediate rows) over the hidden dimension and stream it through
-//     per-warp cp.async rings; 4-bit codes become exact bf16 values 128+q for
+// One persistent kernel per block (one CTA per SM, all CTAs resident), a PDL
+// secondary of whatever ran before it on the stream. Phases:
+//  1. Before the PDL wait: every warp loads its part of one router row
+//     (rows 0..E-1 the experts, row E the shared-expert gate) into
+//     registers, and the shared expert (it needs no routing) is
+//     bulk-prefetched into L2.
+//  2. Every CTA stages x, applies the optional unit RMSNorm (exact double sum
+//     of squares), keeps x in MMA-fragment order with its per-64-column sums
+//     in shared memory, and computes its router rows: logits =
+//     bf16(x.Wr^T [+bias]) and the gate sigmoid(x.w_sg), written to global
+//     memory.
+//  3. Grid barrier (bounded wait). Every CTA then runs the same precise
+//     softmax, top-k (one warp reduction per pick on (bf16 probability,
+//     expert id) keys, lower id wins ties), renormalisation and slot gather,
+//     and builds the same list of "entries" in shared memory: the shared
+//     expert first, then every distinct routed expert in route order.
+//  4. Gate/up: the two warps of a pair split an item (entry, 16 intermediate
+//     rows) over the hidden dimension and stream it through per-warp
+//     cp.async rings; 4-bit codes become exact bf16 values 128+q for
 //     mma.m16n8k16 and the per-group epilogue applies y += s*D + (b-128*s)*
-//     sum(x). SwiGLU (bf16 per op); h in fragment order (hperm). Item blocks
-//     and the matching down-projection rows are bulk-prefetched into L2.
-//  K3 down + combine: one CTA per (entry, 128 output rows), weights requested
-//     before the PDL wait; per route the result is rounded to bf16, times the
-//     route score, rounded again (MLX chain). The last CTA of each 128-row
-//     block (atomic ticket) adds the k routes of every token in rank order
-//     (exact double sum of bf16 values, rounded to float32 then bf16), then
-//     the gated shared expert and the optional residual.
+//     sum(x). SwiGLU (bf16 per op); h goes to global memory in fragment
+//     order and the item is counted on its entry (release).
+//  5. Down: each warp owns a contiguous entry-major range of items (entry, 16
+//     output rows); it copies their weights into its ring (the one it used
+//     for gate/up) and waits (bounded, acquire) until the entry's h is
+//     complete. Per route the result is rounded to bf16, times the route
+//     score, rounded again (MLX chain).
+//  6. Combine: the warp completing a 16-row block (atomic ticket) adds the k
+//     routes of every token in rank order (exact double sum of bf16 values,
+//     rounded to float32 then bf16), then the gated shared expert and the
+//     optional residual.
+// Every wait is bounded (2 s); a wait that gives up sets VB_STATUS_TIMEOUT.
 #include <algorithm>
 #include <mutex>
 #include <vector>
@@ -36,7 +47,6 @@ namespace vb {
 constexpr int DEC_MAX_T = 8;
 constexpr int DEC_MAX_K = 16;
 constexpr int DEC_MAX_E = 1024;
-constexpr int DEC_SMEM_BUDGET = 200 * 1024;
 
 struct DecEntry {
   int32_t slot;
@@ -47,8 +57,7 @@ struct DecEntry {
 };
 
 struct DecodeLayout {
-  size_t counter, n_entries, sgate, rb_count, zero_end, logits, entries, route_ok, xperm, xsum,
-      hperm, hsum, wparts, sparts, total;
+  size_t bar, sgate, ent_done, rb_count, zero_end, logits, hperm, hsum, wparts, sparts, total;
   int max_entries;
 };
 
@@ -56,23 +65,15 @@ static DecodeLayout decode_layout(int T, int H, int I, int E, int k) {
   DecodeLayout L;
   L.max_entries = T * k + 1;
   size_t off = 0;
-  L.counter = off; off += 4;
-  L.n_entries = off; off += 4;
-  off = align_up(off, 16);
+  L.bar = off; off += 16;  // grid barrier: arrivals, generation
   L.sgate = off; off += sizeof(float) * DEC_MAX_T;
   off = align_up(off, 16);
+  L.ent_done = off; off += sizeof(unsigned) * (size_t)L.max_entries;
+  off = align_up(off, 16);
   L.rb_count = off; off += sizeof(unsigned) * (H / 16);
-  L.zero_end = off;  // [0, zero_end) must be zero before a call (tickets)
+  L.zero_end = off;  // [0, zero_end) must be zero before the first call
   off = align_up(off, 256);
   L.logits = off; off += sizeof(float) * (size_t)T * E;
-  off = align_up(off, 256);
-  L.entries = off; off += sizeof(DecEntry) * (size_t)L.max_entries;
-  off = align_up(off, 256);
-  L.route_ok = off; off += sizeof(int32_t) * (size_t)T * k;
-  off = align_up(off, 256);
-  L.xperm = off; off += sizeof(uint32_t) * (size_t)T * (H / 2);
-  off = align_up(off, 256);
-  L.xsum = off; off += sizeof(float) * (size_t)T * (H / 64);
   off = align_up(off, 256);
   L.hperm = off; off += sizeof(uint32_t) * (size_t)L.max_entries * DEC_MAX_T * (I / 2);
   off = align_up(off, 256);
@@ -105,13 +106,13 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
-// Optional span trace: thread 0 of every CTA folds its start/end into the
-// kernel's [min start, max end] pair.
+// Optional trace: thread 0 of every CTA folds its start/end into the
+// kernel's [min start, max end] pair (slots 0, 1).
 struct SpanTrace {
   uint64_t *slot;
   uint64_t t0;
-  __device__ __forceinline__ SpanTrace(uint64_t *trace, int kernel) {
-    slot = (trace && threadIdx.x == 0) ? trace + 2 * kernel : nullptr;
+  __device__ __forceinline__ explicit SpanTrace(uint64_t *trace) {
+    slot = (trace && threadIdx.x == 0) ? trace : nullptr;
     t0 = slot ? globaltimer() : 0;
   }
   __device__ __forceinline__ void end() {
@@ -135,7 +136,6 @@ __device__ __forceinline__ T *wsp(const DecodeParams &p, size_t off) {
   return reinterpret_cast<T *>(p.ws + off);
 }
 
-
 // Bytes of tensor t (gate w,s,b, up w,s,b, down w,s,b) of one 4-bit expert.
 __device__ __forceinline__ uint32_t expert_tensor_bytes(const DecodeParams &p, int t) {
   const int f = t % 3;
@@ -146,16 +146,16 @@ __device__ __forceinline__ uint32_t expert_tensor_bytes(const DecodeParams &p, i
 
 constexpr uint32_t PF_PIECE = 16u << 10;
 
-// L2 bulk prefetch of tensors [t0, t1) of one expert, pieces [first, ...) of
-// the expert's piece sequence with stride `step` (pieces are 16 KB).
-__device__ __forceinline__ int expert_pieces(const DecodeParams &p, int t0, int t1) {
+// An expert as a sequence of 16 KB pieces (tensor by tensor): the count, and
+// an L2 bulk prefetch of one piece.
+__device__ __forceinline__ int expert_pieces(const DecodeParams &p) {
   int n = 0;
-  for (int t = t0; t < t1; ++t) n += (expert_tensor_bytes(p, t) + PF_PIECE - 1) / PF_PIECE;
+  for (int t = 0; t < 9; ++t) n += (expert_tensor_bytes(p, t) + PF_PIECE - 1) / PF_PIECE;
   return n;
 }
 __device__ __forceinline__ void prefetch_expert_piece(const DecodeParams &p, const VbQuantPool &pool,
-                                                      int slot, int t0, int piece) {
-  for (int t = t0; t < 9; ++t) {
+                                                      int slot, int piece) {
+  for (int t = 0; t < 9; ++t) {
     const uint32_t tb = expert_tensor_bytes(p, t);
     const int c = (tb + PF_PIECE - 1) / PF_PIECE;
     if (piece < c) {
@@ -170,24 +170,13 @@ __device__ __forceinline__ void prefetch_expert_piece(const DecodeParams &p, con
 __device__ __forceinline__ uint2 lds64(const uint8_t *p) {
   return *reinterpret_cast<const uint2 *>(p);
 }
-
-// ----------------------------------------------------------------------------
-// K1: router GEMV + last-CTA softmax/top-k/entries. H is a template constant
-// so that every index is a shift. Rows 0..E-1 are the experts' router rows,
-// row E (when there is a shared expert) the shared-expert gate row; each row
-// is split over Q warps (RPC = 8/Q rows per CTA) whose partial dots are added
-// in part order. Rows are loaded before the PDL wait.
-// ----------------------------------------------------------------------------
-constexpr int K1_THREADS = 256;
-constexpr int K1_WARPS = K1_THREADS / 32;
-
-template <int H>
-struct RouterTile {
-  static constexpr int Q = H >= 1024 ? 4 : 2;  // warps per row
-  static constexpr int RPC = K1_WARPS / Q;      // rows per CTA
-  static constexpr int NVQ = H / (256 * Q);     // uint4 of a row part per lane
-  static_assert(NVQ >= 1, "router tile");
-};
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+// bf16 at index i (0..3) of a 2-word vector.
+__device__ __forceinline__ float bf_at2(const uint2 &v, int i) {
+  const uint32_t w = i < 2 ? v.x : v.y;
+  return (i & 1) ? bf_hi(w) : bf_lo(w);
+}
 
 // Orderable key of a float (for unsigned max).
 __device__ __forceinline__ uint32_t f2key(float f) {
@@ -198,219 +187,246 @@ __device__ __forceinline__ float key2f(uint32_t k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-template <int H, int PER>  // PER = ceil(E / 32) logits per lane
-__global__ void __launch_bounds__(K1_THREADS, 2) moe_router_kernel(DecodeParams p) {
-  using Tl = RouterTile<H>;
-  constexpr int Q = Tl::Q, RPC = Tl::RPC, NVQ = Tl::NVQ;
-  constexpr int NG = H / 64;
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  uint16_t *xs = reinterpret_cast<uint16_t *>(smem_raw);  // [T][H] bf16
-  __shared__ double s_ss[K1_WARPS][DEC_MAX_T];
-  __shared__ float s_inv[DEC_MAX_T];
-  __shared__ float s_part[RPC][Q][DEC_MAX_T];
-  const int T = p.T, E = p.E;
+__device__ __forceinline__ void named_bar(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release(unsigned *p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+constexpr uint64_t KL_WAIT_NS = 2000000000ull;  // bound of every wait
+
+// Waits (acquire) until *p != v (ne) or *p >= v (!ne); false after the bound.
+__device__ __forceinline__ bool wait_word(const unsigned *p, unsigned v, bool ne) {
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    const unsigned x = ld_acquire(p);
+    if (ne ? x != v : x >= v) return true;
+    if (globaltimer() - t0 > KL_WAIT_NS) return false;
+    __nanosleep(128);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Tiles and the shared-memory map of the layer kernel.
+// ----------------------------------------------------------------------------
+constexpr int KL_THREADS = 256;
+constexpr int KL_WARPS = KL_THREADS / 32;
+constexpr int KL_PAIRS = KL_WARPS / 2;
+constexpr int KL_MAX_ENT = DEC_MAX_T * DEC_MAX_K + 1;
+constexpr int KL_MAX_ROUTES = DEC_MAX_T * DEC_MAX_K;
+
+constexpr int align_c(int x, int a) { return (x + a - 1) / a * a; }
+
+template <int H, int I>
+struct LayerTile {
+  // Router: a row is split over Q warps, NVQ uint4 of the row part per lane.
+  static constexpr int Q = H >= 1024 ? 2 : 1;
+  static constexpr int RPC = KL_WARPS / Q;  // rows per CTA and round
+  static constexpr int NVQ = H / (256 * Q);
+  // Gate/up: item (entry, 16 intermediate rows) over a warp pair; a chunk is
+  // 16 rows x 4 groups of 64 columns of gate and up plus their scales.
+  static constexpr int NG = H / 64;
+  static constexpr int CG = 4;
+  static constexpr int NCH = NG / CG;
+  static constexpr int CPH = NCH / 2;       // chunks per warp of the pair
+  static constexpr int ROWB = H / 2;        // packed bytes per row
+  static constexpr int CROW = CG * 32;      // chunk bytes per row
+  static constexpr int PITCH = CROW + 32;   // padded row pitch in a stage
+  static constexpr int NS64 = H / 64;       // scales per row at group 64
+  static constexpr int WB = 2 * 16 * PITCH; // gate + up codes of a chunk
+  static constexpr int CHUNK = WB + 4 * 16 * 8;
+  static constexpr int RS = 3;              // ring stages
+  static constexpr int RING = RS * CHUNK;   // one warp's ring
+  static constexpr int PAIR = 2 * RING + 2048 + 512;  // rings, partials, h tile
+  // Down: item (entry, 16 output rows) per warp, in the warp's own ring.
+  static constexpr int NGI = I / 64;
+  static constexpr int DROWB = I / 2;
+  static constexpr int DPITCH = DROWB + 32;
+  static constexpr int DWB = 16 * DPITCH;
+  static constexpr int DSB = 16 * NGI * 2;  // 16 rows of one scale tensor at group 64
+  static constexpr int DSLOT = DWB + 2 * DSB;
+  static constexpr int DRS = RING / DSLOT < 5 ? RING / DSLOT : 5;
+  // Shared memory: x fragments [NG][8][4][8] words, group sums [NG][8],
+  // entries, route flags, a few words, then the pair areas.
+  static constexpr int XF = NG * DEC_MAX_T * 4 * 8 * 4;
+  static constexpr int OFF_XS = XF;
+  static constexpr int OFF_ENT = OFF_XS + NG * DEC_MAX_T * 4;
+  static constexpr int OFF_OK = OFF_ENT + KL_MAX_ENT * (int)sizeof(DecEntry);
+  static constexpr int OFF_MISC = OFF_OK + KL_MAX_ROUTES * 4;
+  static constexpr int OFF_PAIR = align_c(OFF_MISC + 64, 128);
+  static constexpr int SMEM = OFF_PAIR + KL_PAIRS * PAIR;
+  // Router and routing temporaries, inside the pair areas (free until the
+  // entries are built): x [8][H] bf16, slot table, first route of each
+  // expert, routes (expert, slot, score, entry), reduction scratch.
+  static constexpr int TMP_TABLE = DEC_MAX_T * H * 2;
+  static constexpr int TMP_FIRST = TMP_TABLE + DEC_MAX_E * 4;
+  static constexpr int TMP_ROUTE = TMP_FIRST + DEC_MAX_E * 4;
+  static constexpr int TMP_RED = TMP_ROUTE + 4 * KL_MAX_ROUTES * 4;
+  static constexpr int TMP_PART = TMP_RED + KL_WARPS * DEC_MAX_T * 8;
+  static constexpr int TMP_END = TMP_PART + KL_WARPS * DEC_MAX_T * 4;
+  static_assert(TMP_END <= KL_PAIRS * PAIR, "router temporaries");
+  static_assert(SMEM <= 227 * 1024, "layer kernel shared memory");
+  static_assert(DRS >= 2 && CPH >= 1 && NVQ >= 1, "layer tile");
+};
+
+struct GateUpItem {
+  const uint8_t *gw, *uw;  // row block start of the gate and up codes
+  const uint8_t *sc[4];    // row block start of gate s, gate b, up s, up b
+};
+
+template <int H, int I>
+__device__ __forceinline__ void gateup_item(const VbQuantPool &pool, int slot, int rb, int gs,
+                                            GateUpItem &it) {
+  using Tl = LayerTile<H, I>;
+  const size_t sb = (size_t)rb * 16 * (Tl::NS64 >> gs) * 2;
+  it.gw = pool_ptr(pool, 0, slot) + (size_t)rb * 16 * Tl::ROWB;
+  it.uw = pool_ptr(pool, 3, slot) + (size_t)rb * 16 * Tl::ROWB;
+  it.sc[0] = pool_ptr(pool, 1, slot) + sb;
+  it.sc[1] = pool_ptr(pool, 2, slot) + sb;
+  it.sc[2] = pool_ptr(pool, 4, slot) + sb;
+  it.sc[3] = pool_ptr(pool, 5, slot) + sb;
+}
+
+// Chunk ch (codes and scales) of an item into a ring stage.
+template <int H, int I>
+__device__ __forceinline__ void gateup_chunk(uint8_t *stage, const GateUpItem &it, int ch,
+                                             int lane, int gs) {
+  using Tl = LayerTile<H, I>;
+  // 2 matrices x 16 rows x 8 pieces of 16 bytes; lane -> piece lane%8 of
+  // rows lane/8 + 4j.
+  const int r0 = lane >> 3, p16 = (lane & 7) * 16;
+  const uint8_t *g = it.gw + r0 * Tl::ROWB + ch * Tl::CROW + p16;
+  const uint8_t *u = it.uw + r0 * Tl::ROWB + ch * Tl::CROW + p16;
+  uint8_t *dg = stage + r0 * Tl::PITCH + p16;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    cp_async16(dg + 4 * j * Tl::PITCH, g + 4 * j * Tl::ROWB);
+    cp_async16(dg + 16 * Tl::PITCH + 4 * j * Tl::PITCH, u + 4 * j * Tl::ROWB);
+  }
+  // Scales: 4 tensors x 16 rows x SCB bytes -> [tensor][row][SCB].
+  const int ns = Tl::NS64 >> gs, scb = (Tl::CG >> gs) * 2;
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const int piece = lane + 32 * k, a = piece >> 4, r = piece & 15;
+    const uint8_t *src = it.sc[a] + r * ns * 2 + ch * scb;
+    uint8_t *dst = stage + Tl::WB + piece * scb;
+    if (scb == 8) cp_async8(dst, src);
+    else cp_async4(dst, src);
+  }
+}
+
+// Weights of down item (slot, 16-row block rb) into a ring slot:
+// [16 rows x DPITCH] codes, then [16 rows x NSI] scales and biases.
+template <int H, int I>
+__device__ __forceinline__ void down_issue(uint8_t *slot, const VbQuantPool &pool, int pslot,
+                                           int rb, int lane, int gs) {
+  using Tl = LayerTile<H, I>;
+  const uint8_t *dw = pool_ptr(pool, 6, pslot) + (size_t)rb * 16 * Tl::DROWB;
+  constexpr int CPR = Tl::DROWB / 16;  // 16-byte chunks per row
+#pragma unroll
+  for (int j = 0; j < 16 * CPR / 32; ++j) {
+    const int q = lane + 32 * j, r = q / CPR, c16 = (q % CPR) * 16;
+    cp_async16(slot + r * Tl::DPITCH + c16, dw + r * Tl::DROWB + c16);
+  }
+  const int sb = 16 * (Tl::NGI >> gs) * 2, sch = sb / 16;
+  for (int q = lane; q < 2 * sch; q += 32) {
+    const int t = q / sch, cc = q % sch;
+    cp_async16(slot + Tl::DWB + t * sb + cc * 16,
+               pool_ptr(pool, 7 + t, pslot) + (size_t)rb * sb + cc * 16);
+  }
+}
+
+// Rank-order combine of 8 rows of one 16-row block (rows 16 rb + 8 (lane & 1))
+// for tokens t = ((lane >> 1) & 3) + 4 j: a warp combines four blocks at
+// once (lane >> 3 picks the block). Every load of a pass is issued before
+// the first add. ok: route flags [T][k] (shared memory).
+__device__ __forceinline__ void down_combine_rows(const DecodeParams &p, const int32_t *ok,
+                                                  int rb, int lane) {
+  const int T = p.T, H = p.H, k = p.k;
+  const uint16_t *wp = wsp<const uint16_t>(p, p.L.wparts);
+  const int row = 16 * rb + 8 * (lane & 1);
+#pragma unroll 1
+  for (int t = (lane >> 1) & 3; t < T; t += 4) {
+    uint4 v[DEC_MAX_K];
+#pragma unroll
+    for (int j = 0; j < DEC_MAX_K; ++j)
+      if (j < k) v[j] = __ldcg(reinterpret_cast<const uint4 *>(wp + ((size_t)t * k + j) * H + row));
+    const size_t oi = (size_t)t * H + row;
+    float gate = 0.f;
+    uint4 sw = make_uint4(0, 0, 0, 0), rr = sw;
+    if (p.has_shared) {
+      gate = __ldcg(wsp<const float>(p, p.L.sgate) + t);
+      sw = __ldcg(reinterpret_cast<const uint4 *>(wsp<const uint16_t>(p, p.L.sparts) + oi));
+    }
+    if (p.residual) rr = __ldg(reinterpret_cast<const uint4 *>(p.residual + oi));
+    double s[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) s[q] = 0.0;
+#pragma unroll
+    for (int j = 0; j < DEC_MAX_K; ++j) {
+      if (j < k && ok[t * k + j]) {
+        const uint32_t w[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          s[2 * q] += (double)bf2f(w[q] & 0xFFFFu);
+          s[2 * q + 1] += (double)bf2f(w[q] >> 16);
+        }
+      }
+    }
+    const uint32_t sh[4] = {sw.x, sw.y, sw.z, sw.w};
+    const uint32_t re[4] = {rr.x, rr.y, rr.z, rr.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float y0 = rbf((float)s[2 * q]), y1 = rbf((float)s[2 * q + 1]);
+      if (p.has_shared) {
+        y0 = rbf(__fadd_rn(y0, rbf(__fmul_rn(gate, bf2f(sh[q] & 0xFFFFu)))));
+        y1 = rbf(__fadd_rn(y1, rbf(__fmul_rn(gate, bf2f(sh[q] >> 16)))));
+      }
+      if (p.residual) {
+        y0 = rbf(__fadd_rn(bf2f(re[q] & 0xFFFFu), y0));
+        y1 = rbf(__fadd_rn(bf2f(re[q] >> 16), y1));
+      }
+      o[q] = (uint32_t)f2bf(y0) | ((uint32_t)f2bf(y1) << 16);
+    }
+    *reinterpret_cast<uint4 *>(p.out + oi) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// Routing of all T tokens, run identically by every CTA of the layer kernel
+// (all 256 threads call it): precise softmax of the logits, top-k, optional
+// renormalisation, slot gather, then the entry list. Results in shared
+// memory (routes rex/rslot/rscore/rent, flags ok, entries ent); the
+// returned value is the number of entries. primary: this CTA also writes the
+// optional outputs and the status bits.
+template <int PER>  // PER = ceil(E / 32) logits per lane
+__device__ __noinline__ int route_tokens(const float *logits, const int32_t *table, int T, int E,
+                                         int k, int norm_topk, int has_shared, int cap,
+                                         bool primary, int32_t *status, int32_t *out_inds,
+                                         uint16_t *out_scores, int32_t *out_local,
+                                         int *s_table, int *s_first, int *s_rex, int *s_rslot,
+                                         float *s_rscore, int *s_rent, int32_t *s_ok,
+                                         DecEntry *s_ent, int *s_wcnt) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  SpanTrace span(p.trace, 0);
-
-  // This warp's row part; row E is the shared-expert gate.
-  const int rloc = warp / Q, part = warp % Q;
-  const int row = blockIdx.x * RPC + rloc;
-  const int nrows = E + (p.has_shared ? 1 : 0);
-  uint4 wv[NVQ];
-  if (row < nrows) {
-    const uint16_t *src = row < E ? p.router_w + (size_t)row * H : p.shared_gate_w;
-    const uint4 *w4 = reinterpret_cast<const uint4 *>(src + part * (H / Q));
-#pragma unroll
-    for (int u = 0; u < NVQ; ++u) wv[u] = ldg_nc_v4(w4 + u * 32 + lane);
-  }
-  if (blockIdx.x == 0 && tid * 32 < E) prefetch_l2(p.table + tid * 32);  // slot table lines
-  pdl_wait();
-  pdl_launch_dependents();
-  trace_mark(p.trace, 8);
-
-  {
-    // Stage x: independent 16-byte loads issued before the stores.
-    const uint4 *src = reinterpret_cast<const uint4 *>(p.x);
-    uint4 *dst = reinterpret_cast<uint4 *>(xs);
-    constexpr int PT = (DEC_MAX_T * H / 8 + K1_THREADS - 1) / K1_THREADS;
-    const int nvec = T * (H / 8);
-    uint4 v[PT];
-#pragma unroll
-    for (int u = 0; u < PT; ++u) {
-      const int i = u * K1_THREADS + tid;
-      if (i < nvec) v[u] = __ldcg(src + i);
-    }
-#pragma unroll
-    for (int u = 0; u < PT; ++u) {
-      const int i = u * K1_THREADS + tid;
-      if (i < nvec) dst[i] = v[u];
-    }
-  }
-  __syncthreads();
-  trace_mark(p.trace, 11);
-  if (p.norm_eps > 0.f) {
-    // Unit-weight RMSNorm of the block input (decoder post-attention norm):
-    // y = bf16(x * (1/sqrt(mean(x^2) + eps))), float32 math with an exact
-    // (double) sum of squares: squares of bf16 values have 16 significant
-    // bits, so their double sum does not depend on the order. Every CTA
-    // computes it identically.
-    constexpr int VPT = H / 8;  // uint4 per token
-    double ss[DEC_MAX_T];
-#pragma unroll
-    for (int t = 0; t < DEC_MAX_T; ++t) ss[t] = 0.0;
-#pragma unroll
-    for (int t = 0; t < DEC_MAX_T; ++t) {
-      if (t < T) {
-        for (int v = tid; v < VPT; v += K1_THREADS) {
-          const uint4 q = reinterpret_cast<const uint4 *>(xs + (size_t)t * H)[v];
-          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const double a = bf2f(w[j] & 0xFFFF), b = bf2f(w[j] >> 16);
-            ss[t] = fma(a, a, ss[t]);
-            ss[t] = fma(b, b, ss[t]);
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss[t] += __shfl_xor_sync(0xffffffffu, ss[t], o);
-        if (lane == 0) s_ss[warp][t] = ss[t];
-      }
-    }
-    __syncthreads();
-    if (tid < T) {
-      double tot = 0.0;
-#pragma unroll
-      for (int w = 0; w < K1_WARPS; ++w) tot += s_ss[w][tid];
-      const float ms = __fdiv_rn((float)tot, (float)H);
-      s_inv[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.norm_eps)));
-    }
-    __syncthreads();
-    for (int i = tid; i < T * (H / 8); i += K1_THREADS) {
-      const int t = i / (H / 8);
-      uint4 v = reinterpret_cast<const uint4 *>(xs)[i];
-      uint32_t w[4] = {v.x, v.y, v.z, v.w};
-      const float inv = s_inv[t];
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        w[q] = pack_bf2(__fmul_rn(bf2f(w[q] & 0xFFFF), inv), __fmul_rn(bf2f(w[q] >> 16), inv));
-      reinterpret_cast<uint4 *>(xs)[i] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-    __syncthreads();
-  }
-  trace_mark(p.trace, 12);
-
-  if (row < nrows) {
-    float acc[DEC_MAX_T];
-#pragma unroll
-    for (int t = 0; t < DEC_MAX_T; ++t) acc[t] = 0.f;
-#pragma unroll
-    for (int u = 0; u < NVQ; ++u) {
-      const int v = part * (H / Q / 8) + u * 32 + lane;
-      const uint32_t wr[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
-#pragma unroll
-      for (int t = 0; t < DEC_MAX_T; ++t) {
-        if (t < T) {
-          const uint4 xv = reinterpret_cast<const uint4 *>(xs + (size_t)t * H)[v];
-          const uint32_t xr[4] = {xv.x, xv.y, xv.z, xv.w};
-          float a = acc[t];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            a = fmaf(bf2f(wr[q] & 0xFFFF), bf2f(xr[q] & 0xFFFF), a);
-            a = fmaf(bf2f(wr[q] >> 16), bf2f(xr[q] >> 16), a);
-          }
-          acc[t] = a;
-        }
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < DEC_MAX_T; ++t) {
-      if (t < T) {
-        float a = acc[t];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-        if (lane == 0) s_part[rloc][part][t] = a;
-      }
-    }
-  }
-  __syncthreads();
-  if (tid < RPC * DEC_MAX_T) {
-    const int rl = tid / DEC_MAX_T, t = tid % DEC_MAX_T;
-    const int r = blockIdx.x * RPC + rl;
-    if (r < nrows && t < T) {
-      float a = 0.f;
-#pragma unroll
-      for (int q = 0; q < Q; ++q) a += s_part[rl][q][t];
-      if (r < E) {
-        if (p.router_bias) a = a + p.router_bias[r];
-        wsp<float>(p, p.L.logits)[(size_t)t * E + r] = rbf(a);
-      } else {
-        wsp<float>(p, p.L.sgate)[t] = rbf(mlx_sigmoid(rbf(a)));
-      }
-    }
-  }
-  trace_mark(p.trace, 13);
-
-  {
-    // x in MMA fragment order (xperm) and per-64-column sums (xsum), spread
-    // over all CTAs (each holds the whole normalised x in shared memory).
-    uint32_t *xperm = wsp<uint32_t>(p, p.L.xperm);
-    const int gtid = blockIdx.x * blockDim.x + tid, gstride = gridDim.x * blockDim.x;
-    for (int i = gtid; i < T * (H / 2); i += gstride) {
-      const int n = i / (H / 2);
-      const int r = i % (H / 2);
-      const int G = r >> 5, c = (r >> 3) & 3, w = r & 7;
-      const int m = w >> 1, pp = w & 1, j = m >> 1, i0 = 2 * (m & 1);
-      const int base = 64 * G + 16 * c + 8 * j + i0 + pp;
-      const uint32_t lo = xs[(size_t)n * H + base], hi = xs[(size_t)n * H + base + 4];
-      xperm[i] = lo | (hi << 16);
-    }
-    float *xsum = wsp<float>(p, p.L.xsum);
-    const int gwarp = blockIdx.x * K1_WARPS + warp;
-    const int nwarps = gridDim.x * K1_WARPS;
-    for (int it = gwarp; it < T * NG; it += nwarps) {
-      const int n = it / NG, G = it % NG;
-      const uint32_t v = reinterpret_cast<const uint32_t *>(xs + (size_t)n * H + 64 * G)[lane];
-      float s = bf2f(v & 0xFFFF) + bf2f(v >> 16);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-      if (lane == 0) xsum[it] = s;
-    }
-  }
-
-  // Last-CTA ticket.
-  __shared__ unsigned s_ticket;
-  trace_mark(p.trace, 9);
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_ticket = atomicAdd(wsp<unsigned>(p, p.L.counter), 1u);
-  __syncthreads();
-  if (s_ticket != gridDim.x - 1) {
-    span.end();
-    return;
-  }
-  __threadfence();
-  trace_mark(p.trace, 10);
-
-  // ---- softmax + top-k per token (one warp per token) ----
-  __shared__ int s_ex[DEC_MAX_T * DEC_MAX_K];
-  __shared__ int s_slot[DEC_MAX_T * DEC_MAX_K];
-  __shared__ float s_score[DEC_MAX_T * DEC_MAX_K];
-  __shared__ int s_first[DEC_MAX_E];  // first route of each expert
-  __shared__ int s_ent[DEC_MAX_T * DEC_MAX_K];
-  __shared__ int s_wcnt[K1_WARPS];
-  __shared__ __align__(16) DecEntry s_entries[DEC_MAX_T * DEC_MAX_K + 1];
-  __shared__ int s_table[DEC_MAX_E];
-  const int k = p.k;
-  const float *logits = wsp<float>(p, p.L.logits);
   // Slot table and logits are loaded together (one memory round trip).
   float v[PER];
   {
     const int t = warp;
-    int tb[(DEC_MAX_E + K1_THREADS - 1) / K1_THREADS];
+    int tb[(DEC_MAX_E + KL_THREADS - 1) / KL_THREADS];
 #pragma unroll
-    for (int j = 0; j < (DEC_MAX_E + K1_THREADS - 1) / K1_THREADS; ++j) {
-      const int i = tid + j * K1_THREADS;
-      tb[j] = i < E ? __ldg(p.table + i) : -1;
+    for (int j = 0; j < (DEC_MAX_E + KL_THREADS - 1) / KL_THREADS; ++j) {
+      const int i = tid + j * KL_THREADS;
+      tb[j] = i < E ? __ldg(table + i) : -1;
     }
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
@@ -418,8 +434,8 @@ __global__ void __launch_bounds__(K1_THREADS, 2) moe_router_kernel(DecodeParams 
       v[i] = (t < T && idx < E) ? __ldcg(logits + (size_t)t * E + idx) : -INFINITY;
     }
 #pragma unroll
-    for (int j = 0; j < (DEC_MAX_E + K1_THREADS - 1) / K1_THREADS; ++j) {
-      const int i = tid + j * K1_THREADS;
+    for (int j = 0; j < (DEC_MAX_E + KL_THREADS - 1) / KL_THREADS; ++j) {
+      const int i = tid + j * KL_THREADS;
       if (i < E) {
         s_table[i] = tb[j];
         s_first[i] = 0x7fffffff;
@@ -427,7 +443,7 @@ __global__ void __launch_bounds__(K1_THREADS, 2) moe_router_kernel(DecodeParams 
     }
   }
   __syncthreads();
-  for (int t = warp; t < T; t += K1_WARPS) {
+  for (int t = warp; t < T; t += KL_WARPS) {
     uint32_t mk = 0;
 #pragma unroll
     for (int i = 0; i < PER; ++i) mk = max(mk, f2key(v[i]));
@@ -477,7 +493,7 @@ __global__ void __launch_bounds__(K1_THREADS, 2) moe_router_kernel(DecodeParams 
     }
     const float sel_p = bf2f(sel >> 16);
     float score = sel_p;
-    if (p.norm_topk) {
+    if (norm_topk) {
       const float denom = rbf((float)ssum);
       score = rbf(__fdiv_rn(sel_p, denom));
     }
@@ -486,684 +502,689 @@ __global__ void __launch_bounds__(K1_THREADS, 2) moe_router_kernel(DecodeParams 
       int slot = -1;
       if (ex >= 0 && ex < E) {
         slot = s_table[ex];
-        if (slot >= p.pool.cap) {
-          flag_status(p.status, VB_STATUS_BOUNDS);
+        if (slot >= cap) {
+          if (primary) flag_status(status, VB_STATUS_BOUNDS);
           slot = -1;
         } else if (slot < 0) {
-          flag_status(p.status, VB_STATUS_MISS);
+          if (primary) flag_status(status, VB_STATUS_MISS);
           slot = -1;
         }
-      } else {
-        flag_status(p.status, VB_STATUS_BOUNDS);
+      } else if (primary) {
+        flag_status(status, VB_STATUS_BOUNDS);
       }
-      s_ex[t * k + lane] = ex;
-      s_slot[t * k + lane] = slot;
-      s_score[t * k + lane] = score;
-      wsp<int32_t>(p, p.L.route_ok)[t * k + lane] = slot >= 0 ? 1 : 0;
-      if (p.out_inds) p.out_inds[t * k + lane] = ex;
-      if (p.out_scores) p.out_scores[t * k + lane] = f2bf(score);
-      if (p.out_local) p.out_local[t * k + lane] = slot;
+      s_rex[t * k + lane] = ex;
+      s_rslot[t * k + lane] = slot;
+      s_rscore[t * k + lane] = score;
+      s_ok[t * k + lane] = slot >= 0 ? 1 : 0;
+      if (primary) {
+        if (out_inds) out_inds[t * k + lane] = ex;
+        if (out_scores) out_scores[t * k + lane] = f2bf(score);
+        if (out_local) out_local[t * k + lane] = slot;
+      }
     }
   }
   __syncthreads();
-  trace_mark(p.trace, 14);
 
-  // ---- entries: shared expert first, then one entry per distinct routed
-  // expert in route order (t-major, rank-minor): the first route of each
-  // expert is found with an atomic minimum, first routes are numbered with
-  // ballots, and every route fills its (entry, token) cell.
+  // Entries: shared expert first, then one entry per distinct routed expert
+  // in route order (t-major, rank-minor): the first route of each expert is
+  // found with an atomic minimum, first routes are numbered with ballots,
+  // and every route fills its (entry, token) cell.
   const int R = T * k;
-  const int shared_n = p.has_shared ? 1 : 0;
+  const int shared_n = has_shared ? 1 : 0;
   const int r = tid;
-  const bool valid = r < R && s_slot[r] >= 0;
-  if (valid) atomicMin(&s_first[s_ex[r]], r);
-  // Entry table defaults: slot -1 / rank -1.
-  for (int i = tid; i < (R + 1) * (int)(sizeof(DecEntry) / 4); i += K1_THREADS) {
+  const bool valid = r < R && s_rslot[r] >= 0;
+  if (valid) atomicMin(&s_first[s_rex[r]], r);
+  for (int i = tid; i < (R + 1) * (int)(sizeof(DecEntry) / 4); i += KL_THREADS) {
     const int f = i % (int)(sizeof(DecEntry) / 4);  // field word
-    reinterpret_cast<int32_t *>(s_entries)[i] = (f >= 4 && f < 12) ? -1 : 0;
+    reinterpret_cast<int32_t *>(s_ent)[i] = (f >= 4 && f < 12) ? -1 : 0;
   }
   __syncthreads();
-  const bool is_first = valid && s_first[s_ex[r]] == r;
+  const bool is_first = valid && s_first[s_rex[r]] == r;
   const unsigned bal = __ballot_sync(0xffffffffu, is_first);
   if (lane == 0) s_wcnt[warp] = __popc(bal);
   __syncthreads();
   if (is_first) {
     int idx = shared_n + __popc(bal & ((1u << lane) - 1u));
     for (int w = 0; w < warp; ++w) idx += s_wcnt[w];
-    s_ent[r] = idx;
+    s_rent[r] = idx;
   }
   int n_routed = 0;
 #pragma unroll
-  for (int w = 0; w < K1_WARPS; ++w) n_routed += s_wcnt[w];
+  for (int w = 0; w < KL_WARPS; ++w) n_routed += s_wcnt[w];
   __syncthreads();
   if (valid) {
-    const int ei = s_ent[s_first[s_ex[r]]];
+    const int ei = s_rent[s_first[s_rex[r]]];
     const int tt = r / k, jj = r - tt * k;
-    s_entries[ei].slot = s_slot[r];
-    s_entries[ei].rank[tt] = jj;
-    s_entries[ei].score[tt] = s_score[r];
+    s_ent[ei].slot = s_rslot[r];
+    s_ent[ei].rank[tt] = jj;
+    s_ent[ei].score[tt] = s_rscore[r];
   }
-  if (tid == 0 && p.has_shared) {
-    s_entries[0].slot = 0;
-    s_entries[0].flags = 1;
-    for (int q = 0; q < T; ++q) { s_entries[0].rank[q] = 0; s_entries[0].score[q] = 1.f; }
+  if (tid == 0 && has_shared) {
+    s_ent[0].slot = 0;
+    s_ent[0].flags = 1;
+    for (int q = 0; q < T; ++q) {
+      s_ent[0].rank[q] = 0;
+      s_ent[0].score[q] = 1.f;
+    }
   }
   __syncthreads();
-  const int n = shared_n + n_routed;
-  trace_mark(p.trace, 15);
-  const int words = n * (int)(sizeof(DecEntry) / 4);
-  int32_t *dst = wsp<int32_t>(p, p.L.entries);
-  for (int i = tid; i < words; i += K1_THREADS)
-    dst[i] = reinterpret_cast<const int32_t *>(s_entries)[i];
-  if (tid == 0) {
-    *wsp<int32_t>(p, p.L.n_entries) = n;
-    *wsp<unsigned>(p, p.L.counter) = 0u;  // ready for the next launch
-  }
-  span.end();
+  return shared_n + n_routed;
 }
 
 // ----------------------------------------------------------------------------
-// K2: gate/up + SwiGLU. Persistent CTAs of W warps; an item (entry, 16
-// intermediate rows) is split over the hidden dimension between the two
-// warps of a pair, and each warp streams its half through its own cp.async
-// ring of chunks (16 rows x 4 groups of 64 columns of gate and up plus their
-// scales and biases; rows padded so that the MMA fragment reads hit distinct
-// banks), RS-1 chunks ahead of the math. Item i runs on CTA i % grid, so
-// every SM gets the same share. The odd warp hands its partial sums to the
-// even one through shared memory (one named barrier per pair and item), which
-// adds them in half order and applies SwiGLU (bf16 per op); h goes out in MMA
-// fragment order for the down projection. Weights are the A operand of
-// mma.m16n8k16 (4-bit codes as exact bf16 128+q, one LOP3 per pair), tokens
-// the 8 B columns; per 64-column group y += s*D + (b - 128*s)*sum(x). x in
-// fragment order and its group sums sit in shared memory for all warps. The
-// shared expert's first chunks are requested before the PDL wait.
+// The layer kernel. Trace slots (optional): 0/1 span; latest CTA past the
+// PDL wait (2), done with its router rows (3), past the grid barrier (4),
+// done with routing (5); latest warp done with gate/up (6), with its down
+// items (7), with its combines (8).
 // ----------------------------------------------------------------------------
-constexpr int K2_SMEM_MAX = 225 * 1024;
+template <int H, int I>
+__global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p) {
+  using Tl = LayerTile<H, I>;
+  constexpr int Q = Tl::Q, RPC = Tl::RPC, NVQ = Tl::NVQ, NG = Tl::NG, CG = Tl::CG,
+                CPH = Tl::CPH, RS = Tl::RS, NGI = Tl::NGI, DRS = Tl::DRS;
+  constexpr int RB = I / 16;    // gate/up items per entry
+  constexpr int RBN = H / 16;   // down items per entry
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint32_t *xf = reinterpret_cast<uint32_t *>(smem);  // [NG][8][4][8] words
+  float *xsm = reinterpret_cast<float *>(smem + Tl::OFF_XS);  // [NG][8]
+  DecEntry *s_ent = reinterpret_cast<DecEntry *>(smem + Tl::OFF_ENT);
+  int32_t *s_ok = reinterpret_cast<int32_t *>(smem + Tl::OFF_OK);
+  int *s_misc = reinterpret_cast<int *>(smem + Tl::OFF_MISC);
+  uint8_t *pairs = smem + Tl::OFF_PAIR;
+  uint16_t *xb = reinterpret_cast<uint16_t *>(pairs);  // [T][H] bf16 (router phase)
+  double *s_dred = reinterpret_cast<double *>(pairs + Tl::TMP_RED);
+  float *s_part = reinterpret_cast<float *>(pairs + Tl::TMP_PART);
+  __shared__ float s_inv[DEC_MAX_T];
+  __shared__ int s_wcnt[KL_WARPS];
+  __shared__ unsigned long long s_tm[3];
 
-template <int H, int GS>  // GS: log2(group / 64)
-struct GateUpTile {
-  static constexpr int NG = H / 64;           // 64-column groups per row
-  static constexpr int CG = 4;                // groups per chunk
-  static constexpr int NCH = NG / CG;         // chunks per row block
-  static constexpr int CPH = NCH / 2;         // chunks per half
-  static constexpr int ROWB = H / 2;          // packed bytes per row
-  static constexpr int CROW = CG * 32;        // chunk bytes per row (128)
-  static constexpr int PITCH = CROW + 32;     // padded chunk row pitch
-  static constexpr int NS = H >> (6 + GS);    // scales per row
-  static constexpr int SCB = (CG >> GS) * 2;  // scale bytes per row per chunk
-  static constexpr int WB = 2 * 16 * PITCH;   // gate + up codes of a chunk
-  static constexpr int CHUNK = WB + 4 * 16 * SCB;
-  static constexpr int RS = 3;                // ring stages per warp
-  static constexpr int XB = NG * DEC_MAX_T * 4 * 8 * 4 + NG * DEC_MAX_T * 4;  // x frags, sums
-  // Per warp pair: two rings, the odd warp's partials (2 slots x 32 lanes x
-  // 8 floats) and the h tile (16 rows x 8 tokens).
-  static constexpr int PER_PAIR = 2 * RS * CHUNK + 2048 + 512;
-  static constexpr int P_FIT = (K2_SMEM_MAX - XB) / PER_PAIR;
-  static constexpr int WARPS = 2 * (P_FIT < 6 ? P_FIT : 6);
-  static constexpr int THREADS = 32 * WARPS;
-  static constexpr int SMEM = XB + (WARPS / 2) * PER_PAIR;
-  static_assert(CPH >= 1 && WARPS >= 2 && (WARPS & 1) == 0, "gate/up tile");
-};
-
-// Load 2*count bytes of bf16 scales (count in {1,2,4,8}) into a uint4.
-__device__ __forceinline__ uint4 ld_scales(const uint16_t *ptr, int count) {
-  uint4 r = make_uint4(0, 0, 0, 0);
-  if (count >= 8) {
-    r = __ldg(reinterpret_cast<const uint4 *>(ptr));
-  } else if (count == 4) {
-    const uint2 v = __ldg(reinterpret_cast<const uint2 *>(ptr));
-    r.x = v.x;
-    r.y = v.y;
-  } else if (count == 2) {
-    r.x = __ldg(reinterpret_cast<const unsigned *>(ptr));
-  } else {
-    r.x = __ldg(ptr);
-  }
-  return r;
-}
-__device__ __forceinline__ float bf_at(const uint4 &v, int i) {
-  const uint32_t w = i < 2 ? v.x : (i < 4 ? v.y : (i < 6 ? v.z : v.w));
-  return bf2f((i & 1) ? (w >> 16) : (w & 0xFFFF));
-}
-__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
-// bf16 at index i (0..3) of a 2-word vector.
-__device__ __forceinline__ float bf_at2(const uint2 &v, int i) {
-  const uint32_t w = i < 2 ? v.x : v.y;
-  return (i & 1) ? bf_hi(w) : bf_lo(w);
-}
-
-struct GateUpItem {
-  const uint8_t *gw, *uw;  // row block start of the gate and up codes
-  const uint8_t *sc[4];    // row block start of gate s, gate b, up s, up b
-};
-
-template <int H, int GS>
-__device__ __forceinline__ void gateup_item(const VbQuantPool &pool, int slot, int rb,
-                                            GateUpItem &it) {
-  using Tl = GateUpTile<H, GS>;
-  it.gw = pool_ptr(pool, 0, slot) + (size_t)rb * 16 * Tl::ROWB;
-  it.uw = pool_ptr(pool, 3, slot) + (size_t)rb * 16 * Tl::ROWB;
-  it.sc[0] = pool_ptr(pool, 1, slot) + (size_t)rb * 16 * Tl::NS * 2;
-  it.sc[1] = pool_ptr(pool, 2, slot) + (size_t)rb * 16 * Tl::NS * 2;
-  it.sc[2] = pool_ptr(pool, 4, slot) + (size_t)rb * 16 * Tl::NS * 2;
-  it.sc[3] = pool_ptr(pool, 5, slot) + (size_t)rb * 16 * Tl::NS * 2;
-}
-
-// Chunk ch (codes and scales) of an item into a ring stage.
-template <int H, int GS>
-__device__ __forceinline__ void gateup_chunk(uint8_t *stage, const GateUpItem &it, int ch,
-                                             int lane) {
-  using Tl = GateUpTile<H, GS>;
-  // 2 matrices x 16 rows x 8 pieces of 16 bytes; lane -> piece lane%8 of
-  // rows lane/8 + 4j.
-  const int r0 = lane >> 3, p16 = (lane & 7) * 16;
-  const uint8_t *g = it.gw + r0 * Tl::ROWB + ch * Tl::CROW + p16;
-  const uint8_t *u = it.uw + r0 * Tl::ROWB + ch * Tl::CROW + p16;
-  uint8_t *dg = stage + r0 * Tl::PITCH + p16;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    cp_async16(dg + 4 * j * Tl::PITCH, g + 4 * j * Tl::ROWB);
-    cp_async16(dg + 16 * Tl::PITCH + 4 * j * Tl::PITCH, u + 4 * j * Tl::ROWB);
-  }
-  // Scales: 4 tensors x 16 rows x SCB bytes -> [tensor][row][SCB].
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int piece = lane + 32 * k, a = piece >> 4, r = piece & 15;
-    const uint8_t *src = it.sc[a] + r * Tl::NS * 2 + ch * Tl::SCB;
-    uint8_t *dst = stage + Tl::WB + piece * Tl::SCB;
-    if (Tl::SCB == 8) cp_async8(dst, src);
-    else cp_async4(dst, src);
-  }
-}
-
-__device__ __forceinline__ void named_bar(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-template <int H, int GS>
-__global__ void __launch_bounds__(GateUpTile<H, GS>::THREADS, 1) moe_gateup_kernel(DecodeParams p) {
-  using Tl = GateUpTile<H, GS>;
-  constexpr int NG = Tl::NG, CG = Tl::CG, CPH = Tl::CPH, RS = Tl::RS, W = Tl::WARPS;
-  constexpr int PAIRS = W / 2;
-  extern __shared__ __align__(16) uint8_t smem[];
-  uint32_t *xf = reinterpret_cast<uint32_t *>(smem);                         // [NG][8][4][8] words
-  float *xsm = reinterpret_cast<float *>(smem + NG * DEC_MAX_T * 4 * 8 * 4);  // [NG][8]
-  __shared__ int s_slot[DEC_MAX_T * DEC_MAX_K + 1];
-  __shared__ int s_n;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int T = p.T;
-  SpanTrace span(p.trace, 1);
-  const int pair = warp >> 1, half = warp & 1;
-  uint8_t *pbase = smem + Tl::XB + pair * Tl::PER_PAIR;
-  uint8_t *ring = pbase + half * RS * Tl::CHUNK;
-  float *red = reinterpret_cast<float *>(pbase + 2 * RS * Tl::CHUNK);  // [2][32][8]
-  float *hbuf = red + 2 * 32 * 8;                                        // [16][8]
-  const int rb_shift = 31 - __clz(p.I / 16);  // row blocks per entry = I/16
-  const int RB = 1 << rb_shift;
-  const int grid = gridDim.x;
-  // This pair's items: blockIdx.x + grid * (pair + PAIRS * r), r = 0, 1, ...
-  const int first = blockIdx.x + grid * pair, step = grid * PAIRS;
+  const int T = p.T, E = p.E, gs = p.gshift;
+  const int G = gridDim.x;
+  SpanTrace span(p.trace);
 
-  GateUpItem cur;
-  int issue_q = 0;
-  auto issue_next = [&](int n_items) {
-    const int r = issue_q / CPH, ch = half * CPH + issue_q % CPH;
-    const int i = first + r * step;
-    if (i < n_items) {
-      if (issue_q % CPH == 0) {
-        const int e = i >> rb_shift;
-        if (p.has_shared && e == 0) gateup_item<H, GS>(p.shared, 0, i & (RB - 1), cur);
-        else gateup_item<H, GS>(p.pool, s_slot[e], i & (RB - 1), cur);
-      }
-      gateup_chunk<H, GS>(ring + (issue_q % RS) * Tl::CHUNK, cur, ch, lane);
-    }
-    cp_async_commit();
-    ++issue_q;
+  // ---------------- 1. before the PDL wait ----------------
+  const int nrows = E + p.has_shared;
+  const int rloc = warp / Q, part = warp % Q;
+  uint4 wv[NVQ];
+  auto load_row = [&](int row) {
+    const uint16_t *src = row < E ? p.router_w + (size_t)row * H : p.shared_gate_w;
+    const uint4 *w4 = reinterpret_cast<const uint4 *>(src + part * (H / Q));
+#pragma unroll
+    for (int u = 0; u < NVQ; ++u) wv[u] = ldg_nc_v4(w4 + u * 32 + lane);
   };
-
-  // The shared expert (entry 0) needs no routing: its chunks go first.
-  const bool pre = p.has_shared && first < RB;
-  if (pre) {
-#pragma unroll 1
-    for (int k = 0; k < RS - 1; ++k) issue_next(first + 1);
+  if (blockIdx.x * RPC + rloc < nrows) load_row(blockIdx.x * RPC + rloc);
+  if (blockIdx.x == 0 && tid * 32 < E) prefetch_l2(p.table + tid * 32);
+  if (p.has_shared && lane == 0) {
+    const int piece = blockIdx.x * KL_WARPS + warp;
+    if (piece < expert_pieces(p)) prefetch_expert_piece(p, p.shared, 0, piece);
   }
+  if (tid < 3) s_tm[tid] = 0ull;
   pdl_wait();
   pdl_launch_dependents();
-  const int max_e = p.L.max_entries;
-  if (tid == 0) s_n = *wsp<const int32_t>(p, p.L.n_entries);
-  for (int i = tid; i < max_e; i += blockDim.x) s_slot[i] = wsp<const DecEntry>(p, p.L.entries)[i].slot;
+  trace_mark(p.trace, 2);
+
+  // ---------------- 2. x, RMSNorm, fragments, router rows ----------------
   {
-    // x fragments [token][group][c][8 words] -> [group][token][c][8 words],
-    // group sums [token][group] -> [group][8] (zero beyond T).
-    const uint4 *src = reinterpret_cast<const uint4 *>(wsp<const uint32_t>(p, p.L.xperm));
-    uint4 *dst = reinterpret_cast<uint4 *>(xf);
-    for (int u = tid; u < T * NG * 8; u += blockDim.x) {
-      const int n = u / (NG * 8), rest = u % (NG * 8), G = rest >> 3, k = rest & 7;
-      dst[(G * DEC_MAX_T + n) * 8 + k] = __ldcg(src + u);
+    const uint4 *src = reinterpret_cast<const uint4 *>(p.x);
+    uint4 *dst = reinterpret_cast<uint4 *>(xb);
+    constexpr int PT = (DEC_MAX_T * H / 8 + KL_THREADS - 1) / KL_THREADS;
+    const int nvec = T * (H / 8);
+    uint4 v[PT];
+#pragma unroll
+    for (int u = 0; u < PT; ++u) {
+      const int i = u * KL_THREADS + tid;
+      if (i < nvec) v[u] = __ldcg(src + i);
     }
-    const float *xs = wsp<const float>(p, p.L.xsum);
-    for (int i = tid; i < NG * DEC_MAX_T; i += blockDim.x) {
-      const int G = i >> 3, n = i & 7;
-      xsm[i] = n < T ? __ldcg(xs + n * NG + G) : 0.f;
+#pragma unroll
+    for (int u = 0; u < PT; ++u) {
+      const int i = u * KL_THREADS + tid;
+      if (i < nvec) dst[i] = v[u];
     }
+  }
+  if (blockIdx.x == 0)  // entry counters of this launch (all counting follows the grid barrier)
+    for (int i = tid; i < p.L.max_entries; i += KL_THREADS) wsp<unsigned>(p, p.L.ent_done)[i] = 0u;
+  __syncthreads();
+  if (p.norm_eps > 0.f) {
+    // Unit-weight RMSNorm of the block input (decoder post-attention norm):
+    // y = bf16(x * (1/sqrt(mean(x^2) + eps))), float32 math with an exact
+    // (double) sum of squares: squares of bf16 values have 16 significant
+    // bits, so their double sum does not depend on the order.
+    constexpr int VPT = H / 8;  // uint4 per token
+    double ss[DEC_MAX_T];
+#pragma unroll
+    for (int t = 0; t < DEC_MAX_T; ++t) ss[t] = 0.0;
+    for (int v = tid; v < VPT; v += KL_THREADS) {
+#pragma unroll
+      for (int t = 0; t < DEC_MAX_T; ++t) {
+        if (t < T) {
+          const uint4 q = reinterpret_cast<const uint4 *>(xb + (size_t)t * H)[v];
+          const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const double a = bf2f(w[j] & 0xFFFF), b = bf2f(w[j] >> 16);
+            ss[t] = fma(a, a, ss[t]);
+            ss[t] = fma(b, b, ss[t]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int t = 0; t < DEC_MAX_T; ++t) ss[t] += __shfl_xor_sync(0xffffffffu, ss[t], o);
+    if (lane == 0)
+#pragma unroll
+      for (int t = 0; t < DEC_MAX_T; ++t) s_dred[warp * DEC_MAX_T + t] = ss[t];
+    __syncthreads();
+    if (tid < T) {
+      double tot = 0.0;
+#pragma unroll
+      for (int w = 0; w < KL_WARPS; ++w) tot += s_dred[w * DEC_MAX_T + tid];
+      const float ms = __fdiv_rn((float)tot, (float)H);
+      s_inv[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.norm_eps)));
+    }
+    __syncthreads();
+    for (int i = tid; i < T * (H / 8); i += KL_THREADS) {
+      const int t = i / (H / 8);
+      uint4 v = reinterpret_cast<const uint4 *>(xb)[i];
+      uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      const float inv = s_inv[t];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        w[q] = pack_bf2(__fmul_rn(bf2f(w[q] & 0xFFFF), inv), __fmul_rn(bf2f(w[q] >> 16), inv));
+      reinterpret_cast<uint4 *>(xb)[i] = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    __syncthreads();
+  }
+  {
+    // x in MMA fragment order: word (G, n, c, w) = x[n][base], x[n][base+4]
+    // with base = 64G + 16c + 8(w/4) + 2((w/2)&1) + (w&1).
+    for (int i = tid; i < T * (H / 2); i += KL_THREADS) {
+      const int n = i / (H / 2), r = i % (H / 2);
+      const int Gi = r >> 5, cc = (r >> 3) & 3, w = r & 7;
+      const int m = w >> 1, pp = w & 1, j = m >> 1, i0 = 2 * (m & 1);
+      const int base = 64 * Gi + 16 * cc + 8 * j + i0 + pp;
+      xf[((Gi * DEC_MAX_T + n) * 4 + cc) * 8 + w] =
+          (uint32_t)xb[(size_t)n * H + base] | ((uint32_t)xb[(size_t)n * H + base + 4] << 16);
+    }
+    // Per-64-column sums (zero beyond T): a fixed pairwise tree per
+    // (group, token), the order of a 32-lane xor-shuffle reduction of
+    // pair sums.
+    for (int i = tid; i < NG * DEC_MAX_T; i += KL_THREADS) {
+      const int Gi = i / DEC_MAX_T, n = i % DEC_MAX_T;
+      float s = 0.f;
+      if (n < T) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(xb + (size_t)n * H + 64 * Gi);
+        float a[32];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint4 v = src[q];
+          a[4 * q + 0] = bf_lo(v.x) + bf_hi(v.x);
+          a[4 * q + 1] = bf_lo(v.y) + bf_hi(v.y);
+          a[4 * q + 2] = bf_lo(v.z) + bf_hi(v.z);
+          a[4 * q + 3] = bf_lo(v.w) + bf_hi(v.w);
+        }
+#pragma unroll
+        for (int st = 16; st > 0; st >>= 1)
+#pragma unroll
+          for (int L = 0; L < st; ++L) a[L] = a[L] + a[L + st];
+        s = a[0];
+      }
+      xsm[Gi * DEC_MAX_T + n] = s;
+    }
+  }
+  // Router rows: this CTA's rows (blockIdx.x + G * round) * RPC + rloc.
+  for (int round = 0;; ++round) {
+    const int rb0 = (blockIdx.x + G * round) * RPC;
+    if (rb0 >= nrows) break;
+    const int row = rb0 + rloc;
+    if (round > 0 && row < nrows) load_row(row);
+    if (row < nrows) {
+      float acc[DEC_MAX_T];
+#pragma unroll
+      for (int t = 0; t < DEC_MAX_T; ++t) acc[t] = 0.f;
+#pragma unroll
+      for (int u = 0; u < NVQ; ++u) {
+        const int v = part * (H / Q / 8) + u * 32 + lane;
+        const uint32_t wr[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+#pragma unroll
+        for (int t = 0; t < DEC_MAX_T; ++t) {
+          if (t < T) {
+            const uint4 xv = reinterpret_cast<const uint4 *>(xb + (size_t)t * H)[v];
+            const uint32_t xr[4] = {xv.x, xv.y, xv.z, xv.w};
+            float a = acc[t];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              a = fmaf(bf2f(wr[q] & 0xFFFF), bf2f(xr[q] & 0xFFFF), a);
+              a = fmaf(bf2f(wr[q] >> 16), bf2f(xr[q] >> 16), a);
+            }
+            acc[t] = a;
+          }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int t = 0; t < DEC_MAX_T; ++t) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+      if (lane == 0)
+#pragma unroll
+        for (int t = 0; t < DEC_MAX_T; ++t) s_part[(rloc * Q + part) * DEC_MAX_T + t] = acc[t];
+    }
+    __syncthreads();
+    if (tid < RPC * DEC_MAX_T) {
+      const int rl = tid / DEC_MAX_T, t = tid % DEC_MAX_T;
+      const int r = rb0 + rl;
+      if (r < nrows && t < T) {
+        float a = 0.f;
+#pragma unroll
+        for (int q = 0; q < Q; ++q) a += s_part[(rl * Q + q) * DEC_MAX_T + t];
+        if (r < E) {
+          if (p.router_bias) a = a + p.router_bias[r];
+          wsp<float>(p, p.L.logits)[(size_t)t * E + r] = rbf(a);
+        } else {
+          wsp<float>(p, p.L.sgate)[t] = rbf(mlx_sigmoid(rbf(a)));
+        }
+      }
+    }
+    __syncthreads();
+  }
+  trace_mark(p.trace, 3);
+
+  // ---------------- 3. grid barrier, routing ----------------
+  if (tid == 0) {
+    unsigned *bar = wsp<unsigned>(p, p.L.bar);  // [0] arrivals, [1] generation
+    const unsigned gen = *reinterpret_cast<volatile unsigned *>(bar + 1);
+    __threadfence();
+    bool ok = true;
+    if (atomicAdd(bar, 1u) == (unsigned)G - 1) {
+      bar[0] = 0u;  // nobody arrives again before the generation moves
+      __threadfence();
+      st_release(bar + 1, gen + 1u);
+    } else {
+      ok = wait_word(bar + 1, gen, true);
+    }
+    __threadfence();
+    if (!ok) flag_status(p.status, VB_STATUS_TIMEOUT);
+    s_misc[1] = ok ? 0 : 1;
   }
   __syncthreads();
-  trace_mark(p.trace, 6);
-  const int n_items = s_n << rb_shift;
-  if (!pre) {
-#pragma unroll 1
-    for (int k = 0; k < RS - 1; ++k) issue_next(n_items);
+  if (s_misc[1]) {
+    span.end();
+    return;
   }
-  if (!half && lane < 9) {
-    // Whole row blocks of this pair's items into L2 in one go (contiguous
-    // 16-row blocks of gate and up codes and of their four scale tensors):
-    // DRAM then streams each block at once and the chunk copies hit L2.
-    // Lanes 6..8 do the same for the slice of the entry's down projection
-    // (rows [rb, rb + 1) * H / RB) that the next kernel reads.
-    for (int i = first; i < n_items; i += step) {
-      const int e = i >> rb_shift, rb = i & (RB - 1);
-      const VbQuantPool &pool = (p.has_shared && e == 0) ? p.shared : p.pool;
-      const int slot = (p.has_shared && e == 0) ? 0 : s_slot[e];
-      if (lane < 6) {
-        GateUpItem it;
-        gateup_item<H, GS>(pool, slot, rb, it);
-        if (lane < 2) prefetch_l2_bulk(lane ? it.uw : it.gw, 16 * Tl::ROWB);
-        else prefetch_l2_bulk(it.sc[lane - 2], 16 * Tl::NS * 2);
-      } else {
-        const int rows = H / RB, ngi = p.I >> (6 + GS);
-        const uint32_t rbytes = lane == 6 ? (uint32_t)p.I / 2 : (uint32_t)ngi * 2;
-        prefetch_l2_bulk(pool_ptr(pool, lane, slot) + (size_t)rb * rows * rbytes, rows * rbytes);
+  trace_mark(p.trace, 4);
+  {
+    int *s_table = reinterpret_cast<int *>(pairs + Tl::TMP_TABLE);
+    int *s_first = reinterpret_cast<int *>(pairs + Tl::TMP_FIRST);
+    int *s_rex = reinterpret_cast<int *>(pairs + Tl::TMP_ROUTE);
+    int *s_rslot = s_rex + KL_MAX_ROUTES;
+    float *s_rscore = reinterpret_cast<float *>(s_rslot + KL_MAX_ROUTES);
+    int *s_rent = reinterpret_cast<int *>(s_rscore + KL_MAX_ROUTES);
+    const float *lg = wsp<const float>(p, p.L.logits);
+    const bool primary = blockIdx.x == 0;
+    int n;
+#define VB_ROUTE(PER)                                                                           \
+  route_tokens<PER>(lg, p.table, T, E, p.k, p.norm_topk, p.has_shared, p.pool.cap, primary,     \
+                    p.status, p.out_inds, p.out_scores, p.out_local, s_table, s_first, s_rex,   \
+                    s_rslot, s_rscore, s_rent, s_ok, s_ent, s_wcnt)
+    if (E <= 256) n = VB_ROUTE(8);
+    else if (E <= 512) n = VB_ROUTE(16);
+    else n = VB_ROUTE(32);
+#undef VB_ROUTE
+    if (tid == 0) s_misc[0] = n;
+  }
+  __syncthreads();  // the pair areas are free from here on
+  trace_mark(p.trace, 5);
+  const int n_ent = s_misc[0];
+
+  // ---------------- 4. gate/up + SwiGLU ----------------
+  const int pair = warp >> 1, half = warp & 1;
+  uint8_t *pbase = pairs + pair * Tl::PAIR;
+  uint8_t *ring = pbase + half * Tl::RING;
+  float *red = reinterpret_cast<float *>(pbase + 2 * Tl::RING);  // [2][32][8]
+  float *hbuf = red + 2 * 32 * 8;                                 // [16][8]
+  unsigned *ent_done = wsp<unsigned>(p, p.L.ent_done);
+  {
+    // This pair's items: blockIdx.x + G * (pair + KL_PAIRS * r), r = 0, 1, ...
+    const int first = blockIdx.x + G * pair, step = G * KL_PAIRS;
+    const int n_items = n_ent * RB;
+    const int scb = (CG >> gs) * 2;
+    GateUpItem cur;
+    int issue_q = 0;
+    auto issue_next = [&]() {
+      const int r = issue_q / CPH, ch = half * CPH + issue_q % CPH;
+      const int i = first + r * step;
+      if (i < n_items) {
+        if (issue_q % CPH == 0) {
+          const int e = i / RB;
+          if (p.has_shared && e == 0) gateup_item<H, I>(p.shared, 0, i % RB, gs, cur);
+          else gateup_item<H, I>(p.pool, s_ent[e].slot, i % RB, gs, cur);
+        }
+        gateup_chunk<H, I>(ring + (issue_q % RS) * Tl::CHUNK, cur, ch, lane, gs);
+      }
+      cp_async_commit();
+      ++issue_q;
+    };
+#pragma unroll 1
+    for (int kq = 0; kq < RS - 1; ++kq) issue_next();
+    if (!half && lane < 9) {
+      // Whole row blocks of this pair's items into L2 in one go (contiguous
+      // 16-row blocks of gate and up codes and of their four scale tensors):
+      // DRAM then streams each block at once and the chunk copies hit L2.
+      // Lanes 6..8 do the same for the slice of the entry's down projection
+      // (rows [rb, rb + 1) * H / RB) that the down phase reads.
+      for (int i = first; i < n_items; i += step) {
+        const int e = i / RB, rb = i % RB;
+        const bool sh = p.has_shared && e == 0;
+        const VbQuantPool &pool = sh ? p.shared : p.pool;
+        const int slot = sh ? 0 : s_ent[e].slot;
+        if (lane < 6) {
+          GateUpItem it;
+          gateup_item<H, I>(pool, slot, rb, gs, it);
+          if (lane < 2) prefetch_l2_bulk(lane ? it.uw : it.gw, 16 * Tl::ROWB);
+          else prefetch_l2_bulk(it.sc[lane - 2], 16 * (Tl::NS64 >> gs) * 2);
+        } else {
+          constexpr int rows = H / RB;
+          const uint32_t rbytes = lane == 6 ? (uint32_t)I / 2 : (uint32_t)(NGI >> gs) * 2;
+          prefetch_l2_bulk(pool_ptr(pool, lane, slot) + (size_t)rb * rows * rbytes, rows * rbytes);
+        }
       }
     }
-  }
-
-  const int NI = p.I / 64;
-  float accg[4], accu[4];
+    float accg[4], accu[4];
 #pragma unroll 1
-  for (int q = 0;; ++q) {
-    const int r = q / CPH, cq = q % CPH, ch = half * CPH + cq;
-    const int item = first + r * step;
-    if (item >= n_items) break;
-    cp_async_wait<RS - 2>();
+    for (int q = 0;; ++q) {
+      const int r = q / CPH, cq = q % CPH, ch = half * CPH + cq;
+      const int item = first + r * step;
+      if (item >= n_items) break;
+      cp_async_wait<RS - 2>();
+      __syncwarp();
+      issue_next();  // into the stage consumed one chunk ago
+      if (cq == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) accg[j] = accu[j] = 0.f;
+      }
+      const uint8_t *st = ring + (q % RS) * Tl::CHUNK;
+      // Scales of this chunk's groups for rows g and g+8: gate s, gate b,
+      // up s, up b.
+      uint2 sv[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) {
+        const uint8_t *sp = st + Tl::WB + ((a >> 1) * 16 + ((a & 1) ? g + 8 : g)) * scb;
+        if (scb == 8) sv[a] = *reinterpret_cast<const uint2 *>(sp);
+        else sv[a] = make_uint2(*reinterpret_cast<const uint32_t *>(sp), 0u);
+      }
+#pragma unroll
+      for (int gl = 0; gl < CG; ++gl) {
+        const int Gi = ch * CG + gl;
+        uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0;
+        if (g < T) {
+          const uint4 *xp = reinterpret_cast<const uint4 *>(xf + ((Gi * DEC_MAX_T + g) * 4 + c) * 8);
+          x0 = xp[0];
+          x1 = xp[1];
+        }
+        const float2 xs = *reinterpret_cast<const float2 *>(xsm + Gi * DEC_MAX_T + 2 * c);
+        const uint2 ag0 = lds64(st + g * Tl::PITCH + gl * 32 + 8 * c);
+        const uint2 ag1 = lds64(st + (g + 8) * Tl::PITCH + gl * 32 + 8 * c);
+        const uint2 au0 = lds64(st + (16 + g) * Tl::PITCH + gl * 32 + 8 * c);
+        const uint2 au1 = lds64(st + (24 + g) * Tl::PITCH + gl * 32 + 8 * c);
+        uint32_t pg0[2][4], pg1[2][4], pu0[2][4], pu1[2][4];
+        nib_pairs4(ag0.x, pg0[0]);
+        nib_pairs4(ag0.y, pg0[1]);
+        nib_pairs4(ag1.x, pg1[0]);
+        nib_pairs4(ag1.y, pg1[1]);
+        nib_pairs4(au0.x, pu0[0]);
+        nib_pairs4(au0.y, pu0[1]);
+        nib_pairs4(au1.x, pu1[0]);
+        nib_pairs4(au1.y, pu1[1]);
+        const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        float dg[4] = {0.f, 0.f, 0.f, 0.f}, du[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const int i0 = 2 * (m & 1), h = m >> 1;
+          mma_bf16(dg, pg0[h][i0], pg1[h][i0], pg0[h][i0 + 1], pg1[h][i0 + 1], xw[2 * m],
+                   xw[2 * m + 1]);
+          mma_bf16(du, pu0[h][i0], pu1[h][i0], pu0[h][i0 + 1], pu1[h][i0 + 1], xw[2 * m],
+                   xw[2 * m + 1]);
+        }
+        const int si = gl >> gs;
+        const float sg0 = bf_at2(sv[0], si), sg1 = bf_at2(sv[1], si);
+        const float bg0 = bf_at2(sv[2], si), bg1 = bf_at2(sv[3], si);
+        const float su0 = bf_at2(sv[4], si), su1 = bf_at2(sv[5], si);
+        const float bu0 = bf_at2(sv[6], si), bu1 = bf_at2(sv[7], si);
+        const float bpg0 = fmaf(-128.f, sg0, bg0), bpg1 = fmaf(-128.f, sg1, bg1);
+        const float bpu0 = fmaf(-128.f, su0, bu0), bpu1 = fmaf(-128.f, su1, bu1);
+        accg[0] += fmaf(sg0, dg[0], bpg0 * xs.x);
+        accg[1] += fmaf(sg0, dg[1], bpg0 * xs.y);
+        accg[2] += fmaf(sg1, dg[2], bpg1 * xs.x);
+        accg[3] += fmaf(sg1, dg[3], bpg1 * xs.y);
+        accu[0] += fmaf(su0, du[0], bpu0 * xs.x);
+        accu[1] += fmaf(su0, du[1], bpu0 * xs.y);
+        accu[2] += fmaf(su1, du[2], bpu1 * xs.x);
+        accu[3] += fmaf(su1, du[3], bpu1 * xs.y);
+      }
+      if (cq == CPH - 1) {
+        // Pair hand-off: the odd warp's partials to the even warp.
+        float *slot = red + ((r & 1) * 32 + lane) * 8;
+        if (half) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            slot[j] = accg[j];
+            slot[4 + j] = accu[j];
+          }
+        }
+        named_bar(1 + pair, 64);
+        if (!half) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            accg[j] += slot[j];
+            accu[j] += slot[4 + j];
+          }
+          // SwiGLU (bf16 per op) of rows g, g+8 x tokens 2c, 2c+1, then h of
+          // the 16 rows in fragment order and its per-token sums.
+          const int e = item / RB, rb = item % RB;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int row = (j >> 1) ? g + 8 : g, n = 2 * c + (j & 1);
+            hbuf[row * 8 + n] = n < T ? swiglu_bf16(rbf(accg[j]), rbf(accu[j])) : 0.f;
+          }
+          __syncwarp();
+          uint32_t *hperm = wsp<uint32_t>(p, p.L.hperm);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const int idx = lane + 32 * h2;  // (token n, word w)
+            const int n = idx >> 3, w = idx & 7;
+            const int m = w >> 1, pp = w & 1, j = m >> 1, i0 = 2 * (m & 1);
+            const int olo = 8 * j + i0 + pp, ohi = olo + 4;
+            if (n < T)
+              hperm[((((size_t)e * DEC_MAX_T + n) * NGI + (rb >> 2)) * 4 + (rb & 3)) * 8 + w] =
+                  pack_bf2(hbuf[olo * 8 + n], hbuf[ohi * 8 + n]);
+          }
+          if (lane < T) {
+            float sh = 0.f;
+#pragma unroll
+            for (int o = 0; o < 16; ++o) sh += hbuf[o * 8 + lane];
+            wsp<float>(p, p.L.hsum)[((size_t)e * DEC_MAX_T + lane) * RB + rb] = sh;
+          }
+          __syncwarp();
+          if (lane == 0) red_release_add(ent_done + e, 1u);  // h rows of this item are out
+        }
+      }
+    }
+    cp_async_wait<0>();
     __syncwarp();
-    issue_next(n_items);  // into the stage consumed one chunk ago
-    if (cq == 0) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) accg[j] = accu[j] = 0.f;
-    }
-    const uint8_t *st = ring + (q % RS) * Tl::CHUNK;
-    // Scales of this chunk's groups for rows g and g+8: gate s, gate b,
-    // up s, up b.
-    uint2 sv[8];
-#pragma unroll
-    for (int a = 0; a < 8; ++a) {
-      const uint8_t *sp = st + Tl::WB + ((a >> 1) * 16 + ((a & 1) ? g + 8 : g)) * Tl::SCB;
-      if (Tl::SCB == 8) sv[a] = *reinterpret_cast<const uint2 *>(sp);
-      else sv[a] = make_uint2(*reinterpret_cast<const uint32_t *>(sp), 0u);
-    }
-#pragma unroll
-    for (int gl = 0; gl < CG; ++gl) {
-      const int G = ch * CG + gl;
-      uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0;
-      if (g < T) {
-        const uint4 *xp = reinterpret_cast<const uint4 *>(xf + ((G * DEC_MAX_T + g) * 4 + c) * 8);
-        x0 = xp[0];
-        x1 = xp[1];
-      }
-      const float2 xs = *reinterpret_cast<const float2 *>(xsm + G * DEC_MAX_T + 2 * c);
-      const uint2 ag0 = lds64(st + g * Tl::PITCH + gl * 32 + 8 * c);
-      const uint2 ag1 = lds64(st + (g + 8) * Tl::PITCH + gl * 32 + 8 * c);
-      const uint2 au0 = lds64(st + (16 + g) * Tl::PITCH + gl * 32 + 8 * c);
-      const uint2 au1 = lds64(st + (24 + g) * Tl::PITCH + gl * 32 + 8 * c);
-      uint32_t pg0[2][4], pg1[2][4], pu0[2][4], pu1[2][4];
-      nib_pairs4(ag0.x, pg0[0]);
-      nib_pairs4(ag0.y, pg0[1]);
-      nib_pairs4(ag1.x, pg1[0]);
-      nib_pairs4(ag1.y, pg1[1]);
-      nib_pairs4(au0.x, pu0[0]);
-      nib_pairs4(au0.y, pu0[1]);
-      nib_pairs4(au1.x, pu1[0]);
-      nib_pairs4(au1.y, pu1[1]);
-      const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-      float dg[4] = {0.f, 0.f, 0.f, 0.f}, du[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const int i0 = 2 * (m & 1), h = m >> 1;
-        mma_bf16(dg, pg0[h][i0], pg1[h][i0], pg0[h][i0 + 1], pg1[h][i0 + 1], xw[2 * m],
-                 xw[2 * m + 1]);
-        mma_bf16(du, pu0[h][i0], pu1[h][i0], pu0[h][i0 + 1], pu1[h][i0 + 1], xw[2 * m],
-                 xw[2 * m + 1]);
-      }
-      const int si = gl >> GS;
-      const float sg0 = bf_at2(sv[0], si), sg1 = bf_at2(sv[1], si);
-      const float bg0 = bf_at2(sv[2], si), bg1 = bf_at2(sv[3], si);
-      const float su0 = bf_at2(sv[4], si), su1 = bf_at2(sv[5], si);
-      const float bu0 = bf_at2(sv[6], si), bu1 = bf_at2(sv[7], si);
-      const float bpg0 = fmaf(-128.f, sg0, bg0), bpg1 = fmaf(-128.f, sg1, bg1);
-      const float bpu0 = fmaf(-128.f, su0, bu0), bpu1 = fmaf(-128.f, su1, bu1);
-      accg[0] += fmaf(sg0, dg[0], bpg0 * xs.x);
-      accg[1] += fmaf(sg0, dg[1], bpg0 * xs.y);
-      accg[2] += fmaf(sg1, dg[2], bpg1 * xs.x);
-      accg[3] += fmaf(sg1, dg[3], bpg1 * xs.y);
-      accu[0] += fmaf(su0, du[0], bpu0 * xs.x);
-      accu[1] += fmaf(su0, du[1], bpu0 * xs.y);
-      accu[2] += fmaf(su1, du[2], bpu1 * xs.x);
-      accu[3] += fmaf(su1, du[3], bpu1 * xs.y);
-    }
-    if (cq == CPH - 1) {
-      // Pair hand-off: the odd warp's partials to the even warp.
-      float *slot = red + ((r & 1) * 32 + lane) * 8;
-      if (half) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          slot[j] = accg[j];
-          slot[4 + j] = accu[j];
-        }
-      }
-      named_bar(1 + pair, 64);
-      if (!half) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          accg[j] += slot[j];
-          accu[j] += slot[4 + j];
-        }
-        // SwiGLU (bf16 per op) of rows g, g+8 x tokens 2c, 2c+1, then h of
-        // the 16 rows in fragment order and its per-token sums.
-        const int e = item >> rb_shift, rb = item & (RB - 1);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int row = (j >> 1) ? g + 8 : g, n = 2 * c + (j & 1);
-          hbuf[row * 8 + n] = n < T ? swiglu_bf16(rbf(accg[j]), rbf(accu[j])) : 0.f;
-        }
-        __syncwarp();
-        uint32_t *hperm = wsp<uint32_t>(p, p.L.hperm);
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const int idx = lane + 32 * h2;  // (token n, word w)
-          const int n = idx >> 3, w = idx & 7;
-          const int m = w >> 1, pp = w & 1, j = m >> 1, i0 = 2 * (m & 1);
-          const int olo = 8 * j + i0 + pp, ohi = olo + 4;
-          if (n < T)
-            hperm[((((size_t)e * DEC_MAX_T + n) * NI + (rb >> 2)) * 4 + (rb & 3)) * 8 + w] =
-                pack_bf2(hbuf[olo * 8 + n], hbuf[ohi * 8 + n]);
-        }
-        if (lane < T) {
-          float sh = 0.f;
-#pragma unroll
-          for (int o = 0; o < 16; ++o) sh += hbuf[o * 8 + lane];
-          wsp<float>(p, p.L.hsum)[((size_t)e * DEC_MAX_T + lane) * (p.I / 16) + rb] = sh;
-        }
-        __syncwarp();
-        if (r == 0) trace_mark(p.trace, 7);
-      }
-    }
   }
-  cp_async_wait<0>();
-  span.end();
-}
+  if (p.trace && lane == 0) atomicMax(&s_tm[0], (unsigned long long)globaltimer());
 
-// ----------------------------------------------------------------------------
-// K3: down projection + fused combine. Persistent CTAs of 8 warps; the items
-// (entry, 16 output rows) are split into contiguous entry-major ranges, one
-// per warp (warps of consecutive global index sit on different SMs), so a
-// warp keeps one entry's h fragments in registers across its row blocks.
-// Each item's 16 weight rows and scales are copied by the warp with
-// cp.async into a per-warp ring (the first ones before the PDL wait: the
-// entry list is final by then); h and its group sums are read after it.
-// Per route the result is rounded to bf16, times the route score, rounded
-// again (MLX chain). The last warp to finish a 16-row block (atomic ticket
-// per block) adds the routes of every token in rank order (exact double sum
-// of bf16 values, rounded to float32 then bf16), then the gated shared
-// expert and the optional residual.
-// ----------------------------------------------------------------------------
-constexpr int K3_THREADS = 256;
-constexpr int K3_WARPS = K3_THREADS / 32;
-
-template <int I, int GS>
-struct DownTile {
-  static constexpr int NGI = I / 64;
-  static constexpr int ROWB = I / 2;        // packed bytes per row
-  static constexpr int PITCH = ROWB + 32;   // padded smem pitch (conflict-free fragments)
-  static constexpr int NSI = I >> (6 + GS); // scales per row
-  static constexpr int WB = 16 * PITCH;
-  static constexpr int SB = 16 * NSI * 2;   // 16 rows of one scale tensor
-  static constexpr int SLOT = WB + 2 * SB;
-  static constexpr int RS = 5;
-  static constexpr int SMEM = K3_WARPS * RS * SLOT;
-};
-
-template <int I, int GS>
-__device__ __forceinline__ void down_issue(uint8_t *slot, const VbQuantPool &pool, int pslot,
-                                           int rb, int lane) {
-  using Tl = DownTile<I, GS>;
-  const uint8_t *dw = pool_ptr(pool, 6, pslot) + (size_t)rb * 16 * Tl::ROWB;
-  constexpr int CPR = Tl::ROWB / 16;  // chunks per row
-#pragma unroll
-  for (int j = 0; j < 16 * CPR / 32; ++j) {
-    const int q = lane + 32 * j, r = q / CPR, c16 = (q % CPR) * 16;
-    cp_async16(slot + r * Tl::PITCH + c16, dw + r * Tl::ROWB + c16);
-  }
-  constexpr int SCH = Tl::SB / 16;  // chunks per scale tensor
-  for (int q = lane; q < 2 * SCH; q += 32) {
-    const int t = q / SCH, c = q % SCH;
-    cp_async16(slot + Tl::WB + t * Tl::SB + c * 16,
-               pool_ptr(pool, 7 + t, pslot) + (size_t)rb * Tl::SB + c * 16);
-  }
-}
-
-// Rank-order combine of one 16-row block for all tokens (one warp; lane =
-// token t = lane / 8 (+4 per pass), row pair 2 * (lane % 8)). Every load of a
-// pass is issued before the first add.
-__device__ __forceinline__ void down_combine_block(const DecodeParams &p, int rb, int lane) {
-  const int T = p.T, H = p.H, k = p.k;
-  const uint32_t *wp = wsp<const uint32_t>(p, p.L.wparts);
-  const int32_t *okr = wsp<const int32_t>(p, p.L.route_ok);
-  const int rp = 16 * rb + 2 * (lane & 7);
-#pragma unroll 1
-  for (int t = lane >> 3; t < T; t += 4) {
-    uint32_t v[DEC_MAX_K];
-    int ok[DEC_MAX_K];
-#pragma unroll
-    for (int j = 0; j < DEC_MAX_K; ++j) {
-      if (j < k) {
-        ok[j] = __ldcg(okr + t * k + j);
-        v[j] = __ldcg(wp + (((size_t)t * k + j) * H + rp) / 2);
-      }
-    }
-    float gate = 0.f;
-    uint32_t sw = 0, rr = 0;
-    const size_t oi = (size_t)t * H + rp;
-    if (p.has_shared) {
-      gate = __ldcg(wsp<const float>(p, p.L.sgate) + t);
-      sw = __ldcg(wsp<const uint32_t>(p, p.L.sparts) + oi / 2);
-    }
-    if (p.residual) rr = __ldg(reinterpret_cast<const uint32_t *>(p.residual) + oi / 2);
-    double s0 = 0.0, s1 = 0.0;
-#pragma unroll
-    for (int j = 0; j < DEC_MAX_K; ++j) {
-      if (j < k && ok[j]) {
-        s0 += (double)bf2f(v[j] & 0xFFFFu);
-        s1 += (double)bf2f(v[j] >> 16);
-      }
-    }
-    float y0 = rbf((float)s0), y1 = rbf((float)s1);
-    if (p.has_shared) {
-      y0 = rbf(__fadd_rn(y0, rbf(__fmul_rn(gate, bf2f(sw & 0xFFFFu)))));
-      y1 = rbf(__fadd_rn(y1, rbf(__fmul_rn(gate, bf2f(sw >> 16)))));
-    }
-    if (p.residual) {
-      y0 = rbf(__fadd_rn(bf2f(rr & 0xFFFFu), y0));
-      y1 = rbf(__fadd_rn(bf2f(rr >> 16), y1));
-    }
-    reinterpret_cast<uint32_t *>(p.out)[oi / 2] = (uint32_t)f2bf(y0) | ((uint32_t)f2bf(y1) << 16);
-  }
-}
-
-template <int I, int GS>
-__global__ void __launch_bounds__(K3_THREADS, 1) moe_down_kernel(DecodeParams p) {
-  using Tl = DownTile<I, GS>;
-  constexpr int NGI = Tl::NGI, RS = Tl::RS;
-  extern __shared__ __align__(16) uint8_t smem[];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, c = lane & 3;
-  const int T = p.T, H = p.H;
-  SpanTrace span(p.trace, 2);
-  uint8_t *ring = smem + warp * RS * Tl::SLOT;
-  const int RBN = H / 16;
-  const int n_entries = __ldcg(wsp<const int32_t>(p, p.L.n_entries));
-  const DecEntry *ents = wsp<const DecEntry>(p, p.L.entries);
-  // This warp's contiguous item range (entry-major).
-  const int nw = gridDim.x * K3_WARPS;
-  const int wg = blockIdx.x + gridDim.x * warp;
-  const int n_items = n_entries * RBN;
-  const int i0 = (int)(((long long)n_items * wg) / nw);
-  const int i1 = (int)(((long long)n_items * (wg + 1)) / nw);
-
-  // The entry list is final before this kernel starts (the router ran two
-  // launches back): weights are copied before the PDL wait.
-  int issue_i = i0;
-  auto issue_next = [&]() {
-    if (issue_i < i1) {
-      const int e = issue_i / RBN, rb = issue_i % RBN;
-      const int2 sf = __ldcg(reinterpret_cast<const int2 *>(&ents[e]));  // slot, flags
-      const bool sh = sf.y & 1;
-      down_issue<I, GS>(ring + ((issue_i - i0) % RS) * Tl::SLOT, sh ? p.shared : p.pool,
-                        sh ? 0 : sf.x, rb, lane);
-    }
-    cp_async_commit();
-    ++issue_i;
-  };
-#pragma unroll 1
-  for (int k = 0; k < RS - 1; ++k) issue_next();
-  pdl_wait();
-  pdl_launch_dependents();
-
+  // ---------------- 5. down projection ----------------
   uint16_t *wparts = wsp<uint16_t>(p, p.L.wparts);
   uint16_t *sparts = wsp<uint16_t>(p, p.L.sparts);
-  int cur_e = -1;
-  uint32_t hb[NGI][8];
-  float hs0[NGI], hs1[NGI];
-  int rank0 = -1, rank1 = -1;
-  float score0 = 0.f, score1 = 0.f;
-  bool is_sh = false;
+  const int nw = G * KL_WARPS;
+  const int wg = blockIdx.x + G * warp;
+  const int n_items_d = n_ent * RBN;
+  const int i0 = (int)(((long long)n_items_d * wg) / nw);
+  const int i1 = (int)(((long long)n_items_d * (wg + 1)) / nw);
+  int i_end = i1;
+  {
+    int issue_i = i0;
+    auto issue_next = [&]() {
+      if (issue_i < i1) {
+        const int e = issue_i / RBN, rb = issue_i % RBN;
+        const bool sh = p.has_shared && e == 0;
+        down_issue<H, I>(ring + ((issue_i - i0) % DRS) * Tl::DSLOT, sh ? p.shared : p.pool,
+                         sh ? 0 : s_ent[e].slot, rb, lane, gs);
+      }
+      cp_async_commit();
+      ++issue_i;
+    };
 #pragma unroll 1
-  for (int i = i0; i < i1; ++i) {
-    const int e = i / RBN, rb = i % RBN;
-    if (e != cur_e) {
-      // h fragments and group sums of the entry (tokens g and 2c, 2c+1),
-      // requested while the weight copy is still in flight.
-      cur_e = e;
-      const uint32_t *hp = wsp<const uint32_t>(p, p.L.hperm) + (size_t)e * DEC_MAX_T * (I / 2);
-      const float *hsum = wsp<const float>(p, p.L.hsum) + (size_t)e * DEC_MAX_T * (I / 16);
-#pragma unroll
-      for (int G = 0; G < NGI; ++G) {
-        uint4 a = make_uint4(0, 0, 0, 0), b = a;
-        if (g < T) {
-          const uint4 *src = reinterpret_cast<const uint4 *>(hp + ((size_t)g * NGI + G) * 32 + c * 8);
-          a = __ldcg(src);
-          b = __ldcg(src + 1);
+    for (int kq = 0; kq < DRS - 1; ++kq) issue_next();
+
+    const int nsi = NGI >> gs, sbh = 16 * nsi;  // scales per row; bf16 per scale tensor
+    int cur_e = -1;
+    uint32_t hb[NGI][8];
+    float hs0[NGI], hs1[NGI];
+    int rank0 = -1, rank1 = -1;
+    float score0 = 0.f, score1 = 0.f;
+    bool is_sh = false;
+#pragma unroll 1
+    for (int i = i0; i < i1; ++i) {
+      const int e = i / RBN, rb = i % RBN;
+      if (e != cur_e) {
+        // The entry's h is complete once its RB gate/up items are counted.
+        if (!wait_word(ent_done + e, (unsigned)RB, false)) {
+          if (lane == 0) flag_status(p.status, VB_STATUS_TIMEOUT);
+          i_end = i;
+          break;
         }
-        hb[G][0] = a.x; hb[G][1] = a.y; hb[G][2] = a.z; hb[G][3] = a.w;
-        hb[G][4] = b.x; hb[G][5] = b.y; hb[G][6] = b.z; hb[G][7] = b.w;
-        float v0 = 0.f, v1 = 0.f;
-        if (2 * c < T) {
-          const float4 v = __ldcg(reinterpret_cast<const float4 *>(hsum + (size_t)(2 * c) * (I / 16) + 4 * G));
-          v0 = ((v.x + v.y) + v.z) + v.w;
+        cur_e = e;
+        const uint32_t *hp = wsp<const uint32_t>(p, p.L.hperm) + (size_t)e * DEC_MAX_T * (I / 2);
+        const float *hsum = wsp<const float>(p, p.L.hsum) + (size_t)e * DEC_MAX_T * RB;
+#pragma unroll
+        for (int Gi = 0; Gi < NGI; ++Gi) {
+          uint4 a = make_uint4(0, 0, 0, 0), b = a;
+          if (g < T) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(hp + ((size_t)g * NGI + Gi) * 32 + c * 8);
+            a = __ldcg(src);
+            b = __ldcg(src + 1);
+          }
+          hb[Gi][0] = a.x; hb[Gi][1] = a.y; hb[Gi][2] = a.z; hb[Gi][3] = a.w;
+          hb[Gi][4] = b.x; hb[Gi][5] = b.y; hb[Gi][6] = b.z; hb[Gi][7] = b.w;
+          float v0 = 0.f, v1 = 0.f;
+          if (2 * c < T) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(hsum + (size_t)(2 * c) * RB + 4 * Gi));
+            v0 = ((v.x + v.y) + v.z) + v.w;
+          }
+          if (2 * c + 1 < T) {
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(hsum + (size_t)(2 * c + 1) * RB + 4 * Gi));
+            v1 = ((v.x + v.y) + v.z) + v.w;
+          }
+          hs0[Gi] = v0;
+          hs1[Gi] = v1;
         }
-        if (2 * c + 1 < T) {
-          const float4 v = __ldcg(reinterpret_cast<const float4 *>(hsum + (size_t)(2 * c + 1) * (I / 16) + 4 * G));
-          v1 = ((v.x + v.y) + v.z) + v.w;
+        is_sh = s_ent[e].flags & 1;
+        rank0 = 2 * c < T ? s_ent[e].rank[2 * c] : -1;
+        rank1 = 2 * c + 1 < T ? s_ent[e].rank[2 * c + 1] : -1;
+        score0 = 2 * c < T ? s_ent[e].score[2 * c] : 0.f;
+        score1 = 2 * c + 1 < T ? s_ent[e].score[2 * c + 1] : 0.f;
+      }
+      cp_async_wait<DRS - 2>();
+      __syncwarp();
+      issue_next();
+      const uint8_t *st = ring + ((i - i0) % DRS) * Tl::DSLOT;
+      const uint16_t *ss = reinterpret_cast<const uint16_t *>(st + Tl::DWB);
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int Gi = 0; Gi < NGI; ++Gi) {
+        const uint2 a0 = lds64(st + g * Tl::DPITCH + Gi * 32 + 8 * c);
+        const uint2 a1 = lds64(st + (g + 8) * Tl::DPITCH + Gi * 32 + 8 * c);
+        uint32_t p0[2][4], p1[2][4];
+        nib_pairs4(a0.x, p0[0]);
+        nib_pairs4(a0.y, p0[1]);
+        nib_pairs4(a1.x, p1[0]);
+        nib_pairs4(a1.y, p1[1]);
+        float dd[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const int i0m = 2 * (m & 1), h = m >> 1;
+          mma_bf16(dd, p0[h][i0m], p1[h][i0m], p0[h][i0m + 1], p1[h][i0m + 1], hb[Gi][2 * m],
+                   hb[Gi][2 * m + 1]);
         }
-        hs0[G] = v0;
-        hs1[G] = v1;
+        const int si = Gi >> gs;
+        const float s0 = bf2f(ss[g * nsi + si]), s1 = bf2f(ss[(g + 8) * nsi + si]);
+        const float b0 = bf2f(ss[sbh + g * nsi + si]);
+        const float b1 = bf2f(ss[sbh + (g + 8) * nsi + si]);
+        const float bp0 = fmaf(-128.f, s0, b0), bp1 = fmaf(-128.f, s1, b1);
+        acc[0] += fmaf(s0, dd[0], bp0 * hs0[Gi]);
+        acc[1] += fmaf(s0, dd[1], bp0 * hs1[Gi]);
+        acc[2] += fmaf(s1, dd[2], bp1 * hs0[Gi]);
+        acc[3] += fmaf(s1, dd[3], bp1 * hs1[Gi]);
       }
-      is_sh = __ldcg(&ents[e].flags) & 1;
-      rank0 = 2 * c < T ? __ldcg(&ents[e].rank[2 * c]) : -1;
-      rank1 = 2 * c + 1 < T ? __ldcg(&ents[e].rank[2 * c + 1]) : -1;
-      score0 = 2 * c < T ? __ldcg(&ents[e].score[2 * c]) : 0.f;
-      score1 = 2 * c + 1 < T ? __ldcg(&ents[e].score[2 * c + 1]) : 0.f;
-    }
-    cp_async_wait<RS - 2>();
-    __syncwarp();
-    issue_next();
-    const uint8_t *st = ring + ((i - i0) % RS) * Tl::SLOT;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int r0 = 16 * rb + g, r1 = r0 + 8;
 #pragma unroll
-    for (int G = 0; G < NGI; ++G) {
-      const uint2 a0 = lds64(st + g * Tl::PITCH + G * 32 + 8 * c);
-      const uint2 a1 = lds64(st + (g + 8) * Tl::PITCH + G * 32 + 8 * c);
-      uint32_t p0[2][4], p1[2][4];
-      nib_pairs4(a0.x, p0[0]);
-      nib_pairs4(a0.y, p0[1]);
-      nib_pairs4(a1.x, p1[0]);
-      nib_pairs4(a1.y, p1[1]);
-      float dd[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const int i0m = 2 * (m & 1), h = m >> 1;
-        mma_bf16(dd, p0[h][i0m], p1[h][i0m], p0[h][i0m + 1], p1[h][i0m + 1], hb[G][2 * m],
-                 hb[G][2 * m + 1]);
-      }
-      const int si = G >> GS;
-      const uint16_t *ss = reinterpret_cast<const uint16_t *>(st + Tl::WB);
-      const float s0 = bf2f(ss[g * Tl::NSI + si]), s1 = bf2f(ss[(g + 8) * Tl::NSI + si]);
-      const float b0 = bf2f(ss[Tl::SB / 2 + g * Tl::NSI + si]);
-      const float b1 = bf2f(ss[Tl::SB / 2 + (g + 8) * Tl::NSI + si]);
-      const float bp0 = fmaf(-128.f, s0, b0), bp1 = fmaf(-128.f, s1, b1);
-      acc[0] += fmaf(s0, dd[0], bp0 * hs0[G]);
-      acc[1] += fmaf(s0, dd[1], bp0 * hs1[G]);
-      acc[2] += fmaf(s1, dd[2], bp1 * hs0[G]);
-      acc[3] += fmaf(s1, dd[3], bp1 * hs1[G]);
-    }
-    const int r0 = 16 * rb + g, r1 = r0 + 8;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int n = 2 * c + (q & 1);
-      if (n >= T) continue;
-      const int row = (q >> 1) ? r1 : r0;
-      const float yb = rbf(acc[q]);
-      if (is_sh) {
-        sparts[(size_t)n * H + row] = f2bf(yb);
-      } else {
-        const int rk = (q & 1) ? rank1 : rank0;
-        const float sc = (q & 1) ? score1 : score0;
-        if (rk >= 0) wparts[((size_t)n * p.k + rk) * H + row] = f2bf(__fmul_rn(yb, sc));
+      for (int q = 0; q < 4; ++q) {
+        const int n = 2 * c + (q & 1);
+        if (n >= T) continue;
+        const int row = (q >> 1) ? r1 : r0;
+        const float yb = rbf(acc[q]);
+        if (is_sh) {
+          sparts[(size_t)n * H + row] = f2bf(yb);
+        } else {
+          const int rk = (q & 1) ? rank1 : rank0;
+          const float sc = (q & 1) ? score1 : score0;
+          if (rk >= 0) wparts[((size_t)n * p.k + rk) * H + row] = f2bf(__fmul_rn(yb, sc));
+        }
       }
     }
+    cp_async_wait<0>();
   }
-  cp_async_wait<0>();
-  // ---- tickets: one fence for all of this warp's items, one atomic per item
-  // (lanes in parallel); the warp that completes a 16-row block combines it.
+  if (p.trace && lane == 0) atomicMax(&s_tm[1], (unsigned long long)globaltimer());
+
+  // ---------------- 6. tickets and combine ----------------
+  // One fence for all of this warp's items, one atomic per item (lanes in
+  // parallel); the warp that completes a 16-row block combines it.
   __threadfence();
   __syncwarp();
   unsigned *cnt = wsp<unsigned>(p, p.L.rb_count);
 #pragma unroll 1
-  for (int base = i0; base < i1; base += 32) {
+  for (int base = i0; base < i_end; base += 32) {
     const int i = base + lane;
     int rb = 0;
     bool win = false;
-    if (i < i1) {
+    if (i < i_end) {
       rb = i % RBN;
-      win = atomicAdd(cnt + rb, 1u) == (unsigned)n_entries - 1;
+      win = atomicAdd(cnt + rb, 1u) == (unsigned)n_ent - 1;
     }
     unsigned m = __ballot_sync(0xffffffffu, win);
     if (m) __threadfence();
     while (m) {
-      const int src = __ffs(m) - 1;
-      m &= m - 1;
-      const int rbw = __shfl_sync(0xffffffffu, rb, src);
-      down_combine_block(p, rbw, lane);
-      if (lane == 0) cnt[rbw] = 0u;  // ready for the next launch
+      // up to four completed blocks at a time, one per group of 8 lanes
+      int mine = -1;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int src = m ? __ffs(m) - 1 : 0;
+        const int rbq = __shfl_sync(0xffffffffu, rb, src);
+        if (m && (lane >> 3) == q) mine = rbq;
+        m &= m - 1;
+      }
+      if (mine >= 0) {
+        down_combine_rows(p, s_ok, mine, lane);
+        if ((lane & 7) == 0) cnt[mine] = 0u;  // ready for the next launch
+      }
+      __syncwarp();
     }
+  }
+  if (p.trace) {
+    if (lane == 0) atomicMax(&s_tm[2], (unsigned long long)globaltimer());
+    __syncthreads();
+    if (tid < 3) atomicMax(reinterpret_cast<unsigned long long *>(p.trace + 6 + tid), s_tm[tid]);
   }
   span.end();
 }
 
 // One-time per-kernel attributes: the dynamic shared memory it needs and the
-// largest shared-memory carveout, so that consecutive decode kernels never
-// make an SM switch its L1/shared split.
+// largest shared-memory carveout.
 static cudaError_t decode_kernel_attrs(const void *fn, size_t smem) {
   static std::mutex mu;
   static std::vector<std::pair<const void *, size_t>> done;
@@ -1221,6 +1242,24 @@ int noalloc_scratch(void **out) {
   *out = g_noalloc_ptr[dev];
   return VB_OK;
 }
+
+using LayerFn = void (*)(DecodeParams);
+
+// The layer kernel and its shared memory for (H, I).
+bool layer_kernel(int H, int I, LayerFn *fn, size_t *smem) {
+#define VB_HI(HH, II)                                 \
+  if (H == HH && I == II) {                           \
+    *fn = moe_layer_kernel<HH, II>;                   \
+    *smem = LayerTile<HH, II>::SMEM;                  \
+    return true;                                      \
+  }
+  VB_HI(512, 128) VB_HI(512, 256) VB_HI(512, 512)
+  VB_HI(1024, 128) VB_HI(1024, 256) VB_HI(1024, 512)
+  VB_HI(2048, 128) VB_HI(2048, 256) VB_HI(2048, 512)
+  VB_HI(4096, 128) VB_HI(4096, 256) VB_HI(4096, 512)
+#undef VB_HI
+  return false;
+}
 }  // namespace
 
 extern "C" {
@@ -1253,6 +1292,9 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   VB_REQUIRE(a->workspace && a->workspace_bytes >= L.total,
              "vb_moe_decode: workspace %zu < %zu", a->workspace_bytes, L.total);
   VB_REQUIRE(((uintptr_t)a->workspace % 256) == 0, "vb_moe_decode: workspace must be 256-byte aligned");
+  VB_REQUIRE(((uintptr_t)a->x % 16) == 0 && ((uintptr_t)a->out % 16) == 0 &&
+                 ((uintptr_t)a->residual % 16) == 0,
+             "vb_moe_decode: x, out and residual must be 16-byte aligned");
   for (int i = 0; i < 9; ++i)
     VB_REQUIRE(((uintptr_t)a->pool.ptr[i] % 16) == 0 && (a->pool.slot_stride[i] % 16) == 0 &&
                    (!has_shared || (((uintptr_t)a->shared.ptr[i] % 16) == 0)),
@@ -1272,81 +1314,25 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   p.trace = a->trace;
   p.L = L;
 
-  void (*k1)(DecodeParams) = nullptr;
-  void (*k2)(DecodeParams) = nullptr;
-  const int per = E <= 256 ? 8 : (E <= 512 ? 16 : 32);
-#define VB_K1(HH) (per == 8 ? moe_router_kernel<HH, 8> : per == 16 ? moe_router_kernel<HH, 16> \
-                                                      : moe_router_kernel<HH, 32>)
-  size_t k2_smem = 0;
-  int k2_threads = 0;
-#define VB_K2(HH)                                                             \
-  do {                                                                        \
-    k1 = VB_K1(HH);                                                           \
-    if (p.gshift) {                                                           \
-      k2 = moe_gateup_kernel<HH, 1>;                                          \
-      k2_smem = GateUpTile<HH, 1>::SMEM;                                      \
-      k2_threads = GateUpTile<HH, 1>::THREADS;                                \
-    } else {                                                                  \
-      k2 = moe_gateup_kernel<HH, 0>;                                          \
-      k2_smem = GateUpTile<HH, 0>::SMEM;                                      \
-      k2_threads = GateUpTile<HH, 0>::THREADS;                                \
-    }                                                                         \
-  } while (0)
-  switch (H) {
-    case 512: VB_K2(512); break;
-    case 1024: VB_K2(1024); break;
-    case 2048: VB_K2(2048); break;
-    default: VB_K2(4096); break;
-  }
-#undef VB_K2
-#undef VB_K1
-  void (*k3)(DecodeParams) = nullptr;
-  size_t k3_smem = 0;
-#define VB_K3(II)                                                 \
-  do {                                                            \
-    if (p.gshift) {                                               \
-      k3 = moe_down_kernel<II, 1>;                                \
-      k3_smem = DownTile<II, 1>::SMEM;                            \
-    } else {                                                      \
-      k3 = moe_down_kernel<II, 0>;                                \
-      k3_smem = DownTile<II, 0>::SMEM;                            \
-    }                                                             \
-  } while (0)
-  switch (I) {
-    case 128: VB_K3(128); break;
-    case 256: VB_K3(256); break;
-    default: VB_K3(512); break;
-  }
-#undef VB_K3
+  LayerFn fn = nullptr;
+  size_t smem = 0;
+  VB_REQUIRE(layer_kernel(H, I, &fn, &smem), "vb_moe_decode: no kernel for hidden=%d inter=%d", H, I);
+  cudaError_t err = decode_kernel_attrs((const void *)fn, smem);
+  if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "decode kernel attributes: %s", cudaGetErrorString(err));
+  // The grid barrier needs every CTA resident: one CTA per SM.
+  int per_sm = 0;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, KL_THREADS, smem);
+  if (err != cudaSuccess || per_sm < 1)
+    return set_error(VB_ERR_CUDA, "moe_layer_kernel does not fit an SM (%s)",
+                     err != cudaSuccess ? cudaGetErrorString(err) : "occupancy 0");
 
   cudaStream_t s = as_stream(stream);
   cudaEvent_t *ev = a->timing_events ? (cudaEvent_t *)a->timing_events : nullptr;
   const bool pdl = ev == nullptr;  // event records would break the PDL chain
-  // K1 is a PDL secondary of whatever ran before it on the stream (the
-  // previous block's down kernel): it only reads weights before the wait.
   if (ev) cudaEventRecord(ev[0], s);
-  const size_t smem1 = (size_t)T * H * 2;
-  cudaError_t err = decode_kernel_attrs((const void *)k1, smem1);
-  if (err == cudaSuccess) err = decode_kernel_attrs((const void *)k2, k2_smem);
-  if (err == cudaSuccess) err = decode_kernel_attrs((const void *)k3, k3_smem);
-  if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "decode kernel attributes: %s", cudaGetErrorString(err));
-  const int rpc = K1_WARPS / (H >= 1024 ? 4 : 2);
-  const int grid1 = (E + (has_shared ? 1 : 0) + rpc - 1) / rpc;
-  err = vb_launch(k1, dim3(grid1), dim3(K1_THREADS), smem1, s, pdl, p);
-  if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_router_kernel: %s", cudaGetErrorString(err));
+  err = vb_launch(fn, dim3(sm_count()), dim3(KL_THREADS), smem, s, pdl, p);
+  if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_layer_kernel: %s", cudaGetErrorString(err));
   if (ev) cudaEventRecord(ev[1], s);
-
-  {
-    const int grid2 = std::min(sm_count(), L.max_entries * (I / 16));
-    err = vb_launch(k2, dim3(grid2), dim3(k2_threads), k2_smem, s, pdl, p);
-  }
-  if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_gateup_kernel: %s", cudaGetErrorString(err));
-  if (ev) cudaEventRecord(ev[2], s);
-
-  err = vb_launch(k3, dim3(std::min(sm_count(), L.max_entries * (H / 16))), dim3(K3_THREADS),
-                  k3_smem, s, pdl, p);
-  if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_down_kernel: %s", cudaGetErrorString(err));
-  if (ev) cudaEventRecord(ev[3], s);
   return VB_OK;
 }
 
@@ -1363,12 +1349,11 @@ int vb_moe_decode_noalloc(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   void *scratch = nullptr;
   const int rc = noalloc_scratch(&scratch);
   if (rc != VB_OK) return rc;
-  // The array keeps the previous call's contents: zero the words the kernels
-  // expect at zero (route ticket, entry count, shared gates, row-block
-  // tickets) before this call's kernels, in stream order.
+  // The array keeps the previous call's contents: zero the words the kernel
+  // expects at zero (grid barrier, shared gates, entry counters, row-block
+  // tickets) before this call's kernel, in stream order.
   const DecodeLayout L = decode_layout(a->tokens, a->hidden, a->inter, a->num_experts, a->top_k);
-  const size_t clear = L.zero_end;
-  const cudaError_t e = cudaMemsetAsync(scratch, 0, clear, as_stream(stream));
+  const cudaError_t e = cudaMemsetAsync(scratch, 0, L.zero_end, as_stream(stream));
   if (e != cudaSuccess)
     return set_error(VB_ERR_CUDA, "vb_moe_decode_noalloc: clearing scratch: %s", cudaGetErrorString(e));
   VbMoeDecodeArgs b = *a;

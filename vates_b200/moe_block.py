@@ -113,12 +113,13 @@ class MoeBlock:
 
     @staticmethod
     def timing_events():
-        """Four CUDA events (created) and the C array of their handles for the
-        ``timing`` argument of :meth:`decode`."""
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        """Two CUDA events (created) and the C array of their handles for the
+        ``timing`` argument of :meth:`decode` (recorded before and after the
+        layer kernel)."""
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         for e in evs:
             e.record()
-        arr = (C.c_void_p * 4)(*[e.cuda_event for e in evs])
+        arr = (C.c_void_p * 2)(*[e.cuda_event for e in evs])
         return evs, arr
 
     def new_debug(self, T: int, device="cuda") -> dict:

@@ -142,7 +142,7 @@ class DecodeStack:
 
     def step(self, stream=None, trace=None):
         """One whole-stack step: 48 chained MoE blocks over the T tokens.
-        ``trace`` (int64 [L, 8] device tensor) records per-layer kernel spans."""
+        ``trace`` (int64 [L, 16] device tensor) records per-layer kernel spans and markers."""
         for l, blk in enumerate(self.blocks):
             blk.decode(self.hs[l], out=self.hs[l + 1], residual=self.hs[l],
                        norm_eps=self.norm_eps, stream=stream,
