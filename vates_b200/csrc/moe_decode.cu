@@ -65,7 +65,7 @@ static DecodeLayout decode_layout(int T, int H, int I, int E, int k) {
   DecodeLayout L;
   L.max_entries = T * k + 1;
   size_t off = 0;
-  L.bar = off; off += 16;  // grid barrier: arrivals, generation
+  L.bar = off; off += 16;  // grid barrier: 64-bit arrival count
   L.sgate = off; off += sizeof(float) * DEC_MAX_T;
   off = align_up(off, 16);
   L.ent_done = off; off += sizeof(unsigned) * (size_t)L.max_entries;
@@ -196,23 +196,57 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void st_release(unsigned *p, unsigned v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ unsigned long long ld_acquire64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
+__device__ __forceinline__ unsigned atom_add_acq_rel(unsigned *p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// Sums a[0..7] over the lanes of a warp (4 + 2 + 1 + 1 + 1 shuffles): every
+// round a lane keeps half of its values and receives the partner's copy of
+// them. On return lanes 4t..4t+3 hold the total of value t in a[0] (a fixed
+// order, the same in every lane of the group).
+template <typename F>
+__device__ __forceinline__ void warp_sum8(F (&a)[8], int lane) {
+#pragma unroll
+  for (int w = 4, o = 16; w >= 1; w >>= 1, o >>= 1) {
+    const bool up = lane & o;
+#pragma unroll
+    for (int j = 0; j < w; ++j) {
+      const F keep = up ? a[j + w] : a[j], send = up ? a[j] : a[j + w];
+      a[j] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  a[0] += __shfl_xor_sync(0xffffffffu, a[0], 2);
+  a[0] += __shfl_xor_sync(0xffffffffu, a[0], 1);
+}
+
 __device__ __forceinline__ void red_release_add(unsigned *p, unsigned v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
 constexpr uint64_t KL_WAIT_NS = 2000000000ull;  // bound of every wait
 
-// Waits (acquire) until *p != v (ne) or *p >= v (!ne); false after the bound.
-__device__ __forceinline__ bool wait_word(const unsigned *p, unsigned v, bool ne) {
+// Waits (acquire) until *p >= v; false after the bound.
+__device__ __forceinline__ bool wait_ge(const unsigned *p, unsigned v) {
   const uint64_t t0 = globaltimer();
   for (;;) {
-    const unsigned x = ld_acquire(p);
-    if (ne ? x != v : x >= v) return true;
+    if (ld_acquire(p) >= v) return true;
     if (globaltimer() - t0 > KL_WAIT_NS) return false;
     __nanosleep(128);
+  }
+}
+__device__ __forceinline__ bool wait_ge64(const unsigned long long *p, unsigned long long v) {
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    if (ld_acquire64(p) >= v) return true;
+    if (globaltimer() - t0 > KL_WAIT_NS) return false;
+    __nanosleep(64);
   }
 }
 
@@ -221,11 +255,20 @@ __device__ __forceinline__ bool wait_word(const unsigned *p, unsigned v, bool ne
 // ----------------------------------------------------------------------------
 constexpr int KL_THREADS = 256;
 constexpr int KL_WARPS = KL_THREADS / 32;
-constexpr int KL_PAIRS = KL_WARPS / 2;
 constexpr int KL_MAX_ENT = DEC_MAX_T * DEC_MAX_K + 1;
 constexpr int KL_MAX_ROUTES = DEC_MAX_T * DEC_MAX_K;
 
 constexpr int align_c(int x, int a) { return (x + a - 1) / a * a; }
+
+constexpr int KL_SMEM_MAX = 227 * 1024;
+
+// 16-byte unit u of row r of a staged tile lives at unit swz(r, u): the four
+// rows g = 0..3 that one half-warp reads with 8-byte fragment loads (units
+// 2G and 2G+1 of each row) then fall on distinct banks. U = units per row.
+template <int U>
+__device__ __forceinline__ int swz(int r, int u) {
+  return U >= 8 ? u ^ ((r & 3) << 1) : u ^ (((r >> 1) & 1) << 1);
+}
 
 template <int H, int I>
 struct LayerTile {
@@ -233,39 +276,43 @@ struct LayerTile {
   static constexpr int Q = H >= 1024 ? 2 : 1;
   static constexpr int RPC = KL_WARPS / Q;  // rows per CTA and round
   static constexpr int NVQ = H / (256 * Q);
-  // Gate/up: item (entry, 16 intermediate rows) over a warp pair; a chunk is
-  // 16 rows x 4 groups of 64 columns of gate and up plus their scales.
+  // Gate/up: an item (entry, 16 intermediate rows) is split along the hidden
+  // dimension over the S warps of a group; each warp streams CPW chunks of
+  // it (16 rows x 4 groups of 64 columns of gate and up plus their scales).
   static constexpr int NG = H / 64;
   static constexpr int CG = 4;
   static constexpr int NCH = NG / CG;
-  static constexpr int CPH = NCH / 2;       // chunks per warp of the pair
-  static constexpr int ROWB = H / 2;        // packed bytes per row
-  static constexpr int CROW = CG * 32;      // chunk bytes per row
-  static constexpr int PITCH = CROW + 32;   // padded row pitch in a stage
-  static constexpr int NS64 = H / 64;       // scales per row at group 64
-  static constexpr int WB = 2 * 16 * PITCH; // gate + up codes of a chunk
+  static constexpr int S = NCH < KL_WARPS ? NCH : KL_WARPS;  // warps per item
+  static constexpr int NGRP = KL_WARPS / S;                  // item groups per CTA
+  static constexpr int CPW = NCH / S;                        // chunks per warp and item
+  static constexpr int ROWB = H / 2;         // packed bytes per row
+  static constexpr int CROW = CG * 32;       // chunk bytes per row (8 units)
+  static constexpr int NS64 = H / 64;        // scales per row at group 64
+  static constexpr int WB = 2 * 16 * CROW;   // gate + up codes of a chunk
   static constexpr int CHUNK = WB + 4 * 16 * 8;
-  static constexpr int RS = 3;              // ring stages
-  static constexpr int RING = RS * CHUNK;   // one warp's ring
-  static constexpr int PAIR = 2 * RING + 2048 + 512;  // rings, partials, h tile
   // Down: item (entry, 16 output rows) per warp, in the warp's own ring.
   static constexpr int NGI = I / 64;
   static constexpr int DROWB = I / 2;
-  static constexpr int DPITCH = DROWB + 32;
-  static constexpr int DWB = 16 * DPITCH;
+  static constexpr int DWB = 16 * DROWB;
   static constexpr int DSB = 16 * NGI * 2;  // 16 rows of one scale tensor at group 64
   static constexpr int DSLOT = DWB + 2 * DSB;
-  static constexpr int DRS = RING / DSLOT < 5 ? RING / DSLOT : 5;
   // Shared memory: x fragments [NG][8][4][8] words, group sums [NG][8],
-  // entries, route flags, a few words, then the pair areas.
+  // entries, route flags, a few words, item partials [2][warp][lane][8],
+  // per-warp h tiles [16][8], then one ring per warp.
   static constexpr int XF = NG * DEC_MAX_T * 4 * 8 * 4;
   static constexpr int OFF_XS = XF;
   static constexpr int OFF_ENT = OFF_XS + NG * DEC_MAX_T * 4;
   static constexpr int OFF_OK = OFF_ENT + KL_MAX_ENT * (int)sizeof(DecEntry);
   static constexpr int OFF_MISC = OFF_OK + KL_MAX_ROUTES * 4;
-  static constexpr int OFF_PAIR = align_c(OFF_MISC + 64, 128);
-  static constexpr int SMEM = OFF_PAIR + KL_PAIRS * PAIR;
-  // Router and routing temporaries, inside the pair areas (free until the
+  static constexpr int OFF_RED = align_c(OFF_MISC + 64, 128);
+  static constexpr int OFF_HB = OFF_RED + 2 * KL_WARPS * 32 * 8 * 4;
+  static constexpr int OFF_RING = align_c(OFF_HB + KL_WARPS * 16 * 8 * 4, 128);
+  static constexpr int RS0 = (KL_SMEM_MAX - OFF_RING) / (KL_WARPS * CHUNK);
+  static constexpr int RS = RS0 < 6 ? RS0 : 6;  // ring stages (chunks) per warp
+  static constexpr int RING = RS * CHUNK;
+  static constexpr int SMEM = OFF_RING + KL_WARPS * RING;
+  static constexpr int DRS = RING / DSLOT < 5 ? RING / DSLOT : 5;
+  // Router and routing temporaries, inside the rings (free until the
   // entries are built): x [8][H] bf16, slot table, first route of each
   // expert, routes (expert, slot, score, entry), reduction scratch.
   static constexpr int TMP_TABLE = DEC_MAX_T * H * 2;
@@ -274,9 +321,9 @@ struct LayerTile {
   static constexpr int TMP_RED = TMP_ROUTE + 4 * KL_MAX_ROUTES * 4;
   static constexpr int TMP_PART = TMP_RED + KL_WARPS * DEC_MAX_T * 8;
   static constexpr int TMP_END = TMP_PART + KL_WARPS * DEC_MAX_T * 4;
-  static_assert(TMP_END <= KL_PAIRS * PAIR, "router temporaries");
-  static_assert(SMEM <= 227 * 1024, "layer kernel shared memory");
-  static_assert(DRS >= 2 && CPH >= 1 && NVQ >= 1, "layer tile");
+  static_assert(TMP_END <= KL_WARPS * RING, "router temporaries");
+  static_assert(SMEM <= KL_SMEM_MAX, "layer kernel shared memory");
+  static_assert(RS >= 2 && DRS >= 2 && NVQ >= 1 && NCH % S == 0, "layer tile");
 };
 
 struct GateUpItem {
@@ -302,16 +349,17 @@ template <int H, int I>
 __device__ __forceinline__ void gateup_chunk(uint8_t *stage, const GateUpItem &it, int ch,
                                              int lane, int gs) {
   using Tl = LayerTile<H, I>;
-  // 2 matrices x 16 rows x 8 pieces of 16 bytes; lane -> piece lane%8 of
-  // rows lane/8 + 4j.
-  const int r0 = lane >> 3, p16 = (lane & 7) * 16;
-  const uint8_t *g = it.gw + r0 * Tl::ROWB + ch * Tl::CROW + p16;
-  const uint8_t *u = it.uw + r0 * Tl::ROWB + ch * Tl::CROW + p16;
-  uint8_t *dg = stage + r0 * Tl::PITCH + p16;
+  // 2 matrices x 16 rows x 8 units of 16 bytes; lane -> unit lane%8 of
+  // rows lane/8 + 4j, stored swizzled in 128-byte rows.
+  const int r0 = lane >> 3, un = lane & 7;
+  const uint8_t *g = it.gw + r0 * Tl::ROWB + ch * Tl::CROW + un * 16;
+  const uint8_t *u = it.uw + r0 * Tl::ROWB + ch * Tl::CROW + un * 16;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    cp_async16(dg + 4 * j * Tl::PITCH, g + 4 * j * Tl::ROWB);
-    cp_async16(dg + 16 * Tl::PITCH + 4 * j * Tl::PITCH, u + 4 * j * Tl::ROWB);
+    const int r = r0 + 4 * j;
+    uint8_t *d = stage + r * Tl::CROW + (swz<8>(r, un) << 4);
+    cp_async16(d, g + 4 * j * Tl::ROWB);
+    cp_async16(d + 16 * Tl::CROW, u + 4 * j * Tl::ROWB);
   }
   // Scales: 4 tensors x 16 rows x SCB bytes -> [tensor][row][SCB].
   const int ns = Tl::NS64 >> gs, scb = (Tl::CG >> gs) * 2;
@@ -326,17 +374,18 @@ __device__ __forceinline__ void gateup_chunk(uint8_t *stage, const GateUpItem &i
 }
 
 // Weights of down item (slot, 16-row block rb) into a ring slot:
-// [16 rows x DPITCH] codes, then [16 rows x NSI] scales and biases.
+// [16 rows x DROWB] codes (swizzled units), then [16 rows x NSI] scales and
+// biases.
 template <int H, int I>
 __device__ __forceinline__ void down_issue(uint8_t *slot, const VbQuantPool &pool, int pslot,
                                            int rb, int lane, int gs) {
   using Tl = LayerTile<H, I>;
   const uint8_t *dw = pool_ptr(pool, 6, pslot) + (size_t)rb * 16 * Tl::DROWB;
-  constexpr int CPR = Tl::DROWB / 16;  // 16-byte chunks per row
+  constexpr int CPR = Tl::DROWB / 16;  // 16-byte units per row
 #pragma unroll
   for (int j = 0; j < 16 * CPR / 32; ++j) {
-    const int q = lane + 32 * j, r = q / CPR, c16 = (q % CPR) * 16;
-    cp_async16(slot + r * Tl::DPITCH + c16, dw + r * Tl::DROWB + c16);
+    const int q = lane + 32 * j, r = q / CPR, un = q % CPR;
+    cp_async16(slot + r * Tl::DROWB + (swz<CPR>(r, un) << 4), dw + r * Tl::DROWB + un * 16);
   }
   const int sb = 16 * (Tl::NGI >> gs) * 2, sch = sb / 16;
   for (int q = lane; q < 2 * sch; q += 32) {
@@ -469,24 +518,35 @@ __device__ __noinline__ int route_tokens(const float *logits, const int32_t *tab
     // Keys: bf16 probability bits above (0xFFFF - expert id), so the unsigned
     // maximum is the largest probability with ties to the lower id.
     uint32_t key[PER];
-    uint32_t lb = 0;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
       const int idx = lane + 32 * i;
       key[i] = idx < E ? ((uint32_t)f2bf(__fmul_rn(v[i], inv)) << 16) | (0xFFFFu - idx) : 0u;
-      lb = max(lb, key[i]);
     }
+    // Each lane sorts its keys (descending bitonic network); a pick is then
+    // one warp maximum of the lanes' heads, and the lane holding it pops.
+#pragma unroll
+    for (int size = 2; size <= PER; size <<= 1)
+#pragma unroll
+      for (int stride = size >> 1; stride > 0; stride >>= 1)
+#pragma unroll
+        for (int i = 0; i < PER; ++i) {
+          const int j = i ^ stride;
+          if (j > i) {
+            const uint32_t a = key[i], b = key[j];
+            const bool desc = (i & size) == 0;
+            key[i] = desc ? max(a, b) : min(a, b);
+            key[j] = desc ? min(a, b) : max(a, b);
+          }
+        }
     double ssum = 0.0;
     uint32_t sel = 0;
     for (int r = 0; r < k; ++r) {
-      const uint32_t best = __reduce_max_sync(0xffffffffu, lb);
-      if (lb == best) {  // the one lane holding it drops it and rescans
-        lb = 0;
+      const uint32_t best = __reduce_max_sync(0xffffffffu, key[0]);
+      if (key[0] == best) {  // keys are distinct: one lane holds it
 #pragma unroll
-        for (int i = 0; i < PER; ++i) {
-          if (key[i] == best) key[i] = 0u;
-          lb = max(lb, key[i]);
-        }
+        for (int i = 0; i + 1 < PER; ++i) key[i] = key[i + 1];
+        key[PER - 1] = 0u;
       }
       if (lane == r) sel = best;
       ssum += (double)bf2f(best >> 16);
@@ -581,7 +641,8 @@ template <int H, int I>
 __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p) {
   using Tl = LayerTile<H, I>;
   constexpr int Q = Tl::Q, RPC = Tl::RPC, NVQ = Tl::NVQ, NG = Tl::NG, CG = Tl::CG,
-                CPH = Tl::CPH, RS = Tl::RS, NGI = Tl::NGI, DRS = Tl::DRS;
+                S = Tl::S, NGRP = Tl::NGRP, CPW = Tl::CPW, RS = Tl::RS, NGI = Tl::NGI,
+                DRS = Tl::DRS;
   constexpr int RB = I / 16;    // gate/up items per entry
   constexpr int RBN = H / 16;   // down items per entry
   extern __shared__ __align__(128) uint8_t smem[];
@@ -590,10 +651,10 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
   DecEntry *s_ent = reinterpret_cast<DecEntry *>(smem + Tl::OFF_ENT);
   int32_t *s_ok = reinterpret_cast<int32_t *>(smem + Tl::OFF_OK);
   int *s_misc = reinterpret_cast<int *>(smem + Tl::OFF_MISC);
-  uint8_t *pairs = smem + Tl::OFF_PAIR;
-  uint16_t *xb = reinterpret_cast<uint16_t *>(pairs);  // [T][H] bf16 (router phase)
-  double *s_dred = reinterpret_cast<double *>(pairs + Tl::TMP_RED);
-  float *s_part = reinterpret_cast<float *>(pairs + Tl::TMP_PART);
+  uint8_t *rings = smem + Tl::OFF_RING;
+  uint16_t *xb = reinterpret_cast<uint16_t *>(rings);  // [T][H] bf16 (router phase)
+  double *s_dred = reinterpret_cast<double *>(rings + Tl::TMP_RED);
+  float *s_part = reinterpret_cast<float *>(rings + Tl::TMP_PART);
   __shared__ float s_inv[DEC_MAX_T];
   __shared__ int s_wcnt[KL_WARPS];
   __shared__ unsigned long long s_tm[3];
@@ -645,12 +706,17 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
   }
   if (blockIdx.x == 0)  // entry counters of this launch (all counting follows the grid barrier)
     for (int i = tid; i < p.L.max_entries; i += KL_THREADS) wsp<unsigned>(p, p.L.ent_done)[i] = 0u;
+  for (int i = tid; i < NG * DEC_MAX_T; i += KL_THREADS)
+    if ((i & 7) >= T) xsm[i] = 0.f;  // group sums beyond T
   __syncthreads();
-  if (p.norm_eps > 0.f) {
-    // Unit-weight RMSNorm of the block input (decoder post-attention norm):
-    // y = bf16(x * (1/sqrt(mean(x^2) + eps))), float32 math with an exact
-    // (double) sum of squares: squares of bf16 values have 16 significant
-    // bits, so their double sum does not depend on the order.
+  // Unit-weight RMSNorm of the block input (decoder post-attention norm):
+  // y = bf16(x * (1/sqrt(mean(x^2) + eps))), float32 math with an exact
+  // (double) sum of squares: squares of bf16 values have 16 significant
+  // bits, so their double sum does not depend on the order. Every warp
+  // derives the factors itself (lane t for token t).
+  const bool norm = p.norm_eps > 0.f;
+  float inv_lane = 1.f;
+  if (norm) {
     constexpr int VPT = H / 8;  // uint4 per token
     double ss[DEC_MAX_T];
 #pragma unroll
@@ -670,71 +736,54 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
         }
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-      for (int t = 0; t < DEC_MAX_T; ++t) ss[t] += __shfl_xor_sync(0xffffffffu, ss[t], o);
-    if (lane == 0)
-#pragma unroll
-      for (int t = 0; t < DEC_MAX_T; ++t) s_dred[warp * DEC_MAX_T + t] = ss[t];
+    warp_sum8(ss, lane);
+    if ((lane & 3) == 0) s_dred[warp * DEC_MAX_T + (lane >> 2)] = ss[0];
     __syncthreads();
-    if (tid < T) {
+    if (lane < T) {
       double tot = 0.0;
 #pragma unroll
-      for (int w = 0; w < KL_WARPS; ++w) tot += s_dred[w * DEC_MAX_T + tid];
+      for (int w = 0; w < KL_WARPS; ++w) tot += s_dred[w * DEC_MAX_T + lane];
       const float ms = __fdiv_rn((float)tot, (float)H);
-      s_inv[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.norm_eps)));
+      inv_lane = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, p.norm_eps)));
     }
-    __syncthreads();
-    for (int i = tid; i < T * (H / 8); i += KL_THREADS) {
-      const int t = i / (H / 8);
-      uint4 v = reinterpret_cast<const uint4 *>(xb)[i];
-      uint32_t w[4] = {v.x, v.y, v.z, v.w};
-      const float inv = s_inv[t];
-#pragma unroll
-      for (int q = 0; q < 4; ++q)
-        w[q] = pack_bf2(__fmul_rn(bf2f(w[q] & 0xFFFF), inv), __fmul_rn(bf2f(w[q] >> 16), inv));
-      reinterpret_cast<uint4 *>(xb)[i] = make_uint4(w[0], w[1], w[2], w[3]);
-    }
-    __syncthreads();
   }
   {
-    // x in MMA fragment order: word (G, n, c, w) = x[n][base], x[n][base+4]
-    // with base = 64G + 16c + 8(w/4) + 2((w/2)&1) + (w&1).
-    for (int i = tid; i < T * (H / 2); i += KL_THREADS) {
-      const int n = i / (H / 2), r = i % (H / 2);
-      const int Gi = r >> 5, cc = (r >> 3) & 3, w = r & 7;
-      const int m = w >> 1, pp = w & 1, j = m >> 1, i0 = 2 * (m & 1);
-      const int base = 64 * Gi + 16 * cc + 8 * j + i0 + pp;
-      xf[((Gi * DEC_MAX_T + n) * 4 + cc) * 8 + w] =
-          (uint32_t)xb[(size_t)n * H + base] | ((uint32_t)xb[(size_t)n * H + base + 4] << 16);
-    }
-    // Per-64-column sums (zero beyond T): a fixed pairwise tree per
-    // (group, token), the order of a 32-lane xor-shuffle reduction of
-    // pair sums.
-    for (int i = tid; i < NG * DEC_MAX_T; i += KL_THREADS) {
-      const int Gi = i / DEC_MAX_T, n = i % DEC_MAX_T;
-      float s = 0.f;
-      if (n < T) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(xb + (size_t)n * H + 64 * Gi);
-        float a[32];
+    // One pass over x (8 columns per thread and step): normalise in place,
+    // write the MMA fragment words and the per-64-column sums. Fragment
+    // word (G, n, c, w) = x[n][base], x[n][base + 4] with base = 64G + 16c
+    // + 8(w/4) + 2((w/2)&1) + (w&1): the 8 columns 8v..8v+7 (v = 8G + 2c +
+    // j) give words 4j..4j+3 of (G, n, c). The 8 threads of a 64-column
+    // group add their sums with three shuffles.
+    constexpr int VPT = H / 8;
+    for (int i = tid; i < T * VPT; i += KL_THREADS) {  // warp-uniform bound (VPT % 32 == 0)
+      const int n = i / VPT, v = i % VPT;
+      const float inv = __shfl_sync(0xffffffffu, inv_lane, n);
+      const uint4 q = reinterpret_cast<const uint4 *>(xb)[i];
+      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+      float f[8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const uint4 v = src[q];
-          a[4 * q + 0] = bf_lo(v.x) + bf_hi(v.x);
-          a[4 * q + 1] = bf_lo(v.y) + bf_hi(v.y);
-          a[4 * q + 2] = bf_lo(v.z) + bf_hi(v.z);
-          a[4 * q + 3] = bf_lo(v.w) + bf_hi(v.w);
-        }
-#pragma unroll
-        for (int st = 16; st > 0; st >>= 1)
-#pragma unroll
-          for (int L = 0; L < st; ++L) a[L] = a[L] + a[L + st];
-        s = a[0];
+      for (int j = 0; j < 4; ++j) {
+        f[2 * j] = bf2f(w[j] & 0xFFFF);
+        f[2 * j + 1] = bf2f(w[j] >> 16);
       }
-      xsm[Gi * DEC_MAX_T + n] = s;
+      if (norm) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = rbf(__fmul_rn(f[j], inv));
+        reinterpret_cast<uint4 *>(xb)[i] = make_uint4(pack_bf2(f[0], f[1]), pack_bf2(f[2], f[3]),
+                                                      pack_bf2(f[4], f[5]), pack_bf2(f[6], f[7]));
+      }
+      const int Gi = v >> 3, cc = (v >> 1) & 3, j = v & 1;
+      reinterpret_cast<uint4 *>(xf + ((Gi * DEC_MAX_T + n) * 4 + cc) * 8 + 4 * j)[0] =
+          make_uint4(pack_bf2(f[0], f[4]), pack_bf2(f[1], f[5]), pack_bf2(f[2], f[6]),
+                     pack_bf2(f[3], f[7]));
+      float gsum = ((f[0] + f[1]) + (f[2] + f[3])) + ((f[4] + f[5]) + (f[6] + f[7]));
+      gsum += __shfl_xor_sync(0xffffffffu, gsum, 4);
+      gsum += __shfl_xor_sync(0xffffffffu, gsum, 2);
+      gsum += __shfl_xor_sync(0xffffffffu, gsum, 1);
+      if ((v & 7) == 0) xsm[Gi * DEC_MAX_T + n] = gsum;
     }
   }
+  __syncthreads();
   // Router rows: this CTA's rows (blockIdx.x + G * round) * RPC + rloc.
   for (int round = 0;; ++round) {
     const int rb0 = (blockIdx.x + G * round) * RPC;
@@ -764,13 +813,8 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
           }
         }
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int t = 0; t < DEC_MAX_T; ++t) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
-      if (lane == 0)
-#pragma unroll
-        for (int t = 0; t < DEC_MAX_T; ++t) s_part[(rloc * Q + part) * DEC_MAX_T + t] = acc[t];
+      warp_sum8(acc, lane);
+      if ((lane & 3) == 0) s_part[(rloc * Q + part) * DEC_MAX_T + (lane >> 2)] = acc[0];
     }
     __syncthreads();
     if (tid < RPC * DEC_MAX_T) {
@@ -794,17 +838,13 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
 
   // ---------------- 3. grid barrier, routing ----------------
   if (tid == 0) {
-    unsigned *bar = wsp<unsigned>(p, p.L.bar);  // [0] arrivals, [1] generation
-    const unsigned gen = *reinterpret_cast<volatile unsigned *>(bar + 1);
+    // Arrivals only ever grow (by G per launch, the grid size being fixed per
+    // device): this launch's CTAs see old in [n G, (n + 1) G) and wait for
+    // (n + 1) G.
+    unsigned long long *bar = wsp<unsigned long long>(p, p.L.bar);
     __threadfence();
-    bool ok = true;
-    if (atomicAdd(bar, 1u) == (unsigned)G - 1) {
-      bar[0] = 0u;  // nobody arrives again before the generation moves
-      __threadfence();
-      st_release(bar + 1, gen + 1u);
-    } else {
-      ok = wait_word(bar + 1, gen, true);
-    }
+    const unsigned long long old = atomicAdd(bar, 1ull);
+    const bool ok = wait_ge64(bar, (old / G + 1) * G);
     __threadfence();
     if (!ok) flag_status(p.status, VB_STATUS_TIMEOUT);
     s_misc[1] = ok ? 0 : 1;
@@ -816,9 +856,9 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
   }
   trace_mark(p.trace, 4);
   {
-    int *s_table = reinterpret_cast<int *>(pairs + Tl::TMP_TABLE);
-    int *s_first = reinterpret_cast<int *>(pairs + Tl::TMP_FIRST);
-    int *s_rex = reinterpret_cast<int *>(pairs + Tl::TMP_ROUTE);
+    int *s_table = reinterpret_cast<int *>(rings + Tl::TMP_TABLE);
+    int *s_first = reinterpret_cast<int *>(rings + Tl::TMP_FIRST);
+    int *s_rex = reinterpret_cast<int *>(rings + Tl::TMP_ROUTE);
     int *s_rslot = s_rex + KL_MAX_ROUTES;
     float *s_rscore = reinterpret_cast<float *>(s_rslot + KL_MAX_ROUTES);
     int *s_rent = reinterpret_cast<int *>(s_rscore + KL_MAX_ROUTES);
@@ -835,29 +875,29 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
 #undef VB_ROUTE
     if (tid == 0) s_misc[0] = n;
   }
-  __syncthreads();  // the pair areas are free from here on
+  __syncthreads();  // the rings are free from here on
   trace_mark(p.trace, 5);
   const int n_ent = s_misc[0];
 
   // ---------------- 4. gate/up + SwiGLU ----------------
-  const int pair = warp >> 1, half = warp & 1;
-  uint8_t *pbase = pairs + pair * Tl::PAIR;
-  uint8_t *ring = pbase + half * Tl::RING;
-  float *red = reinterpret_cast<float *>(pbase + 2 * Tl::RING);  // [2][32][8]
-  float *hbuf = red + 2 * 32 * 8;                                 // [16][8]
+  uint8_t *ring = rings + warp * Tl::RING;
+  float *red = reinterpret_cast<float *>(smem + Tl::OFF_RED);            // [2][warp][lane][8]
+  float *hbuf = reinterpret_cast<float *>(smem + Tl::OFF_HB) + warp * 128;  // [16][8]
   unsigned *ent_done = wsp<unsigned>(p, p.L.ent_done);
   {
-    // This pair's items: blockIdx.x + G * (pair + KL_PAIRS * r), r = 0, 1, ...
-    const int first = blockIdx.x + G * pair, step = G * KL_PAIRS;
+    // This group's items: blockIdx.x + G * (grp + NGRP * r), r = 0, 1, ...;
+    // warp wi of the group takes chunks [wi * CPW, (wi + 1) * CPW) of each.
+    const int grp = warp / S, wi = warp % S;
+    const int first = blockIdx.x + G * grp, step = G * NGRP;
     const int n_items = n_ent * RB;
     const int scb = (CG >> gs) * 2;
     GateUpItem cur;
     int issue_q = 0;
     auto issue_next = [&]() {
-      const int r = issue_q / CPH, ch = half * CPH + issue_q % CPH;
+      const int r = issue_q / CPW, ch = wi * CPW + issue_q % CPW;
       const int i = first + r * step;
       if (i < n_items) {
-        if (issue_q % CPH == 0) {
+        if (issue_q % CPW == 0) {
           const int e = i / RB;
           if (p.has_shared && e == 0) gateup_item<H, I>(p.shared, 0, i % RB, gs, cur);
           else gateup_item<H, I>(p.pool, s_ent[e].slot, i % RB, gs, cur);
@@ -869,33 +909,14 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
     };
 #pragma unroll 1
     for (int kq = 0; kq < RS - 1; ++kq) issue_next();
-    if (!half && lane < 9) {
-      // Whole row blocks of this pair's items into L2 in one go (contiguous
-      // 16-row blocks of gate and up codes and of their four scale tensors):
-      // DRAM then streams each block at once and the chunk copies hit L2.
-      // Lanes 6..8 do the same for the slice of the entry's down projection
-      // (rows [rb, rb + 1) * H / RB) that the down phase reads.
-      for (int i = first; i < n_items; i += step) {
-        const int e = i / RB, rb = i % RB;
-        const bool sh = p.has_shared && e == 0;
-        const VbQuantPool &pool = sh ? p.shared : p.pool;
-        const int slot = sh ? 0 : s_ent[e].slot;
-        if (lane < 6) {
-          GateUpItem it;
-          gateup_item<H, I>(pool, slot, rb, gs, it);
-          if (lane < 2) prefetch_l2_bulk(lane ? it.uw : it.gw, 16 * Tl::ROWB);
-          else prefetch_l2_bulk(it.sc[lane - 2], 16 * (Tl::NS64 >> gs) * 2);
-        } else {
-          constexpr int rows = H / RB;
-          const uint32_t rbytes = lane == 6 ? (uint32_t)I / 2 : (uint32_t)(NGI >> gs) * 2;
-          prefetch_l2_bulk(pool_ptr(pool, lane, slot) + (size_t)rb * rows * rbytes, rows * rbytes);
-        }
-      }
-    }
+    // Fragment offsets inside a staged chunk (rows g and g+8 share a swizzle).
+    int fo[CG];
+#pragma unroll
+    for (int gl = 0; gl < CG; ++gl) fo[gl] = g * Tl::CROW + (swz<8>(g, 2 * gl + (c >> 1)) << 4) + (c & 1) * 8;
     float accg[4], accu[4];
 #pragma unroll 1
     for (int q = 0;; ++q) {
-      const int r = q / CPH, cq = q % CPH, ch = half * CPH + cq;
+      const int r = q / CPW, cq = q % CPW, ch = wi * CPW + cq;
       const int item = first + r * step;
       if (item >= n_items) break;
       cp_async_wait<RS - 2>();
@@ -925,10 +946,10 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
           x1 = xp[1];
         }
         const float2 xs = *reinterpret_cast<const float2 *>(xsm + Gi * DEC_MAX_T + 2 * c);
-        const uint2 ag0 = lds64(st + g * Tl::PITCH + gl * 32 + 8 * c);
-        const uint2 ag1 = lds64(st + (g + 8) * Tl::PITCH + gl * 32 + 8 * c);
-        const uint2 au0 = lds64(st + (16 + g) * Tl::PITCH + gl * 32 + 8 * c);
-        const uint2 au1 = lds64(st + (24 + g) * Tl::PITCH + gl * 32 + 8 * c);
+        const uint2 ag0 = lds64(st + fo[gl]);
+        const uint2 ag1 = lds64(st + 8 * Tl::CROW + fo[gl]);
+        const uint2 au0 = lds64(st + 16 * Tl::CROW + fo[gl]);
+        const uint2 au1 = lds64(st + 24 * Tl::CROW + fo[gl]);
         uint32_t pg0[2][4], pg1[2][4], pu0[2][4], pu1[2][4];
         nib_pairs4(ag0.x, pg0[0]);
         nib_pairs4(ag0.y, pg0[1]);
@@ -964,22 +985,26 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
         accu[2] += fmaf(su1, du[2], bpu1 * xs.x);
         accu[3] += fmaf(su1, du[3], bpu1 * xs.y);
       }
-      if (cq == CPH - 1) {
-        // Pair hand-off: the odd warp's partials to the even warp.
-        float *slot = red + ((r & 1) * 32 + lane) * 8;
-        if (half) {
+      if (cq == CPW - 1) {
+        // Group hand-off: every warp's partials to the item's leader, which
+        // adds them in warp order and applies SwiGLU.
+        float *mine = red + (((r & 1) * KL_WARPS + warp) * 32 + lane) * 8;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            slot[j] = accg[j];
-            slot[4 + j] = accu[j];
-          }
+        for (int j = 0; j < 4; ++j) {
+          mine[j] = accg[j];
+          mine[4 + j] = accu[j];
         }
-        named_bar(1 + pair, 64);
-        if (!half) {
+        named_bar(1 + grp, S * 32);
+        if (wi == r % S) {
+          float sg[4] = {0.f, 0.f, 0.f, 0.f}, su[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            accg[j] += slot[j];
-            accu[j] += slot[4 + j];
+          for (int w = 0; w < S; ++w) {
+            const float *o = red + (((r & 1) * KL_WARPS + grp * S + w) * 32 + lane) * 8;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              sg[j] += o[j];
+              su[j] += o[4 + j];
+            }
           }
           // SwiGLU (bf16 per op) of rows g, g+8 x tokens 2c, 2c+1, then h of
           // the 16 rows in fragment order and its per-token sums.
@@ -987,7 +1012,7 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int row = (j >> 1) ? g + 8 : g, n = 2 * c + (j & 1);
-            hbuf[row * 8 + n] = n < T ? swiglu_bf16(rbf(accg[j]), rbf(accu[j])) : 0.f;
+            hbuf[row * 8 + n] = n < T ? swiglu_bf16(rbf(sg[j]), rbf(su[j])) : 0.f;
           }
           __syncwarp();
           uint32_t *hperm = wsp<uint32_t>(p, p.L.hperm);
@@ -1020,23 +1045,25 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
   // ---------------- 5. down projection ----------------
   uint16_t *wparts = wsp<uint16_t>(p, p.L.wparts);
   uint16_t *sparts = wsp<uint16_t>(p, p.L.sparts);
+  // Items wg + nw * j (j < nj): consecutive items of an entry sit on
+  // different warps, so the entries finishing gate/up last are spread thin.
   const int nw = G * KL_WARPS;
   const int wg = blockIdx.x + G * warp;
   const int n_items_d = n_ent * RBN;
-  const int i0 = (int)(((long long)n_items_d * wg) / nw);
-  const int i1 = (int)(((long long)n_items_d * (wg + 1)) / nw);
-  int i_end = i1;
+  const int nj = wg < n_items_d ? (n_items_d - 1 - wg) / nw + 1 : 0;
+  int j_end = nj;
   {
-    int issue_i = i0;
+    int issue_j = 0;
     auto issue_next = [&]() {
-      if (issue_i < i1) {
-        const int e = issue_i / RBN, rb = issue_i % RBN;
+      if (issue_j < nj) {
+        const int i = wg + nw * issue_j;
+        const int e = i / RBN, rb = i % RBN;
         const bool sh = p.has_shared && e == 0;
-        down_issue<H, I>(ring + ((issue_i - i0) % DRS) * Tl::DSLOT, sh ? p.shared : p.pool,
+        down_issue<H, I>(ring + (issue_j % DRS) * Tl::DSLOT, sh ? p.shared : p.pool,
                          sh ? 0 : s_ent[e].slot, rb, lane, gs);
       }
       cp_async_commit();
-      ++issue_i;
+      ++issue_j;
     };
 #pragma unroll 1
     for (int kq = 0; kq < DRS - 1; ++kq) issue_next();
@@ -1049,13 +1076,14 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
     float score0 = 0.f, score1 = 0.f;
     bool is_sh = false;
 #pragma unroll 1
-    for (int i = i0; i < i1; ++i) {
+    for (int jj = 0; jj < nj; ++jj) {
+      const int i = wg + nw * jj;
       const int e = i / RBN, rb = i % RBN;
       if (e != cur_e) {
         // The entry's h is complete once its RB gate/up items are counted.
-        if (!wait_word(ent_done + e, (unsigned)RB, false)) {
+        if (!wait_ge(ent_done + e, (unsigned)RB)) {
           if (lane == 0) flag_status(p.status, VB_STATUS_TIMEOUT);
-          i_end = i;
+          j_end = jj;
           break;
         }
         cur_e = e;
@@ -1092,13 +1120,14 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
       cp_async_wait<DRS - 2>();
       __syncwarp();
       issue_next();
-      const uint8_t *st = ring + ((i - i0) % DRS) * Tl::DSLOT;
+      const uint8_t *st = ring + (jj % DRS) * Tl::DSLOT;
       const uint16_t *ss = reinterpret_cast<const uint16_t *>(st + Tl::DWB);
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int Gi = 0; Gi < NGI; ++Gi) {
-        const uint2 a0 = lds64(st + g * Tl::DPITCH + Gi * 32 + 8 * c);
-        const uint2 a1 = lds64(st + (g + 8) * Tl::DPITCH + Gi * 32 + 8 * c);
+        const int fo = g * Tl::DROWB + (swz<Tl::DROWB / 16>(g, 2 * Gi + (c >> 1)) << 4) + (c & 1) * 8;
+        const uint2 a0 = lds64(st + fo);
+        const uint2 a1 = lds64(st + 8 * Tl::DROWB + fo);
         uint32_t p0[2][4], p1[2][4];
         nib_pairs4(a0.x, p0[0]);
         nib_pairs4(a0.y, p0[1]);
@@ -1142,22 +1171,22 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
   if (p.trace && lane == 0) atomicMax(&s_tm[1], (unsigned long long)globaltimer());
 
   // ---------------- 6. tickets and combine ----------------
-  // One fence for all of this warp's items, one atomic per item (lanes in
-  // parallel); the warp that completes a 16-row block combines it.
-  __threadfence();
+  // One acquire-release ticket per item (lanes in parallel; the warp barrier
+  // orders every lane's stores before them); the warp that completes a
+  // 16-row block combines it.
   __syncwarp();
   unsigned *cnt = wsp<unsigned>(p, p.L.rb_count);
 #pragma unroll 1
-  for (int base = i0; base < i_end; base += 32) {
-    const int i = base + lane;
+  for (int base = 0; base < j_end; base += 32) {
+    const int jj = base + lane;
     int rb = 0;
     bool win = false;
-    if (i < i_end) {
-      rb = i % RBN;
-      win = atomicAdd(cnt + rb, 1u) == (unsigned)n_ent - 1;
+    if (jj < j_end) {
+      rb = (wg + nw * jj) % RBN;
+      win = atom_add_acq_rel(cnt + rb, 1u) == (unsigned)n_ent - 1;
     }
     unsigned m = __ballot_sync(0xffffffffu, win);
-    if (m) __threadfence();
+    __syncwarp();
     while (m) {
       // up to four completed blocks at a time, one per group of 8 lanes
       int mine = -1;
