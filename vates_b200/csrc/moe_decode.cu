@@ -68,9 +68,9 @@ static DecodeLayout decode_layout(int T, int H, int I, int E, int k) {
   L.bar = off; off += 16;  // grid barrier: 64-bit arrival count
   L.sgate = off; off += sizeof(float) * DEC_MAX_T;
   off = align_up(off, 16);
-  L.ent_done = off; off += sizeof(unsigned) * (size_t)L.max_entries;
-  off = align_up(off, 16);
-  L.rb_count = off; off += sizeof(unsigned) * (H / 16);
+  off = align_up(off, 128);
+  L.ent_done = off; off += 128 * (size_t)L.max_entries;  // one 128-byte line per counter
+  L.rb_count = off; off += 128 * (size_t)(H / 16);
   L.zero_end = off;  // [0, zero_end) must be zero before the first call
   off = align_up(off, 256);
   L.logits = off; off += sizeof(float) * (size_t)T * E;
@@ -238,7 +238,7 @@ __device__ __forceinline__ bool wait_ge(const unsigned *p, unsigned v) {
   for (;;) {
     if (ld_acquire(p) >= v) return true;
     if (globaltimer() - t0 > KL_WAIT_NS) return false;
-    __nanosleep(128);
+    __nanosleep(256);
   }
 }
 __device__ __forceinline__ bool wait_ge64(const unsigned long long *p, unsigned long long v) {
@@ -257,6 +257,10 @@ constexpr int KL_THREADS = 256;
 constexpr int KL_WARPS = KL_THREADS / 32;
 constexpr int KL_MAX_ENT = DEC_MAX_T * DEC_MAX_K + 1;
 constexpr int KL_MAX_ROUTES = DEC_MAX_T * DEC_MAX_K;
+// Inter-CTA counters (entry completion, row-block tickets) sit one per
+// 128-byte line (32 words apart), so that polls and atomics on different
+// counters do not queue at one L2 line.
+constexpr int KL_CSTRIDE = 32;
 
 constexpr int align_c(int x, int a) { return (x + a - 1) / a * a; }
 
@@ -290,7 +294,7 @@ struct LayerTile {
   static constexpr int NS64 = H / 64;        // scales per row at group 64
   static constexpr int WB = 2 * 16 * CROW;   // gate + up codes of a chunk
   static constexpr int CHUNK = WB + 4 * 16 * 8;
-  // Down: item (entry, 16 output rows) per warp, in the warp's own ring.
+  // Down: item (entry, 16 output rows) per warp, one ring stage each.
   static constexpr int NGI = I / 64;
   static constexpr int DROWB = I / 2;
   static constexpr int DWB = 16 * DROWB;
@@ -311,7 +315,6 @@ struct LayerTile {
   static constexpr int RS = RS0 < 6 ? RS0 : 6;  // ring stages (chunks) per warp
   static constexpr int RING = RS * CHUNK;
   static constexpr int SMEM = OFF_RING + KL_WARPS * RING;
-  static constexpr int DRS = RING / DSLOT < 5 ? RING / DSLOT : 5;
   // Router and routing temporaries, inside the rings (free until the
   // entries are built): x [8][H] bf16, slot table, first route of each
   // expert, routes (expert, slot, score, entry), reduction scratch.
@@ -323,7 +326,7 @@ struct LayerTile {
   static constexpr int TMP_END = TMP_PART + KL_WARPS * DEC_MAX_T * 4;
   static_assert(TMP_END <= KL_WARPS * RING, "router temporaries");
   static_assert(SMEM <= KL_SMEM_MAX, "layer kernel shared memory");
-  static_assert(RS >= 2 && DRS >= 2 && NVQ >= 1 && NCH % S == 0, "layer tile");
+  static_assert(RS >= 2 && DSLOT <= CHUNK && NVQ >= 1 && NCH % S == 0, "layer tile");
 };
 
 struct GateUpItem {
@@ -641,8 +644,7 @@ template <int H, int I>
 __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p) {
   using Tl = LayerTile<H, I>;
   constexpr int Q = Tl::Q, RPC = Tl::RPC, NVQ = Tl::NVQ, NG = Tl::NG, CG = Tl::CG,
-                S = Tl::S, NGRP = Tl::NGRP, CPW = Tl::CPW, RS = Tl::RS, NGI = Tl::NGI,
-                DRS = Tl::DRS;
+                S = Tl::S, NGRP = Tl::NGRP, CPW = Tl::CPW, RS = Tl::RS, NGI = Tl::NGI;
   constexpr int RB = I / 16;    // gate/up items per entry
   constexpr int RBN = H / 16;   // down items per entry
   extern __shared__ __align__(128) uint8_t smem[];
@@ -705,7 +707,8 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
     }
   }
   if (blockIdx.x == 0)  // entry counters of this launch (all counting follows the grid barrier)
-    for (int i = tid; i < p.L.max_entries; i += KL_THREADS) wsp<unsigned>(p, p.L.ent_done)[i] = 0u;
+    for (int i = tid; i < p.L.max_entries; i += KL_THREADS)
+      wsp<unsigned>(p, p.L.ent_done)[i * KL_CSTRIDE] = 0u;
   for (int i = tid; i < NG * DEC_MAX_T; i += KL_THREADS)
     if ((i & 7) >= T) xsm[i] = 0.f;  // group sums beyond T
   __syncthreads();
@@ -884,41 +887,59 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
   float *red = reinterpret_cast<float *>(smem + Tl::OFF_RED);            // [2][warp][lane][8]
   float *hbuf = reinterpret_cast<float *>(smem + Tl::OFF_HB) + warp * 128;  // [16][8]
   unsigned *ent_done = wsp<unsigned>(p, p.L.ent_done);
-  {
-    // This group's items: blockIdx.x + G * (grp + NGRP * r), r = 0, 1, ...;
-    // warp wi of the group takes chunks [wi * CPW, (wi + 1) * CPW) of each.
-    const int grp = warp / S, wi = warp % S;
-    const int first = blockIdx.x + G * grp, step = G * NGRP;
-    const int n_items = n_ent * RB;
-    const int scb = (CG >> gs) * 2;
-    GateUpItem cur;
-    int issue_q = 0;
-    auto issue_next = [&]() {
+  // Each warp runs one sequence of jobs through its ring: its gate/up chunks,
+  // then its down items, so the down weights stream in as soon as gate/up
+  // stages free up.
+  // Gate/up: this group's items blockIdx.x + G * (grp + NGRP * r), r = 0,
+  // 1, ...; warp wi of the group takes chunks [wi * CPW, (wi + 1) * CPW).
+  const int grp = warp / S, wi = warp % S;
+  const int first = blockIdx.x + G * grp, step = G * NGRP;
+  const int n_items = n_ent * RB;
+  const int nq_gu = (first < n_items ? (n_items - 1 - first) / step + 1 : 0) * CPW;
+  // Down: a contiguous entry-major range of items per warp (warps of
+  // consecutive global index sit on different SMs), so a warp mostly loads
+  // one entry's h.
+  const int nw = G * KL_WARPS;
+  const int wg = blockIdx.x + G * warp;
+  const int n_items_d = n_ent * RBN;
+  const int d0 = (int)(((long long)n_items_d * wg) / nw);
+  const int nj = (int)(((long long)n_items_d * (wg + 1)) / nw) - d0;
+  int j_end = nj;
+  GateUpItem cur;
+  int issue_q = 0;
+  auto issue_next = [&]() {
+    uint8_t *stage = ring + (issue_q % RS) * Tl::CHUNK;
+    if (issue_q < nq_gu) {
       const int r = issue_q / CPW, ch = wi * CPW + issue_q % CPW;
       const int i = first + r * step;
-      if (i < n_items) {
-        if (issue_q % CPW == 0) {
-          const int e = i / RB;
-          if (p.has_shared && e == 0) gateup_item<H, I>(p.shared, 0, i % RB, gs, cur);
-          else gateup_item<H, I>(p.pool, s_ent[e].slot, i % RB, gs, cur);
-        }
-        gateup_chunk<H, I>(ring + (issue_q % RS) * Tl::CHUNK, cur, ch, lane, gs);
+      if (issue_q % CPW == 0) {
+        const int e = i / RB;
+        if (p.has_shared && e == 0) gateup_item<H, I>(p.shared, 0, i % RB, gs, cur);
+        else gateup_item<H, I>(p.pool, s_ent[e].slot, i % RB, gs, cur);
       }
-      cp_async_commit();
-      ++issue_q;
-    };
+      gateup_chunk<H, I>(stage, cur, ch, lane, gs);
+    } else if (issue_q - nq_gu < nj) {
+      const int i = d0 + (issue_q - nq_gu);
+      const int e = i / RBN, rb = i % RBN;
+      const bool sh = p.has_shared && e == 0;
+      down_issue<H, I>(stage, sh ? p.shared : p.pool, sh ? 0 : s_ent[e].slot, rb, lane, gs);
+    }
+    cp_async_commit();
+    ++issue_q;
+  };
 #pragma unroll 1
-    for (int kq = 0; kq < RS - 1; ++kq) issue_next();
+  for (int kq = 0; kq < RS - 1; ++kq) issue_next();
+  {
+    const int scb = (CG >> gs) * 2;
     // Fragment offsets inside a staged chunk (rows g and g+8 share a swizzle).
     int fo[CG];
 #pragma unroll
     for (int gl = 0; gl < CG; ++gl) fo[gl] = g * Tl::CROW + (swz<8>(g, 2 * gl + (c >> 1)) << 4) + (c & 1) * 8;
     float accg[4], accu[4];
 #pragma unroll 1
-    for (int q = 0;; ++q) {
+    for (int q = 0; q < nq_gu; ++q) {
       const int r = q / CPW, cq = q % CPW, ch = wi * CPW + cq;
       const int item = first + r * step;
-      if (item >= n_items) break;
       cp_async_wait<RS - 2>();
       __syncwarp();
       issue_next();  // into the stage consumed one chunk ago
@@ -988,7 +1009,8 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
       if (cq == CPW - 1) {
         // Group hand-off: every warp's partials to the item's leader, which
         // adds them in warp order and applies SwiGLU.
-        float *mine = red + (((r & 1) * KL_WARPS + warp) * 32 + lane) * 8;
+        const int b = r & 1;
+        float *mine = red + ((b * KL_WARPS + warp) * 32 + lane) * 8;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           mine[j] = accg[j];
@@ -999,7 +1021,7 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
           float sg[4] = {0.f, 0.f, 0.f, 0.f}, su[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
           for (int w = 0; w < S; ++w) {
-            const float *o = red + (((r & 1) * KL_WARPS + grp * S + w) * 32 + lane) * 8;
+            const float *o = red + ((b * KL_WARPS + grp * S + w) * 32 + lane) * 8;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               sg[j] += o[j];
@@ -1033,41 +1055,17 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
             wsp<float>(p, p.L.hsum)[((size_t)e * DEC_MAX_T + lane) * RB + rb] = sh;
           }
           __syncwarp();
-          if (lane == 0) red_release_add(ent_done + e, 1u);  // h rows of this item are out
+          if (lane == 0) red_release_add(ent_done + e * KL_CSTRIDE, 1u);  // h rows of this item are out
         }
       }
     }
-    cp_async_wait<0>();
-    __syncwarp();
   }
   if (p.trace && lane == 0) atomicMax(&s_tm[0], (unsigned long long)globaltimer());
 
   // ---------------- 5. down projection ----------------
   uint16_t *wparts = wsp<uint16_t>(p, p.L.wparts);
   uint16_t *sparts = wsp<uint16_t>(p, p.L.sparts);
-  // Items wg + nw * j (j < nj): consecutive items of an entry sit on
-  // different warps, so the entries finishing gate/up last are spread thin.
-  const int nw = G * KL_WARPS;
-  const int wg = blockIdx.x + G * warp;
-  const int n_items_d = n_ent * RBN;
-  const int nj = wg < n_items_d ? (n_items_d - 1 - wg) / nw + 1 : 0;
-  int j_end = nj;
   {
-    int issue_j = 0;
-    auto issue_next = [&]() {
-      if (issue_j < nj) {
-        const int i = wg + nw * issue_j;
-        const int e = i / RBN, rb = i % RBN;
-        const bool sh = p.has_shared && e == 0;
-        down_issue<H, I>(ring + (issue_j % DRS) * Tl::DSLOT, sh ? p.shared : p.pool,
-                         sh ? 0 : s_ent[e].slot, rb, lane, gs);
-      }
-      cp_async_commit();
-      ++issue_j;
-    };
-#pragma unroll 1
-    for (int kq = 0; kq < DRS - 1; ++kq) issue_next();
-
     const int nsi = NGI >> gs, sbh = 16 * nsi;  // scales per row; bf16 per scale tensor
     int cur_e = -1;
     uint32_t hb[NGI][8];
@@ -1077,11 +1075,11 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
     bool is_sh = false;
 #pragma unroll 1
     for (int jj = 0; jj < nj; ++jj) {
-      const int i = wg + nw * jj;
+      const int i = d0 + jj;
       const int e = i / RBN, rb = i % RBN;
       if (e != cur_e) {
         // The entry's h is complete once its RB gate/up items are counted.
-        if (!wait_ge(ent_done + e, (unsigned)RB)) {
+        if (!wait_ge(ent_done + e * KL_CSTRIDE, (unsigned)RB)) {
           if (lane == 0) flag_status(p.status, VB_STATUS_TIMEOUT);
           j_end = jj;
           break;
@@ -1117,10 +1115,10 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
         score0 = 2 * c < T ? s_ent[e].score[2 * c] : 0.f;
         score1 = 2 * c + 1 < T ? s_ent[e].score[2 * c + 1] : 0.f;
       }
-      cp_async_wait<DRS - 2>();
+      cp_async_wait<RS - 2>();
       __syncwarp();
       issue_next();
-      const uint8_t *st = ring + (jj % DRS) * Tl::DSLOT;
+      const uint8_t *st = ring + ((nq_gu + jj) % RS) * Tl::CHUNK;
       const uint16_t *ss = reinterpret_cast<const uint16_t *>(st + Tl::DWB);
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -1182,8 +1180,8 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
     int rb = 0;
     bool win = false;
     if (jj < j_end) {
-      rb = (wg + nw * jj) % RBN;
-      win = atom_add_acq_rel(cnt + rb, 1u) == (unsigned)n_ent - 1;
+      rb = (d0 + jj) % RBN;
+      win = atom_add_acq_rel(cnt + rb * KL_CSTRIDE, 1u) == (unsigned)n_ent - 1;
     }
     unsigned m = __ballot_sync(0xffffffffu, win);
     __syncwarp();
@@ -1199,7 +1197,7 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
       }
       if (mine >= 0) {
         down_combine_rows(p, s_ok, mine, lane);
-        if ((lane & 7) == 0) cnt[mine] = 0u;  // ready for the next launch
+        if ((lane & 7) == 0) cnt[mine * KL_CSTRIDE] = 0u;  // ready for the next launch
       }
       __syncwarp();
     }
