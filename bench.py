@@ -30,6 +30,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "MoE tokens/s and HBM GB/s (decode T≤4); prefill tok/s at 1/2/4/8 B200"
 EXPERT_BYTES = 1_769_472          # blob_layout stride at H=2048, I=512, 4-bit g64
+LAYER_TRAFFIC_PER_ENTRY = (73_213_440 + 1_418_752) / 33  # dram read + write / entries
 ROUTER_BYTES = 512 * 2048 * 2
 SHARED_GATE_BYTES = 2048 * 2
 
@@ -418,6 +419,11 @@ def run_decode(args, world, rank, local):
     hbm_gbs = step_bytes / (ms / 1e3) / 1e9
     layer_bytes = step_bytes / L  # per launch, algorithmic
     achieved = layer_bytes / (launch_ms / 1e3) / 1e9
+    # DRAM traffic per launch: one ncu capture of a 4-layer case (33 entries
+    # = 32 routed experts + the shared one per launch) read+wrote
+    # LAYER_TRAFFIC_PER_ENTRY bytes per entry; scaled to this run's mean
+    # entries per launch.
+    traffic = LAYER_TRAFFIC_PER_ENTRY * (sum(U) / L + 1)
 
     out = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -438,7 +444,8 @@ def run_decode(args, world, rank, local):
                 "h2d_bytes_per_step": T * 2048 * 2, "d2h_bytes_per_step": T * 2048 * 2},
         "roofline": {"kernel": "moe_layer_kernel", "bound": "hbm", "achieved": achieved,
                      "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "traffic": None,
+                     "frac": achieved / hbm_peak, "traffic": traffic,
+                     "traffic_unit": "bytes per launch",
                      "bytes_per_launch": layer_bytes, "ms_per_launch": launch_ms,
                      "in_graph_gbs": layer_bytes / (layer_us / 1e6) / 1e9},
         "kernel_trace_us": {"span": kspan, "layer_period": layer_us,
