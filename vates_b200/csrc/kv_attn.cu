@@ -6,27 +6,20 @@
 // inverse V rotation (kv_quant_patch.py:67-68).
 //
 // Split-K ("flash decoding"): each CTA owns one (batch, kv head) and a
-// contiguous key range, processed in rounds of 64 keys; a combine kernel
-// merges the per-split (max, sum, output) triples in split order.
-// Inside a CTA, warp w owns head-dim group w (64 dims, one scale/bias group):
-//  - QK^T: A = q (16 query rows x 16 dims, kept in registers), B = K codes
-//    of 8 keys as exact bf16 (128+q) built with one LOP3 per pair; per key
-//    the group score is s*D + (b-128*s)*sum(q). The four group partials are
-//    exchanged through shared memory and added in group order, so every warp
-//    sees identical scores (rounded to bf16 as MLX does).
-//  - Online softmax in float32; P is multiplied by the key's V scale of the
-//    warp's group and rounded to bf16 as the A operand of P.V; the V bias
-//    term sum(p*b) is accumulated on the CUDA cores.
-//  - V codes (3-bit) of the warp's 64 dims are unpacked to exact bf16 in
-//    shared memory and read as B fragments with ldmatrix.trans.
+// contiguous key range processed in 16-key tiles; a combine kernel merges the
+// per-split (max, sum, output) triples in split order. Two partial kernels:
+// kv_attn1_kernel for up to 8 query rows per kv head (decode, T = 1; every
+// warp owns whole tiles) and kv_attn4_kernel for 9..32 rows (MTP verify,
+// T = 4; the CTA shares each unpacked tile, warp w takes rows 8w..8w+7).
+// Both compute S^T = K Q^T and O^T += V^T P^T on mma.sync with the codes as
+// exact bf16 values 128 + code, the per-64-dim-group scale and bias applied
+// as s*D + (b - 128 s)*sum and the V bias term sum(p*b) on the CUDA cores;
+// scores and P are rounded to bf16 as MLX does.
 #include "common.cuh"
 
 namespace vb {
 
-constexpr int ATT_WARPS = 4;
 constexpr int ATT_ROUND = 64;
-constexpr int ATT_SX_STRIDE = 68;   // floats per score row (64 + pad)
-constexpr int ATT_VS_STRIDE = 72;   // bf16 per unpacked V row (64 + pad)
 
 struct AttnParams {
   const uint16_t *q;
@@ -51,273 +44,6 @@ __device__ __forceinline__ float bf_at2(const uint2 &v, int i) {
   return (i & 1) ? __uint_as_float(w & 0xFFFF0000u) : __uint_as_float(w << 16);
 }
 
-__device__ __forceinline__ uint32_t v3_pair(uint32_t u, int s0) {
-  // codes at bit s0 and s0+3 of u -> exact bf16 pair (c0, c1)
-  const uint32_t lo = u >> s0;
-  const uint32_t hi = (s0 + 3 <= 16) ? (u << (16 - s0 - 3)) : (u >> (s0 + 3 - 16));
-  uint32_t pr = ((lo & 0x7u) | (hi & 0x70000u)) | 0x43004300u;
-  __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162 *>(&pr);
-  const __nv_bfloat162 off = __floats2bfloat162_rn(128.f, 128.f);
-  v = __hsub2(v, off);
-  return *reinterpret_cast<uint32_t *>(&v);
-}
-
-template <int MT>
-__global__ void __launch_bounds__(ATT_WARPS * 32, 2) kv_attn_partial_kernel(AttnParams p) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  float *Sx = reinterpret_cast<float *>(smem_raw);  // [2][4][16*MT][68]
-  uint16_t *Vs = reinterpret_cast<uint16_t *>(Sx + 2 * ATT_WARPS * 16 * MT * ATT_SX_STRIDE);
-  float2 *ksc = reinterpret_cast<float2 *>(Vs + ATT_WARPS * ATT_ROUND * ATT_VS_STRIDE);
-  float2 *vsc = ksc + ATT_WARPS * ATT_ROUND;
-
-  const int bh = blockIdx.x;  // b * Hkv + hkv
-  const int split = blockIdx.y;
-  const int b = bh / p.Hkv, hkv = bh % p.Hkv;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int g = lane >> 2, c = lane & 3;
-  const int G = warp;
-  const int k_begin = split * p.kps;
-  const int k_end = min(p.S, k_begin + p.kps);
-
-  // ---- q fragments (scaled, bf16) for this warp's dim group ----
-  uint32_t aq[MT][4][4];
-  float qsum[MT][2];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = 16 * mt + g + 8 * h;
-      float vals[16];
-      float part = 0.f;
-      if (r < p.QR) {
-        const int rep_i = r / p.L, l = r % p.L;
-        const int hq = hkv * p.rep + rep_i;
-        const uint16_t *qp = p.q + (((size_t)b * p.Hq + hq) * p.L + l) * 256 + 64 * G + 16 * c;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          vals[i] = rbf(__fmul_rn(bf2f(qp[i]), p.scale));
-          part += vals[i];
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) vals[i] = 0.f;
-      }
-#pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const int j = m >> 1, i0 = 2 * (m & 1);
-        const int d0 = 8 * j + i0;
-        aq[mt][m][h] = pack_bf2(vals[d0], vals[d0 + 4]);
-        aq[mt][m][2 + h] = pack_bf2(vals[d0 + 1], vals[d0 + 5]);
-      }
-      part += __shfl_xor_sync(0xffffffffu, part, 1);
-      part += __shfl_xor_sync(0xffffffffu, part, 2);
-      qsum[mt][h] = part;
-    }
-  }
-
-  float O[MT][8][4];
-  float m_run[MT][2], l_run[MT][2], bsum[MT][2];
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-    for (int nd = 0; nd < 8; ++nd)
-#pragma unroll
-      for (int q = 0; q < 4; ++q) O[mt][nd][q] = 0.f;
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      m_run[mt][h] = -INFINITY;
-      l_run[mt][h] = 0.f;
-      bsum[mt][h] = 0.f;
-    }
-  }
-
-  const size_t head_row0 = (size_t)bh * p.cap;
-  uint16_t *Vw = Vs + warp * ATT_ROUND * ATT_VS_STRIDE;
-  float2 *kscw = ksc + warp * ATT_ROUND;
-  float2 *vscw = vsc + warp * ATT_ROUND;
-  int buf = 0;
-
-  for (int kb = k_begin; kb < k_end; kb += ATT_ROUND, buf ^= 1) {
-    // ---- per-warp loads: scales, K words, V unpack ----
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int kl = 2 * lane + h;
-      const int key = min(kb + kl, p.S - 1);
-      const size_t sidx = (head_row0 + key) * 4 + G;
-      const float ks_ = bf2f(__ldg(p.ks + sidx)), kb_ = bf2f(__ldg(p.kb + sidx));
-      const float vs_ = bf2f(__ldg(p.vs + sidx)), vb_ = bf2f(__ldg(p.vb + sidx));
-      kscw[kl] = make_float2(ks_, fmaf(-128.f, ks_, kb_));
-      vscw[kl] = make_float2(vs_, vb_);
-      const uint32_t *vrow = p.vc + (head_row0 + key) * 24 + 6 * G;
-      uint32_t w[7];
-      const uint2 v01 = *reinterpret_cast<const uint2 *>(vrow);
-      const uint2 v23 = *reinterpret_cast<const uint2 *>(vrow + 2);
-      const uint2 v45 = *reinterpret_cast<const uint2 *>(vrow + 4);
-      w[0] = v01.x; w[1] = v01.y; w[2] = v23.x; w[3] = v23.y; w[4] = v45.x; w[5] = v45.y; w[6] = 0;
-      uint16_t *dst = Vw + kl * ATT_VS_STRIDE;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int bit = 24 * i, wi = bit >> 5, sh = bit & 31;
-        const uint32_t u = __funnelshift_r(w[wi], w[wi + 1], sh) & 0xFFFFFFu;
-        uint4 o;
-        o.x = v3_pair(u, 0);
-        o.y = v3_pair(u, 6);
-        o.z = v3_pair(u, 12);
-        o.w = v3_pair(u, 18);
-        *reinterpret_cast<uint4 *>(dst + 8 * i) = o;
-      }
-    }
-    uint2 kw[8];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const int key = min(kb + 8 * nt + g, p.S - 1);
-      kw[nt] = ldg_nc_v2(reinterpret_cast<const uint8_t *>(p.kc + (head_row0 + key) * 32) + 32 * G + 8 * c);
-    }
-    __syncwarp();
-
-    // ---- partial scores of this group ----
-    float *Sxw = Sx + ((size_t)buf * ATT_WARPS + warp) * 16 * MT * ATT_SX_STRIDE;
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const float2 ks0 = kscw[8 * nt + 2 * c], ks1 = kscw[8 * nt + 2 * c + 1];
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        float d[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const int i0 = 2 * (m & 1);
-          const uint32_t wv = (m >> 1) ? kw[nt].y : kw[nt].x;
-          mma_bf16(d, aq[mt][m][0], aq[mt][m][1], aq[mt][m][2], aq[mt][m][3],
-                   nib_pair(wv, i0), nib_pair(wv, i0 + 1));
-        }
-        const float s00 = fmaf(ks0.x, d[0], ks0.y * qsum[mt][0]);
-        const float s01 = fmaf(ks1.x, d[1], ks1.y * qsum[mt][0]);
-        const float s10 = fmaf(ks0.x, d[2], ks0.y * qsum[mt][1]);
-        const float s11 = fmaf(ks1.x, d[3], ks1.y * qsum[mt][1]);
-        float *r0 = Sxw + (16 * mt + g) * ATT_SX_STRIDE + 8 * nt + 2 * c;
-        float *r1 = r0 + 8 * ATT_SX_STRIDE;
-        *reinterpret_cast<float2 *>(r0) = make_float2(s00, s01);
-        *reinterpret_cast<float2 *>(r1) = make_float2(s10, s11);
-      }
-    }
-    __syncthreads();
-
-    // ---- full scores, online softmax, P fragments ----
-    const float *Sxb = Sx + (size_t)buf * ATT_WARPS * 16 * MT * ATT_SX_STRIDE;
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) {
-      float sv[8][4];
-      float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int row = 16 * mt + g + 8 * (q >> 1);
-          const int kl = 8 * nt + 2 * c + (q & 1);
-          float s = 0.f;
-#pragma unroll
-          for (int w = 0; w < ATT_WARPS; ++w)
-            s += Sxb[((size_t)w * 16 * MT + row) * ATT_SX_STRIDE + kl];
-          s = rbf(s);
-          const int key = kb + kl;
-          bool ok = row < p.QR && key < k_end;
-          if (p.causal && ok) ok = key <= p.S - p.L + (row % p.L);
-          s = ok ? s : -INFINITY;
-          sv[nt][q] = s;
-          mx[q >> 1] = fmaxf(mx[q >> 1], s);
-        }
-      }
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
-        mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
-      }
-      float mnew[2], alpha[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        mnew[h] = fmaxf(m_run[mt][h], mx[h]);
-        alpha[h] = (m_run[mt][h] == -INFINITY) ? 0.f : expf(m_run[mt][h] - mnew[h]);
-        if (mnew[h] == -INFINITY) alpha[h] = 1.f;
-        m_run[mt][h] = mnew[h];
-        l_run[mt][h] *= alpha[h];
-        bsum[mt][h] *= alpha[h];
-      }
-#pragma unroll
-      for (int nd = 0; nd < 8; ++nd) {
-        O[mt][nd][0] *= alpha[0];
-        O[mt][nd][1] *= alpha[0];
-        O[mt][nd][2] *= alpha[1];
-        O[mt][nd][3] *= alpha[1];
-      }
-      uint32_t ap[4][4];
-#pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
-        float pr[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int h = q >> 1;
-          const float e = sv[nt][q] == -INFINITY ? 0.f : expf(sv[nt][q] - mnew[h]);
-          const float2 vsb = vscw[8 * nt + 2 * c + (q & 1)];
-          l_run[mt][h] += e;
-          bsum[mt][h] = fmaf(e, vsb.y, bsum[mt][h]);
-          pr[q] = e * vsb.x;
-        }
-        const int ks = nt >> 1, hi = nt & 1;
-        ap[ks][2 * hi + 0] = pack_bf2(pr[0], pr[1]);
-        ap[ks][2 * hi + 1] = pack_bf2(pr[2], pr[3]);
-      }
-      // ---- P.V over this warp's 64 dims ----
-#pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const int mi = lane >> 3, ri = lane & 7;
-#pragma unroll
-        for (int nd = 0; nd < 8; nd += 2) {
-          const int key = 16 * ks + ri + 8 * (mi & 1);
-          const int dim = 8 * (nd + (mi >> 1));
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4_trans(b0, b1, b2, b3, Vw + key * ATT_VS_STRIDE + dim);
-          mma_bf16(O[mt][nd], ap[ks][0], ap[ks][1], ap[ks][2], ap[ks][3], b0, b1);
-          mma_bf16(O[mt][nd + 1], ap[ks][0], ap[ks][1], ap[ks][2], ap[ks][3], b2, b3);
-        }
-      }
-    }
-    __syncwarp();
-  }
-
-  // ---- write split partials ----
-  const size_t cta = (size_t)bh * p.nsplit + split;
-#pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      float l = l_run[mt][h], bs = bsum[mt][h];
-      l += __shfl_xor_sync(0xffffffffu, l, 1);
-      l += __shfl_xor_sync(0xffffffffu, l, 2);
-      bs += __shfl_xor_sync(0xffffffffu, bs, 1);
-      bs += __shfl_xor_sync(0xffffffffu, bs, 2);
-      const int row = 16 * mt + g + 8 * h;
-      if (row < p.QR) {
-        float *orow = p.opart + (cta * 32 + row) * 256 + 64 * G;
-#pragma unroll
-        for (int nd = 0; nd < 8; ++nd) {
-          *reinterpret_cast<float2 *>(orow + 8 * nd + 2 * c) =
-              make_float2(O[mt][nd][2 * h] + bs, O[mt][nd][2 * h + 1] + bs);
-        }
-        if (warp == 0 && c == 0) {
-          p.mpart[cta * 32 + row] = m_run[mt][h];
-          p.lpart[cta * 32 + row] = l;
-        }
-      }
-    }
-  }
-}
-
-// Merge of the split partials: grid (query row, 8 chunks of 32 dims), 256
-// threads = 32 dims x 8 split lanes. Each CTA finds the row max over the
-// splits, keeps exp(m_s - M) of every split in shared memory, sums its
-// split lanes' shares per dim and adds the 8 lanes in lane order; the result
-// is rounded to bf16, with the optional inverse V rotation (4x4 blocks of
-// R_v^T, R rounded to bf16; a 32-dim chunk holds 8 whole blocks).
 constexpr int ATT_MAX_SPLITS = 1024;
 
 __global__ void __launch_bounds__(256) kv_attn_combine_kernel(AttnParams p) {
@@ -735,12 +461,311 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
   }
 }
 
+// ----------------------------------------------------------------------------
+// Multi-position path (8 < rep * L <= 32 query rows per kv head: the MTP
+// verify block, T = 4): the CTA walks 16-key tiles together. Its 128 threads
+// unpack the tile's codes once into shared memory as exact bf16 128 + code
+// (K in the (0,4,1,5,2,6,3,7) order of one LOP3 per pair inside every 8
+// dims, V in dim order), and warp w takes query rows [8w, 8w + 8): scores
+// S^T = K Q^T with K as the A operand (ldmatrix) and the 8 rows as N,
+// per 64-dim group s*D + (b-128s)*sum(q); online softmax; O^T += V^T P^T
+// with V^T by ldmatrix.trans. The rows of different warps are disjoint, so
+// every warp writes its own rows of the split partial.
+// ----------------------------------------------------------------------------
+constexpr int A4_WARPS = 4;
+constexpr int A4_PITCH = 256 + 8;                          // bf16 per unpacked row
+constexpr int A4_TILE = 16 * A4_PITCH;                     // bf16 per unpacked 16-key tile
+constexpr int A4_RAW = 16 * 128 + 16 * 96 + 4 * 16 * 8;    // K codes, V codes, 4 scale tensors
+constexpr int A4_NRAW = 3;                                // staged tiles (two ahead)
+constexpr int A4_SMEM = A4_NRAW * A4_RAW + 2 * 2 * A4_TILE * 2;  // raw, (K, V) unpacked x2
+
+__device__ __forceinline__ void ldsm_x4(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3,
+                                        const void *smem_ptr) {
+  const uint32_t a = (uint32_t)__cvta_generic_to_shared(smem_ptr);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+
+// Raw tile (16 keys from key0; keys past S-1 read key S-1 and are masked
+// later) -> staging: K codes [16][128 B] (16-byte chunk j of key k at chunk
+// j ^ (k % 8), so that eight keys' same chunk sit on distinct banks), V
+// codes [16][96 B], then K scale, K bias, V scale, V bias [4][16][8 B]; 288
+// copies over 128 threads.
+__device__ __forceinline__ void a4_fetch(const uint8_t *kbase, const uint8_t *vbase,
+                                         const uint8_t *const *sc, int S, int key0, uint8_t *raw,
+                                         int tid) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const int q = tid + 128 * i;
+    if (q < 128) {
+      const int kr = q >> 3, j = q & 7, key = min(key0 + kr, S - 1);
+      cp_async16(raw + kr * 128 + ((j ^ (kr & 7)) << 4), kbase + (size_t)key * 128 + j * 16);
+    } else if (q < 224) {
+      const int qq = q - 128, key = min(key0 + qq / 6, S - 1);
+      cp_async16(raw + 2048 + qq * 16, vbase + (size_t)key * 96 + (qq % 6) * 16);
+    } else if (q < 288) {
+      const int qq = q - 224, t = qq >> 4, key = min(key0 + (qq & 15), S - 1);
+      cp_async8(raw + 3584 + qq * 8, sc[t] + (size_t)key * 8);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(A4_WARPS * 32, 3) kv_attn4_kernel(AttnParams p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int bh = blockIdx.x, split = blockIdx.y;
+  const int b = bh / p.Hkv, hkv = bh % p.Hkv;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int k_begin = split * p.kps;
+  const int k_end = min(p.S, k_begin + p.kps);
+  uint8_t *raw0 = smem_raw;
+  uint16_t *tiles = reinterpret_cast<uint16_t *>(smem_raw + A4_NRAW * A4_RAW);  // [2][K, V][16][PITCH]
+
+  // Q^T B fragments of row 8w + g in the stored K order (k-step kk holds
+  // dims 16kk + c, +4 and 16kk + 8 + c, +4 for lane c) and the per-group q
+  // sums of rows 2c, 2c+1 of this warp.
+  uint32_t qb[16][2];
+  float qs[4][2];
+  {
+    const int r = 8 * warp + g;
+    float part[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint16_t *qp = nullptr;
+    if (r < p.QR) {
+      const int rep_i = r / p.L, l = r % p.L;
+      qp = p.q + (((size_t)b * p.Hq + hkv * p.rep + rep_i) * p.L + l) * 256;
+    }
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (qp) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] = rbf(__fmul_rn(bf2f(qp[16 * kk + c + 4 * j]), p.scale));
+      }
+      qb[kk][0] = pack_bf2(v[0], v[1]);
+      qb[kk][1] = pack_bf2(v[2], v[3]);
+      part[kk >> 2] += (v[0] + v[1]) + (v[2] + v[3]);
+    }
+#pragma unroll
+    for (int G = 0; G < 4; ++G) {
+      float t = part[G];
+      t += __shfl_xor_sync(0xffffffffu, t, 1);
+      t += __shfl_xor_sync(0xffffffffu, t, 2);
+      qs[G][0] = __shfl_sync(0xffffffffu, t, (2 * c) * 4);
+      qs[G][1] = __shfl_sync(0xffffffffu, t, (2 * c + 1) * 4);
+    }
+  }
+
+  float O[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) O[i][0] = O[i][1] = O[i][2] = O[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  float bsum[4][2], psum[4][2];
+#pragma unroll
+  for (int G = 0; G < 4; ++G) bsum[G][0] = bsum[G][1] = psum[G][0] = psum[G][1] = 0.f;
+
+  const size_t head_row0 = (size_t)bh * p.cap;
+  const int n_tiles = (k_end - k_begin + 15) / 16;
+  const uint8_t *kbase = reinterpret_cast<const uint8_t *>(p.kc + head_row0 * 32);
+  const uint8_t *vbase = reinterpret_cast<const uint8_t *>(p.vc + head_row0 * 24);
+  const uint8_t *scb[4] = {reinterpret_cast<const uint8_t *>(p.ks + head_row0 * 4),
+                           reinterpret_cast<const uint8_t *>(p.kb + head_row0 * 4),
+                           reinterpret_cast<const uint8_t *>(p.vs + head_row0 * 4),
+                           reinterpret_cast<const uint8_t *>(p.vb + head_row0 * 4)};
+  const int row0 = 8 * warp + 2 * c;  // rows of this lane's score / output columns
+#pragma unroll 1
+  for (int t = 0; t < A4_NRAW - 1; ++t) {
+    if (t < n_tiles) a4_fetch(kbase, vbase, scb, p.S, k_begin + 16 * t, raw0 + t * A4_RAW, tid);
+    cp_async_commit();
+  }
+#pragma unroll 1
+  for (int t = 0; t < n_tiles; ++t) {
+    const int tn = t + A4_NRAW - 1;
+    if (tn < n_tiles) a4_fetch(kbase, vbase, scb, p.S, k_begin + 16 * tn, raw0 + (tn % A4_NRAW) * A4_RAW, tid);
+    cp_async_commit();
+    cp_async_wait<A4_NRAW - 1>();
+    __syncthreads();  // tile t staged by every thread
+    const uint8_t *rw = raw0 + (t % A4_NRAW) * A4_RAW;
+    uint16_t *Kt = tiles + (t & 1) * 2 * A4_TILE, *Vt = Kt + A4_TILE;
+    const int key0 = k_begin + 16 * t;
+    {
+      // K: thread -> key tid % 16, 32 codes (16 bytes) from byte 16 (tid / 16):
+      // the eight lanes of a store phase hold eight different keys.
+      const int key = tid & 15, part = tid >> 4;
+      const uint4 w = *reinterpret_cast<const uint4 *>(rw + key * 128 + ((part ^ (key & 7)) << 4));
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+      uint4 *dk = reinterpret_cast<uint4 *>(Kt + key * A4_PITCH + part * 32);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t pr[4];
+        nib_pairs4(ws[j], pr);
+        dk[j] = make_uint4(pr[0], pr[1], pr[2], pr[3]);
+      }
+      // V: thread -> key tid % 16, codes 32 (tid / 16) .. +32 (12 bytes)
+      const uint32_t *vw = reinterpret_cast<const uint32_t *>(rw + 2048 + key * 96 + part * 12);
+      const uint32_t v0 = vw[0], v1 = vw[1], v2 = vw[2];
+      uint4 *dv = reinterpret_cast<uint4 *>(Vt + key * A4_PITCH + part * 32);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t u = j == 0 ? (v0 & 0xFFFFFFu)
+                         : j == 1 ? (__funnelshift_r(v0, v1, 24) & 0xFFFFFFu)
+                         : j == 2 ? (__funnelshift_r(v1, v2, 16) & 0xFFFFFFu)
+                                  : (v2 >> 8);
+        dv[j] = make_uint4(v3_pair128(u, 0), v3_pair128(u, 6), v3_pair128(u, 12), v3_pair128(u, 18));
+      }
+    }
+    // Scales of keys g, g+8 (read before the barrier: the staging buffer is
+    // refilled once every thread has passed it).
+    const uint8_t *Sk = rw + 3584;
+    const uint2 ksg = lds_u2(Sk + g * 8), ks8 = lds_u2(Sk + (g + 8) * 8);
+    const uint2 kbg = lds_u2(Sk + 128 + g * 8), kb8 = lds_u2(Sk + 128 + (g + 8) * 8);
+    const uint2 vsg = lds_u2(Sk + 256 + g * 8), vs8 = lds_u2(Sk + 256 + (g + 8) * 8);
+    const uint2 vbg = lds_u2(Sk + 384 + g * 8), vb8 = lds_u2(Sk + 384 + (g + 8) * 8);
+    __syncthreads();  // unpacked tile complete
+
+    // ---- scores S^T for keys g, g+8 and rows row0, row0+1 ----
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint16_t *ka = Kt + (lane & 15) * A4_PITCH + (lane >> 4) * 8;
+#pragma unroll
+    for (int G = 0; G < 4; ++G) {
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k4 = 0; k4 < 4; ++k4) {
+        const int kk = 4 * G + k4;
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(a0, a1, a2, a3, ka + 16 * kk);
+        mma_bf16(d, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+      }
+      const float s_g = bf_at2(ksg, G), s_8 = bf_at2(ks8, G);
+      const float bp_g = fmaf(-128.f, s_g, bf_at2(kbg, G));
+      const float bp_8 = fmaf(-128.f, s_8, bf_at2(kb8, G));
+      sc[0] += fmaf(s_g, d[0], bp_g * qs[G][0]);
+      sc[1] += fmaf(s_g, d[1], bp_g * qs[G][1]);
+      sc[2] += fmaf(s_8, d[2], bp_8 * qs[G][0]);
+      sc[3] += fmaf(s_8, d[3], bp_8 * qs[G][1]);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int key = key0 + g + 8 * (j >> 1);
+      const int row = row0 + (j & 1);
+      bool ok = row < p.QR && key < k_end;
+      if (p.causal && ok) ok = key <= p.S - p.L + (row % p.L);
+      sc[j] = ok ? rbf(sc[j]) : -INFINITY;
+    }
+    // ---- online softmax (rows row0, row0+1) ----
+    float mx[2] = {fmaxf(sc[0], sc[2]), fmaxf(sc[1], sc[3])};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 4));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 8));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 16));
+    }
+    float mnew[2], alpha[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mnew[h] = fmaxf(m_run[h], mx[h]);
+      alpha[h] = (m_run[h] == -INFINITY) ? 0.f : expf(m_run[h] - mnew[h]);
+      if (mnew[h] == -INFINITY) alpha[h] = 1.f;
+      m_run[h] = mnew[h];
+    }
+    if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        l_run[h] *= alpha[h];
+#pragma unroll
+        for (int G = 0; G < 4; ++G) {
+          bsum[G][h] *= alpha[h];
+          psum[G][h] *= alpha[h];
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        O[i][0] *= alpha[0];
+        O[i][1] *= alpha[1];
+        O[i][2] *= alpha[0];
+        O[i][3] *= alpha[1];
+      }
+    }
+    float e[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int h = j & 1;
+      e[j] = sc[j] == -INFINITY ? 0.f : expf(sc[j] - mnew[h]);
+      l_run[h] += e[j];
+    }
+    // P^T fragments per V group: p = bf16(e * vs); V bias term on the side.
+    uint32_t pB[4][2];
+#pragma unroll
+    for (int G = 0; G < 4; ++G) {
+      const float sg = bf_at2(vsg, G), s8 = bf_at2(vs8, G);
+      const float bg = bf_at2(vbg, G), b8 = bf_at2(vb8, G);
+      bsum[G][0] = fmaf(e[0], bg, fmaf(e[2], b8, bsum[G][0]));
+      bsum[G][1] = fmaf(e[1], bg, fmaf(e[3], b8, bsum[G][1]));
+      const uint32_t x0 = pack_bf2(e[0] * sg, e[1] * sg);  // key g: rows row0, row0+1
+      const uint32_t x1 = pack_bf2(e[2] * s8, e[3] * s8);  // key g+8
+      psum[G][0] += __uint_as_float(x0 << 16) + __uint_as_float(x1 << 16);
+      psum[G][1] += __uint_as_float(x0 & 0xFFFF0000u) + __uint_as_float(x1 & 0xFFFF0000u);
+      pB[G][0] = movmatrix_trans(x0);
+      pB[G][1] = movmatrix_trans(x1);
+    }
+    // ---- O^T += V^T P^T (V as 128 + c; 128 * sum(p) removed at the end) ----
+    {
+      const int q = lane >> 3, r = lane & 7;
+      const int key = (q >> 1) * 8 + r, dq = (q & 1) * 8;
+#pragma unroll
+      for (int G = 0; G < 4; ++G) {
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_trans(a0, a1, a2, a3, Vt + key * A4_PITCH + 64 * G + 16 * mt + dq);
+          mma_bf16(O[4 * G + mt], a0, a1, a2, a3, pB[G][0], pB[G][1]);
+        }
+      }
+    }
+  }
+  cp_async_wait<0>();
+
+  // ---- reduce the lane partials of l and the V bias sums (over g) ----
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+      l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], o);
+#pragma unroll
+      for (int G = 0; G < 4; ++G) {
+        bsum[G][h] += __shfl_xor_sync(0xffffffffu, bsum[G][h], o);
+        psum[G][h] += __shfl_xor_sync(0xffffffffu, psum[G][h], o);
+      }
+    }
+  }
+  // ---- this warp's rows of the split partial ----
+  const size_t cta = (size_t)bh * p.nsplit + split;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = row0 + h;
+    if (row >= p.QR) continue;
+    float *op = p.opart + (cta * 32 + row) * 256;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int G = i >> 2, mt = i & 3;
+      const int d0 = 64 * G + 16 * mt + g;
+      const float off = fmaf(-128.f, psum[G][h], bsum[G][h]);
+      op[d0] = O[i][h] + off;
+      op[d0 + 8] = O[i][2 + h] + off;
+    }
+    if (g == 0) {
+      p.mpart[cta * 32 + row] = m_run[h];
+      p.lpart[cta * 32 + row] = l_run[h];
+    }
+  }
+}
+
+// Keys per split: about three CTAs per SM over all (batch, kv head) pairs,
+// in multiples of 64 keys.
 static void attn_split(int bhk, int S, int &nsplit, int &kps) {
-  int target = (2 * 148 + bhk - 1) / bhk;
+  int target = (3 * 148 + bhk - 1) / bhk;
   if (target < 1) target = 1;
   kps = (S + target - 1) / target;
   kps = (kps + ATT_ROUND - 1) / ATT_ROUND * ATT_ROUND;
-  if (kps < ATT_ROUND) kps = ATT_ROUND;
   nsplit = (S + kps - 1) / kps;
 }
 
@@ -754,8 +779,8 @@ size_t vb_kv_attn_workspace_size(int32_t batch, int32_t q_heads, int32_t L,
                                  int32_t dim, int32_t keys) {
   (void)q_heads; (void)L; (void)dim;
   if (batch <= 0 || keys <= 0) return 0;
-  // Upper bound over kv_heads >= 1: splits <= 296 per (batch, kv head) and
-  // at most 296 CTAs overall plus one per (batch, kv head).
+  // Upper bound for kv_heads <= 64: at most 3 x 148 split CTAs overall plus
+  // one per (batch, kv head) (the split rounds keys up to 64-key multiples).
   const size_t ctas = 3 * 148 + (size_t)batch * 64;
   return align_up(ctas * 32 * 256 * sizeof(float), 256) + 2 * align_up(ctas * 32 * sizeof(float), 256);
 }
@@ -798,46 +823,23 @@ int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
   p.lpart = reinterpret_cast<float *>(ws + obytes + mbytes);
   p.out = out;
   cudaStream_t s = as_stream(stream);
+  const dim3 grid(batch * kv_heads, p.nsplit);
   if (p.QR <= 8) {
-    // split for the single-position kernel: 3 CTAs per SM, 64-key multiples
-    int target = (3 * 148 + batch * kv_heads - 1) / (batch * kv_heads);
-    if (target < 1) target = 1;
-    int kps = (keys + target - 1) / target;
-    kps = (kps + 63) / 64 * 64;
-    p.kps = kps;
-    p.nsplit = (keys + kps - 1) / kps;
-    VB_REQUIRE(p.nsplit <= ATT_MAX_SPLITS, "vb_kv_decode_attn: %d splits", p.nsplit);
-    const size_t ctas1 = (size_t)batch * kv_heads * p.nsplit;
-    const size_t ob1 = align_up(ctas1 * 32 * 256 * sizeof(float), 256);
-    const size_t mb1 = align_up(ctas1 * 32 * sizeof(float), 256);
-    VB_REQUIRE(workspace_bytes >= ob1 + 2 * mb1, "vb_kv_decode_attn: workspace %zu < %zu",
-               workspace_bytes, ob1 + 2 * mb1);
-    p.mpart = reinterpret_cast<float *>(ws + ob1);
-    p.lpart = reinterpret_cast<float *>(ws + ob1 + mb1);
-    static bool attr_done = false;
-    if (!attr_done) {
+    static bool attr1_done = false;
+    if (!attr1_done) {
       cudaFuncSetAttribute(kv_attn1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, A1_SMEM);
-      attr_done = true;
+      attr1_done = true;
     }
-    kv_attn1_kernel<<<dim3(batch * kv_heads, p.nsplit), A1_WARPS * 32, A1_SMEM, s>>>(p);
-    int rc1 = check_launch("kv_attn1_kernel");
-    if (rc1) return rc1;
-    kv_attn_combine_kernel<<<dim3(batch * q_heads * L, 8), 256, 0, s>>>(p);
-    return check_launch("kv_attn_combine_kernel");
-  }
-  const int MT = p.QR > 16 ? 2 : 1;
-  const size_t smem = (size_t)2 * ATT_WARPS * 16 * MT * ATT_SX_STRIDE * sizeof(float) +
-                      (size_t)ATT_WARPS * ATT_ROUND * ATT_VS_STRIDE * sizeof(uint16_t) +
-                      (size_t)2 * ATT_WARPS * ATT_ROUND * sizeof(float2);
-  dim3 grid(batch * kv_heads, p.nsplit);
-  if (MT == 1) {
-    cudaFuncSetAttribute(kv_attn_partial_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kv_attn_partial_kernel<1><<<grid, ATT_WARPS * 32, smem, s>>>(p);
+    kv_attn1_kernel<<<grid, A1_WARPS * 32, A1_SMEM, s>>>(p);
   } else {
-    cudaFuncSetAttribute(kv_attn_partial_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kv_attn_partial_kernel<2><<<grid, ATT_WARPS * 32, smem, s>>>(p);
+    static bool attr4_done = false;
+    if (!attr4_done) {
+      cudaFuncSetAttribute(kv_attn4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, A4_SMEM);
+      attr4_done = true;
+    }
+    kv_attn4_kernel<<<grid, A4_WARPS * 32, A4_SMEM, s>>>(p);
   }
-  int rc = check_launch("kv_attn_partial_kernel");
+  const int rc = check_launch(p.QR <= 8 ? "kv_attn1_kernel" : "kv_attn4_kernel");
   if (rc) return rc;
   kv_attn_combine_kernel<<<dim3(batch * q_heads * L, 8), 256, 0, s>>>(p);
   return check_launch("kv_attn_combine_kernel");
