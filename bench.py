@@ -319,6 +319,48 @@ def run_isoquant_leg(steps: int = 20, warmup: int = 3, S: int = 131072, layers: 
     return res
 
 
+def run_decode_t1_leg(st, stream, steps: int = 20, warmup: int = 3):
+    """Config 0 shape (decode, T=1) over the same 48-layer stack: token 0 of
+    the config-1 input. Each token is routed independently, so token 0's
+    experts are among the resident ones. Bytes per layer: its distinct
+    experts + the shared one + router + w_sg + x/out."""
+    import torch
+    hbm_peak, _, peak_kind = peaks()
+    L = len(st.blocks)
+    hs = [torch.empty((1, 2048), dtype=torch.bfloat16, device="cuda") for _ in range(L + 1)]
+    hs[0].copy_(st.hs[0][:1])
+
+    def chain():
+        for l, blk in enumerate(st.blocks):
+            blk.decode(hs[l], out=hs[l + 1], residual=hs[l], norm_eps=st.norm_eps, stream=stream)
+
+    with torch.cuda.stream(stream):
+        chain()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        chain()
+    for _ in range(max(warmup, 3)):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    del g
+    per_layer = [len(set(r)) for r in st.token_routes(0)]
+    step_bytes = sum(u * EXPERT_BYTES + EXPERT_BYTES + ROUTER_BYTES + SHARED_GATE_BYTES + 2 * 2048 * 2
+                     for u in per_layer)
+    gbs = step_bytes / (ms / 1e3) / 1e9
+    return {"workload": "decode_T1_48layers", "ms_per_step": ms, "tokens_per_s": 1 / (ms / 1e3),
+            "us_per_layer": ms * 1e3 / L, "hbm_gbs_algorithmic": gbs,
+            "frac_of_hbm_peak": gbs / hbm_peak, "peak_kind": peak_kind,
+            "bytes_per_step": step_bytes, "steps": steps, "warmup": max(warmup, 3)}
+
+
 def run_decode(args, world, rank, local):
     import torch
     from vates_b200.synth import DecodeStack
@@ -454,6 +496,7 @@ def run_decode(args, world, rank, local):
         "clocks": clocks,
     }
     if not args.no_extra:
+        out["decode_t1"] = run_decode_t1_leg(st, stream)
         if world == 1:
             out["prefill"] = run_prefill_leg()
             out["isoquant"] = run_isoquant_leg()

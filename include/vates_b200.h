@@ -158,9 +158,10 @@ typedef struct VbMoeDecodeArgs {
 } VbMoeDecodeArgs;
 
 /* The decode workspace must be zero-filled before its first use; every call
- * leaves it reusable by the next call on the same stream (after a call that
- * reported VB_STATUS_TIMEOUT it must be zero-filled again). Calls sharing
- * one workspace must not overlap on the GPU. */
+ * leaves it reusable by the next call on the same stream with the same
+ * hidden size (any tokens, inter, experts, top_k within its size; after a
+ * call that reported VB_STATUS_TIMEOUT it must be zero-filled again). Calls
+ * sharing one workspace must not overlap on the GPU. */
 size_t vb_moe_decode_workspace_size(int32_t tokens, int32_t hidden,
                                     int32_t inter, int32_t num_experts,
                                     int32_t top_k);

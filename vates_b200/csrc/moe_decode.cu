@@ -68,9 +68,12 @@ static DecodeLayout decode_layout(int T, int H, int I, int E, int k) {
   L.bar = off; off += 16;  // grid barrier: 64-bit arrival count
   L.sgate = off; off += sizeof(float) * DEC_MAX_T;
   off = align_up(off, 16);
+  // Tickets before the entry counters: their place depends only on H, and
+  // every launch zeroes its own entry counters, so calls with different T
+  // (same H) can share one workspace.
   off = align_up(off, 128);
-  L.ent_done = off; off += 128 * (size_t)L.max_entries;  // one 128-byte line per counter
-  L.rb_count = off; off += 128 * (size_t)(H / 16);
+  L.rb_count = off; off += 128 * (size_t)(H / 16);       // one 128-byte line per counter
+  L.ent_done = off; off += 128 * (size_t)L.max_entries;
   L.zero_end = off;  // [0, zero_end) must be zero before the first call
   off = align_up(off, 256);
   L.logits = off; off += sizeof(float) * (size_t)T * E;

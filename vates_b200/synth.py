@@ -149,6 +149,18 @@ class DecodeStack:
                        trace=None if trace is None else trace[l])
         return self.hs[-1]
 
+    def token_routes(self, t: int) -> list[list[int]]:
+        """Routed experts of token ``t`` per layer for the fixed input (tokens
+        are routed independently, so a single-token chain of token ``t``
+        sees the same experts)."""
+        out = []
+        for l, blk in enumerate(self.blocks):
+            dbg = blk.new_debug(self.T, self.device)
+            blk.decode(self.hs[l], out=torch.empty_like(self.hs[l]), residual=self.hs[l],
+                       debug=dbg, norm_eps=self.norm_eps)
+            out.append(dbg["inds"][t].tolist())
+        return out
+
     def unique_experts(self) -> list[int]:
         """Distinct routed experts per layer for the fixed input (U_l)."""
         out = []
