@@ -34,6 +34,7 @@ enum {
   VB_ERR_INVALID = 1,   /* bad argument or unsupported shape */
   VB_ERR_CUDA = 2,      /* CUDA runtime error while launching */
   VB_ERR_WORKSPACE = 3, /* workspace too small */
+  VB_ERR_CAPACITY = 4,  /* residency request does not fit the layer's slots */
 };
 
 /* Device status bits (OR-ed into *status by kernels). */
@@ -418,6 +419,72 @@ int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
                       float scale, int32_t causal, uint16_t *out,
                       void *workspace, size_t workspace_bytes,
                       vb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Expert residency: per-layer expert -> slot state of a pool of `cap` slots
+ * (host state machine, one mutex per manager).
+ * Replaces the native demand path behind ResidentExpertPool
+ * (mlx_streaming/core/cache/resident_pool.py:54-580; native/ext/pool/
+ * demand.cpp). A slot is taken from the front of the free rows, else from the
+ * LFU victim: the resident expert with the smallest access count, ties to the
+ * earliest inserted, never pinned and never one of the current request
+ * (choose_victim_locked 514-529, alloc_slot_locked 542-564). Counts go up by
+ * one per unique expert of each demand and, with decay_interval > 0, halve
+ * every decay_interval accesses (note_access_locked 566-637). lfu = 0 keeps
+ * every count at zero, so the victim is the earliest inserted (FIFO). */
+typedef struct VbResidency VbResidency;
+VbResidency *vb_res_create(int32_t layers, int32_t cap, int32_t num_experts,
+                           int32_t lfu, int32_t decay_interval);
+void vb_res_destroy(VbResidency *r);
+/* demand_core_locked (demand.cpp:966-1027): local[i] = slot of ids[i] after
+ * the call. Every unique miss gets a slot; the (expert, slot) pairs to load
+ * go to place_expert / place_slot (nullable, room for n) in first-miss order,
+ * their count to *n_place. stats (nullable) = {hits, misses, loads}. When the
+ * unique experts of ids plus the pinned experts not in ids exceed cap,
+ * nothing is placed, local is all 0 and the call returns VB_ERR_CAPACITY
+ * (the reference's over_capacity). */
+int vb_res_demand(VbResidency *r, int32_t layer, const int32_t *ids, int32_t n,
+                  int32_t *local, int32_t *place_expert, int32_t *place_slot,
+                  int32_t *n_place, int64_t *stats);
+/* real_pin (demand.cpp:364-394): pins the unique experts of `experts`
+ * (first-seen order, count in *n_unique) and gives each a slot; placed[u] = 1
+ * where the expert was not resident and must be loaded. VB_ERR_CAPACITY when
+ * the pinned set would exceed cap (nothing changes). */
+int vb_res_pin(VbResidency *r, int32_t layer, const int32_t *experts, int32_t n,
+               int32_t *slots, int32_t *placed, int32_t *n_unique);
+/* The layer's expert -> slot table (num_experts entries, -1 = not resident),
+ * the table the slot-table gather and the decode kernel read
+ * (real_table_set_locked, demand.cpp:306-318). */
+int vb_res_table(VbResidency *r, int32_t layer, int32_t *table);
+/* LFU access counts per expert (num_experts entries; the reference's
+ * RealLayer::freq, demand.cpp:22-37). */
+int vb_res_counts(VbResidency *r, int32_t layer, uint32_t *counts);
+/* Resident (expert, slot) pairs in insertion order (nullable outputs with room
+ * for cap; count in *n). */
+int vb_res_resident(VbResidency *r, int32_t layer, int32_t *experts,
+                    int32_t *slots, int32_t *n);
+
+/* Pool fill: copies n expert blobs (host or device memory, the expert_blob_v1
+ * layout of prep/blob_layout.py:14-32: gate, up, down x {weight, scales,
+ * biases}) into pool slots slots[i] on `stream` (stream-ordered; host blobs
+ * should be pinned for asynchronous copies). A pool whose nine tensors are one
+ * blob row per slot takes one copy per expert, otherwise nine. Replaces the
+ * per-miss loads of ResidentExpertPool (resident_pool.py:414-470) and the
+ * blob_loader path feeding them. */
+int vb_pool_fill(const VbQuantPool *pool, int32_t hidden, int32_t inter,
+                 int32_t group, int32_t bits, const int32_t *slots,
+                 const void *const *blobs, int32_t n, vb_stream_t stream);
+/* Device gather of whole expert blobs: row out_rows[r] (r when out_rows is
+ * NULL) of out = row experts[r] of blob_store, rows of blob_stride bytes (a
+ * multiple of 16; 16-byte aligned pointers). experts and out_rows are device
+ * arrays; blob_store may be device memory or mapped pinned host memory. With
+ * out = a blob pool and out_rows = its slots this fills the misses of one
+ * demand in one launch. Ids and rows are not range-checked on the device: the
+ * caller passes the placements of vb_res_demand. Replaces the
+ * blob_mmap_gather_u4 kernel (native/ext/io/blob_load.cpp:185-196). */
+int vb_blob_gather(const void *blob_store, int64_t blob_stride,
+                   const int32_t *experts, const int32_t *out_rows, int32_t n,
+                   void *out, vb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Seeded synthetic data (bench and tests): fills `words` uint32 with a

@@ -15,6 +15,7 @@ VB_OK = 0
 VB_STATUS_MISS = 1
 VB_STATUS_BOUNDS = 2
 VB_STATUS_TIMEOUT = 4
+VB_ERR_CAPACITY = 4
 
 
 class VbQuantPool(C.Structure):
@@ -132,6 +133,16 @@ _SIGNATURES = {
     "vb_kv_decode_attn": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32,
                                  _I32, _I32, _I32, _I32, _I32, _I32, C.c_float, _I32, _P,
                                  _P, _SZ, _P]),
+    "vb_res_create": (_P, [_I32, _I32, _I32, _I32, _I32]),
+    "vb_res_destroy": (None, [_P]),
+    "vb_res_demand": (_I32, [_P, _I32, _P, _I32, _P, _P, _P, _P, _P]),
+    "vb_res_pin": (_I32, [_P, _I32, _P, _I32, _P, _P, _P]),
+    "vb_res_table": (_I32, [_P, _I32, _P]),
+    "vb_res_counts": (_I32, [_P, _I32, _P]),
+    "vb_res_resident": (_I32, [_P, _I32, _P, _P, _P]),
+    "vb_pool_fill": (_I32, [C.POINTER(VbQuantPool), _I32, _I32, _I32, _I32, _P, _P, _I32,
+                            _P]),
+    "vb_blob_gather": (_I32, [_P, _I64, _P, _P, _I32, _P, _P]),
     "vb_synth_fill_u32": (_I32, [_P, _I64, C.c_uint64, _P]),
     "vb_synth_fill_scales": (_I32, [_P, _P, _I64, C.c_uint64, C.c_float, C.c_float,
                                     C.c_float, _P]),

@@ -26,6 +26,7 @@ SOURCES = [
     "kv_quant.cu",
     "kv_attn.cu",
     "moe_prefill.cu",
+    "residency.cu",
 ]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
