@@ -361,6 +361,113 @@ def run_decode_t1_leg(st, stream, steps: int = 20, warmup: int = 3):
             "bytes_per_step": step_bytes, "steps": steps, "warmup": max(warmup, 3)}
 
 
+def run_residency_leg(layers: int = 8, steps: int = 12, warmup: int = 4, T: int = 4,
+                      cap: int = 192, seed: int = 1):
+    """Config-1 layers over a pool of ``cap`` < 512 slots per layer, misses
+    loaded on demand: every step decodes a fresh seeded T-token input (new
+    routes), so the miss path runs as it would for unseen tokens. All 512
+    experts of each layer sit in an HBM blob store; each layer call is one
+    vb_moe_decode_resident: "route_first" = a routing-only launch, read-back,
+    native demand, one vb_blob_gather of the placed experts, table copy, the
+    block launch; "optimistic" = the block first and again only after a miss.
+    Device-timed with events over whole steps (host work between launches
+    included). The gather kernel is also timed on its own: bytes = 2 x
+    experts x 1,769,472 (read + write)."""
+    import torch
+    from vates_b200.moe_block import MoeBlock, Workspace
+    from vates_b200.pool import QuantPool
+    from vates_b200.residency import DeviceBlobStore, ResidentExpertPool
+    from vates_b200.synth import E, H, input_tokens, make_layer
+    hbm_peak, _, peak_kind = peaks()
+    store_pool = QuantPool.empty_blob(layers * E, H, 512, 4, 64)
+    ws = Workspace()
+    src = [make_layer(seed, l, store_pool.view(l * E, E), range(E), workspace=ws)
+           for l in range(layers)]
+    store = DeviceBlobStore(store_pool.blob.view(layers, E, -1))
+    hs = [torch.empty((T, H), dtype=torch.bfloat16, device="cuda") for _ in range(layers + 1)]
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    norm_eps = 1e-6
+    modes = {}
+    for route_first in (True, False):
+        rp = ResidentExpertPool(cap, None, layers=layers, num_experts=E, hidden=H, inter=512,
+                                blob_store=store)
+        blocks = [MoeBlock(b.router_w, rp.tables[l], rp.layer_pool(l), b.shared,
+                           b.shared_gate_w, top_k=b.top_k, workspace=ws)
+                  for l, b in enumerate(src)]
+        dbg = blocks[0].new_debug(T)
+        runs = [0]
+
+        def step(i):
+            hs[0].copy_(input_tokens(seed * 1000 + i, T))
+            for l in range(layers):
+                runs[0] += rp.decode(l, blocks[l], hs[l], hs[l + 1], residual=hs[l],
+                                     status=status, debug=dbg, norm_eps=norm_eps,
+                                     route_first=route_first)
+
+        for i in range(warmup):
+            step(i)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        h0, m0 = rp.hits, rp.misses
+        runs[0] = 0
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(steps):
+            step(warmup + i)
+        e1.record()
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        ms = e0.elapsed_time(e1) / steps
+        hits, misses = rp.hits - h0, rp.misses - m0
+        modes["route_first" if route_first else "optimistic"] = {
+            "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3), "us_per_layer": ms * 1e3 / layers,
+            "unique_expert_hits": hits, "unique_expert_misses": misses,
+            "miss_rate": misses / max(hits + misses, 1),
+            "experts_loaded_per_step": misses / steps,
+            "kernel_launches_per_layer": runs[0] / (steps * layers)}
+        keep = rp
+        del blocks
+
+    # The gather kernel alone: 24 experts (about one T=4 layer's misses) into
+    # slots of layer 0, device-resident indices, CUDA events around each launch;
+    # 85 MB per launch from a different source layer each time (inputs > L2).
+    from vates_b200._lib import check, lib
+    n_g, reps = 24, 20
+    lp = keep.layer_pool(0)
+    idx = [torch.tensor([[(r * 37 + j * 11) % E for j in range(n_g)],
+                         [lp.blob_slot0 + (r * 5 + j) % cap for j in range(n_g)]],
+                        dtype=torch.int32, device="cuda") for r in range(reps)]
+
+    def gather(r):
+        check(lib.vb_blob_gather(store.blobs[r % layers].data_ptr(), store.stride,
+                                 idx[r][0].data_ptr(), idx[r][1].data_ptr(), n_g,
+                                 lp.blob.data_ptr(), torch.cuda.current_stream().cuda_stream),
+              "vb_blob_gather")
+
+    for r in range(3):
+        gather(r)
+    torch.cuda.synchronize()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    gather_ms = 0.0
+    for r in range(reps):
+        g0.record()
+        gather(r)
+        g1.record()
+        g1.synchronize()
+        gather_ms += g0.elapsed_time(g1)
+    gather_ms /= reps
+    gbytes = 2 * n_g * EXPERT_BYTES
+    gbs = gbytes / (gather_ms / 1e3) / 1e9
+    del keep, store, store_pool, src
+    torch.cuda.empty_cache()
+    return {"workload": f"decode_T{T}_{layers}layers_pool{cap}_of_{E}_fresh_tokens",
+            "modes": modes,
+            "blob_gather": {"kernel": "blob_gather_kernel", "experts": n_g, "bytes": gbytes,
+                            "ms": gather_ms, "gbs": gbs, "frac_of_hbm_peak": gbs / hbm_peak,
+                            "peak_kind": peak_kind},
+            "steps": steps, "warmup": warmup}
+
+
 def run_decode(args, world, rank, local):
     import torch
     from vates_b200.synth import DecodeStack
@@ -500,6 +607,7 @@ def run_decode(args, world, rank, local):
         if world == 1:
             out["prefill"] = run_prefill_leg()
             out["isoquant"] = run_isoquant_leg()
+            out["residency"] = run_residency_leg()
         else:
             out["prefill"] = run_prefill_ep_leg(world, rank)
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -126,7 +126,7 @@ typedef struct VbMoeDecodeArgs {
   int32_t norm_topk;    /* renormalise the top-k scores */
   float norm_eps;       /* > 0: the block input is rmsnorm(x) (unit weight,
                            float32 math, bf16 result); 0: x as given */
-  int32_t reserved0;
+  int32_t flags;        /* VB_DECODE_* bits, 0 for the whole block */
   const uint16_t *x;            /* bf16 [T, H]; x, residual and out are
                                    16-byte aligned */
   const uint16_t *router_w;     /* bf16 [E, H] */
@@ -157,6 +157,12 @@ typedef struct VbMoeDecodeArgs {
                                    with its down items [7], with its
                                    combines [8]; [2..15] initialised to 0 */
 } VbMoeDecodeArgs;
+
+/* flags: VB_DECODE_ROUTE_ONLY stops after routing: out_inds, out_scores,
+ * out_local and the status bits (VB_STATUS_MISS for a routed expert without a
+ * slot) are written; out is not. The same routing as the whole-block call, so
+ * a demand on its ids followed by the whole-block call sees no miss. */
+enum { VB_DECODE_ROUTE_ONLY = 1 };
 
 /* The decode workspace must be zero-filled before its first use; every call
  * leaves it reusable by the next call on the same stream with the same
@@ -463,6 +469,27 @@ int vb_res_counts(VbResidency *r, int32_t layer, uint32_t *counts);
  * for cap; count in *n). */
 int vb_res_resident(VbResidency *r, int32_t layer, int32_t *experts,
                     int32_t *slots, int32_t *n);
+
+/* One decode block over a resident pool with misses loaded on demand (the
+ * per-layer demand_dual flow of demand.cpp:1081-1171 with the fused kernel):
+ * route_first != 0: a VB_DECODE_ROUTE_ONLY launch, read back status and
+ * routed ids (one stream synchronisation), vb_res_demand, vb_blob_gather of
+ * the placed experts from blob_store (this layer's num_experts blob rows of
+ * blob_stride bytes, device or mapped pinned host memory) into the pool,
+ * the layer's table copied to args->slot_table, then the whole-block launch.
+ * route_first == 0: the whole block first; only when it flagged
+ * VB_STATUS_MISS are the experts loaded and the block run again. args:
+ * flags 0, out_inds and status required, pool = one blob row per slot of the
+ * manager's capacity. The last launch's status is left in *args->status
+ * (not read). counts (nullable, int64[4]) accumulates unique routed experts
+ * that hit, unique experts loaded, hit positions and kernel launches.
+ * VB_ERR_CAPACITY when the routed experts plus the unused pins exceed the
+ * slots (out not written). Calls on one manager must use one stream and not
+ * overlap (the staging buffers are per layer and reused). */
+int vb_moe_decode_resident(const VbMoeDecodeArgs *args, VbResidency *r,
+                           int32_t layer, const void *blob_store,
+                           int64_t blob_stride, int32_t route_first,
+                           int64_t *counts, vb_stream_t stream);
 
 /* Pool fill: copies n expert blobs (host or device memory, the expert_blob_v1
  * layout of prep/blob_layout.py:14-32: gate, up, down x {weight, scales,

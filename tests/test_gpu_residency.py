@@ -119,11 +119,16 @@ def test_acquire_and_acquire_gpu(cuda):
         rp.acquire(0, [0, 1, 2, 3, 4])
 
 
-@pytest.mark.parametrize("T,cap,source", [(1, 16, "host"), (4, 32, "host"), (2, 16, "device")])
-def test_decode_with_misses_matches_full_pool(cuda, T, cap, source):
+@pytest.mark.parametrize("T,cap,source,route_first", [(1, 16, "host", False),
+                                                     (4, 32, "host", False),
+                                                     (2, 16, "device", True),
+                                                     (4, 32, "device", False)])
+def test_decode_with_misses_matches_full_pool(cuda, T, cap, source, route_first):
     """Decode steps over a pool of ``cap`` < E slots: every routed miss is
-    loaded and the kernel re-run; outputs are bit-identical to the same block
-    over all E experts, and the host state follows the oracle."""
+    loaded (host flow, or the native vb_moe_decode_resident from an HBM blob
+    store) and the block run once all are resident; outputs are
+    bit-identical to the same block over all E experts, and the manager's
+    state follows the oracle."""
     import torch
     from vates_b200.moe_block import MoeBlock
     from vates_b200.pool import QuantPool, make_table
@@ -157,11 +162,51 @@ def test_decode_with_misses_matches_full_pool(cuda, T, cap, source):
             want = full[l].decode(x).clone()
             out = torch.empty_like(x)
             dbg = res[l].new_debug(T)
-            runs.append(rp.decode(l, res[l], x, out, status=status, debug=dbg))
+            runs.append(rp.decode(l, res[l], x, out, status=status, debug=dbg,
+                                  route_first=route_first))
             torch.cuda.synchronize()
+            assert int(status.item()) == 0
             assert torch.equal(out.view(torch.int16), want.view(torch.int16)), f"step {step} layer {l}"
             orc.demand(l, dbg["inds"].reshape(-1).cpu().tolist())
             assert rp.state.table(l) == orc.L[l].table
     repeats = [runs[s * L + l] for s in range(1, 12, 2) for l in range(L)]
-    assert 2 in runs and all(r == 1 for r in repeats)
+    if route_first:
+        assert all(r == 2 for r in runs)
+    else:
+        assert 2 in runs and all(r == 1 for r in repeats)
+    assert rp.state.table(0) == rp.tables[0].cpu().tolist()
     assert rp.misses > 0 and rp.hits > 0
+
+
+def test_route_only_launch(cuda):
+    """VB_DECODE_ROUTE_ONLY writes the routing outputs of the whole-block
+    call, leaves out untouched, and the workspace stays usable."""
+    import ctypes as C
+    import torch
+    from vates_b200._lib import VB_DECODE_ROUTE_ONLY, check, lib
+    from vates_b200.moe_block import MoeBlock
+    from vates_b200.pool import QuantPool, make_table, stream_handle
+    E, k, T = 64, 6, 3
+    rng = np.random.default_rng(5)
+    pool = QuantPool.from_tensors(pool_to_torch(random_pool_np(rng, E, H, I, BITS, G)), H, I, BITS, G)
+    table = make_table(E, {e: e for e in range(0, E, 2)})  # odd experts not resident
+    wr = bf16_tensor(rng.standard_normal((E, H)).astype(np.float32) * 0.05)
+    blk = MoeBlock(wr, table, pool, None, None, top_k=k)
+    x = bf16_tensor(rng.standard_normal((T, H)).astype(np.float32))
+    st_full = torch.zeros(1, dtype=torch.int32, device="cuda")
+    d_full = blk.new_debug(T)
+    ref = blk.decode(x, debug=d_full, status=st_full).clone()
+    out = torch.full_like(x, 7.0)
+    d_ro = blk.new_debug(T)
+    st_ro = torch.zeros(1, dtype=torch.int32, device="cuda")
+    a = blk.decode_args(x, out, debug=d_ro, status=st_ro)
+    a.flags = VB_DECODE_ROUTE_ONLY
+    check(lib.vb_moe_decode(C.byref(a), stream_handle()), "vb_moe_decode")
+    torch.cuda.synchronize()
+    for key in ("inds", "scores", "local"):
+        assert torch.equal(d_ro[key].view(torch.int16) if key == "scores" else d_ro[key],
+                           d_full[key].view(torch.int16) if key == "scores" else d_full[key])
+    assert int(st_ro.item()) == int(st_full.item())
+    assert bool((out == 7.0).all())
+    again = blk.decode(x).clone()
+    assert torch.equal(again.view(torch.int16), ref.view(torch.int16))

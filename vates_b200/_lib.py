@@ -16,6 +16,7 @@ VB_STATUS_MISS = 1
 VB_STATUS_BOUNDS = 2
 VB_STATUS_TIMEOUT = 4
 VB_ERR_CAPACITY = 4
+VB_DECODE_ROUTE_ONLY = 1
 
 
 class VbQuantPool(C.Structure):
@@ -28,7 +29,7 @@ class VbMoeDecodeArgs(C.Structure):
         ("tokens", C.c_int32), ("hidden", C.c_int32), ("inter", C.c_int32),
         ("group", C.c_int32), ("bits", C.c_int32), ("num_experts", C.c_int32),
         ("top_k", C.c_int32), ("norm_topk", C.c_int32),
-        ("norm_eps", C.c_float), ("reserved0", C.c_int32),
+        ("norm_eps", C.c_float), ("flags", C.c_int32),
         ("x", C.c_void_p), ("router_w", C.c_void_p), ("router_bias", C.c_void_p),
         ("slot_table", C.c_void_p), ("pool", VbQuantPool), ("shared", VbQuantPool),
         ("shared_gate_w", C.c_void_p), ("residual", C.c_void_p), ("out", C.c_void_p),
@@ -143,6 +144,8 @@ _SIGNATURES = {
     "vb_pool_fill": (_I32, [C.POINTER(VbQuantPool), _I32, _I32, _I32, _I32, _P, _P, _I32,
                             _P]),
     "vb_blob_gather": (_I32, [_P, _I64, _P, _P, _I32, _P, _P]),
+    "vb_moe_decode_resident": (_I32, [C.POINTER(VbMoeDecodeArgs), _P, _I32, _P, _I64, _I32, _P,
+                                      _P]),
     "vb_synth_fill_u32": (_I32, [_P, _I64, C.c_uint64, _P]),
     "vb_synth_fill_scales": (_I32, [_P, _P, _I64, C.c_uint64, C.c_float, C.c_float,
                                     C.c_float, _P]),

@@ -90,7 +90,7 @@ static DecodeLayout decode_layout(int T, int H, int I, int E, int k) {
 }
 
 struct DecodeParams {
-  int T, H, I, E, k, norm_topk, gshift, has_shared;
+  int T, H, I, E, k, norm_topk, gshift, has_shared, route_only;
   float norm_eps;
   const uint16_t *x, *router_w, *shared_gate_w, *residual;
   const float *router_bias;
@@ -883,6 +883,10 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
   }
   __syncthreads();  // the rings are free from here on
   trace_mark(p.trace, 5);
+  if (p.route_only) {  // routing outputs written; no counter touched yet
+    span.end();
+    return;
+  }
   const int n_ent = s_misc[0];
 
   // ---------------- 4. gate/up + SwiGLU ----------------
@@ -1335,6 +1339,8 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   p.norm_eps = a->norm_eps;
   p.gshift = a->group == 128 ? 1 : 0;
   p.has_shared = has_shared ? 1 : 0;
+  p.route_only = (a->flags & VB_DECODE_ROUTE_ONLY) ? 1 : 0;
+  VB_REQUIRE((a->flags & ~VB_DECODE_ROUTE_ONLY) == 0, "vb_moe_decode: unknown flags %#x", a->flags);
   p.x = a->x; p.router_w = a->router_w; p.shared_gate_w = a->shared_gate_w;
   p.residual = a->residual; p.router_bias = a->router_bias; p.table = a->slot_table;
   p.pool = a->pool; p.shared = a->shared;

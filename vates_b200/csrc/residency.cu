@@ -50,6 +50,16 @@ struct VbResidency {
   int layers = 0, cap = 0, experts = 0, lfu = 1, decay = 0;
   std::vector<vb::ResLayer> L;
   std::mutex mu;
+  // Staging of vb_moe_decode_resident, allocated on its first call (on the
+  // device current then): pinned status + routed ids, per-layer pinned gather
+  // indices and tables, device gather indices.
+  int32_t *h_back = nullptr, *h_idx = nullptr, *h_table = nullptr, *d_idx = nullptr;
+  ~VbResidency() {
+    if (h_back) cudaFreeHost(h_back);
+    if (h_idx) cudaFreeHost(h_idx);
+    if (h_table) cudaFreeHost(h_table);
+    if (d_idx) cudaFree(d_idx);
+  }
 };
 
 namespace vb {
@@ -126,17 +136,49 @@ void blob_segments(int H, int I, int group, int bits, size_t nb[9], size_t off[9
   *stride = o;
 }
 
-// out row rows[r] (or r) <- blob row experts[r], 16 bytes per thread step.
-__global__ void blob_gather_kernel(const uint4 *__restrict__ blob, const int32_t *__restrict__ experts,
-                                   const int32_t *__restrict__ rows, int n, size_t vec_per_expert,
-                                   uint4 *__restrict__ out) {
-  const size_t total = (size_t)n * vec_per_expert;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const size_t r = i / vec_per_expert, v = i % vec_per_expert;
-    const size_t dst = rows ? (size_t)rows[r] : r;
-    out[dst * vec_per_expert + v] = ldg_nc_v4(blob + (size_t)experts[r] * vec_per_expert + v);
+// out row rows[r] (or r) <- blob row experts[r]. blockIdx.y = r; each
+// thread moves GATHER_UNROLL 16-byte vectors, all loads issued before the
+// stores.
+constexpr int GATHER_THREADS = 256, GATHER_UNROLL = 4;
+__global__ void __launch_bounds__(GATHER_THREADS)
+blob_gather_kernel(const uint4 *__restrict__ blob, const int32_t *__restrict__ experts,
+                   const int32_t *__restrict__ rows, size_t vec_per_expert,
+                   uint4 *__restrict__ out) {
+  const int r = blockIdx.y;
+  const uint4 *src = blob + (size_t)experts[r] * vec_per_expert;
+  uint4 *dst = out + (size_t)(rows ? rows[r] : r) * vec_per_expert;
+  const size_t base = (size_t)blockIdx.x * (GATHER_THREADS * GATHER_UNROLL) + threadIdx.x;
+  uint4 v[GATHER_UNROLL];
+#pragma unroll
+  for (int u = 0; u < GATHER_UNROLL; ++u) {
+    const size_t i = base + (size_t)u * GATHER_THREADS;
+    if (i < vec_per_expert) v[u] = ldg_nc_v4(src + i);
   }
+#pragma unroll
+  for (int u = 0; u < GATHER_UNROLL; ++u) {
+    const size_t i = base + (size_t)u * GATHER_THREADS;
+    if (i < vec_per_expert) dst[i] = v[u];
+  }
+}
+
+constexpr int RES_BACK_WORDS = 1 + 8 * 16;  // status + T*k routed ids (T <= 8, k <= 16)
+
+int res_staging(VbResidency *r) {
+  if (r->h_back) return VB_OK;
+  const size_t idx = (size_t)r->layers * 2 * r->cap * sizeof(int32_t);
+  const size_t tab = (size_t)r->layers * r->experts * sizeof(int32_t);
+  cudaError_t e = cudaHostAlloc(&r->h_back, RES_BACK_WORDS * sizeof(int32_t), cudaHostAllocDefault);
+  if (e == cudaSuccess) e = cudaHostAlloc(&r->h_idx, idx, cudaHostAllocDefault);
+  if (e == cudaSuccess) e = cudaHostAlloc(&r->h_table, tab, cudaHostAllocDefault);
+  if (e == cudaSuccess) e = cudaMalloc(&r->d_idx, idx);
+  if (e != cudaSuccess) {
+    if (r->h_back) cudaFreeHost(r->h_back);
+    if (r->h_idx) cudaFreeHost(r->h_idx);
+    if (r->h_table) cudaFreeHost(r->h_table);
+    r->h_back = r->h_idx = r->h_table = r->d_idx = nullptr;
+    return set_error(VB_ERR_CUDA, "residency staging: %s", cudaGetErrorString(e));
+  }
+  return VB_OK;
 }
 
 }  // namespace
@@ -350,13 +392,105 @@ int vb_blob_gather(const void *blob_store, int64_t blob_stride, const int32_t *e
                  ((uintptr_t)blob_store % 16) == 0 && ((uintptr_t)out % 16) == 0,
              "vb_blob_gather: stride %lld and pointers must be 16-byte multiples",
              (long long)blob_stride);
+  VB_REQUIRE(n <= 65535, "vb_blob_gather: %d rows (at most 65535 per call)", n);
   if (n == 0) return VB_OK;
   const size_t vec = (size_t)blob_stride / 16;
-  const size_t total = (size_t)n * vec;
-  const int grid = (int)std::min<size_t>((total + 255) / 256, 148 * 8);
-  blob_gather_kernel<<<grid, 256, 0, as_stream(stream)>>>(
-      static_cast<const uint4 *>(blob_store), experts, out_rows, n, vec, static_cast<uint4 *>(out));
+  const size_t per_block = (size_t)GATHER_THREADS * GATHER_UNROLL;
+  const dim3 grid((unsigned)((vec + per_block - 1) / per_block), (unsigned)n);
+  blob_gather_kernel<<<grid, GATHER_THREADS, 0, as_stream(stream)>>>(
+      static_cast<const uint4 *>(blob_store), experts, out_rows, vec, static_cast<uint4 *>(out));
   return check_launch("blob_gather_kernel");
+}
+
+int vb_moe_decode_resident(const VbMoeDecodeArgs *a, VbResidency *r, int32_t layer,
+                           const void *blob_store, int64_t blob_stride, int32_t route_first,
+                           int64_t *counts, vb_stream_t stream) {
+  VB_REQUIRE(a && r && blob_store, "vb_moe_decode_resident: null argument");
+  VB_REQUIRE(layer >= 0 && layer < r->layers, "vb_moe_decode_resident: layer %d", layer);
+  VB_REQUIRE(a->out_inds && a->status && a->slot_table,
+             "vb_moe_decode_resident: out_inds, status and slot_table are required");
+  VB_REQUIRE(a->num_experts == r->experts && a->pool.cap == r->cap,
+             "vb_moe_decode_resident: pool of %d slots / %d experts, manager has %d / %d",
+             a->pool.cap, a->num_experts, r->cap, r->experts);
+  VB_REQUIRE(a->flags == 0, "vb_moe_decode_resident: flags must be 0");
+  const int n = a->tokens * a->top_k;
+  VB_REQUIRE(n >= 1 && n + 1 <= RES_BACK_WORDS, "vb_moe_decode_resident: %d routes", n);
+  size_t nb[9], off[9], stride;
+  blob_segments(a->hidden, a->inter, a->group, a->bits, nb, off, &stride);
+  VB_REQUIRE(blob_stride == (int64_t)stride && stride % 16 == 0,
+             "vb_moe_decode_resident: blob stride %lld, layout needs %zu", (long long)blob_stride,
+             stride);
+  for (int t = 0; t < 9; ++t)
+    VB_REQUIRE(static_cast<const uint8_t *>(a->pool.ptr[t]) ==
+                       static_cast<const uint8_t *>(a->pool.ptr[0]) + off[t] &&
+                   a->pool.slot_stride[t] == (int64_t)stride,
+               "vb_moe_decode_resident: the pool must be one blob row per slot");
+  int rc = res_staging(r);
+  if (rc != VB_OK) return rc;
+  cudaStream_t s = as_stream(stream);
+  int32_t *back = r->h_back;
+  int runs = 0;
+  auto launch = [&](int32_t flags) -> int {
+    cudaError_t e = cudaMemsetAsync(a->status, 0, sizeof(int32_t), s);
+    if (e != cudaSuccess) return set_error(VB_ERR_CUDA, "status reset: %s", cudaGetErrorString(e));
+    VbMoeDecodeArgs b = *a;
+    b.flags = flags;
+    ++runs;
+    return vb_moe_decode(&b, stream);
+  };
+  // 1. route (route_first) or the whole block (optimistic), then one read-back
+  rc = launch(route_first ? VB_DECODE_ROUTE_ONLY : 0);
+  if (rc != VB_OK) return rc;
+  cudaError_t e = cudaMemcpyAsync(back, a->status, sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess)
+    e = cudaMemcpyAsync(back + 1, a->out_inds, n * sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess)
+    return set_error(VB_ERR_CUDA, "vb_moe_decode_resident: read-back: %s", cudaGetErrorString(e));
+  const int32_t st = back[0];
+  if (st & ~VB_STATUS_MISS)
+    return set_error(VB_ERR_CUDA, "vb_moe_decode_resident: layer %d status %#x", layer, st);
+  // 2. demand: LFU note, slots for the misses
+  int32_t local[8 * 16], pe[8 * 16], ps[8 * 16], n_place = 0;
+  int64_t stats[3] = {0, 0, 0};
+  rc = vb_res_demand(r, layer, back + 1, n, local, pe, ps, &n_place, stats);
+  if (rc != VB_OK) return rc;
+  if (!route_first && !(st & VB_STATUS_MISS) && n_place)
+    return set_error(VB_ERR_INVALID, "vb_moe_decode_resident: device table out of step with the manager");
+  // 3. load the placed experts and publish the layer's table
+  if (n_place) {
+    int32_t *hi = r->h_idx + (size_t)layer * 2 * r->cap, *di = r->d_idx + (size_t)layer * 2 * r->cap;
+    for (int i = 0; i < n_place; ++i) {
+      hi[i] = pe[i];
+      hi[r->cap + i] = ps[i];
+    }
+    int32_t *ht = r->h_table + (size_t)layer * r->experts;
+    rc = vb_res_table(r, layer, ht);
+    if (rc != VB_OK) return rc;
+    e = cudaMemcpyAsync(di, hi, 2 * r->cap * sizeof(int32_t), cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess)
+      return set_error(VB_ERR_CUDA, "vb_moe_decode_resident: index copy: %s", cudaGetErrorString(e));
+    rc = vb_blob_gather(blob_store, blob_stride, di, di + r->cap, n_place,
+                        const_cast<void *>(a->pool.ptr[0]), stream);
+    if (rc != VB_OK) return rc;
+    e = cudaMemcpyAsync(const_cast<int32_t *>(a->slot_table), ht, r->experts * sizeof(int32_t),
+                        cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess)
+      return set_error(VB_ERR_CUDA, "vb_moe_decode_resident: table copy: %s", cudaGetErrorString(e));
+  }
+  // 4. the whole block once every routed expert has a slot
+  if (route_first || (st & VB_STATUS_MISS)) {
+    rc = launch(0);
+    if (rc != VB_OK) return rc;
+  }
+  if (counts) {
+    std::unordered_set<int> uniq(back + 1, back + 1 + n);
+    counts[0] += (int64_t)uniq.size() - n_place;
+    counts[1] += n_place;
+    counts[2] += stats[0];
+    counts[3] += runs;
+  }
+  return VB_OK;
 }
 
 }  // extern "C"

@@ -73,6 +73,25 @@ class NativeResidency:
         place = [(pe[i], ps[i]) for i in range(n_place.value)]
         return list(local[:n]), place, tuple(stats), rc == VB_ERR_CAPACITY
 
+    def demand_into(self, layer: int, ids: np.ndarray, local: np.ndarray, place: np.ndarray,
+                    stats: np.ndarray) -> tuple[int, bool]:
+        """Array form of :meth:`demand` for the per-layer hot path: ``ids``
+        int32 [n]; ``local`` int32 [>= n]; ``place`` int32 [2, >= n] receives
+        experts (row 0) and slots (row 1); ``stats`` int64 [3]. Returns
+        (placements, over_capacity)."""
+        n = int(ids.size)
+        n_place = C.c_int32(0)
+        rc = lib.vb_res_demand(self._h, layer, ids.ctypes.data, n, local.ctypes.data,
+                               place[0].ctypes.data, place[1].ctypes.data, C.byref(n_place),
+                               stats.ctypes.data)
+        if rc not in (VB_OK, VB_ERR_CAPACITY):
+            check(rc, "vb_res_demand")
+        return n_place.value, rc == VB_ERR_CAPACITY
+
+    def table_into(self, layer: int, out: np.ndarray) -> None:
+        """The layer's table into an int32 [num_experts] array (e.g. pinned)."""
+        check(lib.vb_res_table(self._h, layer, out.ctypes.data), "vb_res_table")
+
     def pin(self, layer: int, experts):
         """-> (slots of the unique experts, [(expert, slot)] newly placed)."""
         experts = [int(v) for v in experts]
@@ -115,19 +134,30 @@ class DeviceBlobStore:
         self.blobs = blobs
         self.stride = int(blobs.shape[2])
 
-    def fill(self, layer: int, pool: QuantPool, placements, stream=None) -> None:
-        if not placements:
+    def fill(self, layer: int, pool: QuantPool, placements, stream=None, staging=None) -> None:
+        """Gather experts into pool slots: ``placements`` is a list of
+        (expert, slot) or an int32 array [2, n] (experts, slots). ``staging``
+        (pinned int32 [2, >= n], optional) holds the index copy; the caller
+        must not rewrite it before the copy has run."""
+        if isinstance(placements, np.ndarray):
+            n = int(placements.shape[1])
+        else:
+            n = len(placements)
+            placements = np.array(placements, dtype=np.int32).reshape(n, 2).T if n else None
+        if n == 0:
             return
         assert pool.blob is not None and self.stride == pool.stride
-        idx = torch.tensor([[e for e, _ in placements],
-                            [pool.blob_slot0 + s for _, s in placements]],
-                           dtype=torch.int32).pin_memory()
+        idx = staging if staging is not None else torch.empty((2, n), dtype=torch.int32,
+                                                              pin_memory=True)
+        h = idx.numpy()
+        h[0, :n] = placements[0, :n]
+        h[1, :n] = placements[1, :n] + pool.blob_slot0
         s = stream or torch.cuda.current_stream()
         with torch.cuda.stream(s):
-            dev = idx.to(pool.blob.device, non_blocking=True)
+            dev = idx[:, :n].to(pool.blob.device, non_blocking=True)
             check(lib.vb_blob_gather(self.blobs[layer].data_ptr(), self.stride, dev[0].data_ptr(),
-                                     dev[1].data_ptr(), len(placements), pool.blob.data_ptr(),
-                                     s.cuda_stream), "vb_blob_gather")
+                                     dev[1].data_ptr(), n, pool.blob.data_ptr(), s.cuda_stream),
+                  "vb_blob_gather")
 
 
 def fill_slots(pool: QuantPool, slots, blobs, stream=None) -> None:
@@ -180,6 +210,15 @@ class ResidentExpertPool:
         self.hits = self.misses = self.loads = 0
         self.gpu_fastpath = self.gpu_fallback = 0
         self.over_capacity = 0
+        # Pinned host staging of the per-layer hot path (decode): the status
+        # word and routed ids read back, the host tables, the gather indices.
+        self._h_tables = torch.full((layers, num_experts), -1, dtype=torch.int32,
+                                    pin_memory=True)
+        self._h_back = torch.zeros(1 + 64, dtype=torch.int32, pin_memory=True)
+        self._h_idx = torch.zeros((2, capacity), dtype=torch.int32, pin_memory=True)
+        self._local = np.zeros(64, np.int32)
+        self._place = np.zeros((2, 64), np.int32)
+        self._stats = np.zeros(3, np.int64)
 
     # resident_pool.py:133-135
     def cap_for(self, layer: int) -> int:
@@ -189,20 +228,28 @@ class ResidentExpertPool:
         return self.pool.view(layer * self.capacity, self.capacity)
 
     def _load(self, layer: int, placements, stream=None) -> None:
-        if not placements:
+        """Copy the placed experts' bytes into their slots and the layer's
+        table to the device, stream-ordered (``placements``: (expert, slot)
+        list or int32 [2, n])."""
+        if isinstance(placements, np.ndarray):
+            pl = placements
+        else:
+            pl = np.array(placements, dtype=np.int32).reshape(-1, 2).T
+        n = int(pl.shape[1])
+        if n == 0:
             return
+        s = stream or torch.cuda.current_stream()
         p = self.layer_pool(layer)
         if self.blob_store is not None:
-            self.blob_store.fill(layer, p, placements, stream)
+            self.blob_store.fill(layer, p, pl, s, staging=self._h_idx if n <= self.capacity else None)
         else:
-            fill_slots(p, [s for _, s in placements],
-                       [self.loader(layer, e) for e, _ in placements], stream)
-        self.loads += len(placements)
-        self._sync_table(layer)
-
-    def _sync_table(self, layer: int) -> None:
-        self.tables[layer].copy_(torch.tensor(self.state.table(layer), dtype=torch.int32),
-                                 non_blocking=False)
+            fill_slots(p, pl[1].tolist(), [self.loader(layer, int(e)) for e in pl[0]], s)
+        self.loads += n
+        self.state.table_into(layer, self._h_tables[layer].numpy())
+        with torch.cuda.stream(s):
+            self.tables[layer].copy_(self._h_tables[layer], non_blocking=True)
+        # The staging buffers are rewritten by the next load: wait for these
+        # copies unless the caller synchronises before then (decode does).
 
     def acquire(self, layer: int, expert_ids, stream=None):
         ids = [int(e) for e in expert_ids]
@@ -215,11 +262,13 @@ class ResidentExpertPool:
         self.hits += len(uniq) - len(place)
         self.misses += len(place)
         self._load(layer, place, stream)
+        (stream or torch.cuda.current_stream()).synchronize()
         return self.layer_pool(layer), local
 
     def pin(self, layer: int, expert_ids, stream=None) -> None:
         _, placed = self.state.pin(layer, expert_ids)
         self._load(layer, placed, stream)
+        (stream or torch.cuda.current_stream()).synchronize()
 
     def resident_count(self, layer: int) -> int:
         return len(self.state.resident(layer))
@@ -244,6 +293,7 @@ class ResidentExpertPool:
             self.misses += len(place)
             self.hits += len(set(host)) - len(place)
             self._load(layer, place, stream)
+            (stream or torch.cuda.current_stream()).synchronize()
         else:
             self.gpu_fastpath += 1
             self.hits += len(host)
@@ -252,40 +302,69 @@ class ResidentExpertPool:
 
     def decode(self, layer: int, block, x: torch.Tensor, out: torch.Tensor, *,
                residual=None, status: torch.Tensor, debug: dict, stream=None,
-               norm_eps: float = 0.0) -> int:
+               norm_eps: float = 0.0, route_first: bool = True) -> int:
         """One decode call of ``block`` (a MoeBlock over this layer's pool and
-        table) with misses resolved; returns the number of kernel runs (1, or
-        2 when a routed expert had to be loaded first). ``status`` is a device
-        int32 word (zeroed here); ``debug`` receives the routed ids."""
+        table) with misses resolved; returns the number of kernel launches.
+
+        With a blob store the whole flow is native (``vb_moe_decode_resident``):
+        ``route_first`` runs a routing-only launch, loads the misses and then
+        the block (2 launches, one host synchronisation); otherwise the block
+        runs first and again only after a miss. With a host loader the same
+        optimistic flow runs here. ``status`` is a device int32 word; after a
+        native call it holds the last launch's status (not read here).
+        ``debug`` receives the routed ids."""
         assert out.data_ptr() not in (x.data_ptr(), getattr(residual, "data_ptr", lambda: 0)())
+        if self.blob_store is not None:
+            x2 = x.reshape(-1, block.hidden)
+            a = block.decode_args(x2, out, residual=residual, debug=debug, status=status,
+                                  norm_eps=norm_eps)
+            cnt = (C.c_int64 * 4)()
+            st = self.blob_store.blobs[layer]
+            check(lib.vb_moe_decode_resident(C.byref(a), self.state._h, layer, st.data_ptr(),
+                                             self.blob_store.stride, int(route_first), cnt,
+                                             stream_handle(stream)), "vb_moe_decode_resident")
+            self.hits += cnt[0]
+            self.misses += cnt[1]
+            self.loads += cnt[1]
+            return int(cnt[3])
         s = stream or torch.cuda.current_stream()
+        inds = debug["inds"].reshape(-1)
+        n = int(inds.numel())
+        assert n <= 64
+        back = self._h_back
         with torch.cuda.stream(s):
             status.zero_()
         block.decode(x, out=out, residual=residual, debug=debug, status=status, stream=s,
                      norm_eps=norm_eps)
+        with torch.cuda.stream(s):
+            back[:1].copy_(status, non_blocking=True)
+            back[1:1 + n].copy_(inds, non_blocking=True)
         s.synchronize()
-        st = int(status.item())
-        host = debug["inds"].reshape(-1).cpu().tolist()
-        local, place, _, over = self.state.demand(layer, host)
+        hb = back.numpy()
+        st = int(hb[0])
+        ids = hb[1:1 + n]
+        n_place, over = self.state.demand_into(layer, ids, self._local, self._place, self._stats)
         if over:
             self.over_capacity += 1
             raise ValueError("routed experts do not fit the layer's slots with its pins")
-        uniq = len(set(host))
-        self.hits += uniq - len(place)
-        self.misses += len(place)
+        uniq = len(set(ids.tolist()))
+        self.hits += uniq - n_place
+        self.misses += n_place
         if not (st & VB_STATUS_MISS):
-            if place:
+            if n_place:
                 raise VbError("kernel saw every expert resident but the host state placed some")
             return 1
         if st & ~VB_STATUS_MISS:
             raise VbError(f"decode status {st:#x}")
-        self._load(layer, place, s)
+        self._load(layer, self._place[:, :n_place], s)
         with torch.cuda.stream(s):
             status.zero_()
         block.decode(x, out=out, residual=residual, debug=debug, status=status, stream=s,
                      norm_eps=norm_eps)
+        with torch.cuda.stream(s):
+            back[:1].copy_(status, non_blocking=True)
         s.synchronize()
-        st = int(status.item())
+        st = int(back.numpy()[0])
         if st:
             raise VbError(f"decode status {st:#x} after filling the misses")
         return 2
