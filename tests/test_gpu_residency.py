@@ -210,3 +210,39 @@ def test_route_only_launch(cuda):
     assert bool((out == 7.0).all())
     again = blk.decode(x).clone()
     assert torch.equal(again.view(torch.int16), ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("T,source", [(1, "device"), (11, "host"), (4, "host")])
+def test_mtp_moe_matches_full_pool(cuda, T, source):
+    """The MTP drafter's MoE (StreamingMTPMoE, qwen3_next_mtp.py:70-137) over
+    a pool smaller than the experts (room for one 8-token piece's routes):
+    bit-identical to the block over all experts, token counts above 8 in
+    pieces."""
+    import torch
+    from vates_b200.moe_block import MoeBlock
+    from vates_b200.mtp import StreamingMTPMoE
+    from vates_b200.pool import QuantPool, make_table
+    from vates_b200.residency import DeviceBlobStore
+    E, k = 64, 6
+    cap = max(16, k * min(T, 8))
+    rng = np.random.default_rng(20 + T)
+    pool_np = random_pool_np(rng, E, H, I, BITS, G)
+    blobs = _blobs_np(pool_np, E)
+    sh = QuantPool.from_tensors(pool_to_torch(random_pool_np(rng, 1, H, I, BITS, G)), H, I, BITS, G)
+    wsg = bf16_tensor(rng.standard_normal(H).astype(np.float32) * 0.02)
+    wr = bf16_tensor(rng.standard_normal((E, H)).astype(np.float32) * 0.05)
+    full = MoeBlock(wr, make_table(E, {e: e for e in range(E)}),
+                    QuantPool.from_tensors(pool_to_torch(pool_np), H, I, BITS, G), sh, wsg, top_k=k)
+    if source == "device":
+        mtp = StreamingMTPMoE(wr, sh, wsg, cap, top_k=k, hidden=H, intermediate=I,
+                              blob_store=DeviceBlobStore(torch.from_numpy(blobs[None]).cuda()))
+    else:
+        mtp = StreamingMTPMoE(wr, sh, wsg, cap, top_k=k, hidden=H, intermediate=I,
+                              loader=_loader(blobs))
+    for step in range(6):
+        x = bf16_tensor(rng.standard_normal((1, T, H)).astype(np.float32))
+        got = mtp(x)
+        want = torch.cat([full.decode(x[0, i:i + 8]) for i in range(0, T, 8)])
+        torch.cuda.synchronize()
+        assert torch.equal(got[0].view(torch.int16), want.view(torch.int16)), f"step {step}"
+    assert mtp.pool.misses > 0
