@@ -513,6 +513,23 @@ int vb_blob_gather(const void *blob_store, int64_t blob_stride,
                    const int32_t *experts, const int32_t *out_rows, int32_t n,
                    void *out, vb_stream_t stream);
 
+/* Prefill attention over a packed cache: replaces _tiled_asymmetric_attention
+ * (mlx_streaming/core/attention/expert_major.py:32-95; the query tiling of
+ * 107-182 is not needed) plus the inverse V rotation (kv_quant_patch.py:
+ * 67-68) when rv_blocks != NULL. Arguments as vb_kv_decode_attn, any L <=
+ * keys; q_heads / kv_heads must divide 128. One tcgen05 kernel (S = QK^T and
+ * O += PV in TMEM, online softmax); status (nullable device word) receives
+ * VB_STATUS_TIMEOUT if a bounded wait gave up. No workspace. */
+int vb_kv_prefill_attn(const uint16_t *q, const uint32_t *k_codes,
+                       const uint16_t *k_scales, const uint16_t *k_biases,
+                       const uint32_t *v_codes, const uint16_t *v_scales,
+                       const uint16_t *v_biases, const float *rv_blocks,
+                       int32_t batch, int32_t q_heads, int32_t kv_heads,
+                       int32_t L, int32_t dim, int32_t keys, int32_t cap,
+                       int32_t group, int32_t k_bits, int32_t v_bits,
+                       float scale, int32_t causal, uint16_t *out,
+                       int32_t *status, vb_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Seeded synthetic data (bench and tests): fills `words` uint32 with a
  * counter hash of (seed, index) and bf16 scales uniform in [lo, hi) with

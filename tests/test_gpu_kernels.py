@@ -225,3 +225,41 @@ def test_kv_attention_vs_oracle(cuda, L, S, causal):
         got_unrot = IQ.rotate_last(to_np(out), Rv.numpy())
         cos = float((got_unrot * dense).sum() / (np.linalg.norm(got_unrot) * np.linalg.norm(dense)))
         assert cos > 0.9
+
+
+@pytest.mark.parametrize("L,S,causal,nq,nkv", [(40, 40, True, 16, 2), (200, 300, True, 16, 2),
+                                               (33, 150, False, 16, 2), (130, 130, True, 8, 2),
+                                               (64, 1000, True, 16, 2), (5, 260, True, 16, 2),
+                                               (300, 700, True, 16, 1)])
+def test_prefill_attention_vs_oracle(cuda, L, S, causal, nq, nkv):
+    """tcgen05 prefill attention (_tiled_asymmetric_attention,
+    expert_major.py:32-95) against the oracle's MLX dtype chain, with the
+    inverse V rotation fused; L > 4 also goes through asym_quantized_sdpa."""
+    import torch
+    from vates_b200.quant_kv import (AsymmetricQuantizedKVCache, asym_quantized_sdpa,
+                                     build_block_so4, so4_blocks, tiled_asymmetric_attention)
+    rng = np.random.default_rng(1000 + S + L)
+    D = 256
+    k = M.bf16(rng.standard_normal((1, nkv, S, D)).astype(np.float32))
+    v = M.bf16(rng.standard_normal((1, nkv, S, D)).astype(np.float32))
+    q = M.bf16(rng.standard_normal((1, nq, L, D)).astype(np.float32))
+    Rv = build_block_so4(D, 2)
+    cache = AsymmetricQuantizedKVCache(64, 4, 3)
+    kq, vq = cache.update_and_fetch(bf16_tensor(k), bf16_tensor(v))
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = tiled_asymmetric_attention(bf16_tensor(q), kq, vq, scale=D ** -0.5,
+                                     mask="causal" if causal else None, group_size=64, k_bits=4,
+                                     v_bits=3, rv=so4_blocks(Rv), status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    kq_np = tuple(np.ascontiguousarray(a) for a in (to_np(kq[0]).view(np.uint32),
+                                                   to_np(kq[1].view(torch.int16)).view(np.uint16),
+                                                   to_np(kq[2].view(torch.int16)).view(np.uint16)))
+    vq_np = tuple(np.ascontiguousarray(a) for a in (to_np(vq[0]).view(np.uint32),
+                                                   to_np(vq[1].view(torch.int16)).view(np.uint16),
+                                                   to_np(vq[2].view(torch.int16)).view(np.uint16)))
+    ref = IQ.attention_layer_decode(q, kq_np, vq_np, Rv.numpy(), D ** -0.5, causal=causal)
+    bf16_close(to_np(out), ref, what="prefill attention")
+    again = asym_quantized_sdpa(bf16_tensor(q), kq, vq, D ** -0.5, "causal" if causal else None,
+                                64, 4, 3, rv=so4_blocks(Rv))
+    assert torch.equal(again.view(torch.int16), out.view(torch.int16))

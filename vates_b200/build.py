@@ -27,6 +27,7 @@ SOURCES = [
     "kv_attn.cu",
     "moe_prefill.cu",
     "residency.cu",
+    "kv_prefill_attn.cu",
 ]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

@@ -212,6 +212,10 @@ def asym_quantized_sdpa(queries, q_keys, q_values, scale, mask, group_size, k_bi
         raise ValueError("asym_quantized_sdpa: only mask=None or 'causal' is supported")
     q = queries.contiguous()
     B, Hq, L, D = q.shape
+    if L > 4:  # beyond the decode kernels: the tensor-core prefill kernel
+        return tiled_asymmetric_attention(q, q_keys, q_values, scale=scale, mask=mask,
+                                          group_size=group_size, k_bits=k_bits, v_bits=v_bits,
+                                          rv=rv, stream=stream)
     kc, ks, kb = q_keys
     vc, vs, vb = q_values
     Hkv = kc.shape[-3]
@@ -231,4 +235,33 @@ def asym_quantized_sdpa(queries, q_keys, q_values, scale, mask, group_size, k_bi
                                 int(mask == "causal"), out.data_ptr(), workspace.data_ptr(),
                                 workspace.numel(), stream_handle(stream)),
           "vb_kv_decode_attn")
+    return out
+
+
+def tiled_asymmetric_attention(queries, q_keys, q_values, *, scale, mask, group_size, k_bits,
+                               v_bits, rv=None, status=None, stream=None):
+    """Prefill attention over packed K/V (``_tiled_asymmetric_attention``,
+    mlx_streaming/core/attention/expert_major.py:32-95): bf16(q*scale) K^T
+    rounded to bf16, causal (``mask="causal"``, query ``i`` of ``L`` sees keys
+    ``<= S-L+i``) or no mask, precise softmax, P V -> bf16 ``[B, Hq, L, D]``.
+    One tcgen05 kernel for all query rows (the reference's query tiles only
+    bound its score memory). ``rv`` fuses the inverse V rotation."""
+    if mask is not None and mask != "causal":
+        raise ValueError("tiled_asymmetric_attention: only mask=None or 'causal' is supported")
+    q = queries.contiguous()
+    B, Hq, L, D = q.shape
+    kc, ks, kb = q_keys
+    vc, vs, vb = q_values
+    Hkv = kc.shape[-3]
+    keys = kc.shape[-2]
+    cap = kc.stride(-3) // kc.stride(-2)
+    for t in (kc, ks, kb, vc, vs, vb):
+        assert t.stride(-1) == 1 and t.stride(-3) // t.stride(-2) == cap
+    out = torch.empty_like(q)
+    check(lib.vb_kv_prefill_attn(q.data_ptr(), kc.data_ptr(), ks.data_ptr(), kb.data_ptr(),
+                                 vc.data_ptr(), vs.data_ptr(), vb.data_ptr(), ptr(rv), B, Hq, Hkv,
+                                 L, D, keys, cap, group_size, k_bits, v_bits, float(scale),
+                                 int(mask == "causal"), out.data_ptr(), ptr(status),
+                                 stream_handle(stream)),
+          "vb_kv_prefill_attn")
     return out
