@@ -319,6 +319,53 @@ def run_isoquant_leg(steps: int = 20, warmup: int = 3, S: int = 131072, layers: 
     return res
 
 
+def run_prefill_attention_leg(steps: int = 10, warmup: int = 3, lengths=(4096, 32768)):
+    """Prefill attention over a fresh IsoQuant K4/V3 cache (Hq=16, Hkv=2,
+    D=256, causal, inverse V rotation fused), one layer per length: the
+    tcgen05 kernel behind tiled_asymmetric_attention. Algorithmic FLOPs of the
+    causal product: Hq x L(L+1)/2 visible (query, key) pairs x 4 D (QK^T and
+    PV). Tensor-bound: reported against the measured bf16 peak."""
+    import torch
+    from vates_b200.quant_kv import (AsymmetricQuantizedKVCache, build_block_so4, so4_blocks,
+                                     tiled_asymmetric_attention)
+    _, tf_peak, peak_kind = peaks()
+    g = torch.Generator(device="cuda").manual_seed(4)
+    rk = so4_blocks(build_block_so4(256, seed=0))
+    rv = so4_blocks(build_block_so4(256, seed=1))
+    res = {"kernel": "kv_prefill_attn_kernel", "heads": "16 q / 2 kv", "dim": 256}
+    for L in lengths:
+        c = AsymmetricQuantizedKVCache(64, 4, 3)
+        k = torch.randn((1, 2, L, 256), generator=g, device="cuda").to(torch.bfloat16)
+        v = torch.randn((1, 2, L, 256), generator=g, device="cuda").to(torch.bfloat16)
+        kq, vq = c.update_and_fetch(k, v, rk=rk, rv=rv)
+        q = torch.randn((1, 16, L, 256), generator=g, device="cuda").to(torch.bfloat16)
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+        def call():
+            return tiled_asymmetric_attention(q, kq, vq, scale=256 ** -0.5, mask="causal",
+                                              group_size=64, k_bits=4, v_bits=3, rv=rv,
+                                              status=status)
+        for _ in range(max(warmup, 3)):
+            call()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            call()
+        e1.record()
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        ms = e0.elapsed_time(e1) / steps
+        flops = 16 * L * (L + 1) / 2 * 4 * 256
+        tfs = flops / (ms / 1e3) / 1e12
+        res[f"L{L}"] = {"ms": ms, "tflops": tfs, "frac_of_bf16_peak": tfs / tf_peak,
+                        "flops": flops, "tokens_per_s": L / (ms / 1e3)}
+        del c, k, v, kq, vq, q
+    res["peak_tflops"], res["peak_kind"] = tf_peak, peak_kind
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_decode_t1_leg(st, stream, steps: int = 20, warmup: int = 3):
     """Config 0 shape (decode, T=1) over the same 48-layer stack: token 0 of
     the config-1 input. Each token is routed independently, so token 0's
@@ -607,6 +654,7 @@ def run_decode(args, world, rank, local):
         if world == 1:
             out["prefill"] = run_prefill_leg()
             out["isoquant"] = run_isoquant_leg()
+            out["prefill_attention"] = run_prefill_attention_leg()
             out["residency"] = run_residency_leg()
         else:
             out["prefill"] = run_prefill_ep_leg(world, rank)
