@@ -60,7 +60,11 @@ constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;        // 16 KB
 constexpr int PF_B_BYTES = PF_BN * PF_BK * 2;        // 32 KB
 constexpr int PF_P_BYTES = PF_BN * PF_BK / 2;        // 8 KB packed codes
 constexpr int PF_STAGE_BYTES = PF_A_BYTES + PF_B_BYTES + PF_P_BYTES;
-constexpr int PF_SMEM = PF_STAGES * PF_STAGE_BYTES + 1024;  // + alignment slack
+// Epilogue staging for TMA stores: per epilogue warp two 32-row x 32-column
+// bf16 chunks (64-byte rows, 64-byte swizzle).
+constexpr int PF_OUT_CHUNK = 32 * 64;
+constexpr int PF_OUT_BYTES = 8 * 2 * PF_OUT_CHUNK;
+constexpr int PF_SMEM = PF_STAGES * PF_STAGE_BYTES + PF_OUT_BYTES + 1024;  // + alignment slack
 constexpr uint64_t PF_WAIT_NS = 2000000000ull;       // 2 s per wait
 
 enum PfMode : int { PF_GATEUP = 0, PF_DOWN = 1, PF_ROUTER = 2 };
@@ -90,6 +94,20 @@ __device__ __forceinline__ uint32_t sw128(int r, int c) {
   return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
 
+// (bf16(hi) << 16) | bf16(lo), round to nearest even.
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Elementwise bf16 product, rounded once (the product of two bf16 values is
+// exact in fp32, so this equals bf16(float(a) * float(b))).
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t bf16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
   uint32_t d;
   asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -101,7 +119,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmS0,
                const __grid_constant__ CUtensorMap tmS1, const __grid_constant__ CUtensorMap tmHv,
-               PfGemmParams p) {
+               const __grid_constant__ CUtensorMap tmOut, PfGemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
@@ -138,6 +156,7 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tc::prefetch_tmap(&tmB0);
     if (MODE == PF_GATEUP) tc::prefetch_tmap(&tmB1);
   }
+  if (warp == 12 && lane == 0 && MODE != PF_ROUTER) tc::prefetch_tmap(&tmOut);
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
@@ -319,6 +338,36 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     const int q = warp & 3, hf = (warp - 12) >> 2;
     const int m = q * 32 + lane;  // tile row = TMEM lane
     int tcount = 0;
+    // Chunks of 32 rows x 32 columns whose rows are all valid go out as one
+    // TMA store from a swizzled staging buffer (two per warp, alternating);
+    // the rows of a partial chunk are stored by their threads.
+    uint8_t *obuf = smem + PF_STAGES * PF_STAGE_BYTES + (warp - 12) * 2 * PF_OUT_CHUNK;
+    int nst = 0;
+    auto store_chunk = [&](const uint32_t (&o)[16], bool full, bool valid, size_t orow,
+                           int col) {
+      if (full) {
+        uint8_t *b = obuf + (nst & 1) * PF_OUT_CHUNK;
+        if (lane == 0 && nst >= 2) tc::bulk_wait_read<1>();
+        __syncwarp();
+        const int sw = (lane >> 1) & 3;  // 64-byte swizzle: chunk c ^ ((row >> 1) & 3)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          *reinterpret_cast<uint4 *>(b + lane * 64 + ((c ^ sw) << 4)) =
+              make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tc::tma_store_2d(&tmOut, b, col, (int)(orow - lane));
+          tc::bulk_commit();
+        }
+        ++nst;
+      } else if (valid) {
+        uint4 *dst = reinterpret_cast<uint4 *>(p.out + orow * p.out_ld + col);
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+      }
+    };
     for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++tcount) {
       const int mt = t / p.nt, nt = t % p.nt;
       const int row0 = p.mtiles[3 * mt + 1], rows = p.mtiles[3 * mt + 2];
@@ -330,6 +379,7 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       tc::tc_fence_after();
       const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + acc * PF_BN;
       const bool valid = m < rows;
+      const bool full = q * 32 + 32 <= rows;  // warp-uniform
       const size_t orow = (size_t)(row0 + m);
       if (MODE == PF_GATEUP) {
         // Columns [0,128) gate, [128,256) up of intermediate rows nt*128 + c;
@@ -352,15 +402,26 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 #pragma unroll
             for (int i = 0; i < 4; ++i) o[4 * b + i] = pack_bf2(h[i], h[i + 4]);
           }
-          if (valid) {
-            uint4 *dst = reinterpret_cast<uint4 *>(p.out + orow * p.out_ld + nt * 128 + c0);
+          store_chunk(o, full, valid, orow, nt * 128 + c0);
+        }
+      } else if (MODE == PF_DOWN) {
+        // bf16(bf16(y) * score): the score is a bf16 value.
+        const uint32_t s16 = valid ? (uint32_t)f2bf(p.row_score[orow]) : 0x3F80u;
+        const uint32_t sc2 = s16 | (s16 << 16);
+#pragma unroll 1
+        for (int c0 = 128 * hf; c0 < 128 * hf + 128; c0 += 32) {
+          uint32_t v[32];
+          tc::tmem_ld32(tb + c0, v);
+          tc::tmem_ld_wait();
+          uint32_t o[16];
 #pragma unroll
-            for (int v = 0; v < 4; ++v)
-              dst[v] = make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
-          }
+          for (int j = 0; j < 16; ++j)
+            o[j] = mul_bf16x2(cvt_bf16x2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])),
+                              sc2);
+          store_chunk(o, full, valid, orow, nt * PF_BN + c0);
         }
       } else {
-        const float sc = (MODE == PF_DOWN && valid) ? p.row_score[orow] : 1.f;
+        const float sc = 1.f;
 #pragma unroll 1
         for (int c0 = 128 * hf; c0 < 128 * hf + 128; c0 += 32) {
           uint32_t v[32];
@@ -394,6 +455,7 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&bar_acc_empty[acc]);
     }
+    if (lane == 0) tc::bulk_wait<0>();  // stores complete before the CTA ends
   }
   tc::tc_fence_before();
   __syncthreads();
@@ -1092,6 +1154,22 @@ static int make_map_bf16(CUtensorMap *m, const void *base, uint64_t rows, uint64
   return VB_OK;
 }
 
+// Output rows of a GEMM: bf16 [rows, cols] row-major, box {32 cols, 32 rows},
+// 64-byte swizzle (the epilogue's staging layout).
+static int make_map_out(CUtensorMap *m, const void *base, uint64_t rows, uint64_t cols) {
+  EncodeTiledFn f = encode_fn();
+  if (!f) return set_error(VB_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = f(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides,
+                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                 CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(VB_ERR_INVALID, "tensor map (out) failed: %d", (int)r);
+  return VB_OK;
+}
+
 // bf16 [n][rows][cols] (row-major), box {64 cols, box_rows, 1}, 128-byte swizzle.
 static int make_map_bf16_3d(CUtensorMap *m, const void *base, uint64_t n, uint64_t rows,
                             uint64_t cols, uint32_t box_rows) {
@@ -1139,7 +1217,8 @@ static int pf_sm_count() {
 template <int MODE>
 static int launch_gemm(const CUtensorMap &a, const CUtensorMap &b0, const CUtensorMap &b1,
                        const CUtensorMap &s0, const CUtensorMap &s1, const CUtensorMap &hv,
-                       const PfGemmParams &p, int max_tiles, cudaStream_t s) {
+                       const CUtensorMap &out, const PfGemmParams &p, int max_tiles,
+                       cudaStream_t s) {
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
@@ -1149,7 +1228,7 @@ static int launch_gemm(const CUtensorMap &a, const CUtensorMap &b0, const CUtens
   if (attr_err != cudaSuccess)
     return set_error(VB_ERR_CUDA, "pf_gemm_kernel attributes: %s", cudaGetErrorString(attr_err));
   const int grid = std::max(1, std::min(pf_sm_count(), max_tiles));
-  pf_gemm_kernel<MODE><<<grid, PF_THREADS, PF_SMEM, s>>>(a, b0, b1, s0, s1, hv, p);
+  pf_gemm_kernel<MODE><<<grid, PF_THREADS, PF_SMEM, s>>>(a, b0, b1, s0, s1, hv, out, p);
   return check_launch("pf_gemm_kernel");
 }
 
@@ -1186,7 +1265,7 @@ static int run_route(const uint16_t *x, int T, int H, int E, int k, int norm_top
   p.out_ld = L.NRP;
   p.bias = bias;
   p.status = status;
-  if ((rc = launch_gemm<PF_ROUTER>(ta, tb, tb, tb, tb, tb, p, nm * p.nt, s)) != VB_OK) return rc;
+  if ((rc = launch_gemm<PF_ROUTER>(ta, tb, tb, tb, tb, tb, tb, p, nm * p.nt, s)) != VB_OK) return rc;
   const int per = E <= 256 ? 8 : (E <= 512 ? 16 : 32);
   auto kfn = per == 8 ? pf_topk_kernel<8> : per == 16 ? pf_topk_kernel<16> : pf_topk_kernel<32>;
   kfn<<<(T + 7) / 8, 256, 0, s>>>((const uint16_t *)W(L.logits), L.NRP, T, E, k, norm_topk,
@@ -1233,7 +1312,7 @@ static int run_experts(const uint16_t *x, int R, const int32_t *r_row, const int
   }
   // gate/up
   {
-    CUtensorMap ta, g, u, sg, su, hv;
+    CUtensorMap ta, g, u, sg, su, hv, to;
     if ((rc = make_map_bf16(&ta, W(L.xs), L.rows_alloc, H, PF_BM)) != VB_OK) return rc;
     if ((rc = make_map_codes(&g, pool.ptr[0], pool.cap, pool.slot_stride[0], I, H, 128)) != VB_OK) return rc;
     if ((rc = make_map_codes(&u, pool.ptr[3], pool.cap, pool.slot_stride[3], I, H, 128)) != VB_OK) return rc;
@@ -1260,11 +1339,12 @@ static int run_experts(const uint16_t *x, int R, const int32_t *r_row, const int
     p.out = (uint16_t *)W(L.hs);
     p.out_ld = I;
     p.status = status;
-    if ((rc = launch_gemm<PF_GATEUP>(ta, g, u, sg, su, hv, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
+    if ((rc = make_map_out(&to, W(L.hs), L.rows_alloc, I)) != VB_OK) return rc;
+    if ((rc = launch_gemm<PF_GATEUP>(ta, g, u, sg, su, hv, to, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
   }
   // down
   {
-    CUtensorMap ta, d, sd, hv;
+    CUtensorMap ta, d, sd, hv, to;
     if ((rc = make_map_bf16(&ta, W(L.hs), L.rows_alloc, I, PF_BM)) != VB_OK) return rc;
     if ((rc = make_map_codes(&d, pool.ptr[6], pool.cap, pool.slot_stride[6], H, I, PF_BN)) != VB_OK) return rc;
     if (has_shared) {
@@ -1289,7 +1369,8 @@ static int run_experts(const uint16_t *x, int R, const int32_t *r_row, const int
     p.out_ld = H;
     p.row_score = (const float *)W(L.row_score);
     p.status = status;
-    if ((rc = launch_gemm<PF_DOWN>(ta, d, d, sd, sd, hv, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
+    if ((rc = make_map_out(&to, W(L.ys), L.rows_alloc, H)) != VB_OK) return rc;
+    if ((rc = launch_gemm<PF_DOWN>(ta, d, d, sd, sd, hv, to, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
   }
   return VB_OK;
 }
