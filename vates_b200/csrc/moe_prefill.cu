@@ -17,11 +17,13 @@
 //  P3 plan (one CTA): expert offsets, the reference's group of every expert
 //     (the add order of the final reduce), and the list of 128-row tiles.
 //     The shared expert is expert E and takes every token.
-//  P4 gather: x rows into expert-sorted order (with the 8-column code
-//     permutation described below), route <-> row maps.
+//  P4 sort: every route gets a row of the expert-sorted order (its token
+//     row, its score, route <-> row maps); no rows are copied.
 //  P5 grouped GEMM gate/up: dequantized 4-bit tiles (bf16, exact q*s+b
-//     rounded once) x gathered rows, fp32 accumulation in TMEM; epilogue
-//     bf16(gate), bf16(up), SwiGLU (bf16 per op) -> h rows.
+//     rounded once) x the routes' token rows, which two warps of the GEMM
+//     copy straight from x into the swizzled A tiles (cp.async); fp32
+//     accumulation in TMEM; epilogue bf16(gate), bf16(up), SwiGLU (bf16 per
+//     op) -> h rows.
 //  P6 grouped GEMM down: h rows x dequantized down tiles; epilogue
 //     bf16(bf16(y) * score).
 //  P7 combine: per token, the routed rows are added starting from zero in
@@ -29,17 +31,18 @@
 //     bf16 rounding after every add, then + bf16(bf16(sigmoid) * shared).
 //
 // Code permutation: a packed 32-bit word holds codes 8w..8w+7 (LSB first).
-// One LOP3 turns nibbles (i, i+4) into the bf16 pair (128+q_i, 128+q_{i+4}),
-// so the dequantized B tiles hold, inside every 8-column block, the columns
-// in the order (0,4,1,5,2,6,3,7). The A operands (gathered x rows and h
-// rows) are written in the same order, which leaves every dot product
-// unchanged.
+// One LOP3 turns nibbles (i, i+4) into the bf16 pair (128+q_i, 128+q_{i+4}).
+// Gate/up B tiles are put back into column order (their A rows are x rows
+// as stored); down B tiles keep, inside every 8-column block, the order
+// (0,4,1,5,2,6,3,7), and the gate/up epilogue writes the h rows (the down A
+// operand) in that order too, which leaves every dot product unchanged.
 //
-// GEMM kernel (one persistent CTA per SM, 16 warps): warp 0 issues TMA loads
+// GEMM kernel (one persistent CTA per SM, 20 warps): warp 0 issues TMA loads
 // (A tile 128x64 bf16 with the 128-byte swizzle, packed B 256 rows x 32 B),
-// warp 1 issues tcgen05.mma (M=128, N=256, K=16 steps) into one of two TMEM
-// accumulators, warps 4-11 dequantize B into the swizzled bf16 layout, and
-// warps 12-19 drain TMEM through the epilogue. Every mbarrier wait is
+// warps 2-3 (gate/up) copy the A rows from x instead, warp 1 issues
+// tcgen05.mma (M=128, N=256, K=16 steps) into one of two TMEM accumulators,
+// warps 4-11 dequantize B into the swizzled bf16 layout, and warps 12-19
+// drain TMEM through the epilogue. Every mbarrier wait is
 // bounded; on a timeout the kernel raises VB_STATUS_TIMEOUT, winds down and
 // frees its TMEM.
 #include <algorithm>
@@ -54,7 +57,7 @@ namespace vb {
 constexpr int PF_BM = 128;
 constexpr int PF_BN = 256;
 constexpr int PF_BK = 64;
-constexpr int PF_STAGES = 3;
+constexpr int PF_STAGES_MAX = 4;
 constexpr int PF_THREADS = 640;  // 20 warps
 constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;        // 16 KB
 constexpr int PF_B_BYTES = PF_BN * PF_BK * 2;        // 32 KB
@@ -63,11 +66,20 @@ constexpr int PF_STAGE_BYTES = PF_A_BYTES + PF_B_BYTES + PF_P_BYTES;
 // Epilogue staging for TMA stores: per epilogue warp two 32-row x 32-column
 // bf16 chunks (64-byte rows, 64-byte swizzle).
 constexpr int PF_OUT_CHUNK = 32 * 64;
-constexpr int PF_OUT_BYTES = 8 * 2 * PF_OUT_CHUNK;
-constexpr int PF_SMEM = PF_STAGES * PF_STAGE_BYTES + PF_OUT_BYTES + 1024;  // + alignment slack
 constexpr uint64_t PF_WAIT_NS = 2000000000ull;       // 2 s per wait
 
 enum PfMode : int { PF_GATEUP = 0, PF_DOWN = 1, PF_ROUTER = 2 };
+
+// Gate/up (epilogue light, A rows gathered with two stages in flight) runs
+// four pipeline stages and stores h directly; the other modes run three and
+// stage their output for TMA stores.
+constexpr int pf_stages(int mode) { return mode == PF_GATEUP ? 4 : 3; }
+constexpr int pf_out_bytes(int mode) { return mode == PF_GATEUP ? 0 : 8 * 2 * PF_OUT_CHUNK; }
+constexpr int pf_smem(int mode) {
+  return pf_stages(mode) * PF_STAGE_BYTES + pf_out_bytes(mode) + 1024;  // + alignment slack
+}
+static_assert(pf_smem(PF_GATEUP) <= 232448 - 256 && pf_smem(PF_DOWN) <= 232448 - 256,
+              "pf_gemm_kernel shared memory");
 
 struct PfGemmParams {
   int mode;
@@ -84,6 +96,8 @@ struct PfGemmParams {
   uint16_t *out;    // output rows (bf16)
   int out_ld;
   const float *row_score;  // down: per sorted row
+  const uint16_t *x;       // gate/up: token rows [*, K]
+  const int32_t *tok_of;   // gate/up: row of x behind each sorted row
   const float *bias;       // router: per column (nullable)
   int32_t *status;
 };
@@ -123,7 +137,9 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  __shared__ __align__(8) uint64_t bar_tma[PF_STAGES], bar_deq[PF_STAGES], bar_empty[PF_STAGES];
+  constexpr int NS = pf_stages(MODE);
+  __shared__ __align__(8) uint64_t bar_tma[PF_STAGES_MAX], bar_deq[PF_STAGES_MAX],
+      bar_empty[PF_STAGES_MAX];
   __shared__ __align__(8) uint64_t bar_acc_full[2], bar_acc_empty[2], bar_final;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
@@ -134,8 +150,9 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   constexpr bool DEQ = MODE != PF_ROUTER;
 
   if (tid == 0) {
-    for (int s = 0; s < PF_STAGES; ++s) {
-      tc::mbar_init(&bar_tma[s], 1);
+    for (int s = 0; s < NS; ++s) {
+      // gate/up: the TMA producer + the 64 threads of the A-gather warps
+      tc::mbar_init(&bar_tma[s], MODE == PF_GATEUP ? 1 + 64 : 1);
       tc::mbar_init(&bar_deq[s], 8);
       tc::mbar_init(&bar_empty[s], 1);
     }
@@ -152,7 +169,7 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tc::tmem_relinquish();
   }
   if (warp == 0 && lane == 0) {
-    tc::prefetch_tmap(&tmA);
+    if (MODE != PF_GATEUP) tc::prefetch_tmap(&tmA);
     tc::prefetch_tmap(&tmB0);
     if (MODE == PF_GATEUP) tc::prefetch_tmap(&tmB1);
   }
@@ -181,21 +198,20 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int slot = sh ? 0 : (MODE == PF_ROUTER ? 0 : p.slot_of[e]);
         const int hv = MODE == PF_ROUTER ? -1 : p.heavy_of[e];
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
-          const int s = it % PF_STAGES;
-          const uint32_t ph = (it / PF_STAGES) & 1;
+          const int s = it % NS;
+          const uint32_t ph = (it / NS) & 1;
           if (!tc::mbar_wait(&bar_empty[s], ph ^ 1, abort, PF_WAIT_NS)) { fail(); break; }
           if (hv >= 0) {
             // pre-dequantized bf16 weights: straight into the B tile
-            tc::mbar_arrive_expect_tx(&bar_tma[s], PF_A_BYTES + PF_B_BYTES);
-            tc::tma_load_2d(stage_a(s), &tmA, &bar_tma[s], ks * PF_BK, row0);
+            tc::mbar_arrive_expect_tx(&bar_tma[s], (MODE == PF_GATEUP ? 0 : PF_A_BYTES) + PF_B_BYTES);
+            if (MODE != PF_GATEUP) tc::tma_load_2d(stage_a(s), &tmA, &bar_tma[s], ks * PF_BK, row0);
             tc::tma_load_3d(stage_b(s), &tmHv, &bar_tma[s], ks * PF_BK, nt * PF_BN, hv);
           } else if (MODE == PF_ROUTER) {
             tc::mbar_arrive_expect_tx(&bar_tma[s], PF_A_BYTES + PF_B_BYTES);
             tc::tma_load_2d(stage_a(s), &tmA, &bar_tma[s], ks * PF_BK, row0);
             tc::tma_load_2d(stage_b(s), &tmB0, &bar_tma[s], ks * PF_BK, nt * PF_BN);
           } else if (MODE == PF_GATEUP) {
-            tc::mbar_arrive_expect_tx(&bar_tma[s], PF_A_BYTES + PF_P_BYTES);
-            tc::tma_load_2d(stage_a(s), &tmA, &bar_tma[s], ks * PF_BK, row0);
+            tc::mbar_arrive_expect_tx(&bar_tma[s], PF_P_BYTES);  // A: the gather warps
             const CUtensorMap *g = sh ? &tmS0 : &tmB0;
             const CUtensorMap *u = sh ? &tmS1 : &tmB1;
             tc::tma_load_3d(stage_p(s), g, &bar_tma[s], ks * (PF_BK / 2), nt * 128, slot);
@@ -210,11 +226,51 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
       }
       // Wind down: let the copies already issued land before the CTA ends.
-      for (int k = 0; k < PF_STAGES && it - 1 - k >= 0; ++k) {
+      for (int k = 0; k < NS && it - 1 - k >= 0; ++k) {
         const int j = it - 1 - k;
-        tc::mbar_wait(&bar_tma[j % PF_STAGES], (j / PF_STAGES) & 1, nullptr, PF_WAIT_NS);
+        tc::mbar_wait(&bar_tma[j % NS], (j / NS) & 1, nullptr, PF_WAIT_NS);
       }
     }
+  } else if (MODE == PF_GATEUP && (warp == 2 || warp == 3)) {
+    // ---------------- A gather (gate/up) ----------------
+    // Warp gw copies tile rows 64 gw .. 64 gw + 63 of every k-step: lane l
+    // moves 16-byte chunk l % 8 of rows 64 gw + 4 j + l / 8, j < 16 (rows
+    // past the tile's end repeat its first row), into the swizzled A tile.
+    // Every thread's arrival on the stage barrier fires when its copies
+    // have landed (cp.async.mbarrier.arrive), so the warps never wait for
+    // data, only for free stages.
+    const int gw = warp - 2, c = lane & 7;
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < n_tiles; t += gridDim.x) {
+      if (__shfl_sync(0xffffffffu, (!ok || *abort) ? 1 : 0, 0)) break;  // warp-uniform
+      const int mt = t / p.nt;
+      const int row0 = p.mtiles[3 * mt + 1], rows = p.mtiles[3 * mt + 2];
+      const int tok0 = p.tok_of[row0];
+      const uint16_t *src[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int r = 64 * gw + 4 * j + (lane >> 3);
+        src[j] = p.x + (size_t)(r < rows ? p.tok_of[row0 + r] : tok0) * p.K + c * 8;
+      }
+      for (int ks = 0; ks < ksteps; ++ks, ++it) {
+        const int s = it % NS;
+        const uint32_t ph = (it / NS) & 1;
+        bool got = true;
+        if (lane == 0) got = tc::mbar_wait(&bar_empty[s], ph ^ 1, abort, PF_WAIT_NS);
+        if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) {
+          if (lane == 0) fail();
+          ok = false;
+          break;
+        }
+        uint8_t *a = stage_a(s);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          cp_async16(a + sw128(64 * gw + 4 * j + (lane >> 3), c), src[j] + ks * PF_BK);
+        tc::cp_async_mbar_arrive_noinc(&bar_tma[s]);
+      }
+    }
+    cp_async_wait<0>();
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
@@ -233,8 +289,8 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const uint32_t d = tmem + acc * PF_BN;
         bool ok = true;
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
-          const int s = it % PF_STAGES;
-          const uint32_t ph = (it / PF_STAGES) & 1;
+          const int s = it % NS;
+          const uint32_t ph = (it / NS) & 1;
           // The dequant barrier of a stage only advances on dequantized
           // steps, so its parity is tracked separately.
           uint64_t *ready = deq ? &bar_deq[s] : &bar_tma[s];
@@ -273,7 +329,7 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         // TMA barriers so that no later parity wait can match a stale phase.
         bool ok = true;
         for (int ks = 0; ks < ksteps; ++ks, ++it) {
-          if (!tc::mbar_wait_sleep(&bar_tma[it % PF_STAGES], (it / PF_STAGES) & 1, abort,
+          if (!tc::mbar_wait_sleep(&bar_tma[it % NS], (it / NS) & 1, abort,
                                    PF_WAIT_NS)) {
             fail();
             ok = false;
@@ -301,8 +357,8 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           reinterpret_cast<const uint16_t *>(pool_ptr(pool, tsc + 1, slot)) + (size_t)row * ng;
       bool ok = true;
       for (int ks = 0; ks < ksteps; ++ks, ++it) {
-        const int s = it % PF_STAGES;
-        const uint32_t ph = (it / PF_STAGES) & 1;
+        const int s = it % NS;
+        const uint32_t ph = (it / NS) & 1;
         const int gi = ks >> p.gshift;
         const uint32_t sc = __ldg(sp + gi), bi = __ldg(bp + gi);
         if (!tc::mbar_wait(&bar_tma[s], ph, abort, PF_WAIT_NS)) { fail(); ok = false; break; }
@@ -323,7 +379,13 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(pr[i]), "r"(0x43004300u));
             o[i] = bf16x2_fma(q, s2, b2);
           }
-          *reinterpret_cast<uint4 *>(dst + sw128(r, w)) = make_uint4(o[0], o[1], o[2], o[3]);
+          uint4 chunk;
+          if (MODE == PF_GATEUP)  // pairs (0,4),(1,5),(2,6),(3,7) -> columns 0..7
+            chunk = make_uint4(__byte_perm(o[0], o[1], 0x5410), __byte_perm(o[2], o[3], 0x5410),
+                               __byte_perm(o[0], o[1], 0x7632), __byte_perm(o[2], o[3], 0x7632));
+          else
+            chunk = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4 *>(dst + sw128(r, w)) = chunk;
         }
         tc::fence_proxy_async_smem();
         __syncwarp();
@@ -341,7 +403,7 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     // Chunks of 32 rows x 32 columns whose rows are all valid go out as one
     // TMA store from a swizzled staging buffer (two per warp, alternating);
     // the rows of a partial chunk are stored by their threads.
-    uint8_t *obuf = smem + PF_STAGES * PF_STAGE_BYTES + (warp - 12) * 2 * PF_OUT_CHUNK;
+    uint8_t *obuf = smem + NS * PF_STAGE_BYTES + (warp - 12) * 2 * PF_OUT_CHUNK;  // not gate/up
     int nst = 0;
     auto store_chunk = [&](const uint32_t (&o)[16], bool full, bool valid, size_t orow,
                            int col) {
@@ -379,7 +441,7 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       tc::tc_fence_after();
       const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + acc * PF_BN;
       const bool valid = m < rows;
-      const bool full = q * 32 + 32 <= rows;  // warp-uniform
+      const bool full = MODE != PF_GATEUP && q * 32 + 32 <= rows;  // warp-uniform
       const size_t orow = (size_t)(row0 + m);
       if (MODE == PF_GATEUP) {
         // Columns [0,128) gate, [128,256) up of intermediate rows nt*128 + c;
@@ -504,9 +566,14 @@ __global__ void pf_topk_kernel(const uint16_t *__restrict__ logits, int ld, int 
                                int32_t *__restrict__ counts, float *__restrict__ sgate,
                                int32_t *__restrict__ out_inds, uint16_t *__restrict__ out_scores,
                                uint16_t *__restrict__ out_logits, int32_t *__restrict__ status) {
+  // Route counts go to a shared-memory histogram first (the hot experts of
+  // skewed routing would serialise global atomics on a few addresses).
+  extern __shared__ int32_t s_hist[];  // [E]
+  for (int i = threadIdx.x; i < E; i += blockDim.x) s_hist[i] = 0;
+  __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (t >= T) return;
+  const int nw = blockDim.x >> 5;
+  for (int t = blockIdx.x * nw + (threadIdx.x >> 5); t < T; t += gridDim.x * nw) {
   const uint16_t *lr = logits + (size_t)t * ld;
   float v[PER];
 #pragma unroll
@@ -570,11 +637,15 @@ __global__ void pf_topk_kernel(const uint16_t *__restrict__ logits, int ld, int 
     }
     inds[t * k + lane] = ex;
     scores[t * k + lane] = score;
-    atomicAdd(counts + ex, 1);
+    atomicAdd(s_hist + ex, 1);
     if (out_inds) out_inds[t * k + lane] = ex;
     if (out_scores) out_scores[t * k + lane] = f2bf(score);
   }
   if (lane == 0 && has_shared) sgate[t] = rbf(mlx_sigmoid(bf2f(lr[E])));
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < E; i += blockDim.x)
+    if (s_hist[i]) atomicAdd(counts + i, s_hist[i]);
 }
 
 // ----------------------------------------------------------------------------
@@ -707,10 +778,16 @@ __global__ void pf_set_kernel(int32_t *p, int32_t v) { *p = v; }
 // Route histogram over experts 0..E (E = shared); negative ids are skipped.
 __global__ void pf_hist_kernel(const int32_t *__restrict__ r_exp, int n, int E,
                                int32_t *__restrict__ counts) {
+  extern __shared__ int32_t s_hist[];  // [E + 1]: per-CTA counts, then one flush
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) s_hist[i] = 0;
+  __syncthreads();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const int e = r_exp[i];
-    if (e >= 0 && e <= E) atomicAdd(counts + e, 1);
+    if (e >= 0 && e <= E) atomicAdd(s_hist + e, 1);
   }
+  __syncthreads();
+  for (int i = threadIdx.x; i <= E; i += blockDim.x)
+    if (s_hist[i]) atomicAdd(counts + i, s_hist[i]);
 }
 
 // ----------------------------------------------------------------------------
@@ -768,45 +845,55 @@ __global__ void pf_predequant_kernel(VbQuantPool pool, VbQuantPool shared, int s
       asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(pr[k]), "r"(0x43004300u));
       o[k] = bf16x2_fma(q, s2, b2);
     }
-    *reinterpret_cast<uint4 *>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
+    if (i < wgu_words)  // gate/up rows in column order
+      *reinterpret_cast<uint4 *>(dst) =
+          make_uint4(__byte_perm(o[0], o[1], 0x5410), __byte_perm(o[2], o[3], 0x5410),
+                     __byte_perm(o[0], o[1], 0x7632), __byte_perm(o[2], o[3], 0x7632));
+    else  // down rows in the code order of the h rows
+      *reinterpret_cast<uint4 *>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
 // ----------------------------------------------------------------------------
-// P4: gather rows of x into expert order, in the 8-column code order
-// (0,4,1,5,2,6,3,7). One warp per route (t, j), then one per shared row.
+// P4: sort. Every routed (resident) route gets a row of the expert-sorted
+// order: one CTA per PF_SORT_ROUTES routes counts them per expert in shared
+// memory, reserves each expert's rows with one global add, then hands them
+// out. The order inside an expert is arbitrary (rows are independent).
 // ----------------------------------------------------------------------------
-__global__ void pf_gather_kernel(const uint16_t *__restrict__ x, int H, int n,
-                                 const int32_t *__restrict__ r_row,
-                                 const int32_t *__restrict__ r_exp,
-                                 const float *__restrict__ r_score,
-                                 const int32_t *__restrict__ slot_of,
-                                 const int32_t *__restrict__ offsets,
-                                 int32_t *__restrict__ cursor, uint16_t *__restrict__ xs,
-                                 float *__restrict__ row_score, int32_t *__restrict__ pos_of) {
-  const int lane = threadIdx.x & 31;
-  const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (w >= n) return;
-  const int e = r_exp[w];
-  int pos = -1;
-  if (e >= 0 && slot_of[e] >= 0) {
-    if (lane == 0) pos = offsets[e] + atomicAdd(cursor + e, 1);
-    pos = __shfl_sync(0xffffffffu, pos, 0);
+constexpr int PF_SORT_PER_THREAD = 8;
+constexpr int PF_SORT_ROUTES = 256 * PF_SORT_PER_THREAD;
+__global__ void __launch_bounds__(256) pf_sort_kernel(
+    int n, int E, const int32_t *__restrict__ r_row, const int32_t *__restrict__ r_exp,
+    const float *__restrict__ r_score, const int32_t *__restrict__ slot_of,
+    const int32_t *__restrict__ offsets, int32_t *__restrict__ cursor,
+    int32_t *__restrict__ tok_of, float *__restrict__ row_score, int32_t *__restrict__ pos_of) {
+  extern __shared__ int32_t s_sort[];  // count[E + 1], base[E + 1]
+  int32_t *cnt = s_sort, *base = s_sort + E + 1;
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  const int w0 = blockIdx.x * PF_SORT_ROUTES;
+  int ex[PF_SORT_PER_THREAD], loc[PF_SORT_PER_THREAD];
+#pragma unroll
+  for (int j = 0; j < PF_SORT_PER_THREAD; ++j) {
+    const int w = w0 + threadIdx.x + 256 * j;
+    ex[j] = w < n ? r_exp[w] : -1;
+    loc[j] = -1;
+    if (ex[j] >= 0 && ex[j] <= E && slot_of[ex[j]] >= 0) loc[j] = atomicAdd(cnt + ex[j], 1);
   }
-  if (lane == 0) pos_of[w] = pos;
-  if (pos < 0) return;
-  if (lane == 0) row_score[pos] = r_score[w];
-  const uint4 *src = reinterpret_cast<const uint4 *>(x + (size_t)r_row[w] * H);
-  uint4 *dst = reinterpret_cast<uint4 *>(xs + (size_t)pos * H);
-  for (int c = lane; c < H / 8; c += 32) {
-    const uint4 v = __ldg(src + c);
-    // bf16 lanes 0..7 -> (0,4,1,5,2,6,3,7)
-    uint4 o;
-    o.x = __byte_perm(v.x, v.z, 0x5410);
-    o.y = __byte_perm(v.x, v.z, 0x7632);
-    o.z = __byte_perm(v.y, v.w, 0x5410);
-    o.w = __byte_perm(v.y, v.w, 0x7632);
-    dst[c] = o;
+  __syncthreads();
+  for (int i = threadIdx.x; i <= E; i += blockDim.x)
+    if (cnt[i]) base[i] = offsets[i] + atomicAdd(cursor + i, cnt[i]);
+  __syncthreads();
+#pragma unroll
+  for (int j = 0; j < PF_SORT_PER_THREAD; ++j) {
+    const int w = w0 + threadIdx.x + 256 * j;
+    if (w >= n) continue;
+    const int pos = loc[j] >= 0 ? base[ex[j]] + loc[j] : -1;
+    pos_of[w] = pos;
+    if (pos >= 0) {
+      tok_of[pos] = r_row[w];
+      row_score[pos] = r_score[w];
+    }
   }
 }
 
@@ -1055,7 +1142,7 @@ static RouteLayout route_layout(int T, int H, int E) {
 // Workspace of the expert phase for n routes (experts 0..E, E = shared).
 struct ExpertsLayout {
   size_t counts, offsets, slot_of, heavy_of, heavy_e, n_heavy, cursor, mtiles, n_mtiles, pos_of,
-      row_score, xs, hs, ys, wgu, wd, total;
+      row_score, tok_of, hs, ys, wgu, wd, total;
   int max_mtiles, rows_alloc;
 };
 static ExpertsLayout experts_layout(int n, int H, int I, int E) {
@@ -1079,7 +1166,7 @@ static ExpertsLayout experts_layout(int n, int H, int I, int E) {
   L.n_mtiles = take(4);
   L.pos_of = take((size_t)n * 4 + 4);
   L.row_score = take((size_t)n * 4 + 4);
-  L.xs = take((size_t)L.rows_alloc * H * 2);
+  L.tok_of = take((size_t)L.rows_alloc * 4);
   L.hs = take((size_t)L.rows_alloc * I * 2);
   L.ys = take((size_t)L.rows_alloc * H * 2);
   L.wgu = take((size_t)PF_HEAVY_MAX * 2 * I * H * 2);
@@ -1223,12 +1310,12 @@ static int launch_gemm(const CUtensorMap &a, const CUtensorMap &b0, const CUtens
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
     attr_err = cudaFuncSetAttribute(pf_gemm_kernel<MODE>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, PF_SMEM);
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, pf_smem(MODE));
   });
   if (attr_err != cudaSuccess)
     return set_error(VB_ERR_CUDA, "pf_gemm_kernel attributes: %s", cudaGetErrorString(attr_err));
   const int grid = std::max(1, std::min(pf_sm_count(), max_tiles));
-  pf_gemm_kernel<MODE><<<grid, PF_THREADS, PF_SMEM, s>>>(a, b0, b1, s0, s1, hv, out, p);
+  pf_gemm_kernel<MODE><<<grid, PF_THREADS, pf_smem(MODE), s>>>(a, b0, b1, s0, s1, hv, out, p);
   return check_launch("pf_gemm_kernel");
 }
 
@@ -1268,7 +1355,8 @@ static int run_route(const uint16_t *x, int T, int H, int E, int k, int norm_top
   if ((rc = launch_gemm<PF_ROUTER>(ta, tb, tb, tb, tb, tb, tb, p, nm * p.nt, s)) != VB_OK) return rc;
   const int per = E <= 256 ? 8 : (E <= 512 ? 16 : 32);
   auto kfn = per == 8 ? pf_topk_kernel<8> : per == 16 ? pf_topk_kernel<16> : pf_topk_kernel<32>;
-  kfn<<<(T + 7) / 8, 256, 0, s>>>((const uint16_t *)W(L.logits), L.NRP, T, E, k, norm_topk,
+  const int tk_grid = std::max(1, std::min((T + 7) / 8, pf_sm_count() * 4));
+  kfn<<<tk_grid, 256, (size_t)E * sizeof(int32_t), s>>>((const uint16_t *)W(L.logits), L.NRP, T, E, k, norm_topk,
                                   wsg ? 1 : 0, table, cap, inds, scores, counts, sgate, out_inds,
                                   out_scores, out_logits, status);
   return check_launch("pf_topk_kernel");
@@ -1282,13 +1370,13 @@ static int run_experts(const uint16_t *x, int R, const int32_t *r_row, const int
                        const int32_t *table, const VbQuantPool &pool, const VbQuantPool &shared,
                        bool has_shared, int32_t *status, uint8_t *ws, const ExpertsLayout &L,
                        cudaStream_t s, bool counts_ready) {
-  (void)R;
   auto W = [&](size_t off) { return ws + off; };
   int rc;
   if (!counts_ready) {
     if (cudaMemsetAsync(W(L.counts), 0, (size_t)(E + 2) * 4, s) != cudaSuccess)
       return set_error(VB_ERR_CUDA, "experts: memset");
-    pf_hist_kernel<<<std::max(1, std::min(1024, (n + 255) / 256)), 256, 0, s>>>(
+    pf_hist_kernel<<<std::max(1, std::min(pf_sm_count() * 2, (n + 255) / 256)), 256,
+                     (size_t)(E + 1) * sizeof(int32_t), s>>>(
         r_exp, n, E, (int32_t *)W(L.counts));
     if ((rc = check_launch("pf_hist_kernel")) != VB_OK) return rc;
   }
@@ -1304,16 +1392,16 @@ static int run_experts(const uint16_t *x, int R, const int32_t *r_row, const int
       (uint16_t *)W(L.wgu), (uint16_t *)W(L.wd));
   if ((rc = check_launch("pf_predequant_kernel")) != VB_OK) return rc;
   if (n > 0) {
-    pf_gather_kernel<<<(n + 7) / 8, 256, 0, s>>>(
-        x, H, n, r_row, r_exp, r_score, (const int32_t *)W(L.slot_of),
-        (const int32_t *)W(L.offsets), (int32_t *)W(L.cursor), (uint16_t *)W(L.xs),
+    pf_sort_kernel<<<(n + PF_SORT_ROUTES - 1) / PF_SORT_ROUTES, 256,
+                     (size_t)2 * (E + 1) * sizeof(int32_t), s>>>(
+        n, E, r_row, r_exp, r_score, (const int32_t *)W(L.slot_of),
+        (const int32_t *)W(L.offsets), (int32_t *)W(L.cursor), (int32_t *)W(L.tok_of),
         (float *)W(L.row_score), (int32_t *)W(L.pos_of));
-    if ((rc = check_launch("pf_gather_kernel")) != VB_OK) return rc;
+    if ((rc = check_launch("pf_sort_kernel")) != VB_OK) return rc;
   }
   // gate/up
   {
     CUtensorMap ta, g, u, sg, su, hv, to;
-    if ((rc = make_map_bf16(&ta, W(L.xs), L.rows_alloc, H, PF_BM)) != VB_OK) return rc;
     if ((rc = make_map_codes(&g, pool.ptr[0], pool.cap, pool.slot_stride[0], I, H, 128)) != VB_OK) return rc;
     if ((rc = make_map_codes(&u, pool.ptr[3], pool.cap, pool.slot_stride[3], I, H, 128)) != VB_OK) return rc;
     if (has_shared) {
@@ -1324,6 +1412,7 @@ static int run_experts(const uint16_t *x, int R, const int32_t *r_row, const int
       su = u;
     }
     if ((rc = make_map_bf16_3d(&hv, W(L.wgu), PF_HEAVY_MAX, 2 * (uint64_t)I, H, PF_BN)) != VB_OK) return rc;
+    ta = hv;  // the A rows are copied from x by the kernel's gather warps
     PfGemmParams p{};
     p.mode = PF_GATEUP;
     p.heavy_of = (const int32_t *)W(L.heavy_of);
@@ -1338,6 +1427,8 @@ static int run_experts(const uint16_t *x, int R, const int32_t *r_row, const int
     p.shared = shared;
     p.out = (uint16_t *)W(L.hs);
     p.out_ld = I;
+    p.x = x;
+    p.tok_of = (const int32_t *)W(L.tok_of);
     p.status = status;
     if ((rc = make_map_out(&to, W(L.hs), L.rows_alloc, I)) != VB_OK) return rc;
     if ((rc = launch_gemm<PF_GATEUP>(ta, g, u, sg, su, hv, to, p, L.max_mtiles * p.nt, s)) != VB_OK) return rc;
