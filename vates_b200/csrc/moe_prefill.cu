@@ -796,61 +796,67 @@ __global__ void pf_hist_kernel(const int32_t *__restrict__ r_exp, int n, int E,
 // stored in 256-row blocks [gate rows 128j..128j+127 | up rows 128j..],
 // down rows as they are. One thread per packed word.
 // ----------------------------------------------------------------------------
-__global__ void pf_predequant_kernel(VbQuantPool pool, VbQuantPool shared, int shared_e,
-                                     const int32_t *__restrict__ heavy_e,
-                                     const int32_t *__restrict__ n_heavy,
-                                     const int32_t *__restrict__ slot_of, int H, int I,
-                                     int gshift, uint16_t *__restrict__ wgu,
-                                     uint16_t *__restrict__ wd) {
+__global__ void __launch_bounds__(256)
+pf_predequant_kernel(VbQuantPool pool, VbQuantPool shared, int shared_e,
+                     const int32_t *__restrict__ heavy_e, const int32_t *__restrict__ n_heavy,
+                     const int32_t *__restrict__ slot_of, int H, int I, int gshift,
+                     uint16_t *__restrict__ wgu, uint16_t *__restrict__ wd) {
   const int h = blockIdx.y;
   if (h >= *n_heavy) return;
   const int e = heavy_e[h];
   const bool sh = e == shared_e;
   const VbQuantPool &pl = sh ? shared : pool;
   const int slot = sh ? 0 : slot_of[e];
-  const size_t wgu_words = (size_t)2 * I * (H / 8), wd_words = (size_t)H * (I / 8);
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < wgu_words + wd_words;
+  // One thread per 32 consecutive codes of a row (four packed words, one
+  // scale group): gate/up rows first, then down rows.
+  const size_t wgu_q = (size_t)2 * I * (H / 32), wd_q = (size_t)H * (I / 32);
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < wgu_q + wd_q;
        i += (size_t)gridDim.x * blockDim.x) {
-    int row, wcol, K, tw, tsc;
+    int row, qc, K, tw, tsc;
     uint16_t *dst;
-    if (i < wgu_words) {
+    const bool gu = i < wgu_q;
+    if (gu) {
       K = H;
-      const int r = (int)(i / (H / 8));  // destination row
-      wcol = (int)(i % (H / 8));
+      const int r = (int)(i / (H / 32));  // destination row
+      qc = (int)(i % (H / 32));
       const int blk = r >> 8, within = r & 255;
       const bool up = within >= 128;
       row = blk * 128 + (within & 127);
       tw = up ? 3 : 0;
       tsc = up ? 4 : 1;
-      dst = wgu + ((size_t)h * 2 * I + r) * H + wcol * 8;
+      dst = wgu + ((size_t)h * 2 * I + r) * H + qc * 32;
     } else {
       K = I;
-      const size_t j = i - wgu_words;
-      row = (int)(j / (I / 8));
-      wcol = (int)(j % (I / 8));
+      const size_t j = i - wgu_q;
+      row = (int)(j / (I / 32));
+      qc = (int)(j % (I / 32));
       tw = 6;
       tsc = 7;
-      dst = wd + ((size_t)h * H + row) * I + wcol * 8;
+      dst = wd + ((size_t)h * H + row) * I + qc * 32;
     }
-    const uint32_t w = reinterpret_cast<const uint32_t *>(pool_ptr(pl, tw, slot))[(size_t)row * (K / 8) + wcol];
-    const int ng = (K >> 6) >> gshift, gi = (wcol * 8 / 64) >> gshift;
+    const uint4 w4 = ldg_nc_v4(pool_ptr(pl, tw, slot) + ((size_t)row * (K / 8) + 4 * qc) * 4);
+    const int ng = (K >> 6) >> gshift, gi = (qc >> 1) >> gshift;
     const uint32_t sc = reinterpret_cast<const uint16_t *>(pool_ptr(pl, tsc, slot))[(size_t)row * ng + gi];
     const uint32_t bi = reinterpret_cast<const uint16_t *>(pool_ptr(pl, tsc + 1, slot))[(size_t)row * ng + gi];
     const uint32_t s2 = sc | (sc << 16), b2 = bi | (bi << 16);
-    uint32_t pr[4], o[4];
-    nib_pairs4(w, pr);
+    const uint32_t words[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      uint32_t q;
-      asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(pr[k]), "r"(0x43004300u));
-      o[k] = bf16x2_fma(q, s2, b2);
+    for (int wi = 0; wi < 4; ++wi) {
+      uint32_t pr[4], o[4];
+      nib_pairs4(words[wi], pr);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        uint32_t q;
+        asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(pr[k]), "r"(0x43004300u));
+        o[k] = bf16x2_fma(q, s2, b2);
+      }
+      uint4 *d = reinterpret_cast<uint4 *>(dst + 8 * wi);
+      if (gu)  // gate/up rows in column order
+        *d = make_uint4(__byte_perm(o[0], o[1], 0x5410), __byte_perm(o[2], o[3], 0x5410),
+                        __byte_perm(o[0], o[1], 0x7632), __byte_perm(o[2], o[3], 0x7632));
+      else  // down rows in the code order of the h rows
+        *d = make_uint4(o[0], o[1], o[2], o[3]);
     }
-    if (i < wgu_words)  // gate/up rows in column order
-      *reinterpret_cast<uint4 *>(dst) =
-          make_uint4(__byte_perm(o[0], o[1], 0x5410), __byte_perm(o[2], o[3], 0x5410),
-                     __byte_perm(o[0], o[1], 0x7632), __byte_perm(o[2], o[3], 0x7632));
-    else  // down rows in the code order of the h rows
-      *reinterpret_cast<uint4 *>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -1386,7 +1392,7 @@ static int run_experts(const uint16_t *x, int R, const int32_t *r_row, const int
       (int32_t *)W(L.n_heavy), (int32_t *)W(L.cursor), (int32_t *)W(L.mtiles),
       (int32_t *)W(L.n_mtiles));
   if ((rc = check_launch("pf_plan_kernel")) != VB_OK) return rc;
-  pf_predequant_kernel<<<dim3(384, PF_HEAVY_MAX), 256, 0, s>>>(
+  pf_predequant_kernel<<<dim3(128, PF_HEAVY_MAX), 256, 0, s>>>(
       pool, shared, has_shared ? E : -1, (const int32_t *)W(L.heavy_e),
       (const int32_t *)W(L.n_heavy), (const int32_t *)W(L.slot_of), H, I, gshift,
       (uint16_t *)W(L.wgu), (uint16_t *)W(L.wd));
