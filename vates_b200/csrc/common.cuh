@@ -40,9 +40,12 @@ __device__ __forceinline__ uint16_t f2bf(float f) {
 }
 __device__ __forceinline__ float rbf(float f) { return bf2f(f2bf(f)); }
 
-// Pack two floats into a bf16x2 word (lo in bits 0-15).
+// Pack two floats into a bf16x2 word (lo in bits 0-15), round to nearest
+// even: one cvt.rn.bf16x2.f32.
 __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
-  return static_cast<uint32_t>(f2bf(lo)) | (static_cast<uint32_t>(f2bf(hi)) << 16);
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
 }
 
 // MLX sigmoid: y = 1/(1+exp(-|x|)), x<0 -> 1-y (float32).

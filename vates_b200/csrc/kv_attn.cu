@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       mnew[h] = fmaxf(m_run[h], mx[h]);
-      alpha[h] = (m_run[h] == -INFINITY) ? 0.f : expf(m_run[h] - mnew[h]);
+      alpha[h] = (m_run[h] == -INFINITY) ? 0.f : __expf(m_run[h] - mnew[h]);
       if (mnew[h] == -INFINITY) alpha[h] = 1.f;
       m_run[h] = mnew[h];
     }
@@ -340,7 +340,7 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int h = j & 1;
-      e[j] = sc[j] == -INFINITY ? 0.f : expf(sc[j] - mnew[h]);
+      e[j] = sc[j] == -INFINITY ? 0.f : __expf(sc[j] - mnew[h]);
       l_run[h] += e[j];
     }
     // P^T fragments per V group: p = bf16(e * vs); V bias term on the side.
@@ -663,7 +663,7 @@ __global__ void __launch_bounds__(A4_WARPS * 32, 3) kv_attn4_kernel(AttnParams p
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       mnew[h] = fmaxf(m_run[h], mx[h]);
-      alpha[h] = (m_run[h] == -INFINITY) ? 0.f : expf(m_run[h] - mnew[h]);
+      alpha[h] = (m_run[h] == -INFINITY) ? 0.f : __expf(m_run[h] - mnew[h]);
       if (mnew[h] == -INFINITY) alpha[h] = 1.f;
       m_run[h] = mnew[h];
     }
@@ -689,7 +689,7 @@ __global__ void __launch_bounds__(A4_WARPS * 32, 3) kv_attn4_kernel(AttnParams p
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int h = j & 1;
-      e[j] = sc[j] == -INFINITY ? 0.f : expf(sc[j] - mnew[h]);
+      e[j] = sc[j] == -INFINITY ? 0.f : __expf(sc[j] - mnew[h]);
       l_run[h] += e[j];
     }
     // P^T fragments per V group: p = bf16(e * vs); V bias term on the side.
