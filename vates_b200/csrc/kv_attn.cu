@@ -239,6 +239,14 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
   float bsum[4][2], psum[4][2];
 #pragma unroll
   for (int G = 0; G < 4; ++G) bsum[G][0] = bsum[G][1] = psum[G][0] = psum[G][1] = 0.f;
+  // Last key each of this lane's rows (2c, 2c+1) may see: -1 past the query
+  // rows, S - L + position under the causal mask.
+  int klim[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = 2 * c + h;
+    klim[h] = row >= p.QR ? -1 : (p.causal ? p.S - p.L + row % p.L : INT_MAX);
+  }
 
   const size_t head_row0 = (size_t)bh * p.cap;
   const int n_tiles = (k_end - k_begin + 15) / 16;
@@ -297,9 +305,7 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int key = key0 + g + 8 * (j >> 1);
-      const int row = 2 * c + (j & 1);
-      bool ok = row < p.QR && key < k_end;
-      if (p.causal && ok) ok = key <= p.S - p.L + (row % p.L);
+      const bool ok = key < k_end && key <= klim[j & 1];
       sc[j] = ok ? rbf(sc[j]) : -INFINITY;
     }
     // ---- online softmax (rows 2c, 2c+1) ----
@@ -572,6 +578,14 @@ __global__ void __launch_bounds__(A4_WARPS * 32, 3) kv_attn4_kernel(AttnParams p
                            reinterpret_cast<const uint8_t *>(p.vs + head_row0 * 4),
                            reinterpret_cast<const uint8_t *>(p.vb + head_row0 * 4)};
   const int row0 = 8 * warp + 2 * c;  // rows of this lane's score / output columns
+  // Last key each of rows row0, row0+1 may see: -1 past the query rows,
+  // S - L + position under the causal mask.
+  int klim[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = row0 + h;
+    klim[h] = row >= p.QR ? -1 : (p.causal ? p.S - p.L + row % p.L : INT_MAX);
+  }
 #pragma unroll 1
   for (int t = 0; t < A4_NRAW - 1; ++t) {
     if (t < n_tiles) a4_fetch(kbase, vbase, scb, p.S, k_begin + 16 * t, raw0 + t * A4_RAW, tid);
@@ -646,9 +660,7 @@ __global__ void __launch_bounds__(A4_WARPS * 32, 3) kv_attn4_kernel(AttnParams p
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int key = key0 + g + 8 * (j >> 1);
-      const int row = row0 + (j & 1);
-      bool ok = row < p.QR && key < k_end;
-      if (p.causal && ok) ok = key <= p.S - p.L + (row % p.L);
+      const bool ok = key < k_end && key <= klim[j & 1];
       sc[j] = ok ? rbf(sc[j]) : -INFINITY;
     }
     // ---- online softmax (rows row0, row0+1) ----
