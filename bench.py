@@ -220,26 +220,38 @@ def run_prefill_leg(steps: int = 10, warmup: int = 3, T: int = 32768):
     return res
 
 
-def run_prefill_ep_leg(world: int, rank: int, steps: int = 10, warmup: int = 3, T: int = 32768):
-    """Config 2 expert-parallel over the ranks (one per GPU): rank r owns
-    the experts that a greedy LPT placement over the expected Zipf load
-    gives it and starts with tokens [r*T/N, (r+1)*T/N); dispatch and combine
-    are NCCL all-to-all. Time = max over ranks (strong scaling, T fixed)."""
+def run_prefill_ep_leg(world: int, rank: int, steps: int = 10, warmup: int = 3, T: int = 32768,
+                       hot_share: float = 0.02):
+    """Config 2 expert-parallel over the ranks (one per GPU). The route
+    histogram of the batch (the router is deterministic) decides the
+    placement: experts with at least ``hot_share`` of the routes are held by
+    every rank and computed there for its own tokens, the others are owned
+    by one rank each (greedy LPT over their route counts). Rank r starts
+    with tokens [r*T/N, (r+1)*T/N); dispatch and combine are NCCL
+    all-to-all. Time = max over ranks (strong scaling, T fixed)."""
     import numpy as np
     import torch
     import torch.distributed as dist
-    from vates_b200.ep import CudaEpBackend, ep_prefill, lpt_placement
+    from vates_b200.ep import CudaEpBackend, ep_prefill, placement
     from vates_b200.pool import QuantPool
     from vates_b200.synth import E as NE, H as HH, I as II, input_tokens, make_layer, zipf_bias
     _, bf16_peak, peak_kind = peaks()
     seed = 2
-    bias = zipf_bias(seed, NE)
-    owner = lpt_placement(np.exp(bias.astype(np.float64)), world)
-    owned = [e for e in range(NE) if owner[e] == rank]
+    bias = torch.from_numpy(zipf_bias(seed, NE)).cuda()
+    x_all = input_tokens(seed, T)
+    probe = make_layer(seed, 0, QuantPool.empty_blob(1, HH, II, 4, 64, "cuda"), [], "cuda",
+                       router_bias=bias)
+    counts = CudaEpBackend(probe, torch.zeros(NE, dtype=torch.int32)).route(x_all)[3]
+    counts = counts.cpu().numpy()
+    del probe
+    owner, resident = placement(counts, world, rank, share=hot_share)
+    n_hot = int(((counts >= hot_share * counts.sum()) if world > 1 else np.zeros(NE, bool)).sum())
+    owned = [e for e in range(NE) if resident[e]]
     pool = QuantPool.empty_blob(len(owned), HH, II, 4, 64, "cuda")
-    blk = make_layer(seed, 0, pool, owned, "cuda", router_bias=torch.from_numpy(bias).cuda())
+    blk = make_layer(seed, 0, pool, owned, "cuda", router_bias=bias)
     per = T // world
-    x = input_tokens(seed, T)[rank * per:(rank + 1) * per].contiguous()
+    x = x_all[rank * per:(rank + 1) * per].contiguous()
+    del x_all
     be = CudaEpBackend(blk, torch.from_numpy(owner))
     for _ in range(max(warmup, 3)):
         ep_prefill(be, x)
@@ -258,8 +270,10 @@ def run_prefill_ep_leg(world: int, rank: int, steps: int = 10, warmup: int = 3, 
     return {"workload": "prefill_32k_1layer_ep", "tokens": T, "n_gpus": world,
             "ms_per_step": ms, "tok_per_s": T / (ms / 1e3), "tflops_algorithmic": tf,
             "tflops_per_gpu": tf / world, "frac_of_bf16_peak_per_gpu": tf / world / bf16_peak,
-            "peak_kind": peak_kind, "experts_per_gpu": len(owned),
-            "placement": "LPT over the Zipf(1.1) expected load", "scaling": "strong"}
+            "peak_kind": peak_kind, "experts_per_gpu": len(owned), "hot_experts_replicated": n_hot,
+            "placement": f"experts with >= {hot_share:.0%} of the routes on every rank, "
+                         "the rest LPT over the route counts",
+            "scaling": "strong"}
 
 
 def run_isoquant_leg(steps: int = 20, warmup: int = 3, S: int = 131072, layers: int = 12):

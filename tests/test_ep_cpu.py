@@ -150,6 +150,57 @@ def test_ep_prefill_two_gloo_ranks_matches_single_device():
     assert np.array_equal(got, ref)
 
 
+def _rank_owners(rank, world, port, owners, q):
+    _rank(rank, world, port, owners[rank], q)
+
+
+def test_ep_prefill_with_replicated_hot_experts_matches_single_device():
+    """Hot experts held by both ranks (each computes them for its own
+    tokens), the rest owned by one rank: the output is still bit-identical
+    to the single-device oracle."""
+    from vates_b200.ep import placement
+    world = 2
+    pool, shared, wr, wsg, x = _layer()
+    _, _, inds, _ = OM.router(x, wr, K, True)
+    counts = np.bincount(inds.ravel(), minlength=E)
+    owners = [placement(counts, world, r, share=1.0 / E)[0] for r in range(world)]
+    rep = owners[0] == 0
+    rep &= owners[1] == 1
+    assert rep.any() and (~rep).any()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + (os.getpid() + 150) % 300
+    procs = [ctx.Process(target=_rank_owners, args=(r, world, port, owners, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    got = np.concatenate([res[r] for r in range(world)])
+    routed = OM.expert_major_forward(x, inds, OM.router(x, wr, K, True)[3],
+                                     lambda e: (pool, int(e)), H, I, 64, 4,
+                                     layer_cap=LAYER_CAP, max_assignments=MAX_ASSIGN)
+    ref = M.bf16(routed + OM.shared_prefill(x, shared, wsg, H, I, 64, 4))
+    assert np.array_equal(got, ref)
+
+
+def test_placement_replicates_hot_experts_only():
+    from vates_b200.ep import hot_experts, placement
+    counts = np.array([500, 5, 300, 4, 3, 2, 1, 0])
+    hot = hot_experts(counts, 0.2)
+    assert hot.tolist() == [True, False, True, False, False, False, False, False]
+    o0, res0 = placement(counts, 2, 0, share=0.2)
+    o1, res1 = placement(counts, 2, 1, share=0.2)
+    assert o0[0] == 0 and o1[0] == 1 and o0[2] == 0 and o1[2] == 1
+    cold = ~hot
+    assert np.array_equal(o0[cold], o1[cold])  # one owner per cold expert
+    assert (res0 | res1).all() and (res0 & res1).tolist() == hot.tolist()
+    # one rank: nothing to replicate
+    assert not hot_experts(counts, 0.0).any()
+    assert (placement(counts, 1, 0)[0] == 0).all()
+
+
 def test_lpt_placement_balances_and_is_deterministic():
     from vates_b200.ep import lpt_placement
     load = np.array([10, 9, 8, 1, 1, 1, 1, 1], np.float64)

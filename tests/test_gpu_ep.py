@@ -83,7 +83,7 @@ def test_prefill_phases_compose_to_the_single_call(cuda):
     assert torch.equal(out, ref)
 
 
-def _ep_rank(rank, world, port, q):
+def _ep_rank(rank, world, port, q, owner=None):
     import torch
     import torch.distributed as dist
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
@@ -95,7 +95,8 @@ def _ep_rank(rank, world, port, q):
                             device_id=torch.device("cuda", rank))
     try:
         from vates_b200.ep import CudaEpBackend, ep_prefill, lpt_placement
-        owner = lpt_placement(np.ones(E), world)
+        if owner is None:
+            owner = lpt_placement(np.ones(E), world)
         owned = [e for e in range(E) if owner[e] == rank]
         blk, x = _block(owned=owned)
         per = T // world
@@ -120,6 +121,38 @@ def test_ep_prefill_two_gpus_matches_one(cuda):
     q = ctx.Queue()
     port = 29700 + os.getpid() % 200
     procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    got = np.concatenate([res[0], res[1]])
+    assert np.array_equal(got, ref)
+
+
+def test_ep_prefill_two_gpus_with_replicated_hot_experts(cuda):
+    """Experts with many routes held by both GPUs (each computes them for
+    its own tokens), the rest owned by one GPU: bit-identical to one GPU."""
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from vates_b200.ep import placement
+    from vates_b200.prefill import moe_prefill
+    blk, x = _block()
+    dbg = {"inds": torch.empty((T, K), dtype=torch.int32, device="cuda"),
+           "scores": torch.empty((T, K), dtype=torch.bfloat16, device="cuda")}
+    ref = moe_prefill(blk, x, debug=dbg).float().cpu().numpy()
+    torch.cuda.synchronize()
+    counts = np.bincount(dbg["inds"].cpu().numpy().ravel(), minlength=E)
+    owners = [placement(counts, 2, r, share=1.0 / E)[0] for r in range(2)]
+    hot = (owners[0] == 0) & (owners[1] == 1)
+    assert hot.any() and (~hot).any()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29700 + (os.getpid() + 100) % 200
+    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, q, owners[r])) for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in range(2))

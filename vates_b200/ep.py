@@ -2,7 +2,9 @@
 
 The reference runs one device (``_expert_major_forward``, block.py:111-243);
 here each rank owns the experts ``e`` with ``owner[e] == rank`` and starts
-with its own slice of the tokens. One prefill step:
+with its own slice of the tokens (``owner`` is per rank: experts replicated
+on every rank map to the rank itself, see :func:`placement`). One prefill
+step:
 
 1. route the local tokens (router GEMM, top-k)                 ``vb_moe_route``
 2. all-reduce the route histogram: the reference's reduce groups
@@ -44,6 +46,33 @@ def lpt_placement(load: np.ndarray, world: int) -> np.ndarray:
         owner[e] = r
         acc[r] += load[e]
     return owner
+
+
+def hot_experts(counts: np.ndarray, share: float) -> np.ndarray:
+    """Experts that carry at least ``share`` of all routes (a bool mask).
+
+    Under skewed routing a handful of experts take most routes; sending
+    their token rows to one owner and their route rows back would move most
+    of the batch over NVLink and leave that owner with most of the work.
+    These experts are instead held by every rank, which computes them for
+    its own tokens (placement never changes a result: every route row is
+    computed the same way on any rank)."""
+    counts = np.asarray(counts, np.float64)
+    total = counts.sum()
+    if total <= 0 or share <= 0:
+        return np.zeros(counts.shape[0], bool)
+    return counts >= share * total
+
+
+def placement(counts: np.ndarray, world: int, rank: int, share: float = 0.02):
+    """This rank's ``owner[e]`` and resident-expert mask: experts of
+    :func:`hot_experts` map to ``rank`` (replicated on every rank), the
+    others to one rank each by :func:`lpt_placement` over their counts."""
+    counts = np.asarray(counts, np.float64)
+    hot = hot_experts(counts, share) if world > 1 else np.zeros(counts.shape[0], bool)
+    owner = lpt_placement(np.where(hot, 0.0, counts), world)
+    owner[hot] = rank
+    return owner, (owner == rank)
 
 
 def pack_reference(inds: np.ndarray, owner: np.ndarray, world: int):
