@@ -88,6 +88,7 @@ struct PfGemmParams {
   int gshift;       // log2(group / 64)
   int shared_e;     // expert index of the shared expert (-1: none)
   int n_valid;      // router: valid output columns
+  int tail_n;       // router: columns of the last N tile when narrower than PF_BN (0: none)
   const int32_t *mtiles;   // [n] (expert, row0, rows)
   const int32_t *n_mtiles;
   const int32_t *slot_of;  // expert -> pool slot
@@ -207,9 +208,13 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             if (MODE != PF_GATEUP) tc::tma_load_2d(stage_a(s), &tmA, &bar_tma[s], ks * PF_BK, row0);
             tc::tma_load_3d(stage_b(s), &tmHv, &bar_tma[s], ks * PF_BK, nt * PF_BN, hv);
           } else if (MODE == PF_ROUTER) {
-            tc::mbar_arrive_expect_tx(&bar_tma[s], PF_A_BYTES + PF_B_BYTES);
+            // The last N tile may be narrow (tmB1: box of tail_n rows).
+            const bool narrow = p.tail_n > 0 && nt == p.nt - 1;
+            tc::mbar_arrive_expect_tx(&bar_tma[s],
+                                      PF_A_BYTES + (narrow ? p.tail_n * PF_BK * 2 : PF_B_BYTES));
             tc::tma_load_2d(stage_a(s), &tmA, &bar_tma[s], ks * PF_BK, row0);
-            tc::tma_load_2d(stage_b(s), &tmB0, &bar_tma[s], ks * PF_BK, nt * PF_BN);
+            tc::tma_load_2d(stage_b(s), narrow ? &tmB1 : &tmB0, &bar_tma[s], ks * PF_BK,
+                            nt * PF_BN);
           } else if (MODE == PF_GATEUP) {
             tc::mbar_arrive_expect_tx(&bar_tma[s], PF_P_BYTES);  // A: the gather warps
             const CUtensorMap *g = sh ? &tmS0 : &tmB0;
@@ -274,13 +279,16 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      const uint32_t idesc = tc::idesc_bf16_f32(PF_BM, PF_BN);
+      const uint32_t idesc_full = tc::idesc_bf16_f32(PF_BM, PF_BN);
+      const uint32_t idesc_tail =
+          MODE == PF_ROUTER && p.tail_n > 0 ? tc::idesc_bf16_f32(PF_BM, p.tail_n) : idesc_full;
       int it = 0, tcount = 0;
       uint32_t deq_par = 0;  // per stage: parity of the next dequant phase
       bool issued = false;
       for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x, ++tcount) {
         const int acc = tcount & 1;
         const bool deq = DEQ && p.heavy_of[p.mtiles[3 * (t / p.nt)]] < 0;
+        const uint32_t idesc = (t % p.nt == p.nt - 1) ? idesc_tail : idesc_full;
         if (!tc::mbar_wait(&bar_acc_empty[acc], ((tcount >> 1) & 1) ^ 1, abort, PF_WAIT_NS)) {
           fail();
           break;
@@ -484,8 +492,9 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         }
       } else {
         const float sc = 1.f;
+        const int ncols = (p.tail_n > 0 && nt == p.nt - 1) ? p.tail_n : PF_BN;
 #pragma unroll 1
-        for (int c0 = 128 * hf; c0 < 128 * hf + 128; c0 += 32) {
+        for (int c0 = 128 * hf; c0 < 128 * hf + 128 && c0 < ncols; c0 += 32) {
           uint32_t v[32];
           tc::tmem_ld32(tb + c0, v);
           tc::tmem_ld_wait();
@@ -507,9 +516,10 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           }
           if (valid) {
             uint4 *dst = reinterpret_cast<uint4 *>(p.out + orow * p.out_ld + nt * PF_BN + c0);
+            const int nw = ncols - c0 >= 32 ? 4 : (ncols - c0) / 8;  // tail_n % 16 == 0
 #pragma unroll
             for (int w = 0; w < 4; ++w)
-              dst[w] = make_uint4(o[4 * w], o[4 * w + 1], o[4 * w + 2], o[4 * w + 3]);
+              if (w < nw) dst[w] = make_uint4(o[4 * w], o[4 * w + 1], o[4 * w + 2], o[4 * w + 3]);
           }
         }
       }
@@ -1130,7 +1140,9 @@ struct RouteLayout {
 };
 static RouteLayout route_layout(int T, int H, int E) {
   RouteLayout L;
-  L.NRP = ((E + 1) + PF_BN - 1) / PF_BN * PF_BN;
+  // Router rows (E experts + the shared gate): full PF_BN-row tiles, then a
+  // tail tile of the remaining rows rounded up to 16 (the MMA's N step).
+  L.NRP = (E + 1) / PF_BN * PF_BN + ((E + 1) % PF_BN + 15) / 16 * 16;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -1343,13 +1355,16 @@ static int run_route(const uint16_t *x, int T, int H, int E, int k, int norm_top
   pf_row_tiles_kernel<<<(nm + 255) / 256, 256, 0, s>>>(T, (int32_t *)W(L.mtiles),
                                                        (int32_t *)W(L.n_mtiles));
   if ((rc = check_launch("pf_row_tiles_kernel")) != VB_OK) return rc;
-  CUtensorMap ta, tb;
+  CUtensorMap ta, tb, tbn;
+  const int full = L.NRP / PF_BN, tail = L.NRP % PF_BN;
   if ((rc = make_map_bf16(&ta, x, T, H, PF_BM)) != VB_OK) return rc;
-  if ((rc = make_map_bf16(&tb, W(L.wr), L.NRP, H, PF_BN)) != VB_OK) return rc;
+  if ((rc = make_map_bf16(&tb, W(L.wr), L.NRP, H, full > 0 ? PF_BN : tail)) != VB_OK) return rc;
+  if ((rc = make_map_bf16(&tbn, W(L.wr), L.NRP, H, tail > 0 ? tail : PF_BN)) != VB_OK) return rc;
   PfGemmParams p{};
   p.mode = PF_ROUTER;
   p.K = H;
-  p.nt = L.NRP / PF_BN;
+  p.nt = full + (tail > 0 ? 1 : 0);
+  p.tail_n = tail;
   p.shared_e = -1;
   p.n_valid = E;
   p.mtiles = (const int32_t *)W(L.mtiles);
@@ -1358,7 +1373,7 @@ static int run_route(const uint16_t *x, int T, int H, int E, int k, int norm_top
   p.out_ld = L.NRP;
   p.bias = bias;
   p.status = status;
-  if ((rc = launch_gemm<PF_ROUTER>(ta, tb, tb, tb, tb, tb, tb, p, nm * p.nt, s)) != VB_OK) return rc;
+  if ((rc = launch_gemm<PF_ROUTER>(ta, tb, tbn, tb, tb, tb, tb, p, nm * p.nt, s)) != VB_OK) return rc;
   const int per = E <= 256 ? 8 : (E <= 512 ? 16 : 32);
   auto kfn = per == 8 ? pf_topk_kernel<8> : per == 16 ? pf_topk_kernel<16> : pf_topk_kernel<32>;
   const int tk_grid = std::max(1, std::min((T + 7) / 8, pf_sm_count() * 4));
