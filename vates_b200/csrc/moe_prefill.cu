@@ -70,15 +70,24 @@ constexpr uint64_t PF_WAIT_NS = 2000000000ull;       // 2 s per wait
 
 enum PfMode : int { PF_GATEUP = 0, PF_DOWN = 1, PF_ROUTER = 2 };
 
-// Gate/up (epilogue light, A rows gathered with two stages in flight) runs
-// four pipeline stages and stores h directly; the other modes run three and
-// stage their output for TMA stores.
-constexpr int pf_stages(int mode) { return mode == PF_GATEUP ? 4 : 3; }
-constexpr int pf_out_bytes(int mode) { return mode == PF_GATEUP ? 0 : 8 * 2 * PF_OUT_CHUNK; }
-constexpr int pf_smem(int mode) {
-  return pf_stages(mode) * PF_STAGE_BYTES + pf_out_bytes(mode) + 1024;  // + alignment slack
+// Shared memory per mode:
+//  gate/up: 4 stages of (A, B, packed codes); h rows stored directly;
+//  down:    4 stages of (A, B), the packed codes of dequantized tiles in a
+//           2-slot ring of their own, one 32x32 output staging chunk per
+//           epilogue warp (TMA stores);
+//  router:  3 stages of (A, B, -), two staging chunks per epilogue warp.
+constexpr int pf_stages(int mode) { return mode == PF_ROUTER ? 3 : 4; }
+constexpr bool pf_pring(int mode) { return mode == PF_DOWN; }
+constexpr int pf_stage_bytes(int mode) {
+  return pf_pring(mode) ? PF_A_BYTES + PF_B_BYTES : PF_STAGE_BYTES;
 }
-static_assert(pf_smem(PF_GATEUP) <= 232448 - 256 && pf_smem(PF_DOWN) <= 232448 - 256,
+constexpr int pf_out_bufs(int mode) { return mode == PF_GATEUP ? 0 : (mode == PF_DOWN ? 1 : 2); }
+constexpr int pf_smem(int mode) {
+  return pf_stages(mode) * pf_stage_bytes(mode) + (pf_pring(mode) ? 2 * PF_P_BYTES : 0) +
+         8 * pf_out_bufs(mode) * PF_OUT_CHUNK + 1024;  // + alignment slack
+}
+static_assert(pf_smem(PF_GATEUP) <= 232448 - 256 && pf_smem(PF_DOWN) <= 232448 - 256 &&
+                  pf_smem(PF_ROUTER) <= 232448 - 256,
               "pf_gemm_kernel shared memory");
 
 struct PfGemmParams {
@@ -139,6 +148,10 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
   constexpr int NS = pf_stages(MODE);
+  constexpr int SB = pf_stage_bytes(MODE);
+  constexpr bool PRING = pf_pring(MODE);
+  constexpr int NOUT = pf_out_bufs(MODE);
+  __shared__ __align__(8) uint64_t bar_pempty[2];  // down: code ring slots free
   __shared__ __align__(8) uint64_t bar_tma[PF_STAGES_MAX], bar_deq[PF_STAGES_MAX],
       bar_empty[PF_STAGES_MAX];
   __shared__ __align__(8) uint64_t bar_acc_full[2], bar_acc_empty[2], bar_final;
@@ -162,6 +175,8 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       tc::mbar_init(&bar_acc_empty[a], 8);
     }
     tc::mbar_init(&bar_final, 1);
+    tc::mbar_init(&bar_pempty[0], 8);
+    tc::mbar_init(&bar_pempty[1], 8);
     s_abort = 0;
     tc::fence_mbar_init();
   }
@@ -184,14 +199,17 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     s_abort = 1;
     flag_status(p.status, VB_STATUS_TIMEOUT);
   };
-  auto stage_a = [&](int s) { return smem + s * PF_STAGE_BYTES; };
-  auto stage_b = [&](int s) { return smem + s * PF_STAGE_BYTES + PF_A_BYTES; };
-  auto stage_p = [&](int s) { return smem + s * PF_STAGE_BYTES + PF_A_BYTES + PF_B_BYTES; };
+  auto stage_a = [&](int s) { return smem + s * SB; };
+  auto stage_b = [&](int s) { return smem + s * SB + PF_A_BYTES; };
+  // Packed codes of stage s (down: slot `slot` of the code ring).
+  auto stage_p = [&](int s, int slot) {
+    return PRING ? smem + NS * SB + slot * PF_P_BYTES : smem + s * SB + PF_A_BYTES + PF_B_BYTES;
+  };
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
-      int it = 0;
+      int it = 0, pq = 0;  // pq: dequantized down stages issued (code ring)
       for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
         const int mt = t / p.nt, nt = t % p.nt;
         const int e = p.mtiles[3 * mt], row0 = p.mtiles[3 * mt + 1];
@@ -219,14 +237,25 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             tc::mbar_arrive_expect_tx(&bar_tma[s], PF_P_BYTES);  // A: the gather warps
             const CUtensorMap *g = sh ? &tmS0 : &tmB0;
             const CUtensorMap *u = sh ? &tmS1 : &tmB1;
-            tc::tma_load_3d(stage_p(s), g, &bar_tma[s], ks * (PF_BK / 2), nt * 128, slot);
-            tc::tma_load_3d(stage_p(s) + PF_P_BYTES / 2, u, &bar_tma[s], ks * (PF_BK / 2),
+            tc::tma_load_3d(stage_p(s, 0), g, &bar_tma[s], ks * (PF_BK / 2), nt * 128, slot);
+            tc::tma_load_3d(stage_p(s, 0) + PF_P_BYTES / 2, u, &bar_tma[s], ks * (PF_BK / 2),
                             nt * 128, slot);
           } else {
+            // Down, dequantized tile: the codes go to the next ring slot once
+            // the dequantizing warps have read what it held.
+            int ps = 0;
+            if (PRING) {
+              ps = pq & 1;
+              if (!tc::mbar_wait(&bar_pempty[ps], ((pq >> 1) & 1) ^ 1, abort, PF_WAIT_NS)) {
+                fail();
+                break;
+              }
+              ++pq;
+            }
             tc::mbar_arrive_expect_tx(&bar_tma[s], PF_A_BYTES + PF_P_BYTES);
             tc::tma_load_2d(stage_a(s), &tmA, &bar_tma[s], ks * PF_BK, row0);
             const CUtensorMap *d = sh ? &tmS0 : &tmB0;
-            tc::tma_load_3d(stage_p(s), d, &bar_tma[s], ks * (PF_BK / 2), nt * PF_BN, slot);
+            tc::tma_load_3d(stage_p(s, ps), d, &bar_tma[s], ks * (PF_BK / 2), nt * PF_BN, slot);
           }
         }
       }
@@ -328,7 +357,7 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     // Thread r owns B row r: gate rows 0..127 and up rows 128..255 of the
     // N tile (gate/up), or down rows (down).
     const int r = tid - 128;
-    int it = 0;
+    int it = 0, pq = 0;  // pq: dequantized down stages consumed (code ring)
     for (int t = blockIdx.x; t < n_tiles && !*abort; t += gridDim.x) {
       const int mt = t / p.nt, nt = t % p.nt;
       const int e = p.mtiles[3 * mt];
@@ -370,8 +399,13 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int gi = ks >> p.gshift;
         const uint32_t sc = __ldg(sp + gi), bi = __ldg(bp + gi);
         if (!tc::mbar_wait(&bar_tma[s], ph, abort, PF_WAIT_NS)) { fail(); ok = false; break; }
-        const uint4 *src = reinterpret_cast<const uint4 *>(stage_p(s) + r * 32);
+        const int ps = PRING ? (pq++ & 1) : 0;
+        const uint4 *src = reinterpret_cast<const uint4 *>(stage_p(s, ps) + r * 32);
         const uint4 w0 = src[0], w1 = src[1];
+        if (PRING) {  // the ring slot may be refilled once every warp has its codes
+          __syncwarp();
+          if (lane == 0) tc::mbar_arrive(&bar_pempty[ps]);
+        }
         const uint32_t words[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
         const uint32_t s2 = sc | (sc << 16), b2 = bi | (bi << 16);
         uint8_t *dst = stage_b(s);
@@ -411,13 +445,17 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     // Chunks of 32 rows x 32 columns whose rows are all valid go out as one
     // TMA store from a swizzled staging buffer (two per warp, alternating);
     // the rows of a partial chunk are stored by their threads.
-    uint8_t *obuf = smem + NS * PF_STAGE_BYTES + (warp - 12) * 2 * PF_OUT_CHUNK;  // not gate/up
+    uint8_t *obuf = smem + NS * SB + (PRING ? 2 * PF_P_BYTES : 0) +
+                    (warp - 12) * NOUT * PF_OUT_CHUNK;  // not gate/up
     int nst = 0;
     auto store_chunk = [&](const uint32_t (&o)[16], bool full, bool valid, size_t orow,
                            int col) {
       if (full) {
-        uint8_t *b = obuf + (nst & 1) * PF_OUT_CHUNK;
-        if (lane == 0 && nst >= 2) tc::bulk_wait_read<1>();
+        uint8_t *b = obuf + (NOUT == 2 ? (nst & 1) : 0) * PF_OUT_CHUNK;
+        if (lane == 0 && nst >= NOUT) {
+          if (NOUT == 2) tc::bulk_wait_read<1>();
+          else tc::bulk_wait_read<0>();
+        }
         __syncwarp();
         const int sw = (lane >> 1) & 3;  // 64-byte swizzle: chunk c ^ ((row >> 1) & 3)
 #pragma unroll
