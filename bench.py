@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the vates_b200 hot path (one JSON line on rank 0).
 
-Default workload: MTP K=3 verify decode, T=4 tokens
+Default workload (the reference's MTP-verify configuration): MTP K=3 verify decode, T=4 tokens
 through 48 stacked Qwen3-Next sparse-MoE blocks (H=2048, I=512, 512 experts,
 top-10, MLX 4-bit g64 experts resolved through per-layer 192-slot tables into
 one packed HBM pool of 16.3 GB, shared expert). A step is the whole 48-layer

@@ -531,6 +531,21 @@ int vb_kv_prefill_attn(const uint16_t *q, const uint32_t *k_codes,
                        int32_t *status, vb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Affine dequantization (MLX mx.dequantize; the reference's per-element
+ * `qvalue`, native/ext/compute/fused_moe.cpp:131-145, and its inline form in
+ * mlx_streaming/core/moe/custom_kernel.py:268-285):
+ * out[r, c] = q * scale[r, c/group] + bias[r, c/group], q the c-th
+ * `bits`-wide field of row r's LSB-first uint32 bitstream (straddling fields
+ * continue in the next word). words [rows, cols*bits/32], scales/biases bf16
+ * [rows, cols/group]; out_bf16 != 0: bf16 [rows, cols] (the value rounded
+ * once, as fed to the tensor cores; 4-bit rows use the same device routine as
+ * the prefill GEMMs), 0: f32 [rows, cols]. bits 2..8. */
+int vb_dequantize(const uint32_t *words, const uint16_t *scales,
+                  const uint16_t *biases, int64_t rows, int32_t cols,
+                  int32_t group, int32_t bits, int32_t out_bf16, void *out,
+                  vb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Seeded synthetic data (bench and tests): fills `words` uint32 with a
  * counter hash of (seed, index) and bf16 scales uniform in [lo, hi) with
  * biases = -8*scale (MLX 4-bit affine weights as in the benchmark configs).
@@ -540,6 +555,16 @@ int vb_synth_fill_u32(uint32_t *words, int64_t n, uint64_t seed,
 int vb_synth_fill_scales(uint16_t *scales, uint16_t *biases, int64_t n,
                          uint64_t seed, float lo, float hi, float bias_mul,
                          vb_stream_t stream);
+/* The nine tensors of n experts in one launch: slot slots[i] (host array)
+ * gets expert seed seeds[i] (host array); every tensor holds the values that
+ * vb_synth_fill_u32 / vb_synth_fill_scales give it with the per-tensor seed
+ * mix(seed, 3*proj) for codes and mix(seed, 3*proj + 1) for scales, where
+ * mix(s, t) = z ^ (z >> 31), z = s*0x9E3779B97F4A7C15 + t*0xBF58476D1CE4E5B9
+ * + 0x94D049BB133111EB (mod 2^64). */
+int vb_synth_fill_pool(const VbQuantPool *pool, const int32_t *slots,
+                       const uint64_t *seeds, int32_t n, int32_t hidden,
+                       int32_t inter, int32_t bits, int32_t group, float lo,
+                       float hi, float bias_mul, vb_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -20,5 +20,5 @@ Parity pins:
   ``mlx_streaming/tests/test_expert_major_prefill.py:89-132``.
 - ``mlx_affine_quantize`` / quantized-matmul rounding points follow MLX's
   published source; no MLX run is available to pin them (parity against MLX
-  itself is unpinned for those codes; see the repository design notes).
+  itself is unpinned for those codes).
 """

@@ -103,8 +103,10 @@ def asym_quantized_sdpa(q, kq, vq, scale, group_size, k_bits, v_bits,
     Hkv, S = Kd.shape[1], Kd.shape[2]
     rep = Hq // Hkv
     qs = M.bf16(q * np.float32(scale)).reshape(Bn, Hkv, rep, L, D)
-    scores = np.einsum("bhrld,bhsd->bhrls", qs.astype(np.float64),
-                       Kd.astype(np.float64)).astype(np.float32)
+    # float64 products and sums (BLAS matmul), rounded once to float32
+    scores = np.matmul(qs.reshape(Bn, Hkv, rep * L, D).astype(np.float64),
+                       np.swapaxes(Kd.astype(np.float64), -1, -2))
+    scores = scores.astype(np.float32).reshape(Bn, Hkv, rep, L, S)
     scores = M.bf16(scores)
     if causal:
         qi = np.arange(S - L, S)[:, None]
@@ -112,8 +114,8 @@ def asym_quantized_sdpa(q, kq, vq, scale, group_size, k_bits, v_bits,
         mask = qi >= ki
         scores = np.where(mask, scores, np.float32(-3.3895313892515355e38))
     p = M.bf16(M.softmax_precise(scores))
-    out = np.einsum("bhrls,bhsd->bhrld", p.astype(np.float64),
-                    Vd.astype(np.float64)).astype(np.float32)
+    out = np.matmul(p.reshape(Bn, Hkv, rep * L, S).astype(np.float64), Vd.astype(np.float64))
+    out = out.astype(np.float32).reshape(Bn, Hkv, rep, L, D)
     return M.bf16(out).reshape(Bn, Hq, L, D)
 
 

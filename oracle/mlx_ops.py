@@ -50,6 +50,9 @@ def bf16_ulp(a) -> np.ndarray:
 # ----------------------------------------------------------------------------
 
 
+_CHUNK_ROWS = 8192  # rows per pass of the bit-matrix pack/unpack (bounds host memory)
+
+
 def packed_words(dim: int, bits: int) -> int:
     """uint32 words per packed row: ``dim*bits//32`` (quant_kv.py:75-77)."""
     return dim * bits // 32
@@ -64,11 +67,16 @@ def pack_codes(codes: np.ndarray, bits: int) -> np.ndarray:
     custom_kernel.py:170-185). This is the byte stream MLX's quantize writes
     (power-of-two widths as uint32 words, 3/5/6-bit widths as 3-byte packs).
     """
-    codes = np.asarray(codes, dtype=np.uint64)
+    codes = np.asarray(codes)
     *lead, dim = codes.shape
     assert (dim * bits) % 32 == 0
     nbits = dim * bits
     flat = codes.reshape(-1, dim)
+    if flat.shape[0] > _CHUNK_ROWS:
+        parts = [pack_codes(flat[i:i + _CHUNK_ROWS], bits)
+                 for i in range(0, flat.shape[0], _CHUNK_ROWS)]
+        return np.concatenate(parts).reshape(*lead, nbits // 32)
+    flat = flat.astype(np.uint64)
     # Expand to a bit matrix [rows, dim*bits], LSB first per field.
     shifts = np.arange(bits, dtype=np.uint64)
     bitmat = ((flat[:, :, None] >> shifts[None, None, :]) & 1).astype(np.uint8)
@@ -90,6 +98,10 @@ def unpack_codes(words: np.ndarray, dim: int, bits: int) -> np.ndarray:
         codes = (words[..., None] >> shifts) & np.uint32((1 << bits) - 1)
         return codes.reshape(*lead, dim).astype(np.uint8)
     flat = words.reshape(-1, nw)
+    if flat.shape[0] > _CHUNK_ROWS:
+        parts = [unpack_codes(flat[i:i + _CHUNK_ROWS], dim, bits)
+                 for i in range(0, flat.shape[0], _CHUNK_ROWS)]
+        return np.concatenate(parts).reshape(*lead, dim)
     bytes_ = flat.view(np.uint8).reshape(flat.shape[0], nw * 4)
     bitmat = np.unpackbits(bytes_, axis=-1, bitorder="little")
     bitmat = bitmat.reshape(flat.shape[0], dim, bits).astype(np.uint32)

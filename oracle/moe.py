@@ -308,3 +308,43 @@ def shared_prefill(x, shared, wsg, hidden, inter, group, bits):
     ysh = expert_mlp_prefill(x, wg, wu, wd)
     sg = M.bf16(M.matvec_f32(np.asarray(wsg, np.float32)[None, :], x))
     return M.bf16(M.bf16(M.sigmoid_f32(sg)) * ysh)
+
+
+def expert_major_rows(x_rows, rows_inds, rows_scores, counts, pool_of_expert, hidden,
+                      inter, group, bits, layer_cap: int = 512,
+                      max_assignments: int = 32768, abs_sum: bool = False):
+    """:func:`expert_major_forward` evaluated for a subset of the batch's tokens.
+
+    ``counts`` is the route histogram of the WHOLE batch (after dropping
+    non-resident routes), which fixes the reduce groups (block.py:154-172);
+    ``x_rows``/``rows_inds``/``rows_scores`` are the selected tokens. A token's
+    output depends only on its own routes and on the groups: its weighted
+    rows are added to a bf16 zero row group by group, and inside a group in
+    ascending flat route position, i.e. ascending route rank ``j``
+    (custom_kernel.py:63-77 via block.py:206-224), rounding after every add.
+    This equals the corresponding rows of :func:`expert_major_forward` over
+    the whole batch at a cost proportional to the selected tokens.
+    """
+    x = M.bf16(np.asarray(x_rows, np.float32))
+    n, k = rows_inds.shape
+    group_of = np.full(len(counts), -1, np.int64)
+    for gi, (experts, _) in enumerate(expert_groups(counts, layer_cap, max_assignments)):
+        group_of[experts] = gi
+    ys = np.zeros((n, k, hidden), np.float32)
+    ids = rows_inds.astype(np.int64)
+    for e in np.unique(ids):
+        sel = np.nonzero(ids == e)
+        pool, slot = pool_of_expert(int(e))
+        wg, wu, wd = dequant_expert(pool, slot, hidden, inter, group, bits, to_bf16=True)
+        ys[sel] = expert_mlp_prefill(x[sel[0]], wg, wu, wd)
+    weighted = M.bf16(ys * np.asarray(rows_scores, np.float32)[:, :, None])
+    out = np.zeros((n, hidden), np.float32)
+    absacc = np.zeros((n, hidden), np.float32)
+    for t in range(n):
+        order = sorted(range(k), key=lambda j: (group_of[ids[t, j]], j))
+        for j in order:
+            if group_of[ids[t, j]] < 0:
+                continue  # a route outside every group (not resident) adds nothing
+            out[t] = M.bf16(out[t] + weighted[t, j])
+            absacc[t] += np.abs(weighted[t, j])
+    return (out, absacc) if abs_sum else out

@@ -37,8 +37,8 @@ def bf16_steps(a, b):
 
 def bf16_close(got, ref, atol=2e-2, mean_rel=5e-3, max_ulps=2, frac_beyond=5e-3, scale=None,
                what=""):
-    """The parity bar for bf16 outputs (north star: max-abs 2e-2, mean-rel
-    5e-3 in bf16).
+    """The parity bar for bf16 outputs (max-abs 2e-2, mean-rel 5e-3 in
+    bf16).
 
     The MLX dtype chain rounds to bf16 after every op, so a float32
     summation-order difference can flip an intermediate rounding by one bf16

@@ -11,7 +11,7 @@ minimal numpy stand-in for ``mlx.core``/``mlx.utils``/``mlx_lm`` and runs the
 reference's own rotation builder. The outputs pin :mod:`oracle.isoquant`
 bit-exactly. The route-reduce fixture records the hand-computed expectation of
 ``mlx_streaming/tests/test_expert_major_prefill.py:89-103`` and the packing
-widths of ``mlx_streaming/tests/test_kv_quant.py:263-271``.
+widths of ``mlx_streaming/tests/test_kv_quant.py:64-72``.
 
 Nothing at test time reads the reference: the tests only read the files
 written here.
@@ -74,7 +74,7 @@ def main(ref_root: str) -> None:
     with open(os.path.join(HERE, "route_reduce_rank_order.json"), "w") as f:
         json.dump(fixture, f, indent=1)
     widths = {
-        "source": "mlx_streaming/tests/test_kv_quant.py:263-271",
+        "source": "mlx_streaming/tests/test_kv_quant.py:64-72",
         "head_dim": 256, "k_bits": 4, "v_bits": 3,
         "k_words": mod._packed_words(256, 4), "v_words": mod._packed_words(256, 3),
     }
@@ -84,4 +84,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit(f"usage: python {sys.argv[0]} <path to the reference checkout>")
+    main(sys.argv[1])

@@ -61,3 +61,25 @@ def routes_agree(gpu_inds, ref_probs, ref_inds, k):
         kth = np.sort(p)[::-1][k - 1]
         ok.append(all(p[e] >= kth for e in g))
     return np.array(ok)
+
+
+def oracle_route_and_host(blk, x, gpu_inds, k, norm_eps=0.0):
+    """The oracle's own routing of ``x`` through ``blk``'s router weights
+    (block.py:253, 321-329; rmsnorm first when ``norm_eps > 0``), and a host
+    copy of the layer holding the union of the GPU's and the oracle's routed
+    experts, so that the oracle can evaluate either routing.
+
+    Returns ``(host, probs, inds, scores)``; ``host["full_table"]`` is the
+    block's slot table."""
+    from oracle import moe as OM
+    from vates_b200.synth import layer_to_host
+    xb = M.bf16(np.asarray(x, np.float32))
+    if norm_eps > 0:
+        xb = OM.rmsnorm_unit(xb, norm_eps)
+    wr = blk.router_w.float().cpu().numpy()
+    lb = None if blk.router_bias is None else blk.router_bias.cpu().numpy()
+    _, probs, inds, scores = OM.router(xb, wr, k, blk.norm_topk_prob, lb)
+    experts = np.union1d(np.asarray(gpu_inds).reshape(-1), inds.reshape(-1))
+    host = layer_to_host(blk, experts)
+    host["full_table"] = blk.slot_table.cpu().numpy()
+    return host, probs, inds, scores

@@ -167,7 +167,7 @@ def test_kv_quant_append_codes_bit_exact(cuda, dim, kbits, vbits):
         assert np.array_equal(to_np(got[0]).view(np.uint32), w)
         assert np.array_equal(to_np(got[1].view(torch.int16)).view(np.uint16), s)
         assert np.array_equal(to_np(got[2].view(torch.int16)).view(np.uint16), b)
-    # growth across the 256-step boundary (test_kv_quant.py:280-291)
+    # growth across the 256-step boundary (test_kv_quant.py:81-92)
     for _ in range(5):
         kq, vq = cache.update_and_fetch(bf16_tensor(k[:, :, :1]), bf16_tensor(v[:, :, :1]))
     assert cache.offset == 305 and kq[0].shape[-2] == 305
@@ -212,7 +212,7 @@ def test_kv_attention_vs_oracle(cuda, L, S, causal):
                                                    to_np(vq[2].view(torch.int16)).view(np.uint16)))
     ref = IQ.attention_layer_decode(q, kq_np, vq_np, Rv.numpy(), D ** -0.5, causal=causal)
     bf16_close(to_np(out), ref, what="kv attention")
-    # mechanism check against dense attention (test_kv_quant.py:339-356): cos > 0.9
+    # mechanism check against dense attention (test_kv_quant.py:140-157): cos > 0.9
     if not causal:
         kd = k.reshape(1, nkv, 1, S, D)
         vd = v.reshape(1, nkv, 1, S, D)
@@ -263,3 +263,114 @@ def test_prefill_attention_vs_oracle(cuda, L, S, causal, nq, nkv):
     again = asym_quantized_sdpa(bf16_tensor(q), kq, vq, D ** -0.5, "causal" if causal else None,
                                 64, 4, 3, rv=so4_blocks(Rv))
     assert torch.equal(again.view(torch.int16), out.view(torch.int16))
+
+
+# ------------------------------------------------------------------ dequantized weights
+
+@pytest.mark.parametrize("bits,group,gaussian", [(4, 64, False), (4, 64, True), (4, 128, True),
+                                                 (3, 64, True), (2, 32, True), (5, 64, True),
+                                                 (6, 64, False), (8, 128, True)])
+def test_dequantize_bit_exact(cuda, bits, group, gaussian):
+    """Dequantized weights bit for bit (fused_moe.cpp:131-145 qvalue): the
+    float32 value q*s + b and its bf16 rounding, against the oracle, for
+    benchmark-format weights (uniform codes, bias -8*scale) and for weights
+    quantized with the MLX rule. The 4-bit bf16 output comes from the device
+    routine that feeds every prefill GEMM."""
+    import ctypes as C
+    import torch
+    from vates_b200._lib import check, lib
+    from vates_b200.pool import stream_handle
+    rng = np.random.default_rng(bits * 1000 + group)
+    rows, cols = 96, 512
+    if gaussian:
+        w = M.bf16((rng.standard_normal((rows, cols)) * 0.1).astype(np.float32))
+        q, s, b = M.mlx_affine_quantize(w, group, bits)
+    else:
+        q = rng.integers(0, 2 ** 32, size=(rows, cols * bits // 32), dtype=np.uint64).astype(np.uint32)
+        s = M.bf16_bits(rng.uniform(0.002, 0.02, (rows, cols // group)).astype(np.float32))
+        b = M.bf16_bits(M.bf16_from_bits(s) * np.float32(-8))
+    dq = torch.from_numpy(q.view(np.int32)).cuda()
+    ds = torch.from_numpy(s.view(np.int16)).cuda()
+    db = torch.from_numpy(b.view(np.int16)).cuda()
+    o32 = torch.empty((rows, cols), dtype=torch.float32, device="cuda")
+    o16 = torch.empty((rows, cols), dtype=torch.int16, device="cuda")
+    for out, is_bf16 in ((o32, 0), (o16, 1)):
+        check(lib.vb_dequantize(dq.data_ptr(), ds.data_ptr(), db.data_ptr(), rows, cols, group,
+                                bits, is_bf16, out.data_ptr(), stream_handle()), "vb_dequantize")
+    torch.cuda.synchronize()
+    ref = M.dequantize(q, s, b, cols, group, bits)
+    assert np.array_equal(o32.cpu().numpy().view(np.uint32), ref.view(np.uint32))
+    ref16 = M.bf16_bits(M.dequantize_bf16(q, s, b, cols, group, bits))
+    assert np.array_equal(o16.cpu().numpy().view(np.uint16), ref16)
+
+
+def test_dequantize_synthetic_expert_bit_exact(cuda):
+    """The benchmark pool's own expert bytes (counter-hash codes, 2048-wide
+    rows) dequantized on the device equal the oracle's bf16 weights."""
+    import torch
+    from vates_b200._lib import check, lib
+    from vates_b200.pool import QuantPool, expert_seed, stream_handle
+    pool = QuantPool.empty_blob(2, 2048, 512, 4, 64)
+    pool.fill_synthetic_many([0, 1], [expert_seed(0, 0, 17), expert_seed(0, 0, 401)])
+    for slot in (0, 1):
+        t = pool.slot_tensors(slot)
+        host = pool.to_numpy_slot(slot)
+        for proj, cols in (("gate", 2048), ("up", 2048), ("down", 512)):
+            rows = t[f"{proj}_w"].shape[0]
+            out = torch.empty((rows, cols), dtype=torch.int16, device="cuda")
+            check(lib.vb_dequantize(t[f"{proj}_w"].data_ptr(), t[f"{proj}_s"].data_ptr(),
+                                    t[f"{proj}_b"].data_ptr(), rows, cols, 64, 4, 1,
+                                    out.data_ptr(), stream_handle()), "vb_dequantize")
+            ref = M.bf16_bits(M.dequantize_bf16(host[f"{proj}_w"][0], host[f"{proj}_s"][0],
+                                                host[f"{proj}_b"][0], cols, 64, 4))
+            assert np.array_equal(out.cpu().numpy().view(np.uint16), ref), (slot, proj)
+
+
+def test_synth_pool_one_launch_matches_per_tensor_fill(cuda):
+    import torch
+    from vates_b200.pool import QuantPool, expert_seed
+    a = QuantPool.empty_blob(5, 2048, 512, 4, 64)
+    b = QuantPool.empty_blob(5, 2048, 512, 4, 64)
+    seeds = [expert_seed(3, 2, e) for e in (0, 9, 100, 511, 100_000)]
+    for s, sd in enumerate(seeds):
+        a.fill_synthetic(s, sd)
+    b.fill_synthetic_many(range(5), seeds)
+    torch.cuda.synchronize()
+    assert torch.equal(a.blob, b.blob)
+
+
+@pytest.mark.parametrize("L", [1, 4])
+def test_kv_attention_128k_vs_oracle(cuda, L):
+    """The benchmark's attention layer: 131,072 keys, 16 query / 2 kv heads,
+    head_dim 256, K4/V3 after the seeded SO(4) rotations (K seed 0, V seed
+    1), one query (L=1) and the four causal MTP-verify queries (L=4): packed
+    codes bit-exact against the oracle's quantize of the oracle's rotation,
+    output against the oracle's MLX chain with the inverse V rotation."""
+    import torch
+    from vates_b200.quant_kv import (AsymmetricQuantizedKVCache, asym_quantized_sdpa,
+                                     build_block_so4, so4_blocks)
+    S, nq, nkv, D = 131072, 16, 2, 256
+    rng = np.random.default_rng(131072 + L)
+    k = M.bf16(rng.standard_normal((1, nkv, S, D), dtype=np.float32))
+    v = M.bf16(rng.standard_normal((1, nkv, S, D), dtype=np.float32))
+    q = M.bf16(rng.standard_normal((1, nq, L, D), dtype=np.float32))
+    Rk, Rv = build_block_so4(D, 0), build_block_so4(D, 1)
+    cache = AsymmetricQuantizedKVCache(64, 4, 3)
+    kq, vq = cache.update_and_fetch(bf16_tensor(k), bf16_tensor(v), rk=so4_blocks(Rk),
+                                    rv=so4_blocks(Rv))
+    qr = IQ.rotate_last(q, Rk.numpy())
+    out = asym_quantized_sdpa(bf16_tensor(qr), kq, vq, D ** -0.5, "causal" if L > 1 else None,
+                              64, 4, 3, rv=so4_blocks(Rv))
+    torch.cuda.synchronize()
+    packs = []
+    for got, src, R, bits in ((kq, k, Rk, 4), (vq, v, Rv, 3)):
+        w, s, b = IQ.kv_quantize(IQ.rotate_last(src, R.numpy()), 64, bits)
+        gw = to_np(got[0]).view(np.uint32)
+        gs = to_np(got[1].view(torch.int16)).view(np.uint16)
+        gb = to_np(got[2].view(torch.int16)).view(np.uint16)
+        assert np.array_equal(gw, w) and np.array_equal(gs, s) and np.array_equal(gb, b)
+        packs.append((np.ascontiguousarray(gw), np.ascontiguousarray(gs), np.ascontiguousarray(gb)))
+    del k, v
+    ref = IQ.attention_layer_decode(qr, packs[0], packs[1], Rv.numpy(), D ** -0.5,
+                                    causal=L > 1)
+    bf16_close(to_np(out), ref, what=f"128K-key attention, L={L}")

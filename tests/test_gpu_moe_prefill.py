@@ -130,3 +130,62 @@ def test_prefill_missing_expert_flags_status(cuda):
     got, ref, scale, st = _case(128, 1024, 256, 16, 4, seed=5, missing=(0, 1, 2, 3, 4, 5, 6, 7))
     assert st & 1  # VB_STATUS_MISS
     bf16_close(got, ref, scale=scale, max_ulps=3, what="prefill output with skipped routes")
+
+
+def test_prefill_config2_full_size(cuda):
+    """The benchmark's prefill layer itself: 32,768 tokens, 512 experts,
+    top-10 with the Zipf(1.1) router bias (49 experts above 384 rows, 48 of
+    them pre-dequantized, 10+ reduce groups). Every token's routes against
+    the oracle's own routing (up to bf16 ties) and its scores bit for bit
+    from the GPU's logits; the block output of a seeded sample of 512 tokens
+    (the tokens with the most light-expert routes among them) against the
+    oracle's grouped, canonical-order reduce over the whole batch's groups."""
+    import torch
+    from vates_b200.prefill import moe_prefill
+    from vates_b200.synth import config2, layer_to_host
+    blk, x = config2(seed=2)
+    T, k, E, H, I = 32768, 10, 512, 2048, 512
+    dbg = {"inds": torch.empty((T, k), dtype=torch.int32, device="cuda"),
+           "scores": torch.empty((T, k), dtype=torch.bfloat16, device="cuda"),
+           "logits": torch.empty((T, E), dtype=torch.bfloat16, device="cuda")}
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = moe_prefill(blk, x, debug=dbg, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    xr = to_np(x)
+    wr = blk.router_w.float().cpu().numpy()
+    lb = blk.router_bias.cpu().numpy()
+    g_inds, g_scores, g_logits = to_np(dbg["inds"]), to_np(dbg["scores"]), to_np(dbg["logits"])
+    r_logits, probs, r_inds, _ = OM.router(xr, wr, k, True, logit_bias=lb)
+    assert routes_agree(g_inds, probs, r_inds, k).all(), "top-k differs beyond bf16 ties"
+    dot_abs = np.abs(xr) @ np.abs(wr).T
+    tol = np.maximum(M.bf16_ulp(np.abs(r_logits)), dot_abs * np.float32(2.0 ** -16))
+    assert (np.abs(g_logits - r_logits) <= tol).all(), "router logits"
+    del dot_abs, tol
+    f_probs, f_inds, f_scores = OM.route_from_logits(g_logits, k, True)
+    assert routes_agree(g_inds, f_probs, f_inds, k).all(), "top-k on the GPU logits"
+    gi, fi = np.sort(g_inds, 1), np.sort(f_inds, 1)
+    same = (gi == fi).all(1)
+    assert same.mean() > 0.99
+    go = np.argsort(g_inds, 1)
+    fo = np.argsort(f_inds, 1)
+    gs = np.take_along_axis(g_scores, go, 1)[same]
+    fs = np.take_along_axis(f_scores, fo, 1)[same]
+    assert np.array_equal(gs, fs), "route scores"
+    counts = np.bincount(g_inds.reshape(-1), minlength=E)
+    assert (counts >= 384).sum() >= 48 and len(OM.expert_groups(counts, E)) >= 10
+    heavy = counts >= 384
+    rng = np.random.default_rng(2024)
+    light_routes = (~heavy[g_inds]).sum(1)
+    sample = np.unique(np.concatenate([rng.choice(T, 448, replace=False),
+                                       np.argsort(-light_routes, kind="stable")[:64]]))
+    host = layer_to_host(blk, np.unique(g_inds[sample]))
+    routed, absacc = OM.expert_major_rows(
+        xr[sample], g_inds[sample], g_scores[sample], counts,
+        lambda e: (host["pool"], int(host["table"][e])), H, I, 64, 4, layer_cap=E, abs_sum=True)
+    sh_term = OM.shared_prefill(xr[sample], host["shared"], host["wsg"], H, I, 64, 4)
+    ref = M.bf16(routed + sh_term)
+    scale = np.maximum(absacc, np.abs(sh_term))
+    got = to_np(out)
+    bf16_close(got[sample], ref, scale=scale, max_ulps=3, what="config-2 prefill sample")
+    assert np.isfinite(got).all()

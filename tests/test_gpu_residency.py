@@ -6,7 +6,9 @@ pool."""
 import numpy as np
 import pytest
 
-from helpers import KEYS, bf16_tensor, pool_to_torch, random_pool_np
+from conftest import bf16_close, block_scale
+from helpers import KEYS, bf16_tensor, pool_to_torch, random_pool_np, routes_agree, to_np
+from oracle import moe as OM
 from oracle.residency import ResidencyOracle
 
 pytestmark = pytest.mark.gpu
@@ -228,9 +230,13 @@ def test_mtp_moe_matches_full_pool(cuda, T, source):
     rng = np.random.default_rng(20 + T)
     pool_np = random_pool_np(rng, E, H, I, BITS, G)
     blobs = _blobs_np(pool_np, E)
-    sh = QuantPool.from_tensors(pool_to_torch(random_pool_np(rng, 1, H, I, BITS, G)), H, I, BITS, G)
+    sh_np = random_pool_np(rng, 1, H, I, BITS, G)
+    sh = QuantPool.from_tensors(pool_to_torch(sh_np), H, I, BITS, G)
     wsg = bf16_tensor(rng.standard_normal(H).astype(np.float32) * 0.02)
     wr = bf16_tensor(rng.standard_normal((E, H)).astype(np.float32) * 0.05)
+    layer = {"wr": to_np(wr), "wsg": to_np(wsg), "table": np.arange(E, dtype=np.int32),
+             "pool": pool_np, "shared": sh_np, "hidden": H, "inter": I, "group": G,
+             "bits": BITS}
     full = MoeBlock(wr, make_table(E, {e: e for e in range(E)}),
                     QuantPool.from_tensors(pool_to_torch(pool_np), H, I, BITS, G), sh, wsg, top_k=k)
     if source == "device":
@@ -245,4 +251,17 @@ def test_mtp_moe_matches_full_pool(cuda, T, source):
         want = torch.cat([full.decode(x[0, i:i + 8]) for i in range(0, T, 8)])
         torch.cuda.synchronize()
         assert torch.equal(got[0].view(torch.int16), want.view(torch.int16)), f"step {step}"
+        # against the oracle (StreamingMTPMoE.__call__, qwen3_next_mtp.py:114-137)
+        # with its own routing: route sets agree up to bf16 ties, and every
+        # token whose set is the oracle's matches its output
+        for i in range(0, T, 8):
+            n = min(8, T - i)
+            g_inds = to_np(mtp._debug[n]["inds"])
+            ref = OM.moe_block_decode(to_np(x[0, i:i + n]), layer, k=k)
+            assert routes_agree(g_inds, ref["probs"], ref["inds"], k).all(), f"step {step}"
+            same = np.array([set(a) == set(b) for a, b in zip(g_inds.tolist(),
+                                                              ref["inds"].tolist())])
+            if same.any():
+                bf16_close(to_np(got[0, i:i + n])[same], ref["out"][same],
+                           scale=block_scale(ref)[same], what=f"MTP MoE step {step} vs oracle")
     assert mtp.pool.misses > 0

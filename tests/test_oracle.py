@@ -220,3 +220,24 @@ def test_expert_major_matches_token_major_weighted_sum():
     expected = np.array([[sum((v + e + 1) * s for e, s in zip(r, sc)) for v in row]
                          for row, r, sc in zip(x, inds, scores)], np.float32)
     assert np.allclose(out, expected, atol=1e-6)
+
+
+def test_expert_major_rows_equal_whole_batch_rows():
+    """The per-token restatement (used at the 32K-token size) reproduces the
+    whole-batch reduce bit for bit on the selected tokens, with several reduce
+    groups per layer."""
+    from helpers import random_pool_np
+    rng = np.random.default_rng(4)
+    T, H, I, E, k = 96, 128, 64, 12, 4
+    pool = random_pool_np(rng, E, H, I, 4, 64)
+    x = M.bf16(rng.standard_normal((T, H)).astype(np.float32))
+    inds = np.stack([rng.choice(E, k, replace=False) for _ in range(T)]).astype(np.int32)
+    scores = M.bf16(rng.uniform(0.05, 0.3, (T, k)).astype(np.float32))
+    full = OM.expert_major_forward(x, inds, scores, lambda e: (pool, e), H, I, 64, 4,
+                                   layer_cap=3, max_assignments=40)
+    sel = np.array([0, 5, 17, 42, 95])
+    counts = np.bincount(inds.reshape(-1), minlength=E)
+    rows = OM.expert_major_rows(x[sel], inds[sel], scores[sel], counts, lambda e: (pool, e),
+                                H, I, 64, 4, layer_cap=3, max_assignments=40)
+    assert len(OM.expert_groups(counts, 3, 40)) > 3
+    assert np.array_equal(rows, full[sel])

@@ -149,7 +149,10 @@ _SIGNATURES = {
     "vb_kv_prefill_attn": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32,
                                   _I32, _I32, _I32, _I32, _I32, _I32, C.c_float, _I32, _P, _P,
                                   _P]),
+    "vb_dequantize": (_I32, [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P]),
     "vb_synth_fill_u32": (_I32, [_P, _I64, C.c_uint64, _P]),
+    "vb_synth_fill_pool": (_I32, [C.POINTER(VbQuantPool), _P, _P, _I32, _I32, _I32, _I32,
+                                  _I32, C.c_float, C.c_float, C.c_float, _P]),
     "vb_synth_fill_scales": (_I32, [_P, _P, _I64, C.c_uint64, C.c_float, C.c_float,
                                     C.c_float, _P]),
 }

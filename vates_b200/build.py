@@ -28,6 +28,7 @@ SOURCES = [
     "moe_prefill.cu",
     "residency.cu",
     "kv_prefill_attn.cu",
+    "dequant.cu",
 ]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

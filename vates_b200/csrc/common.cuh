@@ -140,6 +140,31 @@ __device__ __forceinline__ void nib_pairs4(uint32_t w, uint32_t (&p)[4]) {
   p[3] = lop_and_or(w >> 12, M, O);
 }
 
+__device__ __forceinline__ uint32_t bf16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Dequantized bf16 weights of one word of 4-bit codes (MLX affine format,
+// fused_moe.cpp:131-145 qvalue): o[i] holds columns i (low half) and i+4
+// (high half) as bf16(q*s + b). (128 + q) - 128 is exact and q*s is exact, so
+// the one rounding of fma.rn.bf16x2 gives the float32 value q*s + b rounded
+// to bf16 whenever that float32 sum is exact (always for the bias range of a
+// quantized group). s2/b2 hold the group's bf16 scale/bias in both halves.
+// Every bf16 weight operand of the prefill GEMMs comes from here.
+__device__ __forceinline__ void dequant4_bf16x2(uint32_t w, uint32_t s2, uint32_t b2,
+                                                uint32_t (&o)[4]) {
+  uint32_t pr[4];
+  nib_pairs4(w, pr);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t q;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(pr[i]), "r"(0x43004300u));
+    o[i] = bf16x2_fma(q, s2, b2);
+  }
+}
+
 // Programmatic dependent launch controls (no-ops without the launch
 // attribute).
 __device__ __forceinline__ void pdl_wait() {

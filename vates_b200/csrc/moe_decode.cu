@@ -1311,7 +1311,14 @@ size_t vb_moe_decode_workspace_size(int32_t tokens, int32_t hidden,
   return decode_layout(tokens, hidden, inter, num_experts, top_k).total;
 }
 
-int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
+}  // extern "C"
+
+namespace {
+// vb_moe_decode after its argument checks; with clear_bytes > 0 the first
+// clear_bytes of the workspace are zeroed on the stream right before the
+// launch, once every check has passed (a rejected call touches neither the
+// device nor the stream).
+int moe_decode_impl(const VbMoeDecodeArgs *a, vb_stream_t stream, size_t clear_bytes) {
   VB_REQUIRE(a, "vb_moe_decode: null args");
   const int T = a->tokens, H = a->hidden, I = a->inter, E = a->num_experts,
             k = a->top_k;
@@ -1368,6 +1375,12 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
                      err != cudaSuccess ? cudaGetErrorString(err) : "occupancy 0");
 
   cudaStream_t s = as_stream(stream);
+  if (clear_bytes > 0) {
+    err = cudaMemsetAsync(a->workspace, 0, clear_bytes, s);
+    if (err != cudaSuccess)
+      return set_error(VB_ERR_CUDA, "vb_moe_decode_noalloc: clearing scratch: %s",
+                       cudaGetErrorString(err));
+  }
   cudaEvent_t *ev = a->timing_events ? (cudaEvent_t *)a->timing_events : nullptr;
   const bool pdl = ev == nullptr;  // event records would break the PDL chain
   if (ev) cudaEventRecord(ev[0], s);
@@ -1375,6 +1388,13 @@ int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_layer_kernel: %s", cudaGetErrorString(err));
   if (ev) cudaEventRecord(ev[1], s);
   return VB_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int vb_moe_decode(const VbMoeDecodeArgs *a, vb_stream_t stream) {
+  return moe_decode_impl(a, stream, 0);
 }
 
 int vb_moe_decode_noalloc(const VbMoeDecodeArgs *a, vb_stream_t stream) {
@@ -1390,17 +1410,15 @@ int vb_moe_decode_noalloc(const VbMoeDecodeArgs *a, vb_stream_t stream) {
   void *scratch = nullptr;
   const int rc = noalloc_scratch(&scratch);
   if (rc != VB_OK) return rc;
-  // The array keeps the previous call's contents: zero the words the kernel
+  // The array keeps the previous call's contents: the words the kernel
   // expects at zero (grid barrier, shared gates, entry counters, row-block
-  // tickets) before this call's kernel, in stream order.
+  // tickets) are zeroed in stream order before this call's kernel, after
+  // every argument check has passed.
   const DecodeLayout L = decode_layout(a->tokens, a->hidden, a->inter, a->num_experts, a->top_k);
-  const cudaError_t e = cudaMemsetAsync(scratch, 0, L.zero_end, as_stream(stream));
-  if (e != cudaSuccess)
-    return set_error(VB_ERR_CUDA, "vb_moe_decode_noalloc: clearing scratch: %s", cudaGetErrorString(e));
   VbMoeDecodeArgs b = *a;
   b.workspace = scratch;
   b.workspace_bytes = VB_MOE_DECODE_NOALLOC_SCRATCH_BYTES;
-  return vb_moe_decode(&b, stream);
+  return moe_decode_impl(&b, stream, L.zero_end);
 }
 
 }  // extern "C"

@@ -132,11 +132,6 @@ __device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
   return r;
 }
 
-__device__ __forceinline__ uint32_t bf16x2_fma(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t d;
-  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-  return d;
-}
 
 template <int MODE>
 __global__ void __launch_bounds__(PF_THREADS, 1)
@@ -411,16 +406,8 @@ pf_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         uint8_t *dst = stage_b(s);
 #pragma unroll
         for (int w = 0; w < 8; ++w) {
-          uint32_t pr[4];
-          nib_pairs4(words[w], pr);
           uint32_t o[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            // (128 + q) - 128 is exact; q*s + b is rounded once.
-            uint32_t q;
-            asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(pr[i]), "r"(0x43004300u));
-            o[i] = bf16x2_fma(q, s2, b2);
-          }
+          dequant4_bf16x2(words[w], s2, b2, o);
           uint4 chunk;
           if (MODE == PF_GATEUP)  // pairs (0,4),(1,5),(2,6),(3,7) -> columns 0..7
             chunk = make_uint4(__byte_perm(o[0], o[1], 0x5410), __byte_perm(o[2], o[3], 0x5410),
@@ -890,14 +877,8 @@ pf_predequant_kernel(VbQuantPool pool, VbQuantPool shared, int shared_e,
     const uint32_t words[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
     for (int wi = 0; wi < 4; ++wi) {
-      uint32_t pr[4], o[4];
-      nib_pairs4(words[wi], pr);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        uint32_t q;
-        asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(q) : "r"(pr[k]), "r"(0x43004300u));
-        o[k] = bf16x2_fma(q, s2, b2);
-      }
+      uint32_t o[4];
+      dequant4_bf16x2(words[wi], s2, b2, o);
       uint4 *d = reinterpret_cast<uint4 *>(dst + 8 * wi);
       if (gu)  // gate/up rows in column order
         *d = make_uint4(__byte_perm(o[0], o[1], 0x5410), __byte_perm(o[2], o[3], 0x5410),

@@ -34,10 +34,10 @@ def make_layer(seed: int, layer: int, pool: QuantPool, experts_in_slots, device=
     rng = np.random.Generator(np.random.PCG64([seed, layer]))
     wr = normal_bf16(rng, (num_experts, hidden), 0.02, device)
     wsg = normal_bf16(rng, (hidden,), 0.02, device)
-    for s, e in enumerate(experts_in_slots):
-        pool.fill_synthetic(s, expert_seed(seed, layer, int(e)))
+    experts = [int(e) for e in experts_in_slots]
+    pool.fill_synthetic_many(range(len(experts)), [expert_seed(seed, layer, e) for e in experts])
     shared = QuantPool.empty_blob(1, hidden, inter, pool.bits, pool.group, device)
-    shared.fill_synthetic(0, expert_seed(seed, layer, SHARED_ID))
+    shared.fill_synthetic_many([0], [expert_seed(seed, layer, SHARED_ID)])
     table = make_table(num_experts, {int(e): s for s, e in enumerate(experts_in_slots)}, device)
     return MoeBlock(wr, table, pool, shared, wsg, top_k=top_k, router_bias=router_bias,
                     workspace=workspace)
