@@ -29,6 +29,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "MoE tokens/s and HBM GB/s (decode T≤4); prefill tok/s at 1/2/4/8 B200"
+DECODE_WORKLOAD = "decode_verify_T4_48layers_fresh_inputs"
 EXPERT_BYTES = 1_769_472          # blob_layout stride at H=2048, I=512, 4-bit g64
 LAYER_TRAFFIC_PER_ENTRY = (73_213_440 + 1_418_752) / 33  # dram read + write / entries
 ROUTER_BYTES = 512 * 2048 * 2
@@ -133,49 +134,66 @@ def barrier(world):
 
 # ------------------------------------------------------------------ CPU legs
 
-def cpu_decode_sample(layers: int, T: int = 4, seed: int = 1):
-    """Time the CPU restatement of ``layers`` chained MoE blocks (T tokens).
-    Returns (seconds, details)."""
-    import numpy as np
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def cpu_layer_seconds(layer: int, T: int = 4, seed: int = 1) -> float:
+    """CPU restatement of one layer of the benchmark stack (fresh seeded
+    input, the same input, weights and routes as the GPU's layer ``layer``):
+    seconds for one ``FileStreamingMoeBlock.__call__``. The seeded expert
+    arrays of the routed experts are generated before the clock starts."""
+    from oracle import mlx_ops as M
     from oracle import moe as OM
     from oracle import synth_np as SN
-    x = SN.input_tokens(seed, T)
-    lays = [SN.LazyLayer(seed, l) for l in range(layers)]
-    # untimed pass: materialise the routed experts
-    h = x
-    for lay in lays:
-        r = OM.moe_block_decode(h, lay, k=10, norm_eps=1e-6, residual=h)
-        h = r["out"]
+    x = SN.input_tokens(1000 * seed + layer + 1, T)
+    lay = SN.LazyLayer(seed, layer)
+    xn = OM.rmsnorm_unit(M.bf16(x), 1e-6)
+    _, _, inds, _ = OM.router(xn, lay["wr"], 10)
+    lay["pool"].prefetch(sorted(set(inds.reshape(-1).tolist())))
     t0 = time.perf_counter()
-    h = x
-    for lay in lays:
-        h = OM.moe_block_decode(h, lay, k=10, norm_eps=1e-6, residual=h)["out"]
-    dt = time.perf_counter() - t0
-    return dt, {"layers": layers, "T": T}
+    OM.moe_block_decode(x, lay, k=10, norm_eps=1e-6, residual=x)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline_info(sample: str, value: float, kind: str = "port") -> dict:
+    return {"value": value, "unit": "tokens/s", "cores": os.cpu_count(), "kind": kind,
+            "cpu_model": cpu_model(), "sample": sample}
 
 
 def run_reference(args, world, rank):
-    """Reference arm: the CPU restatement (MLX is unavailable on Linux x86)."""
+    """Reference arm: the CPU restatement of the reference path (MLX, which
+    the reference runs on, is not available on Linux x86). One step = one
+    layer of the same 48-layer stack the GPU arm runs (layer W+i for timed
+    step i, each on its own fresh input), so the expert work per step is the
+    GPU's own per-layer work; tokens/s = T / (48 x mean layer time)."""
     if rank != 0:
         return 0
-    import numpy as np  # noqa: F401
-    cores = os.cpu_count() or 1
-    layers_per_step = args.ref_layers
-    for _ in range(args.warmup):
-        cpu_decode_sample(layers_per_step)
-    times = [cpu_decode_sample(layers_per_step)[0] for _ in range(args.steps)]
-    per_layer = sum(times) / (len(times) * layers_per_step)
-    step_s = per_layer * 48
-    value = 4 / step_s
+    L, T = args.layers, 4
+    for i in range(args.warmup):
+        cpu_layer_seconds(i % L, T)
+    times = [cpu_layer_seconds((args.warmup + i) % L, T) for i in range(args.steps)]
+    per_layer = sum(times) / len(times)
+    value = T / (per_layer * L)
+    sample = (f"one layer per step (layers {args.warmup % L}..{(args.warmup + args.steps - 1) % L} "
+              f"of the {L}-layer fresh-input stack, T={T}); tokens/s = T / ({L} x mean layer time)")
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": per_layer * 1e3, "ms_per_48_layer_step": per_layer * L * 1e3,
+        "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, random-init weights)",
-        "config": {"workload": "decode_verify_T4_48layers", "tokens": 4, "layers": 48,
+        "config": {"workload": DECODE_WORKLOAD, "tokens": T, "layers": L,
                    "experts": 512, "top_k": 10, "pool_slots_per_layer": 192},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
-                         "sample": f"{layers_per_step} of 48 layers per step, T=4, scaled x{48 // layers_per_step}"},
+        "cpu_baseline": cpu_baseline_info(sample, value),
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -382,18 +400,18 @@ def run_prefill_attention_leg(steps: int = 10, warmup: int = 3, lengths=(4096, 3
 
 def run_decode_t1_leg(st, stream, steps: int = 20, warmup: int = 3):
     """Config 0 shape (decode, T=1) over the same 48-layer stack: token 0 of
-    the config-1 input. Each token is routed independently, so token 0's
+    every layer's input. Each token is routed independently, so token 0's
     experts are among the resident ones. Bytes per layer: its distinct
     experts + the shared one + router + w_sg + x/out."""
     import torch
     hbm_peak, _, peak_kind = peaks()
     L = len(st.blocks)
+    xs = [st.layer_input(l)[:1].clone() for l in range(L)]
     hs = [torch.empty((1, 2048), dtype=torch.bfloat16, device="cuda") for _ in range(L + 1)]
-    hs[0].copy_(st.hs[0][:1])
 
     def chain():
         for l, blk in enumerate(st.blocks):
-            blk.decode(hs[l], out=hs[l + 1], residual=hs[l], norm_eps=st.norm_eps, stream=stream)
+            blk.decode(xs[l], out=hs[l + 1], residual=xs[l], norm_eps=st.norm_eps, stream=stream)
 
     with torch.cuda.stream(stream):
         chain()
@@ -529,28 +547,78 @@ def run_residency_leg(layers: int = 8, steps: int = 12, warmup: int = 4, T: int 
             "steps": steps, "warmup": warmup}
 
 
-def run_decode(args, world, rank, local):
+def decode_stack_graph(st, stream):
+    """The whole 48-layer step of ``st`` captured as one CUDA graph."""
     import torch
-    from vates_b200.synth import DecodeStack
-
-    hbm_peak, _, peak_kind = peaks()
-    T, L = 4, args.layers
-    st = DecodeStack(seed=1, layers=L, cap=192, T=T)
-    st.ensure_resident()
-    U = st.unique_experts()
-    torch.cuda.synchronize()
-
-    stream = torch.cuda.Stream()
-    x_static = st.hs[0]
-    # warm the kernels (attribute setup) outside capture
-    with torch.cuda.stream(stream):
+    with torch.cuda.stream(stream):  # warm the kernels (attribute setup) outside capture
         st.step(stream=stream)
     stream.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         st.step(stream=stream)
     torch.cuda.synchronize()
+    return graph
 
+
+def time_graph(graph, steps: int, warmup: int) -> float:
+    import torch
+    for _ in range(max(warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def step_bytes_of(U, T: int) -> int:
+    """Algorithmic HBM bytes of one stack step: per layer the distinct routed
+    experts and the shared one (1,769,472 B each), the router (2 MiB), the
+    shared-expert gate, and x, residual and out (T x H bf16 each)."""
+    return sum(u * EXPERT_BYTES + EXPERT_BYTES + ROUTER_BYTES + SHARED_GATE_BYTES
+               + 3 * T * 2048 * 2 for u in U)
+
+
+def run_decode_chain_leg(stream, steps: int = 20, warmup: int = 3, T: int = 4, L: int = 48):
+    """The same stack as a chain (layer l+1's input is layer l's output): with
+    random-init weights the chain routes fewer distinct experts per layer, so
+    a step reads fewer bytes."""
+    import torch
+    from vates_b200.synth import DecodeStack
+    hbm_peak, _, peak_kind = peaks()
+    st = DecodeStack(seed=1, layers=L, cap=192, T=T, fresh=False)
+    st.ensure_resident()
+    U = st.unique_experts()
+    graph = decode_stack_graph(st, stream)
+    ms = time_graph(graph, steps, warmup)
+    del graph
+    sb = step_bytes_of(U, T)
+    gbs = sb / (ms / 1e3) / 1e9
+    del st
+    torch.cuda.empty_cache()
+    return {"workload": f"decode_verify_T{T}_{L}layers_chain", "ms_per_step": ms,
+            "tokens_per_s": T / (ms / 1e3), "unique_experts_per_layer": U,
+            "unique_experts_per_layer_mean": sum(U) / len(U), "bytes_per_step": sb,
+            "hbm_gbs_algorithmic": gbs, "frac_of_hbm_peak": gbs / hbm_peak,
+            "peak_kind": peak_kind}
+
+
+def run_decode(args, world, rank, local):
+    import torch
+    from vates_b200.synth import DecodeStack
+
+    hbm_peak, _, peak_kind = peaks()
+    T, L = 4, args.layers
+    st = DecodeStack(seed=1, layers=L, cap=192, T=T, fresh=True)
+    st.ensure_resident()
+    U = st.unique_experts()
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream()
+    graph = decode_stack_graph(st, stream)
     for _ in range(max(args.warmup, 3)):
         graph.replay()
     torch.cuda.synchronize()
@@ -571,13 +639,15 @@ def run_decode(args, world, rank, local):
     clocks = clk.summary()
     value = world * T / (ms / 1e3)
 
-    # ---- end to end through the public API with host buffers ----
-    x_host = torch.empty((T, 2048), dtype=torch.bfloat16, pin_memory=True)
-    x_host.copy_(st.x.cpu())
+    # ---- end to end through the public API with host buffers: every step
+    # copies its 48 layer inputs from pinned host memory and reads the last
+    # layer's output back ----
+    x_host = torch.empty(tuple(st.xs.shape), dtype=torch.bfloat16, pin_memory=True)
+    x_host.copy_(st.xs.cpu())
     y_host = torch.empty((T, 2048), dtype=torch.bfloat16, pin_memory=True)
     cur = torch.cuda.current_stream()
     for _ in range(3):
-        x_static.copy_(x_host, non_blocking=True)
+        st.xs.copy_(x_host, non_blocking=True)
         graph.replay()
         y_host.copy_(st.hs[-1], non_blocking=True)
     torch.cuda.synchronize()
@@ -585,7 +655,7 @@ def run_decode(args, world, rank, local):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(cur)
     for _ in range(args.steps):
-        x_static.copy_(x_host, non_blocking=True)
+        st.xs.copy_(x_host, non_blocking=True)
         graph.replay()
         y_host.copy_(st.hs[-1], non_blocking=True)
     e1.record(cur)
@@ -611,28 +681,29 @@ def run_decode(args, world, rank, local):
         (2, "pdl_wait"), (3, "router_rows"), (4, "grid_barrier"), (5, "routing"),
         (6, "gateup"), (7, "down"), (8, "combine"))}
 
-    # ---- the layer kernel timed per launch with CUDA events (outside the
-    # PDL chain, so each launch starts cold) ----
+    # ---- the layer kernel timed per launch with CUDA events outside the
+    # graph and the PDL chain (each launch starts cold) ----
     evs, arr = st.blocks[0].timing_events()
-    launch_ms = 0.0
+    cold_ms = 0.0
     reps = 3
     for _ in range(reps):
         for l, blk in enumerate(st.blocks):
-            blk.decode(st.hs[l], out=st.hs[l + 1], residual=st.hs[l], norm_eps=st.norm_eps,
-                       timing=arr)
+            xin = st.layer_input(l)
+            blk.decode(xin, out=st.hs[l + 1], residual=xin, norm_eps=st.norm_eps, timing=arr)
             evs[1].synchronize()
-            launch_ms += evs[0].elapsed_time(evs[1])
-    launch_ms /= reps * L
+            cold_ms += evs[0].elapsed_time(evs[1])
+    cold_ms /= reps * L
 
-    step_bytes = sum(u * EXPERT_BYTES + EXPERT_BYTES + ROUTER_BYTES + SHARED_GATE_BYTES
-                     + 3 * T * 2048 * 2 for u in U)
+    step_bytes = step_bytes_of(U, T)
     hbm_gbs = step_bytes / (ms / 1e3) / 1e9
     layer_bytes = step_bytes / L  # per launch, algorithmic
+    # The timed region holds nothing but the 48 launches of the layer kernel
+    # per step, so its average launch takes ms / L.
+    launch_ms = ms / L
     achieved = layer_bytes / (launch_ms / 1e3) / 1e9
-    # DRAM traffic per launch: one ncu capture of a 4-layer case (33 entries
-    # = 32 routed experts + the shared one per launch) read+wrote
-    # LAYER_TRAFFIC_PER_ENTRY bytes per entry; scaled to this run's mean
-    # entries per launch.
+    # DRAM traffic per launch: one ncu capture of a 4-layer case read+wrote
+    # LAYER_TRAFFIC_PER_ENTRY bytes per entry (routed experts + the shared
+    # one); scaled to this run's mean entries per launch.
     traffic = LAYER_TRAFFIC_PER_ENTRY * (sum(U) / L + 1)
 
     out = {
@@ -640,31 +711,38 @@ def run_decode(args, world, rank, local):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded, random-init weights)",
-        "config": {"workload": "decode_verify_T4_48layers", "tokens": T, "layers": L,
+        "config": {"workload": DECODE_WORKLOAD, "tokens": T, "layers": L,
                    "hidden": 2048, "inter": 512, "experts": 512, "top_k": 10,
                    "pool_slots_per_layer": 192, "quant": "mlx affine 4-bit g64",
+                   "inputs": "a fresh seeded N(0,1) input per layer (independent routes)",
                    "parallelism": f"replicas x{world}",
                    "l2": "inputs larger than L2 (16.3 GB pool, ~3.5 GB read per step)"},
         "hbm_gbs_algorithmic": hbm_gbs,
         "hbm_frac_of_measured": hbm_gbs / hbm_peak,
         "hbm_frac_of_8tbs": hbm_gbs / 8000.0,
         "bytes_per_step": step_bytes,
+        "unique_experts_per_layer": U,
         "unique_experts_per_layer_mean": sum(U) / len(U),
         "e2e": {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s",
-                "h2d_bytes_per_step": T * 2048 * 2, "d2h_bytes_per_step": T * 2048 * 2},
+                "h2d_bytes_per_step": int(st.xs.numel() * 2), "d2h_bytes_per_step": T * 2048 * 2},
         "roofline": {"kernel": "moe_layer_kernel", "bound": "hbm", "achieved": achieved,
                      "peak": hbm_peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": achieved / hbm_peak, "traffic": traffic,
                      "traffic_unit": "bytes per launch",
                      "bytes_per_launch": layer_bytes, "ms_per_launch": launch_ms,
-                     "in_graph_gbs": layer_bytes / (layer_us / 1e6) / 1e9},
+                     "cold_launch_ms": cold_ms,
+                     "cold_launch_gbs": layer_bytes / (cold_ms / 1e3) / 1e9},
         "kernel_trace_us": {"span": kspan, "layer_period": layer_us,
                             "marks_from_start": marks},
         "gpu_launches": L * args.steps,
         "clocks": clocks,
     }
+    del graph
     if not args.no_extra:
         out["decode_t1"] = run_decode_t1_leg(st, stream)
+        del st
+        torch.cuda.empty_cache()
+        out["decode_chain"] = run_decode_chain_leg(stream)
         if world == 1:
             out["prefill"] = run_prefill_leg()
             out["isoquant"] = run_isoquant_leg()
@@ -673,14 +751,13 @@ def run_decode(args, world, rank, local):
         else:
             out["prefill"] = run_prefill_ep_leg(world, rank)
     if rank == 0 and world == 1 and not args.no_cpu:
-        dt, det = cpu_decode_sample(args.cpu_layers)
-        cpu_tok_s = T / (dt * L / args.cpu_layers)
-        out["cpu_baseline"] = {"value": cpu_tok_s, "unit": "tokens/s", "cores": os.cpu_count(),
-                               "kind": "port",
-                               "sample": f"{args.cpu_layers} of {L} chained layers, T={T}, scaled x{L / args.cpu_layers:g}"}
+        secs = [cpu_layer_seconds(l, T) for l in range(args.cpu_layers)]
+        cpu_tok_s = T / (sum(secs) / len(secs) * L)
+        out["cpu_baseline"] = cpu_baseline_info(
+            f"layers 0..{args.cpu_layers - 1} of the {L}-layer fresh-input stack (the GPU's own "
+            f"inputs and routes), T={T}; tokens/s = T / ({L} x mean layer time)", cpu_tok_s)
     if rank == 0:
         print(json.dumps(out), flush=True)
-    del graph
     return 0
 
 
@@ -692,8 +769,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="decode", choices=["decode"])
     ap.add_argument("--layers", type=int, default=48)
-    ap.add_argument("--cpu-layers", type=int, default=2)
-    ap.add_argument("--ref-layers", type=int, default=1)
+    ap.add_argument("--cpu-layers", type=int, default=4)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the prefill (config 2) and IsoQuant (config 3) legs")

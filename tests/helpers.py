@@ -63,6 +63,34 @@ def routes_agree(gpu_inds, ref_probs, ref_inds, k):
     return np.array(ok)
 
 
+def logit_tolerance(x, wr, logits):
+    """Per-logit bound on how far a float32 router GEMM/GEMV may land from
+    the oracle's exactly-rounded bf16 logit: one bf16 ulp of the logit (a
+    value next to a rounding midpoint can round either way), or the float32
+    summation-order error of the dot product where the logit is small
+    (bounded relative to sum |x_i w_i|)."""
+    x = np.asarray(x, np.float32)
+    wr = np.asarray(wr, np.float32)
+    dot_abs = np.abs(x) @ np.abs(wr).T
+    return np.maximum(M.bf16_ulp(np.abs(logits)), dot_abs * np.float32(2.0 ** -16))
+
+
+def routes_agree_logits(gpu_inds, ref_logits, ref_inds, tol):
+    """Per token: True when the GPU's expert set equals the oracle's, or
+    when every expert the GPU picked outside the oracle's set lies within
+    the logit tolerance of the oracle's weakest pick (its logit, rounded
+    either way, can order either way against it: the selection follows the
+    bf16 probabilities, a monotone function of the logits)."""
+    g = np.sort(np.asarray(gpu_inds), 1)
+    r = np.sort(np.asarray(ref_inds), 1)
+    ok = (g == r).all(1)
+    for t in np.nonzero(~ok)[0]:
+        rs = set(r[t].tolist())
+        weakest = min(ref_logits[t, j] - tol[t, j] for j in rs)
+        ok[t] = all(ref_logits[t, e] + tol[t, e] >= weakest for e in g[t] if e not in rs)
+    return ok
+
+
 def oracle_route_and_host(blk, x, gpu_inds, k, norm_eps=0.0):
     """The oracle's own routing of ``x`` through ``blk``'s router weights
     (block.py:253, 321-329; rmsnorm first when ``norm_eps > 0``), and a host
@@ -70,7 +98,8 @@ def oracle_route_and_host(blk, x, gpu_inds, k, norm_eps=0.0):
     experts, so that the oracle can evaluate either routing.
 
     Returns ``(host, probs, inds, scores)``; ``host["full_table"]`` is the
-    block's slot table."""
+    block's slot table, ``host["logits"]`` the oracle's logits and
+    ``host["logit_tol"]`` their :func:`logit_tolerance`."""
     from oracle import moe as OM
     from vates_b200.synth import layer_to_host
     xb = M.bf16(np.asarray(x, np.float32))
@@ -78,8 +107,10 @@ def oracle_route_and_host(blk, x, gpu_inds, k, norm_eps=0.0):
         xb = OM.rmsnorm_unit(xb, norm_eps)
     wr = blk.router_w.float().cpu().numpy()
     lb = None if blk.router_bias is None else blk.router_bias.cpu().numpy()
-    _, probs, inds, scores = OM.router(xb, wr, k, blk.norm_topk_prob, lb)
+    logits, probs, inds, scores = OM.router(xb, wr, k, blk.norm_topk_prob, lb)
     experts = np.union1d(np.asarray(gpu_inds).reshape(-1), inds.reshape(-1))
     host = layer_to_host(blk, experts)
     host["full_table"] = blk.slot_table.cpu().numpy()
+    host["logits"] = logits
+    host["logit_tol"] = logit_tolerance(xb, wr, logits)
     return host, probs, inds, scores

@@ -16,7 +16,8 @@ import numpy as np
 import pytest
 
 from conftest import bf16_close
-from helpers import bf16_tensor, pool_to_torch, random_pool_np, routes_agree, to_np
+from helpers import (bf16_tensor, logit_tolerance, pool_to_torch, random_pool_np, routes_agree,
+                     routes_agree_logits, to_np)
 from oracle import mlx_ops as M
 from oracle import moe as OM
 
@@ -57,7 +58,10 @@ def _case(T, H, I, E, k, group=64, seed=0, shared=True, bias=False, layer_cap=0,
     xr = to_np(x)
     g_inds, g_scores = to_np(dbg["inds"]), to_np(dbg["scores"])
     r_logits, probs, r_inds, _ = OM.router(xr, wr_np, k, True, logit_bias=lb)
-    assert routes_agree(g_inds, probs, r_inds, k).all(), "top-k differs beyond bf16 ties"
+    assert (routes_agree(g_inds, probs, r_inds, k) |
+            routes_agree_logits(g_inds, r_logits, r_inds,
+                                logit_tolerance(xr, wr_np, r_logits))).all(), \
+        "top-k differs beyond bf16 ties and logit rounding"
     g_logits = to_np(dbg["logits"])
     # One bf16 ulp of the logit, or, where the bias cancels the product and
     # the logit lands near zero, the float32 summation-order error of the
@@ -157,11 +161,15 @@ def test_prefill_config2_full_size(cuda):
     lb = blk.router_bias.cpu().numpy()
     g_inds, g_scores, g_logits = to_np(dbg["inds"]), to_np(dbg["scores"]), to_np(dbg["logits"])
     r_logits, probs, r_inds, _ = OM.router(xr, wr, k, True, logit_bias=lb)
-    assert routes_agree(g_inds, probs, r_inds, k).all(), "top-k differs beyond bf16 ties"
-    dot_abs = np.abs(xr) @ np.abs(wr).T
-    tol = np.maximum(M.bf16_ulp(np.abs(r_logits)), dot_abs * np.float32(2.0 ** -16))
+    tol = logit_tolerance(xr, wr, r_logits)
     assert (np.abs(g_logits - r_logits) <= tol).all(), "router logits"
-    del dot_abs, tol
+    # Against the oracle's own routing: the sets agree, or differ only among
+    # experts whose logits sit within the rounding tolerance of the k-th.
+    agree = routes_agree_logits(g_inds, r_logits, r_inds, tol)
+    assert agree.all(), f"{int((~agree).sum())} tokens: top-k beyond logit rounding"
+    print(f"tokens whose set differs from the oracle's by logit rounding: "
+          f"{int((np.sort(g_inds, 1) != np.sort(r_inds, 1)).any(1).sum())} of {T}")
+    del tol
     f_probs, f_inds, f_scores = OM.route_from_logits(g_logits, k, True)
     assert routes_agree(g_inds, f_probs, f_inds, k).all(), "top-k on the GPU logits"
     gi, fi = np.sort(g_inds, 1), np.sort(f_inds, 1)

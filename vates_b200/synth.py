@@ -80,19 +80,31 @@ def config2(seed: int = 2, T: int = 32768, device="cuda", hidden=H, inter=I, num
     return blk, x
 
 
+def fresh_input_seed(seed: int, layer: int) -> int:
+    """Seed of the fresh per-layer input of :class:`DecodeStack` (``fresh``)."""
+    return seed * 1000 + layer + 1
+
+
 class DecodeStack:
     """Config 1: ``L`` stacked MoE blocks, T tokens (MTP K=3 verify uses 4).
 
     Layer ``l``'s experts resolve through its own slot table into rows
     ``[l*cap, (l+1)*cap)`` of one packed HBM pool. Each block computes
-    ``h <- h + MoE_l(rmsnorm(h))`` (the decoder's pre-norm residual around the
-    MoE), so the 48-layer chain keeps a realistic input distribution.
+    ``out <- x + MoE_l(rmsnorm(x))`` (the decoder's pre-norm residual around
+    the MoE). With ``fresh=False`` the layers form a chain (``x_{l+1}`` is
+    layer ``l``'s output); with random-init weights that chain drifts
+    towards a common direction and routes fewer distinct experts per layer
+    than real hidden states do. With ``fresh=True`` every layer gets its own
+    seeded N(0, 1) input (the launches still follow one another on the
+    stream), so the routes of different layers are independent, as they are
+    for real hidden states: about 39 distinct experts per layer at T=4.
     """
 
     def __init__(self, seed: int = 1, layers: int = 48, cap: int = 192, T: int = 4,
                  device="cuda", hidden=H, inter=I, num_experts=E, top_k=K,
-                 norm_eps: float = 1e-6):
+                 norm_eps: float = 1e-6, fresh: bool = False):
         self.seed, self.L, self.cap, self.T = seed, layers, cap, T
+        self.fresh = fresh
         self.hidden, self.inter, self.num_experts, self.top_k = hidden, inter, num_experts, top_k
         self.norm_eps = norm_eps
         self.device = device
@@ -111,6 +123,13 @@ class DecodeStack:
         self.hs = [torch.empty((T, hidden), dtype=torch.bfloat16, device=device)
                    for _ in range(layers + 1)]
         self.hs[0].copy_(self.x)
+        # fresh inputs: one [L, T, H] tensor (one host->device copy per step)
+        self.xs = (torch.stack([input_tokens(fresh_input_seed(seed, l), T, hidden, device)
+                                for l in range(layers)]) if fresh else None)
+
+    def layer_input(self, l: int) -> torch.Tensor:
+        """The input (and residual) of layer ``l``."""
+        return self.xs[l] if self.fresh else self.hs[l]
 
     def ensure_resident(self, max_rounds: int = 4) -> int:
         """Make every expert routed by the stack's fixed input resident.
@@ -122,7 +141,8 @@ class DecodeStack:
         for l, blk in enumerate(self.blocks):
             for _ in range(max_rounds):
                 dbg = blk.new_debug(self.T, self.device)
-                blk.decode(self.hs[l], out=self.hs[l + 1], residual=self.hs[l], debug=dbg,
+                xin = self.layer_input(l)
+                blk.decode(xin, out=self.hs[l + 1], residual=xin, debug=dbg,
                            norm_eps=self.norm_eps)
                 routed = set(dbg["inds"].flatten().tolist())
                 slots = self.slot_experts[l]
@@ -132,8 +152,10 @@ class DecodeStack:
                 free = [s for s, e in enumerate(slots) if e not in routed]
                 for e, s in zip(missing, free):
                     slots[s] = e
-                    blk.pool.fill_synthetic(s, expert_seed(self.seed, l, e))
                     swaps += 1
+                placed = list(zip(missing, free))
+                blk.pool.fill_synthetic_many([s for _, s in placed],
+                                             [expert_seed(self.seed, l, e) for e, _ in placed])
                 blk.slot_table.copy_(make_table(self.num_experts,
                                                 {e: s for s, e in enumerate(slots)},
                                                 self.device))
@@ -144,7 +166,8 @@ class DecodeStack:
         """One whole-stack step: 48 chained MoE blocks over the T tokens.
         ``trace`` (int64 [L, 16] device tensor) records per-layer kernel spans and markers."""
         for l, blk in enumerate(self.blocks):
-            blk.decode(self.hs[l], out=self.hs[l + 1], residual=self.hs[l],
+            xin = self.layer_input(l)
+            blk.decode(xin, out=self.hs[l + 1], residual=xin,
                        norm_eps=self.norm_eps, stream=stream,
                        trace=None if trace is None else trace[l])
         return self.hs[-1]
@@ -156,7 +179,8 @@ class DecodeStack:
         out = []
         for l, blk in enumerate(self.blocks):
             dbg = blk.new_debug(self.T, self.device)
-            blk.decode(self.hs[l], out=torch.empty_like(self.hs[l]), residual=self.hs[l],
+            xin = self.layer_input(l)
+            blk.decode(xin, out=torch.empty_like(xin), residual=xin,
                        debug=dbg, norm_eps=self.norm_eps)
             out.append(dbg["inds"][t].tolist())
         return out
@@ -166,7 +190,8 @@ class DecodeStack:
         out = []
         for l, blk in enumerate(self.blocks):
             dbg = blk.new_debug(self.T, self.device)
-            blk.decode(self.hs[l], out=torch.empty_like(self.hs[l]), residual=self.hs[l],
+            xin = self.layer_input(l)
+            blk.decode(xin, out=torch.empty_like(xin), residual=xin,
                        debug=dbg, norm_eps=self.norm_eps)
             out.append(len(set(dbg["inds"].flatten().tolist())))
         return out
