@@ -8,7 +8,7 @@ mean-rel 5e-3 in bf16.
 import numpy as np
 import pytest
 
-from conftest import bf16_close, block_scale
+from conftest import bf16_close, bf16_steps, block_scale
 from helpers import (bf16_tensor, oracle_route_and_host, pool_to_torch, random_pool_np,
                      routes_agree, routes_agree_logits, to_np)
 from oracle import mlx_ops as M
@@ -38,10 +38,15 @@ def _check_block(blk, x, norm_eps=0.0, residual=None, k=10):
             routes_agree_logits(g_inds, host["logits"], r_inds, host["logit_tol"])).all(), \
         "top-k differs beyond bf16 ties and logit rounding"
     same = np.array([set(a) == set(b) for a, b in zip(g_inds.tolist(), r_inds.tolist())])
+    # Scores per expert id: bit-identical, except that a CUDA expf / numpy exp
+    # ulp difference next to a bf16 rounding midpoint may move one by a bf16
+    # step (and the renormalised scores of that token with it).
     for t in np.nonzero(same)[0]:
         gs = dict(zip(g_inds[t].tolist(), g_scores[t].tolist()))
         rs = dict(zip(r_inds[t].tolist(), r_scores[t].tolist()))
-        assert gs == rs, f"token {t}: route scores differ"
+        ids = sorted(gs)
+        assert bf16_steps([gs[e] for e in ids], [rs[e] for e in ids]).max() <= 1, \
+            f"token {t}: route scores differ"
     ref = OM.moe_block_decode(xr, host, k=k, norm_eps=norm_eps, residual=res)
     assert np.array_equal(ref["inds"], r_inds)
     if same.all():

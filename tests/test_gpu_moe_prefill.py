@@ -179,7 +179,17 @@ def test_prefill_config2_full_size(cuda):
     fo = np.argsort(f_inds, 1)
     gs = np.take_along_axis(g_scores, go, 1)[same]
     fs = np.take_along_axis(f_scores, fo, 1)[same]
-    assert np.array_equal(gs, fs), "route scores"
+    # The softmax exponentials of the GPU (CUDA expf) and of the oracle
+    # (numpy's float32 exp) may differ by an ulp, which moves a bf16
+    # probability next to a rounding midpoint by one bf16 ulp (and with it
+    # the renormalised scores of that token): scores agree bit for bit for
+    # nearly every token and within one bf16 step everywhere.
+    from conftest import bf16_steps
+    steps = bf16_steps(gs, fs)
+    assert steps.max() <= 1, "route scores beyond one bf16 step"
+    exact = (steps == 0).all(1).mean()
+    print(f"tokens with bit-identical scores: {exact:.5f}")
+    assert exact >= 0.999, f"route scores bit-identical for only {exact:.4%} of tokens"
     counts = np.bincount(g_inds.reshape(-1), minlength=E)
     assert (counts >= 384).sum() >= 48 and len(OM.expert_groups(counts, E)) >= 10
     heavy = counts >= 384
