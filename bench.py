@@ -240,58 +240,79 @@ def run_prefill_leg(steps: int = 10, warmup: int = 3, T: int = 32768):
 
 def run_prefill_ep_leg(world: int, rank: int, steps: int = 10, warmup: int = 3, T: int = 32768,
                        hot_share: float = 0.02):
-    """Config 2 expert-parallel over the ranks (one per GPU). The route
-    histogram of the batch (the router is deterministic) decides the
-    placement: experts with at least ``hot_share`` of the routes are held by
-    every rank and computed there for its own tokens, the others are owned
-    by one rank each (greedy LPT over their route counts). Rank r starts
-    with tokens [r*T/N, (r+1)*T/N); dispatch and combine are NCCL
-    all-to-all. Time = max over ranks (strong scaling, T fixed)."""
+    """Config 2 expert-parallel over the ranks (one per GPU) through the C ABI
+    (``vb_moe_prefill_ep``, NCCL point-to-point on a communicator of its own).
+    The placement comes from the route histogram of an EARLIER batch (same
+    Zipf-biased router, other tokens), not of the timed one: experts with at
+    least ``hot_share`` of those routes are held by every rank and computed
+    there for its own tokens, the others are owned by one rank each (greedy
+    LPT over their route counts). Rank r starts with tokens [r*T/N,
+    (r+1)*T/N). Time = max over ranks (strong scaling, T fixed). Rank 0 also
+    runs its token slice through the single-device ``vb_moe_prefill`` with
+    every expert resident and reports whether the outputs are bit-identical."""
     import numpy as np
     import torch
     import torch.distributed as dist
-    from vates_b200.ep import CudaEpBackend, ep_prefill, placement
+    from vates_b200.ep import CudaEpBackend, NativeEp, NcclComm, placement
     from vates_b200.pool import QuantPool
+    from vates_b200.prefill import moe_prefill
     from vates_b200.synth import E as NE, H as HH, I as II, input_tokens, make_layer, zipf_bias
     _, bf16_peak, peak_kind = peaks()
     seed = 2
     bias = torch.from_numpy(zipf_bias(seed, NE)).cuda()
-    x_all = input_tokens(seed, T)
     probe = make_layer(seed, 0, QuantPool.empty_blob(1, HH, II, 4, 64, "cuda"), [], "cuda",
                        router_bias=bias)
-    counts = CudaEpBackend(probe, torch.zeros(NE, dtype=torch.int32)).route(x_all)[3]
+    earlier = input_tokens(seed + 100, T)  # placement batch: not the timed input
+    counts = CudaEpBackend(probe, torch.zeros(NE, dtype=torch.int32)).route(earlier)[3]
     counts = counts.cpu().numpy()
-    del probe
+    del probe, earlier
     owner, resident = placement(counts, world, rank, share=hot_share)
     n_hot = int(((counts >= hot_share * counts.sum()) if world > 1 else np.zeros(NE, bool)).sum())
     owned = [e for e in range(NE) if resident[e]]
     pool = QuantPool.empty_blob(len(owned), HH, II, 4, 64, "cuda")
     blk = make_layer(seed, 0, pool, owned, "cuda", router_bias=bias)
     per = T // world
+    x_all = input_tokens(seed, T)
     x = x_all[rank * per:(rank + 1) * per].contiguous()
     del x_all
-    be = CudaEpBackend(blk, torch.from_numpy(owner))
+    comm = NcclComm()
+    ep = NativeEp(blk, owner, comm, max_tokens=per)
+    out = torch.empty_like(x)
     for _ in range(max(warmup, 3)):
-        ep_prefill(be, x)
+        ep(x, out=out)
     torch.cuda.synchronize()
     dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
-        ep_prefill(be, x)
+        ep(x, out=out)
     e1.record()
     torch.cuda.synchronize()
     ms = max_over_ranks(e0.elapsed_time(e1) / steps, world)
     dist.barrier()
+    comm.close()
+    identical = None
+    if rank == 0:
+        del ep, blk, pool
+        torch.cuda.empty_cache()
+        full = make_layer(seed, 0, QuantPool.empty_blob(NE, HH, II, 4, 64, "cuda"), range(NE),
+                          "cuda", router_bias=bias)
+        ref = moe_prefill(full, x)
+        torch.cuda.synchronize()
+        identical = bool(torch.equal(ref.view(torch.int16), out.view(torch.int16)))
+        del full, ref
+        torch.cuda.empty_cache()
+    dist.barrier()
     flops = PREFILL_FLOPS_32K * T / 32768
     tf = flops / (ms / 1e3) / 1e12
     return {"workload": "prefill_32k_1layer_ep", "tokens": T, "n_gpus": world,
+            "entry": "vb_moe_prefill_ep (C ABI, NCCL send/recv)",
             "ms_per_step": ms, "tok_per_s": T / (ms / 1e3), "tflops_algorithmic": tf,
             "tflops_per_gpu": tf / world, "frac_of_bf16_peak_per_gpu": tf / world / bf16_peak,
             "peak_kind": peak_kind, "experts_per_gpu": len(owned), "hot_experts_replicated": n_hot,
-            "placement": f"experts with >= {hot_share:.0%} of the routes on every rank, "
-                         "the rest LPT over the route counts",
-            "scaling": "strong"}
+            "placement": f"from an earlier batch's routes: experts with >= {hot_share:.0%} of "
+                         "them on every rank, the rest LPT over their counts",
+            "ep_bit_identical": identical, "scaling": "strong"}
 
 
 def run_isoquant_leg(steps: int = 20, warmup: int = 3, S: int = 131072, layers: int = 12):

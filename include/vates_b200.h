@@ -371,6 +371,41 @@ int vb_ep_unpack(const int32_t *recv_meta, int32_t routes,
                  float *route_score, vb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Expert-parallel expert-major prefill over NCCL (one rank per GPU): the
+ * prefill branch of FileStreamingMoeBlock.__call__ (mlx_streaming/core/moe/
+ * block.py:330-347) and _expert_major_forward (block.py:111-243) with the
+ * experts spread over the ranks. Every rank calls it with its own tokens
+ * (base.tokens, base.x, base.out) and the experts it holds (base.pool and
+ * base.slot_table, -1 for experts it does not hold); owner[e] is the rank
+ * that computes expert e for this rank's routes (experts held by every rank
+ * map to the caller's own rank). Schedule on `stream`: route, all-reduce of
+ * the route histogram, pack, count exchange (read on the host: the call
+ * synchronises the stream once), grouped ncclSend/ncclRecv of token rows and
+ * route metadata, the rank's experts and the shared expert, the weighted
+ * route rows back, the reference-order reduce. The output is bit-identical
+ * to vb_moe_prefill on one device for any world size and placement.
+ * nccl_comm is an ncclComm_t of `world` ranks (this process is `rank`); NCCL
+ * is resolved at run time from the loaded libnccl.so.2. Every rank must make
+ * the call with the same world, experts and top_k. The workspace
+ * (vb_moe_prefill_ep_workspace_size, 1024-byte aligned) covers the worst
+ * case, every route of every rank sent to this rank: max_tokens_per_rank is
+ * the largest token count of any rank. */
+typedef struct VbMoePrefillEpArgs {
+  VbMoePrefillArgs base;
+  const int32_t *owner;         /* device [E] */
+  int32_t world;                /* <= 8 */
+  int32_t rank;
+  int32_t max_tokens_per_rank;
+  int32_t reserved;
+} VbMoePrefillEpArgs;
+size_t vb_moe_prefill_ep_workspace_size(int32_t tokens, int32_t hidden,
+                                        int32_t inter, int32_t num_experts,
+                                        int32_t top_k, int32_t world,
+                                        int32_t max_tokens_per_rank);
+int vb_moe_prefill_ep(const VbMoePrefillEpArgs *args, void *nccl_comm,
+                      vb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Deterministic route reduce: replaces deterministic_route_reduce
  * (mlx_streaming/core/moe/custom_kernel.py:20-118). previous [tokens, H],
  * weighted [G, H], assignment_pos int32 [G] (unique flat route positions in
@@ -529,6 +564,28 @@ int vb_kv_prefill_attn(const uint16_t *q, const uint32_t *k_codes,
                        int32_t group, int32_t k_bits, int32_t v_bits,
                        float scale, int32_t causal, uint16_t *out,
                        int32_t *status, vb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Gated-DeltaNet recurrent steps (the linear-attention state update of the
+ * Qwen3-Next GDN layers at decode / MTP verify). Replaces the gated-delta
+ * kernel of mlx_streaming/core/linear_attn/gated_delta_multistate.py:28-198
+ * (vendored from mlx-lm; y, final state and the state after every step) and
+ * the blocked scan of mlx_streaming/core/attention/gdn_fused.py:13-126.
+ * Per value head hv (key head hv / (v_heads / k_heads)) and step t, in
+ * float32: S *= g; kv = S k; delta = (v - kv) * beta; S += delta k^T;
+ * y = bf16(S q). A step with mask[b, t] == 0 leaves S unchanged and gives
+ * y = 0. q, k bf16 [B, T, k_heads, 128]; v bf16 [B, T, v_heads, v_dim];
+ * g f32 [B, T, v_heads] (g_per_key = 0) or [B, T, v_heads, 128]; beta f32
+ * [B, T, v_heads]; state_in/state_out f32 [B, v_heads, v_dim, 128] (may
+ * alias); states_out nullable f32 [B, T, v_heads, v_dim, 128]; mask nullable
+ * u8 [B, T]; y bf16 [B, T, v_heads, v_dim]. tokens <= 16, v_dim % 16 == 0. */
+int vb_gated_delta_step(const uint16_t *q, const uint16_t *k,
+                        const uint16_t *v, const float *g, int32_t g_per_key,
+                        const float *beta, const float *state_in,
+                        float *state_out, float *states_out,
+                        const uint8_t *mask, uint16_t *y, int32_t batch,
+                        int32_t tokens, int32_t k_heads, int32_t v_heads,
+                        int32_t k_dim, int32_t v_dim, vb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Affine dequantization (MLX mx.dequantize; the reference's per-element

@@ -83,7 +83,7 @@ def test_prefill_phases_compose_to_the_single_call(cuda):
     assert torch.equal(out, ref)
 
 
-def _ep_rank(rank, world, port, q, owner=None):
+def _ep_rank(rank, world, port, q, owner=None, native=False):
     import torch
     import torch.distributed as dist
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
@@ -94,21 +94,50 @@ def _ep_rank(rank, world, port, q, owner=None):
                             timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     try:
-        from vates_b200.ep import CudaEpBackend, ep_prefill, lpt_placement
+        from vates_b200.ep import CudaEpBackend, NativeEp, NcclComm, ep_prefill, lpt_placement
         if owner is None:
             owner = lpt_placement(np.ones(E), world)
         owned = [e for e in range(E) if owner[e] == rank]
         blk, x = _block(owned=owned)
         per = T // world
-        be = CudaEpBackend(blk, torch.from_numpy(owner))
-        out = ep_prefill(be, x[rank * per:(rank + 1) * per].contiguous())
+        xr = x[rank * per:(rank + 1) * per].contiguous()
+        if native:
+            comm = NcclComm()
+            out = NativeEp(blk, owner, comm, max_tokens=per)(xr)
+            torch.cuda.synchronize()
+            comm.close()
+        else:
+            be = CudaEpBackend(blk, torch.from_numpy(owner))
+            out = ep_prefill(be, xr)
         torch.cuda.synchronize()
         q.put((rank, out.float().cpu().numpy()))
     finally:
         dist.destroy_process_group()
 
 
-def test_ep_prefill_two_gpus_matches_one(cuda):
+def test_native_ep_one_rank_matches_single_device(cuda):
+    """vb_moe_prefill_ep through the C ABI on a one-rank NCCL communicator
+    (every route stays on the rank: the self chunks are device copies):
+    bit-identical to vb_moe_prefill, with and without replicated experts."""
+    import torch
+    from vates_b200.ep import NativeEp, NcclComm
+    from vates_b200.prefill import moe_prefill
+    blk, x = _block()
+    ref = moe_prefill(blk, x)
+    comm = NcclComm()
+    try:
+        out = NativeEp(blk, np.zeros(E, np.int32), comm, max_tokens=T)(x)
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+        again = NativeEp(blk, np.zeros(E, np.int32), comm, max_tokens=2 * T)(x)
+        torch.cuda.synchronize()
+        assert torch.equal(again.view(torch.int16), ref.view(torch.int16))
+    finally:
+        comm.close()
+
+
+@pytest.mark.parametrize("native", [False, True])
+def test_ep_prefill_two_gpus_matches_one(cuda, native):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -120,7 +149,8 @@ def test_ep_prefill_two_gpus_matches_one(cuda):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29700 + os.getpid() % 200
-    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port + int(native), q, None, native))
+             for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in range(2))
@@ -131,7 +161,8 @@ def test_ep_prefill_two_gpus_matches_one(cuda):
     assert np.array_equal(got, ref)
 
 
-def test_ep_prefill_two_gpus_with_replicated_hot_experts(cuda):
+@pytest.mark.parametrize("native", [False, True])
+def test_ep_prefill_two_gpus_with_replicated_hot_experts(cuda, native):
     """Experts with many routes held by both GPUs (each computes them for
     its own tokens), the rest owned by one GPU: bit-identical to one GPU."""
     import torch
@@ -152,7 +183,8 @@ def test_ep_prefill_two_gpus_with_replicated_hot_experts(cuda):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = 29700 + (os.getpid() + 100) % 200
-    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, q, owners[r])) for r in range(2)]
+    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port + int(native), q, owners[r], native))
+             for r in range(2)]
     for p in procs:
         p.start()
     res = dict(q.get(timeout=300) for _ in range(2))

@@ -241,3 +241,26 @@ def test_expert_major_rows_equal_whole_batch_rows():
                                 H, I, 64, 4, layer_cap=3, max_assignments=40)
     assert len(OM.expert_groups(counts, 3, 40)) > 3
     assert np.array_equal(rows, full[sel])
+
+
+def test_gdn_oracle_states_and_chain():
+    """The oracle's per-step states end in its final state, masked steps keep
+    the state, and a T-step run equals T one-step runs."""
+    from oracle import gdn as OG
+    rng = np.random.default_rng(3)
+    B, T, Hk, Hv, D = 1, 3, 2, 4, 16
+    q = M.bf16(rng.standard_normal((B, T, Hk, D)).astype(np.float32) * 0.1)
+    k = M.bf16(rng.standard_normal((B, T, Hk, D)).astype(np.float32) * 0.2)
+    v = M.bf16(rng.standard_normal((B, T, Hv, D)).astype(np.float32))
+    g = rng.uniform(0.8, 1.0, (B, T, Hv)).astype(np.float32)
+    beta = rng.uniform(0.1, 0.9, (B, T, Hv)).astype(np.float32)
+    s0 = (rng.standard_normal((B, Hv, D, D)) * 0.1).astype(np.float32)
+    y, fin, states = OG.gated_delta(q, k, v, g, beta, s0)
+    assert np.array_equal(states[:, -1], fin)
+    s = s0
+    for t in range(T):
+        y1, s, _ = OG.gated_delta(q[:, t:t + 1], k[:, t:t + 1], v[:, t:t + 1], g[:, t:t + 1],
+                                  beta[:, t:t + 1], s)
+        assert np.array_equal(y1[:, 0], y[:, t]) and np.array_equal(s, states[:, t])
+    ym, finm, sm = OG.gated_delta(q, k, v, g, beta, s0, mask=np.array([[True, False, True]]))
+    assert np.array_equal(sm[:, 1], sm[:, 0]) and (ym[:, 1] == 0).all()

@@ -53,6 +53,12 @@ class VbMoePrefillArgs(C.Structure):
     ]
 
 
+class VbMoePrefillEpArgs(C.Structure):
+    _fields_ = [("base", VbMoePrefillArgs), ("owner", C.c_void_p), ("world", C.c_int32),
+                ("rank", C.c_int32), ("max_tokens_per_rank", C.c_int32),
+                ("reserved", C.c_int32)]
+
+
 class VbMoeRouteArgs(C.Structure):
     _fields_ = [
         ("tokens", C.c_int32), ("hidden", C.c_int32), ("num_experts", C.c_int32),
@@ -116,6 +122,8 @@ _SIGNATURES = {
     "vb_moe_decode_noalloc": (_I32, [C.POINTER(VbMoeDecodeArgs), _P]),
     "vb_moe_prefill_workspace_size": (_SZ, [_I32, _I32, _I32, _I32, _I32]),
     "vb_moe_prefill": (_I32, [C.POINTER(VbMoePrefillArgs), _P]),
+    "vb_moe_prefill_ep_workspace_size": (_SZ, [_I32, _I32, _I32, _I32, _I32, _I32, _I32]),
+    "vb_moe_prefill_ep": (_I32, [C.POINTER(VbMoePrefillEpArgs), _P, _P]),
     "vb_moe_route_workspace_size": (_SZ, [_I32, _I32, _I32]),
     "vb_moe_route": (_I32, [C.POINTER(VbMoeRouteArgs), _P]),
     "vb_moe_experts_workspace_size": (_SZ, [_I32, _I32, _I32, _I32]),
@@ -150,6 +158,8 @@ _SIGNATURES = {
                                   _I32, _I32, _I32, _I32, _I32, _I32, C.c_float, _I32, _P, _P,
                                   _P]),
     "vb_dequantize": (_I32, [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P]),
+    "vb_gated_delta_step": (_I32, [_P, _P, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _I32, _I32,
+                                   _I32, _I32, _I32, _I32, _P]),
     "vb_synth_fill_u32": (_I32, [_P, _I64, C.c_uint64, _P]),
     "vb_synth_fill_pool": (_I32, [C.POINTER(VbQuantPool), _P, _P, _I32, _I32, _I32, _I32,
                                   _I32, C.c_float, C.c_float, C.c_float, _P]),

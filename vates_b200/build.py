@@ -29,6 +29,8 @@ SOURCES = [
     "residency.cu",
     "kv_prefill_attn.cu",
     "dequant.cu",
+    "ep.cu",
+    "gdn.cu",
 ]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
@@ -67,7 +69,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
         objs = list(ex.map(lambda s: _compile(s, verbose), srcs))
     tmp = LIB + ".tmp"
-    cmd = [NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart", "-lcuda"]
+    cmd = [NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart", "-lcuda", "-ldl"]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")

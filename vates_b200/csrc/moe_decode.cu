@@ -4,8 +4,9 @@
 // :245-1013) with PersistentSubGLU.forward (compute.py:145-199) and the
 // shared expert (block.py:102-109, 1009-1012).
 //
-// One persistent kernel per block (one CTA per SM, all CTAs resident), a PDL
-// secondary of whatever ran before it on the stream. Phases:
+// One persistent kernel per block (one CTA of 16 warps per SM, all CTAs
+// resident: a cooperative launch), a PDL secondary of whatever ran before it
+// on the stream. Phases:
 //  1. Before the PDL wait: every warp loads its part of one router row
 //     (rows 0..E-1 the experts, row E the shared-expert gate) into
 //     registers, and the shared expert (it needs no routing) is
@@ -16,27 +17,33 @@
 //     bf16(x.Wr^T [+bias]) and the gate sigmoid(x.w_sg), written to global
 //     memory.
 //  3. Grid barrier (bounded wait). Every CTA then runs the same precise
-//     softmax, top-k (one warp reduction per pick on (bf16 probability,
-//     expert id) keys, lower id wins ties), renormalisation and slot gather,
-//     and builds the same list of "entries" in shared memory: the shared
-//     expert first, then every distinct routed expert in route order.
-//  4. Gate/up: DEC_ITEM_WARPS warps (one by default) take an item (entry, 16
-//     intermediate rows), split over the hidden dimension, and stream it
-//     through per-warp cp.async rings; 4-bit codes become exact bf16 values 128+q for
-//     mma.m16n8k16 and the per-group epilogue applies y += s*D + (b-128*s)*
-//     sum(x). SwiGLU (bf16 per op); h goes to global memory in fragment
-//     order and the item is counted on its entry (release).
-//  5. Down: each warp owns a contiguous entry-major range of items (entry, 16
-//     output rows); it copies their weights into its ring (the one it used
-//     for gate/up) and waits (bounded, acquire) until the entry's h is
-//     complete. Per route the result is rounded to bf16, times the route
-//     score, rounded again (MLX chain).
+//     softmax, top-k, renormalisation and slot gather (16/T warps per token:
+//     each takes the top-k candidates of its share of the logits on
+//     (bf16 probability, expert id) keys, lower id wins ties, and the token's
+//     first warp picks among them), and builds the same list of "entries" in
+//     shared memory: the shared expert first, then every distinct routed
+//     expert in route order.
+//  4. Gate/up: each CTA owns a contiguous range of items (entry, 16
+//     intermediate rows); the four warps of a group split an item along the
+//     hidden dimension and stream it through per-warp cp.async rings; 4-bit
+//     codes become exact bf16 values 128+q for mma.m16n8k16 and the
+//     per-group epilogue applies y += s*D + (b-128*s)*sum(x). The item's
+//     leader adds the four partials (fixed order) and applies SwiGLU (bf16
+//     per op); h goes to global memory in fragment order and the item is
+//     counted on its entry (release).
+//  5. Down: each CTA owns a contiguous range of items (entry, 16 output
+//     rows) dealt round-robin to its warps, which stream the weights in two
+//     chunks through their rings. The first warp to need an entry waits
+//     (bounded, acquire) until its h is complete and stages h in shared
+//     memory for the CTA. Per route the result is rounded to bf16, times the
+//     route score, rounded again (MLX chain).
 //  6. Combine: the warp completing a 16-row block (atomic ticket) adds the k
 //     routes of every token in rank order (exact double sum of bf16 values,
 //     rounded to float32 then bf16), then the gated shared expert and the
 //     optional residual.
 // Every wait is bounded (2 s); a wait that gives up sets VB_STATUS_TIMEOUT.
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -256,7 +263,7 @@ __device__ __forceinline__ bool wait_ge64(const unsigned long long *p, unsigned 
 // ----------------------------------------------------------------------------
 // Tiles and the shared-memory map of the layer kernel.
 // ----------------------------------------------------------------------------
-constexpr int KL_THREADS = 256;
+constexpr int KL_THREADS = 512;
 constexpr int KL_WARPS = KL_THREADS / 32;
 constexpr int KL_MAX_ENT = DEC_MAX_T * DEC_MAX_K + 1;
 constexpr int KL_MAX_ROUTES = DEC_MAX_T * DEC_MAX_K;
@@ -264,77 +271,91 @@ constexpr int KL_MAX_ROUTES = DEC_MAX_T * DEC_MAX_K;
 // 128-byte line (32 words apart), so that polls and atomics on different
 // counters do not queue at one L2 line.
 constexpr int KL_CSTRIDE = 32;
-// Warps that share one gate/up item (split along the hidden dimension). One
-// warp per item measured fastest (1.61 ms per 48-layer step against 1.68 ms
-// with eight): no per-item barrier, and the item's streams still overlap
-// across the warps of the SM.
-constexpr int DEC_ITEM_WARPS = 1;
+// Gate/up: an item (entry, 16 intermediate rows) is split along the hidden
+// dimension over the GU_S warps of a group; their partial sums meet in
+// shared memory and the item's leader applies SwiGLU.
+constexpr int GU_S = 4;
+constexpr int GU_NGRP = KL_WARPS / GU_S;
+// Down: the entries whose h a CTA stages in shared memory (its down items
+// are one contiguous range shorter than an entry's 2048 / 16 row blocks, so
+// they span at most two entries).
+constexpr int KL_HSLOTS = 2;
 
 constexpr int align_c(int x, int a) { return (x + a - 1) / a * a; }
 
 constexpr int KL_SMEM_MAX = 227 * 1024;
 
-// 16-byte unit u of row r of a staged tile lives at unit swz(r, u): the four
-// rows g = 0..3 that one half-warp reads with 8-byte fragment loads (units
-// 2G and 2G+1 of each row) then fall on distinct banks. U = units per row.
+// 16-byte unit u of row r of a staged tile lives at unit swz<U>(r, u): the
+// four rows g = 0..3 that one half-warp reads with 8-byte fragment loads
+// (units 2G and 2G+1 of each row) then fall on distinct banks. U = units per
+// row (rows of 32 bytes need no swizzle).
 template <int U>
 __device__ __forceinline__ int swz(int r, int u) {
-  return U >= 8 ? u ^ ((r & 3) << 1) : u ^ (((r >> 1) & 1) << 1);
+  return U >= 8 ? u ^ ((r & 3) << 1) : (U == 4 ? u ^ (((r >> 1) & 1) << 1) : u);
 }
 
 template <int H, int I>
 struct LayerTile {
   // Router: a row is split over Q warps, NVQ uint4 of the row part per lane.
-  static constexpr int Q = H >= 1024 ? 2 : 1;
+  static constexpr int Q = H >= 2048 ? 4 : (H >= 1024 ? 2 : 1);
   static constexpr int RPC = KL_WARPS / Q;  // rows per CTA and round
   static constexpr int NVQ = H / (256 * Q);
-  // Gate/up: an item (entry, 16 intermediate rows) is split along the hidden
-  // dimension over the S warps of a group; each warp streams CPW chunks of
-  // it (16 rows x 4 groups of 64 columns of gate and up plus their scales).
+  // Gate/up: chunks of CG groups of 64 columns of the item's 16 gate and 16
+  // up rows; a warp streams the KP groups of its part of the hidden
+  // dimension, CPW chunks per item.
   static constexpr int NG = H / 64;
-  static constexpr int CG = 4;
-  static constexpr int NCH = NG / CG;
-  static constexpr int S = NCH < DEC_ITEM_WARPS ? NCH : DEC_ITEM_WARPS;  // warps per item
-  static constexpr int NGRP = KL_WARPS / S;                  // item groups per CTA
-  static constexpr int CPW = NCH / S;                        // chunks per warp and item
+  static constexpr int CG = 2;
+  static constexpr int KP = NG / GU_S;
+  static constexpr int CPW = KP / CG;
   static constexpr int ROWB = H / 2;         // packed bytes per row
-  static constexpr int CROW = CG * 32;       // chunk bytes per row (8 units)
+  static constexpr int CROW = CG * 32;       // chunk bytes per row (4 units)
   static constexpr int NS64 = H / 64;        // scales per row at group 64
   static constexpr int WB = 2 * 16 * CROW;   // gate + up codes of a chunk
-  static constexpr int CHUNK = WB + 4 * 16 * 8;
-  // Down: item (entry, 16 output rows) per warp, one ring stage each.
+  static constexpr int CHUNK = WB + 4 * 16 * 4;  // + one scale word per tensor and row
+  // Down: an item (entry, 16 output rows) in DCH chunks of DG groups; every
+  // chunk also carries the item's whole 16-row scale/bias block.
   static constexpr int NGI = I / 64;
-  static constexpr int DROWB = I / 2;
+  static constexpr int DCH = NGI >= 2 ? 2 : 1;
+  static constexpr int DG = NGI / DCH;
+  static constexpr int DROWB = DG * 32;
   static constexpr int DWB = 16 * DROWB;
-  static constexpr int DSB = 16 * NGI * 2;  // 16 rows of one scale tensor at group 64
+  static constexpr int DSB = 16 * NGI * 2;   // 16 rows of one scale tensor at group 64
   static constexpr int DSLOT = DWB + 2 * DSB;
+  static constexpr int STAGE = align_c(CHUNK > DSLOT ? CHUNK : DSLOT, 128);
   // Shared memory: x fragments [NG][8][4][8] words, group sums [NG][8],
-  // entries, route flags, a few words, item partials [2][warp][lane][8],
-  // per-warp h tiles [16][8], then one ring per warp.
+  // staged h [slot][8 tokens][NGI][4][8] words with group sums
+  // [slot][NGI][8], item partials [2][warp][lane][8], entries, route flags,
+  // a few words, then one ring per warp.
   static constexpr int XF = NG * DEC_MAX_T * 4 * 8 * 4;
   static constexpr int OFF_XS = XF;
-  static constexpr int OFF_ENT = OFF_XS + NG * DEC_MAX_T * 4;
+  static constexpr int HF = DEC_MAX_T * NGI * 32 * 4;
+  static constexpr int OFF_HF = OFF_XS + NG * DEC_MAX_T * 4;
+  static constexpr int OFF_HSG = OFF_HF + KL_HSLOTS * HF;
+  static constexpr int OFF_RED = align_c(OFF_HSG + KL_HSLOTS * NGI * DEC_MAX_T * 4, 128);
+  static constexpr int OFF_ENT = OFF_RED + 2 * KL_WARPS * 32 * 8 * 4;
   static constexpr int OFF_OK = OFF_ENT + KL_MAX_ENT * (int)sizeof(DecEntry);
   static constexpr int OFF_MISC = OFF_OK + KL_MAX_ROUTES * 4;
-  static constexpr int OFF_RED = align_c(OFF_MISC + 64, 128);
-  static constexpr int OFF_HB = OFF_RED + 2 * KL_WARPS * 32 * 8 * 4;
-  static constexpr int OFF_RING = align_c(OFF_HB + KL_WARPS * 16 * 8 * 4, 128);
-  static constexpr int RS0 = (KL_SMEM_MAX - OFF_RING) / (KL_WARPS * CHUNK);
-  static constexpr int RS = RS0 < 6 ? RS0 : 6;  // ring stages (chunks) per warp
-  static constexpr int RING = RS * CHUNK;
+  static constexpr int OFF_RING = align_c(OFF_MISC + 64, 128);
+  static constexpr int RS0 = (KL_SMEM_MAX - OFF_RING) / (KL_WARPS * STAGE);
+  static constexpr int RS = RS0 < 4 ? RS0 : 4;  // ring stages per warp
+  static constexpr int RING = RS * STAGE;
   static constexpr int SMEM = OFF_RING + KL_WARPS * RING;
   // Router and routing temporaries, inside the rings (free until the
   // entries are built): x [8][H] bf16, slot table, first route of each
-  // expert, routes (expert, slot, score, entry), reduction scratch.
+  // expert, routes (expert, slot, score, entry), reductions, candidates.
   static constexpr int TMP_TABLE = DEC_MAX_T * H * 2;
   static constexpr int TMP_FIRST = TMP_TABLE + DEC_MAX_E * 4;
   static constexpr int TMP_ROUTE = TMP_FIRST + DEC_MAX_E * 4;
   static constexpr int TMP_RED = TMP_ROUTE + 4 * KL_MAX_ROUTES * 4;
   static constexpr int TMP_PART = TMP_RED + KL_WARPS * DEC_MAX_T * 8;
-  static constexpr int TMP_END = TMP_PART + KL_WARPS * DEC_MAX_T * 4;
+  static constexpr int TMP_WMAX = TMP_PART + KL_WARPS * DEC_MAX_T * 4;
+  static constexpr int TMP_WSUM = TMP_WMAX + KL_WARPS * 4;
+  static constexpr int TMP_CAND = TMP_WSUM + KL_WARPS * 8;
+  static constexpr int TMP_END = TMP_CAND + KL_WARPS * DEC_MAX_K * 4;
   static_assert(TMP_END <= KL_WARPS * RING, "router temporaries");
   static_assert(SMEM <= KL_SMEM_MAX, "layer kernel shared memory");
-  static_assert(RS >= 2 && DSLOT <= CHUNK && NVQ >= 1 && NCH % S == 0, "layer tile");
+  static_assert(RS >= 2 && NVQ >= 1 && KP % CG == 0 && CPW >= 1 && DG >= 1, "layer tile");
+  static_assert(KP % 2 == 0, "a chunk's scale word starts at an even group");
 };
 
 struct GateUpItem {
@@ -355,53 +376,56 @@ __device__ __forceinline__ void gateup_item(const VbQuantPool &pool, int slot, i
   it.sc[3] = pool_ptr(pool, 5, slot) + sb;
 }
 
-// Chunk ch (codes and scales) of an item into a ring stage.
+// First scale of the groups [g0, g0 + CG) of a gate/up chunk, rounded down
+// to an even index: the 4-byte word holding the chunk's scales.
+__device__ __forceinline__ int gu_scale_word(int g0, int gs) { return (g0 >> gs) & ~1; }
+
+// Chunk (codes of groups [g0, g0 + CG) and their scale words) of an item
+// into a ring stage: [2 matrices][16 rows][CROW] swizzled, then
+// [4 tensors][16 rows] scale words.
 template <int H, int I>
-__device__ __forceinline__ void gateup_chunk(uint8_t *stage, const GateUpItem &it, int ch,
+__device__ __forceinline__ void gateup_chunk(uint8_t *stage, const GateUpItem &it, int g0,
                                              int lane, int gs) {
   using Tl = LayerTile<H, I>;
-  // 2 matrices x 16 rows x 8 units of 16 bytes; lane -> unit lane%8 of
-  // rows lane/8 + 4j, stored swizzled in 128-byte rows.
-  const int r0 = lane >> 3, un = lane & 7;
-  const uint8_t *g = it.gw + r0 * Tl::ROWB + ch * Tl::CROW + un * 16;
-  const uint8_t *u = it.uw + r0 * Tl::ROWB + ch * Tl::CROW + un * 16;
+  // 2 matrices x 16 rows x 4 units of 16 bytes: lane -> unit lane % 4 of
+  // rows lane / 4 and lane / 4 + 8.
+  const int r0 = lane >> 2, un = lane & 3;
+  const size_t cb = (size_t)g0 * 32 + un * 16;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int r = r0 + 4 * j;
-    uint8_t *d = stage + r * Tl::CROW + (swz<8>(r, un) << 4);
-    cp_async16(d, g + 4 * j * Tl::ROWB);
-    cp_async16(d + 16 * Tl::CROW, u + 4 * j * Tl::ROWB);
+  for (int j = 0; j < 2; ++j) {
+    const int r = r0 + 8 * j;
+    uint8_t *d = stage + r * Tl::CROW + (swz<4>(r, un) << 4);
+    cp_async16(d, it.gw + (size_t)r * Tl::ROWB + cb);
+    cp_async16(d + 16 * Tl::CROW, it.uw + (size_t)r * Tl::ROWB + cb);
   }
-  // Scales: 4 tensors x 16 rows x SCB bytes -> [tensor][row][SCB].
-  const int ns = Tl::NS64 >> gs, scb = (Tl::CG >> gs) * 2;
+  // Scale words: 4 tensors x 16 rows, two per lane.
+  const int ns = Tl::NS64 >> gs, w0 = gu_scale_word(g0, gs);
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
     const int piece = lane + 32 * k, a = piece >> 4, r = piece & 15;
-    const uint8_t *src = it.sc[a] + r * ns * 2 + ch * scb;
-    uint8_t *dst = stage + Tl::WB + piece * scb;
-    if (scb == 8) cp_async8(dst, src);
-    else cp_async4(dst, src);
+    cp_async4(stage + Tl::WB + piece * 4, it.sc[a] + ((size_t)r * ns + w0) * 2);
   }
 }
 
-// Weights of down item (slot, 16-row block rb) into a ring slot:
-// [16 rows x DROWB] codes (swizzled units), then [16 rows x NSI] scales and
-// biases.
+// Chunk dc of down item (slot, 16-row block rb) into a ring stage:
+// [16 rows][DROWB] codes (swizzled units), then the item's [16 rows][NSI]
+// scales and biases.
 template <int H, int I>
-__device__ __forceinline__ void down_issue(uint8_t *slot, const VbQuantPool &pool, int pslot,
-                                           int rb, int lane, int gs) {
+__device__ __forceinline__ void down_chunk(uint8_t *stage, const VbQuantPool &pool, int pslot,
+                                           int rb, int dc, int lane, int gs) {
   using Tl = LayerTile<H, I>;
-  const uint8_t *dw = pool_ptr(pool, 6, pslot) + (size_t)rb * 16 * Tl::DROWB;
+  const uint8_t *dw = pool_ptr(pool, 6, pslot) + (size_t)rb * 16 * (I / 2) + dc * Tl::DROWB;
   constexpr int CPR = Tl::DROWB / 16;  // 16-byte units per row
 #pragma unroll
-  for (int j = 0; j < 16 * CPR / 32; ++j) {
+  for (int j = 0; j < (16 * CPR + 31) / 32; ++j) {
     const int q = lane + 32 * j, r = q / CPR, un = q % CPR;
-    cp_async16(slot + r * Tl::DROWB + (swz<CPR>(r, un) << 4), dw + r * Tl::DROWB + un * 16);
+    if (q < 16 * CPR)
+      cp_async16(stage + r * Tl::DROWB + (swz<CPR>(r, un) << 4), dw + (size_t)r * (I / 2) + un * 16);
   }
   const int sb = 16 * (Tl::NGI >> gs) * 2, sch = sb / 16;
   for (int q = lane; q < 2 * sch; q += 32) {
     const int t = q / sch, cc = q % sch;
-    cp_async16(slot + Tl::DWB + t * sb + cc * 16,
+    cp_async16(stage + Tl::DWB + t * sb + cc * 16,
                pool_ptr(pool, 7 + t, pslot) + (size_t)rb * sb + cc * 16);
   }
 }
@@ -463,25 +487,35 @@ __device__ __forceinline__ void down_combine_rows(const DecodeParams &p, const i
   }
 }
 
+
 // Routing of all T tokens, run identically by every CTA of the layer kernel
-// (all 256 threads call it): precise softmax of the logits, top-k, optional
-// renormalisation, slot gather, then the entry list. Results in shared
-// memory (routes rex/rslot/rscore/rent, flags ok, entries ent); the
-// returned value is the number of entries. primary: this CTA also writes the
-// optional outputs and the status bits.
-template <int PER>  // PER = ceil(E / 32) logits per lane
+// (all threads call it): precise softmax of the logits, top-k, optional
+// renormalisation, slot gather, then the entry list. Token t is handled by
+// the wpt warps t*wpt .. t*wpt + wpt - 1, each over PERW * 32 of the E
+// logits: the maximum and the exponential sum meet in shared memory (summed
+// in warp order), every warp selects its own top-k candidates, and the
+// token's first warp picks the top-k of the wpt*k candidates. Keys are the
+// bf16 probability bits above (0xFFFF - expert id), so the unsigned maximum
+// is the largest probability with ties to the lower id. Results in shared
+// memory (routes rex/rslot/rscore/rent, flags ok, entries ent); returns the
+// number of entries. primary: this CTA also writes the optional outputs and
+// the status bits.
+template <int PERW>
 __device__ __noinline__ int route_tokens(const float *logits, const int32_t *table, int T, int E,
-                                         int k, int norm_topk, int has_shared, int cap,
+                                         int k, int wpt, int norm_topk, int has_shared, int cap,
                                          bool primary, int32_t *status, int32_t *out_inds,
                                          uint16_t *out_scores, int32_t *out_local,
                                          int *s_table, int *s_first, int *s_rex, int *s_rslot,
                                          float *s_rscore, int *s_rent, int32_t *s_ok,
-                                         DecEntry *s_ent, int *s_wcnt) {
+                                         DecEntry *s_ent, int *s_wcnt, uint32_t *s_wmax,
+                                         double *s_wsum, uint32_t *s_cand) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int t = warp / wpt, wp = warp - t * wpt;
+  const bool act = t < T;
+  const int base = wp * PERW * 32;
   // Slot table and logits are loaded together (one memory round trip).
-  float v[PER];
+  float v[PERW];
   {
-    const int t = warp;
     int tb[(DEC_MAX_E + KL_THREADS - 1) / KL_THREADS];
 #pragma unroll
     for (int j = 0; j < (DEC_MAX_E + KL_THREADS - 1) / KL_THREADS; ++j) {
@@ -489,9 +523,9 @@ __device__ __noinline__ int route_tokens(const float *logits, const int32_t *tab
       tb[j] = i < E ? __ldg(table + i) : -1;
     }
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int idx = lane + 32 * i;
-      v[i] = (t < T && idx < E) ? __ldcg(logits + (size_t)t * E + idx) : -INFINITY;
+    for (int i = 0; i < PERW; ++i) {
+      const int idx = base + lane + 32 * i;
+      v[i] = (act && idx < E) ? __ldcg(logits + (size_t)t * E + idx) : -INFINITY;
     }
 #pragma unroll
     for (int j = 0; j < (DEC_MAX_E + KL_THREADS - 1) / KL_THREADS; ++j) {
@@ -502,62 +536,82 @@ __device__ __noinline__ int route_tokens(const float *logits, const int32_t *tab
       }
     }
   }
+  uint32_t mk = 0;
+#pragma unroll
+  for (int i = 0; i < PERW; ++i) mk = max(mk, f2key(v[i]));
+  mk = __reduce_max_sync(0xffffffffu, mk);
+  if (lane == 0) s_wmax[warp] = mk;
   __syncthreads();
-  for (int t = warp; t < T; t += KL_WARPS) {
-    uint32_t mk = 0;
+  uint32_t mt = 0;
+  if (act)
+    for (int w = 0; w < wpt; ++w) mt = max(mt, s_wmax[t * wpt + w]);
+  const float m = key2f(mt);
+  double sd[PERW];
 #pragma unroll
-    for (int i = 0; i < PER; ++i) mk = max(mk, f2key(v[i]));
-    const float m = key2f(__reduce_max_sync(0xffffffffu, mk));
-    double sd[PER];
+  for (int i = 0; i < PERW; ++i) {
+    const int idx = base + lane + 32 * i;
+    const float ex = (act && idx < E) ? expf(__fsub_rn(v[i], m)) : 0.f;
+    v[i] = ex;
+    sd[i] = (double)ex;
+  }
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int idx = lane + 32 * i;
-      const float ex = idx < E ? expf(__fsub_rn(v[i], m)) : 0.f;
-      v[i] = ex;
-      sd[i] = (double)ex;
+  for (int w = 1; w < PERW; w *= 2)
+#pragma unroll
+    for (int i = 0; i + w < PERW; i += 2 * w) sd[i] += sd[i + w];
+  double s = sd[0];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) s_wsum[warp] = s;
+  __syncthreads();
+  double st = 0.0;
+  if (act)
+    for (int w = 0; w < wpt; ++w) st += s_wsum[t * wpt + w];
+  const float inv = act ? __frcp_rn((float)st) : 0.f;
+  // This warp's top-k candidates (keys are distinct: one lane holds each).
+  uint32_t key[PERW], lb = 0;
+#pragma unroll
+  for (int i = 0; i < PERW; ++i) {
+    const int idx = base + lane + 32 * i;
+    key[i] = (act && idx < E) ? ((uint32_t)f2bf(__fmul_rn(v[i], inv)) << 16) | (0xFFFFu - idx) : 0u;
+    lb = max(lb, key[i]);
+  }
+  uint32_t mine = 0;
+  for (int r = 0; r < k; ++r) {
+    const uint32_t best = __reduce_max_sync(0xffffffffu, lb);
+    if (lb == best && best != 0u) {
+      lb = 0;
+#pragma unroll
+      for (int i = 0; i < PERW; ++i) {
+        if (key[i] == best) key[i] = 0u;
+        lb = max(lb, key[i]);
+      }
     }
-    // Pairwise sum (float sums of a few hundred exponentials are exact in
-    // double, so the order does not matter).
+    if (lane == r) mine = best;
+  }
+  if (act && lane < k) s_cand[warp * k + lane] = mine;
+  __syncthreads();
+  if (act && wp == 0) {
+    // The token's top-k among its wpt * k candidates (at most 16 * 16).
+    const int nc = wpt * k;
+    uint32_t c[8];
+    lb = 0;
 #pragma unroll
-    for (int w = 1; w < PER; w *= 2)
-#pragma unroll
-      for (int i = 0; i + w < PER; i += 2 * w) sd[i] += sd[i + w];
-    double s = sd[0];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const float inv = __frcp_rn((float)s);
-    // Keys: bf16 probability bits above (0xFFFF - expert id), so the unsigned
-    // maximum is the largest probability with ties to the lower id.
-    uint32_t key[PER];
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int idx = lane + 32 * i;
-      key[i] = idx < E ? ((uint32_t)f2bf(__fmul_rn(v[i], inv)) << 16) | (0xFFFFu - idx) : 0u;
+    for (int j = 0; j < 8; ++j) {
+      const int q = lane + 32 * j;
+      c[j] = q < nc ? s_cand[t * wpt * k + q] : 0u;
+      lb = max(lb, c[j]);
     }
-    // Each lane sorts its keys (descending bitonic network); a pick is then
-    // one warp maximum of the lanes' heads, and the lane holding it pops.
-#pragma unroll
-    for (int size = 2; size <= PER; size <<= 1)
-#pragma unroll
-      for (int stride = size >> 1; stride > 0; stride >>= 1)
-#pragma unroll
-        for (int i = 0; i < PER; ++i) {
-          const int j = i ^ stride;
-          if (j > i) {
-            const uint32_t a = key[i], b = key[j];
-            const bool desc = (i & size) == 0;
-            key[i] = desc ? max(a, b) : min(a, b);
-            key[j] = desc ? min(a, b) : max(a, b);
-          }
-        }
     double ssum = 0.0;
     uint32_t sel = 0;
     for (int r = 0; r < k; ++r) {
-      const uint32_t best = __reduce_max_sync(0xffffffffu, key[0]);
-      if (key[0] == best) {  // keys are distinct: one lane holds it
+      const uint32_t best = __reduce_max_sync(0xffffffffu, lb);
+      if (lb == best) {
+        lb = 0;
 #pragma unroll
-        for (int i = 0; i + 1 < PER; ++i) key[i] = key[i + 1];
-        key[PER - 1] = 0u;
+        for (int j = 0; j < 8; ++j) {
+          if (c[j] == best) c[j] = 0u;
+          lb = max(lb, c[j]);
+        }
       }
       if (lane == r) sel = best;
       ssum += (double)bf2f(best >> 16);
@@ -652,20 +706,22 @@ template <int H, int I>
 __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p) {
   using Tl = LayerTile<H, I>;
   constexpr int Q = Tl::Q, RPC = Tl::RPC, NVQ = Tl::NVQ, NG = Tl::NG, CG = Tl::CG,
-                S = Tl::S, NGRP = Tl::NGRP, CPW = Tl::CPW, RS = Tl::RS, NGI = Tl::NGI;
+                KP = Tl::KP, CPW = Tl::CPW, RS = Tl::RS, NGI = Tl::NGI, DCH = Tl::DCH,
+                DG = Tl::DG;
   constexpr int RB = I / 16;    // gate/up items per entry
   constexpr int RBN = H / 16;   // down items per entry
   extern __shared__ __align__(128) uint8_t smem[];
   uint32_t *xf = reinterpret_cast<uint32_t *>(smem);  // [NG][8][4][8] words
   float *xsm = reinterpret_cast<float *>(smem + Tl::OFF_XS);  // [NG][8]
+  uint32_t *hf = reinterpret_cast<uint32_t *>(smem + Tl::OFF_HF);  // [slot][8][NGI][4][8]
+  float *hsg = reinterpret_cast<float *>(smem + Tl::OFF_HSG);      // [slot][NGI][8]
   DecEntry *s_ent = reinterpret_cast<DecEntry *>(smem + Tl::OFF_ENT);
   int32_t *s_ok = reinterpret_cast<int32_t *>(smem + Tl::OFF_OK);
-  int *s_misc = reinterpret_cast<int *>(smem + Tl::OFF_MISC);
+  int *s_misc = reinterpret_cast<int *>(smem + Tl::OFF_MISC);  // [0] entries, [1] abort, [4..] h slot flags
   uint8_t *rings = smem + Tl::OFF_RING;
   uint16_t *xb = reinterpret_cast<uint16_t *>(rings);  // [T][H] bf16 (router phase)
   double *s_dred = reinterpret_cast<double *>(rings + Tl::TMP_RED);
   float *s_part = reinterpret_cast<float *>(rings + Tl::TMP_PART);
-  __shared__ float s_inv[DEC_MAX_T];
   __shared__ int s_wcnt[KL_WARPS];
   __shared__ unsigned long long s_tm[3];
 
@@ -692,6 +748,7 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
     if (piece < expert_pieces(p)) prefetch_expert_piece(p, p.shared, 0, piece);
   }
   if (tid < 3) s_tm[tid] = 0ull;
+  if (tid < KL_HSLOTS) s_misc[4 + tid] = 0;
   pdl_wait();
   pdl_launch_dependents();
   trace_mark(p.trace, 2);
@@ -873,16 +930,25 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
     int *s_rslot = s_rex + KL_MAX_ROUTES;
     float *s_rscore = reinterpret_cast<float *>(s_rslot + KL_MAX_ROUTES);
     int *s_rent = reinterpret_cast<int *>(s_rscore + KL_MAX_ROUTES);
+    uint32_t *s_wmax = reinterpret_cast<uint32_t *>(rings + Tl::TMP_WMAX);
+    double *s_wsum = reinterpret_cast<double *>(rings + Tl::TMP_WSUM);
+    uint32_t *s_cand = reinterpret_cast<uint32_t *>(rings + Tl::TMP_CAND);
     const float *lg = wsp<const float>(p, p.L.logits);
     const bool primary = blockIdx.x == 0;
+    const int tp = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
+    const int wpt = KL_WARPS / tp;
+    const int need = (E + wpt * 32 - 1) / (wpt * 32);  // logits per lane
     int n;
-#define VB_ROUTE(PER)                                                                           \
-  route_tokens<PER>(lg, p.table, T, E, p.k, p.norm_topk, p.has_shared, p.pool.cap, primary,     \
-                    p.status, p.out_inds, p.out_scores, p.out_local, s_table, s_first, s_rex,   \
-                    s_rslot, s_rscore, s_rent, s_ok, s_ent, s_wcnt)
-    if (E <= 256) n = VB_ROUTE(8);
-    else if (E <= 512) n = VB_ROUTE(16);
-    else n = VB_ROUTE(32);
+#define VB_ROUTE(PERW)                                                                         \
+  route_tokens<PERW>(lg, p.table, T, E, p.k, wpt, p.norm_topk, p.has_shared, p.pool.cap,       \
+                     primary, p.status, p.out_inds, p.out_scores, p.out_local, s_table,        \
+                     s_first, s_rex, s_rslot, s_rscore, s_rent, s_ok, s_ent, s_wcnt, s_wmax,   \
+                     s_wsum, s_cand)
+    if (need <= 1) n = VB_ROUTE(1);
+    else if (need <= 2) n = VB_ROUTE(2);
+    else if (need <= 4) n = VB_ROUTE(4);
+    else if (need <= 8) n = VB_ROUTE(8);
+    else n = VB_ROUTE(16);
 #undef VB_ROUTE
     if (tid == 0) s_misc[0] = n;
   }
@@ -896,45 +962,48 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
 
   // ---------------- 4. gate/up + SwiGLU ----------------
   uint8_t *ring = rings + warp * Tl::RING;
-  float *red = reinterpret_cast<float *>(smem + Tl::OFF_RED);            // [2][warp][lane][8]
-  float *hbuf = reinterpret_cast<float *>(smem + Tl::OFF_HB) + warp * 128;  // [16][8]
+  float *red = reinterpret_cast<float *>(smem + Tl::OFF_RED);  // [2][warp][lane][8]
   unsigned *ent_done = wsp<unsigned>(p, p.L.ent_done);
-  // Each warp runs one sequence of jobs through its ring: its gate/up chunks,
-  // then its down items, so the down weights stream in as soon as gate/up
-  // stages free up.
-  // Gate/up: this group's items blockIdx.x + G * (grp + NGRP * r), r = 0,
-  // 1, ...; warp wi of the group takes chunks [wi * CPW, (wi + 1) * CPW).
-  const int grp = warp / S, wi = warp % S;
-  const int first = blockIdx.x + G * grp, step = G * NGRP;
+  // Each warp runs one sequence of jobs through its ring: its gate/up
+  // chunks, then its down chunks, so the down weights stream in as soon as
+  // gate/up stages free up.
+  // Gate/up: this CTA's items are the contiguous range [a0, a1) of
+  // (entry, row block) pairs; group grp takes items a0 + grp + GU_NGRP r,
+  // and warp wi of the group the groups [wi KP, (wi + 1) KP) of each.
+  const int grp = warp / GU_S, wi = warp % GU_S;
   const int n_items = n_ent * RB;
-  const int nq_gu = (first < n_items ? (n_items - 1 - first) / step + 1 : 0) * CPW;
-  // Down: a contiguous entry-major range of items per warp (warps of
-  // consecutive global index sit on different SMs), so a warp mostly loads
-  // one entry's h.
-  const int nw = G * KL_WARPS;
-  const int wg = blockIdx.x + G * warp;
+  const int a0 = (int)(((long long)n_items * blockIdx.x) / G);
+  const int a1 = (int)(((long long)n_items * (blockIdx.x + 1)) / G);
+  const int my_items = a1 - a0 > grp ? (a1 - a0 - grp + GU_NGRP - 1) / GU_NGRP : 0;
+  const int nq_gu = my_items * CPW;
+  // Down: this CTA's items are the contiguous range [d0, d1) of (entry,
+  // 16-row block) pairs, dealt round-robin over the warps.
   const int n_items_d = n_ent * RBN;
-  const int d0 = (int)(((long long)n_items_d * wg) / nw);
-  const int nj = (int)(((long long)n_items_d * (wg + 1)) / nw) - d0;
+  const int d0 = (int)(((long long)n_items_d * blockIdx.x) / G);
+  const int d1 = (int)(((long long)n_items_d * (blockIdx.x + 1)) / G);
+  const int nj = d1 - d0 > warp ? (d1 - d0 - warp + KL_WARPS - 1) / KL_WARPS : 0;
+  const int e_lo = d0 / RBN;
   int j_end = nj;
   GateUpItem cur;
   int issue_q = 0;
+  const int nq = nq_gu + nj * DCH;
   auto issue_next = [&]() {
-    uint8_t *stage = ring + (issue_q % RS) * Tl::CHUNK;
+    uint8_t *stage = ring + (issue_q % RS) * Tl::STAGE;
     if (issue_q < nq_gu) {
-      const int r = issue_q / CPW, ch = wi * CPW + issue_q % CPW;
-      const int i = first + r * step;
-      if (issue_q % CPW == 0) {
+      const int r = issue_q / CPW, ch = issue_q % CPW;
+      const int i = a0 + grp + GU_NGRP * r;
+      if (ch == 0) {
         const int e = i / RB;
         if (p.has_shared && e == 0) gateup_item<H, I>(p.shared, 0, i % RB, gs, cur);
         else gateup_item<H, I>(p.pool, s_ent[e].slot, i % RB, gs, cur);
       }
-      gateup_chunk<H, I>(stage, cur, ch, lane, gs);
-    } else if (issue_q - nq_gu < nj) {
-      const int i = d0 + (issue_q - nq_gu);
+      gateup_chunk<H, I>(stage, cur, wi * KP + ch * CG, lane, gs);
+    } else if (issue_q < nq) {
+      const int jj = (issue_q - nq_gu) / DCH, dc = (issue_q - nq_gu) % DCH;
+      const int i = d0 + warp + KL_WARPS * jj;
       const int e = i / RBN, rb = i % RBN;
       const bool sh = p.has_shared && e == 0;
-      down_issue<H, I>(stage, sh ? p.shared : p.pool, sh ? 0 : s_ent[e].slot, rb, lane, gs);
+      down_chunk<H, I>(stage, sh ? p.shared : p.pool, sh ? 0 : s_ent[e].slot, rb, dc, lane, gs);
     }
     cp_async_commit();
     ++issue_q;
@@ -942,36 +1011,33 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
 #pragma unroll 1
   for (int kq = 0; kq < RS - 1; ++kq) issue_next();
   {
-    const int scb = (CG >> gs) * 2;
     // Fragment offsets inside a staged chunk (rows g and g+8 share a swizzle).
     int fo[CG];
 #pragma unroll
-    for (int gl = 0; gl < CG; ++gl) fo[gl] = g * Tl::CROW + (swz<8>(g, 2 * gl + (c >> 1)) << 4) + (c & 1) * 8;
+    for (int gl = 0; gl < CG; ++gl) fo[gl] = g * Tl::CROW + (swz<4>(g, 2 * gl + (c >> 1)) << 4) + (c & 1) * 8;
     float accg[4], accu[4];
 #pragma unroll 1
     for (int q = 0; q < nq_gu; ++q) {
-      const int r = q / CPW, cq = q % CPW, ch = wi * CPW + cq;
-      const int item = first + r * step;
+      const int r = q / CPW, ch = q % CPW;
+      const int li = grp + GU_NGRP * r;  // item index inside this CTA's range
       cp_async_wait<RS - 2>();
       __syncwarp();
       issue_next();  // into the stage consumed one chunk ago
-      if (cq == 0) {
+      if (ch == 0) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) accg[j] = accu[j] = 0.f;
       }
-      const uint8_t *st = ring + (q % RS) * Tl::CHUNK;
-      // Scales of this chunk's groups for rows g and g+8: gate s, gate b,
-      // up s, up b.
-      uint2 sv[8];
+      const uint8_t *st = ring + (q % RS) * Tl::STAGE;
+      const int g0 = wi * KP + ch * CG;
+      const int w0 = gu_scale_word(g0, gs);
+      // Scale words of rows g and g+8: gate s, gate b, up s, up b.
+      uint32_t sv[8];
 #pragma unroll
-      for (int a = 0; a < 8; ++a) {
-        const uint8_t *sp = st + Tl::WB + ((a >> 1) * 16 + ((a & 1) ? g + 8 : g)) * scb;
-        if (scb == 8) sv[a] = *reinterpret_cast<const uint2 *>(sp);
-        else sv[a] = make_uint2(*reinterpret_cast<const uint32_t *>(sp), 0u);
-      }
+      for (int a = 0; a < 8; ++a)
+        sv[a] = *reinterpret_cast<const uint32_t *>(st + Tl::WB + ((a >> 1) * 16 + ((a & 1) ? g + 8 : g)) * 4);
 #pragma unroll
       for (int gl = 0; gl < CG; ++gl) {
-        const int Gi = ch * CG + gl;
+        const int Gi = g0 + gl;
         uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0;
         if (g < T) {
           const uint4 *xp = reinterpret_cast<const uint4 *>(xf + ((Gi * DEC_MAX_T + g) * 4 + c) * 8);
@@ -1002,53 +1068,55 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
           mma_bf16(du, pu0[h][i0], pu1[h][i0], pu0[h][i0 + 1], pu1[h][i0 + 1], xw[2 * m],
                    xw[2 * m + 1]);
         }
-        const int si = gl >> gs;
-        const float sg0 = bf_at2(sv[0], si), sg1 = bf_at2(sv[1], si);
-        const float bg0 = bf_at2(sv[2], si), bg1 = bf_at2(sv[3], si);
-        const float su0 = bf_at2(sv[4], si), su1 = bf_at2(sv[5], si);
-        const float bu0 = bf_at2(sv[6], si), bu1 = bf_at2(sv[7], si);
+        // The group's scale is half (Gi >> gs) - w0 of the chunk's word.
+        const bool hi = ((Gi >> gs) - w0) != 0;
+        auto sc = [&](uint32_t w) { return hi ? bf_hi(w) : bf_lo(w); };
+        const float sg0 = sc(sv[0]), sg1 = sc(sv[1]), bg0 = sc(sv[2]), bg1 = sc(sv[3]);
+        const float su0 = sc(sv[4]), su1 = sc(sv[5]), bu0 = sc(sv[6]), bu1 = sc(sv[7]);
         const float bpg0 = fmaf(-128.f, sg0, bg0), bpg1 = fmaf(-128.f, sg1, bg1);
         const float bpu0 = fmaf(-128.f, su0, bu0), bpu1 = fmaf(-128.f, su1, bu1);
-        accg[0] += fmaf(sg0, dg[0], bpg0 * xs.x);
-        accg[1] += fmaf(sg0, dg[1], bpg0 * xs.y);
-        accg[2] += fmaf(sg1, dg[2], bpg1 * xs.x);
-        accg[3] += fmaf(sg1, dg[3], bpg1 * xs.y);
-        accu[0] += fmaf(su0, du[0], bpu0 * xs.x);
-        accu[1] += fmaf(su0, du[1], bpu0 * xs.y);
-        accu[2] += fmaf(su1, du[2], bpu1 * xs.x);
-        accu[3] += fmaf(su1, du[3], bpu1 * xs.y);
+        accg[0] = fmaf(bpg0, xs.x, fmaf(sg0, dg[0], accg[0]));
+        accg[1] = fmaf(bpg0, xs.y, fmaf(sg0, dg[1], accg[1]));
+        accg[2] = fmaf(bpg1, xs.x, fmaf(sg1, dg[2], accg[2]));
+        accg[3] = fmaf(bpg1, xs.y, fmaf(sg1, dg[3], accg[3]));
+        accu[0] = fmaf(bpu0, xs.x, fmaf(su0, du[0], accu[0]));
+        accu[1] = fmaf(bpu0, xs.y, fmaf(su0, du[1], accu[1]));
+        accu[2] = fmaf(bpu1, xs.x, fmaf(su1, du[2], accu[2]));
+        accu[3] = fmaf(bpu1, xs.y, fmaf(su1, du[3], accu[3]));
       }
-      if (cq == CPW - 1) {
+      if (ch == CPW - 1) {
         // Group hand-off: every warp's partials to the item's leader, which
         // adds them in warp order and applies SwiGLU.
         const int b = r & 1;
         float *mine = red + ((b * KL_WARPS + warp) * 32 + lane) * 8;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          mine[j] = accg[j];
-          mine[4 + j] = accu[j];
-        }
-        named_bar(1 + grp, S * 32);
-        if (wi == r % S) {
+        *reinterpret_cast<float4 *>(mine) = make_float4(accg[0], accg[1], accg[2], accg[3]);
+        *reinterpret_cast<float4 *>(mine + 4) = make_float4(accu[0], accu[1], accu[2], accu[3]);
+        named_bar(1 + grp, GU_S * 32);
+        if (wi == r % GU_S) {
           float sg[4] = {0.f, 0.f, 0.f, 0.f}, su[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-          for (int w = 0; w < S; ++w) {
-            const float *o = red + ((b * KL_WARPS + grp * S + w) * 32 + lane) * 8;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              sg[j] += o[j];
-              su[j] += o[4 + j];
-            }
+          for (int w = 0; w < GU_S; ++w) {
+            const float *o = red + ((b * KL_WARPS + grp * GU_S + w) * 32 + lane) * 8;
+            const float4 og = *reinterpret_cast<const float4 *>(o);
+            const float4 ou = *reinterpret_cast<const float4 *>(o + 4);
+            sg[0] += og.x; sg[1] += og.y; sg[2] += og.z; sg[3] += og.w;
+            su[0] += ou.x; su[1] += ou.y; su[2] += ou.z; su[3] += ou.w;
           }
-          // SwiGLU (bf16 per op) of rows g, g+8 x tokens 2c, 2c+1, then h of
-          // the 16 rows in fragment order and its per-token sums.
+          // SwiGLU (bf16 per op) of rows g, g+8 x tokens 2c, 2c+1; h of the
+          // 16 rows in fragment order (via shuffles) and its per-token sums.
+          const int item = a0 + li;
           const int e = item / RB, rb = item % RB;
+          float hv[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const int row = (j >> 1) ? g + 8 : g, n = 2 * c + (j & 1);
-            hbuf[row * 8 + n] = n < T ? swiglu_bf16(rbf(sg[j]), rbf(su[j])) : 0.f;
+            const int n = 2 * c + (j & 1);
+            hv[j] = n < T ? swiglu_bf16(rbf(sg[j]), rbf(su[j])) : 0.f;
           }
-          __syncwarp();
+          // Lane (g, c) holds h[row g | g+8][token 2c | 2c+1]. Fragment word
+          // w of token n = pack(h[olo][n], h[olo + 4][n]) with olo = 8j + i0
+          // + pp (m = w / 2, pp = w & 1, j = m / 2, i0 = 2 (m & 1)); the
+          // owner of h[row][n] is lane 4 (row & 7) + n / 2, value index
+          // (row >= 8 ? 2 : 0) + (n & 1).
           uint32_t *hperm = wsp<uint32_t>(p, p.L.hperm);
 #pragma unroll
           for (int h2 = 0; h2 < 2; ++h2) {
@@ -1056,15 +1124,32 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
             const int n = idx >> 3, w = idx & 7;
             const int m = w >> 1, pp = w & 1, j = m >> 1, i0 = 2 * (m & 1);
             const int olo = 8 * j + i0 + pp, ohi = olo + 4;
+            const int src_lo = 4 * (olo & 7) + (n >> 1), src_hi = 4 * (ohi & 7) + (n >> 1);
+            const int vlo = (olo >= 8 ? 2 : 0) + (n & 1), vhi = (ohi >= 8 ? 2 : 0) + (n & 1);
+            float lo = 0.f, hi2 = 0.f;
+#pragma unroll
+            for (int q2 = 0; q2 < 4; ++q2) {
+              const float a = __shfl_sync(0xffffffffu, hv[q2], src_lo);
+              const float bq = __shfl_sync(0xffffffffu, hv[q2], src_hi);
+              if (q2 == vlo) lo = a;
+              if (q2 == vhi) hi2 = bq;
+            }
             if (n < T)
               hperm[((((size_t)e * DEC_MAX_T + n) * NGI + (rb >> 2)) * 4 + (rb & 3)) * 8 + w] =
-                  pack_bf2(hbuf[olo * 8 + n], hbuf[ohi * 8 + n]);
+                  pack_bf2(lo, hi2);
           }
-          if (lane < T) {
-            float sh = 0.f;
+          // per-token sums of the 16 rows: lanes (g, c) add their rows, then
+          // the 8 lanes of a token column pair add over g
+          float s0 = hv[0] + hv[2], s1 = hv[1] + hv[3];
 #pragma unroll
-            for (int o = 0; o < 16; ++o) sh += hbuf[o * 8 + lane];
-            wsp<float>(p, p.L.hsum)[((size_t)e * DEC_MAX_T + lane) * RB + rb] = sh;
+          for (int o = 4; o < 32; o <<= 1) {
+            s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+          }
+          if (g == 0) {
+            float *hs = wsp<float>(p, p.L.hsum);
+            if (2 * c < T) hs[((size_t)e * DEC_MAX_T + 2 * c) * RB + rb] = s0;
+            if (2 * c + 1 < T) hs[((size_t)e * DEC_MAX_T + 2 * c + 1) * RB + rb] = s1;
           }
           __syncwarp();
           if (lane == 0) red_release_add(ent_done + e * KL_CSTRIDE, 1u);  // h rows of this item are out
@@ -1079,86 +1164,120 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
   uint16_t *sparts = wsp<uint16_t>(p, p.L.sparts);
   {
     const int nsi = NGI >> gs, sbh = 16 * nsi;  // scales per row; bf16 per scale tensor
-    int cur_e = -1;
-    uint32_t hb[NGI][8];
-    float hs0[NGI], hs1[NGI];
+    int cur_e = -1, slot = 0;
     int rank0 = -1, rank1 = -1;
     float score0 = 0.f, score1 = 0.f;
     bool is_sh = false;
+    volatile int *hflag = s_misc + 4;
 #pragma unroll 1
     for (int jj = 0; jj < nj; ++jj) {
-      const int i = d0 + jj;
+      const int i = d0 + warp + KL_WARPS * jj;
       const int e = i / RBN, rb = i % RBN;
       if (e != cur_e) {
-        // The entry's h is complete once its RB gate/up items are counted.
-        if (!wait_ge(ent_done + e * KL_CSTRIDE, (unsigned)RB)) {
+        // The entry's h (complete once its RB gate/up items are counted) is
+        // staged once per CTA: the first warp to need it claims the slot,
+        // waits for the entry and copies h and its group sums; the others
+        // wait for the slot's flag (0 empty, 1 loading, 2 ready, 3 failed).
+        slot = e - e_lo;
+        int claim = 1;
+        if (lane == 0) claim = atomicCAS(const_cast<int *>(hflag + slot), 0, 1);
+        claim = __shfl_sync(0xffffffffu, claim, 0);
+        bool ok = true;
+        if (claim == 0) {
+          ok = wait_ge(ent_done + e * KL_CSTRIDE, (unsigned)RB);
+          ok = __all_sync(0xffffffffu, ok);
+          if (ok) {
+            const uint4 *src = reinterpret_cast<const uint4 *>(wsp<const uint32_t>(p, p.L.hperm) +
+                                                               (size_t)e * DEC_MAX_T * (I / 2));
+            uint4 *dst = reinterpret_cast<uint4 *>(hf + slot * (Tl::HF / 4));
+            for (int u = lane; u < T * NGI * 8; u += 32) dst[u] = __ldcg(src + u);
+            const float *hsum = wsp<const float>(p, p.L.hsum) + (size_t)e * DEC_MAX_T * RB;
+            for (int u = lane; u < T * NGI; u += 32) {
+              const int n = u / NGI, Gi = u % NGI;
+              const float4 v = __ldcg(reinterpret_cast<const float4 *>(hsum + (size_t)n * RB + 4 * Gi));
+              hsg[(slot * NGI + Gi) * DEC_MAX_T + n] = ((v.x + v.y) + v.z) + v.w;
+            }
+            for (int u = lane; u < NGI * DEC_MAX_T; u += 32)
+              if ((u & 7) >= T) hsg[slot * NGI * DEC_MAX_T + u] = 0.f;
+          }
+          __syncwarp();
+          if (lane == 0) {
+            __threadfence_block();
+            hflag[slot] = ok ? 2 : 3;
+          }
+        } else {
+          // every lane observes the flag itself, then reads the slot
+          int f = 0;
+          const uint64_t t0 = globaltimer();
+          for (;;) {
+            f = hflag[slot];
+            if (f >= 2) break;
+            if (globaltimer() - t0 > KL_WAIT_NS) break;
+            __nanosleep(128);
+          }
+          __threadfence_block();
+          ok = __all_sync(0xffffffffu, f == 2);
+        }
+        if (!ok) {
           if (lane == 0) flag_status(p.status, VB_STATUS_TIMEOUT);
           j_end = jj;
           break;
         }
         cur_e = e;
-        const uint32_t *hp = wsp<const uint32_t>(p, p.L.hperm) + (size_t)e * DEC_MAX_T * (I / 2);
-        const float *hsum = wsp<const float>(p, p.L.hsum) + (size_t)e * DEC_MAX_T * RB;
-#pragma unroll
-        for (int Gi = 0; Gi < NGI; ++Gi) {
-          uint4 a = make_uint4(0, 0, 0, 0), b = a;
-          if (g < T) {
-            const uint4 *src = reinterpret_cast<const uint4 *>(hp + ((size_t)g * NGI + Gi) * 32 + c * 8);
-            a = __ldcg(src);
-            b = __ldcg(src + 1);
-          }
-          hb[Gi][0] = a.x; hb[Gi][1] = a.y; hb[Gi][2] = a.z; hb[Gi][3] = a.w;
-          hb[Gi][4] = b.x; hb[Gi][5] = b.y; hb[Gi][6] = b.z; hb[Gi][7] = b.w;
-          float v0 = 0.f, v1 = 0.f;
-          if (2 * c < T) {
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(hsum + (size_t)(2 * c) * RB + 4 * Gi));
-            v0 = ((v.x + v.y) + v.z) + v.w;
-          }
-          if (2 * c + 1 < T) {
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(hsum + (size_t)(2 * c + 1) * RB + 4 * Gi));
-            v1 = ((v.x + v.y) + v.z) + v.w;
-          }
-          hs0[Gi] = v0;
-          hs1[Gi] = v1;
-        }
         is_sh = s_ent[e].flags & 1;
         rank0 = 2 * c < T ? s_ent[e].rank[2 * c] : -1;
         rank1 = 2 * c + 1 < T ? s_ent[e].rank[2 * c + 1] : -1;
         score0 = 2 * c < T ? s_ent[e].score[2 * c] : 0.f;
         score1 = 2 * c + 1 < T ? s_ent[e].score[2 * c + 1] : 0.f;
       }
-      cp_async_wait<RS - 2>();
-      __syncwarp();
-      issue_next();
-      const uint8_t *st = ring + ((nq_gu + jj) % RS) * Tl::CHUNK;
-      const uint16_t *ss = reinterpret_cast<const uint16_t *>(st + Tl::DWB);
+      const uint32_t *hs_f = hf + slot * (Tl::HF / 4);
+      const float *hs_g = hsg + slot * NGI * DEC_MAX_T;
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int dc = 0; dc < DCH; ++dc) {
+        cp_async_wait<RS - 2>();
+        __syncwarp();
+        issue_next();
+        const int qd = nq_gu + jj * DCH + dc;
+        const uint8_t *st = ring + (qd % RS) * Tl::STAGE;
+        const uint16_t *ss = reinterpret_cast<const uint16_t *>(st + Tl::DWB);
 #pragma unroll
-      for (int Gi = 0; Gi < NGI; ++Gi) {
-        const int fo = g * Tl::DROWB + (swz<Tl::DROWB / 16>(g, 2 * Gi + (c >> 1)) << 4) + (c & 1) * 8;
-        const uint2 a0 = lds64(st + fo);
-        const uint2 a1 = lds64(st + 8 * Tl::DROWB + fo);
-        uint32_t p0[2][4], p1[2][4];
-        nib_pairs4(a0.x, p0[0]);
-        nib_pairs4(a0.y, p0[1]);
-        nib_pairs4(a1.x, p1[0]);
-        nib_pairs4(a1.y, p1[1]);
-        float dd[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int gl = 0; gl < DG; ++gl) {
+          const int Gi = dc * DG + gl;
+          constexpr int CPR = Tl::DROWB / 16;
+          const int fo = g * Tl::DROWB + (swz<CPR>(g, 2 * gl + (c >> 1)) << 4) + (c & 1) * 8;
+          const uint2 a0 = lds64(st + fo);
+          const uint2 a1 = lds64(st + 8 * Tl::DROWB + fo);
+          uint4 hb0 = make_uint4(0, 0, 0, 0), hb1 = hb0;
+          if (g < T) {
+            const uint4 *hp = reinterpret_cast<const uint4 *>(hs_f + ((g * NGI + Gi) * 4 + c) * 8);
+            hb0 = hp[0];
+            hb1 = hp[1];
+          }
+          const float2 hsv = *reinterpret_cast<const float2 *>(hs_g + Gi * DEC_MAX_T + 2 * c);
+          uint32_t p0[2][4], p1[2][4];
+          nib_pairs4(a0.x, p0[0]);
+          nib_pairs4(a0.y, p0[1]);
+          nib_pairs4(a1.x, p1[0]);
+          nib_pairs4(a1.y, p1[1]);
+          const uint32_t hw[8] = {hb0.x, hb0.y, hb0.z, hb0.w, hb1.x, hb1.y, hb1.z, hb1.w};
+          float dd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-          const int i0m = 2 * (m & 1), h = m >> 1;
-          mma_bf16(dd, p0[h][i0m], p1[h][i0m], p0[h][i0m + 1], p1[h][i0m + 1], hb[Gi][2 * m],
-                   hb[Gi][2 * m + 1]);
+          for (int m = 0; m < 4; ++m) {
+            const int i0m = 2 * (m & 1), h = m >> 1;
+            mma_bf16(dd, p0[h][i0m], p1[h][i0m], p0[h][i0m + 1], p1[h][i0m + 1], hw[2 * m],
+                     hw[2 * m + 1]);
+          }
+          const int si = Gi >> gs;
+          const float s0 = bf2f(ss[g * nsi + si]), s1 = bf2f(ss[(g + 8) * nsi + si]);
+          const float b0 = bf2f(ss[sbh + g * nsi + si]);
+          const float b1 = bf2f(ss[sbh + (g + 8) * nsi + si]);
+          const float bp0 = fmaf(-128.f, s0, b0), bp1 = fmaf(-128.f, s1, b1);
+          acc[0] = fmaf(bp0, hsv.x, fmaf(s0, dd[0], acc[0]));
+          acc[1] = fmaf(bp0, hsv.y, fmaf(s0, dd[1], acc[1]));
+          acc[2] = fmaf(bp1, hsv.x, fmaf(s1, dd[2], acc[2]));
+          acc[3] = fmaf(bp1, hsv.y, fmaf(s1, dd[3], acc[3]));
         }
-        const int si = Gi >> gs;
-        const float s0 = bf2f(ss[g * nsi + si]), s1 = bf2f(ss[(g + 8) * nsi + si]);
-        const float b0 = bf2f(ss[sbh + g * nsi + si]);
-        const float b1 = bf2f(ss[sbh + (g + 8) * nsi + si]);
-        const float bp0 = fmaf(-128.f, s0, b0), bp1 = fmaf(-128.f, s1, b1);
-        acc[0] += fmaf(s0, dd[0], bp0 * hs0[Gi]);
-        acc[1] += fmaf(s0, dd[1], bp0 * hs1[Gi]);
-        acc[2] += fmaf(s1, dd[2], bp1 * hs0[Gi]);
-        acc[3] += fmaf(s1, dd[3], bp1 * hs1[Gi]);
       }
       const int r0 = 16 * rb + g, r1 = r0 + 8;
 #pragma unroll
@@ -1192,7 +1311,7 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
     int rb = 0;
     bool win = false;
     if (jj < j_end) {
-      rb = (d0 + jj) % RBN;
+      rb = (d0 + warp + KL_WARPS * jj) % RBN;
       win = atom_add_acq_rel(cnt + rb * KL_CSTRIDE, 1u) == (unsigned)n_ent - 1;
     }
     unsigned m = __ballot_sync(0xffffffffu, win);
@@ -1284,6 +1403,50 @@ int noalloc_scratch(void **out) {
 
 using LayerFn = void (*)(DecodeParams);
 
+// Launch of the layer kernel: cooperative (the runtime places every CTA at
+// once, which the grid barrier needs) and, unless timing events surround it,
+// a programmatic dependent launch. If the runtime refuses the pair on the
+// first (uncaptured) launch, later launches use PDL alone: one CTA per SM
+// still fits, so the CTAs are resident whenever the kernel runs alone.
+std::atomic<int> g_coop_state{-1};  // -1 untried, 0 refused, 1 accepted
+
+cudaError_t launch_layer(LayerFn fn, int grid, size_t smem, cudaStream_t s, bool pdl,
+                         const DecodeParams &p) {
+  for (;;) {
+    const int state = g_coop_state.load();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(KL_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+      attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[na].val.programmaticStreamSerializationAllowed = 1;
+      ++na;
+    }
+    if (state != 0) {
+      attr[na].id = cudaLaunchAttributeCooperative;
+      attr[na].val.cooperative = 1;
+      ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, p);
+    if (state != -1) return e;
+    if (e == cudaSuccess) {
+      g_coop_state = 1;
+      return e;
+    }
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone)
+      return e;
+    (void)cudaGetLastError();  // the refusal is not sticky
+    g_coop_state = 0;
+  }
+}
+
 // The layer kernel and its shared memory for (H, I).
 bool layer_kernel(int H, int I, LayerFn *fn, size_t *smem) {
 #define VB_HI(HH, II)                                 \
@@ -1330,6 +1493,8 @@ int moe_decode_impl(const VbMoeDecodeArgs *a, vb_stream_t stream, size_t clear_b
   VB_REQUIRE(H / a->group >= 8 && I >= a->group, "vb_moe_decode: group too large");
   VB_REQUIRE(E >= k && E <= DEC_MAX_E, "vb_moe_decode: num_experts=%d", E);
   VB_REQUIRE(k >= 1 && k <= DEC_MAX_K, "vb_moe_decode: top_k=%d", k);
+  VB_REQUIRE(T * k + 1 <= sm_count(),
+             "vb_moe_decode: tokens*top_k+1=%d entries exceed the %d SMs", T * k + 1, sm_count());
   VB_REQUIRE(a->x && a->router_w && a->slot_table && a->out, "vb_moe_decode: null tensor");
   VB_REQUIRE(a->pool.ptr[0] && a->pool.cap > 0, "vb_moe_decode: empty pool");
   const bool has_shared = a->shared.ptr[0] != nullptr;
@@ -1384,7 +1549,7 @@ int moe_decode_impl(const VbMoeDecodeArgs *a, vb_stream_t stream, size_t clear_b
   cudaEvent_t *ev = a->timing_events ? (cudaEvent_t *)a->timing_events : nullptr;
   const bool pdl = ev == nullptr;  // event records would break the PDL chain
   if (ev) cudaEventRecord(ev[0], s);
-  err = vb_launch(fn, dim3(sm_count()), dim3(KL_THREADS), smem, s, pdl, p);
+  err = launch_layer(fn, sm_count(), smem, s, pdl, p);
   if (err != cudaSuccess) return set_error(VB_ERR_CUDA, "moe_layer_kernel: %s", cudaGetErrorString(err));
   if (ev) cudaEventRecord(ev[1], s);
   return VB_OK;

@@ -223,6 +223,91 @@ class CudaEpBackend:
         return self.blk.num_experts
 
 
+class NcclComm:
+    """An NCCL communicator of its own over the ranks of ``group`` (rank 0's
+    ``ncclUniqueId`` is broadcast through the process group). The native EP
+    prefill issues its point-to-point calls on it, apart from torch's own
+    communicators."""
+
+    class _UniqueId(C.Structure):
+        _fields_ = [("internal", C.c_char * 128)]
+
+    def __init__(self, group=None):
+        self.nccl = C.CDLL("libnccl.so.2")  # the copy torch already loaded
+        self.nccl.ncclGetUniqueId.argtypes = [C.POINTER(self._UniqueId)]
+        self.nccl.ncclCommInitRank.argtypes = [C.POINTER(C.c_void_p), C.c_int, self._UniqueId,
+                                               C.c_int]
+        self.nccl.ncclCommDestroy.argtypes = [C.c_void_p]
+        single = not (dist.is_available() and dist.is_initialized())
+        self.world = 1 if single else dist.get_world_size(group)
+        self.rank = 0 if single else dist.get_rank(group)
+        uid = self._UniqueId()
+        if self.rank == 0:
+            rc = self.nccl.ncclGetUniqueId(C.byref(uid))
+            if rc != 0:
+                raise RuntimeError(f"ncclGetUniqueId failed ({rc})")
+        if not single:
+            box = [bytes(uid.internal) if self.rank == 0 else None]
+            dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group else 0,
+                                       group=group)
+            uid = self._UniqueId()
+            C.memmove(C.addressof(uid), box[0], 128)
+        self.comm = C.c_void_p()
+        rc = self.nccl.ncclCommInitRank(C.byref(self.comm), self.world, uid, self.rank)
+        if rc != 0:
+            raise RuntimeError(f"ncclCommInitRank failed ({rc})")
+
+    def close(self):
+        if self.comm:
+            torch.cuda.synchronize()
+            self.nccl.ncclCommDestroy(self.comm)
+            self.comm = C.c_void_p()
+
+
+class NativeEp:
+    """Expert-parallel prefill through the C ABI (``vb_moe_prefill_ep``): the
+    whole schedule of :func:`ep_prefill` in one native call per step.
+
+    ``blk`` holds this rank's experts (its slot table is -1 for the others),
+    ``owner`` the placement of :func:`placement`, ``max_tokens`` the largest
+    token count of any rank."""
+
+    def __init__(self, blk, owner, comm: NcclComm, max_tokens: int, layer_cap: int = 0,
+                 max_assignments: int = 0):
+        from ._lib import lib
+        self.lib, self.blk, self.comm = lib, blk, comm
+        self.owner = torch.as_tensor(owner).to(device=blk.router_w.device,
+                                               dtype=torch.int32).contiguous()
+        self.max_tokens = int(max_tokens)
+        self.layer_cap, self.max_assignments = int(layer_cap), int(max_assignments)
+        self._ws = None
+
+    def __call__(self, x_local: torch.Tensor, out=None, status=None, stream=None):
+        from ._lib import VbMoePrefillEpArgs, check
+        from .prefill import prefill_args
+        b = self.blk
+        x2 = x_local.reshape(-1, b.hidden).contiguous()
+        T = int(x2.shape[0])
+        if out is None:
+            out = torch.empty_like(x2)
+        need = self.lib.vb_moe_prefill_ep_workspace_size(T, b.hidden, b.inter, b.num_experts,
+                                                         b.top_k, self.comm.world,
+                                                         max(self.max_tokens, T))
+        if self._ws is None or self._ws.numel() < need + 1024:
+            self._ws = None
+            self._ws = torch.empty(need + 1024, dtype=torch.uint8, device=x2.device)
+        ws = (self._ws.data_ptr() + 1023) // 1024 * 1024
+        a = VbMoePrefillEpArgs()
+        a.base = prefill_args(b, x2, out, ws, need, status=status, layer_cap=self.layer_cap,
+                              max_assignments=self.max_assignments)
+        a.owner = self.owner.data_ptr()
+        a.world, a.rank = self.comm.world, self.comm.rank
+        a.max_tokens_per_rank = max(self.max_tokens, T)
+        check(self.lib.vb_moe_prefill_ep(C.byref(a), self.comm.comm, stream_handle(stream)),
+              "vb_moe_prefill_ep")
+        return out
+
+
 def ep_prefill(backend, x_local: torch.Tensor, group=None, timings: dict | None = None):
     """One expert-parallel prefill step of the block on this rank's tokens.
 
