@@ -699,7 +699,8 @@ def run_decode(args, world, rank, local):
     kspan = (tr[:, 1] - tr[:, 0]).mean() / 1e3
     layer_us = (tr[1:, 0] - tr[:-1, 0]).mean() / 1e3
     marks = {name: (tr[:, m] - tr[:, 0]).mean() / 1e3 for m, name in (
-        (2, "pdl_wait"), (3, "router_rows"), (4, "grid_barrier"), (5, "routing"),
+        (2, "pdl_wait"), (3, "router_rows"), (4, "grid_barrier"), (9, "route_max"),
+        (10, "route_sum"), (11, "route_candidates"), (12, "route_topk"), (5, "routing"),
         (6, "gateup"), (7, "down"), (8, "combine"))}
 
     # ---- the layer kernel timed per launch with CUDA events outside the

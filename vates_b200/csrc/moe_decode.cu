@@ -508,7 +508,7 @@ __device__ __noinline__ int route_tokens(const float *logits, const int32_t *tab
                                          int *s_table, int *s_first, int *s_rex, int *s_rslot,
                                          float *s_rscore, int *s_rent, int32_t *s_ok,
                                          DecEntry *s_ent, int *s_wcnt, uint32_t *s_wmax,
-                                         double *s_wsum, uint32_t *s_cand) {
+                                         double *s_wsum, uint32_t *s_cand, uint64_t *trace) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int t = warp / wpt, wp = warp - t * wpt;
   const bool act = t < T;
@@ -542,6 +542,7 @@ __device__ __noinline__ int route_tokens(const float *logits, const int32_t *tab
   mk = __reduce_max_sync(0xffffffffu, mk);
   if (lane == 0) s_wmax[warp] = mk;
   __syncthreads();
+  trace_mark(trace, 9);
   uint32_t mt = 0;
   if (act)
     for (int w = 0; w < wpt; ++w) mt = max(mt, s_wmax[t * wpt + w]);
@@ -563,6 +564,7 @@ __device__ __noinline__ int route_tokens(const float *logits, const int32_t *tab
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   if (lane == 0) s_wsum[warp] = s;
   __syncthreads();
+  trace_mark(trace, 10);
   double st = 0.0;
   if (act)
     for (int w = 0; w < wpt; ++w) st += s_wsum[t * wpt + w];
@@ -590,6 +592,7 @@ __device__ __noinline__ int route_tokens(const float *logits, const int32_t *tab
   }
   if (act && lane < k) s_cand[warp * k + lane] = mine;
   __syncthreads();
+  trace_mark(trace, 11);
   if (act && wp == 0) {
     // The token's top-k among its wpt * k candidates (at most 16 * 16).
     const int nc = wpt * k;
@@ -649,6 +652,7 @@ __device__ __noinline__ int route_tokens(const float *logits, const int32_t *tab
     }
   }
   __syncthreads();
+  trace_mark(trace, 12);
 
   // Entries: shared expert first, then one entry per distinct routed expert
   // in route order (t-major, rank-minor): the first route of each expert is
@@ -700,7 +704,9 @@ __device__ __noinline__ int route_tokens(const float *logits, const int32_t *tab
 // The layer kernel. Trace slots (optional): 0/1 span; latest CTA past the
 // PDL wait (2), done with its router rows (3), past the grid barrier (4),
 // done with routing (5); latest warp done with gate/up (6), with its down
-// items (7), with its combines (8).
+// items (7), with its combines (8); latest CTA past the routing steps: the
+// maximum (9), the exponential sum (10), the per-warp candidates (11), the
+// top-k (12).
 // ----------------------------------------------------------------------------
 template <int H, int I>
 __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p) {
@@ -943,7 +949,7 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
   route_tokens<PERW>(lg, p.table, T, E, p.k, wpt, p.norm_topk, p.has_shared, p.pool.cap,       \
                      primary, p.status, p.out_inds, p.out_scores, p.out_local, s_table,        \
                      s_first, s_rex, s_rslot, s_rscore, s_rent, s_ok, s_ent, s_wcnt, s_wmax,   \
-                     s_wsum, s_cand)
+                     s_wsum, s_cand, p.trace)
     if (need <= 1) n = VB_ROUTE(1);
     else if (need <= 2) n = VB_ROUTE(2);
     else if (need <= 4) n = VB_ROUTE(4);
