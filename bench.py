@@ -31,7 +31,7 @@ sys.path.insert(0, ROOT)
 METRIC = "MoE tokens/s and HBM GB/s (decode T≤4); prefill tok/s at 1/2/4/8 B200"
 DECODE_WORKLOAD = "decode_verify_T4_48layers_fresh_inputs"
 EXPERT_BYTES = 1_769_472          # blob_layout stride at H=2048, I=512, 4-bit g64
-LAYER_TRAFFIC_PER_ENTRY = (73_213_440 + 1_418_752) / 33  # dram read + write / entries
+LAYER_TRAFFIC_PER_ENTRY = 1_849_937  # dram read + write per entry (profiles/decode_moe_layer_kernel.md)
 ROUTER_BYTES = 512 * 2048 * 2
 SHARED_GATE_BYTES = 2048 * 2
 
@@ -723,9 +723,9 @@ def run_decode(args, world, rank, local):
     # per step, so its average launch takes ms / L.
     launch_ms = ms / L
     achieved = layer_bytes / (launch_ms / 1e3) / 1e9
-    # DRAM traffic per launch: one ncu capture of a 4-layer case read+wrote
-    # LAYER_TRAFFIC_PER_ENTRY bytes per entry (routed experts + the shared
-    # one); scaled to this run's mean entries per launch.
+    # DRAM traffic per launch: an ncu capture of the 4-layer fresh-input case
+    # read+wrote LAYER_TRAFFIC_PER_ENTRY bytes per entry (routed experts + the
+    # shared one); scaled to this run's mean entries per launch.
     traffic = LAYER_TRAFFIC_PER_ENTRY * (sum(U) / L + 1)
 
     out = {
@@ -795,8 +795,20 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the prefill (config 2) and IsoQuant (config 3) legs")
+    ap.add_argument("--leg", default=None,
+                    choices=["prefill", "isoquant", "prefill_attention", "residency"],
+                    help="run only this extra leg on one GPU and print its result (for profiling)")
+    ap.add_argument("--iso-layers", type=int, default=12)
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
+    if args.leg is not None:
+        legs = {"prefill": lambda: run_prefill_leg(args.steps, args.warmup),
+                "isoquant": lambda: run_isoquant_leg(args.steps, args.warmup,
+                                                     layers=args.iso_layers),
+                "prefill_attention": lambda: run_prefill_attention_leg(args.steps, args.warmup),
+                "residency": lambda: run_residency_leg()}
+        print(json.dumps({args.leg: legs[args.leg]()}), flush=True)
+        return 0
     try:
         if args.impl == "reference":
             rc = run_reference(args, world, rank)

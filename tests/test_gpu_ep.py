@@ -115,6 +115,29 @@ def _ep_rank(rank, world, port, q, owner=None, native=False):
         dist.destroy_process_group()
 
 
+def _collect(q, procs, limit_s=300):
+    """Results of the rank processes; fails as soon as one of them exits
+    without reporting (no waiting for the full limit)."""
+    import queue
+    import time
+    res, t0 = {}, time.time()
+    while len(res) < len(procs):
+        try:
+            r, out = q.get(timeout=2)
+            res[r] = out
+        except queue.Empty:
+            dead = [p for p in procs if p.exitcode not in (None, 0)]
+            if dead or time.time() - t0 > limit_s:
+                for p in procs:
+                    if p.is_alive():
+                        p.terminate()
+                pytest.fail(f"rank processes failed: {[p.exitcode for p in procs]}")
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return res
+
+
 def test_native_ep_one_rank_matches_single_device(cuda):
     """vb_moe_prefill_ep through the C ABI on a one-rank NCCL communicator
     (every route stays on the rank: the self chunks are device copies):
@@ -153,10 +176,7 @@ def test_ep_prefill_two_gpus_matches_one(cuda, native):
              for r in range(2)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in range(2))
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
+    res = _collect(q, procs)
     got = np.concatenate([res[0], res[1]])
     assert np.array_equal(got, ref)
 
@@ -187,9 +207,6 @@ def test_ep_prefill_two_gpus_with_replicated_hot_experts(cuda, native):
              for r in range(2)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=300) for _ in range(2))
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
+    res = _collect(q, procs)
     got = np.concatenate([res[0], res[1]])
     assert np.array_equal(got, ref)

@@ -172,3 +172,31 @@ def test_stack_layers_match_oracle(cuda):
                                   route=(inds, to_np(dbg["scores"])))
         bf16_close(to_np(st.hs[l + 1]), ref["out"], scale=block_scale(ref, to_np(st.hs[l])),
                    what=f"layer {l}")
+
+
+def test_decode_bounded_wait_runs_out(cuda):
+    """A grid barrier that cannot complete: the arrival counter of the
+    workspace is preset so that all but one CTA wait for one arrival too
+    many. Every wait gives up after its bound (about 2 s), the call returns
+    VB_STATUS_TIMEOUT in the status word, and the context stays usable: the
+    next call on a cleared workspace is correct."""
+    import torch
+    from vates_b200.moe_block import Workspace
+    from vates_b200.synth import config0, input_tokens
+    blk, _ = config0(seed=0)
+    x = input_tokens(21, 4)
+    ref = blk.decode(x).clone()
+    G = torch.cuda.get_device_properties(0).multi_processor_count
+    blk.workspace = Workspace()
+    ws = blk.workspace.get(1 << 21)
+    ws.view(torch.int64)[0] = 5 * G + G - 1  # (n + 1) G - 1 arrivals so far
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    blk.decode(x, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) & 4  # VB_STATUS_TIMEOUT
+    blk.workspace = Workspace()  # zero-filled again
+    status.zero_()
+    again = blk.decode(x, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(again.view(torch.int16), ref.view(torch.int16))

@@ -63,7 +63,7 @@ constexpr int PF_A_BYTES = PF_BM * PF_BK * 2;        // 16 KB
 constexpr int PF_B_BYTES = PF_BN * PF_BK * 2;        // 32 KB
 constexpr int PF_P_BYTES = PF_BN * PF_BK / 2;        // 8 KB packed codes
 constexpr int PF_STAGE_BYTES = PF_A_BYTES + PF_B_BYTES + PF_P_BYTES;
-// Epilogue staging for TMA stores: per epilogue warp two 32-row x 32-column
+// Epilogue staging for TMA stores (down): per epilogue warp one 32-row x 32-column
 // bf16 chunks (64-byte rows, 64-byte swizzle).
 constexpr int PF_OUT_CHUNK = 32 * 64;
 constexpr uint64_t PF_WAIT_NS = 2000000000ull;       // 2 s per wait
@@ -75,13 +75,14 @@ enum PfMode : int { PF_GATEUP = 0, PF_DOWN = 1, PF_ROUTER = 2 };
 //  down:    4 stages of (A, B), the packed codes of dequantized tiles in a
 //           2-slot ring of their own, one 32x32 output staging chunk per
 //           epilogue warp (TMA stores);
-//  router:  3 stages of (A, B, -), two staging chunks per epilogue warp.
-constexpr int pf_stages(int mode) { return mode == PF_ROUTER ? 3 : 4; }
+//  router:  4 stages of (A, B); its rows are stored directly (no packed
+//           codes, no staging).
+constexpr int pf_stages(int mode) { return 4; }
 constexpr bool pf_pring(int mode) { return mode == PF_DOWN; }
 constexpr int pf_stage_bytes(int mode) {
-  return pf_pring(mode) ? PF_A_BYTES + PF_B_BYTES : PF_STAGE_BYTES;
+  return pf_pring(mode) || mode == PF_ROUTER ? PF_A_BYTES + PF_B_BYTES : PF_STAGE_BYTES;
 }
-constexpr int pf_out_bufs(int mode) { return mode == PF_GATEUP ? 0 : (mode == PF_DOWN ? 1 : 2); }
+constexpr int pf_out_bufs(int mode) { return mode == PF_DOWN ? 1 : 0; }
 constexpr int pf_smem(int mode) {
   return pf_stages(mode) * pf_stage_bytes(mode) + (pf_pring(mode) ? 2 * PF_P_BYTES : 0) +
          8 * pf_out_bufs(mode) * PF_OUT_CHUNK + 1024;  // + alignment slack

@@ -247,10 +247,11 @@ class NcclComm:
             if rc != 0:
                 raise RuntimeError(f"ncclGetUniqueId failed ({rc})")
         if not single:
-            box = [bytes(uid.internal) if self.rank == 0 else None]
+            # all 128 bytes (a c_char array field would stop at the first NUL)
+            box = [C.string_at(C.addressof(uid), 128) if self.rank == 0 else None]
             dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group else 0,
                                        group=group)
-            uid = self._UniqueId()
+            assert len(box[0]) == 128
             C.memmove(C.addressof(uid), box[0], 128)
         self.comm = C.c_void_p()
         rc = self.nccl.ncclCommInitRank(C.byref(self.comm), self.world, uid, self.rank)
