@@ -8,10 +8,9 @@
 // Split-K ("flash decoding"): each CTA owns one (batch, kv head) and a
 // contiguous key range processed in 16-key tiles; a combine kernel merges the
 // per-split (max, sum, output) triples in split order. Two partial kernels:
-// kv_attn1_kernel for up to 8 query rows per kv head (decode, T = 1; the
-// CTA's four warps share each tile, warp w owning the 64-dim group w) and
-// kv_attn4_kernel for 9..32 rows (MTP verify, T = 4; the CTA shares each
-// unpacked tile, warp w takes rows 8w..8w+7).
+// kv_attn1_kernel for up to 8 query rows per kv head (decode, T = 1; every
+// warp owns whole tiles) and kv_attn4_kernel for 9..32 rows (MTP verify,
+// T = 4; the CTA shares each unpacked tile, warp w takes rows 8w..8w+7).
 // Both compute S^T = K Q^T and O^T += V^T P^T on mma.sync with the codes as
 // exact bf16 values 128 + code, the per-64-dim-group scale and bias applied
 // as s*D + (b - 128 s)*sum and the V bias term sum(p*b) on the CUDA cores;
@@ -117,27 +116,24 @@ __global__ void __launch_bounds__(256) kv_attn_combine_kernel(AttnParams p) {
 
 // ----------------------------------------------------------------------------
 // Single-query-position path (rep * L <= 8 query rows per kv head, i.e. GQA
-// decode at T=1). The CTA's four warps walk the same 16-key tiles, warp w
-// owning the 64-dim group w: it unpacks only its group's K and V codes,
-// computes the group's part of the scores S^T[key][row] (the 4-bit K codes
-// as exact bf16 128+q in the A operand, the 8 query rows as N = 8, the group
-// epilogue s*D + (b-128s)*sum(q)), and the four parts meet in shared memory
-// and are added in group order, so every warp holds the same bf16 scores and
-// runs the same online softmax. The output O^T[dim][row] += V^T P^T of its
-// 64 dims uses V unpacked to exact bf16 in shared memory (ldmatrix.trans)
-// and P (bf16, times the key's V scale of the group) moved to the B layout
-// with movmatrix.trans. Raw K/V codes and scales of the next two tiles are
-// staged with cp.async by the whole CTA. Small registers and shared memory
-// (up to 8 CTAs per SM) keep enough warps in flight to hide the latency of
-// each tile's chain.
+// decode at T=1): every warp owns whole 16-key tiles. Scores are computed
+// transposed, S^T[key][row] = K * Q^T, with the 4-bit K codes as the A
+// operand (exact bf16 128+q by one LOP3 per pair) and the 8 query rows as
+// the N=8 columns; per 64-dim group the epilogue applies s*D + (b-128s)*sum(q)
+// and the group partials are added in group order, then rounded to bf16.
+// The output is accumulated transposed too, O^T[dim][row] += V^T * P^T, with
+// V unpacked to exact bf16 in shared memory (read as A by ldmatrix.trans)
+// and P (bf16, times the key's V scale of the dim group) moved from the S^T
+// accumulator layout to the B layout with movmatrix.trans. Raw K/V codes and
+// scales of the next tile are prefetched with cp.async. The 4 warps' partial
+// softmax states are merged in shared memory into the CTA's split partial.
 // ----------------------------------------------------------------------------
 constexpr int A1_WARPS = 4;
-constexpr int A1_VPITCH = 64 + 8;                         // bf16 per unpacked V row (one group)
-constexpr int A1_VBYTES = 16 * A1_VPITCH * 2;             // per warp
-constexpr int A1_NRAW = 3;                                // staged raw tiles (two ahead)
-constexpr int A1_SPART = A1_WARPS * 32 * 4 * 4;           // score parts [group][lane][4]
-constexpr int A1_SMEM = A1_NRAW * 4096 + A1_WARPS * A1_VBYTES + A1_SPART;
-constexpr int A1_CTAS_PER_SM = 8;
+constexpr int A1_VPITCH = 256 + 8;                       // bf16 per unpacked V row
+constexpr int A1_VBYTES = 16 * A1_VPITCH * 2;            // 8448
+constexpr int A1_RAW = 16 * 128 + 16 * 96 + 4 * 16 * 8;  // K codes, V codes, 4 scale tensors
+constexpr int A1_WARP_SMEM = A1_VBYTES + 2 * A1_RAW;     // 16640
+constexpr int A1_SMEM = A1_WARPS * A1_WARP_SMEM;
 
 // Codes at bits s0 and s0+3 of u (3-bit) -> bf16 pair (128 + c0, 128 + c1).
 __device__ __forceinline__ uint32_t v3_pair128(uint32_t u, int s0) {
@@ -155,80 +151,94 @@ __device__ __forceinline__ uint2 lds_u2(const uint8_t *p) {
 }
 
 // Raw tile (16 keys from key0; keys past S-1 read key S-1 and are masked
-// later) -> staging: K codes [16][128 B] (16-byte chunk j of key k at chunk
-// j ^ (k % 8), so that eight keys' same chunk sit on distinct banks), V
-// codes [16][96 B], then K scale, K bias, V scale, V bias [4][16][8 B]; 288
-// copies over 128 threads.
-__device__ __forceinline__ void a4_fetch(const uint8_t *kbase, const uint8_t *vbase,
-                                         const uint8_t *const *sc, int S, int key0, uint8_t *raw,
-                                         int tid) {
+// later) -> staging buffer: K codes [16][128 B], V codes [16][96 B], then
+// the K scale, K bias, V scale, V bias of each key [4][16][8 B]. A lane's
+// chunks are fixed: keys key0 + kq[i] at byte offsets that do not change
+// from tile to tile.
+__device__ __forceinline__ void a1_fetch(const uint8_t *kbase, const uint8_t *vbase,
+                                         const uint8_t *s0, const uint8_t *s1, int S, int key0,
+                                         uint8_t *raw, int lane) {
+  // K codes: piece lane + 32 i, i < 4 -> key (lane >> 3) + 4 i, offset (lane & 7) * 16
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int key = min(key0 + (lane >> 3) + 4 * i, S - 1);
+    cp_async16(raw + (lane + 32 * i) * 16, kbase + (size_t)key * 128 + (lane & 7) * 16);
+  }
+  // V codes: pieces 128 + lane + 32 i -> key qq / 6, offset (qq % 6) * 16
 #pragma unroll
   for (int i = 0; i < 3; ++i) {
-    const int q = tid + 128 * i;
-    if (q < 128) {
-      const int kr = q >> 3, j = q & 7, key = min(key0 + kr, S - 1);
-      cp_async16(raw + kr * 128 + ((j ^ (kr & 7)) << 4), kbase + (size_t)key * 128 + j * 16);
-    } else if (q < 224) {
-      const int qq = q - 128, key = min(key0 + qq / 6, S - 1);
-      cp_async16(raw + 2048 + qq * 16, vbase + (size_t)key * 96 + (qq % 6) * 16);
-    } else if (q < 288) {
-      const int qq = q - 224, t = qq >> 4, key = min(key0 + (qq & 15), S - 1);
-      cp_async8(raw + 3584 + qq * 8, sc[t] + (size_t)key * 8);
-    }
+    const int qq = lane + 32 * i;
+    const int key = min(key0 + qq / 6, S - 1);
+    cp_async16(raw + 2048 + qq * 16, vbase + (size_t)key * 96 + (qq % 6) * 16);
+  }
+  // scales: piece lane + 32 i -> tensor (lane >> 4) + 2 i, key lane & 15
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const int key = min(key0 + (lane & 15), S - 1);
+    cp_async8(raw + 3584 + (lane + 32 * i) * 8, (i ? s1 : s0) + (size_t)key * 8);
   }
 }
 
-__global__ void __launch_bounds__(A1_WARPS * 32, A1_CTAS_PER_SM) kv_attn1_kernel(AttnParams p) {
+__global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int bh = blockIdx.x, split = blockIdx.y;
   const int b = bh / p.Hkv, hkv = bh % p.Hkv;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
-  const int G = warp;  // this warp's 64-dim group
   const int k_begin = split * p.kps;
   const int k_end = min(p.S, k_begin + p.kps);
-  uint8_t *raw0 = smem_raw;
-  uint16_t *Vt = reinterpret_cast<uint16_t *>(smem_raw + A1_NRAW * 4096 + warp * A1_VBYTES);
-  float *spart = reinterpret_cast<float *>(smem_raw + A1_NRAW * 4096 + A1_WARPS * A1_VBYTES);
+  uint8_t *wsm = smem_raw + warp * A1_WARP_SMEM;
+  uint16_t *Vt = reinterpret_cast<uint16_t *>(wsm);
+  uint8_t *raw0 = wsm + A1_VBYTES;
 
-  // Q^T as B fragments of group G (row g; zero for rows >= QR) and the
-  // group's q sums of rows 2c, 2c+1.
-  uint32_t qb[4][2];
-  float qs[2];
+  // Q^T as B fragments (row g; zero for rows >= QR) and the per-group q sums
+  // of rows 2c, 2c+1.
+  uint32_t qb[4][4][2];
+  float qs[4][2];
   {
-    float vals[16];
-    float part = 0.f;
-    if (g < p.QR) {
-      const int rep_i = g / p.L, l = g % p.L;
+    float vals[64];
+    const int r = g;
+    float part[4] = {0.f, 0.f, 0.f, 0.f};
+    if (r < p.QR) {
+      const int rep_i = r / p.L, l = r % p.L;
       const int hq = hkv * p.rep + rep_i;
       const uint16_t *qp = p.q + (((size_t)b * p.Hq + hq) * p.L + l) * 256;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float v = rbf(__fmul_rn(bf2f(qp[64 * G + 16 * c + i]), p.scale));
-        vals[i] = v;
-        part += v;
-      }
+      for (int G = 0; G < 4; ++G)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float v = rbf(__fmul_rn(bf2f(qp[64 * G + 16 * c + i]), p.scale));
+          vals[16 * G + i] = v;
+          part[G] += v;
+        }
     } else {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) vals[i] = 0.f;
+      for (int i = 0; i < 64; ++i) vals[i] = 0.f;
     }
 #pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const int d0 = 8 * (m >> 1) + 2 * (m & 1);
-      qb[m][0] = pack_bf2(vals[d0], vals[d0 + 4]);
-      qb[m][1] = pack_bf2(vals[d0 + 1], vals[d0 + 5]);
+    for (int G = 0; G < 4; ++G) {
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const int d0 = 16 * G + 8 * (m >> 1) + 2 * (m & 1);
+        qb[G][m][0] = pack_bf2(vals[d0], vals[d0 + 4]);
+        qb[G][m][1] = pack_bf2(vals[d0 + 1], vals[d0 + 5]);
+      }
+      float t = part[G];
+      t += __shfl_xor_sync(0xffffffffu, t, 1);
+      t += __shfl_xor_sync(0xffffffffu, t, 2);
+      // row g's sum -> lanes needing rows 2c, 2c+1
+      qs[G][0] = __shfl_sync(0xffffffffu, t, (2 * c) * 4);
+      qs[G][1] = __shfl_sync(0xffffffffu, t, (2 * c + 1) * 4);
     }
-    part += __shfl_xor_sync(0xffffffffu, part, 1);
-    part += __shfl_xor_sync(0xffffffffu, part, 2);
-    qs[0] = __shfl_sync(0xffffffffu, part, (2 * c) * 4);
-    qs[1] = __shfl_sync(0xffffffffu, part, (2 * c + 1) * 4);
   }
 
-  float O[4][4];
+  float O[16][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) O[i][0] = O[i][1] = O[i][2] = O[i][3] = 0.f;
+  for (int i = 0; i < 16; ++i) O[i][0] = O[i][1] = O[i][2] = O[i][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-  float bsum[2] = {0.f, 0.f}, psum[2] = {0.f, 0.f};
+  float bsum[4][2], psum[4][2];
+#pragma unroll
+  for (int G = 0; G < 4; ++G) bsum[G][0] = bsum[G][1] = psum[G][0] = psum[G][1] = 0.f;
   // Last key each of this lane's rows (2c, 2c+1) may see: -1 past the query
   // rows, S - L + position under the causal mask.
   int klim[2];
@@ -242,33 +252,35 @@ __global__ void __launch_bounds__(A1_WARPS * 32, A1_CTAS_PER_SM) kv_attn1_kernel
   const int n_tiles = (k_end - k_begin + 15) / 16;
   const uint8_t *kbase = reinterpret_cast<const uint8_t *>(p.kc + head_row0 * 32);
   const uint8_t *vbase = reinterpret_cast<const uint8_t *>(p.vc + head_row0 * 24);
-  const uint8_t *scb[4] = {reinterpret_cast<const uint8_t *>(p.ks + head_row0 * 4),
-                           reinterpret_cast<const uint8_t *>(p.kb + head_row0 * 4),
-                           reinterpret_cast<const uint8_t *>(p.vs + head_row0 * 4),
-                           reinterpret_cast<const uint8_t *>(p.vb + head_row0 * 4)};
-#pragma unroll 1
-  for (int t = 0; t < A1_NRAW - 1; ++t) {
-    if (t < n_tiles) a4_fetch(kbase, vbase, scb, p.S, k_begin + 16 * t, raw0 + t * 4096, tid);
+  // scale tensors of this lane's two pieces: (lane >> 4) and (lane >> 4) + 2
+  const uint16_t *sc_t[4] = {p.ks, p.kb, p.vs, p.vb};
+  const uint8_t *sb0 = reinterpret_cast<const uint8_t *>(((lane >> 4) ? sc_t[1] : sc_t[0]) + head_row0 * 4);
+  const uint8_t *sb1 = reinterpret_cast<const uint8_t *>(((lane >> 4) ? sc_t[3] : sc_t[2]) + head_row0 * 4);
+  int it = 0;
+  int t_cur = warp;
+  if (t_cur < n_tiles) a1_fetch(kbase, vbase, sb0, sb1, p.S, k_begin + 16 * t_cur, raw0, lane);
+  cp_async_commit();
+  for (; t_cur < n_tiles; t_cur += A1_WARPS, ++it) {
+    const int t_next = t_cur + A1_WARPS;
+    if (t_next < n_tiles)
+      a1_fetch(kbase, vbase, sb0, sb1, p.S, k_begin + 16 * t_next,
+               raw0 + ((it + 1) & 1) * A1_RAW, lane);
     cp_async_commit();
-  }
-#pragma unroll 1
-  for (int t = 0; t < n_tiles; ++t) {
-    cp_async_wait<A1_NRAW - 2>();
-    __syncthreads();  // tile t staged; every warp is done with tile t - 1
-    {
-      const int tn = t + A1_NRAW - 1;
-      if (tn < n_tiles)
-        a4_fetch(kbase, vbase, scb, p.S, k_begin + 16 * tn, raw0 + (tn % A1_NRAW) * 4096, tid);
-      cp_async_commit();
-    }
-    const uint8_t *rw = raw0 + (t % A1_NRAW) * 4096;
-    const uint8_t *Sk = rw + 3584;
-    const int key0 = k_begin + 16 * t;
-    // ---- this group's part of S^T for keys g, g+8 and rows 2c, 2c+1 ----
-    {
-      const int ch = 2 * G + (c >> 1);  // 16-byte chunk of the 128-byte K row
-      const uint2 wa = lds_u2(rw + g * 128 + ((ch ^ (g & 7)) << 4) + (c & 1) * 8);
-      const uint2 wb = lds_u2(rw + (g + 8) * 128 + ((ch ^ (g & 7)) << 4) + (c & 1) * 8);
+    cp_async_wait<1>();
+    __syncwarp();
+    const uint8_t *rw = raw0 + (it & 1) * A1_RAW;
+    const uint8_t *Kr = rw, *Vr = rw + 2048, *Sk = rw + 3584, *Bk = Sk + 128, *Sv = Sk + 256,
+                  *Bv = Sk + 384;
+    const int key0 = k_begin + 16 * t_cur;
+
+    // ---- scores S^T for keys g, g+8 and rows 2c, 2c+1 ----
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint2 ksg = lds_u2(Sk + g * 8), ks8 = lds_u2(Sk + (g + 8) * 8);
+    const uint2 kbg = lds_u2(Bk + g * 8), kb8 = lds_u2(Bk + (g + 8) * 8);
+#pragma unroll
+    for (int G = 0; G < 4; ++G) {
+      const uint2 wa = lds_u2(Kr + g * 128 + G * 32 + 8 * c);
+      const uint2 wb = lds_u2(Kr + (g + 8) * 128 + G * 32 + 8 * c);
       uint32_t pa[2][4], pb[2][4];
       nib_pairs4(wa.x, pa[0]);
       nib_pairs4(wa.y, pa[1]);
@@ -278,55 +290,25 @@ __global__ void __launch_bounds__(A1_WARPS * 32, A1_CTAS_PER_SM) kv_attn1_kernel
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
         const int i0 = 2 * (m & 1), h = m >> 1;
-        mma_bf16(d, pa[h][i0], pb[h][i0], pa[h][i0 + 1], pb[h][i0 + 1], qb[m][0], qb[m][1]);
+        mma_bf16(d, pa[h][i0], pb[h][i0], pa[h][i0 + 1], pb[h][i0 + 1], qb[G][m][0], qb[G][m][1]);
       }
-      const uint2 ksg = lds_u2(Sk + g * 8), ks8 = lds_u2(Sk + (g + 8) * 8);
-      const uint2 kbg = lds_u2(Sk + 128 + g * 8), kb8 = lds_u2(Sk + 128 + (g + 8) * 8);
       const float s_g = bf_at2(ksg, G), s_8 = bf_at2(ks8, G);
       const float bp_g = fmaf(-128.f, s_g, bf_at2(kbg, G));
       const float bp_8 = fmaf(-128.f, s_8, bf_at2(kb8, G));
-      *reinterpret_cast<float4 *>(spart + (G * 32 + lane) * 4) =
-          make_float4(fmaf(s_g, d[0], bp_g * qs[0]), fmaf(s_g, d[1], bp_g * qs[1]),
-                      fmaf(s_8, d[2], bp_8 * qs[0]), fmaf(s_8, d[3], bp_8 * qs[1]));
+      sc[0] += fmaf(s_g, d[0], bp_g * qs[G][0]);
+      sc[1] += fmaf(s_g, d[1], bp_g * qs[G][1]);
+      sc[2] += fmaf(s_8, d[2], bp_8 * qs[G][0]);
+      sc[3] += fmaf(s_8, d[3], bp_8 * qs[G][1]);
     }
-    // ---- V codes of this group -> exact bf16 rows of Vt (16 keys x 64) ----
-    {
-      const int kk = lane >> 1, hh = lane & 1;  // key, 32-dim half of the group
-      const uint32_t *vw =
-          reinterpret_cast<const uint32_t *>(rw + 2048 + kk * 96 + 24 * G + 12 * hh);
-      const uint32_t v0 = vw[0], v1 = vw[1], v2 = vw[2];
-      uint4 *dv = reinterpret_cast<uint4 *>(Vt + kk * A1_VPITCH + 32 * hh);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t u = j == 0 ? (v0 & 0xFFFFFFu)
-                         : j == 1 ? (__funnelshift_r(v0, v1, 24) & 0xFFFFFFu)
-                         : j == 2 ? (__funnelshift_r(v1, v2, 16) & 0xFFFFFFu)
-                                  : (v2 >> 8);
-        dv[j] = make_uint4(v3_pair128(u, 0), v3_pair128(u, 6), v3_pair128(u, 12), v3_pair128(u, 18));
-      }
-    }
-    const uint2 vsg = lds_u2(Sk + 256 + g * 8), vs8 = lds_u2(Sk + 256 + (g + 8) * 8);
-    const uint2 vbg = lds_u2(Sk + 384 + g * 8), vb8 = lds_u2(Sk + 384 + (g + 8) * 8);
-    __syncthreads();  // every group's score part is in
-    // ---- scores: the four parts added in group order, rounded, masked ----
-    float sc[4];
-    {
-      const float4 p0 = *reinterpret_cast<const float4 *>(spart + (0 * 32 + lane) * 4);
-      const float4 p1 = *reinterpret_cast<const float4 *>(spart + (1 * 32 + lane) * 4);
-      const float4 p2 = *reinterpret_cast<const float4 *>(spart + (2 * 32 + lane) * 4);
-      const float4 p3 = *reinterpret_cast<const float4 *>(spart + (3 * 32 + lane) * 4);
-      sc[0] = ((p0.x + p1.x) + p2.x) + p3.x;
-      sc[1] = ((p0.y + p1.y) + p2.y) + p3.y;
-      sc[2] = ((p0.z + p1.z) + p2.z) + p3.z;
-      sc[3] = ((p0.w + p1.w) + p2.w) + p3.w;
-    }
+    // bf16 scores; mask keys outside [k_begin, k_end), rows >= QR and the
+    // causal bound key <= S - L + l.
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int key = key0 + g + 8 * (j >> 1);
       const bool ok = key < k_end && key <= klim[j & 1];
       sc[j] = ok ? rbf(sc[j]) : -INFINITY;
     }
-    // ---- online softmax (rows 2c, 2c+1; the same in every warp) ----
+    // ---- online softmax (rows 2c, 2c+1) ----
     float mx[2] = {fmaxf(sc[0], sc[2]), fmaxf(sc[1], sc[3])};
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -346,11 +328,14 @@ __global__ void __launch_bounds__(A1_WARPS * 32, A1_CTAS_PER_SM) kv_attn1_kernel
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         l_run[h] *= alpha[h];
-        bsum[h] *= alpha[h];
-        psum[h] *= alpha[h];
+#pragma unroll
+        for (int G = 0; G < 4; ++G) {
+          bsum[G][h] *= alpha[h];
+          psum[G][h] *= alpha[h];
+        }
       }
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < 16; ++i) {
         O[i][0] *= alpha[0];
         O[i][1] *= alpha[1];
         O[i][2] *= alpha[0];
@@ -364,33 +349,60 @@ __global__ void __launch_bounds__(A1_WARPS * 32, A1_CTAS_PER_SM) kv_attn1_kernel
       e[j] = sc[j] == -INFINITY ? 0.f : __expf(sc[j] - mnew[h]);
       l_run[h] += e[j];
     }
-    // P^T fragments of this group: p = bf16(e * vs); V bias term on the side.
-    uint32_t pB0, pB1;
-    {
+    // P^T fragments per V group: p = bf16(e * vs); V bias term on the side.
+    const uint2 vsg = lds_u2(Sv + g * 8), vs8 = lds_u2(Sv + (g + 8) * 8);
+    const uint2 vbg = lds_u2(Bv + g * 8), vb8 = lds_u2(Bv + (g + 8) * 8);
+    uint32_t pB[4][2];
+#pragma unroll
+    for (int G = 0; G < 4; ++G) {
       const float sg = bf_at2(vsg, G), s8 = bf_at2(vs8, G);
       const float bg = bf_at2(vbg, G), b8 = bf_at2(vb8, G);
-      bsum[0] = fmaf(e[0], bg, fmaf(e[2], b8, bsum[0]));
-      bsum[1] = fmaf(e[1], bg, fmaf(e[3], b8, bsum[1]));
+      bsum[G][0] = fmaf(e[0], bg, fmaf(e[2], b8, bsum[G][0]));
+      bsum[G][1] = fmaf(e[1], bg, fmaf(e[3], b8, bsum[G][1]));
       const uint32_t x0 = pack_bf2(e[0] * sg, e[1] * sg);  // key g: rows 2c, 2c+1
       const uint32_t x1 = pack_bf2(e[2] * s8, e[3] * s8);  // key g+8
-      psum[0] += __uint_as_float(x0 << 16) + __uint_as_float(x1 << 16);
-      psum[1] += __uint_as_float(x0 & 0xFFFF0000u) + __uint_as_float(x1 & 0xFFFF0000u);
-      pB0 = movmatrix_trans(x0);  // keys 2c, 2c+1 of row g
-      pB1 = movmatrix_trans(x1);  // keys 8+2c, 8+2c+1
+      psum[G][0] += __uint_as_float(x0 << 16) + __uint_as_float(x1 << 16);
+      psum[G][1] += __uint_as_float(x0 & 0xFFFF0000u) + __uint_as_float(x1 & 0xFFFF0000u);
+      pB[G][0] = movmatrix_trans(x0);  // keys 2c, 2c+1 of row g
+      pB[G][1] = movmatrix_trans(x1);  // keys 8+2c, 8+2c+1
     }
-    __syncwarp();  // Vt rows of this warp written
-    // ---- O^T += V^T P^T over this group's 64 dims (V as 128 + c) ----
+    // ---- V codes -> exact bf16 rows of Vt ----
+    {
+      const int kk = lane >> 1, hh = lane & 1;
+      const uint32_t *vw = reinterpret_cast<const uint32_t *>(Vr + kk * 96 + hh * 48);
+      uint32_t w[13];
+#pragma unroll
+      for (int i = 0; i < 12; ++i) w[i] = vw[i];
+      w[12] = 0;
+      uint16_t *dst = Vt + kk * A1_VPITCH + 128 * hh;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int bit = 24 * j, wi = bit >> 5, sh = bit & 31;
+        const uint32_t u = __funnelshift_r(w[wi], w[wi + 1], sh) & 0xFFFFFFu;
+        uint4 o;
+        o.x = v3_pair128(u, 0);
+        o.y = v3_pair128(u, 6);
+        o.z = v3_pair128(u, 12);
+        o.w = v3_pair128(u, 18);
+        *reinterpret_cast<uint4 *>(dst + 8 * j) = o;
+      }
+    }
+    __syncwarp();
+    // ---- O^T += V^T P^T (V as 128 + c; 128 * sum(p) removed at the end) ----
     {
       const int q = lane >> 3, r = lane & 7;
       const int key = (q >> 1) * 8 + r, dq = (q & 1) * 8;
 #pragma unroll
-      for (int mt = 0; mt < 4; ++mt) {
-        uint32_t a0, a1, a2, a3;
-        ldsm_x4_trans(a0, a1, a2, a3, Vt + key * A1_VPITCH + 16 * mt + dq);
-        mma_bf16(O[mt], a0, a1, a2, a3, pB0, pB1);
+      for (int G = 0; G < 4; ++G) {
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4_trans(a0, a1, a2, a3, Vt + key * A1_VPITCH + 64 * G + 16 * mt + dq);
+          mma_bf16(O[4 * G + mt], a0, a1, a2, a3, pB[G][0], pB[G][1]);
+        }
       }
     }
-    __syncwarp();  // Vt read before the next tile rewrites it
+    __syncwarp();
   }
   cp_async_wait<0>();
 
@@ -400,27 +412,57 @@ __global__ void __launch_bounds__(A1_WARPS * 32, A1_CTAS_PER_SM) kv_attn1_kernel
 #pragma unroll
     for (int o = 4; o < 32; o <<= 1) {
       l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], o);
-      bsum[h] += __shfl_xor_sync(0xffffffffu, bsum[h], o);
-      psum[h] += __shfl_xor_sync(0xffffffffu, psum[h], o);
+#pragma unroll
+      for (int G = 0; G < 4; ++G) {
+        bsum[G][h] += __shfl_xor_sync(0xffffffffu, bsum[G][h], o);
+        psum[G][h] += __shfl_xor_sync(0xffffffffu, psum[G][h], o);
+      }
     }
   }
-  // ---- this group's dims of the split partial (m and l are the same in
-  // every warp; warp 0 writes them) ----
-  const size_t cta = (size_t)bh * p.nsplit + split;
+  // ---- merge the 4 warps in shared memory: [warp][row 8][dim 256] + m, l ----
+  __syncthreads();
+  float *Om = reinterpret_cast<float *>(smem_raw);            // 4 x 8 x 256 floats (32 KB)
+  float *Mm = Om + A1_WARPS * 8 * 256, *Lm = Mm + A1_WARPS * 8;
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int row = 2 * c + h;
-    if (row >= p.QR) continue;
-    const float off = fmaf(-128.f, psum[h], bsum[h]);
-    float *op = p.opart + (cta * 32 + row) * 256 + 64 * G;
+  for (int i = 0; i < 16; ++i) {
+    const int G = i >> 2, mt = i & 3;
+    const int d0 = 64 * G + 16 * mt + g;
 #pragma unroll
-    for (int mt = 0; mt < 4; ++mt) {
-      op[16 * mt + g] = O[mt][h] + off;
-      op[16 * mt + g + 8] = O[mt][2 + h] + off;
+    for (int h = 0; h < 2; ++h) {
+      const int row = 2 * c + h;
+      const float off = fmaf(-128.f, psum[G][h], bsum[G][h]);
+      Om[(warp * 8 + row) * 256 + d0] = O[i][h] + off;
+      Om[(warp * 8 + row) * 256 + d0 + 8] = O[i][2 + h] + off;
     }
-    if (warp == 0 && g == 0) {
-      p.mpart[cta * 32 + row] = m_run[h];
-      p.lpart[cta * 32 + row] = l_run[h];
+  }
+  if (g == 0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      Mm[warp * 8 + 2 * c + h] = m_run[h];
+      Lm[warp * 8 + 2 * c + h] = l_run[h];
+    }
+  }
+  __syncthreads();
+  const size_t cta = (size_t)bh * p.nsplit + split;
+  for (int i = threadIdx.x; i < 8 * 256; i += blockDim.x) {
+    const int row = i >> 8, d = i & 255;
+    if (row >= p.QR) continue;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < A1_WARPS; ++w) M = fmaxf(M, Mm[w * 8 + row]);
+    float num = 0.f, den = 0.f;
+#pragma unroll
+    for (int w = 0; w < A1_WARPS; ++w) {
+      const float mw = Mm[w * 8 + row];
+      if (mw == -INFINITY) continue;
+      const float sw = expf(mw - M);
+      num = fmaf(Om[(w * 8 + row) * 256 + d], sw, num);
+      den = fmaf(Lm[w * 8 + row], sw, den);
+    }
+    p.opart[(cta * 32 + row) * 256 + d] = num;
+    if (d == 0) {
+      p.mpart[cta * 32 + row] = M;
+      p.lpart[cta * 32 + row] = den;
     }
   }
 }
@@ -448,6 +490,30 @@ __device__ __forceinline__ void ldsm_x4(uint32_t &r0, uint32_t &r1, uint32_t &r2
   const uint32_t a = (uint32_t)__cvta_generic_to_shared(smem_ptr);
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(a));
+}
+
+// Raw tile (16 keys from key0; keys past S-1 read key S-1 and are masked
+// later) -> staging: K codes [16][128 B] (16-byte chunk j of key k at chunk
+// j ^ (k % 8), so that eight keys' same chunk sit on distinct banks), V
+// codes [16][96 B], then K scale, K bias, V scale, V bias [4][16][8 B]; 288
+// copies over 128 threads.
+__device__ __forceinline__ void a4_fetch(const uint8_t *kbase, const uint8_t *vbase,
+                                         const uint8_t *const *sc, int S, int key0, uint8_t *raw,
+                                         int tid) {
+#pragma unroll
+  for (int i = 0; i < 3; ++i) {
+    const int q = tid + 128 * i;
+    if (q < 128) {
+      const int kr = q >> 3, j = q & 7, key = min(key0 + kr, S - 1);
+      cp_async16(raw + kr * 128 + ((j ^ (kr & 7)) << 4), kbase + (size_t)key * 128 + j * 16);
+    } else if (q < 224) {
+      const int qq = q - 128, key = min(key0 + qq / 6, S - 1);
+      cp_async16(raw + 2048 + qq * 16, vbase + (size_t)key * 96 + (qq % 6) * 16);
+    } else if (q < 288) {
+      const int qq = q - 224, t = qq >> 4, key = min(key0 + (qq & 15), S - 1);
+      cp_async8(raw + 3584 + qq * 8, sc[t] + (size_t)key * 8);
+    }
+  }
 }
 
 __global__ void __launch_bounds__(A4_WARPS * 32, 3) kv_attn4_kernel(AttnParams p) {
@@ -705,10 +771,10 @@ __global__ void __launch_bounds__(A4_WARPS * 32, 3) kv_attn4_kernel(AttnParams p
   }
 }
 
-// Keys per split: about `per_sm` CTAs per SM over all (batch, kv head)
-// pairs, in multiples of 64 keys.
-static void attn_split(int bhk, int S, int per_sm, int &nsplit, int &kps) {
-  int target = (per_sm * 148 + bhk - 1) / bhk;
+// Keys per split: about three CTAs per SM over all (batch, kv head) pairs,
+// in multiples of 64 keys.
+static void attn_split(int bhk, int S, int &nsplit, int &kps) {
+  int target = (3 * 148 + bhk - 1) / bhk;
   if (target < 1) target = 1;
   kps = (S + target - 1) / target;
   kps = (kps + ATT_ROUND - 1) / ATT_ROUND * ATT_ROUND;
@@ -725,10 +791,9 @@ size_t vb_kv_attn_workspace_size(int32_t batch, int32_t q_heads, int32_t L,
                                  int32_t dim, int32_t keys) {
   (void)q_heads; (void)L; (void)dim;
   if (batch <= 0 || keys <= 0) return 0;
-  // Upper bound for kv_heads <= 64: at most A1_CTAS_PER_SM x 148 split CTAs
-  // overall plus one per (batch, kv head) (the split rounds keys up to
-  // 64-key multiples).
-  const size_t ctas = (size_t)A1_CTAS_PER_SM * 148 + (size_t)batch * 64;
+  // Upper bound for kv_heads <= 64: at most 3 x 148 split CTAs overall plus
+  // one per (batch, kv head) (the split rounds keys up to 64-key multiples).
+  const size_t ctas = 3 * 148 + (size_t)batch * 64;
   return align_up(ctas * 32 * 256 * sizeof(float), 256) + 2 * align_up(ctas * 32 * sizeof(float), 256);
 }
 
@@ -757,7 +822,7 @@ int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
   p.vs = v_scales; p.vb = v_biases; p.rv = rv_blocks;
   p.B = batch; p.Hq = q_heads; p.Hkv = kv_heads; p.L = L; p.S = keys; p.cap = cap;
   p.rep = rep; p.QR = rep * L; p.causal = causal; p.scale = scale;
-  attn_split(batch * kv_heads, keys, p.QR <= 8 ? A1_CTAS_PER_SM : 3, p.nsplit, p.kps);
+  attn_split(batch * kv_heads, keys, p.nsplit, p.kps);
   VB_REQUIRE(p.nsplit <= ATT_MAX_SPLITS, "vb_kv_decode_attn: %d splits", p.nsplit);
   const size_t ctas = (size_t)batch * kv_heads * p.nsplit;
   const size_t obytes = align_up(ctas * 32 * 256 * sizeof(float), 256);
