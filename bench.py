@@ -274,8 +274,19 @@ def run_prefill_ep_leg(world: int, rank: int, steps: int = 10, warmup: int = 3, 
     per = T // world
     x_all = input_tokens(seed, T)
     x = x_all[rank * per:(rank + 1) * per].contiguous()
-    del x_all
-    comm = NcclComm()
+    if rank != 0:
+        del x_all
+    # NCCL prints its version line on the first communicator it creates in
+    # the process: keep it off stdout, where the bench line goes.
+    sys.stdout.flush()
+    saved_fd = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        comm = NcclComm()
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved_fd, 1)
+        os.close(saved_fd)
     ep = NativeEp(blk, owner, comm, max_tokens=per)
     out = torch.empty_like(x)
     for _ in range(max(warmup, 3)):
@@ -293,14 +304,16 @@ def run_prefill_ep_leg(world: int, rank: int, steps: int = 10, warmup: int = 3, 
     comm.close()
     identical = None
     if rank == 0:
+        # the whole batch on one device (its reduce groups come from the
+        # whole batch's routes, as the EP call's do): rank 0's rows must match
         del ep, blk, pool
         torch.cuda.empty_cache()
         full = make_layer(seed, 0, QuantPool.empty_blob(NE, HH, II, 4, 64, "cuda"), range(NE),
                           "cuda", router_bias=bias)
-        ref = moe_prefill(full, x)
+        ref = moe_prefill(full, x_all)[:per]
         torch.cuda.synchronize()
         identical = bool(torch.equal(ref.view(torch.int16), out.view(torch.int16)))
-        del full, ref
+        del full, ref, x_all
         torch.cuda.empty_cache()
     dist.barrier()
     flops = PREFILL_FLOPS_32K * T / 32768
@@ -312,6 +325,8 @@ def run_prefill_ep_leg(world: int, rank: int, steps: int = 10, warmup: int = 3, 
             "peak_kind": peak_kind, "experts_per_gpu": len(owned), "hot_experts_replicated": n_hot,
             "placement": f"from an earlier batch's routes: experts with >= {hot_share:.0%} of "
                          "them on every rank, the rest LPT over their counts",
+            "ep_bit_identical_reference": "rank 0's rows of vb_moe_prefill over the whole "
+                                          "batch on one device",
             "ep_bit_identical": identical, "scaling": "strong"}
 
 

@@ -159,7 +159,7 @@ def test_native_ep_one_rank_matches_single_device(cuda):
         comm.close()
 
 
-@pytest.mark.parametrize("native", [False, True])
+@pytest.mark.parametrize("native", [False, True], ids=["torch_dist", "native"])
 def test_ep_prefill_two_gpus_matches_one(cuda, native):
     import torch
     import torch.multiprocessing as mp
@@ -181,7 +181,7 @@ def test_ep_prefill_two_gpus_matches_one(cuda, native):
     assert np.array_equal(got, ref)
 
 
-@pytest.mark.parametrize("native", [False, True])
+@pytest.mark.parametrize("native", [False, True], ids=["torch_dist", "native"])
 def test_ep_prefill_two_gpus_with_replicated_hot_experts(cuda, native):
     """Experts with many routes held by both GPUs (each computes them for
     its own tokens), the rest owned by one GPU: bit-identical to one GPU."""
