@@ -16,6 +16,7 @@ not installable here) on the host cores with a bounded sample per step.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -100,6 +101,22 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(rows)}
 
 
+@contextlib.contextmanager
+def stdout_to_stderr():
+    """Send file descriptor 1 to stderr while NCCL creates a communicator:
+    NCCL prints its version line there, and stdout carries only the bench
+    line."""
+    sys.stdout.flush()
+    saved_fd = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        yield
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved_fd, 1)
+        os.close(saved_fd)
+
+
 def dist_setup(n_gpus):
     import torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -109,8 +126,9 @@ def dist_setup(n_gpus):
         import datetime
         import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        with stdout_to_stderr():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local
@@ -276,17 +294,8 @@ def run_prefill_ep_leg(world: int, rank: int, steps: int = 10, warmup: int = 3, 
     x = x_all[rank * per:(rank + 1) * per].contiguous()
     if rank != 0:
         del x_all
-    # NCCL prints its version line on the first communicator it creates in
-    # the process: keep it off stdout, where the bench line goes.
-    sys.stdout.flush()
-    saved_fd = os.dup(1)
-    os.dup2(2, 1)
-    try:
+    with stdout_to_stderr():
         comm = NcclComm()
-    finally:
-        sys.stdout.flush()
-        os.dup2(saved_fd, 1)
-        os.close(saved_fd)
     ep = NativeEp(blk, owner, comm, max_tokens=per)
     out = torch.empty_like(x)
     for _ in range(max(warmup, 3)):
