@@ -434,6 +434,14 @@ int vb_kv_quant_append(const uint16_t *src, const float *so4_blocks,
                        int32_t cap, uint32_t *codes, uint16_t *scales,
                        uint16_t *biases, vb_stream_t stream);
 
+/* The same with the row offset read on the device (*offset; rows past cap
+ * are skipped and flag VB_STATUS_BOUNDS in the nullable status word). */
+int vb_kv_quant_append_at(const uint16_t *src, const float *so4_blocks,
+                          int32_t batch, int32_t heads, int32_t n, int32_t dim,
+                          int32_t group, int32_t bits, const int32_t *offset,
+                          int32_t cap, uint32_t *codes, uint16_t *scales,
+                          uint16_t *biases, int32_t *status, vb_stream_t stream);
+
 /* Rotation only: dst = src @ R (4x4 SO(4) blocks, R rounded to bf16),
  * bf16 [rows, D]; transpose != 0 applies R^T (quant_kv.py:68-70 with Rv.T,
  * kv_quant_patch.py:67-68). */
@@ -460,6 +468,32 @@ int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
                       float scale, int32_t causal, uint16_t *out,
                       void *workspace, size_t workspace_bytes,
                       vb_stream_t stream);
+
+/* The same with the key count read on the device: keys = *pos + L (pos =
+ * cache length before this step's L rows); keys_max (<= cap) sizes the split
+ * grid, so one launch (and one CUDA graph node) serves every step. Used by the
+ * decode stack, whose cache offset lives in device memory. */
+int vb_kv_decode_attn_at(const uint16_t *q, const uint32_t *k_codes,
+                         const uint16_t *k_scales, const uint16_t *k_biases,
+                         const uint32_t *v_codes, const uint16_t *v_scales,
+                         const uint16_t *v_biases, const float *rv_blocks,
+                         int32_t batch, int32_t q_heads, int32_t kv_heads,
+                         int32_t L, int32_t dim, const int32_t *pos, int32_t keys_max,
+                         int32_t cap, int32_t group, int32_t k_bits, int32_t v_bits,
+                         float scale, int32_t causal, uint16_t *out, void *workspace,
+                         size_t workspace_bytes, vb_stream_t stream);
+
+/* GQA decode attention over a plain bf16 cache [B, Hkv, cap, 256] (the MTP
+ * layer's mlx-lm KVCache attended by mx.fast.scaled_dot_product_attention,
+ * mtp/qwen3_next_mtp.py:40-56): float32 scores, softmax and P V, one bf16
+ * rounding. keys = *pos + pos_add + L, read on the device; q bf16
+ * [B, Hq, L, 256]; out bf16 [B, Hq, L, 256]; (Hq/Hkv) * L <= 32. Workspace as
+ * vb_kv_attn_workspace_size(batch, q_heads, L, dim, keys_max) + 256. */
+int vb_kv_bf16_attn_at(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                       int32_t batch, int32_t q_heads, int32_t kv_heads, int32_t L,
+                       int32_t dim, const int32_t *pos, int32_t pos_add, int32_t keys_max,
+                       int32_t cap, float scale, int32_t causal, uint16_t *out,
+                       void *workspace, size_t workspace_bytes, vb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Expert residency: per-layer expert -> slot state of a pool of `cap` slots
@@ -587,6 +621,18 @@ int vb_gated_delta_step(const uint16_t *q, const uint16_t *k,
                         int32_t tokens, int32_t k_heads, int32_t v_heads,
                         int32_t k_dim, int32_t v_dim, vb_stream_t stream);
 
+/* Speculative-verify form (batch 1): states f32 [slots, v_heads, v_dim, 128];
+ * the step starts from states[*in_slot] (slot index read on the device: the
+ * accepted count - 1 of the previous verify) and writes the state after
+ * token t to states[t], t < tokens <= slots (mtp/kv_cache.py:80-100 keeps
+ * these per-token checkpoints for the commit). */
+int vb_gated_delta_step_at(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                           const float *g, int32_t g_per_key, const float *beta,
+                           float *states, int32_t slots, const int32_t *in_slot,
+                           const uint8_t *mask, uint16_t *y, int32_t batch,
+                           int32_t tokens, int32_t k_heads, int32_t v_heads,
+                           int32_t k_dim, int32_t v_dim, vb_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Affine dequantization (MLX mx.dequantize; the reference's per-element
  * `qvalue`, native/ext/compute/fused_moe.cpp:131-145, and its inline form in
@@ -601,6 +647,120 @@ int vb_dequantize(const uint32_t *words, const uint16_t *scales,
                   const uint16_t *biases, int64_t rows, int32_t cols,
                   int32_t group, int32_t bits, int32_t out_bf16, void *out,
                   vb_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Dense decoder layers of the Qwen3-Next stack around the MoE block (mlx-lm
+ * 0.31.3 models/qwen3_next.py as patched by the reference; 4-bit group-64
+ * quantized linears as in mtp/qwen3_next_mtp.py:170-181).
+ *
+ * vb_qlinear: y[T, N] = x' @ dequant(W)^T (+ residual), MLX quantized_matmul
+ * (per group s * sum(x q) + b * sum(x), float32, one bf16 rounding; the
+ * residual add is a second bf16 rounding, h = x + r of the decoder layer).
+ * x' = x, or rms_norm(x) * norm_w (bf16 at each op) when norm_w != NULL.
+ * T <= 8, in_features a multiple of 256, bits 4, group 64. The workspace
+ * (vb_qlinear_workspace_size, zero-filled once, reusable) holds the split-K
+ * partials and per-row-block tickets. */
+size_t vb_qlinear_workspace_size(int32_t tokens, int32_t in_features, int32_t out_features);
+int vb_qlinear(const uint16_t *x, int32_t tokens, int32_t in_features,
+               const uint32_t *codes, const uint16_t *scales, const uint16_t *biases,
+               int32_t out_features, int32_t group, int32_t bits, const uint16_t *norm_w,
+               float norm_eps, const uint16_t *residual, uint16_t *y, void *workspace,
+               size_t workspace_bytes, vb_stream_t stream);
+
+/* mx.fast.rms_norm with an optional residual add before it: h = bf16(x + r)
+ * (written to h_out when given), y = bf16(bf16(h * rsqrt(mean(h^2) + eps)) * w)
+ * (w NULL: unit weight). x, residual, h_out [rows, dim]; y rows y_stride
+ * elements apart (0: dim), so two norms can fill the halves of one
+ * concatenated row (the MTP head's fc input). */
+int vb_rms_norm(const uint16_t *x, const uint16_t *residual, const uint16_t *weight,
+                int32_t rows, int32_t dim, float eps, uint16_t *h_out, uint16_t *y,
+                int32_t y_stride, vb_stream_t stream);
+
+/* mx.argmax over each row of bf16 values (ties to the smallest index). The
+ * workspace (vb_argmax_workspace_size, zero-filled once) holds tickets. */
+size_t vb_argmax_workspace_size(int32_t rows);
+int vb_argmax(const uint16_t *values, int32_t rows, int32_t n, int32_t *out, void *workspace,
+              size_t workspace_bytes, vb_stream_t stream);
+
+/* nn.QuantizedEmbedding: out[t] = dequant(table row ids[t]) (bf16, 4-bit
+ * group 64). Ids out of range give zero rows and VB_STATUS_BOUNDS. */
+int vb_embed_rows(const int32_t *ids, int32_t tokens, const uint32_t *codes,
+                  const uint16_t *scales, const uint16_t *biases, int32_t vocab,
+                  int32_t hidden, int32_t group, int32_t bits, uint16_t *out, int32_t *status,
+                  vb_stream_t stream);
+
+/* Gated-DeltaNet input side (mtp/kv_cache.py:34-91; gated_delta_multistate.py:
+ * 201-226): proj bf16 [T, proj_stride] = in_proj_qkvz | in_proj_ba outputs
+ * (per key head [q Dk, k Dk, v r*Dv, z r*Dv], then per key head [b r, a r]).
+ * conv_buf bf16 [3 + max_tokens, C], C = 2 Hk Dk + Hv Dv: rows [*conv_off,
+ * *conv_off + 3) hold the conv state (conv_off NULL: 0); the call leaves the
+ * state in rows 0..2 and the T new rows in 3..3+T-1, so the state after
+ * accepting a rows is rows [a, a+3). conv_w bf16 [C, 4]. Outputs q, k bf16
+ * [T, Hk, Dk] (rms-normalised and scaled by Dk^-1 / Dk^-0.5), v bf16
+ * [T, Hv, Dv], g and beta f32 [T, Hv]. T <= max_tokens <= 8. */
+int vb_gdn_prepare(const uint16_t *proj, int32_t proj_stride, int32_t tokens, int32_t k_heads,
+                   int32_t v_heads, int32_t head_k, int32_t head_v, uint16_t *conv_buf,
+                   int32_t max_tokens, const int32_t *conv_off, const uint16_t *conv_w,
+                   const float *a_log, const uint16_t *dt_bias, uint16_t *q, uint16_t *k,
+                   uint16_t *v, float *g, float *beta, int32_t *status, vb_stream_t stream);
+
+/* Gated RMSNorm of the recurrence output (kv_cache.py:102, mlx-lm
+ * Qwen3NextRMSNormGated): out = silu(z) * (w * rms_norm(y)), z read from the
+ * projection rows. y, out bf16 [T, Hv, Dv]; weight bf16 [Dv]. */
+int vb_gdn_gated_norm(const uint16_t *y, const uint16_t *proj, int32_t proj_stride,
+                      int32_t tokens, int32_t k_heads, int32_t v_heads, int32_t head_k,
+                      int32_t head_v, const uint16_t *weight, float eps, uint16_t *out,
+                      vb_stream_t stream);
+
+/* Attention input side (kv_quant_patch.py:29-56): proj bf16 [T, proj_stride]
+ * = q_proj (per head [query 256, gate 256]) | k_proj | v_proj. Queries and
+ * keys get their RMSNorm (weights [256]) and RoPE over the first rope_dims
+ * dims at position *pos + pos_add + t (non-traditional pairs (i, i + dims/2),
+ * theta = pos * base^(-2i/dims)); queries are then rotated by the SO(4)
+ * blocks rk_blocks (NULL: none). q_out bf16 [Hq, T, 256]; keys and values go
+ * to k_out/v_out [Hkv, T, 256] (kv_cap 0) or into bf16 caches
+ * [Hkv, kv_cap, 256] at their positions. */
+int vb_attn_prepare(const uint16_t *proj, int32_t proj_stride, int32_t tokens, int32_t q_heads,
+                    int32_t kv_heads, int32_t head_dim, const uint16_t *q_norm_w,
+                    const uint16_t *k_norm_w, float eps, int32_t rope_dims, float rope_base,
+                    const int32_t *pos, int32_t pos_add, const float *rk_blocks,
+                    uint16_t *q_out, uint16_t *k_out, uint16_t *v_out, int32_t kv_cap,
+                    int32_t *status, vb_stream_t stream);
+
+/* output * sigmoid(gate) (kv_quant_patch.py:70-71): attn_out bf16 [Hq, T, 256]
+ * -> out bf16 [T, Hq * 256], gate read from the projection rows. */
+int vb_attn_gate(const uint16_t *attn_out, const uint16_t *proj, int32_t proj_stride,
+                 int32_t tokens, int32_t q_heads, uint16_t *out, vb_stream_t stream);
+
+/* Speculative (MTP) loop, device side. state int32 [16]: [0] main cache
+ * length, [1] MTP cache length, [2] accepted rows of the last verify or
+ * prefill chunk, [3] that minus one (recurrent state slot), [4] pending
+ * token, [5] emitted tokens, [6] verify steps, [7..14] histogram of matched
+ * drafts. ids int32 [1 + drafts]: ids[0] pending token, ids[1..] drafts; the
+ * verify step feeds ids[0..verify_len).
+ * vb_spec_accept (generate.py:338-352, 818-853): mode 0 compares the verify
+ * argmaxes preds[verify_len] with the drafts, commits a = min(matched + 1,
+ * verify_len) rows, appends the emitted tokens (drafts[:matched] and the
+ * model's token at the first mismatch) to out_tokens, sets the pending token;
+ * mode 1 (prefill chunk) commits all rows and also writes the pending token
+ * to ids[0]. Both copy h_last to prev_h and the last committed row of
+ * verify_hidden [verify_len, hidden] to h_last. */
+int vb_spec_accept(int32_t *state, int32_t *ids, const int32_t *preds, int32_t verify_len,
+                   int32_t drafts, int32_t mode, const uint16_t *verify_hidden,
+                   uint16_t *h_last, uint16_t *prev_h, int32_t hidden, int32_t *out_tokens,
+                   int32_t out_cap, vb_stream_t stream);
+/* MTP cache sync inputs (drafter.py:178-186): slot i < a gets ids[i] and
+ * hidden (i == 0 ? prev_h : verify_hidden[i - 1]); later slots repeat slot
+ * a - 1. sync_ids [verify_len], sync_hidden [verify_len, hidden]. Then
+ * ids[0] = the pending token, for the next drafts. */
+int vb_spec_sync_inputs(const int32_t *state, int32_t *ids, const uint16_t *verify_hidden,
+                        const uint16_t *prev_h, int32_t verify_len, int32_t hidden,
+                        int32_t *sync_ids, uint16_t *sync_hidden, vb_stream_t stream);
+/* MTP cache length += accepted rows. */
+int vb_spec_advance_mtp(int32_t *state, vb_stream_t stream);
+/* Prompt chunk: ids[i] = prompt[state[0] + i], i < tokens. */
+int vb_spec_prompt_ids(const int32_t *state, const int32_t *prompt, int32_t prompt_len,
+                       int32_t tokens, int32_t *ids, vb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Seeded synthetic data (bench and tests): fills `words` uint32 with a

@@ -55,13 +55,13 @@ def fill_scales(n: int, seed: int, lo=0.002, hi=0.02, bias_mul=-8.0):
     return s, b
 
 
-def expert_arrays(seed: int, hidden=H, inter=I, bits=4, group=64) -> dict:
+def expert_arrays(seed: int, hidden=H, inter=I, bits=4, group=64, bias_mul=-8.0) -> dict:
     """One expert in the oracle's nine-array format (slot axis of length 1)."""
     out = {}
     for j, (name, (o, i)) in enumerate((("gate", (inter, hidden)), ("up", (inter, hidden)),
                                         ("down", (hidden, inter)))):
         w = fill_u32(o * i * bits // 32, _mix_int(seed, 3 * j)).reshape(1, o, i * bits // 32)
-        s, b = fill_scales(o * (i // group), _mix_int(seed, 3 * j + 1))
+        s, b = fill_scales(o * (i // group), _mix_int(seed, 3 * j + 1), bias_mul=bias_mul)
         out[name + "_w"] = w
         out[name + "_s"] = s.reshape(1, o, i // group)
         out[name + "_b"] = b.reshape(1, o, i // group)
@@ -90,24 +90,26 @@ class LazyLayer(dict):
     """Oracle layer dict whose expert pool materialises experts on demand
     (identity slot table over all experts)."""
 
-    def __init__(self, seed: int, layer: int, hidden=H, inter=I, num_experts=E):
+    def __init__(self, seed: int, layer: int, hidden=H, inter=I, num_experts=E, bias_mul=-8.0):
         wr, wsg = dense_layer(seed, layer, hidden, num_experts)
         super().__init__(wr=wr, wsg=wsg, table=np.arange(num_experts, dtype=np.int32),
-                         shared=expert_arrays(expert_seed(seed, layer, SHARED_ID), hidden, inter),
+                         shared=expert_arrays(expert_seed(seed, layer, SHARED_ID), hidden, inter,
+                                              bias_mul=bias_mul),
                          hidden=hidden, inter=inter, group=64, bits=4)
-        self["pool"] = _LazyPool(seed, layer, hidden, inter)
+        self["pool"] = _LazyPool(seed, layer, hidden, inter, bias_mul)
 
 
 class _LazyPool(dict):
-    def __init__(self, seed, layer, hidden, inter):
+    def __init__(self, seed, layer, hidden, inter, bias_mul=-8.0):
         super().__init__()
-        self._args = (seed, layer, hidden, inter)
+        self._args = (seed, layer, hidden, inter, bias_mul)
         self._cache = {}
 
     def _expert(self, e):
         if e not in self._cache:
-            seed, layer, hidden, inter = self._args
-            self._cache[e] = expert_arrays(expert_seed(seed, layer, e), hidden, inter)
+            seed, layer, hidden, inter, bias_mul = self._args
+            self._cache[e] = expert_arrays(expert_seed(seed, layer, e), hidden, inter,
+                                           bias_mul=bias_mul)
         return self._cache[e]
 
     def __getitem__(self, key):

@@ -160,6 +160,33 @@ _SIGNATURES = {
     "vb_dequantize": (_I32, [_P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _P]),
     "vb_gated_delta_step": (_I32, [_P, _P, _P, _P, _I32, _P, _P, _P, _P, _P, _P, _I32, _I32,
                                    _I32, _I32, _I32, _I32, _P]),
+    "vb_gated_delta_step_at": (_I32, [_P, _P, _P, _P, _I32, _P, _P, _I32, _P, _P, _P, _I32,
+                                      _I32, _I32, _I32, _I32, _I32, _P]),
+    "vb_kv_quant_append_at": (_I32, [_P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I32, _P,
+                                     _P, _P, _P, _P]),
+    "vb_kv_decode_attn_at": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32,
+                                    _I32, _P, _I32, _I32, _I32, _I32, _I32, C.c_float, _I32,
+                                    _P, _P, _SZ, _P]),
+    "vb_kv_bf16_attn_at": (_I32, [_P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _I32, _I32,
+                                  _I32, C.c_float, _I32, _P, _P, _SZ, _P]),
+    "vb_qlinear_workspace_size": (_SZ, [_I32, _I32, _I32]),
+    "vb_qlinear": (_I32, [_P, _I32, _I32, _P, _P, _P, _I32, _I32, _I32, _P, C.c_float, _P, _P,
+                          _P, _SZ, _P]),
+    "vb_rms_norm": (_I32, [_P, _P, _P, _I32, _I32, C.c_float, _P, _P, _I32, _P]),
+    "vb_argmax_workspace_size": (_SZ, [_I32]),
+    "vb_argmax": (_I32, [_P, _I32, _I32, _P, _P, _SZ, _P]),
+    "vb_embed_rows": (_I32, [_P, _I32, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P]),
+    "vb_gdn_prepare": (_I32, [_P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I32, _P, _P, _P, _P,
+                              _P, _P, _P, _P, _P, _P, _P]),
+    "vb_gdn_gated_norm": (_I32, [_P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P, C.c_float, _P,
+                                 _P]),
+    "vb_attn_prepare": (_I32, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, C.c_float, _I32,
+                               C.c_float, _P, _I32, _P, _P, _P, _P, _I32, _P, _P]),
+    "vb_attn_gate": (_I32, [_P, _P, _I32, _I32, _I32, _P, _P]),
+    "vb_spec_accept": (_I32, [_P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _I32, _P]),
+    "vb_spec_sync_inputs": (_I32, [_P, _P, _P, _P, _I32, _I32, _P, _P, _P]),
+    "vb_spec_advance_mtp": (_I32, [_P, _P]),
+    "vb_spec_prompt_ids": (_I32, [_P, _P, _I32, _I32, _P, _P]),
     "vb_synth_fill_u32": (_I32, [_P, _I64, C.c_uint64, _P]),
     "vb_synth_fill_pool": (_I32, [C.POINTER(VbQuantPool), _P, _P, _I32, _I32, _I32, _I32,
                                   _I32, C.c_float, C.c_float, C.c_float, _P]),

@@ -31,6 +31,8 @@ SOURCES = [
     "dequant.cu",
     "ep.cu",
     "gdn.cu",
+    "dense.cu",
+    "qwen_next.cu",
 ]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

@@ -165,6 +165,28 @@ __device__ __forceinline__ void dequant4_bf16x2(uint32_t w, uint32_t s2, uint32_
   }
 }
 
+// Rotate 8 consecutive dims (two 4x4 blocks) held by one lane.
+// out[4b+i] = sum_k x[4b+k] * R[b][k][i] (R rounded to bf16), products and
+// sums in float32 in ascending k, then rounded to bf16.
+__device__ __forceinline__ void rotate8(float (&v)[8], const float *__restrict__ blocks,
+                                        int blk0, bool transpose) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const float *R = blocks + (size_t)(blk0 + h) * 16;
+    float x[4] = {v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float acc = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float r = rbf(transpose ? __ldg(R + i * 4 + kk) : __ldg(R + kk * 4 + i));
+        acc = __fadd_rn(acc, __fmul_rn(x[kk], r));
+      }
+      v[4 * h + i] = rbf(acc);
+    }
+  }
+}
+
 // Programmatic dependent launch controls (no-ops without the launch
 // attribute).
 __device__ __forceinline__ void pdl_wait() {

@@ -32,7 +32,9 @@ struct GdnParams {
   float *state_out, *states_out;
   const uint8_t *mask;
   uint16_t *y;
-  int B, T, Hk, Hv, Dv, g_per_key;
+  const int32_t *in_slot;  // nullable: state_in = state_in + *in_slot * slot_stride
+  size_t slot_stride;
+  int B, T, Hk, Hv, Dv, g_per_key, slots;
 };
 
 __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(GdnParams p) {
@@ -66,7 +68,9 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(GdnParams p) {
   const int dv = row0 + r;
   const size_t srow = (((size_t)b * p.Hv + hv) * p.Dv + dv) * GDN_DK + d0;
   float4 st[4];
-  const float4 *sin = reinterpret_cast<const float4 *>(p.state_in + srow);
+  const float *state_in = p.state_in;
+  if (p.in_slot) state_in += (size_t)min(max(*p.in_slot, 0), p.slots - 1) * p.slot_stride;
+  const float4 *sin = reinterpret_cast<const float4 *>(state_in + srow);
 #pragma unroll
   for (int i = 0; i < 4; ++i) st[i] = sin[i];
   __syncthreads();
@@ -114,9 +118,11 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(GdnParams p) {
       for (int i = 0; i < 4; ++i) so[i] = st[i];
     }
   }
-  float4 *sout = reinterpret_cast<float4 *>(p.state_out + srow);
+  if (p.state_out) {
+    float4 *sout = reinterpret_cast<float4 *>(p.state_out + srow);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) sout[i] = st[i];
+    for (int i = 0; i < 4; ++i) sout[i] = st[i];
+  }
 }
 
 }  // namespace vb
@@ -148,6 +154,33 @@ int vb_gated_delta_step(const uint16_t *q, const uint16_t *k, const uint16_t *v,
   p.mask = mask; p.y = y;
   p.B = batch; p.T = tokens; p.Hk = k_heads; p.Hv = v_heads; p.Dv = v_dim;
   p.g_per_key = g_per_key ? 1 : 0;
+  p.in_slot = nullptr; p.slot_stride = 0; p.slots = 1;
+  gdn_step_kernel<<<dim3(v_dim / GDN_ROWS, v_heads, batch), GDN_THREADS, 0, as_stream(stream)>>>(p);
+  return check_launch("gdn_step_kernel");
+}
+
+int vb_gated_delta_step_at(const uint16_t *q, const uint16_t *k, const uint16_t *v,
+                           const float *g, int32_t g_per_key, const float *beta, float *states,
+                           int32_t slots, const int32_t *in_slot, const uint8_t *mask,
+                           uint16_t *y, int32_t batch, int32_t tokens, int32_t k_heads,
+                           int32_t v_heads, int32_t k_dim, int32_t v_dim, vb_stream_t stream) {
+  VB_REQUIRE(batch == 1 && tokens >= 1 && tokens <= GDN_MAX_T && tokens <= slots,
+             "vb_gated_delta_step_at: batch=%d (1 only) tokens=%d slots=%d", batch, tokens, slots);
+  VB_REQUIRE(k_dim == GDN_DK, "vb_gated_delta_step_at: key dim %d (128 only)", k_dim);
+  VB_REQUIRE(v_dim >= GDN_ROWS && v_dim % GDN_ROWS == 0, "vb_gated_delta_step_at: value dim %d",
+             v_dim);
+  VB_REQUIRE(k_heads >= 1 && v_heads >= k_heads && v_heads % k_heads == 0,
+             "vb_gated_delta_step_at: heads k=%d v=%d", k_heads, v_heads);
+  VB_REQUIRE(q && k && v && g && beta && states && in_slot && y,
+             "vb_gated_delta_step_at: null tensor");
+  VB_REQUIRE(((uintptr_t)states % 16) == 0, "vb_gated_delta_step_at: states 16-byte aligned");
+  GdnParams p;
+  p.q = q; p.k = k; p.v = v; p.g = g; p.beta = beta;
+  p.state_in = states; p.state_out = nullptr; p.states_out = states;
+  p.mask = mask; p.y = y;
+  p.B = batch; p.T = tokens; p.Hk = k_heads; p.Hv = v_heads; p.Dv = v_dim;
+  p.g_per_key = g_per_key ? 1 : 0;
+  p.in_slot = in_slot; p.slot_stride = (size_t)batch * v_heads * v_dim * GDN_DK; p.slots = slots;
   gdn_step_kernel<<<dim3(v_dim / GDN_ROWS, v_heads, batch), GDN_THREADS, 0, as_stream(stream)>>>(p);
   return check_launch("gdn_step_kernel");
 }

@@ -26,6 +26,7 @@ struct AttnParams {
   const uint32_t *kc, *vc;
   const uint16_t *ks, *kb, *vs, *vb;
   const float *rv;
+  const int32_t *pos_dev;  // nullable: S = *pos_dev + L read on the device
   int B, Hq, Hkv, L, S, cap, rep, QR, causal, nsplit, kps;
   float scale;
   float *opart, *mpart, *lpart;
@@ -179,14 +180,16 @@ __device__ __forceinline__ void a1_fetch(const uint8_t *kbase, const uint8_t *vb
   }
 }
 
+template <bool DEV_POS>
 __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int S_ = DEV_POS ? min(max(*p.pos_dev, 0) + p.L, p.cap) : p.S;
   const int bh = blockIdx.x, split = blockIdx.y;
   const int b = bh / p.Hkv, hkv = bh % p.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, c = lane & 3;
   const int k_begin = split * p.kps;
-  const int k_end = min(p.S, k_begin + p.kps);
+  const int k_end = min(S_, k_begin + p.kps);
   uint8_t *wsm = smem_raw + warp * A1_WARP_SMEM;
   uint16_t *Vt = reinterpret_cast<uint16_t *>(wsm);
   uint8_t *raw0 = wsm + A1_VBYTES;
@@ -245,7 +248,7 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int row = 2 * c + h;
-    klim[h] = row >= p.QR ? -1 : (p.causal ? p.S - p.L + row % p.L : INT_MAX);
+    klim[h] = row >= p.QR ? -1 : (p.causal ? S_ - p.L + row % p.L : INT_MAX);
   }
 
   const size_t head_row0 = (size_t)bh * p.cap;
@@ -258,12 +261,12 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
   const uint8_t *sb1 = reinterpret_cast<const uint8_t *>(((lane >> 4) ? sc_t[3] : sc_t[2]) + head_row0 * 4);
   int it = 0;
   int t_cur = warp;
-  if (t_cur < n_tiles) a1_fetch(kbase, vbase, sb0, sb1, p.S, k_begin + 16 * t_cur, raw0, lane);
+  if (t_cur < n_tiles) a1_fetch(kbase, vbase, sb0, sb1, S_, k_begin + 16 * t_cur, raw0, lane);
   cp_async_commit();
   for (; t_cur < n_tiles; t_cur += A1_WARPS, ++it) {
     const int t_next = t_cur + A1_WARPS;
     if (t_next < n_tiles)
-      a1_fetch(kbase, vbase, sb0, sb1, p.S, k_begin + 16 * t_next,
+      a1_fetch(kbase, vbase, sb0, sb1, S_, k_begin + 16 * t_next,
                raw0 + ((it + 1) & 1) * A1_RAW, lane);
     cp_async_commit();
     cp_async_wait<1>();
@@ -516,14 +519,16 @@ __device__ __forceinline__ void a4_fetch(const uint8_t *kbase, const uint8_t *vb
   }
 }
 
+template <bool DEV_POS>
 __global__ void __launch_bounds__(A4_WARPS * 32, 3) kv_attn4_kernel(AttnParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int S_ = DEV_POS ? min(max(*p.pos_dev, 0) + p.L, p.cap) : p.S;
   const int bh = blockIdx.x, split = blockIdx.y;
   const int b = bh / p.Hkv, hkv = bh % p.Hkv;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, c = lane & 3;
   const int k_begin = split * p.kps;
-  const int k_end = min(p.S, k_begin + p.kps);
+  const int k_end = min(S_, k_begin + p.kps);
   uint8_t *raw0 = smem_raw;
   uint16_t *tiles = reinterpret_cast<uint16_t *>(smem_raw + A4_NRAW * A4_RAW);  // [2][K, V][16][PITCH]
 
@@ -584,17 +589,17 @@ __global__ void __launch_bounds__(A4_WARPS * 32, 3) kv_attn4_kernel(AttnParams p
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int row = row0 + h;
-    klim[h] = row >= p.QR ? -1 : (p.causal ? p.S - p.L + row % p.L : INT_MAX);
+    klim[h] = row >= p.QR ? -1 : (p.causal ? S_ - p.L + row % p.L : INT_MAX);
   }
 #pragma unroll 1
   for (int t = 0; t < A4_NRAW - 1; ++t) {
-    if (t < n_tiles) a4_fetch(kbase, vbase, scb, p.S, k_begin + 16 * t, raw0 + t * A4_RAW, tid);
+    if (t < n_tiles) a4_fetch(kbase, vbase, scb, S_, k_begin + 16 * t, raw0 + t * A4_RAW, tid);
     cp_async_commit();
   }
 #pragma unroll 1
   for (int t = 0; t < n_tiles; ++t) {
     const int tn = t + A4_NRAW - 1;
-    if (tn < n_tiles) a4_fetch(kbase, vbase, scb, p.S, k_begin + 16 * tn, raw0 + (tn % A4_NRAW) * A4_RAW, tid);
+    if (tn < n_tiles) a4_fetch(kbase, vbase, scb, S_, k_begin + 16 * tn, raw0 + (tn % A4_NRAW) * A4_RAW, tid);
     cp_async_commit();
     cp_async_wait<A4_NRAW - 1>();
     __syncthreads();  // tile t staged by every thread
@@ -771,6 +776,141 @@ __global__ void __launch_bounds__(A4_WARPS * 32, 3) kv_attn4_kernel(AttnParams p
   }
 }
 
+// ----------------------------------------------------------------------------
+// Plain bf16 cache (the MTP layer's mlx-lm KVCache, attended with
+// mx.fast.scaled_dot_product_attention): q * scale, scores, softmax and P V in
+// float32, one rounding of the output (in the combine). CUDA-core split-K
+// kernel: a CTA walks its key range in 32-key chunks staged in shared memory;
+// thread t scores key t % 32 against rows t / 32 + 8 i (conflict-free with
+// the 258-element K pitch) and accumulates 4 output dims of 8 rows. The
+// partials use the quantized kernels' layout, so the same combine merges them.
+// ----------------------------------------------------------------------------
+constexpr int B16_KP = 258;  // bf16 per staged K row
+constexpr int B16_SMEM = 32 * 256 * 4 + 32 * B16_KP * 2 + 32 * 256 * 2 + 32 * 33 * 4 + 3 * 32 * 4;
+
+template <bool DEV_POS>
+__global__ void __launch_bounds__(256) kv_bf16_attn_kernel(AttnParams p) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int S_ = DEV_POS ? min(max(*p.pos_dev, 0) + p.L, p.cap) : p.S;
+  float *qs = reinterpret_cast<float *>(smem_raw);                    // [32][256]
+  uint16_t *ks = reinterpret_cast<uint16_t *>(qs + 32 * 256);         // [32][B16_KP]
+  uint16_t *vs = ks + 32 * B16_KP;                                    // [32][256]
+  float *sc = reinterpret_cast<float *>(vs + 32 * 256);               // [32][33]
+  float *m_s = sc + 32 * 33, *l_s = m_s + 32, *f_s = l_s + 32;
+  const int bh = blockIdx.x, split = blockIdx.y;
+  const int b = bh / p.Hkv, hkv = bh % p.Hkv;
+  const int tid = threadIdx.x;
+  const int k_begin = split * p.kps;
+  const int k_end = min(S_, k_begin + p.kps);
+  const uint16_t *kc = reinterpret_cast<const uint16_t *>(p.kc) + (size_t)bh * p.cap * 256;
+  const uint16_t *vc = reinterpret_cast<const uint16_t *>(p.vc) + (size_t)bh * p.cap * 256;
+  for (int i = tid; i < 32 * 256; i += 256) {
+    const int r = i >> 8, d = i & 255;
+    float v = 0.f;
+    if (r < p.QR) {
+      const int hq = hkv * p.rep + r / p.L, l = r % p.L;
+      v = bf2f(p.q[(((size_t)b * p.Hq + hq) * p.L + l) * 256 + d]) * p.scale;
+    }
+    qs[i] = v;
+  }
+  if (tid < 32) { m_s[tid] = -INFINITY; l_s[tid] = 0.f; }
+  const int dq = (tid & 63) * 4, r0 = (tid >> 6) * 8;  // output dims, rows
+  float O[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) O[i][0] = O[i][1] = O[i][2] = O[i][3] = 0.f;
+  for (int key0 = k_begin; key0 < k_end; key0 += 32) {
+    const int nk = min(32, k_end - key0);
+    __syncthreads();
+    for (int i = tid; i < 32 * 128; i += 256) {  // 2 bf16 per step
+      const int kk = i >> 7, d2 = (i & 127) * 2;
+      uint32_t kw = 0, vw = 0;
+      if (kk < nk) {
+        kw = *reinterpret_cast<const uint32_t *>(kc + (size_t)(key0 + kk) * 256 + d2);
+        vw = *reinterpret_cast<const uint32_t *>(vc + (size_t)(key0 + kk) * 256 + d2);
+      }
+      *reinterpret_cast<uint32_t *>(ks + kk * B16_KP + d2) = kw;
+      *reinterpret_cast<uint32_t *>(vs + kk * 256 + d2) = vw;
+    }
+    __syncthreads();
+    {  // scores
+      const int kk = tid & 31, rb = tid >> 5;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint16_t *kr = ks + kk * B16_KP;
+      for (int d = 0; d < 256; d += 2) {
+        const uint32_t kw = *reinterpret_cast<const uint32_t *>(kr + d);
+        const float k0 = __uint_as_float(kw << 16), k1 = __uint_as_float(kw & 0xFFFF0000u);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float2 qv = *reinterpret_cast<const float2 *>(qs + (rb + 8 * i) * 256 + d);
+          acc[i] = fmaf(qv.x, k0, acc[i]);
+          acc[i] = fmaf(qv.y, k1, acc[i]);
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = rb + 8 * i;
+        const int key = key0 + kk;
+        bool ok = kk < nk && r < p.QR;
+        if (ok && p.causal) ok = key <= S_ - p.L + r % p.L;
+        sc[r * 33 + kk] = ok ? acc[i] : -INFINITY;
+      }
+    }
+    __syncthreads();
+    if (tid < 32) {  // online softmax state of row tid
+      const int r = tid;
+      float mx = m_s[r];
+      for (int kk = 0; kk < 32; ++kk) mx = fmaxf(mx, sc[r * 33 + kk]);
+      const float mo = m_s[r];
+      const float f = (mx == -INFINITY) ? 1.f : expf(mo - mx);
+      float lsum = l_s[r] * (mo == -INFINITY ? 0.f : f);
+      for (int kk = 0; kk < 32; ++kk) {
+        const float sv = sc[r * 33 + kk];
+        const float e = sv == -INFINITY ? 0.f : expf(sv - mx);
+        sc[r * 33 + kk] = e;
+        lsum += e;
+      }
+      m_s[r] = mx;
+      l_s[r] = lsum;
+      f_s[r] = (mo == -INFINITY) ? 0.f : f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float f = f_s[r0 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) O[i][j] *= f;
+    }
+    for (int kk = 0; kk < 32; ++kk) {
+      const uint2 vw = *reinterpret_cast<const uint2 *>(vs + kk * 256 + dq);
+      const float v0 = __uint_as_float(vw.x << 16), v1 = __uint_as_float(vw.x & 0xFFFF0000u);
+      const float v2 = __uint_as_float(vw.y << 16), v3 = __uint_as_float(vw.y & 0xFFFF0000u);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float pv = sc[(r0 + i) * 33 + kk];
+        O[i][0] = fmaf(pv, v0, O[i][0]);
+        O[i][1] = fmaf(pv, v1, O[i][1]);
+        O[i][2] = fmaf(pv, v2, O[i][2]);
+        O[i][3] = fmaf(pv, v3, O[i][3]);
+      }
+    }
+  }
+  __syncthreads();
+  const size_t cta = (size_t)bh * p.nsplit + split;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = r0 + i;
+    if (r >= p.QR) continue;
+    *reinterpret_cast<float4 *>(p.opart + (cta * 32 + r) * 256 + dq) =
+        make_float4(O[i][0], O[i][1], O[i][2], O[i][3]);
+  }
+  if (tid < p.QR) {
+    p.mpart[cta * 32 + tid] = m_s[tid];
+    p.lpart[cta * 32 + tid] = l_s[tid];
+  }
+}
+
+__global__ void add_i32_kernel(const int32_t *a, int32_t add, int32_t *out) { *out = *a + add; }
+
 // Keys per split: about three CTAs per SM over all (batch, kv head) pairs,
 // in multiples of 64 keys.
 static void attn_split(int bhk, int S, int &nsplit, int &kps) {
@@ -797,16 +937,16 @@ size_t vb_kv_attn_workspace_size(int32_t batch, int32_t q_heads, int32_t L,
   return align_up(ctas * 32 * 256 * sizeof(float), 256) + 2 * align_up(ctas * 32 * sizeof(float), 256);
 }
 
-int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
-                      const uint16_t *k_scales, const uint16_t *k_biases,
-                      const uint32_t *v_codes, const uint16_t *v_scales,
-                      const uint16_t *v_biases, const float *rv_blocks,
-                      int32_t batch, int32_t q_heads, int32_t kv_heads,
-                      int32_t L, int32_t dim, int32_t keys, int32_t cap,
-                      int32_t group, int32_t k_bits, int32_t v_bits,
-                      float scale, int32_t causal, uint16_t *out,
-                      void *workspace, size_t workspace_bytes,
-                      vb_stream_t stream) {
+static int kv_decode_attn_impl(const uint16_t *q, const uint32_t *k_codes,
+                               const uint16_t *k_scales, const uint16_t *k_biases,
+                               const uint32_t *v_codes, const uint16_t *v_scales,
+                               const uint16_t *v_biases, const float *rv_blocks,
+                               int32_t batch, int32_t q_heads, int32_t kv_heads,
+                               int32_t L, int32_t dim, int32_t keys, int32_t cap,
+                               int32_t group, int32_t k_bits, int32_t v_bits,
+                               float scale, int32_t causal, const int32_t *pos_dev,
+                               uint16_t *out, void *workspace, size_t workspace_bytes,
+                               vb_stream_t stream) {
   VB_REQUIRE(dim == 256 && group == 64 && k_bits == 4 && v_bits == 3,
              "vb_kv_decode_attn: supports D=256, group 64, K4/V3 (got D=%d g=%d k%d v%d)",
              dim, group, k_bits, v_bits);
@@ -819,7 +959,7 @@ int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
              "vb_kv_decode_attn: null pointer");
   AttnParams p;
   p.q = q; p.kc = k_codes; p.vc = v_codes; p.ks = k_scales; p.kb = k_biases;
-  p.vs = v_scales; p.vb = v_biases; p.rv = rv_blocks;
+  p.vs = v_scales; p.vb = v_biases; p.rv = rv_blocks; p.pos_dev = pos_dev;
   p.B = batch; p.Hq = q_heads; p.Hkv = kv_heads; p.L = L; p.S = keys; p.cap = cap;
   p.rep = rep; p.QR = rep * L; p.causal = causal; p.scale = scale;
   attn_split(batch * kv_heads, keys, p.nsplit, p.kps);
@@ -836,25 +976,121 @@ int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
   p.out = out;
   cudaStream_t s = as_stream(stream);
   const dim3 grid(batch * kv_heads, p.nsplit);
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaFuncSetAttribute(kv_attn1_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         A1_SMEM);
+    cudaFuncSetAttribute(kv_attn1_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         A1_SMEM);
+    cudaFuncSetAttribute(kv_attn4_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         A4_SMEM);
+    cudaFuncSetAttribute(kv_attn4_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         A4_SMEM);
+    attr_done = true;
+  }
   if (p.QR <= 8) {
-    static bool attr1_done = false;
-    if (!attr1_done) {
-      cudaFuncSetAttribute(kv_attn1_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, A1_SMEM);
-      attr1_done = true;
-    }
-    kv_attn1_kernel<<<grid, A1_WARPS * 32, A1_SMEM, s>>>(p);
+    if (pos_dev)
+      kv_attn1_kernel<true><<<grid, A1_WARPS * 32, A1_SMEM, s>>>(p);
+    else
+      kv_attn1_kernel<false><<<grid, A1_WARPS * 32, A1_SMEM, s>>>(p);
   } else {
-    static bool attr4_done = false;
-    if (!attr4_done) {
-      cudaFuncSetAttribute(kv_attn4_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, A4_SMEM);
-      attr4_done = true;
-    }
-    kv_attn4_kernel<<<grid, A4_WARPS * 32, A4_SMEM, s>>>(p);
+    if (pos_dev)
+      kv_attn4_kernel<true><<<grid, A4_WARPS * 32, A4_SMEM, s>>>(p);
+    else
+      kv_attn4_kernel<false><<<grid, A4_WARPS * 32, A4_SMEM, s>>>(p);
   }
   const int rc = check_launch(p.QR <= 8 ? "kv_attn1_kernel" : "kv_attn4_kernel");
   if (rc) return rc;
   kv_attn_combine_kernel<<<dim3(batch * q_heads * L, 8), 256, 0, s>>>(p);
   return check_launch("kv_attn_combine_kernel");
+}
+
+int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
+                      const uint16_t *k_scales, const uint16_t *k_biases,
+                      const uint32_t *v_codes, const uint16_t *v_scales,
+                      const uint16_t *v_biases, const float *rv_blocks,
+                      int32_t batch, int32_t q_heads, int32_t kv_heads,
+                      int32_t L, int32_t dim, int32_t keys, int32_t cap,
+                      int32_t group, int32_t k_bits, int32_t v_bits,
+                      float scale, int32_t causal, uint16_t *out,
+                      void *workspace, size_t workspace_bytes,
+                      vb_stream_t stream) {
+  return kv_decode_attn_impl(q, k_codes, k_scales, k_biases, v_codes, v_scales, v_biases,
+                             rv_blocks, batch, q_heads, kv_heads, L, dim, keys, cap, group,
+                             k_bits, v_bits, scale, causal, nullptr, out, workspace,
+                             workspace_bytes, stream);
+}
+
+int vb_kv_bf16_attn_at(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                       int32_t batch, int32_t q_heads, int32_t kv_heads, int32_t L,
+                       int32_t dim, const int32_t *pos, int32_t pos_add, int32_t keys_max,
+                       int32_t cap, float scale, int32_t causal, uint16_t *out,
+                       void *workspace, size_t workspace_bytes, vb_stream_t stream) {
+  VB_REQUIRE(dim == 256, "vb_kv_bf16_attn_at: D=%d (256 only)", dim);
+  VB_REQUIRE(batch > 0 && kv_heads > 0 && q_heads % kv_heads == 0,
+             "vb_kv_bf16_attn_at: heads %d/%d", q_heads, kv_heads);
+  const int rep = q_heads / kv_heads;
+  VB_REQUIRE(L >= 1 && rep * L <= 32, "vb_kv_bf16_attn_at: L=%d rep=%d", L, rep);
+  VB_REQUIRE(keys_max >= L && keys_max <= cap, "vb_kv_bf16_attn_at: keys_max=%d cap=%d",
+             keys_max, cap);
+  VB_REQUIRE(q && k_cache && v_cache && out && pos, "vb_kv_bf16_attn_at: null pointer");
+  AttnParams p;
+  p.q = q; p.kc = reinterpret_cast<const uint32_t *>(k_cache);
+  p.vc = reinterpret_cast<const uint32_t *>(v_cache);
+  p.ks = p.kb = p.vs = p.vb = nullptr; p.rv = nullptr; p.pos_dev = nullptr;
+  p.B = batch; p.Hq = q_heads; p.Hkv = kv_heads; p.L = L; p.S = keys_max; p.cap = cap;
+  p.rep = rep; p.QR = rep * L; p.causal = causal; p.scale = scale;
+  attn_split(batch * kv_heads, keys_max, p.nsplit, p.kps);
+  VB_REQUIRE(p.nsplit <= ATT_MAX_SPLITS, "vb_kv_bf16_attn_at: %d splits", p.nsplit);
+  const size_t ctas = (size_t)batch * kv_heads * p.nsplit;
+  const size_t obytes = align_up(ctas * 32 * 256 * sizeof(float), 256);
+  const size_t mbytes = align_up(ctas * 32 * sizeof(float), 256);
+  VB_REQUIRE(workspace && workspace_bytes >= obytes + 2 * mbytes + 256,
+             "vb_kv_bf16_attn_at: workspace %zu < %zu", workspace_bytes,
+             obytes + 2 * mbytes + 256);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  p.opart = reinterpret_cast<float *>(ws);
+  p.mpart = reinterpret_cast<float *>(ws + obytes);
+  p.lpart = reinterpret_cast<float *>(ws + obytes + mbytes);
+  p.out = out;
+  cudaStream_t s = as_stream(stream);
+  // the key count pos + pos_add + L is read on the device: a one-int scratch
+  int32_t *pos_eff = reinterpret_cast<int32_t *>(ws + obytes + 2 * mbytes);
+  if (pos_add != 0) {
+    add_i32_kernel<<<1, 1, 0, s>>>(pos, pos_add, pos_eff);
+    const int rc0 = check_launch("add_i32_kernel");
+    if (rc0) return rc0;
+    p.pos_dev = pos_eff;
+  } else {
+    p.pos_dev = pos;
+  }
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaFuncSetAttribute(kv_bf16_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         B16_SMEM);
+    attr_done = true;
+  }
+  kv_bf16_attn_kernel<true><<<dim3(batch * kv_heads, p.nsplit), 256, B16_SMEM, s>>>(p);
+  const int rc = check_launch("kv_bf16_attn_kernel");
+  if (rc) return rc;
+  kv_attn_combine_kernel<<<dim3(batch * q_heads * L, 8), 256, 0, s>>>(p);
+  return check_launch("kv_attn_combine_kernel");
+}
+
+int vb_kv_decode_attn_at(const uint16_t *q, const uint32_t *k_codes,
+                         const uint16_t *k_scales, const uint16_t *k_biases,
+                         const uint32_t *v_codes, const uint16_t *v_scales,
+                         const uint16_t *v_biases, const float *rv_blocks,
+                         int32_t batch, int32_t q_heads, int32_t kv_heads,
+                         int32_t L, int32_t dim, const int32_t *pos, int32_t keys_max,
+                         int32_t cap, int32_t group, int32_t k_bits, int32_t v_bits,
+                         float scale, int32_t causal, uint16_t *out, void *workspace,
+                         size_t workspace_bytes, vb_stream_t stream) {
+  VB_REQUIRE(pos != nullptr, "vb_kv_decode_attn_at: null position");
+  return kv_decode_attn_impl(q, k_codes, k_scales, k_biases, v_codes, v_scales, v_biases,
+                             rv_blocks, batch, q_heads, kv_heads, L, dim, keys_max, cap, group,
+                             k_bits, v_bits, scale, causal, pos, out, workspace,
+                             workspace_bytes, stream);
 }
 
 }  // extern "C"

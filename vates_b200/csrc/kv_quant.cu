@@ -15,35 +15,21 @@
 
 namespace vb {
 
-// Rotate 8 consecutive dims (two 4x4 blocks) held by one lane.
-// out[4b+i] = sum_k x[4b+k] * R[b][k][i] (R rounded to bf16), products and
-// sums in float32 in ascending k, then rounded to bf16.
-__device__ __forceinline__ void rotate8(float (&v)[8], const float *__restrict__ blocks,
-                                        int blk0, bool transpose) {
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const float *R = blocks + (size_t)(blk0 + h) * 16;
-    float x[4] = {v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float acc = 0.f;
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const float r = rbf(transpose ? __ldg(R + i * 4 + kk) : __ldg(R + kk * 4 + i));
-        acc = __fadd_rn(acc, __fmul_rn(x[kk], r));
-      }
-      v[4 * h + i] = rbf(acc);
-    }
-  }
-}
-
 template <int LPR>  // lanes per row = D/8
 __global__ void __launch_bounds__(256) kv_quant_kernel(
     const uint16_t *__restrict__ src, const float *__restrict__ blocks,
     int64_t rows, int n, int heads_total, int bits, int offset, int cap,
     uint32_t *__restrict__ codes, uint16_t *__restrict__ scales,
-    uint16_t *__restrict__ biases) {
+    uint16_t *__restrict__ biases, const int32_t *__restrict__ offset_dev,
+    int32_t *status) {
   constexpr int D = LPR * 8;
+  if (offset_dev) {  // position read on the device (the same for every thread)
+    offset = *offset_dev;
+    if (offset < 0 || offset + n > cap) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) flag_status(status, VB_STATUS_BOUNDS);
+      return;
+    }
+  }
   const int lane = threadIdx.x & 31;
   const int sub = lane % LPR;           // lane within the row
   const int rsub = lane / LPR;          // row within the warp
@@ -151,16 +137,18 @@ using namespace vb;
 
 extern "C" {
 
-int vb_kv_quant_append(const uint16_t *src, const float *so4_blocks,
-                       int32_t batch, int32_t heads, int32_t n, int32_t dim,
-                       int32_t group, int32_t bits, int32_t offset,
-                       int32_t cap, uint32_t *codes, uint16_t *scales,
-                       uint16_t *biases, vb_stream_t stream) {
+static int kv_quant_append_impl(const uint16_t *src, const float *so4_blocks,
+                                int32_t batch, int32_t heads, int32_t n, int32_t dim,
+                                int32_t group, int32_t bits, int32_t offset,
+                                const int32_t *offset_dev, int32_t cap, uint32_t *codes,
+                                uint16_t *scales, uint16_t *biases, int32_t *status,
+                                vb_stream_t stream) {
   VB_REQUIRE(dim == 64 || dim == 128 || dim == 256, "vb_kv_quant_append: dim=%d", dim);
   VB_REQUIRE(group == 64, "vb_kv_quant_append: group=%d (64 only)", group);
   VB_REQUIRE(bits == 2 || bits == 3 || bits == 4 || bits == 5 || bits == 6 || bits == 8,
              "vb_kv_quant_append: bits=%d", bits);
-  VB_REQUIRE(batch > 0 && heads > 0 && n >= 0 && offset >= 0 && offset + n <= cap,
+  VB_REQUIRE(batch > 0 && heads > 0 && n >= 0 && n <= cap &&
+                 (offset_dev || (offset >= 0 && offset + n <= cap)),
              "vb_kv_quant_append: batch=%d heads=%d n=%d offset=%d cap=%d", batch,
              heads, n, offset, cap);
   if (n == 0) return VB_OK;
@@ -172,14 +160,36 @@ int vb_kv_quant_append(const uint16_t *src, const float *so4_blocks,
   cudaStream_t s = as_stream(stream);
   if (lpr == 32)
     kv_quant_kernel<32><<<blocks, 256, 0, s>>>(src, so4_blocks, rows, n, batch * heads,
-                                               bits, offset, cap, codes, scales, biases);
+                                               bits, offset, cap, codes, scales, biases,
+                                               offset_dev, status);
   else if (lpr == 16)
     kv_quant_kernel<16><<<blocks, 256, 0, s>>>(src, so4_blocks, rows, n, batch * heads,
-                                               bits, offset, cap, codes, scales, biases);
+                                               bits, offset, cap, codes, scales, biases,
+                                               offset_dev, status);
   else
     kv_quant_kernel<8><<<blocks, 256, 0, s>>>(src, so4_blocks, rows, n, batch * heads,
-                                              bits, offset, cap, codes, scales, biases);
+                                              bits, offset, cap, codes, scales, biases,
+                                               offset_dev, status);
   return check_launch("kv_quant_kernel");
+}
+
+int vb_kv_quant_append(const uint16_t *src, const float *so4_blocks,
+                       int32_t batch, int32_t heads, int32_t n, int32_t dim,
+                       int32_t group, int32_t bits, int32_t offset,
+                       int32_t cap, uint32_t *codes, uint16_t *scales,
+                       uint16_t *biases, vb_stream_t stream) {
+  return kv_quant_append_impl(src, so4_blocks, batch, heads, n, dim, group, bits, offset,
+                              nullptr, cap, codes, scales, biases, nullptr, stream);
+}
+
+int vb_kv_quant_append_at(const uint16_t *src, const float *so4_blocks,
+                          int32_t batch, int32_t heads, int32_t n, int32_t dim,
+                          int32_t group, int32_t bits, const int32_t *offset,
+                          int32_t cap, uint32_t *codes, uint16_t *scales,
+                          uint16_t *biases, int32_t *status, vb_stream_t stream) {
+  VB_REQUIRE(offset != nullptr, "vb_kv_quant_append_at: null position");
+  return kv_quant_append_impl(src, so4_blocks, batch, heads, n, dim, group, bits, 0, offset,
+                              cap, codes, scales, biases, status, stream);
 }
 
 int vb_so4_rotate(const uint16_t *src, const float *so4_blocks, int64_t rows,

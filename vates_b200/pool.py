@@ -130,7 +130,7 @@ class QuantPool:
                                            -8.0, st), "vb_synth_fill_scales")
 
     def fill_synthetic_many(self, slots, seeds, scale_lo=0.002, scale_hi=0.02,
-                            stream=None) -> None:
+                            stream=None, bias_mul: float = -8.0) -> None:
         """:meth:`fill_synthetic` of every ``(slot, seed)`` pair in one launch."""
         import ctypes as C
         n = len(slots)
@@ -141,7 +141,7 @@ class QuantPool:
         sd = (C.c_uint64 * n)(*[int(s) for s in seeds])
         check(lib.vb_synth_fill_pool(C.byref(self.c_struct()), sl, sd, n, self.hidden,
                                      self.inter, self.bits, self.group, scale_lo, scale_hi,
-                                     -8.0, stream_handle(stream)), "vb_synth_fill_pool")
+                                     bias_mul, stream_handle(stream)), "vb_synth_fill_pool")
 
     def to_numpy_slot(self, slot: int) -> dict:
         """Copy one slot back to host numpy arrays (uint32 words, uint16 bf16

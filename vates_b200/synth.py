@@ -28,16 +28,17 @@ def normal_bf16(rng: np.random.Generator, shape, std: float, device) -> torch.Te
 
 def make_layer(seed: int, layer: int, pool: QuantPool, experts_in_slots, device="cuda",
                hidden=H, inter=I, num_experts=E, top_k=K, router_bias=None,
-               workspace: Workspace | None = None) -> MoeBlock:
+               workspace: Workspace | None = None, bias_mul: float = -8.0) -> MoeBlock:
     """One synthetic MoE layer whose ``pool`` slot ``s`` holds expert
     ``experts_in_slots[s]`` (filled here)."""
     rng = np.random.Generator(np.random.PCG64([seed, layer]))
     wr = normal_bf16(rng, (num_experts, hidden), 0.02, device)
     wsg = normal_bf16(rng, (hidden,), 0.02, device)
     experts = [int(e) for e in experts_in_slots]
-    pool.fill_synthetic_many(range(len(experts)), [expert_seed(seed, layer, e) for e in experts])
+    pool.fill_synthetic_many(range(len(experts)), [expert_seed(seed, layer, e) for e in experts],
+                             bias_mul=bias_mul)
     shared = QuantPool.empty_blob(1, hidden, inter, pool.bits, pool.group, device)
-    shared.fill_synthetic_many([0], [expert_seed(seed, layer, SHARED_ID)])
+    shared.fill_synthetic_many([0], [expert_seed(seed, layer, SHARED_ID)], bias_mul=bias_mul)
     table = make_table(num_experts, {int(e): s for s, e in enumerate(experts_in_slots)}, device)
     return MoeBlock(wr, table, pool, shared, wsg, top_k=top_k, router_bias=router_bias,
                     workspace=workspace)
