@@ -485,6 +485,111 @@ def run_decode_t1_leg(st, stream, steps: int = 20, warmup: int = 3):
             "bytes_per_step": step_bytes, "steps": steps, "warmup": max(warmup, 3)}
 
 
+def _qlin_bytes(out_f: int, in_f: int) -> int:
+    return out_f * in_f // 2 + out_f * (in_f // 64) * 4
+
+
+def full_stack_iteration_bytes(cfg, V: int, K: int, pos: int, accepted: float) -> float:
+    """Algorithmic HBM bytes of one speculative iteration of the config-4
+    stack: every weight read once per pass (K drafts, the verify pass over V
+    rows, the MTP sync), expected distinct experts E[U] = E (1 - (1 - k/E)^n)
+    of n independent tokens (the verify's V rows; one row for a draft; the
+    accepted rows for the sync), GDN states read once and written per row,
+    caches read up to the current position."""
+    E, k, H = cfg.experts, cfg.top_k, cfg.hidden
+    expert = EXPERT_BYTES
+    moe = lambda n: (E * (1 - (1 - k / E) ** n) + 1) * expert + E * H * 2 + H * 2
+    gdn = _qlin_bytes(cfg.gdn_proj, H) + _qlin_bytes(H, cfg.value_dim)
+    att = _qlin_bytes(cfg.attn_proj, H) + _qlin_bytes(H, cfg.attn_out)
+    state = cfg.v_heads * cfg.head_v * cfg.head_k * 4
+    n_gdn = sum(1 for l in range(cfg.layers) if cfg.is_linear(l))
+    n_att = cfg.layers - n_gdn
+    head = _qlin_bytes(cfg.vocab, H)
+    verify = (n_gdn * (gdn + state * (1 + V)) + n_att * (att + cfg.kv_heads * (pos + V) * 256)
+              + cfg.layers * moe(V) + head)
+    mtp_layer = _qlin_bytes(H, 2 * H) + att
+    mtp_cache = cfg.kv_heads * (pos + V) * 512 * 2
+    draft = mtp_layer + moe(1) + head + mtp_cache
+    sync = mtp_layer + moe(accepted) + mtp_cache
+    return K * draft + verify + sync
+
+
+def run_full_stack_leg(new_tokens: int = 128, prompt_len: int = 4096, seed: int = 4,
+                       V: int = 4, K: int = 3, replays: int = 20):
+    """Config 4: random-init Qwen3-Next-80B-A3B-shaped stack (48 layers: 36
+    Gated-DeltaNet + 12 IsoQuant full attention, 512-expert 4-bit MoE blocks,
+    vocab 151,936, MTP head), all weights resident, batch 1. A seeded
+    4096-token random prompt is prefilled (chunks of V rows through the
+    verify graph), then greedy MTP self-speculative decoding with K = 3
+    drafts and verify at T = 4 runs for ``new_tokens`` tokens. decode_tok_s
+    = generated tokens / wall time of the decode loop (host clock, one
+    emitted-token counter read per iteration, as the reference's
+    mtp_generate wall). Device time per iteration from CUDA events over
+    back-to-back graph replays."""
+    import numpy as np
+    import torch
+    from vates_b200.qwen_next import QwenNextConfig, QwenNextModel, SP_HIST, SP_NOUT
+    hbm_peak, _, peak_kind = peaks()
+    cfg = QwenNextConfig()
+    cache = (prompt_len + new_tokens + 4 * replays + 256 + 255) // 256 * 256
+    t0 = time.perf_counter()
+    model = QwenNextModel(cfg, seed=seed, cache_len=cache, verify_len=V, drafts=K)
+    torch.cuda.synchronize()
+    build_s = time.perf_counter() - t0
+    rng = np.random.Generator(np.random.PCG64([seed, 4096]))
+    prompt = rng.integers(0, cfg.vocab, prompt_len).astype(np.int32)
+    # warm-up (captures the prefill and iteration graphs), then the measured run
+    model.generate(prompt[:64], 8)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    model.prefill(prompt)
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    st0 = model.buf["state"].cpu().numpy().copy()
+    t0 = time.perf_counter()
+    n_out = 1
+    iters = 0
+    g = model._graph(("iter",), lambda s: model.spec_iteration(s))
+    while n_out < new_tokens:
+        g.replay()
+        iters += 1
+        n_out = int(model.buf["state"][SP_NOUT].item())
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    st = model.buf["state"].cpu().numpy()
+    toks = model.buf["out"][:new_tokens].cpu().numpy()
+    hist = [int(v) for v in (st[SP_HIST:SP_HIST + V + 1] - st0[SP_HIST:SP_HIST + V + 1])]
+    steps = max(sum(hist), 1)
+    accepted = sum((min(m + 1, V)) * c for m, c in enumerate(hist)) / steps
+    # device time: back-to-back replays without host reads
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(replays):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    dev_ms = e0.elapsed_time(e1) / replays
+    pos = int(st[0])
+    it_bytes = full_stack_iteration_bytes(cfg, V, K, pos, accepted)
+    gbs = it_bytes / (dev_ms / 1e3) / 1e9
+    out = {"workload": "config4_qwen3next_48L_mtp_k3_verify_t4", "prompt_tokens": prompt_len,
+           "new_tokens": int(n_out), "decode_tok_s": (n_out - 1) / wall if n_out > 1 else 0.0,
+           "wall_s": wall, "iterations": iters, "tokens_per_iteration": (n_out - 1) / max(iters, 1),
+           "accept_hist": hist, "ms_per_iteration_device": dev_ms,
+           "bytes_per_iteration_est": it_bytes, "hbm_gbs_est": gbs,
+           "frac_of_hbm_peak": gbs / hbm_peak, "peak_gbs": hbm_peak, "peak_kind": peak_kind,
+           "prefill_s": prefill_s, "prefill_tok_s": prompt_len / prefill_s, "build_s": build_s,
+           "status": int(model.buf["status"].item()),
+           "first_tokens": [int(t) for t in toks[:8]],
+           "hbm_allocated_gb": torch.cuda.memory_allocated() / 1e9,
+           "note": "random-init weights: the MTP drafts rarely match, so about one token per "
+                   "iteration (the reference's acceptance on trained weights is not reproducible "
+                   "here)"}
+    del model, g
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_residency_leg(layers: int = 8, steps: int = 12, warmup: int = 4, T: int = 4,
                       cap: int = 192, seed: int = 1):
     """Config-1 layers over a pool of ``cap`` < 512 slots per layer, misses
@@ -794,6 +899,7 @@ def run_decode(args, world, rank, local):
             out["isoquant"] = run_isoquant_leg()
             out["prefill_attention"] = run_prefill_attention_leg()
             out["residency"] = run_residency_leg()
+            out["full_stack"] = run_full_stack_leg()
         else:
             out["prefill"] = run_prefill_ep_leg(world, rank)
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -820,7 +926,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the prefill (config 2) and IsoQuant (config 3) legs")
     ap.add_argument("--leg", default=None,
-                    choices=["prefill", "isoquant", "prefill_attention", "residency"],
+                    choices=["prefill", "isoquant", "prefill_attention", "residency",
+                             "full_stack"],
                     help="run only this extra leg on one GPU and print its result (for profiling)")
     ap.add_argument("--iso-layers", type=int, default=12)
     args = ap.parse_args()
@@ -830,7 +937,8 @@ def main():
                 "isoquant": lambda: run_isoquant_leg(args.steps, args.warmup,
                                                      layers=args.iso_layers),
                 "prefill_attention": lambda: run_prefill_attention_leg(args.steps, args.warmup),
-                "residency": lambda: run_residency_leg()}
+                "residency": lambda: run_residency_leg(),
+                "full_stack": lambda: run_full_stack_leg()}
         print(json.dumps({args.leg: legs[args.leg]()}), flush=True)
         return 0
     try:
