@@ -25,6 +25,7 @@ namespace vb {
 constexpr int QL_THREADS = 256;
 constexpr int QL_ROWS = 128;     // output rows per CTA (16 per warp)
 constexpr int QL_MAX_T = 8;
+constexpr int QL_MAX_S = 16;     // K slices per row block (K <= 4096)
 
 struct QlParams {
   const uint16_t *x;            // bf16 [T, K]
@@ -72,14 +73,34 @@ __global__ void __launch_bounds__(QL_THREADS) qlinear_kernel(QlParams p) {
     wa[j] = va ? ldg_nc_v2(p.codes + (size_t)ra * wpr + off) : make_uint2(0, 0);
     wb[j] = vb8 ? ldg_nc_v2(p.codes + (size_t)rb8 * wpr + off) : make_uint2(0, 0);
   }
-  uint16_t sa[KS], sb[KS], ba[KS], bb[KS];
-#pragma unroll
-  for (int j = 0; j < KS; ++j) {
-    sa[j] = va ? p.scales[(size_t)ra * gpr + grp0 + j] : 0;
-    ba[j] = va ? p.biases[(size_t)ra * gpr + grp0 + j] : 0;
-    sb[j] = vb8 ? p.scales[(size_t)rb8 * gpr + grp0 + j] : 0;
-    bb[j] = vb8 ? p.biases[(size_t)rb8 * gpr + grp0 + j] : 0;
+  // KS consecutive bf16 scales (biases) of a row: one 16-byte (KS = 8) or
+  // 8-byte (KS = 4) load each; word i holds groups 2i (low) and 2i+1 (high)
+  uint32_t sa[KS / 2], sb[KS / 2], ba[KS / 2], bb[KS / 2];
+  {
+    const size_t oa = (size_t)ra * gpr + grp0, ob = (size_t)rb8 * gpr + grp0;
+    if constexpr (KS == 8) {
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      const uint4 s0 = va ? ldg_nc_v4(p.scales + oa) : z, b0 = va ? ldg_nc_v4(p.biases + oa) : z;
+      const uint4 s1 = vb8 ? ldg_nc_v4(p.scales + ob) : z, b1 = vb8 ? ldg_nc_v4(p.biases + ob) : z;
+      sa[0] = s0.x; sa[1] = s0.y; sa[2] = s0.z; sa[3] = s0.w;
+      ba[0] = b0.x; ba[1] = b0.y; ba[2] = b0.z; ba[3] = b0.w;
+      sb[0] = s1.x; sb[1] = s1.y; sb[2] = s1.z; sb[3] = s1.w;
+      bb[0] = b1.x; bb[1] = b1.y; bb[2] = b1.z; bb[3] = b1.w;
+    } else {
+      const uint2 z = make_uint2(0, 0);
+      const uint2 s0 = va ? ldg_nc_v2(p.scales + oa) : z, b0 = va ? ldg_nc_v2(p.biases + oa) : z;
+      const uint2 s1 = vb8 ? ldg_nc_v2(p.scales + ob) : z, b1 = vb8 ? ldg_nc_v2(p.biases + ob) : z;
+      sa[0] = s0.x; sa[1] = s0.y; ba[0] = b0.x; ba[1] = b0.y;
+      sb[0] = s1.x; sb[1] = s1.y; bb[0] = b1.x; bb[1] = b1.y;
+    }
   }
+  // Everything above is weights. The kernels of the decode stack are
+  // launched plainly (a programmatic-dependent launch of every kernel was
+  // measured slower in the 48-layer graph), so pdl_wait is a no-op; the
+  // trigger lets a programmatic dependent (the MoE block kernel) launch
+  // while this grid drains.
+  pdl_launch_dependents();
+  pdl_wait();
 
   // 2. x: inverse RMS over the whole row (warp t takes token t), then the
   //    slice, normalised as bf16(bf16(x * inv) * w).
@@ -135,11 +156,16 @@ __global__ void __launch_bounds__(QL_THREADS) qlinear_kernel(QlParams p) {
     xfrag[m][l] = make_uint2((uint32_t)xr[kb] | ((uint32_t)xr[kb + 4] << 16),
                              (uint32_t)xr[kb + 1] | ((uint32_t)xr[kb + 5] << 16));
   }
-  if (tid < KS * QL_MAX_T) {
-    const int j = tid / QL_MAX_T, n = tid % QL_MAX_T;
+  // per-group sums of x: warp j takes group j, lane (n, quarter) 16 columns,
+  // the quarters added by shuffles (fixed order)
+  if (warp < KS) {
+    const int n = lane >> 2, qq = lane & 3;
     float sum = 0.f;
-    for (int k = 0; k < 64; ++k) sum += bf2f(xs_raw[n][j * 64 + k]);
-    xsum[j][n] = sum;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) sum += bf2f(xs_raw[n][warp * 64 + qq * 16 + k]);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if (qq == 0) xsum[warp][n] = sum;
   }
   __syncthreads();
 
@@ -159,8 +185,11 @@ __global__ void __launch_bounds__(QL_THREADS) qlinear_kernel(QlParams p) {
       const uint2 bf = xfrag[j * 4 + mm][lane];
       mma_bf16(d, pa[jw][2 * h], pb[jw][2 * h], pa[jw][2 * h + 1], pb[jw][2 * h + 1], bf.x, bf.y);
     }
-    const float s_a = bf2f(sa[j]), s_b = bf2f(sb[j]);
-    const float c_a = bf2f(ba[j]) - 128.f * s_a, c_b = bf2f(bb[j]) - 128.f * s_b;
+    const int sh = (j & 1) ? 0 : 16;  // low half: even group
+    const float s_a = __uint_as_float((sa[j >> 1] << sh) & 0xFFFF0000u);
+    const float s_b = __uint_as_float((sb[j >> 1] << sh) & 0xFFFF0000u);
+    const float c_a = __uint_as_float((ba[j >> 1] << sh) & 0xFFFF0000u) - 128.f * s_a;
+    const float c_b = __uint_as_float((bb[j >> 1] << sh) & 0xFFFF0000u) - 128.f * s_b;
     const float x0 = xsum[j][2 * c], x1 = xsum[j][2 * c + 1];
     acc[0] += fmaf(s_a, d[0], c_a * x0);
     acc[1] += fmaf(s_a, d[1], c_a * x1);
@@ -205,8 +234,13 @@ __global__ void __launch_bounds__(QL_THREADS) qlinear_kernel(QlParams p) {
   for (int i = tid; i < QL_ROWS * T; i += QL_THREADS) {
     const int n = i / QL_ROWS, row = row0 + i % QL_ROWS;
     if (row >= N) continue;
+    float part[QL_MAX_S];
+#pragma unroll
+    for (int ss = 0; ss < QL_MAX_S; ++ss)
+      part[ss] = ss < p.S ? __ldcg(p.partial + ((size_t)ss * T + n) * N + row) : 0.f;
     float v = 0.f;
-    for (int ss = 0; ss < p.S; ++ss) v += __ldcg(p.partial + ((size_t)ss * T + n) * N + row);
+#pragma unroll
+    for (int ss = 0; ss < QL_MAX_S; ++ss) v += part[ss];
     v = rbf(v);
     if (p.residual) v = bf2f(p.residual[(size_t)n * N + row]) + v;
     p.y[(size_t)n * N + row] = f2bf(v);
@@ -223,6 +257,8 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const uint16_t *__restric
                                                        float eps, uint16_t *__restrict__ h_out,
                                                        uint16_t *__restrict__ y, int y_stride) {
   __shared__ float red[8];
+  pdl_launch_dependents();
+  pdl_wait();
   const size_t row = blockIdx.x;
   const uint16_t *xr = x + row * D;
   float ss = 0.f;
@@ -261,6 +297,8 @@ __global__ void __launch_bounds__(256) argmax_kernel(const uint16_t *__restrict_
   __shared__ int si[8];
   __shared__ int last;
   const int row = blockIdx.x, part = blockIdx.y, tid = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
   const uint16_t *r = v + (size_t)row * n;
   float best = -INFINITY;
   int bi = INT_MAX;
@@ -311,6 +349,8 @@ __global__ void __launch_bounds__(256) embed4_kernel(const int32_t *__restrict__
                                                      uint16_t *__restrict__ out,
                                                      int32_t *status) {
   const int t = blockIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
   const int id = ids[t];
   const bool ok = id >= 0 && id < vocab;
   if (!ok && threadIdx.x == 0) flag_status(status, VB_STATUS_BOUNDS);
@@ -367,6 +407,8 @@ int vb_qlinear(const uint16_t *x, int32_t tokens, int32_t in_features,
                  (!norm_w || ((uintptr_t)norm_w % 16) == 0),
              "vb_qlinear: x and norm weights 16-byte aligned, codes 8-byte aligned");
   VB_REQUIRE(!norm_w || norm_eps > 0.f, "vb_qlinear: norm_eps %g", (double)norm_eps);
+  VB_REQUIRE(((uintptr_t)scales % 16) == 0 && ((uintptr_t)biases % 16) == 0,
+             "vb_qlinear: scales and biases 16-byte aligned");
   const int KS = ql_slice_groups(in_features, out_features);
   QlParams p;
   p.x = x; p.codes = codes; p.scales = scales; p.biases = biases; p.norm_w = norm_w;
@@ -384,11 +426,15 @@ int vb_qlinear(const uint16_t *x, int32_t tokens, int32_t in_features,
     p.partial = reinterpret_cast<float *>((char *)workspace +
                                           align_up((size_t)blocks * sizeof(uint32_t), 256));
   }
+  VB_REQUIRE(p.S <= QL_MAX_S, "vb_qlinear: %d K slices (in_features <= %d)", p.S,
+             QL_MAX_S * 4 * 64);
   const dim3 grid(blocks, p.S);
+  cudaError_t e;
   if (KS == 8)
-    qlinear_kernel<8><<<grid, QL_THREADS, 0, as_stream(stream)>>>(p);
+    e = vb_launch(qlinear_kernel<8>, grid, dim3(QL_THREADS), 0, as_stream(stream), false, p);
   else
-    qlinear_kernel<4><<<grid, QL_THREADS, 0, as_stream(stream)>>>(p);
+    e = vb_launch(qlinear_kernel<4>, grid, dim3(QL_THREADS), 0, as_stream(stream), false, p);
+  if (e != cudaSuccess) return check_launch("qlinear_kernel");
   return check_launch("qlinear_kernel");
 }
 
@@ -400,8 +446,8 @@ int vb_rms_norm(const uint16_t *x, const uint16_t *residual, const uint16_t *wei
   VB_REQUIRE(y_stride == 0 || y_stride >= dim, "vb_rms_norm: y_stride %d < dim %d", y_stride,
              dim);
   VB_REQUIRE(x && y, "vb_rms_norm: null tensor");
-  rms_norm_kernel<<<rows, 256, 0, as_stream(stream)>>>(x, residual, weight, dim, eps, h_out, y,
-                                                       y_stride ? y_stride : dim);
+  vb_launch(rms_norm_kernel, dim3(rows), dim3(256), 0, as_stream(stream), false, x, residual,
+            weight, dim, eps, h_out, y, (int)(y_stride ? y_stride : dim));
   return check_launch("rms_norm_kernel");
 }
 
@@ -423,8 +469,8 @@ int vb_argmax(const uint16_t *values, int32_t rows, int32_t n, int32_t *out, voi
   float *pv = reinterpret_cast<float *>((char *)workspace +
                                         align_up((size_t)rows * sizeof(uint32_t), 256));
   int32_t *pi = reinterpret_cast<int32_t *>(pv + (size_t)rows * AM_PARTS);
-  argmax_kernel<<<dim3(rows, AM_PARTS), 256, 0, as_stream(stream)>>>(values, n, pv, pi, tickets,
-                                                                     out);
+  vb_launch(argmax_kernel, dim3(rows, AM_PARTS), dim3(256), 0, as_stream(stream), false, values,
+            (int)n, pv, pi, tickets, out);
   return check_launch("argmax_kernel");
 }
 
@@ -438,8 +484,8 @@ int vb_embed_rows(const int32_t *ids, int32_t tokens, const uint32_t *codes,
              bits);
   VB_REQUIRE(ids && codes && scales && biases && out, "vb_embed_rows: null tensor");
   VB_REQUIRE(((uintptr_t)out % 16) == 0, "vb_embed_rows: out must be 16-byte aligned");
-  embed4_kernel<<<tokens, 256, 0, as_stream(stream)>>>(ids, codes, scales, biases, vocab, hidden,
-                                                       out, status);
+  vb_launch(embed4_kernel, dim3(tokens), dim3(256), 0, as_stream(stream), false, ids, codes, scales,
+            biases, (int)vocab, (int)hidden, out, status);
   return check_launch("embed4_kernel");
 }
 

@@ -45,6 +45,8 @@ __global__ void __launch_bounds__(GDN_THREADS) gdn_step_kernel(GdnParams p) {
   __shared__ float s_b[GDN_MAX_T];
   __shared__ int s_m[GDN_MAX_T];
   const int tid = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
   const int row0 = blockIdx.x * GDN_ROWS, hv = blockIdx.y, b = blockIdx.z;
   const int hk = hv / (p.Hv / p.Hk);
   const int T = p.T;
@@ -181,7 +183,8 @@ int vb_gated_delta_step_at(const uint16_t *q, const uint16_t *k, const uint16_t 
   p.B = batch; p.T = tokens; p.Hk = k_heads; p.Hv = v_heads; p.Dv = v_dim;
   p.g_per_key = g_per_key ? 1 : 0;
   p.in_slot = in_slot; p.slot_stride = (size_t)batch * v_heads * v_dim * GDN_DK; p.slots = slots;
-  gdn_step_kernel<<<dim3(v_dim / GDN_ROWS, v_heads, batch), GDN_THREADS, 0, as_stream(stream)>>>(p);
+  vb_launch(gdn_step_kernel, dim3(v_dim / GDN_ROWS, v_heads, batch), dim3(GDN_THREADS), 0,
+            as_stream(stream), false, p);
   return check_launch("gdn_step_kernel");
 }
 

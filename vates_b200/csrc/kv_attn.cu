@@ -48,6 +48,8 @@ __device__ __forceinline__ float bf_at2(const uint2 &v, int i) {
 constexpr int ATT_MAX_SPLITS = 1024;
 
 __global__ void __launch_bounds__(256) kv_attn_combine_kernel(AttnParams p) {
+  pdl_launch_dependents();
+  pdl_wait();  // no-op unless launched as a programmatic dependent
   __shared__ float s_red[256];
   __shared__ float s_e[ATT_MAX_SPLITS];
   __shared__ float s_num[8][32];
@@ -183,6 +185,10 @@ __device__ __forceinline__ void a1_fetch(const uint8_t *kbase, const uint8_t *vb
 template <bool DEV_POS>
 __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  if (DEV_POS) {  // launched as a programmatic dependent by the *_at entries
+    pdl_launch_dependents();
+    pdl_wait();
+  }
   const int S_ = DEV_POS ? min(max(*p.pos_dev, 0) + p.L, p.cap) : p.S;
   const int bh = blockIdx.x, split = blockIdx.y;
   const int b = bh / p.Hkv, hkv = bh % p.Hkv;
@@ -522,6 +528,10 @@ __device__ __forceinline__ void a4_fetch(const uint8_t *kbase, const uint8_t *vb
 template <bool DEV_POS>
 __global__ void __launch_bounds__(A4_WARPS * 32, 3) kv_attn4_kernel(AttnParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  if (DEV_POS) {  // launched as a programmatic dependent by the *_at entries
+    pdl_launch_dependents();
+    pdl_wait();
+  }
   const int S_ = DEV_POS ? min(max(*p.pos_dev, 0) + p.L, p.cap) : p.S;
   const int bh = blockIdx.x, split = blockIdx.y;
   const int b = bh / p.Hkv, hkv = bh % p.Hkv;
@@ -791,6 +801,10 @@ constexpr int B16_SMEM = 32 * 256 * 4 + 32 * B16_KP * 2 + 32 * 256 * 2 + 32 * 33
 template <bool DEV_POS>
 __global__ void __launch_bounds__(256) kv_bf16_attn_kernel(AttnParams p) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
+  if (DEV_POS) {  // launched as a programmatic dependent by the *_at entries
+    pdl_launch_dependents();
+    pdl_wait();
+  }
   const int S_ = DEV_POS ? min(max(*p.pos_dev, 0) + p.L, p.cap) : p.S;
   float *qs = reinterpret_cast<float *>(smem_raw);                    // [32][256]
   uint16_t *ks = reinterpret_cast<uint16_t *>(qs + 32 * 256);         // [32][B16_KP]
@@ -909,7 +923,11 @@ __global__ void __launch_bounds__(256) kv_bf16_attn_kernel(AttnParams p) {
   }
 }
 
-__global__ void add_i32_kernel(const int32_t *a, int32_t add, int32_t *out) { *out = *a + add; }
+__global__ void add_i32_kernel(const int32_t *a, int32_t add, int32_t *out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  *out = *a + add;
+}
 
 // Keys per split: about three CTAs per SM over all (batch, kv head) pairs,
 // in multiples of 64 keys.
@@ -990,18 +1008,21 @@ static int kv_decode_attn_impl(const uint16_t *q, const uint32_t *k_codes,
   }
   if (p.QR <= 8) {
     if (pos_dev)
-      kv_attn1_kernel<true><<<grid, A1_WARPS * 32, A1_SMEM, s>>>(p);
+      vb_launch(kv_attn1_kernel<true>, grid, dim3(A1_WARPS * 32), A1_SMEM, s, false, p);
     else
       kv_attn1_kernel<false><<<grid, A1_WARPS * 32, A1_SMEM, s>>>(p);
   } else {
     if (pos_dev)
-      kv_attn4_kernel<true><<<grid, A4_WARPS * 32, A4_SMEM, s>>>(p);
+      vb_launch(kv_attn4_kernel<true>, grid, dim3(A4_WARPS * 32), A4_SMEM, s, false, p);
     else
       kv_attn4_kernel<false><<<grid, A4_WARPS * 32, A4_SMEM, s>>>(p);
   }
   const int rc = check_launch(p.QR <= 8 ? "kv_attn1_kernel" : "kv_attn4_kernel");
   if (rc) return rc;
-  kv_attn_combine_kernel<<<dim3(batch * q_heads * L, 8), 256, 0, s>>>(p);
+  if (pos_dev)
+    vb_launch(kv_attn_combine_kernel, dim3(batch * q_heads * L, 8), dim3(256), 0, s, false, p);
+  else
+    kv_attn_combine_kernel<<<dim3(batch * q_heads * L, 8), 256, 0, s>>>(p);
   return check_launch("kv_attn_combine_kernel");
 }
 
@@ -1057,7 +1078,7 @@ int vb_kv_bf16_attn_at(const uint16_t *q, const uint16_t *k_cache, const uint16_
   // the key count pos + pos_add + L is read on the device: a one-int scratch
   int32_t *pos_eff = reinterpret_cast<int32_t *>(ws + obytes + 2 * mbytes);
   if (pos_add != 0) {
-    add_i32_kernel<<<1, 1, 0, s>>>(pos, pos_add, pos_eff);
+    vb_launch(add_i32_kernel, dim3(1), dim3(1), 0, s, false, pos, (int32_t)pos_add, pos_eff);
     const int rc0 = check_launch("add_i32_kernel");
     if (rc0) return rc0;
     p.pos_dev = pos_eff;
@@ -1070,10 +1091,11 @@ int vb_kv_bf16_attn_at(const uint16_t *q, const uint16_t *k_cache, const uint16_
                          B16_SMEM);
     attr_done = true;
   }
-  kv_bf16_attn_kernel<true><<<dim3(batch * kv_heads, p.nsplit), 256, B16_SMEM, s>>>(p);
+  vb_launch(kv_bf16_attn_kernel<true>, dim3(batch * kv_heads, p.nsplit), dim3(256), B16_SMEM, s,
+            true, p);
   const int rc = check_launch("kv_bf16_attn_kernel");
   if (rc) return rc;
-  kv_attn_combine_kernel<<<dim3(batch * q_heads * L, 8), 256, 0, s>>>(p);
+  vb_launch(kv_attn_combine_kernel, dim3(batch * q_heads * L, 8), dim3(256), 0, s, false, p);
   return check_launch("kv_attn_combine_kernel");
 }
 

@@ -23,6 +23,8 @@ __global__ void __launch_bounds__(256) kv_quant_kernel(
     uint16_t *__restrict__ biases, const int32_t *__restrict__ offset_dev,
     int32_t *status) {
   constexpr int D = LPR * 8;
+  pdl_launch_dependents();
+  pdl_wait();
   if (offset_dev) {  // position read on the device (the same for every thread)
     offset = *offset_dev;
     if (offset < 0 || offset + n > cap) {
@@ -158,18 +160,10 @@ static int kv_quant_append_impl(const uint16_t *src, const float *so4_blocks,
   const int64_t rows_per_block = 8 * (32 / lpr);  // 8 warps
   const unsigned blocks = (unsigned)((rows + rows_per_block - 1) / rows_per_block);
   cudaStream_t s = as_stream(stream);
-  if (lpr == 32)
-    kv_quant_kernel<32><<<blocks, 256, 0, s>>>(src, so4_blocks, rows, n, batch * heads,
-                                               bits, offset, cap, codes, scales, biases,
-                                               offset_dev, status);
-  else if (lpr == 16)
-    kv_quant_kernel<16><<<blocks, 256, 0, s>>>(src, so4_blocks, rows, n, batch * heads,
-                                               bits, offset, cap, codes, scales, biases,
-                                               offset_dev, status);
-  else
-    kv_quant_kernel<8><<<blocks, 256, 0, s>>>(src, so4_blocks, rows, n, batch * heads,
-                                              bits, offset, cap, codes, scales, biases,
-                                               offset_dev, status);
+  auto kern = lpr == 32 ? kv_quant_kernel<32> : (lpr == 16 ? kv_quant_kernel<16> : kv_quant_kernel<8>);
+  vb_launch(kern, dim3(blocks), dim3(256), 0, s, false, src, so4_blocks, rows, (int)n,
+            (int)(batch * heads), (int)bits, (int)offset, (int)cap, codes, scales, biases,
+            offset_dev, status);
   return check_launch("kv_quant_kernel");
 }
 

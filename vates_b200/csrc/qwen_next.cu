@@ -76,6 +76,11 @@ __global__ void __launch_bounds__(1024) gdn_prepare_kernel(GdnPrepParams p) {
     ch = 2 * p.Hk * p.Dk + hk * r * p.Dv + d;
     col = hk * W + 2 * p.Dk + d;
   }
+  float cw[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) cw[j] = bf2f(p.conv_w[(size_t)ch * 4 + j]);
+  pdl_launch_dependents();
+  pdl_wait();
   int off = p.conv_off ? *p.conv_off : 0;
   if (off < 0 || off > p.max_t) {
     if (tid == 0) flag_status(p.status, VB_STATUS_BOUNDS);
@@ -90,9 +95,6 @@ __global__ void __launch_bounds__(1024) gdn_prepare_kernel(GdnPrepParams p) {
 #pragma unroll
   for (int i = 0; i < 3 + QN_MAX_T; ++i)
     if (i < 3 + T) p.conv[(size_t)i * C + ch] = f2bf(win[i]);
-  float cw[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) cw[j] = bf2f(p.conv_w[(size_t)ch * 4 + j]);
   float y[QN_MAX_T];
 #pragma unroll
   for (int t = 0; t < QN_MAX_T; ++t) {
@@ -149,6 +151,8 @@ __global__ void __launch_bounds__(256) gdn_gated_norm_kernel(
     int Hk, int Hv, int Dk, int Dv, const uint16_t *__restrict__ w, float eps,
     uint16_t *__restrict__ out) {
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  pdl_launch_dependents();
+  pdl_wait();
   if (row >= T * Hv) return;
   const int t = row / Hv, hv = row % Hv;
   const int r = Hv / Hk, hk = hv / r, j = hv % r;
@@ -194,6 +198,8 @@ struct AttnPrepParams {
 __global__ void __launch_bounds__(256) attn_prepare_kernel(AttnPrepParams p) {
   const int wid = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   const int rows = p.Hq + 2 * p.Hkv;
+  pdl_launch_dependents();
+  pdl_wait();
   if (wid >= p.T * rows) return;
   const int t = wid / rows, h = wid % rows;
   const int kind = h < p.Hq ? 0 : (h < p.Hq + p.Hkv ? 1 : 2);
@@ -276,6 +282,8 @@ __global__ void __launch_bounds__(256) attn_gate_kernel(const uint16_t *__restri
                                                         int stride, int T, int Hq,
                                                         uint16_t *__restrict__ out) {
   const int i = blockIdx.x * 256 + threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
   if (i >= T * Hq * 256) return;
   const int t = i / (Hq * 256), rem = i % (Hq * 256), h = rem >> 8, d = rem & 255;
   const float gv = bf2f(proj[(size_t)t * stride + h * 512 + 256 + d]);
@@ -297,6 +305,8 @@ __global__ void __launch_bounds__(256) spec_accept_kernel(
     const uint16_t *__restrict__ vh, uint16_t *h_last, uint16_t *prev_h, int H,
     int32_t *out_tokens, int out_cap) {
   __shared__ int s_a;
+  pdl_launch_dependents();
+  pdl_wait();
   if (threadIdx.x == 0) {
     int a, pending;
     if (mode == 1) {  // prefill chunk: every row is committed
@@ -342,6 +352,8 @@ __global__ void __launch_bounds__(256) spec_sync_inputs_kernel(
     const int32_t *state, int32_t *ids, const uint16_t *__restrict__ vh,
     const uint16_t *__restrict__ prev_h, int V, int H, int32_t *sync_ids,
     uint16_t *sync_h) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int a = max(1, min(state[SP_ACC], V));
   for (int i = 0; i < V; ++i) {
     const int j = min(i, a - 1);
@@ -354,6 +366,8 @@ __global__ void __launch_bounds__(256) spec_sync_inputs_kernel(
 }
 
 __global__ void spec_advance_mtp_kernel(int32_t *state) {
+  pdl_launch_dependents();
+  pdl_wait();
   state[SP_MTP_POS] += state[SP_ACC];
 }
 
@@ -361,6 +375,8 @@ __global__ void spec_advance_mtp_kernel(int32_t *state) {
 __global__ void spec_prompt_ids_kernel(const int32_t *state, const int32_t *prompt,
                                        int prompt_len, int T, int32_t *ids) {
   const int i = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
   if (i < T) {
     const int at = state[SP_POS] + i;
     ids[i] = at < prompt_len ? prompt[at] : 0;
@@ -395,7 +411,7 @@ int vb_gdn_prepare(const uint16_t *proj, int32_t proj_stride, int32_t tokens, in
   p.Dk = head_k; p.Dv = head_v; p.max_t = max_tokens; p.conv = conv_buf; p.conv_off = conv_off;
   p.conv_w = conv_w; p.a_log = a_log; p.dt_bias = dt_bias; p.q = q; p.k = k; p.v = v;
   p.g = g; p.beta = beta; p.status = status;
-  gdn_prepare_kernel<<<k_heads, threads, 0, as_stream(stream)>>>(p);
+  vb_launch(gdn_prepare_kernel, dim3(k_heads), dim3(threads), 0, as_stream(stream), false, p);
   return check_launch("gdn_prepare_kernel");
 }
 
@@ -407,8 +423,9 @@ int vb_gdn_gated_norm(const uint16_t *y, const uint16_t *proj, int32_t proj_stri
              "vb_gdn_gated_norm: tokens=%d heads %d/%d", tokens, k_heads, v_heads);
   VB_REQUIRE(y && proj && weight && out, "vb_gdn_gated_norm: null tensor");
   const int rows = tokens * v_heads;
-  gdn_gated_norm_kernel<<<(rows + 7) / 8, 256, 0, as_stream(stream)>>>(
-      y, proj, proj_stride, tokens, k_heads, v_heads, head_k, head_v, weight, eps, out);
+  vb_launch(gdn_gated_norm_kernel, dim3((rows + 7) / 8), dim3(256), 0, as_stream(stream), false, y,
+            proj, (int)proj_stride, (int)tokens, (int)k_heads, (int)v_heads, (int)head_k,
+            (int)head_v, weight, eps, out);
   return check_launch("gdn_gated_norm_kernel");
 }
 
@@ -435,7 +452,7 @@ int vb_attn_prepare(const uint16_t *proj, int32_t proj_stride, int32_t tokens, i
   p.rope_log2_base = log2f(rope_base); p.pos = pos; p.pos_add = pos_add; p.rk = rk_blocks;
   p.q_out = q_out; p.k_out = k_out; p.v_out = v_out; p.kv_cap = kv_cap; p.status = status;
   const int warps = tokens * (q_heads + 2 * kv_heads);
-  attn_prepare_kernel<<<(warps + 7) / 8, 256, 0, as_stream(stream)>>>(p);
+  vb_launch(attn_prepare_kernel, dim3((warps + 7) / 8), dim3(256), 0, as_stream(stream), false, p);
   return check_launch("attn_prepare_kernel");
 }
 
@@ -444,8 +461,8 @@ int vb_attn_gate(const uint16_t *attn_out, const uint16_t *proj, int32_t proj_st
   VB_REQUIRE(tokens >= 1 && q_heads >= 1, "vb_attn_gate: tokens=%d heads=%d", tokens, q_heads);
   VB_REQUIRE(attn_out && proj && out, "vb_attn_gate: null tensor");
   const int n = tokens * q_heads * 256;
-  attn_gate_kernel<<<(n + 255) / 256, 256, 0, as_stream(stream)>>>(attn_out, proj, proj_stride,
-                                                                    tokens, q_heads, out);
+  vb_launch(attn_gate_kernel, dim3((n + 255) / 256), dim3(256), 0, as_stream(stream), false,
+            attn_out, proj, (int)proj_stride, (int)tokens, (int)q_heads, out);
   return check_launch("attn_gate_kernel");
 }
 
@@ -459,9 +476,9 @@ int vb_spec_accept(int32_t *state, int32_t *ids, const int32_t *preds, int32_t v
              "vb_spec_accept: verify_len %d > drafts + 1", verify_len);
   VB_REQUIRE(state && ids && preds && verify_hidden && h_last && prev_h && hidden > 0,
              "vb_spec_accept: null tensor");
-  spec_accept_kernel<<<1, 256, 0, as_stream(stream)>>>(state, ids, preds, verify_len, drafts,
-                                                       mode, verify_hidden, h_last, prev_h,
-                                                       hidden, out_tokens, out_cap);
+  vb_launch(spec_accept_kernel, dim3(1), dim3(256), 0, as_stream(stream), false, state, ids, preds,
+            (int)verify_len, (int)drafts, (int)mode, verify_hidden, h_last, prev_h, (int)hidden,
+            out_tokens, (int)out_cap);
   return check_launch("spec_accept_kernel");
 }
 
@@ -472,15 +489,15 @@ int vb_spec_sync_inputs(const int32_t *state, int32_t *ids, const uint16_t *veri
              "vb_spec_sync_inputs: verify_len=%d", verify_len);
   VB_REQUIRE(state && ids && verify_hidden && prev_h && sync_ids && sync_hidden,
              "vb_spec_sync_inputs: null tensor");
-  spec_sync_inputs_kernel<<<1, 256, 0, as_stream(stream)>>>(state, ids, verify_hidden, prev_h,
-                                                            verify_len, hidden, sync_ids,
-                                                            sync_hidden);
+  vb_launch(spec_sync_inputs_kernel, dim3(1), dim3(256), 0, as_stream(stream), false,
+            (const int32_t *)state, ids, verify_hidden, prev_h, (int)verify_len, (int)hidden,
+            sync_ids, sync_hidden);
   return check_launch("spec_sync_inputs_kernel");
 }
 
 int vb_spec_advance_mtp(int32_t *state, vb_stream_t stream) {
   VB_REQUIRE(state, "vb_spec_advance_mtp: null state");
-  spec_advance_mtp_kernel<<<1, 1, 0, as_stream(stream)>>>(state);
+  vb_launch(spec_advance_mtp_kernel, dim3(1), dim3(1), 0, as_stream(stream), false, state);
   return check_launch("spec_advance_mtp_kernel");
 }
 
@@ -489,7 +506,8 @@ int vb_spec_prompt_ids(const int32_t *state, const int32_t *prompt, int32_t prom
   VB_REQUIRE(tokens >= 1 && tokens <= QN_MAX_T && prompt_len >= 0,
              "vb_spec_prompt_ids: tokens=%d", tokens);
   VB_REQUIRE(state && prompt && ids, "vb_spec_prompt_ids: null tensor");
-  spec_prompt_ids_kernel<<<1, 32, 0, as_stream(stream)>>>(state, prompt, prompt_len, tokens, ids);
+  vb_launch(spec_prompt_ids_kernel, dim3(1), dim3(32), 0, as_stream(stream), false, state, prompt,
+            (int)prompt_len, (int)tokens, ids);
   return check_launch("spec_prompt_ids_kernel");
 }
 
