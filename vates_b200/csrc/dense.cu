@@ -9,23 +9,23 @@
 // s * sum(x q) + b * sum(x), float32 accumulation, one rounding to bf16; the
 // decoder's residual adds (h = x + r in bf16) and mx.fast.rms_norm.
 //
-// vb_qlinear, T <= 8 tokens (HBM-bound, 0.5 B per weight): a CTA of 8 warps
-// owns 128 output rows (16 per warp) and a K slice of KS groups of 64
-// columns; the K slices of one row block are separate CTAs whose float32
-// partials are added, in slice order, by the last CTA to finish (a ticket per
-// row block, reset by that CTA, so the kernel is deterministic and replayable
-// in a CUDA graph). Each lane loads its 8-byte share of every group of rows
-// g and g+8 up front, turns the codes into exact bf16 pairs 128 + q (LOP3)
-// and runs mma.m16n8k16 against x staged in shared memory in fragment order;
-// the group's scale and bias are applied as s * D + (b - 128 s) * sum(x).
+// vb_qlinear, T <= 8 tokens (HBM-bound, 0.5 B per weight): a persistent grid
+// (two CTAs of 8 warps per SM) walks items of 16 output rows over the whole K.
+// A CTA stages x once (RMS-normalised when asked) in MMA fragment order with
+// per-group sums; for an item, warp w takes groups [w*GPW, (w+1)*GPW) of the
+// 16 rows: each lane loads its 8-byte share of every group of rows g and g+8
+// plus a vector of scales and biases, turns the codes into exact bf16 pairs
+// 128 + q (LOP3) and runs mma.m16n8k16 against x; the group's scale and bias
+// are applied as s * D + (b - 128 s) * sum(x). The eight warps' partial sums
+// meet in shared memory and warp 0 adds them in warp order (deterministic).
+// The next item's codes are loaded while the current one is computed.
 #include "common.cuh"
 
 namespace vb {
 
 constexpr int QL_THREADS = 256;
-constexpr int QL_ROWS = 128;     // output rows per CTA (16 per warp)
 constexpr int QL_MAX_T = 8;
-constexpr int QL_MAX_S = 16;     // K slices per row block (K <= 4096)
+constexpr int QL_MAX_K = 4096;
 
 struct QlParams {
   const uint16_t *x;            // bf16 [T, K]
@@ -34,76 +34,129 @@ struct QlParams {
   const uint16_t *norm_w;       // nullable bf16 [K]: x -> rms_norm(x) * w
   const uint16_t *residual;     // nullable bf16 [T, N]
   uint16_t *y;                  // bf16 [T, N]
-  float *partial;               // [S, T, N] when S > 1
-  uint32_t *tickets;            // [ceil(N/128)] when S > 1, zero between launches
   float eps;
-  int T, K, N, S;
+  int T, K, N, items;
 };
 
-// Stage the K slice of x (optionally RMS-normalised) in fragment order.
-// Fragment of MMA m = 4 j + mm (group j of the slice, mm = 2 jw + h) for lane
-// (n = lane / 4, c = lane % 4): the word of 8 codes this lane holds for that
-// MMA covers columns kb .. kb+7 with kb = 64 (slice group) + 8 (2c + jw); the
-// A pairs it feeds are nibbles (2h, 2h+4) and (2h+1, 2h+5) of that word, so
-// b0 = x[n][kb + 2h], x[n][kb + 2h + 4] and b1 = x[n][kb + 2h + 1],
-// x[n][kb + 2h + 5].
-template <int KS>
-__global__ void __launch_bounds__(QL_THREADS) qlinear_kernel(QlParams p) {
-  __shared__ __align__(16) uint16_t xs_raw[QL_MAX_T][KS * 64];
-  __shared__ __align__(16) uint2 xfrag[KS * 4][32];
-  __shared__ float xsum[KS][QL_MAX_T];
-  __shared__ float inv_rms[QL_MAX_T];
-  __shared__ int last_cta;
+template <int GPW>
+struct QlItem {
+  uint2 wa[GPW], wb[GPW];
+  uint32_t sa[(GPW + 1) / 2], sb[(GPW + 1) / 2], ba[(GPW + 1) / 2], bb[(GPW + 1) / 2];
+};
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+// Codes and scales of item `it` for this lane (rows 16 it + g, + 8; groups
+// g0 .. g0 + GPW - 1, those past ng zero).
+template <int GPW>
+__device__ __forceinline__ void ql_load(const QlParams &p, int it, int g0, int ng, int lane,
+                                        QlItem<GPW> &d) {
   const int g = lane >> 2, c = lane & 3;
-  const int rb = blockIdx.x, s = blockIdx.y;
-  const int K = p.K, N = p.N, T = p.T;
-  const int wpr = K >> 3, gpr = K >> 6;
-  const int grp0 = s * KS;
-  const int ra = rb * QL_ROWS + warp * 16 + g, rb8 = ra + 8;
-  const bool va = ra < N, vb8 = rb8 < N;
-
-  // 1. Weight codes of both rows for every group of the slice, then scales
-  //    and biases (KS consecutive bf16 per row).
-  uint2 wa[KS], wb[KS];
+  const int ra = it * 16 + g, rb = ra + 8;
+  const bool va = ra < p.N, vb = rb < p.N;
+  const int wpr = p.K >> 3, gpr = p.K >> 6;
 #pragma unroll
-  for (int j = 0; j < KS; ++j) {
-    const int off = (grp0 + j) * 8 + 2 * c;
-    wa[j] = va ? ldg_nc_v2(p.codes + (size_t)ra * wpr + off) : make_uint2(0, 0);
-    wb[j] = vb8 ? ldg_nc_v2(p.codes + (size_t)rb8 * wpr + off) : make_uint2(0, 0);
+  for (int j = 0; j < GPW; ++j) {
+    const bool ok = j < ng;
+    const int off = (g0 + j) * 8 + 2 * c;
+    d.wa[j] = (va && ok) ? ldg_nc_v2(p.codes + (size_t)ra * wpr + off) : make_uint2(0, 0);
+    d.wb[j] = (vb && ok) ? ldg_nc_v2(p.codes + (size_t)rb * wpr + off) : make_uint2(0, 0);
   }
-  // KS consecutive bf16 scales (biases) of a row: one 16-byte (KS = 8) or
-  // 8-byte (KS = 4) load each; word i holds groups 2i (low) and 2i+1 (high)
-  uint32_t sa[KS / 2], sb[KS / 2], ba[KS / 2], bb[KS / 2];
-  {
-    const size_t oa = (size_t)ra * gpr + grp0, ob = (size_t)rb8 * gpr + grp0;
-    if constexpr (KS == 8) {
+  const size_t oa = (size_t)ra * gpr + g0, ob = (size_t)rb * gpr + g0;
+  // warps past the last group load no scales (their vectors would run past
+  // the row); a warp with groups has all GPW of them (G % GPW == 0)
+  const bool va_s = va && ng > 0, vb_s = vb && ng > 0;
+  if constexpr (GPW >= 8) {
+#pragma unroll
+    for (int h = 0; h < GPW / 8; ++h) {
       const uint4 z = make_uint4(0, 0, 0, 0);
-      const uint4 s0 = va ? ldg_nc_v4(p.scales + oa) : z, b0 = va ? ldg_nc_v4(p.biases + oa) : z;
-      const uint4 s1 = vb8 ? ldg_nc_v4(p.scales + ob) : z, b1 = vb8 ? ldg_nc_v4(p.biases + ob) : z;
-      sa[0] = s0.x; sa[1] = s0.y; sa[2] = s0.z; sa[3] = s0.w;
-      ba[0] = b0.x; ba[1] = b0.y; ba[2] = b0.z; ba[3] = b0.w;
-      sb[0] = s1.x; sb[1] = s1.y; sb[2] = s1.z; sb[3] = s1.w;
-      bb[0] = b1.x; bb[1] = b1.y; bb[2] = b1.z; bb[3] = b1.w;
-    } else {
-      const uint2 z = make_uint2(0, 0);
-      const uint2 s0 = va ? ldg_nc_v2(p.scales + oa) : z, b0 = va ? ldg_nc_v2(p.biases + oa) : z;
-      const uint2 s1 = vb8 ? ldg_nc_v2(p.scales + ob) : z, b1 = vb8 ? ldg_nc_v2(p.biases + ob) : z;
-      sa[0] = s0.x; sa[1] = s0.y; ba[0] = b0.x; ba[1] = b0.y;
-      sb[0] = s1.x; sb[1] = s1.y; bb[0] = b1.x; bb[1] = b1.y;
+      const uint4 s0 = va_s ? ldg_nc_v4(p.scales + oa + 8 * h) : z;
+      const uint4 b0 = va_s ? ldg_nc_v4(p.biases + oa + 8 * h) : z;
+      const uint4 s1 = vb_s ? ldg_nc_v4(p.scales + ob + 8 * h) : z;
+      const uint4 b1 = vb_s ? ldg_nc_v4(p.biases + ob + 8 * h) : z;
+      d.sa[4 * h] = s0.x; d.sa[4 * h + 1] = s0.y; d.sa[4 * h + 2] = s0.z; d.sa[4 * h + 3] = s0.w;
+      d.ba[4 * h] = b0.x; d.ba[4 * h + 1] = b0.y; d.ba[4 * h + 2] = b0.z; d.ba[4 * h + 3] = b0.w;
+      d.sb[4 * h] = s1.x; d.sb[4 * h + 1] = s1.y; d.sb[4 * h + 2] = s1.z; d.sb[4 * h + 3] = s1.w;
+      d.bb[4 * h] = b1.x; d.bb[4 * h + 1] = b1.y; d.bb[4 * h + 2] = b1.z; d.bb[4 * h + 3] = b1.w;
     }
+  } else if constexpr (GPW == 4) {
+    const uint2 z = make_uint2(0, 0);
+    const uint2 s0 = va_s ? ldg_nc_v2(p.scales + oa) : z, b0 = va_s ? ldg_nc_v2(p.biases + oa) : z;
+    const uint2 s1 = vb_s ? ldg_nc_v2(p.scales + ob) : z, b1 = vb_s ? ldg_nc_v2(p.biases + ob) : z;
+    d.sa[0] = s0.x; d.sa[1] = s0.y; d.ba[0] = b0.x; d.ba[1] = b0.y;
+    d.sb[0] = s1.x; d.sb[1] = s1.y; d.bb[0] = b1.x; d.bb[1] = b1.y;
+  } else if constexpr (GPW == 2) {
+    d.sa[0] = va_s ? __ldg(reinterpret_cast<const uint32_t *>(p.scales + oa)) : 0u;
+    d.ba[0] = va_s ? __ldg(reinterpret_cast<const uint32_t *>(p.biases + oa)) : 0u;
+    d.sb[0] = vb_s ? __ldg(reinterpret_cast<const uint32_t *>(p.scales + ob)) : 0u;
+    d.bb[0] = vb_s ? __ldg(reinterpret_cast<const uint32_t *>(p.biases + ob)) : 0u;
+  } else {
+    d.sa[0] = (va_s) ? (uint32_t)__ldg(p.scales + oa) : 0u;
+    d.ba[0] = (va_s) ? (uint32_t)__ldg(p.biases + oa) : 0u;
+    d.sb[0] = (vb_s) ? (uint32_t)__ldg(p.scales + ob) : 0u;
+    d.bb[0] = (vb_s) ? (uint32_t)__ldg(p.biases + ob) : 0u;
   }
-  // Everything above is weights. The kernels of the decode stack are
-  // launched plainly (a programmatic-dependent launch of every kernel was
-  // measured slower in the 48-layer graph), so pdl_wait is a no-op; the
-  // trigger lets a programmatic dependent (the MoE block kernel) launch
-  // while this grid drains.
+}
+
+// bf16 value of group j (low half: even j) of a packed scale/bias word array.
+template <int GPW>
+__device__ __forceinline__ float ql_half(const uint32_t (&w)[(GPW + 1) / 2], int j) {
+  const uint32_t v = w[j >> 1];
+  return __uint_as_float((j & 1) ? (v & 0xFFFF0000u) : (v << 16));
+}
+
+template <int GPW>
+__device__ __forceinline__ void ql_compute(const QlItem<GPW> &d, const uint2 *xfrag,
+                                           const float *xsum, int g0, int ng, int lane,
+                                           float (&acc)[4]) {
+  const int c = lane & 3;
+#pragma unroll
+  for (int j = 0; j < GPW; ++j) {
+    if (j >= ng) break;
+    const int grp = g0 + j;
+    float dd[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t pa[2][4], pb[2][4];
+    nib_pairs4(d.wa[j].x, pa[0]);
+    nib_pairs4(d.wa[j].y, pa[1]);
+    nib_pairs4(d.wb[j].x, pb[0]);
+    nib_pairs4(d.wb[j].y, pb[1]);
+#pragma unroll
+    for (int mm = 0; mm < 4; ++mm) {
+      const int jw = mm >> 1, h = mm & 1;
+      const uint2 bf = xfrag[(grp * 4 + mm) * 32 + lane];
+      mma_bf16(dd, pa[jw][2 * h], pb[jw][2 * h], pa[jw][2 * h + 1], pb[jw][2 * h + 1], bf.x,
+               bf.y);
+    }
+    const float s_a = ql_half<GPW>(d.sa, j), s_b = ql_half<GPW>(d.sb, j);
+    const float c_a = ql_half<GPW>(d.ba, j) - 128.f * s_a, c_b = ql_half<GPW>(d.bb, j) - 128.f * s_b;
+    const float x0 = xsum[grp * QL_MAX_T + 2 * c], x1 = xsum[grp * QL_MAX_T + 2 * c + 1];
+    acc[0] += fmaf(s_a, dd[0], c_a * x0);
+    acc[1] += fmaf(s_a, dd[1], c_a * x1);
+    acc[2] += fmaf(s_b, dd[2], c_b * x0);
+    acc[3] += fmaf(s_b, dd[3], c_b * x1);
+  }
+}
+
+// Dynamic shared memory: xfrag [K/16][32] uint2 and xsum [K/64][8] f32.
+template <int GPW>
+__global__ void __launch_bounds__(QL_THREADS, 2) qlinear_kernel(QlParams p) {
+  extern __shared__ __align__(16) uint8_t ql_smem[];
+  __shared__ float inv_rms[QL_MAX_T];
+  __shared__ float red[2][8][32][4];
+  const int K = p.K, T = p.T;
+  uint2 *xfrag = reinterpret_cast<uint2 *>(ql_smem);
+  float *xsum = reinterpret_cast<float *>(ql_smem + (size_t)K * 16);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = K >> 6;
+  const int g0 = warp * GPW, ng = max(0, min(GPW, G - g0));
+
+  // First item's weights (independent of earlier kernels) before anything else.
+  QlItem<GPW> cur, nxt;
+  int it = blockIdx.x;
+  if (it < p.items) ql_load<GPW>(p, it, g0, ng, lane, cur);
   pdl_launch_dependents();
   pdl_wait();
 
-  // 2. x: inverse RMS over the whole row (warp t takes token t), then the
-  //    slice, normalised as bf16(bf16(x * inv) * w).
+  // x: inverse RMS per row (warp t takes row t), then the rows staged as
+  // bf16(bf16(x * inv) * w) (or x), then fragments and group sums.
   if (p.norm_w) {
     for (int t = warp; t < T; t += QL_THREADS / 32) {
       const uint16_t *xr = p.x + (size_t)t * K;
@@ -124,128 +177,82 @@ __global__ void __launch_bounds__(QL_THREADS) qlinear_kernel(QlParams p) {
     }
     __syncthreads();
   }
-  for (int i = tid; i < QL_MAX_T * KS * 8; i += QL_THREADS) {
-    const int t = i / (KS * 8), k8 = (i % (KS * 8)) * 8;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (t < T) {
-      v = *reinterpret_cast<const uint4 *>(p.x + (size_t)t * K + grp0 * 64 + k8);
+  // Fragments straight from x: work item (row n, group grp, word w) loads
+  // the 8 columns kb = 64 grp + 8 w of row n and writes the two fragments
+  // that word feeds. Fragment of MMA m = 4 grp + mm (mm = 2 jw + h) for lane
+  // (n, c): the lane's code word covers columns 64 grp + 8 (2c + jw) .. +7,
+  // its A pairs are nibbles (2h, 2h+4) and (2h+1, 2h+5), so b0 = x[n][kb+2h],
+  // x[n][kb+2h+4] and b1 = x[n][kb+2h+1], x[n][kb+2h+5] with w = 2c + jw.
+  // The 8 words of (n, grp) are 8 consecutive lanes: their sum by shuffles
+  // (fixed order) is the group sum.
+  for (int i = tid; i < QL_MAX_T * G * 8; i += QL_THREADS) {
+    const int w = i & 7, grp = (i >> 3) % G, n = (i >> 3) / G;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (n < T) {
+      const int k8 = grp * 64 + w * 8;
+      const uint4 raw = *reinterpret_cast<const uint4 *>(p.x + (size_t)n * K + k8);
+      const uint32_t xv[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        v[2 * q] = __uint_as_float(xv[q] << 16);
+        v[2 * q + 1] = __uint_as_float(xv[q] & 0xFFFF0000u);
+      }
       if (p.norm_w) {
-        const uint4 w = *reinterpret_cast<const uint4 *>(p.norm_w + grp0 * 64 + k8);
-        uint32_t xv[4] = {v.x, v.y, v.z, v.w};
-        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-        const float inv = inv_rms[t];
+        const uint4 wr = *reinterpret_cast<const uint4 *>(p.norm_w + k8);
+        const uint32_t wv[4] = {wr.x, wr.y, wr.z, wr.w};
+        const float inv = inv_rms[n];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const float lo = rbf(__uint_as_float(xv[q] << 16) * inv);
-          const float hi = rbf(__uint_as_float(xv[q] & 0xFFFF0000u) * inv);
-          xv[q] = pack_bf2(lo * __uint_as_float(wv[q] << 16),
-                           hi * __uint_as_float(wv[q] & 0xFFFF0000u));
+          v[2 * q] = rbf(rbf(v[2 * q] * inv) * __uint_as_float(wv[q] << 16));
+          v[2 * q + 1] = rbf(rbf(v[2 * q + 1] * inv) * __uint_as_float(wv[q] & 0xFFFF0000u));
         }
-        v = make_uint4(xv[0], xv[1], xv[2], xv[3]);
       }
     }
-    *reinterpret_cast<uint4 *>(&xs_raw[t][k8]) = v;
-  }
-  __syncthreads();
-  for (int i = tid; i < KS * 4 * 32; i += QL_THREADS) {
-    const int m = i >> 5, l = i & 31;
-    const int j = m >> 2, mm = m & 3, jw = mm >> 1, h = mm & 1;
-    const int n = l >> 2, cc = l & 3;
-    const int kb = j * 64 + 8 * (2 * cc + jw) + 2 * h;
-    const uint16_t *xr = xs_raw[n];
-    xfrag[m][l] = make_uint2((uint32_t)xr[kb] | ((uint32_t)xr[kb + 4] << 16),
-                             (uint32_t)xr[kb + 1] | ((uint32_t)xr[kb + 5] << 16));
-  }
-  // per-group sums of x: warp j takes group j, lane (n, quarter) 16 columns,
-  // the quarters added by shuffles (fixed order)
-  if (warp < KS) {
-    const int n = lane >> 2, qq = lane & 3;
+    const int cc = w >> 1, jw = w & 1, l = n * 4 + cc;
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      xfrag[(grp * 4 + 2 * jw + h) * 32 + l] =
+          make_uint2(pack_bf2(v[2 * h], v[2 * h + 4]), pack_bf2(v[2 * h + 1], v[2 * h + 5]));
     float sum = 0.f;
 #pragma unroll
-    for (int k = 0; k < 16; ++k) sum += bf2f(xs_raw[n][warp * 64 + qq * 16 + k]);
+    for (int q = 0; q < 8; ++q) sum += v[q];
     sum += __shfl_xor_sync(0xffffffffu, sum, 1);
     sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    if (qq == 0) xsum[warp][n] = sum;
+    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+    if (w == 0) xsum[grp * QL_MAX_T + n] = sum;
   }
   __syncthreads();
 
-  // 3. Four MMAs per group, then the group's scale and bias.
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const int c = lane & 3, g = lane >> 2;
+  int buf = 0;
+  for (; it < p.items; it += gridDim.x) {
+    const int next = it + gridDim.x;
+    if (next < p.items) ql_load<GPW>(p, next, g0, ng, lane, nxt);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    ql_compute<GPW>(cur, xfrag, xsum, g0, ng, lane, acc);
+    *reinterpret_cast<float4 *>(red[buf][warp][lane]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    __syncthreads();
+    if (warp == 0) {
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int j = 0; j < KS; ++j) {
-    float d[4] = {0.f, 0.f, 0.f, 0.f};
-    uint32_t pa[2][4], pb[2][4];
-    nib_pairs4(wa[j].x, pa[0]);
-    nib_pairs4(wa[j].y, pa[1]);
-    nib_pairs4(wb[j].x, pb[0]);
-    nib_pairs4(wb[j].y, pb[1]);
+      for (int w = 0; w < 8; ++w) {
+        const float4 v = *reinterpret_cast<const float4 *>(red[buf][w][lane]);
+        o[0] += v.x; o[1] += v.y; o[2] += v.z; o[3] += v.w;
+      }
+      const int rows[2] = {it * 16 + g, it * 16 + g + 8};
 #pragma unroll
-    for (int mm = 0; mm < 4; ++mm) {
-      const int jw = mm >> 1, h = mm & 1;
-      const uint2 bf = xfrag[j * 4 + mm][lane];
-      mma_bf16(d, pa[jw][2 * h], pb[jw][2 * h], pa[jw][2 * h + 1], pb[jw][2 * h + 1], bf.x, bf.y);
-    }
-    const int sh = (j & 1) ? 0 : 16;  // low half: even group
-    const float s_a = __uint_as_float((sa[j >> 1] << sh) & 0xFFFF0000u);
-    const float s_b = __uint_as_float((sb[j >> 1] << sh) & 0xFFFF0000u);
-    const float c_a = __uint_as_float((ba[j >> 1] << sh) & 0xFFFF0000u) - 128.f * s_a;
-    const float c_b = __uint_as_float((bb[j >> 1] << sh) & 0xFFFF0000u) - 128.f * s_b;
-    const float x0 = xsum[j][2 * c], x1 = xsum[j][2 * c + 1];
-    acc[0] += fmaf(s_a, d[0], c_a * x0);
-    acc[1] += fmaf(s_a, d[1], c_a * x1);
-    acc[2] += fmaf(s_b, d[2], c_b * x0);
-    acc[3] += fmaf(s_b, d[3], c_b * x1);
-  }
-
-  // 4. Output: directly when the row block has one slice, else partials and
-  //    the last CTA's ordered reduction.
-  const int n0 = 2 * c, n1 = 2 * c + 1;
-  if (p.S == 1) {
-    const int rows[2] = {ra, rb8};
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int row = rows[q >> 1], n = (q & 1) ? n1 : n0;
-      if (row < N && n < T) {
-        float v = rbf(acc[q]);
-        if (p.residual) v = bf2f(p.residual[(size_t)n * N + row]) + v;
-        p.y[(size_t)n * N + row] = f2bf(v);
+      for (int q = 0; q < 4; ++q) {
+        const int row = rows[q >> 1], n = 2 * c + (q & 1);
+        if (row < p.N && n < T) {
+          float v = rbf(o[q]);
+          if (p.residual) v = bf2f(p.residual[(size_t)n * p.N + row]) + v;
+          p.y[(size_t)n * p.N + row] = f2bf(v);
+        }
       }
     }
-    return;
+    buf ^= 1;  // the next item writes the other partial buffer: one barrier per item
+    cur = nxt;
   }
-  {
-    const int rows[2] = {ra, rb8};
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int row = rows[q >> 1], n = (q & 1) ? n1 : n0;
-      if (row < N && n < T) p.partial[((size_t)s * T + n) * N + row] = acc[q];
-    }
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const uint32_t ticket = atomicAdd(p.tickets + rb, 1u);
-    last_cta = ticket == (uint32_t)(p.S - 1);
-  }
-  __syncthreads();
-  if (!last_cta) return;
-  __threadfence();
-  const int row0 = rb * QL_ROWS;
-  for (int i = tid; i < QL_ROWS * T; i += QL_THREADS) {
-    const int n = i / QL_ROWS, row = row0 + i % QL_ROWS;
-    if (row >= N) continue;
-    float part[QL_MAX_S];
-#pragma unroll
-    for (int ss = 0; ss < QL_MAX_S; ++ss)
-      part[ss] = ss < p.S ? __ldcg(p.partial + ((size_t)ss * T + n) * N + row) : 0.f;
-    float v = 0.f;
-#pragma unroll
-    for (int ss = 0; ss < QL_MAX_S; ++ss) v += part[ss];
-    v = rbf(v);
-    if (p.residual) v = bf2f(p.residual[(size_t)n * N + row]) + v;
-    p.y[(size_t)n * N + row] = f2bf(v);
-  }
-  if (tid == 0) p.tickets[rb] = 0u;
 }
 
 // RMSNorm with an optional residual add: h = bf16(x + r) (written to h_out
@@ -369,11 +376,32 @@ __global__ void __launch_bounds__(256) embed4_kernel(const int32_t *__restrict__
   }
 }
 
-// Groups per K slice: 8 when the grid still has two CTAs per SM with it,
-// else 4 (more slices for narrow outputs).
-static int ql_slice_groups(int K, int N) {
-  const long blocks = (N + QL_ROWS - 1) / QL_ROWS;
-  return (K % 512 == 0 && blocks * (K / 512) >= 2 * 148) ? 8 : 4;
+static size_t ql_smem_bytes(int K) {
+  return (size_t)K * 16 + (size_t)(K / 64) * QL_MAX_T * 4;
+}
+
+static int ql_sm_count() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
+template <int GPW>
+static cudaError_t ql_launch(const QlParams &p, cudaStream_t s) {
+  static bool attr_done = false;
+  const size_t smem = ql_smem_bytes(p.K);
+  if (!attr_done) {
+    cudaFuncSetAttribute(qlinear_kernel<GPW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)ql_smem_bytes(QL_MAX_K));
+    attr_done = true;
+  }
+  const int grid = min(p.items, 2 * ql_sm_count());
+  return vb_launch(qlinear_kernel<GPW>, dim3(grid), dim3(QL_THREADS), smem, s, false, p);
 }
 
 }  // namespace vb
@@ -383,12 +411,8 @@ using namespace vb;
 extern "C" {
 
 size_t vb_qlinear_workspace_size(int32_t tokens, int32_t in_features, int32_t out_features) {
-  if (tokens < 1 || in_features < 256 || out_features < 1) return 0;
-  const int S = in_features / 64 / ql_slice_groups(in_features, out_features);
-  const size_t blocks = (size_t)(out_features + QL_ROWS - 1) / QL_ROWS;
-  if (S <= 1) return 0;
-  return align_up(blocks * sizeof(uint32_t), 256) +
-         (size_t)S * tokens * out_features * sizeof(float);
+  (void)tokens; (void)in_features; (void)out_features;
+  return 0;  // no scratch: the K reduction stays inside a CTA
 }
 
 int vb_qlinear(const uint16_t *x, int32_t tokens, int32_t in_features,
@@ -396,11 +420,14 @@ int vb_qlinear(const uint16_t *x, int32_t tokens, int32_t in_features,
                int32_t out_features, int32_t group, int32_t bits, const uint16_t *norm_w,
                float norm_eps, const uint16_t *residual, uint16_t *y, void *workspace,
                size_t workspace_bytes, vb_stream_t stream) {
+  (void)workspace; (void)workspace_bytes;
   VB_REQUIRE(tokens >= 1 && tokens <= QL_MAX_T, "vb_qlinear: tokens=%d (1..%d)", tokens,
              QL_MAX_T);
   VB_REQUIRE(group == 64 && bits == 4, "vb_qlinear: group %d bits %d (64, 4 only)", group, bits);
-  VB_REQUIRE(in_features >= 256 && in_features % 256 == 0,
-             "vb_qlinear: in_features %d (a multiple of 256)", in_features);
+  VB_REQUIRE(in_features >= 256 && in_features % 256 == 0 && in_features <= QL_MAX_K &&
+                 (in_features <= 2048 || in_features % 512 == 0),
+             "vb_qlinear: in_features %d (a multiple of 256 up to 2048, of 512 up to %d)",
+             in_features, QL_MAX_K);
   VB_REQUIRE(out_features >= 1, "vb_qlinear: out_features %d", out_features);
   VB_REQUIRE(x && codes && scales && biases && y, "vb_qlinear: null tensor");
   VB_REQUIRE(((uintptr_t)x % 16) == 0 && ((uintptr_t)codes % 8) == 0 &&
@@ -409,32 +436,23 @@ int vb_qlinear(const uint16_t *x, int32_t tokens, int32_t in_features,
   VB_REQUIRE(!norm_w || norm_eps > 0.f, "vb_qlinear: norm_eps %g", (double)norm_eps);
   VB_REQUIRE(((uintptr_t)scales % 16) == 0 && ((uintptr_t)biases % 16) == 0,
              "vb_qlinear: scales and biases 16-byte aligned");
-  const int KS = ql_slice_groups(in_features, out_features);
   QlParams p;
   p.x = x; p.codes = codes; p.scales = scales; p.biases = biases; p.norm_w = norm_w;
   p.residual = residual; p.y = y; p.eps = norm_eps;
   p.T = tokens; p.K = in_features; p.N = out_features;
-  p.S = in_features / 64 / KS;
-  p.partial = nullptr; p.tickets = nullptr;
-  const int blocks = (out_features + QL_ROWS - 1) / QL_ROWS;
-  if (p.S > 1) {
-    const size_t need = vb_qlinear_workspace_size(tokens, in_features, out_features);
-    VB_REQUIRE(workspace && workspace_bytes >= need,
-               "vb_qlinear: workspace %zu bytes, %zu needed (zero-filled once)", workspace_bytes,
-               need);
-    p.tickets = reinterpret_cast<uint32_t *>(workspace);
-    p.partial = reinterpret_cast<float *>((char *)workspace +
-                                          align_up((size_t)blocks * sizeof(uint32_t), 256));
-  }
-  VB_REQUIRE(p.S <= QL_MAX_S, "vb_qlinear: %d K slices (in_features <= %d)", p.S,
-             QL_MAX_S * 4 * 64);
-  const dim3 grid(blocks, p.S);
+  p.items = (out_features + 15) / 16;
+  const int G = in_features / 64;   // groups; eight warps share them
+  const cudaStream_t s = as_stream(stream);
   cudaError_t e;
-  if (KS == 8)
-    e = vb_launch(qlinear_kernel<8>, grid, dim3(QL_THREADS), 0, as_stream(stream), false, p);
+  if (G <= 8)
+    e = ql_launch<1>(p, s);
+  else if (G <= 16)
+    e = ql_launch<2>(p, s);
+  else if (G <= 32)
+    e = ql_launch<4>(p, s);
   else
-    e = vb_launch(qlinear_kernel<4>, grid, dim3(QL_THREADS), 0, as_stream(stream), false, p);
-  if (e != cudaSuccess) return check_launch("qlinear_kernel");
+    e = ql_launch<8>(p, s);
+  (void)e;
   return check_launch("qlinear_kernel");
 }
 
