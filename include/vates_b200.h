@@ -712,6 +712,21 @@ int vb_gdn_gated_norm(const uint16_t *y, const uint16_t *proj, int32_t proj_stri
                       int32_t head_v, const uint16_t *weight, float eps, uint16_t *out,
                       vb_stream_t stream);
 
+/* The three calls above (vb_gdn_prepare -> vb_gated_delta_step_at ->
+ * vb_gdn_gated_norm, batch 1) in one launch, bit-identical to them: one
+ * thread-block cluster of (v_heads / k_heads) x (head_v / 32) <= 8 CTAs per
+ * key head; the conv window is moved after a cluster barrier and the gated
+ * norm's row sums cross the cluster through distributed shared memory.
+ * states f32 [slots, v_heads, head_v, 128] as vb_gated_delta_step_at (start
+ * state in slot *in_slot, the state after row t in slot t); out bf16
+ * [T, v_heads * head_v]. head_k = 128, T <= max_tokens <= 8. */
+int vb_gdn_fused(const uint16_t *proj, int32_t proj_stride, int32_t tokens, int32_t k_heads,
+                 int32_t v_heads, int32_t head_k, int32_t head_v, uint16_t *conv_buf,
+                 int32_t max_tokens, const int32_t *conv_off, const uint16_t *conv_w,
+                 const float *a_log, const uint16_t *dt_bias, float *states, int32_t slots,
+                 const int32_t *in_slot, const uint16_t *norm_w, float eps, uint16_t *out,
+                 int32_t *status, vb_stream_t stream);
+
 /* Attention input side (kv_quant_patch.py:29-56): proj bf16 [T, proj_stride]
  * = q_proj (per head [query 256, gate 256]) | k_proj | v_proj. Queries and
  * keys get their RMSNorm (weights [256]) and RoPE over the first rope_dims

@@ -158,6 +158,40 @@ def test_layers_two_steps_vs_oracle(tiny):
     assert int(b["status"].item()) == 0
 
 
+def _gdn_fused_vs_split(model, layer, steps, seed):
+    """Run a GDN layer (in_proj -> core -> out_proj) with the fused core and
+    with the three-kernel core from the same buffers; outputs, conv windows
+    and state checkpoints must be bit-identical."""
+    import torch
+    from vates_b200.qwen_next import SP_ACC, SP_SLOT
+    b, m, cfg = model.buf, layer.mixer, model.cfg
+    rng = np.random.default_rng(seed)
+    for T, acc in steps:
+        if acc is not None:
+            b["state"][SP_ACC] = acc
+            b["state"][SP_SLOT] = acc - 1
+        b["x0"][:T] = _bf(rng.standard_normal((T, cfg.hidden)).astype(np.float32))
+        conv0, st0 = m.conv_buf.clone(), m.states.clone()
+        model._gdn(m, layer, b["x0"], b["h"], T, None, fused=False)
+        torch.cuda.synchronize()
+        ref = (b["h"][:T].clone(), m.conv_buf[:3 + T].clone(), m.states[:T].clone())
+        m.conv_buf.copy_(conv0)
+        m.states.copy_(st0)
+        model._gdn(m, layer, b["x0"], b["h"], T, None, fused=True)
+        torch.cuda.synchronize()
+        assert torch.equal(b["h"][:T], ref[0]), f"out T={T}"
+        assert torch.equal(m.conv_buf[:3 + T], ref[1]), f"conv window T={T}"
+        assert torch.equal(m.states[:T], ref[2]), f"state checkpoints T={T}"
+
+
+def test_gdn_fused_equals_three_kernels(tiny):
+    """One cluster launch per GDN layer core = prepare + step + gated norm,
+    bit for bit, across a commit of 2 of 4 rows and a 3-row step."""
+    model, _ = tiny
+    model.reset()
+    _gdn_fused_vs_split(model, model.layers[0], ((4, None), (3, 2), (1, 3)), 7)
+
+
 def test_forward_logits_vs_oracle(tiny):
     """Embeddings -> 4 layers -> final norm + lm_head -> argmax, two chunks,
     free-running. Each block matches on identical inputs (test above); over a
@@ -275,6 +309,8 @@ def test_config4_layers_and_loop(cuda):
     b = model.buf
     rng = np.random.default_rng(2)
     c = om.cfg
+    _gdn_fused_vs_split(model, model.layers[0], ((4, None), (4, 1)), 8)
+    model.reset()
     for i in (0, 3):
         x = M.bf16(rng.standard_normal((4, cfg.hidden)).astype(np.float32))
         L = om.layers[i]

@@ -178,6 +178,8 @@ _SIGNATURES = {
     "vb_embed_rows": (_I32, [_P, _I32, _P, _P, _P, _I32, _I32, _I32, _I32, _P, _P, _P]),
     "vb_gdn_prepare": (_I32, [_P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I32, _P, _P, _P, _P,
                               _P, _P, _P, _P, _P, _P, _P]),
+    "vb_gdn_fused": (_I32, [_P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I32, _P, _P, _P, _P, _P,
+                            _I32, _P, _P, C.c_float, _P, _P, _P]),
     "vb_gdn_gated_norm": (_I32, [_P, _P, _I32, _I32, _I32, _I32, _I32, _I32, _P, C.c_float, _P,
                                  _P]),
     "vb_attn_prepare": (_I32, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, C.c_float, _I32,

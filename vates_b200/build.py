@@ -33,6 +33,7 @@ SOURCES = [
     "gdn.cu",
     "dense.cu",
     "qwen_next.cu",
+    "gdn_fused.cu",
 ]
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

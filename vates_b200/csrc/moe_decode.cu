@@ -491,28 +491,25 @@ __device__ __forceinline__ void down_combine_rows(const DecodeParams &p, const i
 // Routing of all T tokens, run identically by every CTA of the layer kernel
 // (all threads call it): precise softmax of the logits, top-k, optional
 // renormalisation, slot gather, then the entry list. Token t is handled by
-// the wpt warps t*wpt .. t*wpt + wpt - 1, each over PERW * 32 of the E
-// logits: the maximum and the exponential sum meet in shared memory (summed
-// in warp order), every warp selects its own top-k candidates, and the
-// token's first warp picks the top-k of the wpt*k candidates. Keys are the
-// bf16 probability bits above (0xFFFF - expert id), so the unsigned maximum
-// is the largest probability with ties to the lower id. Results in shared
-// memory (routes rex/rslot/rscore/rent, flags ok, entries ent); returns the
-// number of entries. primary: this CTA also writes the optional outputs and
-// the status bits.
+// warp t alone, PERW = E/32 logits per lane, warp-synchronously (no block
+// barrier before the entry list): maximum, exponential sum (double, exact
+// for the softmax's range, so independent of the order), then k extractions
+// of the largest key. Keys are the bf16 probability bits above (0xFFFF -
+// expert id), so the unsigned maximum is the largest probability with ties
+// to the lower id. Results in shared memory (routes rex/rslot/rscore/rent,
+// flags ok, entries ent); returns the number of entries. primary: this CTA
+// also writes the optional outputs and the status bits.
 template <int PERW>
 __device__ __noinline__ int route_tokens(const float *logits, const int32_t *table, int T, int E,
-                                         int k, int wpt, int norm_topk, int has_shared, int cap,
+                                         int k, int norm_topk, int has_shared, int cap,
                                          bool primary, int32_t *status, int32_t *out_inds,
                                          uint16_t *out_scores, int32_t *out_local,
                                          int *s_table, int *s_first, int *s_rex, int *s_rslot,
                                          float *s_rscore, int *s_rent, int32_t *s_ok,
-                                         DecEntry *s_ent, int *s_wcnt, uint32_t *s_wmax,
-                                         double *s_wsum, uint32_t *s_cand, uint64_t *trace) {
+                                         DecEntry *s_ent, int *s_wcnt, uint64_t *trace) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int t = warp / wpt, wp = warp - t * wpt;
+  const int t = warp;                 // token of this warp
   const bool act = t < T;
-  const int base = wp * PERW * 32;
   // Slot table and logits are loaded together (one memory round trip).
   float v[PERW];
   {
@@ -524,7 +521,7 @@ __device__ __noinline__ int route_tokens(const float *logits, const int32_t *tab
     }
 #pragma unroll
     for (int i = 0; i < PERW; ++i) {
-      const int idx = base + lane + 32 * i;
+      const int idx = lane + 32 * i;
       v[i] = (act && idx < E) ? __ldcg(logits + (size_t)t * E + idx) : -INFINITY;
     }
 #pragma unroll
@@ -536,89 +533,55 @@ __device__ __noinline__ int route_tokens(const float *logits, const int32_t *tab
       }
     }
   }
-  uint32_t mk = 0;
+  __syncthreads();  // slot table and first-route markers
+  if (act) {
+    uint32_t mk = 0;
 #pragma unroll
-  for (int i = 0; i < PERW; ++i) mk = max(mk, f2key(v[i]));
-  mk = __reduce_max_sync(0xffffffffu, mk);
-  if (lane == 0) s_wmax[warp] = mk;
-  __syncthreads();
-  trace_mark(trace, 9);
-  uint32_t mt = 0;
-  if (act)
-    for (int w = 0; w < wpt; ++w) mt = max(mt, s_wmax[t * wpt + w]);
-  const float m = key2f(mt);
-  double sd[PERW];
+    for (int i = 0; i < PERW; ++i) mk = max(mk, f2key(v[i]));
+    const float m = key2f(__reduce_max_sync(0xffffffffu, mk));
+    trace_mark(trace, 9);
+    double sd[PERW];
 #pragma unroll
-  for (int i = 0; i < PERW; ++i) {
-    const int idx = base + lane + 32 * i;
-    const float ex = (act && idx < E) ? expf(__fsub_rn(v[i], m)) : 0.f;
-    v[i] = ex;
-    sd[i] = (double)ex;
-  }
-#pragma unroll
-  for (int w = 1; w < PERW; w *= 2)
-#pragma unroll
-    for (int i = 0; i + w < PERW; i += 2 * w) sd[i] += sd[i + w];
-  double s = sd[0];
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if (lane == 0) s_wsum[warp] = s;
-  __syncthreads();
-  trace_mark(trace, 10);
-  double st = 0.0;
-  if (act)
-    for (int w = 0; w < wpt; ++w) st += s_wsum[t * wpt + w];
-  const float inv = act ? __frcp_rn((float)st) : 0.f;
-  // This warp's top-k candidates (keys are distinct: one lane holds each).
-  uint32_t key[PERW], lb = 0;
-#pragma unroll
-  for (int i = 0; i < PERW; ++i) {
-    const int idx = base + lane + 32 * i;
-    key[i] = (act && idx < E) ? ((uint32_t)f2bf(__fmul_rn(v[i], inv)) << 16) | (0xFFFFu - idx) : 0u;
-    lb = max(lb, key[i]);
-  }
-  uint32_t mine = 0;
-  for (int r = 0; r < k; ++r) {
-    const uint32_t best = __reduce_max_sync(0xffffffffu, lb);
-    if (lb == best && best != 0u) {
-      lb = 0;
-#pragma unroll
-      for (int i = 0; i < PERW; ++i) {
-        if (key[i] == best) key[i] = 0u;
-        lb = max(lb, key[i]);
-      }
+    for (int i = 0; i < PERW; ++i) {
+      const int idx = lane + 32 * i;
+      const float ex = idx < E ? expf(__fsub_rn(v[i], m)) : 0.f;
+      v[i] = ex;
+      sd[i] = (double)ex;
     }
-    if (lane == r) mine = best;
-  }
-  if (act && lane < k) s_cand[warp * k + lane] = mine;
-  __syncthreads();
-  trace_mark(trace, 11);
-  if (act && wp == 0) {
-    // The token's top-k among its wpt * k candidates (at most 16 * 16).
-    const int nc = wpt * k;
-    uint32_t c[8];
-    lb = 0;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int q = lane + 32 * j;
-      c[j] = q < nc ? s_cand[t * wpt * k + q] : 0u;
-      lb = max(lb, c[j]);
+    for (int w = 1; w < PERW; w *= 2)
+#pragma unroll
+      for (int i = 0; i + w < PERW; i += 2 * w) sd[i] += sd[i + w];
+    double st = sd[0];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) st += __shfl_xor_sync(0xffffffffu, st, o);
+    trace_mark(trace, 10);
+    const float inv = __frcp_rn((float)st);
+    uint32_t key[PERW], lb = 0;
+#pragma unroll
+    for (int i = 0; i < PERW; ++i) {
+      const int idx = lane + 32 * i;
+      key[i] = idx < E ? ((uint32_t)f2bf(__fmul_rn(v[i], inv)) << 16) | (0xFFFFu - idx) : 0u;
+      lb = max(lb, key[i]);
     }
+    // k extractions in descending key order; the selected probabilities are
+    // summed in that order for the renormalisation
     double ssum = 0.0;
     uint32_t sel = 0;
     for (int r = 0; r < k; ++r) {
       const uint32_t best = __reduce_max_sync(0xffffffffu, lb);
-      if (lb == best) {
+      if (lb == best && best != 0u) {
         lb = 0;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (c[j] == best) c[j] = 0u;
-          lb = max(lb, c[j]);
+        for (int i = 0; i < PERW; ++i) {
+          if (key[i] == best) key[i] = 0u;
+          lb = max(lb, key[i]);
         }
       }
       if (lane == r) sel = best;
       ssum += (double)bf2f(best >> 16);
     }
+    trace_mark(trace, 11);
     const float sel_p = bf2f(sel >> 16);
     float score = sel_p;
     if (norm_topk) {
@@ -936,25 +899,18 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
     int *s_rslot = s_rex + KL_MAX_ROUTES;
     float *s_rscore = reinterpret_cast<float *>(s_rslot + KL_MAX_ROUTES);
     int *s_rent = reinterpret_cast<int *>(s_rscore + KL_MAX_ROUTES);
-    uint32_t *s_wmax = reinterpret_cast<uint32_t *>(rings + Tl::TMP_WMAX);
-    double *s_wsum = reinterpret_cast<double *>(rings + Tl::TMP_WSUM);
-    uint32_t *s_cand = reinterpret_cast<uint32_t *>(rings + Tl::TMP_CAND);
     const float *lg = wsp<const float>(p, p.L.logits);
     const bool primary = blockIdx.x == 0;
-    const int tp = T <= 1 ? 1 : T <= 2 ? 2 : T <= 4 ? 4 : 8;
-    const int wpt = KL_WARPS / tp;
-    const int need = (E + wpt * 32 - 1) / (wpt * 32);  // logits per lane
+    const int need = (E + 31) / 32;  // logits per lane (one warp per token)
     int n;
 #define VB_ROUTE(PERW)                                                                         \
-  route_tokens<PERW>(lg, p.table, T, E, p.k, wpt, p.norm_topk, p.has_shared, p.pool.cap,       \
-                     primary, p.status, p.out_inds, p.out_scores, p.out_local, s_table,        \
-                     s_first, s_rex, s_rslot, s_rscore, s_rent, s_ok, s_ent, s_wcnt, s_wmax,   \
-                     s_wsum, s_cand, p.trace)
-    if (need <= 1) n = VB_ROUTE(1);
-    else if (need <= 2) n = VB_ROUTE(2);
-    else if (need <= 4) n = VB_ROUTE(4);
+  route_tokens<PERW>(lg, p.table, T, E, p.k, p.norm_topk, p.has_shared, p.pool.cap, primary,  \
+                     p.status, p.out_inds, p.out_scores, p.out_local, s_table, s_first, s_rex, \
+                     s_rslot, s_rscore, s_rent, s_ok, s_ent, s_wcnt, p.trace)
+    if (need <= 4) n = VB_ROUTE(4);
     else if (need <= 8) n = VB_ROUTE(8);
-    else n = VB_ROUTE(16);
+    else if (need <= 16) n = VB_ROUTE(16);
+    else n = VB_ROUTE(32);
 #undef VB_ROUTE
     if (tid == 0) s_misc[0] = n;
   }

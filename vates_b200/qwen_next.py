@@ -317,10 +317,20 @@ class QwenNextModel:
         self.buf["prev_h"].zero_()
 
     # ------------------------------------------------------------------ layers
-    def _gdn(self, m: GdnLayer, lay: DecoderLayer, x, h, T, st):
+    def _gdn(self, m: GdnLayer, lay: DecoderLayer, x, h, T, st, fused: bool = True):
         cfg, b = self.cfg, self.buf
         state = b["state"]
         m.in_proj(x, b["proj"], T, norm_w=lay.input_norm, eps=cfg.eps, stream=st)
+        if fused:
+            check(lib.vb_gdn_fused(b["proj"].data_ptr(), cfg.gdn_proj, T, cfg.k_heads,
+                                   cfg.v_heads, cfg.head_k, cfg.head_v, m.conv_buf.data_ptr(),
+                                   self.max_t, _i32(state, SP_ACC), m.conv_w.data_ptr(),
+                                   m.a_log.data_ptr(), m.dt_bias.data_ptr(), m.states.data_ptr(),
+                                   self.max_t, _i32(state, SP_SLOT), m.norm_w.data_ptr(), cfg.eps,
+                                   b["gout"].data_ptr(), b["status"].data_ptr(),
+                                   stream_handle(st)), "vb_gdn_fused")
+            m.out_proj(b["gout"], h, T, residual=x, stream=st)
+            return
         check(lib.vb_gdn_prepare(b["proj"].data_ptr(), cfg.gdn_proj, T, cfg.k_heads, cfg.v_heads,
                                  cfg.head_k, cfg.head_v, m.conv_buf.data_ptr(), self.max_t,
                                  _i32(state, SP_ACC), m.conv_w.data_ptr(), m.a_log.data_ptr(),
