@@ -950,7 +950,7 @@ __global__ void pf_unsort_kernel(const uint16_t *__restrict__ ys, int H, int n,
 // P7: combine. One warp per token; routes are ordered by (group of the
 // expert, route rank); lanes own 8 columns at a time.
 // ----------------------------------------------------------------------------
-__global__ void pf_combine_kernel(const uint16_t *__restrict__ y, int T, int H, int k,
+__global__ void __launch_bounds__(256, 4) pf_combine_kernel(const uint16_t *__restrict__ y, int T, int H, int k,
                                   const int32_t *__restrict__ inds,
                                   const int32_t *__restrict__ group_of,
                                   const int32_t *__restrict__ route_row,
@@ -990,17 +990,28 @@ __global__ void pf_combine_kernel(const uint16_t *__restrict__ y, int T, int H, 
     float acc[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-    for (int j = 0; j < n; ++j) {
-      const uint4 v = *reinterpret_cast<const uint4 *>(y + (size_t)order[j] * H + c);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    // the chunk's route rows four at a time in flight, added in the
+    // canonical order
+    uint4 sv = make_uint4(0, 0, 0, 0);
+    if (has_shared) sv = ldg_nc_v4(shr + c);
+    for (int j0 = 0; j0 < n; j0 += 4) {
+      uint4 rv[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        acc[2 * i] = rbf(acc[2 * i] + bf2f(w[i] & 0xFFFF));
-        acc[2 * i + 1] = rbf(acc[2 * i + 1] + bf2f(w[i] >> 16));
+      for (int q = 0; q < 4; ++q)
+        if (j0 + q < n) rv[q] = ldg_nc_v4(y + (size_t)order[j0 + q] * H + c);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (j0 + q >= n) break;
+        const uint32_t w[4] = {rv[q].x, rv[q].y, rv[q].z, rv[q].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc[2 * i] = rbf(acc[2 * i] + bf2f(w[i] & 0xFFFF));
+          acc[2 * i + 1] = rbf(acc[2 * i + 1] + bf2f(w[i] >> 16));
+        }
       }
     }
     if (has_shared) {
-      const uint4 v = *reinterpret_cast<const uint4 *>(shr + c);
+      const uint4 v = sv;
       const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
