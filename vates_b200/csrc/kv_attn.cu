@@ -64,16 +64,18 @@ __global__ void __launch_bounds__(256) kv_attn_combine_kernel(AttnParams p) {
   const size_t bh = (size_t)b * p.Hkv + hkv;
   const int tid = threadIdx.x;
   const int ns = p.nsplit;
+  // maximum and denominator: per-thread partials, warp shuffles, then the 8
+  // warp values in warp order (one block barrier each)
+  const int wid = tid >> 5;
   float m = -INFINITY;
   for (int s = tid; s < ns; s += 256) m = fmaxf(m, p.mpart[(bh * ns + s) * 32 + r]);
-  s_red[tid] = m;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((tid & 31) == 0) s_red[wid] = m;
   __syncthreads();
-  for (int o = 128; o > 0; o >>= 1) {
-    if (tid < o) s_red[tid] = fmaxf(s_red[tid], s_red[tid + o]);
-    __syncthreads();
-  }
-  const float M = s_red[0];
-  __syncthreads();
+  float M = s_red[0];
+#pragma unroll
+  for (int w = 1; w < 8; ++w) M = fmaxf(M, s_red[w]);
   float dn = 0.f;
   for (int s = tid; s < ns; s += 256) {
     const size_t cta = bh * ns + s;
@@ -82,13 +84,13 @@ __global__ void __launch_bounds__(256) kv_attn_combine_kernel(AttnParams p) {
     s_e[s] = e;
     dn = fmaf(p.lpart[cta * 32 + r], e, dn);
   }
-  s_red[tid] = dn;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) dn += __shfl_xor_sync(0xffffffffu, dn, o);
+  if ((tid & 31) == 0) s_red[8 + wid] = dn;
   __syncthreads();
-  for (int o = 128; o > 0; o >>= 1) {
-    if (tid < o) s_red[tid] += s_red[tid + o];
-    __syncthreads();
-  }
-  const float den = s_red[0];
+  float den = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) den += s_red[8 + w];
   const int dl = tid & 31, sl = tid >> 5;
   const int d = 32 * chunk + dl;
   float num = 0.f;
