@@ -155,18 +155,21 @@ __global__ void __launch_bounds__(GF_THREADS) gdn_fused_kernel(GdnFusedParams p)
     const int w0 = kind * (Dk / 32), nw = Dk / 32;
     const float k_scale = rbf(rsqrtf((float)Dk));
     const float q_scale = rbf(1.f / (float)Dk);
-    for (int t = 0; t < T; ++t) {
-      float tot = 0.f;
-      for (int w = 0; w < nw; ++w) tot += red[t][w0 + w];
-      const float inv = rsqrtf(tot / (float)Dk + 1e-6f);
-      const float nv = rbf(y[t] * inv);
-      if (kind == 0)
-        s_q[t][d] = rbf(nv * q_scale);
-      else
-        s_k[t][d] = rbf(nv * k_scale);
+    // (loops over the fixed row bound, so y and yv stay in registers)
+#pragma unroll
+    for (int t = 0; t < GF_T; ++t) {
+      if (t < T) {
+        float tot = 0.f;
+        for (int w = 0; w < nw; ++w) tot += red[t][w0 + w];
+        const float inv = rsqrtf(tot / (float)Dk + 1e-6f);
+        const float nv = rbf(y[t] * inv);
+        if (kind == 0)
+          s_q[t][d] = rbf(nv * q_scale);
+        else
+          s_k[t][d] = rbf(nv * k_scale);
+        if (has_v) s_v[t][tid] = yv[t];
+      }
     }
-    if (has_v)
-      for (int t = 0; t < T; ++t) s_v[t][tid] = yv[t];
   }
   // 4. every CTA has read the window: move it (owners only)
   cluster.sync();

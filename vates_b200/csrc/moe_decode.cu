@@ -17,10 +17,10 @@
 //     bf16(x.Wr^T [+bias]) and the gate sigmoid(x.w_sg), written to global
 //     memory.
 //  3. Grid barrier (bounded wait). Every CTA then runs the same precise
-//     softmax, top-k, renormalisation and slot gather (16/T warps per token:
-//     each takes the top-k candidates of its share of the logits on
-//     (bf16 probability, expert id) keys, lower id wins ties, and the token's
-//     first warp picks among them), and builds the same list of "entries" in
+//     softmax, top-k, renormalisation and slot gather (one warp per token,
+//     E/32 logits per lane in registers: maximum, exponential sum in double,
+//     then k extractions of the largest (bf16 probability, expert id) key,
+//     lower id winning ties), and builds the same list of "entries" in
 //     shared memory: the shared expert first, then every distinct routed
 //     expert in route order.
 //  4. Gate/up: each CTA owns a contiguous range of items (entry, 16
@@ -358,22 +358,26 @@ struct LayerTile {
   static_assert(KP % 2 == 0, "a chunk's scale word starts at an even group");
 };
 
+// The item's row block: gate and up codes, and the two scale tensors this
+// lane loads scale words from (lanes 0-15: gate s and up s; lanes 16-31:
+// gate b and up b). Only fixed fields, so the item stays in registers (a
+// table of four scale pointers indexed by lane would live in local memory,
+// and every chunk issue would wait for a local load first).
 struct GateUpItem {
-  const uint8_t *gw, *uw;  // row block start of the gate and up codes
-  const uint8_t *sc[4];    // row block start of gate s, gate b, up s, up b
+  const uint8_t *gw, *uw;
+  const uint8_t *sg, *su;
 };
 
 template <int H, int I>
 __device__ __forceinline__ void gateup_item(const VbQuantPool &pool, int slot, int rb, int gs,
-                                            GateUpItem &it) {
+                                            int lane, GateUpItem &it) {
   using Tl = LayerTile<H, I>;
   const size_t sb = (size_t)rb * 16 * (Tl::NS64 >> gs) * 2;
+  const bool bias = lane >= 16;
   it.gw = pool_ptr(pool, 0, slot) + (size_t)rb * 16 * Tl::ROWB;
   it.uw = pool_ptr(pool, 3, slot) + (size_t)rb * 16 * Tl::ROWB;
-  it.sc[0] = pool_ptr(pool, 1, slot) + sb;
-  it.sc[1] = pool_ptr(pool, 2, slot) + sb;
-  it.sc[2] = pool_ptr(pool, 4, slot) + sb;
-  it.sc[3] = pool_ptr(pool, 5, slot) + sb;
+  it.sg = pool_ptr(pool, bias ? 2 : 1, slot) + sb;
+  it.su = pool_ptr(pool, bias ? 5 : 4, slot) + sb;
 }
 
 // First scale of the groups [g0, g0 + CG) of a gate/up chunk, rounded down
@@ -398,13 +402,12 @@ __device__ __forceinline__ void gateup_chunk(uint8_t *stage, const GateUpItem &i
     cp_async16(d, it.gw + (size_t)r * Tl::ROWB + cb);
     cp_async16(d + 16 * Tl::CROW, it.uw + (size_t)r * Tl::ROWB + cb);
   }
-  // Scale words: 4 tensors x 16 rows, two per lane.
-  const int ns = Tl::NS64 >> gs, w0 = gu_scale_word(g0, gs);
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    const int piece = lane + 32 * k, a = piece >> 4, r = piece & 15;
-    cp_async4(stage + Tl::WB + piece * 4, it.sc[a] + ((size_t)r * ns + w0) * 2);
-  }
+  // Scale words: 4 tensors (gate s, gate b, up s, up b) x 16 rows, two per
+  // lane: piece lane + 32 k is tensor (lane >> 4) + 2 k, row lane & 15.
+  const int ns = Tl::NS64 >> gs, w0 = gu_scale_word(g0, gs), r = lane & 15;
+  const size_t so = ((size_t)r * ns + w0) * 2;
+  cp_async4(stage + Tl::WB + lane * 4, it.sg + so);
+  cp_async4(stage + Tl::WB + (lane + 32) * 4, it.su + so);
 }
 
 // Chunk dc of down item (slot, 16-row block rb) into a ring stage:
@@ -956,8 +959,8 @@ __global__ void __launch_bounds__(KL_THREADS, 1) moe_layer_kernel(DecodeParams p
       const int i = a0 + grp + GU_NGRP * r;
       if (ch == 0) {
         const int e = i / RB;
-        if (p.has_shared && e == 0) gateup_item<H, I>(p.shared, 0, i % RB, gs, cur);
-        else gateup_item<H, I>(p.pool, s_ent[e].slot, i % RB, gs, cur);
+        if (p.has_shared && e == 0) gateup_item<H, I>(p.shared, 0, i % RB, gs, lane, cur);
+        else gateup_item<H, I>(p.pool, s_ent[e].slot, i % RB, gs, lane, cur);
       }
       gateup_chunk<H, I>(stage, cur, wi * KP + ch * CG, lane, gs);
     } else if (issue_q < nq) {

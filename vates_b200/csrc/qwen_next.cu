@@ -117,7 +117,9 @@ __global__ void __launch_bounds__(1024) gdn_prepare_kernel(GdnPrepParams p) {
     const int w0 = kind * (p.Dk / 32), nw = p.Dk / 32;
     const float k_scale = rbf(rsqrtf((float)p.Dk));           // bf16(Dk^-0.5)
     const float q_scale = rbf(1.f / (float)p.Dk);              // bf16(Dk^-1)
-    for (int t = 0; t < T; ++t) {
+#pragma unroll
+    for (int t = 0; t < QN_MAX_T; ++t) {
+      if (t >= T) break;
       float tot = 0.f;
       for (int w = 0; w < nw; ++w) tot += red[t][w0 + w];
       const float inv = rsqrtf(tot / (float)p.Dk + 1e-6f);
@@ -130,7 +132,9 @@ __global__ void __launch_bounds__(1024) gdn_prepare_kernel(GdnPrepParams p) {
     }
   } else {
     const int j = d / p.Dv, dd = d % p.Dv, hv = hk * r + j;
-    for (int t = 0; t < T; ++t) p.v[((size_t)t * p.Hv + hv) * p.Dv + dd] = f2bf(y[t]);
+#pragma unroll
+    for (int t = 0; t < QN_MAX_T; ++t)
+      if (t < T) p.v[((size_t)t * p.Hv + hv) * p.Dv + dd] = f2bf(y[t]);
   }
   if (tid < r * T) {
     const int t = tid / r, j = tid % r, hv = hk * r + j;
