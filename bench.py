@@ -64,12 +64,32 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200", "-i", str(self.index)],
+                 "-lms", "100", "-i", str(self.index)],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
-        time.sleep(0.3)
+        # wait (up to 5 s) for the first sample, which is taken before the
+        # load starts and is dropped from the summary
+        t0 = time.time()
+        while self.proc is not None and time.time() - t0 < 5.0:
+            try:
+                if os.path.getsize(self.path) > 0:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.05)
         return self
+
+    @staticmethod
+    def keep_busy(fn, seconds: float):
+        """Replay `fn` (untimed) for about `seconds` of device time, so that
+        the samples around a short timed region are taken under the same load."""
+        import torch
+        t0 = time.time()
+        while time.time() - t0 < seconds:
+            for _ in range(8):
+                fn()
+            torch.cuda.synchronize()
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -91,6 +111,7 @@ class ClockSampler:
         finally:
             if self.path and os.path.exists(self.path):
                 os.unlink(self.path)
+        rows = rows[1:]  # the first sample precedes the load
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         sm = [float(r[1]) for r in rows]
@@ -775,7 +796,11 @@ def run_decode(args, world, rank, local):
 
     # ---- timed region: K graph replays (device time, max over ranks) ----
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # The sampler runs from 0.5 s of untimed replays before the timed region
+    # to 0.5 s after it: nvidia-smi samples every 100 ms, and the timed
+    # region alone is shorter than that.
     with ClockSampler(local) as clk:
+        ClockSampler.keep_busy(graph.replay, 0.5)
         barrier(world)
         torch.cuda.synchronize()
         ev0.record()
@@ -784,6 +809,7 @@ def run_decode(args, world, rank, local):
         ev1.record()
         torch.cuda.synchronize()
         barrier(world)
+        ClockSampler.keep_busy(graph.replay, 0.5)
     ms = ev0.elapsed_time(ev1) / args.steps
     ms = max_over_ranks(ms, world)
     clocks = clk.summary()

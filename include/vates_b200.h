@@ -657,9 +657,10 @@ int vb_dequantize(const uint32_t *words, const uint16_t *scales,
  * (per group s * sum(x q) + b * sum(x), float32, one bf16 rounding; the
  * residual add is a second bf16 rounding, h = x + r of the decoder layer).
  * x' = x, or rms_norm(x) * norm_w (bf16 at each op) when norm_w != NULL.
- * T <= 8, in_features a multiple of 256, bits 4, group 64. The workspace
- * (vb_qlinear_workspace_size, zero-filled once, reusable) holds the split-K
- * partials and per-row-block tickets. */
+ * T <= 8, in_features a multiple of 256 (of 512 above 2048, at most 4096),
+ * bits 4, group 64; x, scales, biases and norm_w 16-byte aligned, codes 8. No
+ * workspace is needed (vb_qlinear_workspace_size returns 0; the K reduction
+ * stays inside a CTA). */
 size_t vb_qlinear_workspace_size(int32_t tokens, int32_t in_features, int32_t out_features);
 int vb_qlinear(const uint16_t *x, int32_t tokens, int32_t in_features,
                const uint32_t *codes, const uint16_t *scales, const uint16_t *biases,

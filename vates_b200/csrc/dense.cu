@@ -443,16 +443,14 @@ int vb_qlinear(const uint16_t *x, int32_t tokens, int32_t in_features,
   p.items = (out_features + 15) / 16;
   const int G = in_features / 64;   // groups; eight warps share them
   const cudaStream_t s = as_stream(stream);
-  cudaError_t e;
   if (G <= 8)
-    e = ql_launch<1>(p, s);
+    ql_launch<1>(p, s);
   else if (G <= 16)
-    e = ql_launch<2>(p, s);
+    ql_launch<2>(p, s);
   else if (G <= 32)
-    e = ql_launch<4>(p, s);
+    ql_launch<4>(p, s);
   else
-    e = ql_launch<8>(p, s);
-  (void)e;
+    ql_launch<8>(p, s);
   return check_launch("qlinear_kernel");
 }
 
