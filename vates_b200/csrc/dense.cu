@@ -161,6 +161,7 @@ __global__ void __launch_bounds__(QL_THREADS, 2) qlinear_kernel(QlParams p) {
     for (int t = warp; t < T; t += QL_THREADS / 32) {
       const uint16_t *xr = p.x + (size_t)t * K;
       float ss = 0.f;
+#pragma unroll 4
       for (int k = lane * 8; k < K; k += 256) {
         const uint4 v = *reinterpret_cast<const uint4 *>(xr + k);
         const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
@@ -184,42 +185,58 @@ __global__ void __launch_bounds__(QL_THREADS, 2) qlinear_kernel(QlParams p) {
   // its A pairs are nibbles (2h, 2h+4) and (2h+1, 2h+5), so b0 = x[n][kb+2h],
   // x[n][kb+2h+4] and b1 = x[n][kb+2h+1], x[n][kb+2h+5] with w = 2c + jw.
   // The 8 words of (n, grp) are 8 consecutive lanes: their sum by shuffles
-  // (fixed order) is the group sum.
-  for (int i = tid; i < QL_MAX_T * G * 8; i += QL_THREADS) {
-    const int w = i & 7, grp = (i >> 3) % G, n = (i >> 3) / G;
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (n < T) {
-      const int k8 = grp * 64 + w * 8;
-      const uint4 raw = *reinterpret_cast<const uint4 *>(p.x + (size_t)n * K + k8);
-      const uint32_t xv[4] = {raw.x, raw.y, raw.z, raw.w};
+  // (fixed order) is the group sum. Only rows n < T are staged (the MMA
+  // columns of rows past T are never stored), and each thread issues the
+  // loads of four work items before it uses the first, so a CTA waits for
+  // x about once instead of once per work item.
+  {
+    const int total = T * G * 8;  // a multiple of 32: the bounds below are warp-uniform
+    for (int i0 = 0; i0 < total; i0 += 4 * QL_THREADS) {
+      uint4 raw[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        v[2 * q] = __uint_as_float(xv[q] << 16);
-        v[2 * q + 1] = __uint_as_float(xv[q] & 0xFFFF0000u);
-      }
-      if (p.norm_w) {
-        const uint4 wr = *reinterpret_cast<const uint4 *>(p.norm_w + k8);
-        const uint32_t wv[4] = {wr.x, wr.y, wr.z, wr.w};
-        const float inv = inv_rms[n];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          v[2 * q] = rbf(rbf(v[2 * q] * inv) * __uint_as_float(wv[q] << 16));
-          v[2 * q + 1] = rbf(rbf(v[2 * q + 1] * inv) * __uint_as_float(wv[q] & 0xFFFF0000u));
+      for (int b = 0; b < 4; ++b) {
+        const int i = i0 + b * QL_THREADS + tid;
+        if (i < total) {
+          const int w = i & 7, grp = (i >> 3) % G, n = (i >> 3) / G;
+          raw[b] = *reinterpret_cast<const uint4 *>(p.x + (size_t)n * K + grp * 64 + w * 8);
         }
       }
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int i = i0 + b * QL_THREADS + tid;
+        if (i >= total) break;
+        const int w = i & 7, grp = (i >> 3) % G, n = (i >> 3) / G;
+        const uint32_t xv[4] = {raw[b].x, raw[b].y, raw[b].z, raw[b].w};
+        float v[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          v[2 * q] = __uint_as_float(xv[q] << 16);
+          v[2 * q + 1] = __uint_as_float(xv[q] & 0xFFFF0000u);
+        }
+        if (p.norm_w) {
+          const uint4 wr = *reinterpret_cast<const uint4 *>(p.norm_w + grp * 64 + w * 8);
+          const uint32_t wv[4] = {wr.x, wr.y, wr.z, wr.w};
+          const float inv = inv_rms[n];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            v[2 * q] = rbf(rbf(v[2 * q] * inv) * __uint_as_float(wv[q] << 16));
+            v[2 * q + 1] = rbf(rbf(v[2 * q + 1] * inv) * __uint_as_float(wv[q] & 0xFFFF0000u));
+          }
+        }
+        const int cc = w >> 1, jw = w & 1, l = n * 4 + cc;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+          xfrag[(grp * 4 + 2 * jw + h) * 32 + l] =
+              make_uint2(pack_bf2(v[2 * h], v[2 * h + 4]), pack_bf2(v[2 * h + 1], v[2 * h + 5]));
+        float sum = 0.f;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) sum += v[q];
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        if (w == 0) xsum[grp * QL_MAX_T + n] = sum;
+      }
     }
-    const int cc = w >> 1, jw = w & 1, l = n * 4 + cc;
-#pragma unroll
-    for (int h = 0; h < 2; ++h)
-      xfrag[(grp * 4 + 2 * jw + h) * 32 + l] =
-          make_uint2(pack_bf2(v[2 * h], v[2 * h + 4]), pack_bf2(v[2 * h + 1], v[2 * h + 5]));
-    float sum = 0.f;
-#pragma unroll
-    for (int q = 0; q < 8; ++q) sum += v[q];
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
-    if (w == 0) xsum[grp * QL_MAX_T + n] = sum;
   }
   __syncthreads();
 
