@@ -939,6 +939,19 @@ def run_decode(args, world, rank, local):
     return 0
 
 
+def _fresh_stack(layers: int):
+    """The headline decode stack (fresh seeded inputs per layer, T = 4)."""
+    from vates_b200.synth import DecodeStack
+    st = DecodeStack(seed=1, layers=layers, cap=192, T=4, fresh=True)
+    st.ensure_resident()
+    return st
+
+
+def torch_stream():
+    import torch
+    return torch.cuda.Stream()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -953,7 +966,7 @@ def main():
                     help="skip the prefill (config 2) and IsoQuant (config 3) legs")
     ap.add_argument("--leg", default=None,
                     choices=["prefill", "isoquant", "prefill_attention", "residency",
-                             "full_stack"],
+                             "full_stack", "decode_t1"],
                     help="run only this extra leg on one GPU and print its result (for profiling)")
     ap.add_argument("--iso-layers", type=int, default=12)
     args = ap.parse_args()
@@ -964,7 +977,9 @@ def main():
                                                      layers=args.iso_layers),
                 "prefill_attention": lambda: run_prefill_attention_leg(args.steps, args.warmup),
                 "residency": lambda: run_residency_leg(),
-                "full_stack": lambda: run_full_stack_leg()}
+                "full_stack": lambda: run_full_stack_leg(),
+                "decode_t1": lambda: run_decode_t1_leg(
+                    _fresh_stack(args.layers), torch_stream(), args.steps, args.warmup)}
         print(json.dumps({args.leg: legs[args.leg]()}), flush=True)
         return 0
     try:

@@ -743,6 +743,25 @@ int vb_attn_prepare(const uint16_t *proj, int32_t proj_stride, int32_t tokens, i
                     uint16_t *q_out, uint16_t *k_out, uint16_t *v_out, int32_t kv_cap,
                     int32_t *status, vb_stream_t stream);
 
+/* vb_attn_prepare with the IsoQuant cache append fused in (kv_quant_patch.py
+ * :29-56 and AsymmetricQuantizedKVCache.update_and_fetch, quant_kv.py:
+ * 105-137): queries as in vb_attn_prepare (RoPE at *pos + t, rotated by
+ * rk_blocks) into q_out [Hq, T, 256]; keys (after their norm and RoPE) rotated
+ * by rk_blocks and values by rv_blocks, quantized (group 64, k_bits / v_bits)
+ * and packed into the caches [Hkv, cap, ...] at position *pos + t: the same
+ * bits as vb_attn_prepare to bf16 rows followed by vb_kv_quant_append_at of
+ * each, in one launch. A position outside [0, cap) sets VB_STATUS_BOUNDS and
+ * stores nothing for that row. */
+int vb_attn_prepare_quant(const uint16_t *proj, int32_t proj_stride, int32_t tokens,
+                          int32_t q_heads, int32_t kv_heads, int32_t head_dim,
+                          const uint16_t *q_norm_w, const uint16_t *k_norm_w, float eps,
+                          int32_t rope_dims, float rope_base, const int32_t *pos,
+                          const float *rk_blocks, const float *rv_blocks, uint16_t *q_out,
+                          int32_t cap, int32_t k_bits, uint32_t *k_codes, uint16_t *k_scales,
+                          uint16_t *k_biases, int32_t v_bits, uint32_t *v_codes,
+                          uint16_t *v_scales, uint16_t *v_biases, int32_t *status,
+                          vb_stream_t stream);
+
 /* output * sigmoid(gate) (kv_quant_patch.py:70-71): attn_out bf16 [Hq, T, 256]
  * -> out bf16 [T, Hq * 256], gate read from the projection rows. */
 int vb_attn_gate(const uint16_t *attn_out, const uint16_t *proj, int32_t proj_stride,

@@ -192,6 +192,41 @@ def test_gdn_fused_equals_three_kernels(tiny):
     _gdn_fused_vs_split(model, model.layers[0], ((4, None), (3, 2), (1, 3)), 7)
 
 
+def test_attn_prepare_quant_equals_unfused(tiny):
+    """The input side with the IsoQuant append fused in (one launch) = bf16
+    rows then two vb_kv_quant_append_at, bit for bit: queries, the K4/V3
+    cache rows at positions 5..8 and 9..10, and the attention layer's
+    output."""
+    import torch
+    from vates_b200.qwen_next import AttnLayer, SP_POS
+    model, _ = tiny
+    model.reset()
+    b, cfg = model.buf, model.cfg
+    lay = next(l for l in model.layers if isinstance(l.mixer, AttnLayer))
+    m = lay.mixer
+    rng = np.random.default_rng(11)
+    pos_ptr = b["state"].data_ptr() + 4 * SP_POS
+    for T, pos in ((4, 5), (2, 9)):
+        b["state"][SP_POS] = pos
+        b["x0"][:T] = _bf(rng.standard_normal((T, cfg.hidden)).astype(np.float32))
+        cache0 = {k: v.clone() for k, v in m.cache.items()}
+        outs = []
+        for fused in (False, True):
+            for k, v in cache0.items():
+                m.cache[k].copy_(v)
+            model.fused_append = fused
+            model._attn(m, lay, b["x0"], b["h"], T, None, pos_ptr)
+            torch.cuda.synchronize()
+            outs.append((b["h"][:T].clone(), b["q"].clone(),
+                         {k: v.clone() for k, v in m.cache.items()}))
+        model.fused_append = True
+        assert int(b["status"][0].item()) == 0
+        assert torch.equal(outs[0][0], outs[1][0]), f"layer output T={T}"
+        assert torch.equal(outs[0][1], outs[1][1]), f"queries T={T}"
+        for k in ("kc", "ks", "kb", "vc", "vs", "vb"):
+            assert torch.equal(outs[0][2][k], outs[1][2][k]), f"cache {k} T={T}"
+
+
 def test_forward_logits_vs_oracle(tiny):
     """Embeddings -> 4 layers -> final norm + lm_head -> argmax, two chunks,
     free-running. Each block matches on identical inputs (test above); over a

@@ -184,6 +184,9 @@ _SIGNATURES = {
                                  _P]),
     "vb_attn_prepare": (_I32, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, C.c_float, _I32,
                                C.c_float, _P, _I32, _P, _P, _P, _P, _I32, _P, _P]),
+    "vb_attn_prepare_quant": (_I32, [_P, _I32, _I32, _I32, _I32, _I32, _P, _P, C.c_float,
+                                     _I32, C.c_float, _P, _P, _P, _P, _I32, _I32, _P, _P, _P,
+                                     _I32, _P, _P, _P, _P, _P]),
     "vb_attn_gate": (_I32, [_P, _P, _I32, _I32, _I32, _P, _P]),
     "vb_spec_accept": (_I32, [_P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _I32, _P]),
     "vb_spec_sync_inputs": (_I32, [_P, _P, _P, _P, _I32, _I32, _P, _P, _P]),

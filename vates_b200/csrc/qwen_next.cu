@@ -22,7 +22,7 @@
 //   drafter.py:178-186 (MTP cache sync over the accepted pairs).
 // Every sequence position (cache offset, accepted count) is read from device
 // memory, so a whole decode / verify step is one CUDA graph.
-#include "common.cuh"
+#include "kv_quant.cuh"
 
 namespace vb {
 
@@ -197,6 +197,12 @@ struct AttnPrepParams {
   uint16_t *q_out, *k_out, *v_out;
   int kv_cap;
   int32_t *status;
+  // Quantized caches (kc non-null): keys and values are rotated by rk / rv
+  // and quantized straight into [Hkv, qcap, ...] at their positions.
+  const float *rv;
+  uint32_t *kc, *vc;
+  uint16_t *ks, *kb, *vs, *vb;
+  int kbits, vbits, qcap;
 };
 
 __global__ void __launch_bounds__(256) attn_prepare_kernel(AttnPrepParams p) {
@@ -255,6 +261,21 @@ __global__ void __launch_bounds__(256) attn_prepare_kernel(AttnPrepParams p) {
       }
     }
     if (kind == 0 && p.rk) rotate8(v, p.rk, lane * 2, false);
+  }
+  if (kind != 0 && p.kc) {
+    // IsoQuant append of this key / value row: the bf16 row the unfused path
+    // would write (v holds bf16 values), SO(4)-rotated, quantized and packed
+    // exactly as vb_kv_quant_append_at does with it.
+    const int at = p0 + t;
+    if (at < 0 || at >= p.qcap) {
+      if (lane == 0) flag_status(p.status, VB_STATUS_BOUNDS);
+      return;
+    }
+    const bool key = kind == 1;
+    rotate8(v, key ? p.rk : p.rv, lane * 2, false);
+    kv_quant_store<32>(v, lane, 0, key ? p.kbits : p.vbits, true, (int64_t)hh * p.qcap + at,
+                       key ? p.kc : p.vc, key ? p.ks : p.vs, key ? p.kb : p.vb);
+    return;
   }
   uint4 o;
   o.x = pack_bf2(v[0], v[1]);
@@ -450,11 +471,47 @@ int vb_attn_prepare(const uint16_t *proj, int32_t proj_stride, int32_t tokens, i
   VB_REQUIRE(proj && q_norm_w && k_norm_w && q_out && k_out && v_out && eps > 0.f &&
                  rope_base > 1.f,
              "vb_attn_prepare: bad arguments");
-  AttnPrepParams p;
+  AttnPrepParams p = {};
   p.proj = proj; p.stride = proj_stride; p.T = tokens; p.Hq = q_heads; p.Hkv = kv_heads;
   p.qw = q_norm_w; p.kw = k_norm_w; p.eps = eps; p.rope_dims = rope_dims;
   p.rope_log2_base = log2f(rope_base); p.pos = pos; p.pos_add = pos_add; p.rk = rk_blocks;
   p.q_out = q_out; p.k_out = k_out; p.v_out = v_out; p.kv_cap = kv_cap; p.status = status;
+  const int warps = tokens * (q_heads + 2 * kv_heads);
+  vb_launch(attn_prepare_kernel, dim3((warps + 7) / 8), dim3(256), 0, as_stream(stream), false, p);
+  return check_launch("attn_prepare_kernel");
+}
+
+int vb_attn_prepare_quant(const uint16_t *proj, int32_t proj_stride, int32_t tokens,
+                          int32_t q_heads, int32_t kv_heads, int32_t head_dim,
+                          const uint16_t *q_norm_w, const uint16_t *k_norm_w, float eps,
+                          int32_t rope_dims, float rope_base, const int32_t *pos,
+                          const float *rk_blocks, const float *rv_blocks, uint16_t *q_out,
+                          int32_t cap, int32_t k_bits, uint32_t *k_codes, uint16_t *k_scales,
+                          uint16_t *k_biases, int32_t v_bits, uint32_t *v_codes,
+                          uint16_t *v_scales, uint16_t *v_biases, int32_t *status,
+                          vb_stream_t stream) {
+  VB_REQUIRE(head_dim == 256, "vb_attn_prepare_quant: head_dim %d (256 only)", head_dim);
+  VB_REQUIRE(tokens >= 1 && q_heads >= 1 && kv_heads >= 1,
+             "vb_attn_prepare_quant: tokens=%d heads %d/%d", tokens, q_heads, kv_heads);
+  VB_REQUIRE(rope_dims >= 16 && rope_dims <= head_dim && rope_dims % 16 == 0 &&
+                 ((rope_dims / 16) & (rope_dims / 16 - 1)) == 0,
+             "vb_attn_prepare_quant: rope_dims %d (16 x a power of two)", rope_dims);
+  VB_REQUIRE(proj_stride % 8 == 0 && proj_stride >= q_heads * 512 + 2 * kv_heads * 256,
+             "vb_attn_prepare_quant: projection row of %d elements", proj_stride);
+  auto bits_ok = [](int b) { return b == 2 || b == 3 || b == 4 || b == 5 || b == 6 || b == 8; };
+  VB_REQUIRE(bits_ok(k_bits) && bits_ok(v_bits), "vb_attn_prepare_quant: bits %d/%d", k_bits,
+             v_bits);
+  VB_REQUIRE(proj && q_norm_w && k_norm_w && q_out && pos && rk_blocks && rv_blocks && k_codes &&
+                 k_scales && k_biases && v_codes && v_scales && v_biases && cap >= 1 &&
+                 eps > 0.f && rope_base > 1.f,
+             "vb_attn_prepare_quant: bad arguments");
+  AttnPrepParams p = {};
+  p.proj = proj; p.stride = proj_stride; p.T = tokens; p.Hq = q_heads; p.Hkv = kv_heads;
+  p.qw = q_norm_w; p.kw = k_norm_w; p.eps = eps; p.rope_dims = rope_dims;
+  p.rope_log2_base = log2f(rope_base); p.pos = pos; p.pos_add = 0; p.rk = rk_blocks;
+  p.q_out = q_out; p.kv_cap = 0; p.status = status;
+  p.rv = rv_blocks; p.kc = k_codes; p.ks = k_scales; p.kb = k_biases; p.vc = v_codes;
+  p.vs = v_scales; p.vb = v_biases; p.kbits = k_bits; p.vbits = v_bits; p.qcap = cap;
   const int warps = tokens * (q_heads + 2 * kv_heads);
   vb_launch(attn_prepare_kernel, dim3((warps + 7) / 8), dim3(256), 0, as_stream(stream), false, p);
   return check_launch("attn_prepare_kernel");

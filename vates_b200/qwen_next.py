@@ -251,6 +251,9 @@ class QwenNextModel:
         # IsoQuant rotations (kv_quant_patch.py:92-93)
         self.rk = so4_blocks(build_block_so4(cfg.head_dim, seed=0), device)
         self.rv = so4_blocks(build_block_so4(cfg.head_dim, seed=1), device)
+        # keys and values quantized into the caches by the input-side kernel
+        # (vb_attn_prepare_quant); False: bf16 rows, then two appends
+        self.fused_append = True
         self.out_cap = out_cap
         self._alloc_buffers()
         self.reset()
@@ -370,18 +373,32 @@ class QwenNextModel:
                   "vb_kv_bf16_attn_at")
         else:
             c = m.cache
-            check(lib.vb_attn_prepare(b["proj"].data_ptr(), cfg.attn_proj, T, cfg.q_heads,
-                                      cfg.kv_heads, D, m.q_norm.data_ptr(), m.k_norm.data_ptr(),
-                                      cfg.eps, cfg.rope_dims, cfg.rope_base, pos_ptr, 0,
-                                      self.rk.data_ptr(), b["q"].data_ptr(), b["krow"].data_ptr(),
-                                      b["vrow"].data_ptr(), 0, b["status"].data_ptr(),
-                                      stream_handle(st)), "vb_attn_prepare")
-            for src, rot, key, bits in ((b["krow"], self.rk, "k", 4), (b["vrow"], self.rv, "v", 3)):
-                check(lib.vb_kv_quant_append_at(src.data_ptr(), rot.data_ptr(), 1, cfg.kv_heads, T,
-                                                D, 64, bits, pos_ptr, self.cache_len,
-                                                c[key + "c"].data_ptr(), c[key + "s"].data_ptr(),
-                                                c[key + "b"].data_ptr(), b["status"].data_ptr(),
-                                                stream_handle(st)), "vb_kv_quant_append_at")
+            if self.fused_append:
+                check(lib.vb_attn_prepare_quant(
+                    b["proj"].data_ptr(), cfg.attn_proj, T, cfg.q_heads, cfg.kv_heads, D,
+                    m.q_norm.data_ptr(), m.k_norm.data_ptr(), cfg.eps, cfg.rope_dims,
+                    cfg.rope_base, pos_ptr, self.rk.data_ptr(), self.rv.data_ptr(),
+                    b["q"].data_ptr(), self.cache_len, 4, c["kc"].data_ptr(),
+                    c["ks"].data_ptr(), c["kb"].data_ptr(), 3, c["vc"].data_ptr(),
+                    c["vs"].data_ptr(), c["vb"].data_ptr(), b["status"].data_ptr(),
+                    stream_handle(st)), "vb_attn_prepare_quant")
+            else:
+                check(lib.vb_attn_prepare(b["proj"].data_ptr(), cfg.attn_proj, T, cfg.q_heads,
+                                          cfg.kv_heads, D, m.q_norm.data_ptr(),
+                                          m.k_norm.data_ptr(), cfg.eps, cfg.rope_dims,
+                                          cfg.rope_base, pos_ptr, 0, self.rk.data_ptr(),
+                                          b["q"].data_ptr(), b["krow"].data_ptr(),
+                                          b["vrow"].data_ptr(), 0, b["status"].data_ptr(),
+                                          stream_handle(st)), "vb_attn_prepare")
+                for src, rot, key, bits in ((b["krow"], self.rk, "k", 4),
+                                            (b["vrow"], self.rv, "v", 3)):
+                    check(lib.vb_kv_quant_append_at(src.data_ptr(), rot.data_ptr(), 1,
+                                                    cfg.kv_heads, T, D, 64, bits, pos_ptr,
+                                                    self.cache_len, c[key + "c"].data_ptr(),
+                                                    c[key + "s"].data_ptr(),
+                                                    c[key + "b"].data_ptr(),
+                                                    b["status"].data_ptr(), stream_handle(st)),
+                          "vb_kv_quant_append_at")
             check(lib.vb_kv_decode_attn_at(b["q"].data_ptr(), c["kc"].data_ptr(),
                                            c["ks"].data_ptr(), c["kb"].data_ptr(),
                                            c["vc"].data_ptr(), c["vs"].data_ptr(),
