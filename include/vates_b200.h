@@ -472,7 +472,12 @@ int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
 /* The same with the key count read on the device: keys = *pos + L (pos =
  * cache length before this step's L rows); keys_max (<= cap) sizes the split
  * grid, so one launch (and one CUDA graph node) serves every step. Used by the
- * decode stack, whose cache offset lives in device memory. */
+ * decode stack, whose cache offset lives in device memory. With gate_proj
+ * (batch 1) the output gate of the attention layer is applied in the same
+ * pass (kv_quant_patch.py:70-71, = vb_attn_gate): out bf16 [L, Hq * 256] =
+ * bf16(o * bf16(sigmoid(g))), g = gate_proj[l * gate_stride + hq * 512 + 256
+ * + d] (the gate half of each query head's projection); without it, out bf16
+ * [B, Hq, L, 256] = o. */
 int vb_kv_decode_attn_at(const uint16_t *q, const uint32_t *k_codes,
                          const uint16_t *k_scales, const uint16_t *k_biases,
                          const uint32_t *v_codes, const uint16_t *v_scales,
@@ -480,20 +485,23 @@ int vb_kv_decode_attn_at(const uint16_t *q, const uint32_t *k_codes,
                          int32_t batch, int32_t q_heads, int32_t kv_heads,
                          int32_t L, int32_t dim, const int32_t *pos, int32_t keys_max,
                          int32_t cap, int32_t group, int32_t k_bits, int32_t v_bits,
-                         float scale, int32_t causal, uint16_t *out, void *workspace,
+                         float scale, int32_t causal, const uint16_t *gate_proj,
+                         int32_t gate_stride, uint16_t *out, void *workspace,
                          size_t workspace_bytes, vb_stream_t stream);
 
 /* GQA decode attention over a plain bf16 cache [B, Hkv, cap, 256] (the MTP
  * layer's mlx-lm KVCache attended by mx.fast.scaled_dot_product_attention,
  * mtp/qwen3_next_mtp.py:40-56): float32 scores, softmax and P V, one bf16
  * rounding. keys = *pos + pos_add + L, read on the device; q bf16
- * [B, Hq, L, 256]; out bf16 [B, Hq, L, 256]; (Hq/Hkv) * L <= 32. Workspace as
+ * [B, Hq, L, 256]; out bf16 [B, Hq, L, 256], or the gated [L, Hq * 256] rows
+ * with gate_proj as in vb_kv_decode_attn_at; (Hq/Hkv) * L <= 32. Workspace as
  * vb_kv_attn_workspace_size(batch, q_heads, L, dim, keys_max) + 256. */
 int vb_kv_bf16_attn_at(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
                        int32_t batch, int32_t q_heads, int32_t kv_heads, int32_t L,
                        int32_t dim, const int32_t *pos, int32_t pos_add, int32_t keys_max,
-                       int32_t cap, float scale, int32_t causal, uint16_t *out,
-                       void *workspace, size_t workspace_bytes, vb_stream_t stream);
+                       int32_t cap, float scale, int32_t causal, const uint16_t *gate_proj,
+                       int32_t gate_stride, uint16_t *out, void *workspace,
+                       size_t workspace_bytes, vb_stream_t stream);
 
 /* ---------------------------------------------------------------------------
  * Expert residency: per-layer expert -> slot state of a pool of `cap` slots

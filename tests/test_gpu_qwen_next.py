@@ -227,6 +227,56 @@ def test_attn_prepare_quant_equals_unfused(tiny):
             assert torch.equal(outs[0][2][k], outs[1][2][k]), f"cache {k} T={T}"
 
 
+def test_attn_gate_fused_equals_separate(tiny):
+    """The output gate applied in the attention's combine pass = the plain
+    attention output followed by vb_attn_gate, bit for bit (IsoQuant cache
+    and plain bf16 cache)."""
+    import torch
+    from vates_b200._lib import lib, check
+    from vates_b200.pool import stream_handle
+    from vates_b200.qwen_next import AttnLayer, SP_POS
+    model, _ = tiny
+    model.reset()
+    b, cfg = model.buf, model.cfg
+    lay = next(l for l in model.layers if isinstance(l.mixer, AttnLayer))
+    m, D, T = lay.mixer, cfg.head_dim, 3
+    rng = np.random.default_rng(12)
+    b["state"][SP_POS] = 6
+    pos_ptr = b["state"].data_ptr() + 4 * SP_POS
+    b["x0"][:T] = _bf(rng.standard_normal((T, cfg.hidden)).astype(np.float32))
+    model._attn(m, lay, b["x0"], b["h"], T, None, pos_ptr)  # fills the caches and b["q"]
+    torch.cuda.synchronize()
+    c = m.cache
+    st = stream_handle()
+    plain = torch.empty((cfg.q_heads, T, D), dtype=torch.bfloat16, device="cuda")
+    sep = torch.empty((T, cfg.q_heads * D), dtype=torch.bfloat16, device="cuda")
+    fused = torch.empty_like(sep)
+    for gate, out in ((None, plain), (b["proj"].data_ptr(), fused)):
+        check(lib.vb_kv_decode_attn_at(
+            b["q"].data_ptr(), c["kc"].data_ptr(), c["ks"].data_ptr(), c["kb"].data_ptr(),
+            c["vc"].data_ptr(), c["vs"].data_ptr(), c["vb"].data_ptr(), model.rv.data_ptr(), 1,
+            cfg.q_heads, cfg.kv_heads, T, D, pos_ptr, model.cache_len, model.cache_len, 64, 4, 3,
+            D ** -0.5, 1, gate, cfg.attn_proj, out.data_ptr(), model.attn_ws.data_ptr(),
+            model.attn_ws.numel(), st), "vb_kv_decode_attn_at")
+    check(lib.vb_attn_gate(plain.data_ptr(), b["proj"].data_ptr(), cfg.attn_proj, T,
+                           cfg.q_heads, sep.data_ptr(), st), "vb_attn_gate")
+    torch.cuda.synchronize()
+    assert torch.equal(fused, sep)
+    # plain bf16 cache (the MTP layer's), keys = pos + pos_add + T
+    kc = torch.randn((cfg.kv_heads, model.cache_len, D), device="cuda").to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    for gate, out in ((None, plain), (b["proj"].data_ptr(), fused)):
+        check(lib.vb_kv_bf16_attn_at(
+            b["q"].data_ptr(), kc.data_ptr(), vc.data_ptr(), 1, cfg.q_heads, cfg.kv_heads, T, D,
+            pos_ptr, 2, model.cache_len, model.cache_len, D ** -0.5, 1, gate, cfg.attn_proj,
+            out.data_ptr(), model.attn_ws.data_ptr(), model.attn_ws.numel(), st),
+            "vb_kv_bf16_attn_at")
+    check(lib.vb_attn_gate(plain.data_ptr(), b["proj"].data_ptr(), cfg.attn_proj, T,
+                           cfg.q_heads, sep.data_ptr(), st), "vb_attn_gate")
+    torch.cuda.synchronize()
+    assert torch.equal(fused, sep)
+
+
 def test_forward_logits_vs_oracle(tiny):
     """Embeddings -> 4 layers -> final norm + lm_head -> argmax, two chunks,
     free-running. Each block matches on identical inputs (test above); over a

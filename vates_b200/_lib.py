@@ -166,9 +166,9 @@ _SIGNATURES = {
                                      _P, _P, _P, _P]),
     "vb_kv_decode_attn_at": (_I32, [_P, _P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _I32,
                                     _I32, _P, _I32, _I32, _I32, _I32, _I32, C.c_float, _I32,
-                                    _P, _P, _SZ, _P]),
+                                    _P, _I32, _P, _P, _SZ, _P]),
     "vb_kv_bf16_attn_at": (_I32, [_P, _P, _P, _I32, _I32, _I32, _I32, _I32, _P, _I32, _I32,
-                                  _I32, C.c_float, _I32, _P, _P, _SZ, _P]),
+                                  _I32, C.c_float, _I32, _P, _I32, _P, _P, _SZ, _P]),
     "vb_qlinear_workspace_size": (_SZ, [_I32, _I32, _I32]),
     "vb_qlinear": (_I32, [_P, _I32, _I32, _P, _P, _P, _I32, _I32, _I32, _P, C.c_float, _P, _P,
                           _P, _SZ, _P]),

@@ -26,10 +26,16 @@ struct AttnParams {
   const uint32_t *kc, *vc;
   const uint16_t *ks, *kb, *vs, *vb;
   const float *rv;
-  const int32_t *pos_dev;  // nullable: S = *pos_dev + L read on the device
+  const int32_t *pos_dev;  // nullable: S = *pos_dev + pos_add + L read on the device
+  int pos_add;
   int B, Hq, Hkv, L, S, cap, rep, QR, causal, nsplit, kps;
   float scale;
   float *opart, *mpart, *lpart;
+  // gate (nullable, batch 1): out receives bf16(o * bf16(sigmoid(g))) in
+  // [L, Hq * 256] with g = gate[l * gate_stride + hq * 512 + 256 + d] (the
+  // gate half of each query head's projection), else o in [B, Hq, L, 256]
+  const uint16_t *gate;
+  int gate_stride;
   uint16_t *out;
 };
 
@@ -64,6 +70,10 @@ __global__ void __launch_bounds__(256) kv_attn_combine_kernel(AttnParams p) {
   const size_t bh = (size_t)b * p.Hkv + hkv;
   const int tid = threadIdx.x;
   const int ns = p.nsplit;
+  // the gate value of this thread's output dim, loaded before the reductions
+  float gv = 0.f;
+  if (p.gate && tid < 32)
+    gv = bf2f(p.gate[(size_t)l * p.gate_stride + hq * 512 + 256 + 32 * chunk + tid]);
   // maximum and denominator: per-thread partials, warp shuffles, then the 8
   // warp values in warp order (one block barrier each)
   const int wid = tid >> 5;
@@ -115,7 +125,10 @@ __global__ void __launch_bounds__(256) kv_attn_combine_kernel(AttnParams p) {
         acc = __fadd_rn(acc, __fmul_rn(ov[(tid & ~3) + kk], rbf(__ldg(R + i * 4 + kk))));
       o = rbf(acc);
     }
-    p.out[(size_t)row_id * 256 + d] = f2bf(o);
+    if (p.gate)  // attention output times the sigmoid gate (kv_quant_patch.py:70-71)
+      p.out[((size_t)l * p.Hq + hq) * 256 + d] = f2bf(o * rbf(mlx_sigmoid(gv)));
+    else
+      p.out[(size_t)row_id * 256 + d] = f2bf(o);
   }
 }
 
@@ -191,7 +204,7 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
     pdl_launch_dependents();
     pdl_wait();
   }
-  const int S_ = DEV_POS ? min(max(*p.pos_dev, 0) + p.L, p.cap) : p.S;
+  const int S_ = DEV_POS ? min(max(*p.pos_dev + p.pos_add, 0) + p.L, p.cap) : p.S;
   const int bh = blockIdx.x, split = blockIdx.y;
   const int b = bh / p.Hkv, hkv = bh % p.Hkv;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -534,7 +547,7 @@ __global__ void __launch_bounds__(A4_WARPS * 32, 3) kv_attn4_kernel(AttnParams p
     pdl_launch_dependents();
     pdl_wait();
   }
-  const int S_ = DEV_POS ? min(max(*p.pos_dev, 0) + p.L, p.cap) : p.S;
+  const int S_ = DEV_POS ? min(max(*p.pos_dev + p.pos_add, 0) + p.L, p.cap) : p.S;
   const int bh = blockIdx.x, split = blockIdx.y;
   const int b = bh / p.Hkv, hkv = bh % p.Hkv;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -807,7 +820,7 @@ __global__ void __launch_bounds__(256) kv_bf16_attn_kernel(AttnParams p) {
     pdl_launch_dependents();
     pdl_wait();
   }
-  const int S_ = DEV_POS ? min(max(*p.pos_dev, 0) + p.L, p.cap) : p.S;
+  const int S_ = DEV_POS ? min(max(*p.pos_dev + p.pos_add, 0) + p.L, p.cap) : p.S;
   float *qs = reinterpret_cast<float *>(smem_raw);                    // [32][256]
   uint16_t *ks = reinterpret_cast<uint16_t *>(qs + 32 * 256);         // [32][B16_KP]
   uint16_t *vs = ks + 32 * B16_KP;                                    // [32][256]
@@ -925,12 +938,6 @@ __global__ void __launch_bounds__(256) kv_bf16_attn_kernel(AttnParams p) {
   }
 }
 
-__global__ void add_i32_kernel(const int32_t *a, int32_t add, int32_t *out) {
-  pdl_launch_dependents();
-  pdl_wait();
-  *out = *a + add;
-}
-
 // Keys per split: about three CTAs per SM over all (batch, kv head) pairs,
 // in multiples of 64 keys.
 static void attn_split(int bhk, int S, int &nsplit, int &kps) {
@@ -965,6 +972,7 @@ static int kv_decode_attn_impl(const uint16_t *q, const uint32_t *k_codes,
                                int32_t L, int32_t dim, int32_t keys, int32_t cap,
                                int32_t group, int32_t k_bits, int32_t v_bits,
                                float scale, int32_t causal, const int32_t *pos_dev,
+                               const uint16_t *gate, int32_t gate_stride,
                                uint16_t *out, void *workspace, size_t workspace_bytes,
                                vb_stream_t stream) {
   VB_REQUIRE(dim == 256 && group == 64 && k_bits == 4 && v_bits == 3,
@@ -977,9 +985,12 @@ static int kv_decode_attn_impl(const uint16_t *q, const uint32_t *k_codes,
   VB_REQUIRE(keys >= L && keys <= cap, "vb_kv_decode_attn: keys=%d cap=%d L=%d", keys, cap, L);
   VB_REQUIRE(q && k_codes && k_scales && k_biases && v_codes && v_scales && v_biases && out,
              "vb_kv_decode_attn: null pointer");
-  AttnParams p;
+  VB_REQUIRE(!gate || (batch == 1 && gate_stride >= q_heads * 512),
+             "vb_kv_decode_attn: gate with batch %d, stride %d", batch, gate_stride);
+  AttnParams p = {};
   p.q = q; p.kc = k_codes; p.vc = v_codes; p.ks = k_scales; p.kb = k_biases;
   p.vs = v_scales; p.vb = v_biases; p.rv = rv_blocks; p.pos_dev = pos_dev;
+  p.gate = gate; p.gate_stride = gate_stride;
   p.B = batch; p.Hq = q_heads; p.Hkv = kv_heads; p.L = L; p.S = keys; p.cap = cap;
   p.rep = rep; p.QR = rep * L; p.causal = causal; p.scale = scale;
   attn_split(batch * kv_heads, keys, p.nsplit, p.kps);
@@ -1040,15 +1051,16 @@ int vb_kv_decode_attn(const uint16_t *q, const uint32_t *k_codes,
                       vb_stream_t stream) {
   return kv_decode_attn_impl(q, k_codes, k_scales, k_biases, v_codes, v_scales, v_biases,
                              rv_blocks, batch, q_heads, kv_heads, L, dim, keys, cap, group,
-                             k_bits, v_bits, scale, causal, nullptr, out, workspace,
+                             k_bits, v_bits, scale, causal, nullptr, nullptr, 0, out, workspace,
                              workspace_bytes, stream);
 }
 
 int vb_kv_bf16_attn_at(const uint16_t *q, const uint16_t *k_cache, const uint16_t *v_cache,
                        int32_t batch, int32_t q_heads, int32_t kv_heads, int32_t L,
                        int32_t dim, const int32_t *pos, int32_t pos_add, int32_t keys_max,
-                       int32_t cap, float scale, int32_t causal, uint16_t *out,
-                       void *workspace, size_t workspace_bytes, vb_stream_t stream) {
+                       int32_t cap, float scale, int32_t causal, const uint16_t *gate_proj,
+                       int32_t gate_stride, uint16_t *out, void *workspace,
+                       size_t workspace_bytes, vb_stream_t stream) {
   VB_REQUIRE(dim == 256, "vb_kv_bf16_attn_at: D=%d (256 only)", dim);
   VB_REQUIRE(batch > 0 && kv_heads > 0 && q_heads % kv_heads == 0,
              "vb_kv_bf16_attn_at: heads %d/%d", q_heads, kv_heads);
@@ -1057,10 +1069,13 @@ int vb_kv_bf16_attn_at(const uint16_t *q, const uint16_t *k_cache, const uint16_
   VB_REQUIRE(keys_max >= L && keys_max <= cap, "vb_kv_bf16_attn_at: keys_max=%d cap=%d",
              keys_max, cap);
   VB_REQUIRE(q && k_cache && v_cache && out && pos, "vb_kv_bf16_attn_at: null pointer");
-  AttnParams p;
+  VB_REQUIRE(!gate_proj || (batch == 1 && gate_stride >= q_heads * 512),
+             "vb_kv_bf16_attn_at: gate with batch %d, stride %d", batch, gate_stride);
+  AttnParams p = {};
   p.q = q; p.kc = reinterpret_cast<const uint32_t *>(k_cache);
   p.vc = reinterpret_cast<const uint32_t *>(v_cache);
-  p.ks = p.kb = p.vs = p.vb = nullptr; p.rv = nullptr; p.pos_dev = nullptr;
+  p.ks = p.kb = p.vs = p.vb = nullptr; p.rv = nullptr; p.pos_dev = pos; p.pos_add = pos_add;
+  p.gate = gate_proj; p.gate_stride = gate_stride;
   p.B = batch; p.Hq = q_heads; p.Hkv = kv_heads; p.L = L; p.S = keys_max; p.cap = cap;
   p.rep = rep; p.QR = rep * L; p.causal = causal; p.scale = scale;
   attn_split(batch * kv_heads, keys_max, p.nsplit, p.kps);
@@ -1077,16 +1092,6 @@ int vb_kv_bf16_attn_at(const uint16_t *q, const uint16_t *k_cache, const uint16_
   p.lpart = reinterpret_cast<float *>(ws + obytes + mbytes);
   p.out = out;
   cudaStream_t s = as_stream(stream);
-  // the key count pos + pos_add + L is read on the device: a one-int scratch
-  int32_t *pos_eff = reinterpret_cast<int32_t *>(ws + obytes + 2 * mbytes);
-  if (pos_add != 0) {
-    vb_launch(add_i32_kernel, dim3(1), dim3(1), 0, s, false, pos, (int32_t)pos_add, pos_eff);
-    const int rc0 = check_launch("add_i32_kernel");
-    if (rc0) return rc0;
-    p.pos_dev = pos_eff;
-  } else {
-    p.pos_dev = pos;
-  }
   static bool attr_done = false;
   if (!attr_done) {
     cudaFuncSetAttribute(kv_bf16_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1108,13 +1113,14 @@ int vb_kv_decode_attn_at(const uint16_t *q, const uint32_t *k_codes,
                          int32_t batch, int32_t q_heads, int32_t kv_heads,
                          int32_t L, int32_t dim, const int32_t *pos, int32_t keys_max,
                          int32_t cap, int32_t group, int32_t k_bits, int32_t v_bits,
-                         float scale, int32_t causal, uint16_t *out, void *workspace,
+                         float scale, int32_t causal, const uint16_t *gate_proj,
+                         int32_t gate_stride, uint16_t *out, void *workspace,
                          size_t workspace_bytes, vb_stream_t stream) {
   VB_REQUIRE(pos != nullptr, "vb_kv_decode_attn_at: null position");
   return kv_decode_attn_impl(q, k_codes, k_scales, k_biases, v_codes, v_scales, v_biases,
                              rv_blocks, batch, q_heads, kv_heads, L, dim, keys_max, cap, group,
-                             k_bits, v_bits, scale, causal, pos, out, workspace,
-                             workspace_bytes, stream);
+                             k_bits, v_bits, scale, causal, pos, gate_proj, gate_stride, out,
+                             workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

@@ -368,7 +368,8 @@ class QwenNextModel:
             check(lib.vb_kv_bf16_attn_at(b["q"].data_ptr(), c["k"].data_ptr(), c["v"].data_ptr(),
                                          1, cfg.q_heads, cfg.kv_heads, T, D, pos_ptr, pos_add,
                                          self.cache_len, self.cache_len, D ** -0.5, 1,
-                                         b["attn"].data_ptr(), self.attn_ws.data_ptr(),
+                                         b["proj"].data_ptr(), cfg.attn_proj,
+                                         b["gout"].data_ptr(), self.attn_ws.data_ptr(),
                                          self.attn_ws.numel(), stream_handle(st)),
                   "vb_kv_bf16_attn_at")
         else:
@@ -405,12 +406,11 @@ class QwenNextModel:
                                            c["vb"].data_ptr(), self.rv.data_ptr(), 1,
                                            cfg.q_heads, cfg.kv_heads, T, D, pos_ptr,
                                            self.cache_len, self.cache_len, 64, 4, 3, D ** -0.5,
-                                           1, b["attn"].data_ptr(), self.attn_ws.data_ptr(),
+                                           1, b["proj"].data_ptr(), cfg.attn_proj,
+                                           b["gout"].data_ptr(), self.attn_ws.data_ptr(),
                                            self.attn_ws.numel(), stream_handle(st)),
                   "vb_kv_decode_attn_at")
-        check(lib.vb_attn_gate(b["attn"].data_ptr(), b["proj"].data_ptr(), cfg.attn_proj, T,
-                               cfg.q_heads, b["gout"].data_ptr(), stream_handle(st)),
-              "vb_attn_gate")
+        # (the output gate is applied by the attention's combine pass)
         m.o_proj(b["gout"], h, T, residual=x, stream=st)
 
     def _moe(self, lay: DecoderLayer, h, out, T, st):
