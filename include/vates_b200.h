@@ -691,6 +691,17 @@ size_t vb_argmax_workspace_size(int32_t rows);
 int vb_argmax(const uint16_t *values, int32_t rows, int32_t n, int32_t *out, void *workspace,
               size_t workspace_bytes, vb_stream_t stream);
 
+/* The MTP head's fc input (qwen3_next_mtp.py:40-46) in one launch: row t of
+ * out bf16 [T, 2 * hidden] = [rms_norm(embed(ids[t])) * emb_norm_w |
+ * rms_norm(prev_hidden[t]) * hid_norm_w], bit for bit vb_embed_rows followed
+ * by two vb_rms_norm into the halves (weights NULL: unit). hidden <= 8192.
+ * Ids out of range give a zero embedding half and VB_STATUS_BOUNDS. */
+int vb_mtp_fc_input(const int32_t *ids, int32_t tokens, const uint32_t *codes,
+                    const uint16_t *scales, const uint16_t *biases, int32_t vocab,
+                    int32_t hidden, const uint16_t *emb_norm_w, const uint16_t *prev_hidden,
+                    const uint16_t *hid_norm_w, float eps, uint16_t *out, int32_t *status,
+                    vb_stream_t stream);
+
 /* nn.QuantizedEmbedding: out[t] = dequant(table row ids[t]) (bf16, 4-bit
  * group 64). Ids out of range give zero rows and VB_STATUS_BOUNDS. */
 int vb_embed_rows(const int32_t *ids, int32_t tokens, const uint32_t *codes,

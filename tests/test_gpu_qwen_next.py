@@ -277,6 +277,49 @@ def test_attn_gate_fused_equals_separate(tiny):
     assert torch.equal(fused, sep)
 
 
+def test_mtp_fc_input_equals_separate(tiny):
+    """The MTP fc input in one launch = embedding rows, then the two RMS
+    norms into the halves, bit for bit; an id out of range gives a zero
+    embedding half and the bounds status."""
+    import torch
+    from vates_b200._lib import lib, check
+    from vates_b200.pool import stream_handle
+    model, _ = tiny
+    cfg, H, T = model.cfg, model.cfg.hidden, 3
+    rng = np.random.default_rng(13)
+    st = stream_handle()
+    e = model.embed
+    ids = torch.from_numpy(rng.integers(0, cfg.vocab, T).astype(np.int32)).cuda()
+    hid = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32)).cuda().to(torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    emb = torch.empty((T, H), dtype=torch.bfloat16, device="cuda")
+    ref = torch.empty((T, 2 * H), dtype=torch.bfloat16, device="cuda")
+    got = torch.empty_like(ref)
+    check(lib.vb_embed_rows(ids.data_ptr(), T, e.codes.data_ptr(), e.scales.data_ptr(),
+                            e.biases.data_ptr(), cfg.vocab, H, 64, 4, emb.data_ptr(),
+                            status.data_ptr(), st), "vb_embed_rows")
+    check(lib.vb_rms_norm(emb.data_ptr(), None, model.mtp_norm_emb.data_ptr(), T, H, cfg.eps,
+                          None, ref.data_ptr(), 2 * H, st), "vb_rms_norm")
+    check(lib.vb_rms_norm(hid.data_ptr(), None, model.mtp_norm_hid.data_ptr(), T, H, cfg.eps,
+                          None, ref.data_ptr() + 2 * H, 2 * H, st), "vb_rms_norm")
+    check(lib.vb_mtp_fc_input(ids.data_ptr(), T, e.codes.data_ptr(), e.scales.data_ptr(),
+                              e.biases.data_ptr(), cfg.vocab, H, model.mtp_norm_emb.data_ptr(),
+                              hid.data_ptr(), model.mtp_norm_hid.data_ptr(), cfg.eps,
+                              got.data_ptr(), status.data_ptr(), st), "vb_mtp_fc_input")
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(got, ref)
+    ids[1] = cfg.vocab  # out of range
+    check(lib.vb_mtp_fc_input(ids.data_ptr(), T, e.codes.data_ptr(), e.scales.data_ptr(),
+                              e.biases.data_ptr(), cfg.vocab, H, model.mtp_norm_emb.data_ptr(),
+                              hid.data_ptr(), model.mtp_norm_hid.data_ptr(), cfg.eps,
+                              got.data_ptr(), status.data_ptr(), st), "vb_mtp_fc_input")
+    torch.cuda.synchronize()
+    assert int(status.item()) & 2  # VB_STATUS_BOUNDS
+    assert not got[1, :H].float().abs().sum().item()
+    assert torch.equal(got[1, H:], ref[1, H:]) and torch.equal(got[0], ref[0])
+
+
 def test_forward_logits_vs_oracle(tiny):
     """Embeddings -> 4 layers -> final norm + lm_head -> argmax, two chunks,
     free-running. Each block matches on identical inputs (test above); over a

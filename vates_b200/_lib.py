@@ -188,6 +188,8 @@ _SIGNATURES = {
                                      _I32, C.c_float, _P, _P, _P, _P, _I32, _I32, _P, _P, _P,
                                      _I32, _P, _P, _P, _P, _P]),
     "vb_attn_gate": (_I32, [_P, _P, _I32, _I32, _I32, _P, _P]),
+    "vb_mtp_fc_input": (_I32, [_P, _I32, _P, _P, _P, _I32, _I32, _P, _P, _P, C.c_float, _P, _P,
+                               _P]),
     "vb_spec_accept": (_I32, [_P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _I32, _P, _I32, _P]),
     "vb_spec_sync_inputs": (_I32, [_P, _P, _P, _P, _I32, _I32, _P, _P, _P]),
     "vb_spec_advance_mtp": (_I32, [_P, _P]),

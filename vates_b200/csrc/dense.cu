@@ -393,6 +393,68 @@ __global__ void __launch_bounds__(256) embed4_kernel(const int32_t *__restrict__
   }
 }
 
+// The MTP head's fc input in one launch (qwen3_next_mtp.py:40-46): row t of
+// out [T, 2H] = [rms_norm(embed(ids[t])) * w_emb | rms_norm(hidden[t]) * w_hid].
+// CTA (t, half) stages its source row in shared memory as bf16 (the
+// embedding row dequantized exactly as embed4_kernel does it), then
+// normalises it with rms_norm_kernel's arithmetic and summation order, so
+// the result equals vb_embed_rows followed by two vb_rms_norm calls.
+constexpr int MTPI_MAX_H = 8192;
+__global__ void __launch_bounds__(256) mtp_fc_input_kernel(
+    const int32_t *__restrict__ ids, const uint32_t *__restrict__ codes,
+    const uint16_t *__restrict__ scales, const uint16_t *__restrict__ biases, int vocab, int H,
+    const uint16_t *__restrict__ w_emb, const uint16_t *__restrict__ hidden,
+    const uint16_t *__restrict__ w_hid, float eps, uint16_t *__restrict__ out,
+    int32_t *status) {
+  __shared__ __align__(16) uint16_t row[MTPI_MAX_H];
+  __shared__ float red[8];
+  const int t = blockIdx.x, half = blockIdx.y, tid = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
+  if (half == 0) {
+    const int id = ids[t];
+    const bool ok = id >= 0 && id < vocab;
+    if (!ok && tid == 0) flag_status(status, VB_STATUS_BOUNDS);
+    const int wpr = H >> 3;
+    for (int wi = tid; wi < wpr; wi += 256) {
+      uint4 o4 = make_uint4(0, 0, 0, 0);
+      if (ok) {
+        const size_t gi = (size_t)id * (H >> 6) + (wi >> 3);
+        const uint32_t sc = scales[gi], bi = biases[gi];
+        uint32_t o[4];
+        dequant4_bf16x2(codes[(size_t)id * wpr + wi], sc | (sc << 16), bi | (bi << 16), o);
+        o4 = make_uint4(__byte_perm(o[0], o[1], 0x5410), __byte_perm(o[2], o[3], 0x5410),
+                        __byte_perm(o[0], o[1], 0x7632), __byte_perm(o[2], o[3], 0x7632));
+      }
+      *reinterpret_cast<uint4 *>(row + wi * 8) = o4;
+    }
+  } else {
+    for (int k = tid * 8; k < H; k += 256 * 8)
+      *reinterpret_cast<uint4 *>(row + k) =
+          *reinterpret_cast<const uint4 *>(hidden + (size_t)t * H + k);
+  }
+  __syncthreads();
+  float ss = 0.f;
+  for (int k = tid; k < H; k += 256) {
+    const float v = bf2f(row[k]);
+    ss = fmaf(v, v, ss);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float inv = rsqrtf(tot / (float)H + eps);
+  const uint16_t *w = half == 0 ? w_emb : w_hid;
+  uint16_t *y = out + (size_t)t * 2 * H + half * H;
+  for (int k = tid; k < H; k += 256) {
+    const float nv = rbf(bf2f(row[k]) * inv);
+    y[k] = f2bf(w ? nv * bf2f(w[k]) : nv);
+  }
+}
+
 static size_t ql_smem_bytes(int K) {
   return (size_t)K * 16 + (size_t)(K / 64) * QL_MAX_T * 4;
 }
@@ -505,6 +567,23 @@ int vb_argmax(const uint16_t *values, int32_t rows, int32_t n, int32_t *out, voi
   vb_launch(argmax_kernel, dim3(rows, AM_PARTS), dim3(256), 0, as_stream(stream), false, values,
             (int)n, pv, pi, tickets, out);
   return check_launch("argmax_kernel");
+}
+
+int vb_mtp_fc_input(const int32_t *ids, int32_t tokens, const uint32_t *codes,
+                    const uint16_t *scales, const uint16_t *biases, int32_t vocab,
+                    int32_t hidden, const uint16_t *emb_norm_w, const uint16_t *prev_hidden,
+                    const uint16_t *hid_norm_w, float eps, uint16_t *out, int32_t *status,
+                    vb_stream_t stream) {
+  VB_REQUIRE(tokens >= 1 && vocab >= 1 && hidden >= 64 && hidden % 64 == 0 &&
+                 hidden <= MTPI_MAX_H && eps > 0.f,
+             "vb_mtp_fc_input: tokens=%d vocab=%d hidden=%d", tokens, vocab, hidden);
+  VB_REQUIRE(ids && codes && scales && biases && prev_hidden && out,
+             "vb_mtp_fc_input: null tensor");
+  VB_REQUIRE(((uintptr_t)prev_hidden % 16) == 0, "vb_mtp_fc_input: hidden rows 16-byte aligned");
+  vb_launch(mtp_fc_input_kernel, dim3(tokens, 2), dim3(256), 0, as_stream(stream), false, ids,
+            codes, scales, biases, (int)vocab, (int)hidden, emb_norm_w, prev_hidden, hid_norm_w,
+            eps, out, status);
+  return check_launch("mtp_fc_input_kernel");
 }
 
 int vb_embed_rows(const int32_t *ids, int32_t tokens, const uint32_t *codes,

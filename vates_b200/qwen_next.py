@@ -463,17 +463,14 @@ class QwenNextModel:
         st = stream
         H = cfg.hidden
         state = b["state"]
-        e = b["hn"]
-        check(lib.vb_embed_rows(ids_ptr, T, self.embed.codes.data_ptr(),
-                                self.embed.scales.data_ptr(), self.embed.biases.data_ptr(),
-                                cfg.vocab, H, 64, 4, e.data_ptr(), b["status"].data_ptr(),
-                                stream_handle(st)), "vb_embed_rows")
         cat = b["cat"]
-        check(lib.vb_rms_norm(e.data_ptr(), None, self.mtp_norm_emb.data_ptr(), T, H, cfg.eps,
-                              None, cat.data_ptr(), 2 * H, stream_handle(st)), "vb_rms_norm")
-        check(lib.vb_rms_norm(hidden.data_ptr(), None, self.mtp_norm_hid.data_ptr(), T, H,
-                              cfg.eps, None, cat.data_ptr() + 2 * H, 2 * H, stream_handle(st)),
-              "vb_rms_norm")
+        # embedding + its norm | hidden norm, the halves of the fc input
+        check(lib.vb_mtp_fc_input(ids_ptr, T, self.embed.codes.data_ptr(),
+                                  self.embed.scales.data_ptr(), self.embed.biases.data_ptr(),
+                                  cfg.vocab, H, self.mtp_norm_emb.data_ptr(),
+                                  hidden.data_ptr(), self.mtp_norm_hid.data_ptr(), cfg.eps,
+                                  cat.data_ptr(), b["status"].data_ptr(), stream_handle(st)),
+              "vb_mtp_fc_input")
         x, y = b["x0"], b["x1"]
         self.mtp_fc(cat, x, T, stream=st)
         self._layer(self.mtp_layer, x, b["h"], y, T, st, _i32(state, SP_MTP_POS), mtp=True,
