@@ -32,7 +32,7 @@ sys.path.insert(0, ROOT)
 METRIC = "MoE tokens/s and HBM GB/s (decode T≤4); prefill tok/s at 1/2/4/8 B200"
 DECODE_WORKLOAD = "decode_verify_T4_48layers_fresh_inputs"
 EXPERT_BYTES = 1_769_472          # blob_layout stride at H=2048, I=512, 4-bit g64
-LAYER_TRAFFIC_PER_ENTRY = 1_877_900  # dram read + write per entry (profiles/decode_moe_layer_kernel.md)
+LAYER_TRAFFIC_PER_ENTRY = 1_854_185  # dram read + write per entry (profiles/decode_moe_layer_kernel.md)
 ROUTER_BYTES = 512 * 2048 * 2
 SHARED_GATE_BYTES = 2048 * 2
 
