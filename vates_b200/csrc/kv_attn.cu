@@ -216,8 +216,10 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
   uint8_t *raw0 = wsm + A1_VBYTES;
 
   // Q^T as B fragments (row g; zero for rows >= QR) and the per-group q sums
-  // of rows 2c, 2c+1.
-  uint32_t qb[4][4][2];
+  // of rows 2c, 2c+1. The fragments are the same in every warp of the CTA;
+  // they live in shared memory (warp w writes group w), which keeps the tile
+  // loop within the register budget of three CTAs per SM without spills.
+  __shared__ uint2 s_qb[4][4][32];
   float qs[4][2];
   {
     float vals[64];
@@ -241,11 +243,13 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
     }
 #pragma unroll
     for (int G = 0; G < 4; ++G) {
+      if (G == warp) {
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const int d0 = 16 * G + 8 * (m >> 1) + 2 * (m & 1);
-        qb[G][m][0] = pack_bf2(vals[d0], vals[d0 + 4]);
-        qb[G][m][1] = pack_bf2(vals[d0 + 1], vals[d0 + 5]);
+        for (int m = 0; m < 4; ++m) {
+          const int d0 = 16 * G + 8 * (m >> 1) + 2 * (m & 1);
+          s_qb[G][m][lane] = make_uint2(pack_bf2(vals[d0], vals[d0 + 4]),
+                                        pack_bf2(vals[d0 + 1], vals[d0 + 5]));
+        }
       }
       float t = part[G];
       t += __shfl_xor_sync(0xffffffffu, t, 1);
@@ -255,6 +259,8 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
       qs[G][1] = __shfl_sync(0xffffffffu, t, (2 * c + 1) * 4);
     }
   }
+  static_assert(A1_WARPS == 4, "warp w stores the Q fragments of group w");
+  __syncthreads();
 
   float O[16][4];
 #pragma unroll
@@ -314,7 +320,8 @@ __global__ void __launch_bounds__(A1_WARPS * 32, 3) kv_attn1_kernel(AttnParams p
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
         const int i0 = 2 * (m & 1), h = m >> 1;
-        mma_bf16(d, pa[h][i0], pb[h][i0], pa[h][i0 + 1], pb[h][i0 + 1], qb[G][m][0], qb[G][m][1]);
+        const uint2 qf = s_qb[G][m][lane];
+        mma_bf16(d, pa[h][i0], pb[h][i0], pa[h][i0 + 1], pb[h][i0 + 1], qf.x, qf.y);
       }
       const float s_g = bf_at2(ksg, G), s_8 = bf_at2(ks8, G);
       const float bp_g = fmaf(-128.f, s_g, bf_at2(kbg, G));

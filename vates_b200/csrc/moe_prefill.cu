@@ -1115,17 +1115,22 @@ __global__ void ep_pack_kernel(const uint16_t *__restrict__ x, const int32_t *__
                                const int32_t *__restrict__ dest_routes,
                                uint16_t *__restrict__ send_x, int32_t *__restrict__ send_meta,
                                int32_t *__restrict__ route_send_idx) {
+  // Per-destination chunk offsets in shared memory (indexed by a routed
+  // expert's owner: a per-thread array would live in local memory).
+  __shared__ int row_off[EP_MAX_WORLD], route_off[EP_MAX_WORLD];
+  if (threadIdx.x == 0) {
+    int ro = 0, qo = 0;
+    for (int d = 0; d < world; ++d) {
+      row_off[d] = ro;
+      route_off[d] = qo;
+      ro += dest_rows[d];
+      qo += dest_routes[d];
+    }
+  }
+  __syncthreads();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= T) return;
-  int row_off[EP_MAX_WORLD], route_off[EP_MAX_WORLD];
-  int ro = 0, qo = 0;
-  for (int d = 0; d < world; ++d) {
-    row_off[d] = ro;
-    route_off[d] = qo;
-    ro += dest_rows[d];
-    qo += dest_routes[d];
-  }
   if (lane < k) {
     const int e = inds[t * k + lane];
     const int d = owner[e];
