@@ -74,11 +74,25 @@ __global__ void __launch_bounds__(256) kv_attn_combine_kernel(AttnParams p) {
   float gv = 0.f;
   if (p.gate && tid < 32)
     gv = bf2f(p.gate[(size_t)l * p.gate_stride + hq * 512 + 256 + 32 * chunk + tid]);
+  // The first 256 splits' maxima and sums and this thread's first 32
+  // partial outputs are loaded before any of them is used (one memory round
+  // trip instead of three); the sums below keep the split order.
+  const int wid = tid >> 5;
+  const int dl = tid & 31, sl = tid >> 5;
+  const int d = 32 * chunk + dl;
+  constexpr int CB_PRE = 32;  // splits sl + 8 j, j < CB_PRE, in registers
+  const float mp0 = tid < ns ? p.mpart[(bh * ns + tid) * 32 + r] : -INFINITY;
+  const float lp0 = tid < ns ? p.lpart[(bh * ns + tid) * 32 + r] : 0.f;
+  float opre[CB_PRE];
+#pragma unroll
+  for (int j = 0; j < CB_PRE; ++j) {
+    const int s = sl + 8 * j;
+    opre[j] = s < ns ? p.opart[((bh * ns + s) * 32 + r) * 256 + d] : 0.f;
+  }
   // maximum and denominator: per-thread partials, warp shuffles, then the 8
   // warp values in warp order (one block barrier each)
-  const int wid = tid >> 5;
-  float m = -INFINITY;
-  for (int s = tid; s < ns; s += 256) m = fmaxf(m, p.mpart[(bh * ns + s) * 32 + r]);
+  float m = mp0;
+  for (int s = tid + 256; s < ns; s += 256) m = fmaxf(m, p.mpart[(bh * ns + s) * 32 + r]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   if ((tid & 31) == 0) s_red[wid] = m;
@@ -89,10 +103,10 @@ __global__ void __launch_bounds__(256) kv_attn_combine_kernel(AttnParams p) {
   float dn = 0.f;
   for (int s = tid; s < ns; s += 256) {
     const size_t cta = bh * ns + s;
-    const float ms = p.mpart[cta * 32 + r];
+    const float ms = s == tid ? mp0 : p.mpart[cta * 32 + r];
     const float e = ms == -INFINITY ? 0.f : expf(ms - M);
     s_e[s] = e;
-    dn = fmaf(p.lpart[cta * 32 + r], e, dn);
+    dn = fmaf(s == tid ? lp0 : p.lpart[cta * 32 + r], e, dn);
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) dn += __shfl_xor_sync(0xffffffffu, dn, o);
@@ -101,11 +115,14 @@ __global__ void __launch_bounds__(256) kv_attn_combine_kernel(AttnParams p) {
   float den = 0.f;
 #pragma unroll
   for (int w = 0; w < 8; ++w) den += s_red[8 + w];
-  const int dl = tid & 31, sl = tid >> 5;
-  const int d = 32 * chunk + dl;
   float num = 0.f;
+#pragma unroll
+  for (int j = 0; j < CB_PRE; ++j) {
+    const int s = sl + 8 * j;
+    if (s < ns) num = fmaf(opre[j], s_e[s], num);
+  }
 #pragma unroll 4
-  for (int s = sl; s < ns; s += 8)
+  for (int s = sl + 8 * CB_PRE; s < ns; s += 8)
     num = fmaf(p.opart[((bh * ns + s) * 32 + r) * 256 + d], s_e[s], num);
   s_num[sl][dl] = num;
   __syncthreads();
