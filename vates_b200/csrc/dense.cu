@@ -103,10 +103,19 @@ __device__ __forceinline__ float ql_half(const uint32_t (&w)[(GPW + 1) / 2], int
   return __uint_as_float((j & 1) ? (v & 0xFFFF0000u) : (v << 16));
 }
 
+// This warp's x fragments and group sums (its groups are the same for every
+// item): in registers when GPW <= 4, read from shared memory otherwise.
+template <int GPW>
+struct QlX {
+  static constexpr bool REG = GPW <= 4;
+  uint2 f[REG ? GPW : 1][4];
+  float s[REG ? GPW : 1][2];
+};
+
 template <int GPW>
 __device__ __forceinline__ void ql_compute(const QlItem<GPW> &d, const uint2 *xfrag,
-                                           const float *xsum, int g0, int ng, int lane,
-                                           float (&acc)[4]) {
+                                           const float *xsum, const QlX<GPW> &xr, int g0, int ng,
+                                           int lane, float (&acc)[4]) {
   const int c = lane & 3;
 #pragma unroll
   for (int j = 0; j < GPW; ++j) {
@@ -121,13 +130,16 @@ __device__ __forceinline__ void ql_compute(const QlItem<GPW> &d, const uint2 *xf
 #pragma unroll
     for (int mm = 0; mm < 4; ++mm) {
       const int jw = mm >> 1, h = mm & 1;
-      const uint2 bf = xfrag[(grp * 4 + mm) * 32 + lane];
+      const uint2 bf = QlX<GPW>::REG ? xr.f[QlX<GPW>::REG ? j : 0][mm]
+                                     : xfrag[(grp * 4 + mm) * 32 + lane];
       mma_bf16(dd, pa[jw][2 * h], pb[jw][2 * h], pa[jw][2 * h + 1], pb[jw][2 * h + 1], bf.x,
                bf.y);
     }
     const float s_a = ql_half<GPW>(d.sa, j), s_b = ql_half<GPW>(d.sb, j);
     const float c_a = ql_half<GPW>(d.ba, j) - 128.f * s_a, c_b = ql_half<GPW>(d.bb, j) - 128.f * s_b;
-    const float x0 = xsum[grp * QL_MAX_T + 2 * c], x1 = xsum[grp * QL_MAX_T + 2 * c + 1];
+    const float x0 = QlX<GPW>::REG ? xr.s[QlX<GPW>::REG ? j : 0][0] : xsum[grp * QL_MAX_T + 2 * c];
+    const float x1 = QlX<GPW>::REG ? xr.s[QlX<GPW>::REG ? j : 0][1]
+                                   : xsum[grp * QL_MAX_T + 2 * c + 1];
     acc[0] += fmaf(s_a, dd[0], c_a * x0);
     acc[1] += fmaf(s_a, dd[1], c_a * x1);
     acc[2] += fmaf(s_b, dd[2], c_b * x0);
@@ -241,12 +253,23 @@ __global__ void __launch_bounds__(QL_THREADS, 2) qlinear_kernel(QlParams p) {
   __syncthreads();
 
   const int c = lane & 3, g = lane >> 2;
+  QlX<GPW> xr;
+  if constexpr (QlX<GPW>::REG) {
+#pragma unroll
+    for (int j = 0; j < GPW; ++j) {
+      const int grp = j < ng ? g0 + j : 0;
+#pragma unroll
+      for (int mm = 0; mm < 4; ++mm) xr.f[j][mm] = xfrag[(grp * 4 + mm) * 32 + lane];
+      xr.s[j][0] = xsum[grp * QL_MAX_T + 2 * c];
+      xr.s[j][1] = xsum[grp * QL_MAX_T + 2 * c + 1];
+    }
+  }
   int buf = 0;
   for (; it < p.items; it += gridDim.x) {
     const int next = it + gridDim.x;
     if (next < p.items) ql_load<GPW>(p, next, g0, ng, lane, nxt);
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    ql_compute<GPW>(cur, xfrag, xsum, g0, ng, lane, acc);
+    ql_compute<GPW>(cur, xfrag, xsum, xr, g0, ng, lane, acc);
     *reinterpret_cast<float4 *>(red[buf][warp][lane]) = make_float4(acc[0], acc[1], acc[2], acc[3]);
     __syncthreads();
     if (warp == 0) {
