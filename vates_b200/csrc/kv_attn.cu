@@ -53,7 +53,7 @@ __device__ __forceinline__ float bf_at2(const uint2 &v, int i) {
 
 constexpr int ATT_MAX_SPLITS = 1024;
 
-__global__ void __launch_bounds__(256) kv_attn_combine_kernel(AttnParams p) {
+__global__ void __launch_bounds__(256, 4) kv_attn_combine_kernel(AttnParams p) {
   pdl_launch_dependents();
   pdl_wait();  // no-op unless launched as a programmatic dependent
   __shared__ float s_red[256];
@@ -74,13 +74,16 @@ __global__ void __launch_bounds__(256) kv_attn_combine_kernel(AttnParams p) {
   float gv = 0.f;
   if (p.gate && tid < 32)
     gv = bf2f(p.gate[(size_t)l * p.gate_stride + hq * 512 + 256 + 32 * chunk + tid]);
-  // The first 256 splits' maxima and sums and this thread's first 32
+  // The first 256 splits' maxima and sums and this thread's first 16
   // partial outputs are loaded before any of them is used (one memory round
   // trip instead of three); the sums below keep the split order.
   const int wid = tid >> 5;
   const int dl = tid & 31, sl = tid >> 5;
   const int d = 32 * chunk + dl;
-  constexpr int CB_PRE = 32;  // splits sl + 8 j, j < CB_PRE, in registers
+  // splits sl + 8 j, j < CB_PRE, in registers: 16 keeps the kernel at 64
+  // registers, four CTAs per SM (32 raised it to 70 and three CTAs, slower on
+  // short caches with few splits)
+  constexpr int CB_PRE = 16;
   const float mp0 = tid < ns ? p.mpart[(bh * ns + tid) * 32 + r] : -INFINITY;
   const float lp0 = tid < ns ? p.lpart[(bh * ns + tid) * 32 + r] : 0.f;
   float opre[CB_PRE];
