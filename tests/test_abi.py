@@ -26,6 +26,28 @@ def test_library_exports_every_header_symbol():
     assert _lib.lib.vb_version() >= 100
 
 
+def _header_prototypes():
+    """name -> parameter count of every vb_ function the header declares."""
+    src = open(os.path.join(ROOT, "include", "vates_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    protos = {}
+    for m in re.finditer(r"\b(vb_[a-z0-9_]+)\s*\(([^;{]*?)\)\s*;", src):
+        params = m.group(2).strip()
+        protos[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return protos
+
+
+def test_ctypes_signatures_match_header_arity():
+    """Every ctypes declaration has as many arguments as the C prototype:
+    a stale Python signature would pass wrong values without an error."""
+    from vates_b200 import _lib
+    protos = _header_prototypes()
+    assert set(protos) == set(_lib.EXPORTED), set(protos) ^ set(_lib.EXPORTED)
+    bad = {n: (len(_lib._SIGNATURES[n][1]), k) for n, k in protos.items()
+           if len(_lib._SIGNATURES[n][1]) != k}
+    assert not bad, f"ctypes vs header argument counts: {bad}"
+
+
 def test_invalid_arguments_fail_without_launching():
     from vates_b200 import _lib
     a = _lib.VbMoeDecodeArgs()
